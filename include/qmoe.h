@@ -1,0 +1,180 @@
+/*
+ * qmoe.h -- C ABI of the B200 (sm_100a) Qwen3-MoE decoder-layer hot path.
+ *
+ * Conventions (every entry point):
+ *   - Plain device pointers, int64 sizes, a cudaStream_t passed as void*.
+ *     No torch or C++ types cross this boundary, and no C++ exception does.
+ *   - Outputs and scratch are allocated by the caller (the caller's allocator
+ *     owns memory); a *_workspace_size() query gives the scratch bytes.
+ *   - Return 0 on success or a negative qmoe_status.  Arguments are checked on
+ *     the host before anything is launched; a failed check launches nothing.
+ *     qmoe_last_error() gives a one-line reason for the last failure of the
+ *     calling thread.
+ *   - Work is stream-ordered and asynchronous; no entry point synchronises.
+ *     The library keeps no mutable global state except a lazily built,
+ *     read-only per-device property cache and the device error word read by
+ *     qmoe_device_error().
+ *   - bf16 tensors are row-major with unit inner stride; base pointers must be
+ *     16-byte aligned.
+ *
+ * Device weight layout (HF order; the NxDI layout of qwen.py:164-226 is its
+ * transpose and is converted once at load time):
+ *   w_router   (E, H)      bf16
+ *   w_gate_up  (E, 2I, H)  bf16, rows [0, I) = gate, rows [I, 2I) = up
+ *   w_down     (E, H, I)   bf16
+ */
+#ifndef QMOE_H_
+#define QMOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define QMOE_API __attribute__((visibility("default")))
+#else
+#define QMOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum qmoe_status {
+  QMOE_OK = 0,
+  QMOE_ERR_INVALID_ARGUMENT = -1,   /* null pointer, negative size, k > E ... */
+  QMOE_ERR_UNSUPPORTED_SHAPE = -2,  /* a size outside what the kernels handle */
+  QMOE_ERR_MISALIGNED = -3,         /* base pointer not 16-byte aligned */
+  QMOE_ERR_WORKSPACE_TOO_SMALL = -4,
+  QMOE_ERR_CUDA = -5,               /* CUDA runtime / launch error */
+  QMOE_ERR_DEVICE = -6,             /* device is not sm_100 */
+} qmoe_status;
+
+/* Library version (major*10000 + minor*100 + patch). */
+QMOE_API int qmoe_version(void);
+
+/* Human-readable name of a status code. */
+QMOE_API const char* qmoe_status_string(int status);
+
+/* One-line description of the last failure on the calling thread ("" if none). */
+QMOE_API const char* qmoe_last_error(void);
+
+/* Reads (and, if clear != 0, resets) the device error word of the current
+ * device: 0 = none, otherwise the code of the first bounded wait that gave up
+ * or the first out-of-range index a kernel refused.  Synchronises the current
+ * device. */
+QMOE_API int qmoe_device_error(int clear, unsigned int* code_out);
+
+/* ------------------------------------------------------------------------
+ * K1  router: logits, softmax, top-k, renormalised weights.
+ * Replaces the NxDI RouterTopK configured at qwen.py:260-269 (fp32 router,
+ * softmax, normalize_top_k_affinities) and the affinity gather + L1
+ * renormalisation at qwen_with_nki.py:2398-2405.
+ *
+ *   x         (T, H)  bf16 activations
+ *   w_router  (E, H)  bf16
+ *   bias      (E,)    fp32 or NULL; added to every logit after the dot product
+ *   logits    (T, E)  fp32 out or NULL
+ *   topk_idx  (T, k)  int32 out: experts by descending logit, ties -> lower index
+ *   topk_w    (T, k)  fp32 out: softmax probabilities of the chosen experts,
+ *                     divided by their sum when normalize != 0
+ *   chunk_hist (ceil(T/QMOE_ROUTER_CHUNK), E) int32 out or NULL: per-chunk
+ *                     expert histogram consumed by qmoe_moe_permute
+ * Logits are fp32 sums in one fixed order (see the kernel source), so expert
+ * indices are reproducible bit-for-bit.  Requires H % 256 == 0, H <= 4096,
+ * E % 32 == 0, E <= 256, 1 <= k <= min(E, 32).
+ * ---------------------------------------------------------------------- */
+#define QMOE_ROUTER_CHUNK 8
+QMOE_API int qmoe_router_topk(const void* x, const void* w_router, const float* bias, int64_t T,
+                     int64_t H, int64_t E, int64_t k, int normalize, float* logits,
+                     int32_t* topk_idx, float* topk_w, int32_t* chunk_hist, void* stream);
+
+/* ------------------------------------------------------------------------
+ * K2  expert-grouped permutation (histogram + scan + scatter + row gather).
+ * Produces the grouping the blockwise expert kernels consume
+ * (token_position_to_id / block_to_expert at qwen_with_nki.py:5872-5881),
+ * as contiguous per-expert row ranges instead of fixed 512-row blocks.
+ *
+ *   topk_idx, topk_w  from qmoe_router_topk
+ *   chunk_hist        from qmoe_router_topk (overwritten: becomes the
+ *                     per-chunk exclusive prefix)
+ *   x                 (T, H) bf16; gathered into x_perm if x_perm != NULL
+ *   counts   (E)      int32 out: rows per expert
+ *   offsets  (E+1)    int32 out: exclusive prefix of counts
+ *   row_token (T*k)   int32 out: source token of permuted row r
+ *   row_w    (T*k)    fp32 out: routing weight of permuted row r
+ *   slot_row (T, k)   int32 out: permuted row of (token, slot)
+ *   tiles   (1 + 3*qmoe_max_tiles(T*k, E)) int32 out: tile count, then the
+ *                     expert, first row and row count of every 128-row tile
+ *   x_perm  (T*k, H)  bf16 out or NULL
+ *   acc_zero (T, H)   fp32 or NULL: zero-filled here (the down-projection
+ *                     accumulator of the fused forward)
+ * Rows of one expert are ordered by ascending token id.  Bit-exact.
+ * ---------------------------------------------------------------------- */
+QMOE_API int64_t qmoe_max_tiles(int64_t rows, int64_t E);
+QMOE_API int qmoe_moe_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chunk_hist,
+                     const void* x, int64_t T, int64_t H, int64_t E, int64_t k,
+                     int32_t* counts, int32_t* offsets, int32_t* row_token, float* row_w,
+                     int32_t* slot_row, int32_t* tiles, void* x_perm, float* acc_zero,
+                     void* stream);
+
+/* ------------------------------------------------------------------------
+ * K3a  grouped GEMM, gate/up projection fused with SiLU(gate)*up.
+ * Replaces _nki_cte_moe_left_gate_up_kernel (qwen_with_nki.py:5341-5369) and
+ * the decode gate/up stage of _nki_batched_moe_kernel
+ * (qwen_with_nki.py:1874-1907).  TMA-fed tcgen05 MMA, fp32 accumulation in
+ * TMEM, fp32 SiLU*up, one bf16 cast.
+ *
+ *   x_perm   (R, H)       bf16 expert-grouped rows
+ *   w_gate_up (E, 2I, H)  bf16
+ *   tiles                 from qmoe_moe_permute (or qmoe_blockwise_prepare)
+ *   act      (R, I)       bf16 out: silu(x W_gate^T) * (x W_up^T)
+ * Requires H % 64 == 0, I % 128 == 0.
+ * ---------------------------------------------------------------------- */
+QMOE_API int qmoe_grouped_gemm_gateup_swiglu(const void* x_perm, const void* w_gate_up,
+                                    const int32_t* tiles, int64_t max_tiles, int64_t R,
+                                    int64_t H, int64_t I, int64_t E, void* act, void* stream);
+
+/* ------------------------------------------------------------------------
+ * K3b  grouped GEMM, down projection with the weighted combine in the
+ * epilogue: acc[row_dst[r], :] += row_w[r] * (act[r, :] W_down[e]^T).
+ * Replaces _nki_cte_moe_down_scatter_kernel (qwen_with_nki.py:4967-5040) and
+ * the decode down/affinity/reduce stage (qwen_with_nki.py:1938-1976).
+ *
+ *   act     (R, I)   bf16
+ *   w_down  (E, H, I) bf16
+ *   row_dst (R)      int32: destination row in acc; rows < 0 are skipped
+ *   row_w   (R)      fp32 weight
+ *   acc     (n_acc, H) fp32, accumulated into (fp32 atomic adds, so the
+ *                    order of the k contributions of a row is not fixed)
+ * Requires H % 128 == 0, I % 64 == 0.
+ * ---------------------------------------------------------------------- */
+QMOE_API int qmoe_grouped_gemm_down_combine(const void* act, const void* w_down, const int32_t* tiles,
+                                   int64_t max_tiles, const int32_t* row_dst,
+                                   const float* row_w, int64_t R, int64_t H, int64_t I,
+                                   int64_t E, float* acc, int64_t n_acc, void* stream);
+
+/* out (T, H) bf16 = bf16(acc + residual); residual (T, H) bf16 or NULL. */
+QMOE_API int qmoe_combine_finalize(const float* acc, const void* residual, int64_t T, int64_t H,
+                          void* out, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Fused sparse-MoE block forward: K1 -> K2 -> K3a -> K3b -> finalize.
+ * Replaces the module call self.mlp(hidden_states, padding_mask)[0]
+ * (qwen.py:429) for the routed-expert MoE of Qwen3.
+ *
+ *   out (T, H) bf16 = residual + MoE(x) (residual may be NULL)
+ *   topk_idx (T, k) int32 / topk_w (T, k) fp32 outputs may be NULL
+ *   workspace of qmoe_moe_forward_workspace_size() bytes, 256-byte aligned
+ * ---------------------------------------------------------------------- */
+QMOE_API size_t qmoe_moe_forward_workspace_size(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I);
+QMOE_API int qmoe_moe_forward(const void* x, const void* w_router, const float* router_bias,
+                     const void* w_gate_up, const void* w_down, const void* residual,
+                     int64_t T, int64_t H, int64_t E, int64_t k, int64_t I, int normalize,
+                     void* out, int32_t* topk_idx, float* topk_w, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QMOE_H_ */

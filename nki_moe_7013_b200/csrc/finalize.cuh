@@ -1,0 +1,37 @@
+// Combine finalisation: out = bf16(acc [+ residual]).  The residual add of the
+// decoder layer (qwen.py:430) is folded in so the layer writes its output once.
+#pragma once
+
+#include "common.cuh"
+
+namespace qmoe {
+
+__global__ void __launch_bounds__(256)
+    combine_finalize_kernel(const float* __restrict__ acc, const __nv_bfloat16* __restrict__ residual,
+                            __nv_bfloat16* __restrict__ out, long long n_vec8) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n_vec8;
+       i += (long long)gridDim.x * blockDim.x) {
+    const float4 a = reinterpret_cast<const float4*>(acc)[2 * i];
+    const float4 b = reinterpret_cast<const float4*>(acc)[2 * i + 1];
+    float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    if (residual) {
+      const uint4 r = reinterpret_cast<const uint4*>(residual)[i];
+      const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[2 * j] += bf16lo_to_f32(rw[j]);
+        v[2 * j + 1] += bf16hi_to_f32(rw[j]);
+      }
+    }
+    uint4 o;
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __nv_bfloat162 p = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+      ow[j] = *reinterpret_cast<const uint32_t*>(&p);
+    }
+    reinterpret_cast<uint4*>(out)[i] = o;
+  }
+}
+
+}  // namespace qmoe

@@ -1,0 +1,293 @@
+// K3a / K3b: persistent TMA + tcgen05 grouped GEMMs over expert tiles.
+//
+// Both kernels compute D = W_e[f0:f0+128, :] . X_tile^T ("swap AB"): the
+// 128-row MMA M dimension runs over output features of one expert (weights
+// are K-major in the (E, 2I, H) / (E, H, I) layout), and the MMA N dimension
+// runs over the tile's token rows (16..128, a multiple of 16).  Decode tiles
+// with a handful of tokens therefore cost one N=16 MMA column block while the
+// weights stream from HBM at full width, and prefill tiles use N up to 128.
+//
+// Work unit = (tile, feature block).  Units are assigned round-robin to a
+// persistent grid of one CTA per SM; consecutive CTAs share a tile so the
+// tile's activation rows are reused from L2.
+//
+// Warp roles (192 threads):
+//   warp 0      one lane issues TMA loads (weights evict-first, rows evict-last)
+//   warp 1      allocates TMEM; one lane issues tcgen05.mma and commits
+//   warps 2..5  epilogue: tcgen05.ld from TMEM (lane quadrant = warp % 4)
+// The smem ring has kStages stages guarded by full/empty mbarriers; the TMEM
+// accumulator is double-buffered so the epilogue of unit i overlaps the
+// main loop of unit i+1.  Every wait is bounded (see mbar_wait_bounded).
+//
+// K3a (gate/up) issues two MMAs per k-step into two accumulators -- gate rows
+// f0.. and up rows I+f0.. of the same expert -- so a thread's TMEM lane holds
+// gate and up of the same feature and SiLU(gate)*up needs no exchange.
+// K3b (down) multiplies each column (row r of the tile) by row_w[r] and adds
+// it into the fp32 accumulator row row_dst[r] (the weighted combine).
+#pragma once
+
+#include "common.cuh"
+
+namespace qmoe {
+
+constexpr int kBM = 128;       // MMA M: output features per unit
+constexpr int kBK = 64;        // k elements per stage (one 128-byte swizzle row)
+constexpr int kBNMax = 128;    // token rows per tile
+constexpr int kBoxRows = 16;   // rows per activation TMA box
+constexpr int kUmmaK = 16;     // k per tcgen05.mma (bf16)
+constexpr int kGemmThreads = 192;
+
+template <bool kGateUp>
+struct GemmCfg {
+  static constexpr int kATiles = kGateUp ? 2 : 1;
+  static constexpr int kABytes = kBM * kBK * 2;           // 16 KB
+  static constexpr int kBBytes = kBNMax * kBK * 2;        // 16 KB
+  static constexpr int kStageBytes = kATiles * kABytes + kBBytes;
+  static constexpr int kStages = kGateUp ? 4 : 6;
+  static constexpr int kAccCols = kGateUp ? 256 : 128;    // TMEM columns per accumulator buffer
+  static constexpr int kTmemCols = 2 * kAccCols;
+  static constexpr int kBarrierBytes = 256;
+  static constexpr int kSmemBytes = 1024 /*align slack*/ + kStages * kStageBytes + kBarrierBytes;
+};
+
+struct GemmArgs {
+  const int32_t* tiles;  // [0] = ntiles, then expert[max_tiles], row0[max_tiles], nrows[max_tiles]
+  int max_tiles;
+  int n_mtiles;          // feature blocks per tile
+  int num_kb;            // K / kBK
+  int a_rows_per_expert; // 2I (gate/up) or H (down)
+  int up_row_offset;     // I (gate/up only)
+  // gate/up epilogue
+  __nv_bfloat16* act;
+  int act_ld;
+  // down epilogue
+  const int32_t* row_dst;
+  const float* row_w;
+  float* acc;
+  int acc_ld;
+  int n_acc;
+};
+
+template <bool kGateUp>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
+  using C = GemmCfg<kGateUp>;
+  extern __shared__ uint8_t gemm_smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(gemm_smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* acc_full = empty + C::kStages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;       // [2]
+  uint64_t* drain = acc_empty + 2;          // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int ntiles = min(args.tiles[0], args.max_tiles);
+  const int total_units = ntiles * args.n_mtiles;
+  const int32_t* t_exp = args.tiles + 1;
+  const int32_t* t_row0 = t_exp + args.max_tiles;
+  const int32_t* t_rows = t_row0 + args.max_tiles;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_x = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0;       // stages holding a load issued by this thread
+      uint32_t issued_parity = 0;     // parity of that load's full-barrier phase
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < total_units; u += gridDim.x) {
+        const int tile = u / args.n_mtiles;
+        const int mt = u - tile * args.n_mtiles;
+        const int e = t_exp[tile];
+        const int row0 = t_row0[tile];
+        const int nb = (t_rows[tile] + kBoxRows - 1) / kBoxRows;
+        const int a_row = e * args.a_rows_per_expert + mt * kBM;
+        const uint32_t bytes = C::kATiles * C::kABytes + nb * kBoxRows * kBK * 2;
+        for (int kb = 0; kb < args.num_kb; ++kb) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, kDevErrWaitTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sb = stages + stage * C::kStageBytes;
+          mbar_arrive_expect_tx(&full[stage], bytes);
+          tma_load_2d_hint(sb, &tmA, kb * kBK, a_row, &full[stage], pol_w);
+          if (kGateUp)
+            tma_load_2d_hint(sb + C::kABytes, &tmA, kb * kBK, a_row + args.up_row_offset,
+                             &full[stage], pol_w);
+          uint8_t* bs = sb + C::kATiles * C::kABytes;
+          for (int b = 0; b < nb; ++b)
+            tma_load_2d_hint(bs + b * (kBoxRows * kBK * 2), &tmB, kb * kBK, row0 + b * kBoxRows,
+                             &full[stage], pol_x);
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Let every load this thread issued land before the CTA's smem goes away.
+        for (int s = 0; s < C::kStages; ++s) {
+          if ((issued_mask >> s) & 1u) {
+            const unsigned long long t0 = globaltimer_ns();
+            while (!mbar_try_wait(&full[s], (issued_parity >> s) & 1u)) {
+              if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < total_units; u += gridDim.x, ++local) {
+        const int tile = u / args.n_mtiles;
+        const int nb = (t_rows[tile] + kBoxRows - 1) / kBoxRows;
+        const uint32_t idesc = make_idesc_bf16(kBM, nb * kBoxRows);
+        const int buf = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait_bounded(&acc_empty[buf], acc_phase ^ 1u, abort_flag, kDevErrWaitTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_gate = tmem_base + buf * C::kAccCols;
+        const uint32_t d_up = d_gate + kBM;
+        for (int kb = 0; kb < args.num_kb; ++kb) {
+          if (!mbar_wait_bounded(&full[stage], phase, abort_flag, kDevErrWaitTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sb = smem_u32(stages + stage * C::kStageBytes);
+          const uint32_t bsb = sb + C::kATiles * C::kABytes;
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k) {
+            const uint32_t accum = (kb | k) != 0 ? 1u : 0u;
+            const uint64_t bdesc = make_sw128_desc(bsb + k * kUmmaK * 2);
+            umma_bf16(d_gate, make_sw128_desc(sb + k * kUmmaK * 2), bdesc, idesc, accum);
+            if (kGateUp)
+              umma_bf16(d_up, make_sw128_desc(sb + C::kABytes + k * kUmmaK * 2), bdesc, idesc,
+                        accum);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[buf]);
+      }
+      // Drain: every MMA issued above has completed once this barrier fires.
+      umma_commit(drain);
+      const unsigned long long t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain, 0)) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          record_device_error(kDevErrWaitTimeoutMma);
+          break;
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quad = warp & 3;
+    const int m = quad * 32 + lane;  // feature row inside the unit = TMEM lane
+    int local = 0;
+    for (int u = blockIdx.x; u < total_units; u += gridDim.x, ++local) {
+      const int tile = u / args.n_mtiles;
+      const int mt = u - tile * args.n_mtiles;
+      const int row0 = t_row0[tile];
+      const int nrows = t_rows[tile];
+      const int nb = (nrows + kBoxRows - 1) / kBoxRows;
+      const int buf = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait_bounded(&acc_full[buf], acc_phase, abort_flag, kDevErrWaitTimeoutEpilogue))
+        break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) + buf * C::kAccCols;
+      const int feat = mt * kBM + m;
+      for (int c = 0; c < nb; ++c) {
+        uint32_t v[16];
+        tmem_ld_32x32b_x16(taddr + c * 16, v);
+        if constexpr (kGateUp) {
+          uint32_t up[16];
+          tmem_ld_32x32b_x16(taddr + kBM + c * 16, up);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int n = c * 16 + i;
+            if (n < nrows) {
+              const float g = __uint_as_float(v[i]);
+              const float uval = __uint_as_float(up[i]);
+              const float h = g / (1.0f + __expf(-g)) * uval;
+              args.act[size_t(row0 + n) * args.act_ld + feat] = __float2bfloat16_rn(h);
+            }
+          }
+        } else {
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int n = c * 16 + i;
+            if (n < nrows) {
+              const int r = row0 + n;
+              const int dst = args.row_dst[r];
+              if (dst >= 0 && dst < args.n_acc)
+                atomicAdd(args.acc + size_t(dst) * args.acc_ld + feat,
+                          args.row_w[r] * __uint_as_float(v[i]));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+}  // namespace qmoe

@@ -1,0 +1,498 @@
+// C ABI of the Qwen3-MoE hot path (include/qmoe.h): host-side argument checks,
+// TMA descriptor encoding, workspace carving and kernel launches.
+//
+// One translation unit: the kernels live in the *.cuh files included below.
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+#include "finalize.cuh"
+#include "grouped_gemm.cuh"
+#include "permute.cuh"
+#include "router.cuh"
+
+// ---------------------------------------------------------------------------
+// host helpers
+// ---------------------------------------------------------------------------
+namespace qmoe_host {
+
+static thread_local std::string t_last_error;
+
+int set_error(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return status;
+}
+
+int check_launch(const char* what) {
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess)
+    return set_error(QMOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+  return QMOE_OK;
+}
+
+struct DeviceInfo {
+  int sms = 0;
+  int major = 0;
+  int minor = 0;
+  bool ok = false;
+};
+
+static constexpr int kMaxDevices = 64;
+static DeviceInfo g_dev[kMaxDevices];
+static std::once_flag g_dev_once[kMaxDevices];
+
+static int device_info(DeviceInfo** out) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return set_error(QMOE_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(err));
+  if (dev < 0 || dev >= kMaxDevices) return set_error(QMOE_ERR_DEVICE, "device ordinal %d out of range", dev);
+  std::call_once(g_dev_once[dev], [dev]() {
+    DeviceInfo& d = g_dev[dev];
+    if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return;
+    if (cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return;
+    if (cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) return;
+    d.ok = true;
+  });
+  DeviceInfo& d = g_dev[dev];
+  if (!d.ok) return set_error(QMOE_ERR_CUDA, "could not query device %d", dev);
+  if (d.major != 10 || d.minor != 0)
+    return set_error(QMOE_ERR_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a", dev,
+                     d.major, d.minor);
+  *out = &d;
+  return QMOE_OK;
+}
+
+int num_sms(int) {
+  DeviceInfo* d = nullptr;
+  if (device_info(&d) != QMOE_OK) return 0;
+  return d->sms;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeTiledFn g_encode = nullptr;
+static std::once_flag g_encode_once;
+
+static int get_encode(EncodeTiledFn* fn) {
+  std::call_once(g_encode_once, []() {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  if (!g_encode) return set_error(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  *fn = g_encode;
+  return QMOE_OK;
+}
+
+// 2D bf16 tensor map, row-major (outer, inner), 128-byte swizzle, box
+// (box_outer rows x 64 elements).  Out-of-range rows read as zero.
+static int make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                          uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn enc = nullptr;
+  int st = get_encode(&enc);
+  if (st != QMOE_OK) return st;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for %llux%llu box %ux%u",
+                     int(r), (unsigned long long)outer, (unsigned long long)inner, box_outer,
+                     box_inner);
+  return QMOE_OK;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <typename Kernel>
+static int set_smem(Kernel k, int bytes) {
+  cudaError_t err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (err != cudaSuccess)
+    return set_error(QMOE_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(err));
+  return QMOE_OK;
+}
+
+}  // namespace qmoe_host
+
+using namespace qmoe_host;
+
+#define QMOE_CHECK(expr)            \
+  do {                              \
+    int _st = (expr);               \
+    if (_st != QMOE_OK) return _st; \
+  } while (0)
+
+#define QMOE_REQUIRE(cond, status, ...)                   \
+  do {                                                    \
+    if (!(cond)) return set_error((status), __VA_ARGS__); \
+  } while (0)
+
+// ---------------------------------------------------------------------------
+// launches
+// ---------------------------------------------------------------------------
+namespace {
+
+int launch_router(const void* x, const void* w, const float* bias, int64_t T, int64_t H, int64_t E,
+                  int64_t k, int normalize, float* logits, int32_t* topk_idx, float* topk_w,
+                  int32_t* chunk_hist, cudaStream_t stream) {
+  const int G = int(H / 256);
+  const int nchunks = int((T + qmoe::kRouterChunk - 1) / qmoe::kRouterChunk);
+  const int smem = int(sizeof(float) * qmoe::kRouterChunk * (H + E));
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  const auto* wb = static_cast<const __nv_bfloat16*>(w);
+#define QMOE_ROUTER_CASE(GG)                                                                   \
+  case GG: {                                                                                   \
+    QMOE_CHECK(set_smem(qmoe::router_topk_kernel<GG>, smem));                                  \
+    qmoe::router_topk_kernel<GG><<<nchunks, qmoe::kRouterThreads, smem, stream>>>(            \
+        xb, wb, bias, int(T), int(E), int(k), normalize, logits, topk_idx, topk_w, chunk_hist); \
+    break;                                                                                     \
+  }
+  switch (G) {
+    QMOE_ROUTER_CASE(1)
+    QMOE_ROUTER_CASE(2)
+    QMOE_ROUTER_CASE(4)
+    QMOE_ROUTER_CASE(8)
+    QMOE_ROUTER_CASE(16)
+    default:
+      return set_error(QMOE_ERR_UNSUPPORTED_SHAPE, "router: H/256 = %d not in {1,2,4,8,16}", G);
+  }
+#undef QMOE_ROUTER_CASE
+  return check_launch("router_topk_kernel");
+}
+
+int check_router_args(const void* x, const void* w, int64_t T, int64_t H, int64_t E, int64_t k,
+                      const int32_t* topk_idx, const float* topk_w) {
+  QMOE_REQUIRE(x && w && topk_idx && topk_w, QMOE_ERR_INVALID_ARGUMENT, "router: null pointer");
+  QMOE_REQUIRE(T >= 0 && T < (int64_t(1) << 31) / 32, QMOE_ERR_INVALID_ARGUMENT, "router: bad T=%lld",
+               (long long)T);
+  QMOE_REQUIRE(H > 0 && H % 256 == 0 && H <= 4096, QMOE_ERR_UNSUPPORTED_SHAPE,
+               "router: H=%lld must be a multiple of 256 and <= 4096", (long long)H);
+  QMOE_REQUIRE(E >= 32 && E <= 256 && E % 32 == 0, QMOE_ERR_UNSUPPORTED_SHAPE,
+               "router: E=%lld must be a multiple of 32 in [32, 256]", (long long)E);
+  QMOE_REQUIRE(k >= 1 && k <= E && k <= 32, QMOE_ERR_INVALID_ARGUMENT, "router: k=%lld invalid",
+               (long long)k);
+  QMOE_REQUIRE(aligned16(x) && aligned16(w), QMOE_ERR_MISALIGNED, "router: x / w_router not 16-byte aligned");
+  return QMOE_OK;
+}
+
+int launch_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chunk_hist, const void* x,
+                   int64_t T, int64_t H, int64_t E, int64_t k, int32_t* counts, int32_t* offsets,
+                   int32_t* row_token, float* row_w, int32_t* slot_row, int32_t* tiles,
+                   void* x_perm, float* acc_zero, cudaStream_t stream) {
+  const int nchunks = int((T + qmoe::kRouterChunk - 1) / qmoe::kRouterChunk);
+  const int64_t max_tiles = qmoe_max_tiles(T * k, E);
+  qmoe::permute_scan_kernel<<<1, qmoe::kScanThreads, 0, stream>>>(chunk_hist, nchunks, int(E), counts,
+                                                                  offsets, tiles, int(max_tiles));
+  QMOE_CHECK(check_launch("permute_scan_kernel"));
+  if (nchunks > 0) {
+    qmoe::permute_scatter_kernel<<<nchunks, qmoe::kScatterThreads, 0, stream>>>(
+        topk_idx, topk_w, chunk_hist, offsets, static_cast<const __nv_bfloat16*>(x), int(T), int(H),
+        int(E), int(k), row_token, row_w, slot_row, static_cast<__nv_bfloat16*>(x_perm), acc_zero);
+    QMOE_CHECK(check_launch("permute_scatter_kernel"));
+  }
+  return QMOE_OK;
+}
+
+int launch_gemm_gateup(const void* x_perm, const void* w_gate_up, const int32_t* tiles,
+                       int64_t max_tiles, int64_t R, int64_t H, int64_t I, int64_t E, void* act,
+                       cudaStream_t stream) {
+  using C = qmoe::GemmCfg<true>;
+  CUtensorMap tmA, tmB;
+  QMOE_CHECK(make_tmap_bf16(&tmA, w_gate_up, uint64_t(H), uint64_t(E * 2 * I), qmoe::kBK, qmoe::kBM));
+  QMOE_CHECK(make_tmap_bf16(&tmB, x_perm, uint64_t(H), uint64_t(R), qmoe::kBK, qmoe::kBoxRows));
+  qmoe::GemmArgs a{};
+  a.tiles = tiles;
+  a.max_tiles = int(max_tiles);
+  a.n_mtiles = int(I / qmoe::kBM);
+  a.num_kb = int(H / qmoe::kBK);
+  a.a_rows_per_expert = int(2 * I);
+  a.up_row_offset = int(I);
+  a.act = static_cast<__nv_bfloat16*>(act);
+  a.act_ld = int(I);
+  const int64_t units = max_tiles * a.n_mtiles;
+  const int grid = int(std::min<int64_t>(units, num_sms(0)));
+  if (grid <= 0) return QMOE_OK;
+  QMOE_CHECK(set_smem(qmoe::grouped_gemm_kernel<true>, C::kSmemBytes));
+  qmoe::grouped_gemm_kernel<true><<<grid, qmoe::kGemmThreads, C::kSmemBytes, stream>>>(tmA, tmB, a);
+  return check_launch("grouped_gemm_kernel<gate_up>");
+}
+
+int launch_gemm_down(const void* act, const void* w_down, const int32_t* tiles, int64_t max_tiles,
+                     const int32_t* row_dst, const float* row_w, int64_t R, int64_t H, int64_t I,
+                     int64_t E, float* acc, int64_t n_acc, cudaStream_t stream) {
+  using C = qmoe::GemmCfg<false>;
+  CUtensorMap tmA, tmB;
+  QMOE_CHECK(make_tmap_bf16(&tmA, w_down, uint64_t(I), uint64_t(E * H), qmoe::kBK, qmoe::kBM));
+  QMOE_CHECK(make_tmap_bf16(&tmB, act, uint64_t(I), uint64_t(R), qmoe::kBK, qmoe::kBoxRows));
+  qmoe::GemmArgs a{};
+  a.tiles = tiles;
+  a.max_tiles = int(max_tiles);
+  a.n_mtiles = int(H / qmoe::kBM);
+  a.num_kb = int(I / qmoe::kBK);
+  a.a_rows_per_expert = int(H);
+  a.up_row_offset = 0;
+  a.row_dst = row_dst;
+  a.row_w = row_w;
+  a.acc = acc;
+  a.acc_ld = int(H);
+  a.n_acc = int(n_acc);
+  const int64_t units = max_tiles * a.n_mtiles;
+  const int grid = int(std::min<int64_t>(units, num_sms(0)));
+  if (grid <= 0) return QMOE_OK;
+  QMOE_CHECK(set_smem(qmoe::grouped_gemm_kernel<false>, C::kSmemBytes));
+  qmoe::grouped_gemm_kernel<false><<<grid, qmoe::kGemmThreads, C::kSmemBytes, stream>>>(tmA, tmB, a);
+  return check_launch("grouped_gemm_kernel<down>");
+}
+
+int launch_finalize(const float* acc, const void* residual, int64_t T, int64_t H, void* out,
+                    cudaStream_t stream) {
+  const long long n8 = (long long)(T * H / 8);
+  if (n8 == 0) return QMOE_OK;
+  const int grid = int(std::min<long long>((n8 + 255) / 256, (long long)num_sms(0) * 8));
+  qmoe::combine_finalize_kernel<<<grid, 256, 0, stream>>>(
+      acc, static_cast<const __nv_bfloat16*>(residual), static_cast<__nv_bfloat16*>(out), n8);
+  return check_launch("combine_finalize_kernel");
+}
+
+// Workspace carving for the fused forward.
+struct FwdLayout {
+  size_t chunk_hist, counts, offsets, row_token, row_w, slot_row, tiles, topk_idx, topk_w, x_perm,
+      act, acc, total;
+};
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+FwdLayout fwd_layout(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I) {
+  FwdLayout L{};
+  const int64_t R = T * k;
+  const int64_t nchunks = (T + qmoe::kRouterChunk - 1) / qmoe::kRouterChunk;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    size_t at = o;
+    o = align256(o + bytes);
+    return at;
+  };
+  L.chunk_hist = take(sizeof(int32_t) * size_t(nchunks * E));
+  L.counts = take(sizeof(int32_t) * size_t(E));
+  L.offsets = take(sizeof(int32_t) * size_t(E + 1));
+  L.row_token = take(sizeof(int32_t) * size_t(R));
+  L.row_w = take(sizeof(float) * size_t(R));
+  L.slot_row = take(sizeof(int32_t) * size_t(R));
+  L.tiles = take(sizeof(int32_t) * size_t(1 + 3 * qmoe_max_tiles(R, E)));
+  L.topk_idx = take(sizeof(int32_t) * size_t(R));
+  L.topk_w = take(sizeof(float) * size_t(R));
+  L.x_perm = take(2 * size_t(R * H));
+  L.act = take(2 * size_t(R * I));
+  L.acc = take(sizeof(float) * size_t(T * H));
+  L.total = o;
+  return L;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+extern "C" {
+
+int qmoe_version(void) { return 100; }
+
+const char* qmoe_status_string(int status) {
+  switch (status) {
+    case QMOE_OK: return "ok";
+    case QMOE_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case QMOE_ERR_UNSUPPORTED_SHAPE: return "unsupported shape";
+    case QMOE_ERR_MISALIGNED: return "misaligned pointer";
+    case QMOE_ERR_WORKSPACE_TOO_SMALL: return "workspace too small";
+    case QMOE_ERR_CUDA: return "CUDA error";
+    case QMOE_ERR_DEVICE: return "unsupported device";
+    default: return "unknown status";
+  }
+}
+
+const char* qmoe_last_error(void) { return t_last_error.c_str(); }
+
+int qmoe_device_error(int clear, unsigned int* code_out) {
+  QMOE_REQUIRE(code_out, QMOE_ERR_INVALID_ARGUMENT, "device_error: null output");
+  cudaError_t err = cudaDeviceSynchronize();
+  if (err != cudaSuccess) return set_error(QMOE_ERR_CUDA, "cudaDeviceSynchronize: %s", cudaGetErrorString(err));
+  unsigned int v = 0;
+  err = cudaMemcpyFromSymbol(&v, qmoe::g_device_error, sizeof(v));
+  if (err != cudaSuccess) return set_error(QMOE_ERR_CUDA, "read device error: %s", cudaGetErrorString(err));
+  if (clear) {
+    unsigned int z = 0;
+    err = cudaMemcpyToSymbol(qmoe::g_device_error, &z, sizeof(z));
+    if (err != cudaSuccess) return set_error(QMOE_ERR_CUDA, "clear device error: %s", cudaGetErrorString(err));
+  }
+  *code_out = v;
+  return QMOE_OK;
+}
+
+int64_t qmoe_max_tiles(int64_t rows, int64_t E) {
+  if (rows < 0 || E < 0) return 0;
+  return E + rows / qmoe::kTileRows + 1;
+}
+
+int qmoe_router_topk(const void* x, const void* w_router, const float* bias, int64_t T, int64_t H,
+                     int64_t E, int64_t k, int normalize, float* logits, int32_t* topk_idx,
+                     float* topk_w, int32_t* chunk_hist, void* stream) {
+  QMOE_CHECK(check_router_args(x, w_router, T, H, E, k, topk_idx, topk_w));
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  if (T == 0) return QMOE_OK;
+  return launch_router(x, w_router, bias, T, H, E, k, normalize, logits, topk_idx, topk_w,
+                       chunk_hist, static_cast<cudaStream_t>(stream));
+}
+
+int qmoe_moe_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chunk_hist,
+                     const void* x, int64_t T, int64_t H, int64_t E, int64_t k, int32_t* counts,
+                     int32_t* offsets, int32_t* row_token, float* row_w, int32_t* slot_row,
+                     int32_t* tiles, void* x_perm, float* acc_zero, void* stream) {
+  QMOE_REQUIRE(topk_idx && topk_w && chunk_hist && counts && offsets && row_token && row_w &&
+                   slot_row && tiles,
+               QMOE_ERR_INVALID_ARGUMENT, "permute: null pointer");
+  QMOE_REQUIRE(T >= 0 && T < (int64_t(1) << 31) / 32, QMOE_ERR_INVALID_ARGUMENT, "permute: bad T");
+  QMOE_REQUIRE(E >= 1 && E <= 256, QMOE_ERR_UNSUPPORTED_SHAPE, "permute: E=%lld not in [1, 256]",
+               (long long)E);
+  QMOE_REQUIRE(k >= 1 && k <= E && k <= 32, QMOE_ERR_INVALID_ARGUMENT, "permute: k=%lld invalid",
+               (long long)k);
+  if (x_perm || acc_zero) {
+    QMOE_REQUIRE(H > 0 && H % 8 == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "permute: H must be a multiple of 8");
+    QMOE_REQUIRE(!x_perm || (x && aligned16(x) && aligned16(x_perm)), QMOE_ERR_MISALIGNED,
+                 "permute: x / x_perm null or not 16-byte aligned");
+    QMOE_REQUIRE(!acc_zero || aligned16(acc_zero), QMOE_ERR_MISALIGNED, "permute: acc not aligned");
+  }
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  return launch_permute(topk_idx, topk_w, chunk_hist, x, T, H, E, k, counts, offsets, row_token,
+                        row_w, slot_row, tiles, x_perm, acc_zero, static_cast<cudaStream_t>(stream));
+}
+
+int qmoe_grouped_gemm_gateup_swiglu(const void* x_perm, const void* w_gate_up,
+                                    const int32_t* tiles, int64_t max_tiles, int64_t R, int64_t H,
+                                    int64_t I, int64_t E, void* act, void* stream) {
+  QMOE_REQUIRE(x_perm && w_gate_up && tiles && act, QMOE_ERR_INVALID_ARGUMENT, "gate_up: null pointer");
+  QMOE_REQUIRE(R >= 0 && R < (int64_t(1) << 31), QMOE_ERR_INVALID_ARGUMENT, "gate_up: bad R");
+  QMOE_REQUIRE(H > 0 && H % qmoe::kBK == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "gate_up: H %% 64 != 0");
+  QMOE_REQUIRE(I > 0 && I % qmoe::kBM == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "gate_up: I %% 128 != 0");
+  QMOE_REQUIRE(E > 0 && E * 2 * I < (int64_t(1) << 31), QMOE_ERR_UNSUPPORTED_SHAPE, "gate_up: E too large");
+  QMOE_REQUIRE(max_tiles >= 0 && max_tiles < (int64_t(1) << 24), QMOE_ERR_INVALID_ARGUMENT, "gate_up: bad max_tiles");
+  QMOE_REQUIRE(aligned16(x_perm) && aligned16(w_gate_up) && aligned16(act), QMOE_ERR_MISALIGNED,
+               "gate_up: pointers must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  if (R == 0) return QMOE_OK;
+  return launch_gemm_gateup(x_perm, w_gate_up, tiles, max_tiles, R, H, I, E, act,
+                            static_cast<cudaStream_t>(stream));
+}
+
+int qmoe_grouped_gemm_down_combine(const void* act, const void* w_down, const int32_t* tiles,
+                                   int64_t max_tiles, const int32_t* row_dst, const float* row_w,
+                                   int64_t R, int64_t H, int64_t I, int64_t E, float* acc,
+                                   int64_t n_acc, void* stream) {
+  QMOE_REQUIRE(act && w_down && tiles && row_dst && row_w && acc, QMOE_ERR_INVALID_ARGUMENT,
+               "down: null pointer");
+  QMOE_REQUIRE(R >= 0 && R < (int64_t(1) << 31), QMOE_ERR_INVALID_ARGUMENT, "down: bad R");
+  QMOE_REQUIRE(H > 0 && H % qmoe::kBM == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "down: H %% 128 != 0");
+  QMOE_REQUIRE(I > 0 && I % qmoe::kBK == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "down: I %% 64 != 0");
+  QMOE_REQUIRE(E > 0 && E * H < (int64_t(1) << 31), QMOE_ERR_UNSUPPORTED_SHAPE, "down: E too large");
+  QMOE_REQUIRE(n_acc >= 0 && n_acc * H < (int64_t(1) << 40), QMOE_ERR_INVALID_ARGUMENT, "down: bad n_acc");
+  QMOE_REQUIRE(max_tiles >= 0 && max_tiles < (int64_t(1) << 24), QMOE_ERR_INVALID_ARGUMENT, "down: bad max_tiles");
+  QMOE_REQUIRE(aligned16(act) && aligned16(w_down), QMOE_ERR_MISALIGNED, "down: pointers must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  if (R == 0) return QMOE_OK;
+  return launch_gemm_down(act, w_down, tiles, max_tiles, row_dst, row_w, R, H, I, E, acc, n_acc,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int qmoe_combine_finalize(const float* acc, const void* residual, int64_t T, int64_t H, void* out,
+                          void* stream) {
+  QMOE_REQUIRE(acc && out, QMOE_ERR_INVALID_ARGUMENT, "finalize: null pointer");
+  QMOE_REQUIRE(T >= 0 && H > 0 && H % 8 == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "finalize: H %% 8 != 0");
+  QMOE_REQUIRE(aligned16(acc) && aligned16(out) && (!residual || aligned16(residual)),
+               QMOE_ERR_MISALIGNED, "finalize: pointers must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  return launch_finalize(acc, residual, T, H, out, static_cast<cudaStream_t>(stream));
+}
+
+size_t qmoe_moe_forward_workspace_size(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I) {
+  if (T < 0 || H <= 0 || E <= 0 || k <= 0 || I <= 0) return 0;
+  return fwd_layout(T, H, E, k, I).total;
+}
+
+int qmoe_moe_forward(const void* x, const void* w_router, const float* router_bias,
+                     const void* w_gate_up, const void* w_down, const void* residual, int64_t T,
+                     int64_t H, int64_t E, int64_t k, int64_t I, int normalize, void* out,
+                     int32_t* topk_idx, float* topk_w, void* workspace, size_t workspace_bytes,
+                     void* stream) {
+  QMOE_REQUIRE(x && w_router && w_gate_up && w_down && out, QMOE_ERR_INVALID_ARGUMENT,
+               "moe_forward: null pointer");
+  QMOE_REQUIRE(T >= 0 && T < (int64_t(1) << 31) / 32, QMOE_ERR_INVALID_ARGUMENT, "moe_forward: bad T");
+  QMOE_REQUIRE(H > 0 && H % 256 == 0 && H <= 4096, QMOE_ERR_UNSUPPORTED_SHAPE,
+               "moe_forward: H=%lld must be a multiple of 256 and <= 4096", (long long)H);
+  QMOE_REQUIRE(E >= 32 && E <= 256 && E % 32 == 0, QMOE_ERR_UNSUPPORTED_SHAPE,
+               "moe_forward: E=%lld must be a multiple of 32 in [32, 256]", (long long)E);
+  QMOE_REQUIRE(k >= 1 && k <= E && k <= 32, QMOE_ERR_INVALID_ARGUMENT, "moe_forward: k invalid");
+  QMOE_REQUIRE(I > 0 && I % qmoe::kBM == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "moe_forward: I %% 128 != 0");
+  QMOE_REQUIRE(E * 2 * I < (int64_t(1) << 31) && E * H < (int64_t(1) << 31), QMOE_ERR_UNSUPPORTED_SHAPE,
+               "moe_forward: weights too large");
+  QMOE_REQUIRE(aligned16(x) && aligned16(w_router) && aligned16(w_gate_up) && aligned16(w_down) &&
+                   aligned16(out) && (!residual || aligned16(residual)),
+               QMOE_ERR_MISALIGNED, "moe_forward: pointers must be 16-byte aligned");
+  const FwdLayout L = fwd_layout(T, H, E, k, I);
+  QMOE_REQUIRE(workspace || L.total == 0, QMOE_ERR_INVALID_ARGUMENT, "moe_forward: null workspace");
+  QMOE_REQUIRE(workspace_bytes >= L.total, QMOE_ERR_WORKSPACE_TOO_SMALL,
+               "moe_forward: workspace %zu < required %zu bytes", workspace_bytes, L.total);
+  QMOE_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255u) == 0, QMOE_ERR_MISALIGNED,
+               "moe_forward: workspace must be 256-byte aligned");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  if (T == 0) return QMOE_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int32_t* chunk_hist = reinterpret_cast<int32_t*>(ws + L.chunk_hist);
+  int32_t* counts = reinterpret_cast<int32_t*>(ws + L.counts);
+  int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
+  int32_t* row_token = reinterpret_cast<int32_t*>(ws + L.row_token);
+  float* row_w = reinterpret_cast<float*>(ws + L.row_w);
+  int32_t* slot_row = reinterpret_cast<int32_t*>(ws + L.slot_row);
+  int32_t* tiles = reinterpret_cast<int32_t*>(ws + L.tiles);
+  int32_t* idx = topk_idx ? topk_idx : reinterpret_cast<int32_t*>(ws + L.topk_idx);
+  float* tw = topk_w ? topk_w : reinterpret_cast<float*>(ws + L.topk_w);
+  void* x_perm = ws + L.x_perm;
+  void* act = ws + L.act;
+  float* acc = reinterpret_cast<float*>(ws + L.acc);
+  const int64_t R = T * k;
+  const int64_t max_tiles = qmoe_max_tiles(R, E);
+
+  QMOE_CHECK(launch_router(x, w_router, router_bias, T, H, E, k, normalize, nullptr, idx, tw,
+                           chunk_hist, s));
+  QMOE_CHECK(launch_permute(idx, tw, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w,
+                            slot_row, tiles, x_perm, acc, s));
+  QMOE_CHECK(launch_gemm_gateup(x_perm, w_gate_up, tiles, max_tiles, R, H, I, E, act, s));
+  QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s));
+  return launch_finalize(acc, residual, T, H, out, s);
+}
+
+}  // extern "C"

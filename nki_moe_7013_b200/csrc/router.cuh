@@ -1,0 +1,185 @@
+// K1: fused router -- fp32 logits in a fixed reduction order, softmax,
+// warp-shuffle top-k (ties -> lower expert index), L1 renormalisation, and the
+// per-chunk expert histogram that the permutation consumes.
+//
+// Reference semantics: qwen.py:260-269 (fp32 router, softmax,
+// normalize_top_k_affinities), qwen_with_nki.py:2398-2405 (affinity gather,
+// F.normalize(p=1)).
+//
+// Canonical logit order (restated exactly by the CPU oracle, so logits and
+// expert indices are bit-exact): H is cut into 256-element groups; lane l of a
+// warp owns elements [8l, 8l+8) of every group and accumulates them
+// group-major from +0.0f with fmaf (bf16*bf16 products are exact in fp32, so
+// each step rounds once); the 32 lane sums are folded by an xor butterfly
+// (16, 8, 4, 2, 1).
+#pragma once
+
+#include "common.cuh"
+
+namespace qmoe {
+
+constexpr int kRouterChunk = QMOE_ROUTER_CHUNK;  // tokens per CTA (= histogram chunk)
+constexpr int kRouterThreads = 256;                // 8 warps
+static_assert(kRouterChunk == kRouterThreads / 32, "one warp per token in the top-k phase");
+
+template <int G>  // G = H / 256
+__global__ void __launch_bounds__(kRouterThreads, 1)
+    router_topk_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                       const float* __restrict__ bias, int T, int E, int k, int normalize,
+                       float* __restrict__ logits_out, int32_t* __restrict__ topk_idx,
+                       float* __restrict__ topk_w, int32_t* __restrict__ chunk_hist) {
+  constexpr int H = G * 256;
+  extern __shared__ __align__(16) float router_smem[];
+  float* xs = router_smem;                        // [kRouterChunk][H]
+  float* ls = router_smem + kRouterChunk * H;     // [kRouterChunk][E]
+  __shared__ int hist[256];
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int t0 = blockIdx.x * kRouterChunk;
+  const int nt = min(kRouterChunk, T - t0);
+
+  // Stage the chunk's activations in shared memory as fp32.
+  for (int i = threadIdx.x; i < kRouterChunk * (H / 8); i += kRouterThreads) {
+    const int t = i / (H / 8);
+    const int c = (i % (H / 8)) * 8;
+    float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
+    if (t < nt) {
+      const uint4 v = *reinterpret_cast<const uint4*>(x + size_t(t0 + t) * H + c);
+      lo = make_float4(bf16lo_to_f32(v.x), bf16hi_to_f32(v.x), bf16lo_to_f32(v.y),
+                       bf16hi_to_f32(v.y));
+      hi = make_float4(bf16lo_to_f32(v.z), bf16hi_to_f32(v.z), bf16lo_to_f32(v.w),
+                       bf16hi_to_f32(v.w));
+    }
+    *reinterpret_cast<float4*>(xs + t * H + c) = lo;
+    *reinterpret_cast<float4*>(xs + t * H + c + 4) = hi;
+  }
+  for (int i = threadIdx.x; i < 256; i += kRouterThreads) hist[i] = 0;
+  __syncthreads();
+
+  // Logits: warp w handles experts w, w+8, ...; the lane keeps its slice of the
+  // expert row in registers and reuses it for every token of the chunk.
+  for (int e = warp; e < E; e += kRouterThreads / 32) {
+    float wr[G * 8];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(w + size_t(e) * H + 256 * g + 8 * lane));
+      wr[8 * g + 0] = bf16lo_to_f32(v.x);
+      wr[8 * g + 1] = bf16hi_to_f32(v.x);
+      wr[8 * g + 2] = bf16lo_to_f32(v.y);
+      wr[8 * g + 3] = bf16hi_to_f32(v.y);
+      wr[8 * g + 4] = bf16lo_to_f32(v.z);
+      wr[8 * g + 5] = bf16hi_to_f32(v.z);
+      wr[8 * g + 6] = bf16lo_to_f32(v.w);
+      wr[8 * g + 7] = bf16hi_to_f32(v.w);
+    }
+    const float be = bias ? bias[e] : 0.f;
+    for (int t = 0; t < nt; ++t) {
+      const float* xr = xs + t * H + 8 * lane;
+      float acc = 0.f;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float4 a = *reinterpret_cast<const float4*>(xr + 256 * g);
+        const float4 b = *reinterpret_cast<const float4*>(xr + 256 * g + 4);
+        acc = fmaf(a.x, wr[8 * g + 0], acc);
+        acc = fmaf(a.y, wr[8 * g + 1], acc);
+        acc = fmaf(a.z, wr[8 * g + 2], acc);
+        acc = fmaf(a.w, wr[8 * g + 3], acc);
+        acc = fmaf(b.x, wr[8 * g + 4], acc);
+        acc = fmaf(b.y, wr[8 * g + 5], acc);
+        acc = fmaf(b.z, wr[8 * g + 6], acc);
+        acc = fmaf(b.w, wr[8 * g + 7], acc);
+      }
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, off);
+      if (lane == 0) ls[t * E + e] = bias ? __fadd_rn(acc, be) : acc;
+    }
+  }
+  __syncthreads();
+
+  // Softmax + top-k: one warp per token; lane holds experts lane + 32*i.
+  const int t = warp;
+  if (t < nt) {
+    const int tok = t0 + t;
+    const int per_lane = E / 32;  // <= 8
+    float lv[8];
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      lv[i] = (i < per_lane) ? ls[t * E + lane + 32 * i] : -INFINITY;
+      m = fmaxf(m, lv[i]);
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+    float ex[8];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      ex[i] = (i < per_lane) ? expf(lv[i] - m) : 0.f;
+      s += ex[i];
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, off);
+    const float inv_s = 1.0f / s;
+
+    if (logits_out) {
+      for (int i = 0; i < per_lane; ++i) logits_out[size_t(tok) * E + lane + 32 * i] = lv[i];
+    }
+
+    unsigned taken = 0u;  // bit i: expert lane + 32*i already chosen
+    float chosen_p = 0.f;  // lane j (< k) keeps the probability of pick j
+    int chosen_e = 0;
+    for (int j = 0; j < k; ++j) {
+      // best remaining candidate of this lane: larger logit, then lower index
+      float bv = -INFINITY;
+      int be = 0x7FFFFFFF;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (i < per_lane && !((taken >> i) & 1u)) {
+          const int ei = lane + 32 * i;
+          if (lv[i] > bv || (lv[i] == bv && ei < be)) {
+            bv = lv[i];
+            be = ei;
+          }
+        }
+      }
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, off);
+        const int oe = __shfl_xor_sync(0xFFFFFFFFu, be, off);
+        if (ov > bv || (ov == bv && oe < be)) {
+          bv = ov;
+          be = oe;
+        }
+      }
+      if ((be & 31) == lane) taken |= 1u << (be >> 5);
+      const int owner = be & 31;
+      // probability of the winner, read from its owning lane
+      float mine = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (lane + 32 * i == be) mine = ex[i] * inv_s;
+      const float p = __shfl_sync(0xFFFFFFFFu, mine, owner);
+      if (lane == j) {
+        chosen_p = p;
+        chosen_e = be;
+      }
+    }
+    // L1 renormalisation over the k picks, summed in pick order.
+    float denom = 0.f;
+    for (int j = 0; j < k; ++j) denom += __shfl_sync(0xFFFFFFFFu, chosen_p, j);
+    if (lane < k) {
+      const float wv = normalize ? chosen_p / fmaxf(denom, 1e-12f) : chosen_p;
+      topk_idx[size_t(tok) * k + lane] = chosen_e;
+      topk_w[size_t(tok) * k + lane] = wv;
+      atomicAdd(&hist[chosen_e], 1);
+    }
+  }
+  if (chunk_hist) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += kRouterThreads)
+      chunk_hist[size_t(blockIdx.x) * E + e] = hist[e];
+  }
+}
+
+}  // namespace qmoe

@@ -1,0 +1,202 @@
+"""torch-facing wrappers of the C ABI (one function per qmoe_* entry point).
+
+Every wrapper checks dtype / device / contiguity, allocates outputs with the
+torch caching allocator, passes raw pointers plus the current CUDA stream to
+the library, and raises ``QmoeError`` on a non-zero status.  Nothing here
+computes on the CPU.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _C
+
+ROUTER_CHUNK = 8  # QMOE_ROUTER_CHUNK
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(dev: torch.device):
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _need(t: torch.Tensor, name: str, dtype=None, dim=None):
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a tensor")
+    if t.device.type != "cuda":
+        raise ValueError(f"{name} must be a CUDA tensor (got {t.device}); there is no CPU path")
+    if dtype is not None and t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype} (got {t.dtype})")
+    if dim is not None and t.dim() != dim:
+        raise ValueError(f"{name} must have {dim} dims (got shape {tuple(t.shape)})")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return t
+
+
+def max_tiles(rows: int, num_experts: int) -> int:
+    return int(_C.lib().qmoe_max_tiles(rows, num_experts))
+
+
+def router_topk(x: torch.Tensor, w_router: torch.Tensor, k: int, normalize: bool = True,
+                bias: Optional[torch.Tensor] = None, return_logits: bool = False,
+                return_hist: bool = False):
+    """K1.  Returns (topk_idx int32 (T,k), topk_w fp32 (T,k)[, logits fp32 (T,E)][, chunk_hist])."""
+    _need(x, "x", torch.bfloat16, 2)
+    _need(w_router, "w_router", torch.bfloat16, 2)
+    T, H = x.shape
+    E = w_router.shape[0]
+    if bias is not None:
+        _need(bias, "bias", torch.float32, 1)
+    dev = x.device
+    idx = torch.empty((T, k), dtype=torch.int32, device=dev)
+    w = torch.empty((T, k), dtype=torch.float32, device=dev)
+    logits = torch.empty((T, E), dtype=torch.float32, device=dev) if return_logits else None
+    hist = (torch.empty(((T + ROUTER_CHUNK - 1) // ROUTER_CHUNK, E), dtype=torch.int32, device=dev)
+            if return_hist else None)
+    with torch.cuda.device(dev):
+        _C.check(_C.lib().qmoe_router_topk(
+            _ptr(x), _ptr(w_router), _ptr(bias), T, H, E, k, 1 if normalize else 0,
+            _ptr(logits), _ptr(idx), _ptr(w), _ptr(hist), _stream(dev)), "qmoe_router_topk")
+    out = [idx, w]
+    if return_logits:
+        out.append(logits)
+    if return_hist:
+        out.append(hist)
+    return tuple(out)
+
+
+def moe_permute(topk_idx: torch.Tensor, topk_w: torch.Tensor, chunk_hist: torch.Tensor,
+                num_experts: int, x: Optional[torch.Tensor] = None, gather: bool = True,
+                acc_zero: Optional[torch.Tensor] = None):
+    """K2.  ``chunk_hist`` is overwritten.  Returns a dict of device tensors."""
+    _need(topk_idx, "topk_idx", torch.int32, 2)
+    _need(topk_w, "topk_w", torch.float32, 2)
+    _need(chunk_hist, "chunk_hist", torch.int32, 2)
+    T, k = topk_idx.shape
+    E = num_experts
+    R = T * k
+    dev = topk_idx.device
+    H = 0
+    x_perm = None
+    if x is not None:
+        _need(x, "x", torch.bfloat16, 2)
+        H = x.shape[1]
+        if gather:
+            x_perm = torch.empty((R, H), dtype=torch.bfloat16, device=dev)
+    if acc_zero is not None:
+        _need(acc_zero, "acc_zero", torch.float32, 2)
+        H = acc_zero.shape[1]
+    mt = max_tiles(R, E)
+    counts = torch.empty(E, dtype=torch.int32, device=dev)
+    offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    row_token = torch.empty(R, dtype=torch.int32, device=dev)
+    row_w = torch.empty(R, dtype=torch.float32, device=dev)
+    slot_row = torch.empty((T, k), dtype=torch.int32, device=dev)
+    tiles = torch.empty(1 + 3 * mt, dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        _C.check(_C.lib().qmoe_moe_permute(
+            _ptr(topk_idx), _ptr(topk_w), _ptr(chunk_hist), _ptr(x), T, H, E, k,
+            _ptr(counts), _ptr(offsets), _ptr(row_token), _ptr(row_w), _ptr(slot_row),
+            _ptr(tiles), _ptr(x_perm), _ptr(acc_zero), _stream(dev)), "qmoe_moe_permute")
+    return dict(counts=counts, offsets=offsets, row_token=row_token, row_w=row_w,
+                slot_row=slot_row, tiles=tiles, max_tiles=mt, x_perm=x_perm)
+
+
+def grouped_gemm_gateup_swiglu(x_perm: torch.Tensor, w_gate_up: torch.Tensor, tiles: torch.Tensor,
+                               max_tiles_: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """K3a.  x_perm (R,H) bf16, w_gate_up (E,2I,H) bf16 -> act (R,I) bf16."""
+    _need(x_perm, "x_perm", torch.bfloat16, 2)
+    _need(w_gate_up, "w_gate_up", torch.bfloat16, 3)
+    _need(tiles, "tiles", torch.int32, 1)
+    R, H = x_perm.shape
+    E, I2, H2 = w_gate_up.shape
+    if H2 != H or I2 % 2:
+        raise ValueError("w_gate_up must be (E, 2I, H) matching x_perm")
+    I = I2 // 2
+    dev = x_perm.device
+    act = out if out is not None else torch.empty((R, I), dtype=torch.bfloat16, device=dev)
+    with torch.cuda.device(dev):
+        _C.check(_C.lib().qmoe_grouped_gemm_gateup_swiglu(
+            _ptr(x_perm), _ptr(w_gate_up), _ptr(tiles), max_tiles_, R, H, I, E, _ptr(act),
+            _stream(dev)), "qmoe_grouped_gemm_gateup_swiglu")
+    return act
+
+
+def grouped_gemm_down_combine(act: torch.Tensor, w_down: torch.Tensor, tiles: torch.Tensor,
+                              max_tiles_: int, row_dst: torch.Tensor, row_w: torch.Tensor,
+                              acc: torch.Tensor) -> torch.Tensor:
+    """K3b.  acc[row_dst[r]] += row_w[r] * act[r] @ W_down[e]^T (fp32, in place)."""
+    _need(act, "act", torch.bfloat16, 2)
+    _need(w_down, "w_down", torch.bfloat16, 3)
+    _need(tiles, "tiles", torch.int32, 1)
+    _need(row_dst, "row_dst", torch.int32, 1)
+    _need(row_w, "row_w", torch.float32, 1)
+    _need(acc, "acc", torch.float32, 2)
+    R, I = act.shape
+    E, H, I2 = w_down.shape
+    if I2 != I or acc.shape[1] != H:
+        raise ValueError("w_down must be (E, H, I) matching act and acc")
+    dev = act.device
+    with torch.cuda.device(dev):
+        _C.check(_C.lib().qmoe_grouped_gemm_down_combine(
+            _ptr(act), _ptr(w_down), _ptr(tiles), max_tiles_, _ptr(row_dst), _ptr(row_w),
+            R, H, I, E, _ptr(acc), acc.shape[0], _stream(dev)), "qmoe_grouped_gemm_down_combine")
+    return acc
+
+
+def combine_finalize(acc: torch.Tensor, residual: Optional[torch.Tensor] = None,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    _need(acc, "acc", torch.float32, 2)
+    T, H = acc.shape
+    if residual is not None:
+        _need(residual, "residual", torch.bfloat16, 2)
+    dev = acc.device
+    out = out if out is not None else torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    with torch.cuda.device(dev):
+        _C.check(_C.lib().qmoe_combine_finalize(_ptr(acc), _ptr(residual), T, H, _ptr(out),
+                                                _stream(dev)), "qmoe_combine_finalize")
+    return out
+
+
+def moe_forward_workspace_size(T: int, H: int, E: int, k: int, I: int) -> int:
+    return int(_C.lib().qmoe_moe_forward_workspace_size(T, H, E, k, I))
+
+
+def moe_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate_up: torch.Tensor,
+                w_down: torch.Tensor, k: int, normalize: bool = True,
+                residual: Optional[torch.Tensor] = None, bias: Optional[torch.Tensor] = None,
+                workspace: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                return_routing: bool = False):
+    """Fused sparse-MoE block (K1..finalize).  Returns out (T,H) bf16
+    [, topk_idx (T,k) int32, topk_w (T,k) fp32]."""
+    _need(x, "x", torch.bfloat16, 2)
+    _need(w_router, "w_router", torch.bfloat16, 2)
+    _need(w_gate_up, "w_gate_up", torch.bfloat16, 3)
+    _need(w_down, "w_down", torch.bfloat16, 3)
+    if residual is not None:
+        _need(residual, "residual", torch.bfloat16, 2)
+    if bias is not None:
+        _need(bias, "bias", torch.float32, 1)
+    T, H = x.shape
+    E = w_router.shape[0]
+    I = w_down.shape[2]
+    dev = x.device
+    ws_bytes = moe_forward_workspace_size(T, H, E, k, I)
+    if workspace is None or workspace.numel() < ws_bytes:
+        workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    out = out if out is not None else torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    idx = torch.empty((T, k), dtype=torch.int32, device=dev) if return_routing else None
+    tw = torch.empty((T, k), dtype=torch.float32, device=dev) if return_routing else None
+    with torch.cuda.device(dev):
+        _C.check(_C.lib().qmoe_moe_forward(
+            _ptr(x), _ptr(w_router), _ptr(bias), _ptr(w_gate_up), _ptr(w_down), _ptr(residual),
+            T, H, E, k, I, 1 if normalize else 0, _ptr(out), _ptr(idx), _ptr(tw),
+            _ptr(workspace), workspace.numel(), _stream(dev)), "qmoe_moe_forward")
+    if return_routing:
+        return out, idx, tw
+    return out

@@ -1,0 +1,59 @@
+"""The C-ABI library: it loads without a GPU, exports every function the public
+header declares, and rejects bad arguments on the host before any launch."""
+import ctypes
+
+import pytest
+
+from nki_moe_7013_b200 import _C
+from nki_moe_7013_b200.build import LIB_PATH, build
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build()
+    return _C.lib()
+
+
+def test_exports_every_header_symbol(lib):
+    names = _C.header_symbols()
+    assert len(names) >= 10
+    handle = ctypes.CDLL(LIB_PATH)
+    missing = [n for n in names if not hasattr(handle, n)]
+    assert not missing, f"declared but not exported: {missing}"
+    # and the binding table covers every declared symbol
+    assert sorted(_C._SIGNATURES) == names
+
+
+def test_status_strings(lib):
+    assert lib.qmoe_version() >= 100
+    assert lib.qmoe_status_string(0) == b"ok"
+    assert lib.qmoe_status_string(-4) == b"workspace too small"
+
+
+def test_host_side_validation_needs_no_gpu(lib):
+    # null pointers are refused before the device is touched
+    st = lib.qmoe_router_topk(None, None, None, 4, 2048, 128, 8, 1, None, None, None, None, None)
+    assert st == -1 and b"null" in lib.qmoe_last_error()
+    buf = ctypes.create_string_buffer(64)
+    p = ctypes.addressof(buf)
+    # unsupported hidden size
+    st = lib.qmoe_router_topk(p, p, None, 4, 300, 128, 8, 1, None, p, p, None, None)
+    assert st == -2
+    # k > E
+    st = lib.qmoe_router_topk(p, p, None, 4, 2048, 32, 33, 1, None, p, p, None, None)
+    assert st == -1
+    # I not a multiple of 128
+    st = lib.qmoe_grouped_gemm_gateup_swiglu(p, p, p, 10, 8, 2048, 100, 128, p, None)
+    assert st == -2
+    # misaligned pointer
+    st = lib.qmoe_combine_finalize(p + 4, None, 2, 64, p, None)
+    assert st == -3
+
+
+def test_workspace_size_query(lib):
+    small = lib.qmoe_moe_forward_workspace_size(1, 2048, 128, 8, 768)
+    big = lib.qmoe_moe_forward_workspace_size(1024, 2048, 128, 8, 768)
+    assert 0 < small < big
+    # dominated by x_perm (T*k*H bf16) + act (T*k*I bf16) + fp32 accumulator (T*H)
+    assert big >= 1024 * 8 * 2048 * 2 + 1024 * 8 * 768 * 2 + 1024 * 2048 * 4
+    assert lib.qmoe_max_tiles(8192, 128) == 128 + 64 + 1

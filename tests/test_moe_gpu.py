@@ -1,0 +1,131 @@
+"""K2 permutation (bit-exact), K3a / K3b grouped GEMMs and the fused MoE block
+against the CPU oracle.  Activation tolerance: max relative error <= 2e-2
+(normwise: max|gpu - oracle| / max|oracle|), the north-star bar."""
+import numpy as np
+import pytest
+import torch
+
+from helpers import MAX_REL, activations, max_rel_err, moe_weights, to_f32_np
+
+pytestmark = pytest.mark.gpu
+
+
+def _routing(cuda_dev, x, wr, k):
+    from nki_moe_7013_b200 import ops
+
+    idx, w, hist = ops.router_topk(x, wr, k, return_hist=True)
+    return idx, w, hist
+
+
+@pytest.mark.parametrize("T,H,E,k", [(1, 2048, 128, 8), (5, 256, 32, 4), (128, 2048, 128, 8),
+                                     (1024, 2048, 128, 8), (37, 512, 64, 8)])
+def test_permute_bit_exact(cuda_dev, oracle, T, H, E, k):
+    from nki_moe_7013_b200 import ops
+
+    wr = moe_weights(2, E, H, 128, cuda_dev)[0]
+    x = activations(2, T, H, cuda_dev)
+    idx, w, hist = _routing(cuda_dev, x, wr, k)
+    acc = torch.full((T, H), 7.0, dtype=torch.float32, device=cuda_dev)
+    p = ops.moe_permute(idx, w, hist, E, x=x, gather=True, acc_zero=acc)
+    torch.cuda.synchronize()
+    ref = oracle.permute(idx.cpu().numpy(), E)
+    np.testing.assert_array_equal(p["counts"].cpu().numpy(), ref["counts"])
+    np.testing.assert_array_equal(p["offsets"].cpu().numpy(), ref["offsets"])
+    np.testing.assert_array_equal(p["row_token"].cpu().numpy(), ref["row_token"])
+    np.testing.assert_array_equal(p["slot_row"].cpu().numpy(), ref["slot_row"])
+    wn = w.cpu().numpy()
+    np.testing.assert_array_equal(p["row_w"].cpu().numpy(),
+                                  wn.reshape(-1)[np.argsort(ref["slot_row"].reshape(-1))])
+    # x_perm rows are the gathered token rows
+    xp = p["x_perm"].cpu()
+    assert torch.equal(xp, x.cpu()[torch.from_numpy(ref["row_token"]).long()])
+    assert torch.count_nonzero(acc).item() == 0
+    # tile list: every expert's rows cut into 128-row tiles in expert order
+    tiles = p["tiles"].cpu().numpy()
+    mt = p["max_tiles"]
+    nt = tiles[0]
+    exp_tiles = []
+    for e in range(E):
+        n = int(ref["counts"][e])
+        for i in range(0, n, 128):
+            exp_tiles.append((e, int(ref["offsets"][e]) + i, min(128, n - i)))
+    got = list(zip(tiles[1:1 + nt], tiles[1 + mt:1 + mt + nt], tiles[1 + 2 * mt:1 + 2 * mt + nt]))
+    assert [tuple(map(int, g)) for g in got] == exp_tiles
+
+
+@pytest.mark.parametrize("T,H,E,k,I", [(1, 2048, 128, 8, 768), (128, 2048, 128, 8, 768),
+                                       (16, 256, 32, 4, 128), (300, 512, 32, 8, 256)])
+def test_grouped_gemms_vs_oracle(cuda_dev, oracle, T, H, E, k, I):
+    from nki_moe_7013_b200 import ops
+
+    wr, wgu, wd = moe_weights(3, E, H, I, cuda_dev)
+    x = activations(3, T, H, cuda_dev)
+    idx, w, hist = _routing(cuda_dev, x, wr, k)
+    acc = torch.empty((T, H), dtype=torch.float32, device=cuda_dev)
+    p = ops.moe_permute(idx, w, hist, E, x=x, gather=True, acc_zero=acc)
+    act = ops.grouped_gemm_gateup_swiglu(p["x_perm"], wgu, p["tiles"], p["max_tiles"])
+    ops.grouped_gemm_down_combine(act, wd, p["tiles"], p["max_tiles"], p["row_token"], p["row_w"], acc)
+    torch.cuda.synchronize()
+    from nki_moe_7013_b200 import _C
+
+    assert _C.device_error() == 0
+    ref_out, inter = oracle.moe_block(x.cpu(), wr.cpu(), wgu.cpu(), wd.cpu(), k,
+                                      return_intermediates=True)
+    assert np.array_equal(idx.cpu().numpy(), inter["topk_idx"])
+    err_act = max_rel_err(to_f32_np(act), inter["act"])
+    assert err_act <= MAX_REL, f"act max rel err {err_act:.3e}"
+    err_out = max_rel_err(acc.cpu().numpy(), ref_out)
+    assert err_out <= MAX_REL, f"combine max rel err {err_out:.3e}"
+
+
+@pytest.mark.parametrize("T", [1, 8, 64, 128, 1024])
+def test_moe_forward_cfg0_shapes(cuda_dev, oracle, T):
+    from nki_moe_7013_b200 import ops
+
+    H, E, k, I = 2048, 128, 8, 768
+    wr, wgu, wd = moe_weights(0, E, H, I, cuda_dev)
+    x = activations(0, T, H, cuda_dev)
+    out, idx, tw = ops.moe_forward(x, wr, wgu, wd, k, return_routing=True)
+    torch.cuda.synchronize()
+    ref_out, inter = oracle.moe_block(x.cpu(), wr.cpu(), wgu.cpu(), wd.cpu(), k,
+                                      return_intermediates=True)
+    assert np.array_equal(idx.cpu().numpy(), inter["topk_idx"])
+    np.testing.assert_allclose(tw.cpu().numpy(), inter["topk_w"], rtol=2e-6, atol=1e-7)
+    err = max_rel_err(to_f32_np(out), oracle.round_to_bf16(ref_out))
+    assert err <= MAX_REL, f"moe_forward max rel err {err:.3e}"
+
+
+def test_moe_forward_residual_and_determinism(cuda_dev, oracle):
+    from nki_moe_7013_b200 import ops
+
+    T, H, E, k, I = 96, 2048, 128, 8, 768
+    wr, wgu, wd = moe_weights(4, E, H, I, cuda_dev)
+    x = activations(4, T, H, cuda_dev)
+    res = activations(5, T, H, cuda_dev)
+    out1, idx1, _ = ops.moe_forward(x, wr, wgu, wd, k, residual=res, return_routing=True)
+    out2, idx2, _ = ops.moe_forward(x, wr, wgu, wd, k, residual=res, return_routing=True)
+    torch.cuda.synchronize()
+    assert torch.equal(idx1, idx2)  # routing is bit-reproducible
+    ref = oracle.moe_block(x.cpu(), wr.cpu(), wgu.cpu(), wd.cpu(), k) + to_f32_np(res)
+    err = max_rel_err(to_f32_np(out1), ref)
+    assert err <= MAX_REL
+
+
+def test_moe_forward_zipf_skew(cuda_dev, oracle):
+    """Config-4-style skew: Zipf(1.2) expert popularity through a router bias."""
+    from nki_moe_7013_b200 import ops
+    from nki_moe_7013_b200.synth import zipf_expert_bias
+
+    T, H, E, k, I = 2048, 2048, 128, 8, 768
+    wr, wgu, wd = moe_weights(6, E, H, I, cuda_dev)
+    x = activations(6, T, H, cuda_dev)
+    bias = zipf_expert_bias(0, E).to(cuda_dev)
+    out, idx, _ = ops.moe_forward(x, wr, wgu, wd, k, bias=bias, return_routing=True)
+    torch.cuda.synchronize()
+    ref_out, inter = oracle.moe_block(x.cpu(), wr.cpu(), wgu.cpu(), wd.cpu(), k,
+                                      bias=bias.cpu().numpy(), return_intermediates=True)
+    assert np.array_equal(idx.cpu().numpy(), inter["topk_idx"])
+    counts = np.bincount(inter["topk_idx"].reshape(-1), minlength=E)
+    assert counts.max() > 4 * counts.mean()  # the skew is real: several 128-row tiles per hot expert
+    err = max_rel_err(to_f32_np(out), oracle.round_to_bf16(ref_out))
+    assert err <= MAX_REL

@@ -1,0 +1,71 @@
+"""K1 router parity on the GPU: logits and expert indices bit-exact against the
+C oracle (same fp32 reduction order), weights within fp32 rounding."""
+import numpy as np
+import pytest
+import torch
+
+from helpers import activations
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(x, wr, k, bias=None, normalize=True):
+    from nki_moe_7013_b200 import ops
+
+    idx, w, logits, hist = ops.router_topk(x, wr, k, normalize=normalize, bias=bias,
+                                           return_logits=True, return_hist=True)
+    torch.cuda.synchronize()
+    return idx.cpu().numpy(), w.cpu().numpy(), logits.cpu().numpy(), hist.cpu().numpy()
+
+
+@pytest.mark.parametrize("T,H,E,k", [(1, 2048, 128, 8), (7, 256, 32, 4), (128, 2048, 128, 8),
+                                     (1000, 2048, 128, 8), (33, 512, 64, 8), (9, 4096, 256, 32)])
+def test_router_matches_oracle(cuda_dev, oracle, T, H, E, k):
+    from nki_moe_7013_b200.synth import normal_bf16_device
+
+    wr = normal_bf16_device(11 + T, (E, H), 0.02, cuda_dev)
+    x = activations(T, T, H, cuda_dev)
+    idx, w, logits, hist = _run(x, wr, k)
+    ref_logits, ref_idx, ref_w = oracle.router(x.cpu(), wr.cpu(), k, True)
+    assert np.array_equal(logits.view(np.uint32), ref_logits.view(np.uint32)), "logits not bit-exact"
+    assert np.array_equal(idx, ref_idx), "expert indices differ"
+    np.testing.assert_allclose(w, ref_w, rtol=2e-6, atol=1e-7)
+    # chunk histogram = per-chunk expert counts
+    chunk = 8
+    for c in range(hist.shape[0]):
+        sel = ref_idx[c * chunk:(c + 1) * chunk].reshape(-1)
+        np.testing.assert_array_equal(hist[c], np.bincount(sel, minlength=E))
+
+
+def test_router_ties_lower_index_wins(cuda_dev, oracle):
+    from nki_moe_7013_b200.synth import normal_bf16_device
+
+    T, H, E, k = 16, 2048, 128, 8
+    wr = normal_bf16_device(5, (E, H), 0.02, cuda_dev)
+    # duplicated expert rows give exactly equal logits
+    for a, b in [(3, 77), (10, 11), (120, 5), (64, 65), (0, 127)]:
+        wr[b] = wr[a]
+    x = activations(3, T, H, cuda_dev)
+    x[0].zero_()                      # all 128 logits equal -> experts 0..7
+    x[1] = x[2]                       # identical tokens
+    idx, w, logits, _ = _run(x, wr, k)
+    ref_logits, ref_idx, ref_w = oracle.router(x.cpu(), wr.cpu(), k, True)
+    assert np.array_equal(idx, ref_idx)
+    assert list(idx[0]) == list(range(8))
+    np.testing.assert_allclose(w[0], np.full(8, 0.125, np.float32), rtol=1e-6)
+    assert np.array_equal(idx[1], idx[2])
+    np.testing.assert_allclose(w, ref_w, rtol=2e-6, atol=1e-7)
+
+
+def test_router_bias_and_unnormalized(cuda_dev, oracle):
+    from nki_moe_7013_b200.synth import normal_bf16_device, zipf_expert_bias
+
+    T, H, E, k = 64, 2048, 128, 8
+    wr = normal_bf16_device(7, (E, H), 0.02, cuda_dev)
+    x = activations(8, T, H, cuda_dev)
+    bias = zipf_expert_bias(0, E).to(cuda_dev)
+    idx, w, logits, _ = _run(x, wr, k, bias=bias, normalize=False)
+    ref_logits, ref_idx, ref_w = oracle.router(x.cpu(), wr.cpu(), k, False, bias=bias.cpu().numpy())
+    assert np.array_equal(logits.view(np.uint32), ref_logits.view(np.uint32))
+    assert np.array_equal(idx, ref_idx)
+    np.testing.assert_allclose(w, ref_w, rtol=2e-6, atol=1e-8)
