@@ -1,0 +1,472 @@
+#!/usr/bin/env python
+"""MoE-layer throughput of the B200 Qwen3-MoE hot path (one JSON line).
+
+Workload (N=1): the sparse-MoE block of the config-1 decoder layer -- prefill
+batch 1 x seq 1024 = 1024 tokens, hidden 2048, 128 experts, top-8,
+moe_intermediate 768, bf16, random-init weights ~N(0, 0.02), activations
+~N(0, 1).  A step = one MoE-layer forward (router -> permutation -> gate/up +
+SiLU*up -> down + weighted combine -> bf16 output) over the 1024 tokens, with
+inputs resident in HBM.  The 1.2 GB of expert weights are larger than L2
+(126 MB), so every step streams them from HBM again.
+
+N>1 (torchrun): every rank runs its own copy of the layer on its own 1024
+tokens (replicas; weak scaling); value = tokens of all ranks / max-over-ranks
+time.
+
+Also reported on the same line:
+  e2e          same metric through the public module API with the step's
+               input copied from pinned host memory and its output read back
+  roofline     gate/up grouped GEMM (the dominant kernel) vs measured HBM peak
+  cpu_baseline the reference CPU path (HF transformers Qwen3MoeSparseMoeBlock,
+               the module the reference uses in CPU mode) on the host cores
+  extras       decode steps (B = 1/8/32/64 tokens per layer, CUDA graph) and
+               the Zipf-skewed 16384-token block (config 4)
+
+``--impl reference`` times only the reference CPU path (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+if REPO not in sys.path:
+    sys.path.insert(0, REPO)
+
+H, E, K_TOP, I_MOE = 2048, 128, 8, 768
+GATE_UP_BYTES_PER_EXPERT = 2 * I_MOE * H * 2   # 6,291,456
+DOWN_BYTES_PER_EXPERT = H * I_MOE * 2          # 3,145,728
+METRIC = "MoE-layer tokens/s/GPU (prefill & decode) at 1-8 B200; % of HBM/tensor roofline"
+UNIT = "tokens/s"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=1024)
+    ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget-s", type=float, default=12.0)
+    ap.add_argument("--clock-settle-s", type=float, default=1.0,
+                    help="untimed load before warm-up so clocks settle and get sampled")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------
+# peaks, clocks
+# ----------------------------------------------------------------------------
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), float(p.get("bf16_tflops_sustained", 0)), "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 10:
+                continue
+            try:
+                rows.append(dict(sm=float(parts[1]), smax=float(parts[2]), util=float(parts[4]),
+                                 hw=parts[6], hwt=parts[7], swt=parts[8], pcap=parts[9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        loaded = [r for r in rows if r["util"] >= 50] or rows
+        if not loaded:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        reasons = set()
+        for r in loaded:
+            if r["hw"] == "Active":
+                reasons.add("hw_slowdown")
+            if r["hwt"] == "Active":
+                reasons.add("hw_thermal_slowdown")
+            if r["swt"] == "Active":
+                reasons.add("sw_thermal_slowdown")
+            if r["pcap"] == "Active":
+                reasons.add("sw_power_cap")
+        return {"sm_mhz": statistics.median(r["sm"] for r in loaded),
+                "sm_max_mhz": max(r["smax"] for r in loaded), "reasons": sorted(reasons),
+                "samples": len(loaded)}
+
+
+BAD_REASONS = {"hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown"}
+
+
+# ----------------------------------------------------------------------------
+# reference CPU path (HF transformers, the reference's CPU-mode module)
+# ----------------------------------------------------------------------------
+
+def make_hf_block(w_router, w_gate_up, w_down):
+    import torch
+    from transformers import Qwen3MoeConfig as HFConfig
+    from transformers.models.qwen3_moe.modeling_qwen3_moe import Qwen3MoeSparseMoeBlock
+
+    cfg = HFConfig(hidden_size=H, num_experts=E, num_experts_per_tok=K_TOP, moe_intermediate_size=I_MOE,
+                   norm_topk_prob=True, hidden_act="silu")
+    blk = Qwen3MoeSparseMoeBlock(cfg).to(torch.bfloat16)
+    with torch.no_grad():
+        blk.gate.weight.copy_(w_router.cpu())
+        blk.experts.gate_up_proj.copy_(w_gate_up.cpu())
+        blk.experts.down_proj.copy_(w_down.cpu())
+    return blk.eval()
+
+
+def time_cpu_reference(blk, x_cpu, budget_s: float, min_runs: int = 3):
+    """Median seconds of HF forward on x_cpu (1, T, H), all host threads."""
+    import torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    with torch.no_grad():
+        blk(x_cpu)  # warm-up
+        times = []
+        t_start = time.perf_counter()
+        while len(times) < min_runs or (time.perf_counter() - t_start) < budget_s * 0.5:
+            t0 = time.perf_counter()
+            blk(x_cpu)
+            times.append(time.perf_counter() - t0)
+            if time.perf_counter() - t_start > budget_s:
+                break
+    return statistics.median(times), len(times)
+
+
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+def run_reference(args):
+    import torch
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    T = args.tokens
+    # Weights drawn on the host (same distributions as the GPU arm).
+    g = torch.Generator().manual_seed(0)
+    w_router = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16)
+    w_gate_up = (torch.randn(E, 2 * I_MOE, H, generator=g) * 0.02).to(torch.bfloat16)
+    w_down = (torch.randn(E, H, I_MOE, generator=g) * 0.02).to(torch.bfloat16)
+    blk = make_hf_block(w_router, w_gate_up, w_down)
+    torch.set_num_threads(os.cpu_count() or 1)
+    x_full = torch.randn(1, T, H, generator=g).to(torch.bfloat16)
+    with torch.no_grad():
+        t0 = time.perf_counter()
+        blk(x_full)
+        t1 = time.perf_counter() - t0
+    # bounded sample: K steps of at most ~120 s in total
+    budget = 120.0
+    per_step_tokens = T
+    if (args.steps + args.warmup) * t1 > budget:
+        per_step_tokens = max(8, int(T * budget / ((args.steps + args.warmup) * t1)))
+    x = x_full[:, :per_step_tokens].contiguous()
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            blk(x)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            blk(x)
+        el = time.perf_counter() - t0
+    value = per_step_tokens * args.steps / el
+    cores = torch.get_num_threads()
+    sample = (f"HF transformers Qwen3MoeSparseMoeBlock (eager experts, bf16) on {per_step_tokens} of the "
+              f"{T} tokens per step, {args.steps} steps, {cores} threads on {cpu_model()}")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded random-init weights and activations)",
+        "config": {"workload": f"qwen3-moe sparse block, cfg1 prefill 1x{T} tokens (reference CPU path)",
+                   "hidden": H, "experts": E, "top_k": K_TOP, "moe_intermediate": I_MOE},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+# ----------------------------------------------------------------------------
+# our arm
+# ----------------------------------------------------------------------------
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from nki_moe_7013_b200 import _C
+    from nki_moe_7013_b200.config import Qwen3MoeConfig
+    from nki_moe_7013_b200.moe import MoEPlan, MoEWeights, Qwen3MoeSparseMoeBlock
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    _C.lib()
+
+    cfg = Qwen3MoeConfig()
+    T = args.tokens
+    weights = MoEWeights.random(cfg, seed=0, device=dev)
+    from nki_moe_7013_b200.synth import normal_bf16_device
+
+    x = normal_bf16_device(1000 + rank, (T, H), 1.0, dev)
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    plan = MoEPlan(weights, T, K_TOP)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    sampler = ClockSampler() if rank == 0 else None
+
+    def timed_run():
+        # load phase: settle clocks and give the sampler samples (untimed)
+        t_end = time.perf_counter() + args.clock_settle_s
+        while time.perf_counter() < t_end:
+            for _ in range(20):
+                plan.run(x, out)
+            torch.cuda.synchronize()
+        for _ in range(args.warmup):
+            plan.run(x, out)
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(args.steps)]
+        barrier()
+        for s in range(args.steps):
+            plan.run(x, out, events=ev[s])
+        barrier()
+        total_ms = sum(ev[s][0].elapsed_time(ev[s][5]) for s in range(args.steps))
+        # device time of the K steps: first event to last event
+        span_ms = ev[0][0].elapsed_time(ev[-1][5])
+        stage_ms = [statistics.mean(ev[s][i].elapsed_time(ev[s][i + 1]) for s in range(args.steps))
+                    for i in range(5)]
+        return span_ms, total_ms, stage_ms
+
+    if sampler:
+        sampler.start()
+    span_ms, total_ms, stage_ms = timed_run()
+    clocks = sampler.stop() if sampler else None
+    if clocks and set(clocks["reasons"]) & BAD_REASONS:
+        sampler.start()
+        span_ms, total_ms, stage_ms = timed_run()
+        clocks = sampler.stop()
+        clocks["remeasured"] = True
+
+    t_max = torch.tensor([span_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    span_ms = float(t_max.item())
+    ms_per_step = span_ms / args.steps
+    value = T * world * args.steps / (span_ms / 1e3)
+
+    # routing statistics of this workload (distinct experts hit)
+    counts = plan.counts.cpu()
+    U = int((counts > 0).sum().item())
+    R = T * K_TOP
+    hbm_gbs, tf_burst, tf_sust, peak_kind = load_peaks()
+    gate_up_bytes = U * GATE_UP_BYTES_PER_EXPERT + R * H * 2 + R * I_MOE * 2
+    gate_up_us = stage_ms[2] * 1e3
+    achieved = gate_up_bytes / (gate_up_us * 1e-6) / 1e9
+    layer_bytes = U * (GATE_UP_BYTES_PER_EXPERT + DOWN_BYTES_PER_EXPERT) + E * H * 2 + 4 * T * H + 8 * T * K_TOP
+    layer_gbs = layer_bytes / (ms_per_step * 1e-3) / 1e9
+
+    # ---------------- e2e through the public module API ----------------
+    block = Qwen3MoeSparseMoeBlock(cfg, weights=weights, device=dev)
+    x_host = x.reshape(1, T, H).cpu().pin_memory()
+    y_host = torch.empty((1, T, H), dtype=torch.bfloat16).pin_memory()
+    for _ in range(max(args.warmup, 3)):
+        y_host.copy_(block(x_host.to(dev, non_blocking=True))[0], non_blocking=True)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        xd = x_host.to(dev, non_blocking=True)
+        y_host.copy_(block(xd)[0], non_blocking=True)
+    e1.record()
+    barrier()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = T * world * args.steps / (float(e2e_ms.item()) / 1e3)
+
+    # ---------------- traffic from the committed ncu capture ----------------
+    traffic = None
+    try:
+        with open(os.path.join(REPO, "profiles", "ncu_traffic.json")) as f:
+            tr = json.load(f)
+        ent = tr.get(f"gate_up_T{T}")
+        if ent:
+            traffic = float(ent["dram_bytes_per_launch"])
+    except Exception:
+        pass
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded random-init weights ~N(0,0.02), activations ~N(0,1))",
+        "config": {"workload": f"qwen3-moe sparse block of the cfg1 decoder layer, prefill 1x{T} tokens",
+                   "tokens_per_gpu": T, "hidden": H, "experts": E, "top_k": K_TOP,
+                   "moe_intermediate": I_MOE, "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2: 1.21 GB of expert weights streamed per step"},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T * H * 2,
+                "d2h_bytes_per_step": T * H * 2,
+                "api": "Qwen3MoeSparseMoeBlock.forward(hidden_states)[0], pinned host in/out"},
+        "gpu_launches": MoEPlan.LAUNCHES_PER_RUN * args.steps,
+        "stage_us": dict(zip(MoEPlan.STAGES, [round(s * 1e3, 2) for s in stage_ms])),
+        "roofline": {"bound": "hbm", "kernel": "grouped_gemm_kernel<gate_up>",
+                     "achieved": achieved, "peak": hbm_gbs, "unit": "GB/s", "frac": achieved / hbm_gbs,
+                     "peak_kind": peak_kind, "traffic": traffic,
+                     "algorithmic_bytes_per_launch": gate_up_bytes, "experts_hit": U},
+        "layer_roofline": {"bound": "hbm", "achieved": layer_gbs, "peak": hbm_gbs, "unit": "GB/s",
+                           "frac": layer_gbs / hbm_gbs, "algorithmic_bytes_per_step": layer_bytes},
+        "clocks": clocks,
+    }
+
+    if rank == 0 and not args.no_extras:
+        line["extras"] = run_extras(cfg, weights, dev, hbm_gbs, tf_burst)
+
+    if rank == 0 and not args.no_cpu_baseline:
+        blk = make_hf_block(weights.router, weights.gate_up, weights.down)
+        med, runs = time_cpu_reference(blk, x.reshape(1, T, H).cpu(), args.cpu_budget_s)
+        import torch as _t
+
+        line["cpu_baseline"] = {
+            "value": T / med, "unit": UNIT, "cores": _t.get_num_threads(), "kind": "reference",
+            "sample": (f"HF transformers Qwen3MoeSparseMoeBlock (the module the reference uses in CPU "
+                       f"mode, qwen.py:35-37), bf16, same weights and {T} tokens, median of {runs} runs "
+                       f"on {cpu_model()}")}
+    if rank == 0:
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def run_extras(cfg, weights, dev, hbm_gbs, tf_burst):
+    """Decode-sized MoE layers (CUDA graph replay) and the config-4 skewed block."""
+    import torch
+
+    from nki_moe_7013_b200.moe import MoEPlan
+    from nki_moe_7013_b200.synth import normal_bf16_device, zipf_expert_bias
+
+    res = {}
+    dec = {}
+    for B in (1, 8, 32, 64):
+        plan = MoEPlan(weights, B, K_TOP)
+        x = normal_bf16_device(77 + B, (B, H), 1.0, dev)
+        out = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                plan.run(x, out)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            plan.run(x, out)
+        for _ in range(5):
+            g.replay()
+        torch.cuda.synchronize()
+        n = 200
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / n
+        U = int((plan.counts.cpu() > 0).sum().item())
+        byts = U * (GATE_UP_BYTES_PER_EXPERT + DOWN_BYTES_PER_EXPERT) + E * H * 2 + 4 * B * H + 8 * B * K_TOP
+        dec[str(B)] = {"us_per_layer": round(us, 2), "tokens_per_s": B / (us * 1e-6),
+                       "experts_hit": U, "hbm_frac": byts / (us * 1e-6) / 1e9 / hbm_gbs}
+        del g
+    res["decode_moe_layer_cuda_graph"] = dec
+
+    T = 16384
+    bias = zipf_expert_bias(0, E).to(dev)
+    plan = MoEPlan(weights, T, K_TOP, bias=bias)
+    x = normal_bf16_device(4242, (T, H), 1.0, dev)
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    for _ in range(3):
+        plan.run(x, out)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(10)]
+    torch.cuda.synchronize()
+    for s in range(10):
+        plan.run(x, out, events=ev[s])
+    torch.cuda.synchronize()
+    stage = [statistics.mean(ev[s][i].elapsed_time(ev[s][i + 1]) for s in range(10)) for i in range(5)]
+    total_ms = statistics.mean(ev[s][0].elapsed_time(ev[s][5]) for s in range(10))
+    counts = plan.counts.cpu()
+    flops_gemm = T * 6 * K_TOP * H * I_MOE
+    res["cfg4_zipf_T16384"] = {
+        "ms_per_layer": round(total_ms, 3), "tokens_per_s": T / (total_ms * 1e-3),
+        "stage_us": dict(zip(MoEPlan.STAGES, [round(v * 1e3, 1) for v in stage])),
+        "expert_gemm_tflops": flops_gemm / ((stage[2] + stage[3]) * 1e-3) / 1e12,
+        "tensor_frac": flops_gemm / ((stage[2] + stage[3]) * 1e-3) / 1e12 / tf_burst,
+        "max_expert_rows": int(counts.max().item()), "mean_expert_rows": float(counts.float().mean().item()),
+    }
+    return res
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

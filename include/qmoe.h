@@ -153,6 +153,31 @@ QMOE_API int qmoe_grouped_gemm_down_combine(const void* act, const void* w_down,
                                    const float* row_w, int64_t R, int64_t H, int64_t I,
                                    int64_t E, float* acc, int64_t n_acc, void* stream);
 
+/* ------------------------------------------------------------------------
+ * NxDI blockwise seam: ExpertMLPsV2.torch_blockwise_matmul_inference
+ * (qwen_with_nki.py:5872-5881, kernels wired at qwen_with_nki.py:5440-5502).
+ * Builds the row description of the grouped GEMMs from fixed-size blocks:
+ *
+ *   x                    (T, H) bf16 hidden states
+ *   affinities           (aff_rows, E) fp32 expert_affinities_masked
+ *   token_position_to_id (num_blocks * block_size) int32; ids outside [0, T)
+ *                        are padding positions
+ *   block_to_expert      (num_blocks) int32
+ *   x_perm   (num_blocks*block_size, H) bf16 out: gathered rows (0 for padding)
+ *   row_dst  (num_blocks*block_size) int32 out: token, or -1 for padding and
+ *                        for all but the last occurrence of a token in a
+ *                        block (qwen_with_nki.py:5656-5667)
+ *   row_w    (num_blocks*block_size) fp32 out: affinity[token, expert]
+ *   tiles    (1 + 3*qmoe_blockwise_max_tiles()) int32 out
+ * Then run K3a / K3b with these tiles and finalize.
+ * ---------------------------------------------------------------------- */
+QMOE_API int64_t qmoe_blockwise_max_tiles(int64_t block_size, int64_t num_blocks);
+QMOE_API int qmoe_blockwise_prepare(const void* x, const float* affinities, int64_t aff_rows,
+                           const int32_t* token_position_to_id, const int32_t* block_to_expert,
+                           int64_t T, int64_t H, int64_t E, int64_t block_size, int64_t num_blocks,
+                           void* x_perm, int32_t* row_dst, float* row_w, int32_t* tiles,
+                           void* stream);
+
 /* out (T, H) bf16 = bf16(acc + residual); residual (T, H) bf16 or NULL. */
 QMOE_API int qmoe_combine_finalize(const float* acc, const void* residual, int64_t T, int64_t H,
                           void* out, void* stream);

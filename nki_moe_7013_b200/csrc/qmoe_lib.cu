@@ -12,6 +12,7 @@
 #include <mutex>
 #include <string>
 
+#include "blockwise.cuh"
 #include "common.cuh"
 #include "finalize.cuh"
 #include "grouped_gemm.cuh"
@@ -434,6 +435,43 @@ int qmoe_combine_finalize(const float* acc, const void* residual, int64_t T, int
   DeviceInfo* d = nullptr;
   QMOE_CHECK(device_info(&d));
   return launch_finalize(acc, residual, T, H, out, static_cast<cudaStream_t>(stream));
+}
+
+int64_t qmoe_blockwise_max_tiles(int64_t block_size, int64_t num_blocks) {
+  if (block_size <= 0 || num_blocks <= 0) return 0;
+  return num_blocks * ((block_size + qmoe::kTileRows - 1) / qmoe::kTileRows);
+}
+
+int qmoe_blockwise_prepare(const void* x, const float* affinities, int64_t aff_rows,
+                           const int32_t* token_position_to_id, const int32_t* block_to_expert,
+                           int64_t T, int64_t H, int64_t E, int64_t block_size, int64_t num_blocks,
+                           void* x_perm, int32_t* row_dst, float* row_w, int32_t* tiles,
+                           void* stream) {
+  QMOE_REQUIRE(x && affinities && token_position_to_id && block_to_expert && x_perm && row_dst &&
+                   row_w && tiles,
+               QMOE_ERR_INVALID_ARGUMENT, "blockwise_prepare: null pointer");
+  QMOE_REQUIRE(T >= 0 && T < (int64_t(1) << 31) && aff_rows >= 0, QMOE_ERR_INVALID_ARGUMENT,
+               "blockwise_prepare: bad T / aff_rows");
+  QMOE_REQUIRE(H > 0 && H % 8 == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "blockwise_prepare: H %% 8 != 0");
+  QMOE_REQUIRE(E > 0, QMOE_ERR_INVALID_ARGUMENT, "blockwise_prepare: E <= 0");
+  QMOE_REQUIRE(block_size >= 1 && block_size <= 8192, QMOE_ERR_UNSUPPORTED_SHAPE,
+               "blockwise_prepare: block_size %lld not in [1, 8192]", (long long)block_size);
+  QMOE_REQUIRE(num_blocks >= 0 && num_blocks * block_size < (int64_t(1) << 31),
+               QMOE_ERR_INVALID_ARGUMENT, "blockwise_prepare: bad num_blocks");
+  QMOE_REQUIRE(aligned16(x) && aligned16(x_perm), QMOE_ERR_MISALIGNED,
+               "blockwise_prepare: x / x_perm must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  if (num_blocks == 0) return QMOE_OK;
+  const int64_t max_tiles = qmoe_blockwise_max_tiles(block_size, num_blocks);
+  const int smem = int(2 * sizeof(int) * block_size);
+  QMOE_CHECK(set_smem(qmoe::blockwise_prepare_kernel, smem));
+  qmoe::blockwise_prepare_kernel<<<int(num_blocks), qmoe::kBlockwiseThreads, smem,
+                                   static_cast<cudaStream_t>(stream)>>>(
+      token_position_to_id, block_to_expert, affinities, int(aff_rows),
+      static_cast<const __nv_bfloat16*>(x), int(T), int(H), int(E), int(block_size),
+      static_cast<__nv_bfloat16*>(x_perm), row_dst, row_w, tiles, int(max_tiles));
+  return check_launch("blockwise_prepare_kernel");
 }
 
 size_t qmoe_moe_forward_workspace_size(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I) {

@@ -1,0 +1,278 @@
+"""Sparse-MoE block with the reference's module interfaces.
+
+* ``Qwen3MoeSparseMoeBlock`` -- drop-in for the MoE module the decoder layer
+  calls as ``self.mlp(hidden_states, padding_mask)[0]`` (qwen.py:429,
+  ``initialize_moe_module`` at qwen.py:365-371).  Returns a tuple whose [0] is
+  the (T, H) or (B, S, H) bf16 output.
+* ``Qwen3MoeSparseMoeBlockHF`` -- same block with the HF signature
+  ``forward(hidden_states) -> Tensor`` (transformers Qwen3MoeSparseMoeBlock).
+* ``ExpertMLPs`` -- the two ExpertMLPsV2 operator seams the reference team
+  patched: ``forward_selective_loading`` (qwen_with_nki.py:2377-2453) and
+  ``torch_blockwise_matmul_inference`` (qwen_with_nki.py:5872-5881).
+* ``MoEPlan`` -- buffers preallocated for a fixed token count; runs the five
+  kernels through the C ABI with no per-call allocation (CUDA-graph friendly,
+  and able to time every kernel with CUDA events).
+
+All compute goes through the CUDA library; there is no CPU path.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+from torch import nn
+
+from . import _C, ops
+from .config import Qwen3MoeConfig
+
+
+@dataclass
+class MoEWeights:
+    """Device layout: router (E,H), gate_up (E,2I,H) gate rows first, down (E,H,I)."""
+
+    router: torch.Tensor
+    gate_up: torch.Tensor
+    down: torch.Tensor
+
+    @property
+    def num_experts(self) -> int:
+        return self.router.shape[0]
+
+    @property
+    def hidden_size(self) -> int:
+        return self.router.shape[1]
+
+    @property
+    def intermediate_size(self) -> int:
+        return self.down.shape[2]
+
+    @staticmethod
+    def random(cfg: Qwen3MoeConfig, seed: int = 0, device="cuda", std: float = 0.02) -> "MoEWeights":
+        from .synth import normal_bf16_device
+
+        E, H, I = cfg.num_experts, cfg.hidden_size, cfg.moe_intermediate_size
+        return MoEWeights(normal_bf16_device(seed * 10 + 1, (E, H), std, device),
+                          normal_bf16_device(seed * 10 + 2, (E, 2 * I, H), std, device),
+                          normal_bf16_device(seed * 10 + 3, (E, H, I), std, device))
+
+    @staticmethod
+    def from_neuron_layout(router: torch.Tensor, gate_up_ehi: torch.Tensor, down_eih: torch.Tensor,
+                           device="cuda") -> "MoEWeights":
+        """From the NxDI layout of convert_qwen3_moe_hf_to_neuron_state_dict
+        (qwen.py:164-226): gate_up (E, H, 2I) gate first, down (E, I, H)."""
+        return MoEWeights(router.to(device=device, dtype=torch.bfloat16).contiguous(),
+                          gate_up_ehi.to(device=device, dtype=torch.bfloat16).transpose(1, 2).contiguous(),
+                          down_eih.to(device=device, dtype=torch.bfloat16).transpose(1, 2).contiguous())
+
+    @staticmethod
+    def from_hf_block(block, device="cuda") -> "MoEWeights":
+        """From a transformers Qwen3MoeSparseMoeBlock (gate.weight (E,H),
+        experts.gate_up_proj (E,2I,H), experts.down_proj (E,H,I))."""
+        bf = dict(device=device, dtype=torch.bfloat16)
+        return MoEWeights(block.gate.weight.detach().to(**bf).contiguous(),
+                          block.experts.gate_up_proj.detach().to(**bf).contiguous(),
+                          block.experts.down_proj.detach().to(**bf).contiguous())
+
+
+class Qwen3MoeSparseMoeBlock(nn.Module):
+    """Routed-expert MoE of Qwen3 (no shared experts, qwen.py:253-255)."""
+
+    def __init__(self, cfg: Qwen3MoeConfig, weights: Optional[MoEWeights] = None, device="cuda",
+                 seed: int = 0, return_router_logits: bool = False, return_expert_index: bool = False):
+        super().__init__()
+        self.cfg = cfg
+        self.top_k = cfg.num_experts_per_tok
+        self.normalize = cfg.norm_topk_prob
+        self.return_router_logits = return_router_logits
+        self.return_expert_index = return_expert_index
+        w = weights if weights is not None else MoEWeights.random(cfg, seed, device)
+        self.router_weight = nn.Parameter(w.router, requires_grad=False)
+        self.gate_up = nn.Parameter(w.gate_up, requires_grad=False)
+        self.down = nn.Parameter(w.down, requires_grad=False)
+        self.router_bias: Optional[torch.Tensor] = None
+        self._workspace: Optional[torch.Tensor] = None
+
+    @property
+    def weights(self) -> MoEWeights:
+        return MoEWeights(self.router_weight.data, self.gate_up.data, self.down.data)
+
+    def _moe(self, x2d: torch.Tensor, residual: Optional[torch.Tensor] = None):
+        T, H = x2d.shape
+        ws = ops.moe_forward_workspace_size(T, H, self.cfg.num_experts, self.top_k,
+                                            self.cfg.moe_intermediate_size)
+        if self._workspace is None or self._workspace.numel() < ws or self._workspace.device != x2d.device:
+            self._workspace = torch.empty(max(ws, 1), dtype=torch.uint8, device=x2d.device)
+        return ops.moe_forward(x2d, self.router_weight, self.gate_up, self.down, self.top_k,
+                               normalize=self.normalize, residual=residual, bias=self.router_bias,
+                               workspace=self._workspace, return_routing=True)
+
+    def forward(self, hidden_states: torch.Tensor, padding_mask: Optional[torch.Tensor] = None):
+        shape = hidden_states.shape
+        x2d = hidden_states.reshape(-1, shape[-1]).to(torch.bfloat16).contiguous()
+        out, idx, tw = self._moe(x2d)
+        if padding_mask is not None:
+            # padded positions (mask == 0) produce no MoE output
+            out = out * padding_mask.reshape(-1, 1).to(out.dtype)
+        out = out.reshape(shape)
+        result = (out,)
+        if self.return_router_logits:
+            logits = ops.router_topk(x2d, self.router_weight, self.top_k, bias=self.router_bias,
+                                     return_logits=True)[2]
+            result = result + (logits,)
+        if self.return_expert_index:
+            result = result + (idx.long(),)
+        return result
+
+
+class Qwen3MoeSparseMoeBlockHF(Qwen3MoeSparseMoeBlock):
+    """HF-compatible variant: forward(hidden_states) -> Tensor."""
+
+    def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:  # type: ignore[override]
+        return super().forward(hidden_states)[0]
+
+
+class ExpertMLPs(nn.Module):
+    """The ExpertMLPsV2 seams of the reference (weights in device layout)."""
+
+    def __init__(self, weights: MoEWeights, normalize_top_k_affinities: bool = True):
+        super().__init__()
+        self.w = weights
+        self.normalize_top_k_affinities = normalize_top_k_affinities
+
+    def forward_selective_loading(self, hidden_states: torch.Tensor, expert_affinities: torch.Tensor,
+                                  expert_index: torch.Tensor) -> torch.Tensor:
+        """qwen_with_nki.py:2377-2453: affinities (T, E) over all experts,
+        expert_index (T, k); the chosen affinities are L1-renormalised when
+        normalize_top_k_affinities (qwen_with_nki.py:2402-2405)."""
+        x = hidden_states.reshape(-1, hidden_states.shape[-1]).to(torch.bfloat16).contiguous()
+        T, H = x.shape
+        E = self.w.num_experts
+        idx = expert_index.reshape(T, -1).to(torch.int32).contiguous()
+        k = idx.shape[1]
+        chosen = torch.gather(expert_affinities.reshape(T, E).float(), 1, idx.long())
+        if self.normalize_top_k_affinities:
+            chosen = torch.nn.functional.normalize(chosen, p=1.0, dim=1)
+        return _run_routed(x, self.w, idx, chosen.contiguous(), k)
+
+    def torch_blockwise_matmul_inference(self, block_size, num_blocks, hidden_states,
+                                         expert_affinities_masked, token_position_to_id,
+                                         block_to_expert, pad_inputs_for_matmul=False) -> torch.Tensor:
+        """qwen_with_nki.py:5872-5881 / 5440-5502: blocks of ``block_size``
+        token positions, one expert per block; positions outside [0, T) are
+        padding; a token repeated inside a block contributes once."""
+        return blockwise_forward(hidden_states, expert_affinities_masked, token_position_to_id,
+                                 block_to_expert, int(block_size), int(num_blocks), self.w)
+
+
+def _run_routed(x: torch.Tensor, w: MoEWeights, idx: torch.Tensor, tw: torch.Tensor, k: int) -> torch.Tensor:
+    """Permutation + grouped GEMMs + combine for caller-provided routing."""
+    T, H = x.shape
+    E = w.num_experts
+    hist = torch.zeros(((T + ops.ROUTER_CHUNK - 1) // ops.ROUTER_CHUNK, E), dtype=torch.int32,
+                       device=x.device)
+    _chunk_histogram(idx, E, hist)
+    acc = torch.empty((T, H), dtype=torch.float32, device=x.device)
+    p = ops.moe_permute(idx, tw, hist, E, x=x, gather=True, acc_zero=acc)
+    act = ops.grouped_gemm_gateup_swiglu(p["x_perm"], w.gate_up, p["tiles"], p["max_tiles"])
+    ops.grouped_gemm_down_combine(act, w.down, p["tiles"], p["max_tiles"], p["row_token"], p["row_w"], acc)
+    return ops.combine_finalize(acc)
+
+
+def _chunk_histogram(idx: torch.Tensor, E: int, hist: torch.Tensor) -> None:
+    """Per-chunk expert histogram for caller-provided routing (device ops)."""
+    T, k = idx.shape
+    chunk = torch.arange(T, device=idx.device).div(ops.ROUTER_CHUNK, rounding_mode="floor")
+    flat = (chunk.unsqueeze(1) * E + idx.long()).reshape(-1)
+    hist.view(-1).index_add_(0, flat, torch.ones_like(flat, dtype=torch.int32))
+
+
+def blockwise_forward(hidden_states, expert_affinities_masked, token_position_to_id, block_to_expert,
+                      block_size: int, num_blocks: int, w: MoEWeights) -> torch.Tensor:
+    x = hidden_states.reshape(-1, hidden_states.shape[-1]).to(torch.bfloat16).contiguous()
+    T, H = x.shape
+    tpi = token_position_to_id.reshape(-1).to(torch.int32).contiguous()
+    b2e = block_to_expert.reshape(-1).to(torch.int32).contiguous()
+    aff = expert_affinities_masked.float().contiguous()
+    acc = torch.zeros((T, H), dtype=torch.float32, device=x.device)
+    prep = ops.blockwise_prepare(x, aff, tpi, b2e, block_size, num_blocks)
+    act = ops.grouped_gemm_gateup_swiglu(prep["x_perm"], w.gate_up, prep["tiles"], prep["max_tiles"])
+    ops.grouped_gemm_down_combine(act, w.down, prep["tiles"], prep["max_tiles"], prep["row_dst"],
+                                  prep["row_w"], acc)
+    return ops.combine_finalize(acc)
+
+
+class MoEPlan:
+    """Preallocated buffers + direct C-ABI launches for a fixed (T, H, E, k, I).
+
+    ``run(x, out, residual=None, events=None)``: when ``events`` is a list of 6
+    CUDA events, they are recorded before the router and after each of the
+    five stages (router, permute-scan+scatter, gate/up, down, finalize), on the
+    current stream."""
+
+    STAGES = ("router", "permute", "gate_up", "down", "finalize")
+
+    def __init__(self, weights: MoEWeights, T: int, k: int, normalize: bool = True,
+                 bias: Optional[torch.Tensor] = None):
+        self.w = weights
+        self.T, self.k = T, k
+        self.E, self.H, self.I = weights.num_experts, weights.hidden_size, weights.intermediate_size
+        self.normalize = normalize
+        self.bias = bias
+        dev = weights.router.device
+        self.device = dev
+        R = T * k
+        E, H, I = self.E, self.H, self.I
+        self.R = R
+        self.max_tiles = ops.max_tiles(R, E)
+        nchunks = (T + ops.ROUTER_CHUNK - 1) // ops.ROUTER_CHUNK
+        i32 = dict(dtype=torch.int32, device=dev)
+        f32 = dict(dtype=torch.float32, device=dev)
+        self.topk_idx = torch.empty((T, k), **i32)
+        self.topk_w = torch.empty((T, k), **f32)
+        self.hist = torch.empty((max(nchunks, 1), E), **i32)
+        self.counts = torch.empty(E, **i32)
+        self.offsets = torch.empty(E + 1, **i32)
+        self.row_token = torch.empty(max(R, 1), **i32)
+        self.row_w = torch.empty(max(R, 1), **f32)
+        self.slot_row = torch.empty((T, k), **i32)
+        self.tiles = torch.empty(1 + 3 * self.max_tiles, **i32)
+        self.x_perm = torch.empty((max(R, 1), H), dtype=torch.bfloat16, device=dev)
+        self.act = torch.empty((max(R, 1), I), dtype=torch.bfloat16, device=dev)
+        self.acc = torch.empty((max(T, 1), H), **f32)
+        self._lib = _C.lib()
+
+    def run(self, x: torch.Tensor, out: torch.Tensor, residual: Optional[torch.Tensor] = None,
+            events=None) -> torch.Tensor:
+        lib, p = self._lib, ops._ptr
+        s = torch.cuda.current_stream(self.device).cuda_stream
+        T, H, E, k, I, R = self.T, self.H, self.E, self.k, self.I, self.R
+        w = self.w
+
+        def mark(i):
+            if events is not None:
+                events[i].record()
+
+        mark(0)
+        _C.check(lib.qmoe_router_topk(p(x), p(w.router), p(self.bias), T, H, E, k,
+                                      1 if self.normalize else 0, None, p(self.topk_idx),
+                                      p(self.topk_w), p(self.hist), s), "router")
+        mark(1)
+        _C.check(lib.qmoe_moe_permute(p(self.topk_idx), p(self.topk_w), p(self.hist), p(x), T, H, E, k,
+                                      p(self.counts), p(self.offsets), p(self.row_token), p(self.row_w),
+                                      p(self.slot_row), p(self.tiles), p(self.x_perm), p(self.acc), s),
+                 "permute")
+        mark(2)
+        _C.check(lib.qmoe_grouped_gemm_gateup_swiglu(p(self.x_perm), p(w.gate_up), p(self.tiles),
+                                                     self.max_tiles, R, H, I, E, p(self.act), s),
+                 "gate_up")
+        mark(3)
+        _C.check(lib.qmoe_grouped_gemm_down_combine(p(self.act), p(w.down), p(self.tiles), self.max_tiles,
+                                                    p(self.row_token), p(self.row_w), R, H, I, E,
+                                                    p(self.acc), T, s), "down")
+        mark(4)
+        _C.check(lib.qmoe_combine_finalize(p(self.acc), p(residual), T, H, p(out), s), "finalize")
+        mark(5)
+        return out
+
+    LAUNCHES_PER_RUN = 6  # router, scan, scatter, gate/up, down, finalize

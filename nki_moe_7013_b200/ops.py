@@ -149,6 +149,32 @@ def grouped_gemm_down_combine(act: torch.Tensor, w_down: torch.Tensor, tiles: to
     return acc
 
 
+def blockwise_prepare(x: torch.Tensor, affinities: torch.Tensor, token_position_to_id: torch.Tensor,
+                      block_to_expert: torch.Tensor, block_size: int, num_blocks: int):
+    """NxDI blockwise seam -> rows + tiles for the grouped GEMMs."""
+    _need(x, "x", torch.bfloat16, 2)
+    _need(affinities, "affinities", torch.float32, 2)
+    _need(token_position_to_id, "token_position_to_id", torch.int32, 1)
+    _need(block_to_expert, "block_to_expert", torch.int32, 1)
+    T, H = x.shape
+    E = affinities.shape[1]
+    n = block_size * num_blocks
+    if token_position_to_id.numel() != n or block_to_expert.numel() != num_blocks:
+        raise ValueError("token_position_to_id must hold num_blocks*block_size ids")
+    dev = x.device
+    mt = int(_C.lib().qmoe_blockwise_max_tiles(block_size, num_blocks))
+    x_perm = torch.empty((max(n, 1), H), dtype=torch.bfloat16, device=dev)
+    row_dst = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
+    row_w = torch.empty(max(n, 1), dtype=torch.float32, device=dev)
+    tiles = torch.zeros(1 + 3 * mt, dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        _C.check(_C.lib().qmoe_blockwise_prepare(
+            _ptr(x), _ptr(affinities), affinities.shape[0], _ptr(token_position_to_id),
+            _ptr(block_to_expert), T, H, E, block_size, num_blocks, _ptr(x_perm), _ptr(row_dst),
+            _ptr(row_w), _ptr(tiles), _stream(dev)), "qmoe_blockwise_prepare")
+    return dict(x_perm=x_perm, row_dst=row_dst, row_w=row_w, tiles=tiles, max_tiles=mt)
+
+
 def combine_finalize(acc: torch.Tensor, residual: Optional[torch.Tensor] = None,
                      out: Optional[torch.Tensor] = None) -> torch.Tensor:
     _need(acc, "acc", torch.float32, 2)
