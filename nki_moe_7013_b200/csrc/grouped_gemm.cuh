@@ -23,7 +23,8 @@
 // f0.. and up rows I+f0.. of the same expert -- so a thread's TMEM lane holds
 // gate and up of the same feature and SiLU(gate)*up needs no exchange.
 // K3b (down) multiplies each column (row r of the tile) by row_w[r] and adds
-// it into the fp32 accumulator row row_dst[r] (the weighted combine).
+// it into the fp32 accumulator row row_dst[r] (the weighted combine) with
+// 16-byte vector reductions.
 #pragma once
 
 #include "common.cuh"
@@ -47,7 +48,10 @@ struct GemmCfg {
   static constexpr int kAccCols = kGateUp ? 256 : 128;    // TMEM columns per accumulator buffer
   static constexpr int kTmemCols = 2 * kAccCols;
   static constexpr int kBarrierBytes = 256;
-  static constexpr int kSmemBytes = 1024 /*align slack*/ + kStages * kStageBytes + kBarrierBytes;
+  // down epilogue: per epilogue warp a [16 rows][33] fp32 transpose buffer
+  static constexpr int kStagingBytes = kGateUp ? 0 : 4 * 16 * 33 * 4;
+  static constexpr int kSmemBytes =
+      1024 /*align slack*/ + kStages * kStageBytes + kBarrierBytes + kStagingBytes;
 };
 
 struct GemmArgs {
@@ -84,6 +88,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* drain = acc_empty + 2;          // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* staging = reinterpret_cast<float*>(smem + C::kStages * C::kStageBytes + C::kBarrierBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -240,8 +245,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int nb = (nrows + kBoxRows - 1) / kBoxRows;
       const int buf = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait_bounded(&acc_full[buf], acc_phase, abort_flag, kDevErrWaitTimeoutEpilogue))
-        break;
+      const bool ok =
+          mbar_wait_bounded(&acc_full[buf], acc_phase, abort_flag, kDevErrWaitTimeoutEpilogue);
+      // The four epilogue warps agree before going on, so a failed wait in one
+      // of them can never leave the others waiting at a named barrier.
+      if (named_barrier_or(1, 128, !ok)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) + buf * C::kAccCols;
       const int feat = mt * kBM + m;
@@ -264,17 +272,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         } else {
           tmem_ld_wait();
+          // Each warp transposes its [32 features x 16 rows] block through
+          // shared memory so that a lane holds 4 consecutive features of one
+          // row, then adds them into acc[row_dst] with one 16-byte vector
+          // reduction (red.global.add.v4.f32): 4 per lane per chunk.
+          float* wsb = staging + (warp - 2) * (16 * 33);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
+          for (int i = 0; i < 16; ++i) wsb[i * 33 + lane] = __uint_as_float(v[i]);
+          __syncwarp();
+          const int fq = (lane & 7) * 4;        // feature offset inside the warp's 32
+#pragma unroll
+          for (int it = 0; it < 4; ++it) {
+            const int i = it * 4 + (lane >> 3);  // row inside the chunk
             const int n = c * 16 + i;
             if (n < nrows) {
               const int r = row0 + n;
               const int dst = args.row_dst[r];
-              if (dst >= 0 && dst < args.n_acc)
-                atomicAdd(args.acc + size_t(dst) * args.acc_ld + feat,
-                          args.row_w[r] * __uint_as_float(v[i]));
+              if (dst >= 0 && dst < args.n_acc) {
+                const float wv = args.row_w[r];
+                red_add_v4_f32(args.acc + size_t(dst) * args.acc_ld + mt * kBM + quad * 32 + fq,
+                               wv * wsb[i * 33 + fq], wv * wsb[i * 33 + fq + 1],
+                               wv * wsb[i * 33 + fq + 2], wv * wsb[i * 33 + fq + 3]);
+              }
             }
           }
+          __syncwarp();
         }
       }
       tc_fence_before();

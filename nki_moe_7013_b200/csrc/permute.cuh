@@ -7,9 +7,11 @@
 // range of rows (no padding rows at all) cut into 128-row tiles for the
 // grouped GEMMs.
 //
-//   scan kernel    (1 CTA): per-chunk histograms -> per-chunk exclusive
-//                  prefixes, expert counts / offsets, and the tile list.
-//   scatter kernel (1 CTA per router chunk): the rank of a (token, slot) pair
+//   scan kernel    (1 CTA per expert): per-chunk histogram column ->
+//                  per-chunk exclusive prefix and the expert's row count.
+//   scatter kernel (1 CTA per router chunk): expert offsets by a block scan
+//                  of the counts (CTA 0 also publishes offsets and the tile
+//                  list); the rank of a (token, slot) pair
 //                  inside its expert is the number of earlier tokens of the
 //                  chunk that chose the same expert (popcount of a bitmask)
 //                  plus the chunk prefix, so rows inside an expert follow
@@ -24,140 +26,169 @@
 namespace qmoe {
 
 constexpr int kTileRows = 128;  // rows per grouped-GEMM tile
-constexpr int kScanThreads = 1024;
+constexpr int kScanThreads = 256;
 constexpr int kScatterThreads = 256;
 
-__global__ void __launch_bounds__(kScanThreads, 1)
-    permute_scan_kernel(int32_t* __restrict__ chunk_hist, int nchunks, int E,
-                        int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
-                        int32_t* __restrict__ tiles, int max_tiles) {
-  __shared__ int part_sum[kScanThreads];  // [part][E]
-  __shared__ int tot[1024];
-  __shared__ int off_s[1025];
-  __shared__ int tile_base[1025];
-  const int tid = threadIdx.x;
-  const int parts = kScanThreads / E;
-  const int e = tid % E;
-  const int part = tid / E;
-  const bool active = part < parts;
-  const int cpp = (nchunks + parts - 1) / parts;
-  const int c0 = min(nchunks, part * cpp);
-  const int c1 = min(nchunks, c0 + cpp);
-
-  int local = 0;
-  if (active)
-    for (int c = c0; c < c1; ++c) local += chunk_hist[size_t(c) * E + e];
-  part_sum[tid] = local;
+// Exclusive block-wide scan of one int per thread (blockDim.x == 256).
+__device__ __forceinline__ int block_exclusive_scan_256(int v, int* total, int* warp_sums) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int n = __shfl_up_sync(0xFFFFFFFFu, incl, off);
+    if (lane >= off) incl += n;
+  }
+  if (lane == 31) warp_sums[warp] = incl;
   __syncthreads();
-  if (active) {
-    int run = 0;
-    for (int p = 0; p < part; ++p) run += part_sum[p * E + e];
-    for (int c = c0; c < c1; ++c) {
-      const int v = chunk_hist[size_t(c) * E + e];
-      chunk_hist[size_t(c) * E + e] = run;
-      run += v;
+  if (warp == 0) {
+    int ws = lane < 8 ? warp_sums[lane] : 0;
+#pragma unroll
+    for (int off = 1; off < 8; off <<= 1) {
+      const int n = __shfl_up_sync(0xFFFFFFFFu, ws, off);
+      if (lane >= off) ws += n;
     }
-    if (part == 0) {
-      int total = 0;
-      for (int p = 0; p < parts; ++p) total += part_sum[p * E + e];
-      tot[e] = total;
-    }
+    if (lane < 8) warp_sums[lane] = ws;  // inclusive
   }
   __syncthreads();
-  if (tid == 0) {
-    int o = 0, tb = 0;
-    for (int i = 0; i < E; ++i) {
-      off_s[i] = o;
-      tile_base[i] = tb;
-      o += tot[i];
-      tb += (tot[i] + kTileRows - 1) / kTileRows;
-    }
-    off_s[E] = o;
-    tile_base[E] = tb;
-    offsets[E] = o;
-    tiles[0] = min(tb, max_tiles);
-  }
+  const int base = warp > 0 ? warp_sums[warp - 1] : 0;
+  *total = warp_sums[7];
   __syncthreads();
-  if (tid < E) {
-    counts[tid] = tot[tid];
-    offsets[tid] = off_s[tid];
-    const int n = tot[tid];
-    int32_t* t_exp = tiles + 1;
-    int32_t* t_row0 = t_exp + max_tiles;
-    int32_t* t_rows = t_row0 + max_tiles;
-    for (int i = 0; i * kTileRows < n; ++i) {
-      const int ti = tile_base[tid] + i;
-      if (ti < max_tiles) {
-        t_exp[ti] = tid;
-        t_row0[ti] = off_s[tid] + i * kTileRows;
-        t_rows[ti] = min(kTileRows, n - i * kTileRows);
-      }
-    }
-  }
+  return base + incl - v;
 }
 
+// Column scan: CTA e turns chunk_hist[:, e] into its exclusive prefix over
+// chunks and writes counts[e].
+__global__ void __launch_bounds__(kScanThreads)
+    permute_scan_kernel(int32_t* __restrict__ chunk_hist, int nchunks, int E,
+                        int32_t* __restrict__ counts) {
+  __shared__ int warp_sums[8];
+  const int e = blockIdx.x;
+  const int per = (nchunks + kScanThreads - 1) / kScanThreads;
+  const int c0 = min(nchunks, int(threadIdx.x) * per);
+  const int c1 = min(nchunks, c0 + per);
+  int local = 0;
+  for (int c = c0; c < c1; ++c) local += chunk_hist[size_t(c) * E + e];
+  int total = 0;
+  int run = block_exclusive_scan_256(local, &total, warp_sums);
+  for (int c = c0; c < c1; ++c) {
+    const int v = chunk_hist[size_t(c) * E + e];
+    chunk_hist[size_t(c) * E + e] = run;
+    run += v;
+  }
+  if (threadIdx.x == 0) counts[e] = total;
+}
+
+// One CTA per router chunk (8 tokens); gridDim.y CTAs share the row gather.
 __global__ void __launch_bounds__(kScatterThreads)
     permute_scatter_kernel(const int32_t* __restrict__ topk_idx, const float* __restrict__ topk_w,
                            const int32_t* __restrict__ chunk_prefix,
-                           const int32_t* __restrict__ offsets,
+                           const int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
                            const __nv_bfloat16* __restrict__ x, int T, int H, int E, int k,
                            int32_t* __restrict__ row_token, float* __restrict__ row_w,
                            int32_t* __restrict__ slot_row, __nv_bfloat16* __restrict__ x_perm,
-                           float* __restrict__ acc_zero) {
+                           float* __restrict__ acc_zero, int32_t* __restrict__ tiles, int max_tiles) {
   __shared__ unsigned mask[256];
+  __shared__ int off_s[256];
   __shared__ int pos_s[kScatterThreads];
+  __shared__ int warp_sums[8];
   const int c = blockIdx.x;
+  const int part = blockIdx.y;
   const int t0 = c * kRouterChunk;
   const int nt = min(kRouterChunk, T - t0);
   const int npairs = nt * k;
-  for (int i = threadIdx.x; i < E; i += kScatterThreads) mask[i] = 0u;
+  const int tid = threadIdx.x;
+
+  // Expert offsets: exclusive scan of counts (E <= 256).
+  const int cnt = tid < E ? counts[tid] : 0;
+  int total = 0;
+  const int off = block_exclusive_scan_256(cnt, &total, warp_sums);
+  if (tid < E) off_s[tid] = off;
+  if (c == 0 && part == 0) {
+    // Also publish offsets and the 128-row tile list (expert order).
+    int tot_tiles = 0;
+    const int nt_e = (cnt + kTileRows - 1) / kTileRows;
+    const int tbase = block_exclusive_scan_256(nt_e, &tot_tiles, warp_sums);
+    if (tid < E) {
+      offsets[tid] = off;
+      int32_t* t_exp = tiles + 1;
+      int32_t* t_row0 = t_exp + max_tiles;
+      int32_t* t_rows = t_row0 + max_tiles;
+      for (int i = 0; i < nt_e; ++i) {
+        const int ti = tbase + i;
+        if (ti < max_tiles) {
+          t_exp[ti] = tid;
+          t_row0[ti] = off + i * kTileRows;
+          t_rows[ti] = min(kTileRows, cnt - i * kTileRows);
+        }
+      }
+    }
+    if (tid == 0) {
+      offsets[E] = total;
+      tiles[0] = min(tot_tiles, max_tiles);
+    }
+  }
+  for (int i = tid; i < E; i += kScatterThreads) mask[i] = 0u;
   __syncthreads();
-  const int i = threadIdx.x;
   int e = -1;
-  if (i < npairs) {
-    e = topk_idx[size_t(t0) * k + i];
+  if (tid < npairs) {
+    e = topk_idx[size_t(t0) * k + tid];
     if (e < 0 || e >= E) {
       record_device_error(kDevErrBadIndex);
       e = -1;
     } else {
-      atomicOr(&mask[e], 1u << (i / k));
+      atomicOr(&mask[e], 1u << (tid / k));
     }
   }
   __syncthreads();
-  if (i < npairs) {
+  if (tid < npairs) {
     int pos = -1;
     if (e >= 0) {
-      const int tl = i / k;
+      const int tl = tid / k;
       const int rank = __popc(mask[e] & ((1u << tl) - 1u));
-      pos = offsets[e] + chunk_prefix[size_t(c) * E + e] + rank;
-      row_token[pos] = t0 + tl;
-      row_w[pos] = topk_w[size_t(t0) * k + i];
+      pos = off_s[e] + chunk_prefix[size_t(c) * E + e] + rank;
+      if (part == 0) {
+        row_token[pos] = t0 + tl;
+        row_w[pos] = topk_w[size_t(t0) * k + tid];
+      }
     }
-    slot_row[size_t(t0) * k + i] = pos;
-    pos_s[i] = pos;
+    if (part == 0) slot_row[size_t(t0) * k + tid] = pos;
+    pos_s[tid] = pos;
   }
   __syncthreads();
   if (x_perm) {
-    const int vec_per_row = H / 8;  // 16-byte vectors
-    const int total = npairs * vec_per_row;
-    for (int v = threadIdx.x; v < total; v += kScatterThreads) {
-      const int p = v / vec_per_row;
-      const int col = (v % vec_per_row) * 8;
-      const int dst = pos_s[p];
-      if (dst < 0) continue;
-      const int tok = t0 + p / k;
-      const uint4 val = *reinterpret_cast<const uint4*>(x + size_t(tok) * H + col);
-      *reinterpret_cast<uint4*>(x_perm + size_t(dst) * H + col) = val;
+    // rows of this chunk split across gridDim.y CTAs; 4 independent 16-byte
+    // copies in flight per thread
+    const int vec_per_row = H / 8;
+    const int total_v = npairs * vec_per_row;
+    const int stride = kScatterThreads * gridDim.y;
+    for (int v0 = part * kScatterThreads + tid; v0 < total_v; v0 += 4 * stride) {
+      uint4 val[4];
+      int dst[4], col[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int v = v0 + u * stride;
+        dst[u] = -1;
+        if (v < total_v) {
+          const int p = v / vec_per_row;
+          col[u] = (v - p * vec_per_row) * 8;
+          dst[u] = pos_s[p];
+          if (dst[u] >= 0)
+            val[u] = *reinterpret_cast<const uint4*>(x + size_t(t0 + p / k) * H + col[u]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (dst[u] >= 0) *reinterpret_cast<uint4*>(x_perm + size_t(dst[u]) * H + col[u]) = val[u];
     }
   }
-  if (acc_zero) {
+  if (acc_zero && part == 0) {
     const int vec_per_row = H / 4;
-    const int total = nt * vec_per_row;
-    for (int v = threadIdx.x; v < total; v += kScatterThreads) {
+    const int total_v = nt * vec_per_row;
+    for (int v = tid; v < total_v; v += kScatterThreads) {
       const int tl = v / vec_per_row;
-      const int col = (v % vec_per_row) * 4;
-      *reinterpret_cast<float4*>(acc_zero + size_t(t0 + tl) * H + col) =
-          make_float4(0.f, 0.f, 0.f, 0.f);
+      const int cc = (v % vec_per_row) * 4;
+      *reinterpret_cast<float4*>(acc_zero + size_t(t0 + tl) * H + cc) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
 }

@@ -163,7 +163,7 @@ int launch_router(const void* x, const void* w, const float* bias, int64_t T, in
 #define QMOE_ROUTER_CASE(GG)                                                                   \
   case GG: {                                                                                   \
     QMOE_CHECK(set_smem(qmoe::router_topk_kernel<GG>, smem));                                  \
-    qmoe::router_topk_kernel<GG><<<nchunks, qmoe::kRouterThreads, smem, stream>>>(            \
+    qmoe::router_topk_kernel<GG><<<nchunks, qmoe::router_warps<GG>() * 32, smem, stream>>>(   \
         xb, wb, bias, int(T), int(E), int(k), normalize, logits, topk_idx, topk_w, chunk_hist); \
     break;                                                                                     \
   }
@@ -201,13 +201,16 @@ int launch_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chunk_
                    void* x_perm, float* acc_zero, cudaStream_t stream) {
   const int nchunks = int((T + qmoe::kRouterChunk - 1) / qmoe::kRouterChunk);
   const int64_t max_tiles = qmoe_max_tiles(T * k, E);
-  qmoe::permute_scan_kernel<<<1, qmoe::kScanThreads, 0, stream>>>(chunk_hist, nchunks, int(E), counts,
-                                                                  offsets, tiles, int(max_tiles));
+  qmoe::permute_scan_kernel<<<int(E), qmoe::kScanThreads, 0, stream>>>(chunk_hist, nchunks, int(E),
+                                                                       counts);
   QMOE_CHECK(check_launch("permute_scan_kernel"));
   if (nchunks > 0) {
-    qmoe::permute_scatter_kernel<<<nchunks, qmoe::kScatterThreads, 0, stream>>>(
-        topk_idx, topk_w, chunk_hist, offsets, static_cast<const __nv_bfloat16*>(x), int(T), int(H),
-        int(E), int(k), row_token, row_w, slot_row, static_cast<__nv_bfloat16*>(x_perm), acc_zero);
+    // Enough CTAs to keep the row gather from being latency-bound.
+    const int parts = x_perm ? int(std::max<int64_t>(1, std::min<int64_t>(8, (2 * num_sms(0) + nchunks - 1) / nchunks))) : 1;
+    qmoe::permute_scatter_kernel<<<dim3(nchunks, parts), qmoe::kScatterThreads, 0, stream>>>(
+        topk_idx, topk_w, chunk_hist, counts, offsets, static_cast<const __nv_bfloat16*>(x), int(T),
+        int(H), int(E), int(k), row_token, row_w, slot_row, static_cast<__nv_bfloat16*>(x_perm),
+        acc_zero, tiles, int(max_tiles));
     QMOE_CHECK(check_launch("permute_scatter_kernel"));
   }
   return QMOE_OK;

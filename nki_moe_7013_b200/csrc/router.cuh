@@ -19,16 +19,68 @@
 namespace qmoe {
 
 constexpr int kRouterChunk = QMOE_ROUTER_CHUNK;  // tokens per CTA (= histogram chunk)
-constexpr int kRouterThreads = 256;                // 8 warps
-static_assert(kRouterChunk == kRouterThreads / 32, "one warp per token in the top-k phase");
+constexpr int kRouterTE = 4;                       // experts per register tile
+// Warps per router CTA: 16 (two 4-expert tiles each for E=128) keeps enough
+// warps resident to hide the L2 latency of the weight stream; H = 4096 uses 8
+// so its larger register footprint fits.
+template <int G>
+constexpr int router_warps() { return G >= 16 ? 8 : 16; }
+static_assert(kRouterChunk * kRouterTE == 32, "one reduced chain per lane");
 
+// Sums v[0..31] of every lane across the warp; returns in lane l the total of
+// chain l.  Step s exchanges half of the remaining chains with lane ^ (16>>s).
+__device__ __forceinline__ float warp_reduce_32_chains(const float* v, int lane) {
+  float a[16];
+  {
+    const bool hi = lane & 16;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float keep = hi ? v[i + 16] : v[i];
+      const float send = hi ? v[i] : v[i + 16];
+      a[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, 16);
+    }
+  }
+  {
+    const bool hi = lane & 8;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float keep = hi ? a[i + 8] : a[i];
+      const float send = hi ? a[i] : a[i + 8];
+      a[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, 8);
+    }
+  }
+  {
+    const bool hi = lane & 4;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float keep = hi ? a[i + 4] : a[i];
+      const float send = hi ? a[i] : a[i + 4];
+      a[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, 4);
+    }
+  }
+  {
+    const bool hi = lane & 2;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float keep = hi ? a[i + 2] : a[i];
+      const float send = hi ? a[i] : a[i + 2];
+      a[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, 2);
+    }
+  }
+  const bool hi = lane & 1;
+  const float keep = hi ? a[1] : a[0];
+  const float send = hi ? a[0] : a[1];
+  return keep + __shfl_xor_sync(0xFFFFFFFFu, send, 1);
+}
 template <int G>  // G = H / 256
-__global__ void __launch_bounds__(kRouterThreads, 1)
+__global__ void __launch_bounds__(router_warps<G>() * 32, 1)
     router_topk_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                        const float* __restrict__ bias, int T, int E, int k, int normalize,
                        float* __restrict__ logits_out, int32_t* __restrict__ topk_idx,
                        float* __restrict__ topk_w, int32_t* __restrict__ chunk_hist) {
   constexpr int H = G * 256;
+  constexpr int kThreads = router_warps<G>() * 32;
+  static_assert(kRouterChunk <= router_warps<G>(), "one warp per token in the top-k phase");
   extern __shared__ __align__(16) float router_smem[];
   float* xs = router_smem;                        // [kRouterChunk][H]
   float* ls = router_smem + kRouterChunk * H;     // [kRouterChunk][E]
@@ -40,7 +92,7 @@ __global__ void __launch_bounds__(kRouterThreads, 1)
   const int nt = min(kRouterChunk, T - t0);
 
   // Stage the chunk's activations in shared memory as fp32.
-  for (int i = threadIdx.x; i < kRouterChunk * (H / 8); i += kRouterThreads) {
+  for (int i = threadIdx.x; i < kRouterChunk * (H / 8); i += kThreads) {
     const int t = i / (H / 8);
     const int c = (i % (H / 8)) * 8;
     float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
@@ -54,46 +106,70 @@ __global__ void __launch_bounds__(kRouterThreads, 1)
     *reinterpret_cast<float4*>(xs + t * H + c) = lo;
     *reinterpret_cast<float4*>(xs + t * H + c + 4) = hi;
   }
-  for (int i = threadIdx.x; i < 256; i += kRouterThreads) hist[i] = 0;
+  for (int i = threadIdx.x; i < 256; i += kThreads) hist[i] = 0;
   __syncthreads();
 
-  // Logits: warp w handles experts w, w+8, ...; the lane keeps its slice of the
-  // expert row in registers and reuses it for every token of the chunk.
-  for (int e = warp; e < E; e += kRouterThreads / 32) {
-    float wr[G * 8];
+  // Logits.  Experts are taken four at a time (tile i = experts 4i..4i+3,
+  // tiles dealt round-robin to the warps) for all 8 tokens of the chunk: 32
+  // independent fp32 chains per lane (token t x expert j), each accumulating
+  // the lane's canonical slice group-major.  Weights stream from L2 one group
+  // ahead; activations come from shared memory.
+  for (int tile = warp; tile < E / kRouterTE; tile += router_warps<G>()) {
+    const int e0 = tile * kRouterTE;
+    const __nv_bfloat16* wp = w + size_t(e0) * H + 8 * lane;
+    float acc[kRouterChunk][kRouterTE];
+#pragma unroll
+    for (int t = 0; t < kRouterChunk; ++t)
+#pragma unroll
+      for (int j = 0; j < kRouterTE; ++j) acc[t][j] = 0.f;
+    uint4 wv[kRouterTE];
+#pragma unroll
+    for (int j = 0; j < kRouterTE; ++j)
+      wv[j] = __ldg(reinterpret_cast<const uint4*>(wp + size_t(j) * H));
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      const uint4 v = __ldg(reinterpret_cast<const uint4*>(w + size_t(e) * H + 256 * g + 8 * lane));
-      wr[8 * g + 0] = bf16lo_to_f32(v.x);
-      wr[8 * g + 1] = bf16hi_to_f32(v.x);
-      wr[8 * g + 2] = bf16lo_to_f32(v.y);
-      wr[8 * g + 3] = bf16hi_to_f32(v.y);
-      wr[8 * g + 4] = bf16lo_to_f32(v.z);
-      wr[8 * g + 5] = bf16hi_to_f32(v.z);
-      wr[8 * g + 6] = bf16lo_to_f32(v.w);
-      wr[8 * g + 7] = bf16hi_to_f32(v.w);
-    }
-    const float be = bias ? bias[e] : 0.f;
-    for (int t = 0; t < nt; ++t) {
-      const float* xr = xs + t * H + 8 * lane;
-      float acc = 0.f;
+      uint4 wn[kRouterTE];
+      if (g + 1 < G) {
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float4 a = *reinterpret_cast<const float4*>(xr + 256 * g);
-        const float4 b = *reinterpret_cast<const float4*>(xr + 256 * g + 4);
-        acc = fmaf(a.x, wr[8 * g + 0], acc);
-        acc = fmaf(a.y, wr[8 * g + 1], acc);
-        acc = fmaf(a.z, wr[8 * g + 2], acc);
-        acc = fmaf(a.w, wr[8 * g + 3], acc);
-        acc = fmaf(b.x, wr[8 * g + 4], acc);
-        acc = fmaf(b.y, wr[8 * g + 5], acc);
-        acc = fmaf(b.z, wr[8 * g + 6], acc);
-        acc = fmaf(b.w, wr[8 * g + 7], acc);
+        for (int j = 0; j < kRouterTE; ++j)
+          wn[j] = __ldg(reinterpret_cast<const uint4*>(wp + size_t(j) * H + 256 * (g + 1)));
+      }
+      float wf[kRouterTE][8];
+#pragma unroll
+      for (int j = 0; j < kRouterTE; ++j) {
+        wf[j][0] = bf16lo_to_f32(wv[j].x);
+        wf[j][1] = bf16hi_to_f32(wv[j].x);
+        wf[j][2] = bf16lo_to_f32(wv[j].y);
+        wf[j][3] = bf16hi_to_f32(wv[j].y);
+        wf[j][4] = bf16lo_to_f32(wv[j].z);
+        wf[j][5] = bf16hi_to_f32(wv[j].z);
+        wf[j][6] = bf16lo_to_f32(wv[j].w);
+        wf[j][7] = bf16hi_to_f32(wv[j].w);
       }
 #pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, off);
-      if (lane == 0) ls[t * E + e] = bias ? __fadd_rn(acc, be) : acc;
+      for (int t = 0; t < kRouterChunk; ++t) {
+        const float* xr = xs + t * H + 256 * g + 8 * lane;
+        const float4 a = *reinterpret_cast<const float4*>(xr);
+        const float4 b = *reinterpret_cast<const float4*>(xr + 4);
+        const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+#pragma unroll
+          for (int j = 0; j < kRouterTE; ++j) acc[t][j] = fmaf(xv[q], wf[j][q], acc[t][j]);
+      }
+      if (g + 1 < G) {
+#pragma unroll
+        for (int j = 0; j < kRouterTE; ++j) wv[j] = wn[j];
+      }
     }
+    // Cross-lane sum of the 32 chains by recursive halving.  Every partial
+    // sum formed here is the same pairwise sum the xor butterfly forms (fp32
+    // addition commutes), so the result is bit-identical to the butterfly;
+    // it ends with chain index v = lane in lane `lane`.
+    const float v = warp_reduce_32_chains(&acc[0][0], lane);
+    const int t = lane / kRouterTE;
+    const int e = e0 + lane % kRouterTE;
+    if (t < nt) ls[t * E + e] = bias ? __fadd_rn(v, bias[e]) : v;
   }
   __syncthreads();
 
@@ -177,7 +253,7 @@ __global__ void __launch_bounds__(kRouterThreads, 1)
   }
   if (chunk_hist) {
     __syncthreads();
-    for (int e = threadIdx.x; e < E; e += kRouterThreads)
+    for (int e = threadIdx.x; e < E; e += kThreads)
       chunk_hist[size_t(blockIdx.x) * E + e] = hist[e];
   }
 }

@@ -52,18 +52,21 @@ def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
 def normal_bf16(seed: int, name: str, shape, std: float = 1.0, mean: float = 0.0) -> torch.Tensor:
     """Counter-based N(mean, std^2) sample rounded to bf16 (CPU tensor)."""
     n = int(np.prod(shape)) if len(shape) else 1
-    ctr = np.arange(n, dtype=np.uint64)
-    with np.errstate(over="ignore"):
-        base = (ctr * np.uint64(2)) ^ _stream_key(seed, name)
-    a = _splitmix64(base)
-    b = _splitmix64(base ^ np.uint64(0xD1B54A32D192ED03))
-    # 53-bit uniforms in (0, 1]
-    u1 = ((a >> np.uint64(11)).astype(np.float64) + 1.0) / 9007199254740992.0
-    u2 = (b >> np.uint64(11)).astype(np.float64) / 9007199254740992.0
-    z = np.sqrt(-2.0 * np.log(u1)) * np.cos(2.0 * np.pi * u2)
-    vals = (z * std + mean).astype(np.float32).reshape(shape)
-    bits = f32_to_bf16_bits(vals)
-    return torch.from_numpy(bits.view(np.int16).copy()).view(torch.bfloat16).reshape(shape)
+    key = _stream_key(seed, name)
+    out = np.empty(n, dtype=np.uint16)
+    block = 1 << 18  # cache-sized blocks
+    for s0 in range(0, n, block):
+        ctr = np.arange(s0, min(n, s0 + block), dtype=np.uint64)
+        with np.errstate(over="ignore"):
+            base = (ctr * np.uint64(2)) ^ key
+        a = _splitmix64(base)
+        b = _splitmix64(base ^ np.uint64(0xD1B54A32D192ED03))
+        # 53-bit uniforms in (0, 1]
+        u1 = ((a >> np.uint64(11)).astype(np.float64) + 1.0) / 9007199254740992.0
+        u2 = (b >> np.uint64(11)).astype(np.float64) / 9007199254740992.0
+        z = np.sqrt(-2.0 * np.log(u1)) * np.cos(2.0 * np.pi * u2)
+        out[s0:s0 + len(ctr)] = f32_to_bf16_bits((z * std + mean).astype(np.float32))
+    return torch.from_numpy(out.view(np.int16)).view(torch.bfloat16).reshape(shape)
 
 
 def normal_bf16_device(seed: int, shape, std: float = 1.0, device="cuda") -> torch.Tensor:
