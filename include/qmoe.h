@@ -198,6 +198,30 @@ QMOE_API int qmoe_moe_forward(const void* x, const void* w_router, const float* 
                      void* out, int32_t* topk_idx, float* topk_w, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Allocation-free fused forward.  No counterpart in the reference: it exists
+ * for callers that cannot allocate device memory where they run the layer --
+ * plugin enqueue hooks of inference runtimes, which may only queue work on the
+ * stream they are given (cudaMalloc there can synchronise the device), and
+ * embedders that own all device memory and hand this library no workspace.
+ *
+ * Same arguments and result as qmoe_moe_forward without the workspace.  Its
+ * scratch is one built-in device array of QMOE_NOALLOC_SCRATCH_BYTES (8 MiB,
+ * held on every GPU that loads the library until the process exits): enough
+ * for up to 150 tokens per call at Qwen3-30B-A3B shapes.  Larger calls return
+ * QMOE_ERR_WORKSPACE_TOO_SMALL without launching anything.  The first call on
+ * each device looks the array up (cudaGetSymbolAddress) -- make it before any
+ * stream capture.  All calls share the array: calls that overlap on the GPU
+ * race, so serialise them (e.g. one stream).  Nothing in it needs clearing;
+ * every call rewrites what it reads.
+ * ---------------------------------------------------------------------- */
+#define QMOE_NOALLOC_SCRATCH_BYTES (8u << 20)
+QMOE_API int qmoe_moe_forward_noalloc(const void* x, const void* w_router, const float* router_bias,
+                                      const void* w_gate_up, const void* w_down,
+                                      const void* residual, int64_t T, int64_t H, int64_t E,
+                                      int64_t k, int64_t I, int normalize, void* out,
+                                      int32_t* topk_idx, float* topk_w, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -37,6 +37,7 @@ _SIGNATURES = {
     "qmoe_combine_finalize": (I32, [P, P, I64, I64, P, P]),
     "qmoe_moe_forward_workspace_size": (SZ, [I64, I64, I64, I64, I64]),
     "qmoe_moe_forward": (I32, [P, P, P, P, P, P, I64, I64, I64, I64, I64, I32, P, P, P, P, SZ, P]),
+    "qmoe_moe_forward_noalloc": (I32, [P, P, P, P, P, P, I64, I64, I64, I64, I64, I32, P, P, P, P]),
 }
 
 

@@ -537,3 +537,114 @@ int qmoe_moe_forward(const void* x, const void* w_router, const float* router_bi
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of qmoe_moe_forward (no counterpart in the
+// reference).  Some callers cannot allocate device memory at the point where
+// they run the layer: plugin "enqueue" hooks of inference runtimes may only
+// queue work on the stream they are handed (a cudaMalloc there can
+// synchronise the whole device), and embedders that own every byte of device
+// memory hand this library no workspace.  This entry point takes its scratch
+// from the fixed array below instead of a caller workspace.
+//
+//  - Size limit: kNoAllocScratchBytes (QMOE_NOALLOC_SCRATCH_BYTES, 8 MiB).
+//    At Qwen3-30B-A3B shapes (H 2048, 128 experts, top-8, I 768) that holds
+//    the scratch of up to 150 tokens per call -- decode-sized batches.
+//    Larger calls are rejected with QMOE_ERR_WORKSPACE_TOO_SMALL before
+//    anything is launched.
+//  - The array lives in every GPU's memory as soon as the library's device
+//    code is loaded on that GPU, and stays there until the process exits.
+//  - Set-up: the first call on each device looks up the array's device
+//    address with cudaGetSymbolAddress (which also loads the module on that
+//    device); make that first call before any stream capture.
+//  - All calls share the one array and it keeps the last call's contents.
+//    Nothing in it needs to start at zero: the routing kernels rewrite every
+//    index buffer and the permutation kernel zero-fills the fp32 combine
+//    accumulator on each call.  Calls that overlap on the GPU (different
+//    streams, or several host threads) race on the array: serialise them.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = QMOE_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::once_flag g_noalloc_once[kMaxDevices];
+void* g_noalloc_ptr[kMaxDevices];
+cudaError_t g_noalloc_status[kMaxDevices];
+
+// Device address of g_noalloc_scratch on the current device (looked up once
+// per device, with that device current).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return set_error(QMOE_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(err));
+  if (dev < 0 || dev >= kMaxDevices) return set_error(QMOE_ERR_DEVICE, "device ordinal %d out of range", dev);
+  std::call_once(g_noalloc_once[dev], [dev]() {
+    void* p = nullptr;
+    g_noalloc_status[dev] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    g_noalloc_ptr[dev] = p;
+  });
+  if (g_noalloc_status[dev] != cudaSuccess || g_noalloc_ptr[dev] == nullptr)
+    return set_error(QMOE_ERR_CUDA, "cudaGetSymbolAddress(scratch) on device %d: %s", dev,
+                     cudaGetErrorString(g_noalloc_status[dev]));
+  *out = g_noalloc_ptr[dev];
+  return QMOE_OK;
+}
+
+}  // namespace
+
+extern "C" int qmoe_moe_forward_noalloc(const void* x, const void* w_router,
+                                        const float* router_bias, const void* w_gate_up,
+                                        const void* w_down, const void* residual, int64_t T,
+                                        int64_t H, int64_t E, int64_t k, int64_t I, int normalize,
+                                        void* out, int32_t* topk_idx, float* topk_w, void* stream) {
+  QMOE_REQUIRE(x && w_router && w_gate_up && w_down && out, QMOE_ERR_INVALID_ARGUMENT,
+               "moe_forward_noalloc: null pointer");
+  QMOE_REQUIRE(T >= 0 && T < (int64_t(1) << 31) / 32, QMOE_ERR_INVALID_ARGUMENT,
+               "moe_forward_noalloc: bad T");
+  QMOE_REQUIRE(H > 0 && H % 256 == 0 && H <= 4096, QMOE_ERR_UNSUPPORTED_SHAPE,
+               "moe_forward_noalloc: H=%lld must be a multiple of 256 and <= 4096", (long long)H);
+  QMOE_REQUIRE(E >= 32 && E <= 256 && E % 32 == 0, QMOE_ERR_UNSUPPORTED_SHAPE,
+               "moe_forward_noalloc: E=%lld must be a multiple of 32 in [32, 256]", (long long)E);
+  QMOE_REQUIRE(k >= 1 && k <= E && k <= 32, QMOE_ERR_INVALID_ARGUMENT, "moe_forward_noalloc: k invalid");
+  QMOE_REQUIRE(I > 0 && I % qmoe::kBM == 0, QMOE_ERR_UNSUPPORTED_SHAPE,
+               "moe_forward_noalloc: I %% 128 != 0");
+  QMOE_REQUIRE(E * 2 * I < (int64_t(1) << 31) && E * H < (int64_t(1) << 31), QMOE_ERR_UNSUPPORTED_SHAPE,
+               "moe_forward_noalloc: weights too large");
+  QMOE_REQUIRE(aligned16(x) && aligned16(w_router) && aligned16(w_gate_up) && aligned16(w_down) &&
+                   aligned16(out) && (!residual || aligned16(residual)),
+               QMOE_ERR_MISALIGNED, "moe_forward_noalloc: pointers must be 16-byte aligned");
+  const FwdLayout L = fwd_layout(T, H, E, k, I);
+  QMOE_REQUIRE(L.total <= kNoAllocScratchBytes, QMOE_ERR_WORKSPACE_TOO_SMALL,
+               "moe_forward_noalloc: %lld tokens need %zu bytes of scratch but the built-in scratch "
+               "holds %zu; use qmoe_moe_forward with a caller workspace",
+               (long long)T, L.total, kNoAllocScratchBytes);
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  void* scratch = nullptr;
+  QMOE_CHECK(noalloc_scratch(&scratch));
+  if (T == 0) return QMOE_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(scratch);
+  int32_t* chunk_hist = reinterpret_cast<int32_t*>(ws + L.chunk_hist);
+  int32_t* counts = reinterpret_cast<int32_t*>(ws + L.counts);
+  int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
+  int32_t* row_token = reinterpret_cast<int32_t*>(ws + L.row_token);
+  float* row_w = reinterpret_cast<float*>(ws + L.row_w);
+  int32_t* slot_row = reinterpret_cast<int32_t*>(ws + L.slot_row);
+  int32_t* tiles = reinterpret_cast<int32_t*>(ws + L.tiles);
+  int32_t* idx = topk_idx ? topk_idx : reinterpret_cast<int32_t*>(ws + L.topk_idx);
+  float* tw = topk_w ? topk_w : reinterpret_cast<float*>(ws + L.topk_w);
+  void* x_perm = ws + L.x_perm;
+  void* act = ws + L.act;
+  float* acc = reinterpret_cast<float*>(ws + L.acc);
+  const int64_t R = T * k;
+  const int64_t max_tiles = qmoe_max_tiles(R, E);
+  QMOE_CHECK(launch_router(x, w_router, router_bias, T, H, E, k, normalize, nullptr, idx, tw,
+                           chunk_hist, s));
+  QMOE_CHECK(launch_permute(idx, tw, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w,
+                            slot_row, tiles, x_perm, acc, s));
+  QMOE_CHECK(launch_gemm_gateup(x_perm, w_gate_up, tiles, max_tiles, R, H, I, E, act, s));
+  QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s));
+  return launch_finalize(acc, residual, T, H, out, s);
+}
