@@ -199,6 +199,78 @@ QMOE_API int qmoe_moe_forward(const void* x, const void* w_router, const float* 
                      size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Dense projection out (T, N) bf16 = x (T, K) . w (N, K)^T, the nn.Linear
+ * convention, on the same TMA + tcgen05 pipeline as the expert GEMMs (one
+ * "expert", dense row tiles).  Replaces the QKV and o_proj projections of
+ * NeuronAttentionBase (qwen.py:313-341).  Requires K % 64 == 0, N % 128 == 0.
+ * ---------------------------------------------------------------------- */
+QMOE_API int qmoe_linear(const void* x, const void* w, int64_t T, int64_t K, int64_t N, void* out,
+                         void* stream);
+
+/* ------------------------------------------------------------------------
+ * K4  RMSNorm: out = x * rsqrt(mean(x^2) + eps) * weight, fp32 math, one
+ * output rounding (NxDI CustomRMSNorm / _nki_rmsnorm_kernel,
+ * qwen_with_nki.py:1286-1342; get_rmsnorm_cls qwen.py:236-240).
+ *   x        (rows, H) bf16, or fp32 when x_is_fp32
+ *   residual (rows, H) bf16 or NULL: when given, s = bf16(x + residual) is
+ *            written to residual_out and normalised (the decoder layer's
+ *            residual add, qwen.py:423 and 428)
+ *   weight   (H) fp32
+ *   out      (rows, H) bf16, or fp32 when out_is_fp32
+ * ---------------------------------------------------------------------- */
+QMOE_API int qmoe_rmsnorm(const void* x, int x_is_fp32, const void* residual, const float* weight,
+                          int64_t rows, int64_t H, float eps, void* out, int out_is_fp32,
+                          void* residual_out, void* stream);
+
+/* ------------------------------------------------------------------------
+ * K4  per-head QK-RMSNorm + RoPE + KV-cache append (q_layernorm /
+ * k_layernorm qwen.py:333-335, RotaryEmbedding qwen.py:315-319).
+ *   qkv       (T, (nh + 2 nkv) * 128) bf16: q heads, k heads, v heads
+ *   positions (T) int32 absolute positions; cache_slot (T) int32 or NULL (0)
+ *   q_norm_w, k_norm_w (128) fp32; inv_freq (64) fp32 (1/theta^(2i/128))
+ *   q_out     (T, nh, 128) bf16 normalised + rotated queries
+ *   k_cache, v_cache (n_slots, nkv, max_seq, 128) bf16: row `positions[t]` of
+ *             slot cache_slot[t] receives the rotated key / the value
+ * head_dim must be 128.
+ * ---------------------------------------------------------------------- */
+QMOE_API int qmoe_qk_norm_rope(const void* qkv, const int32_t* positions, const int32_t* cache_slot,
+                               const float* q_norm_w, const float* k_norm_w, const float* inv_freq,
+                               int64_t T, int64_t nh, int64_t nkv, int64_t head_dim, float eps,
+                               void* q_out, void* k_cache, void* v_cache, int64_t n_slots,
+                               int64_t max_seq, void* stream);
+
+/* ------------------------------------------------------------------------
+ * K5  causal GQA flash-prefill over the KV cache (NxDI attention with the
+ * flash kernel of qwen.py:25-28, 49).  B sequences of S queries each:
+ *   q (B*S, nh, 128) bf16; query i of sequence b sits at position
+ *   q_start[b] + i and attends to cache rows 0 .. q_start[b] + i of slot
+ *   cache_slot[b] (NULL: slot b) of the (n_slots, nkv, max_seq, 128) caches.
+ *   out (B*S, nh*128) bf16.  scale is usually 1/sqrt(128).  A q_start or
+ *   slot outside the cache makes the CTA record QMOE device error 4 and
+ *   write nothing.
+ * ---------------------------------------------------------------------- */
+QMOE_API int qmoe_attention_prefill(const void* q, const void* k_cache, const void* v_cache,
+                                    const int32_t* q_start, const int32_t* cache_slot, int64_t B,
+                                    int64_t S, int64_t nh, int64_t nkv, int64_t head_dim,
+                                    int64_t n_slots, int64_t max_seq, float scale, void* out,
+                                    void* stream);
+
+/* ------------------------------------------------------------------------
+ * K5  split-KV flash-decode: one query per sequence (q (B, nh, 128) bf16)
+ * against kv_len[b] cache rows; 8 query heads per KV head.  max_len bounds
+ * kv_len; nsplit from qmoe_attention_decode_splits; workspace of
+ * qmoe_attention_decode_workspace_size bytes (256-byte aligned).
+ * out (B, nh*128) bf16.
+ * ---------------------------------------------------------------------- */
+QMOE_API int64_t qmoe_attention_decode_splits(int64_t B, int64_t nkv, int64_t max_len);
+QMOE_API size_t qmoe_attention_decode_workspace_size(int64_t B, int64_t nh, int64_t nsplit);
+QMOE_API int qmoe_attention_decode(const void* q, const void* k_cache, const void* v_cache,
+                                   const int32_t* kv_len, const int32_t* cache_slot, int64_t B,
+                                   int64_t nh, int64_t nkv, int64_t head_dim, int64_t n_slots,
+                                   int64_t max_seq, int64_t max_len, int64_t nsplit, float scale,
+                                   void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
  * Allocation-free fused forward.  No counterpart in the reference: it exists
  * for callers that cannot allocate device memory where they run the layer --
  * plugin enqueue hooks of inference runtimes, which may only queue work on the

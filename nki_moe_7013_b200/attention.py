@@ -1,0 +1,136 @@
+"""Attention sub-layer of the Qwen3-MoE decoder layer (secondary target).
+
+``Qwen3MoeAttention.forward(hidden_states, position_ids=None,
+past_key_value=None) -> (out, present_kv)`` mirrors NxDI's
+NeuronQwen3MoEAttention (qwen.py:313-341): fused QKV projection, per-head
+q/k RMSNorm (qwen.py:333-335), RoPE theta 1e6 (qwen.py:315-319), causal GQA
+over a KV cache, o_proj.  Positions follow the HF convention (the position of
+a new token = the number of tokens already cached).
+
+All kernels come from the CUDA library: tcgen05 projections (``ops.linear``),
+the fused QK-norm + RoPE + cache append, flash-prefill / split-KV
+flash-decode.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List, Optional
+
+import torch
+from torch import nn
+
+from . import ops
+from .config import Qwen3MoeConfig
+
+
+def rope_inv_freq(head_dim: int, theta: float, device) -> torch.Tensor:
+    """fp32 inverse frequencies, computed the way HF / NxDI RotaryEmbedding do."""
+    return (1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).float() / head_dim))).to(device)
+
+
+class KVCache:
+    """K and V caches (slots, nkv, max_seq, head_dim) bf16 plus per-slot lengths.
+
+    ``lengths`` is kept on the host (it drives shapes and launch sizes) and
+    mirrored on the device for the kernels."""
+
+    def __init__(self, n_slots: int, nkv: int, max_seq: int, head_dim: int, device="cuda"):
+        self.k = torch.zeros((n_slots, nkv, max_seq, head_dim), dtype=torch.bfloat16, device=device)
+        self.v = torch.zeros_like(self.k)
+        self.lengths: List[int] = [0] * n_slots
+        self.max_seq = max_seq
+
+    @property
+    def n_slots(self) -> int:
+        return self.k.shape[0]
+
+    def fill_random(self, length: int, seed: int = 0) -> "KVCache":
+        """Config-2 setup: every slot holds `length` tokens of ~N(0,1) bf16."""
+        g = torch.Generator(device=self.k.device)
+        g.manual_seed(seed)
+        self.k[:, :, :length].normal_(generator=g)
+        self.v[:, :, :length].normal_(generator=g)
+        self.lengths = [length] * self.n_slots
+        return self
+
+
+@dataclass
+class AttnWeights:
+    wqkv: torch.Tensor     # (nh*hd + 2*nkv*hd, H) bf16: q rows, k rows, v rows
+    wo: torch.Tensor       # (H, nh*hd) bf16
+    q_norm: torch.Tensor   # (hd,) fp32
+    k_norm: torch.Tensor   # (hd,) fp32
+
+    @staticmethod
+    def random(cfg: Qwen3MoeConfig, seed: int = 0, device="cuda", std: float = 0.02) -> "AttnWeights":
+        from .synth import normal_bf16_device
+
+        H, nh, nkv, hd = cfg.hidden_size, cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        g = torch.Generator(device=device)
+        g.manual_seed(seed * 10 + 7)
+        return AttnWeights(
+            normal_bf16_device(seed * 10 + 5, ((nh + 2 * nkv) * hd, H), std, device),
+            normal_bf16_device(seed * 10 + 6, (H, nh * hd), std, device),
+            (1.0 + 0.1 * torch.randn(hd, generator=g, device=device)).float(),
+            (1.0 + 0.1 * torch.randn(hd, generator=g, device=device)).float())
+
+    @staticmethod
+    def from_hf(attn, device="cuda") -> "AttnWeights":
+        """From a transformers Qwen3MoeAttention (q/k/v/o_proj, q_norm, k_norm)."""
+        bf = dict(device=device, dtype=torch.bfloat16)
+        wqkv = torch.cat([attn.q_proj.weight, attn.k_proj.weight, attn.v_proj.weight], 0)
+        return AttnWeights(wqkv.detach().to(**bf).contiguous(), attn.o_proj.weight.detach().to(**bf).contiguous(),
+                           attn.q_norm.weight.detach().float().to(device).contiguous(),
+                           attn.k_norm.weight.detach().float().to(device).contiguous())
+
+
+class Qwen3MoeAttention(nn.Module):
+    def __init__(self, cfg: Qwen3MoeConfig, weights: Optional[AttnWeights] = None, device="cuda",
+                 seed: int = 0):
+        super().__init__()
+        if cfg.head_dim != 128:
+            raise ValueError("the attention kernels are built for head_dim 128")
+        self.cfg = cfg
+        self.w = weights if weights is not None else AttnWeights.random(cfg, seed, device)
+        self.inv_freq = rope_inv_freq(cfg.head_dim, cfg.rope_theta, self.w.wqkv.device)
+        self._decode_ws: Optional[torch.Tensor] = None
+
+    def new_cache(self, n_slots: int, max_seq: int) -> KVCache:
+        return KVCache(n_slots, self.cfg.num_key_value_heads, max_seq, self.cfg.head_dim, self.w.wqkv.device)
+
+    def forward(self, hidden_states: torch.Tensor, position_ids: Optional[torch.Tensor] = None,
+                past_key_value: Optional[KVCache] = None):
+        cfg = self.cfg
+        B, S, H = hidden_states.shape
+        dev = hidden_states.device
+        cache = past_key_value if past_key_value is not None else self.new_cache(B, S)
+        if cache.n_slots < B:
+            raise ValueError("KV cache has fewer slots than the batch")
+        L0 = cache.lengths[:B]
+        if max(L0) + S > cache.max_seq:
+            raise ValueError("KV cache is full")
+        x2d = hidden_states.reshape(B * S, H).to(torch.bfloat16).contiguous()
+        if position_ids is None:
+            pos = (torch.tensor(L0, dtype=torch.int32).unsqueeze(1) + torch.arange(S, dtype=torch.int32))
+        else:
+            pos = position_ids.reshape(B, S).to(torch.int32).cpu()
+            if not torch.equal(pos[:, 0], torch.tensor(L0, dtype=torch.int32)) or (
+                    S > 1 and not torch.all(pos[:, 1:] - pos[:, :-1] == 1)):
+                raise ValueError("position_ids must continue each sequence's cache contiguously")
+        positions = pos.reshape(-1).to(dev, non_blocking=True)
+        slots = torch.arange(B, dtype=torch.int32).repeat_interleave(S).to(dev, non_blocking=True)
+        qkv = ops.linear(x2d, self.w.wqkv)
+        q = ops.qk_norm_rope(qkv, positions, self.w.q_norm, self.w.k_norm, self.inv_freq,
+                             cfg.num_attention_heads, cfg.num_key_value_heads, cfg.rms_norm_eps,
+                             cache.k, cache.v, cache_slot=slots)
+        if S == 1:
+            kv_len = torch.tensor([l + 1 for l in L0], dtype=torch.int32).to(dev, non_blocking=True)
+            attn = ops.attention_decode(q, cache.k, cache.v, kv_len, max(L0) + 1,
+                                        workspace=self._decode_ws)
+        else:
+            q_start = torch.tensor(L0, dtype=torch.int32).to(dev, non_blocking=True)
+            attn = ops.attention_prefill(q, cache.k, cache.v, q_start, B, S)
+        for b in range(B):
+            cache.lengths[b] += S
+        out = ops.linear(attn, self.w.wo)
+        return out.reshape(B, S, H), cache

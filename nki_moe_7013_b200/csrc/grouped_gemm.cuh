@@ -38,8 +38,16 @@ constexpr int kBoxRows = 16;   // rows per activation TMA box
 constexpr int kUmmaK = 16;     // k per tcgen05.mma (bf16)
 constexpr int kGemmThreads = 192;
 
-template <bool kGateUp>
+// Epilogue modes of the one GEMM kernel.
+enum GemmMode : int {
+  kModeDown = 0,    // weighted rows reduced into an fp32 accumulator (combine)
+  kModeGateUp = 1,  // two accumulators (gate, up) -> bf16 SiLU(gate)*up
+  kModePlain = 2,   // one accumulator -> bf16 store (dense projections)
+};
+
+template <int kMode>
 struct GemmCfg {
+  static constexpr bool kGateUp = kMode == kModeGateUp;
   static constexpr int kATiles = kGateUp ? 2 : 1;
   static constexpr int kABytes = kBM * kBK * 2;           // 16 KB
   static constexpr int kBBytes = kBNMax * kBK * 2;        // 16 KB
@@ -49,19 +57,21 @@ struct GemmCfg {
   static constexpr int kTmemCols = 2 * kAccCols;
   static constexpr int kBarrierBytes = 256;
   // down epilogue: per epilogue warp a [16 rows][33] fp32 transpose buffer
-  static constexpr int kStagingBytes = kGateUp ? 0 : 4 * 16 * 33 * 4;
+  static constexpr int kStagingBytes = kMode == kModeDown ? 4 * 16 * 33 * 4 : 0;
   static constexpr int kSmemBytes =
       1024 /*align slack*/ + kStages * kStageBytes + kBarrierBytes + kStagingBytes;
 };
 
 struct GemmArgs {
-  const int32_t* tiles;  // [0] = ntiles, then expert[max_tiles], row0[max_tiles], nrows[max_tiles]
+  const int32_t* tiles;  // [0] = ntiles, then expert[max_tiles], row0[max_tiles], nrows[max_tiles];
+                         // nullptr = dense: ceil(dense_rows/128) tiles of expert 0
   int max_tiles;
+  int dense_rows;
   int n_mtiles;          // feature blocks per tile
   int num_kb;            // K / kBK
   int a_rows_per_expert; // 2I (gate/up) or H (down)
   int up_row_offset;     // I (gate/up only)
-  // gate/up epilogue
+  // gate/up and plain epilogues: bf16 output rows
   __nv_bfloat16* act;
   int act_ld;
   // down epilogue
@@ -72,11 +82,25 @@ struct GemmArgs {
   int n_acc;
 };
 
-template <bool kGateUp>
+// Tile accessors: the device-built tile list, or a dense row range.
+struct TileView {
+  const int32_t* exp;
+  const int32_t* row0;
+  const int32_t* rows;
+  int dense_rows;
+  __device__ __forceinline__ int expert(int t) const { return exp ? exp[t] : 0; }
+  __device__ __forceinline__ int first_row(int t) const { return exp ? row0[t] : t * kBNMax; }
+  __device__ __forceinline__ int nrows(int t) const {
+    return exp ? rows[t] : min(kBNMax, dense_rows - t * kBNMax);
+  }
+};
+
+template <int kMode>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
-  using C = GemmCfg<kGateUp>;
+  using C = GemmCfg<kMode>;
+  constexpr bool kGateUp = C::kGateUp;
   extern __shared__ uint8_t gemm_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(gemm_smem_raw) + 1023) & ~uintptr_t(1023));
@@ -117,11 +141,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int ntiles = min(args.tiles[0], args.max_tiles);
+  const int ntiles = args.tiles ? min(args.tiles[0], args.max_tiles)
+                                 : (args.dense_rows + kBNMax - 1) / kBNMax;
   const int total_units = ntiles * args.n_mtiles;
-  const int32_t* t_exp = args.tiles + 1;
-  const int32_t* t_row0 = t_exp + args.max_tiles;
-  const int32_t* t_rows = t_row0 + args.max_tiles;
+  const TileView tv{args.tiles ? args.tiles + 1 : nullptr,
+                    args.tiles ? args.tiles + 1 + args.max_tiles : nullptr,
+                    args.tiles ? args.tiles + 1 + 2 * args.max_tiles : nullptr, args.dense_rows};
 
   if (warp == 0) {
     if (lane == 0) {
@@ -136,9 +161,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int u = blockIdx.x; ok && u < total_units; u += gridDim.x) {
         const int tile = u / args.n_mtiles;
         const int mt = u - tile * args.n_mtiles;
-        const int e = t_exp[tile];
-        const int row0 = t_row0[tile];
-        const int nb = (t_rows[tile] + kBoxRows - 1) / kBoxRows;
+        const int e = tv.expert(tile);
+        const int row0 = tv.first_row(tile);
+        const int nb = (tv.nrows(tile) + kBoxRows - 1) / kBoxRows;
         const int a_row = e * args.a_rows_per_expert + mt * kBM;
         const uint32_t bytes = C::kATiles * C::kABytes + nb * kBoxRows * kBK * 2;
         for (int kb = 0; kb < args.num_kb; ++kb) {
@@ -185,7 +210,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool ok = true;
       for (int u = blockIdx.x; ok && u < total_units; u += gridDim.x, ++local) {
         const int tile = u / args.n_mtiles;
-        const int nb = (t_rows[tile] + kBoxRows - 1) / kBoxRows;
+        const int nb = (tv.nrows(tile) + kBoxRows - 1) / kBoxRows;
         const uint32_t idesc = make_idesc_bf16(kBM, nb * kBoxRows);
         const int buf = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
@@ -240,8 +265,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int u = blockIdx.x; u < total_units; u += gridDim.x, ++local) {
       const int tile = u / args.n_mtiles;
       const int mt = u - tile * args.n_mtiles;
-      const int row0 = t_row0[tile];
-      const int nrows = t_rows[tile];
+      const int row0 = tv.first_row(tile);
+      const int nrows = tv.nrows(tile);
       const int nb = (nrows + kBoxRows - 1) / kBoxRows;
       const int buf = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
@@ -256,7 +281,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int c = 0; c < nb; ++c) {
         uint32_t v[16];
         tmem_ld_32x32b_x16(taddr + c * 16, v);
-        if constexpr (kGateUp) {
+        if constexpr (kMode == kModePlain) {
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int n = c * 16 + i;
+            if (n < nrows)
+              args.act[size_t(row0 + n) * args.act_ld + feat] = __float2bfloat16_rn(__uint_as_float(v[i]));
+          }
+        } else if constexpr (kGateUp) {
           uint32_t up[16];
           tmem_ld_32x32b_x16(taddr + kBM + c * 16, up);
           tmem_ld_wait();

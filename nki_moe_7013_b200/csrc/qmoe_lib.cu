@@ -12,10 +12,12 @@
 #include <mutex>
 #include <string>
 
+#include "attention.cuh"
 #include "blockwise.cuh"
 #include "common.cuh"
 #include "finalize.cuh"
 #include "grouped_gemm.cuh"
+#include "norm_rope.cuh"
 #include "permute.cuh"
 #include "router.cuh"
 
@@ -219,7 +221,7 @@ int launch_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chunk_
 int launch_gemm_gateup(const void* x_perm, const void* w_gate_up, const int32_t* tiles,
                        int64_t max_tiles, int64_t R, int64_t H, int64_t I, int64_t E, void* act,
                        cudaStream_t stream) {
-  using C = qmoe::GemmCfg<true>;
+  using C = qmoe::GemmCfg<qmoe::kModeGateUp>;
   CUtensorMap tmA, tmB;
   QMOE_CHECK(make_tmap_bf16(&tmA, w_gate_up, uint64_t(H), uint64_t(E * 2 * I), qmoe::kBK, qmoe::kBM));
   QMOE_CHECK(make_tmap_bf16(&tmB, x_perm, uint64_t(H), uint64_t(R), qmoe::kBK, qmoe::kBoxRows));
@@ -235,15 +237,15 @@ int launch_gemm_gateup(const void* x_perm, const void* w_gate_up, const int32_t*
   const int64_t units = max_tiles * a.n_mtiles;
   const int grid = int(std::min<int64_t>(units, num_sms(0)));
   if (grid <= 0) return QMOE_OK;
-  QMOE_CHECK(set_smem(qmoe::grouped_gemm_kernel<true>, C::kSmemBytes));
-  qmoe::grouped_gemm_kernel<true><<<grid, qmoe::kGemmThreads, C::kSmemBytes, stream>>>(tmA, tmB, a);
+  QMOE_CHECK(set_smem(qmoe::grouped_gemm_kernel<qmoe::kModeGateUp>, C::kSmemBytes));
+  qmoe::grouped_gemm_kernel<qmoe::kModeGateUp><<<grid, qmoe::kGemmThreads, C::kSmemBytes, stream>>>(tmA, tmB, a);
   return check_launch("grouped_gemm_kernel<gate_up>");
 }
 
 int launch_gemm_down(const void* act, const void* w_down, const int32_t* tiles, int64_t max_tiles,
                      const int32_t* row_dst, const float* row_w, int64_t R, int64_t H, int64_t I,
                      int64_t E, float* acc, int64_t n_acc, cudaStream_t stream) {
-  using C = qmoe::GemmCfg<false>;
+  using C = qmoe::GemmCfg<qmoe::kModeDown>;
   CUtensorMap tmA, tmB;
   QMOE_CHECK(make_tmap_bf16(&tmA, w_down, uint64_t(I), uint64_t(E * H), qmoe::kBK, qmoe::kBM));
   QMOE_CHECK(make_tmap_bf16(&tmB, act, uint64_t(I), uint64_t(R), qmoe::kBK, qmoe::kBoxRows));
@@ -262,9 +264,31 @@ int launch_gemm_down(const void* act, const void* w_down, const int32_t* tiles, 
   const int64_t units = max_tiles * a.n_mtiles;
   const int grid = int(std::min<int64_t>(units, num_sms(0)));
   if (grid <= 0) return QMOE_OK;
-  QMOE_CHECK(set_smem(qmoe::grouped_gemm_kernel<false>, C::kSmemBytes));
-  qmoe::grouped_gemm_kernel<false><<<grid, qmoe::kGemmThreads, C::kSmemBytes, stream>>>(tmA, tmB, a);
+  QMOE_CHECK(set_smem(qmoe::grouped_gemm_kernel<qmoe::kModeDown>, C::kSmemBytes));
+  qmoe::grouped_gemm_kernel<qmoe::kModeDown><<<grid, qmoe::kGemmThreads, C::kSmemBytes, stream>>>(tmA, tmB, a);
   return check_launch("grouped_gemm_kernel<down>");
+}
+
+int launch_linear(const void* x, const void* w, int64_t T, int64_t K, int64_t N, void* out,
+                  cudaStream_t stream) {
+  using C = qmoe::GemmCfg<qmoe::kModePlain>;
+  CUtensorMap tmA, tmB;
+  QMOE_CHECK(make_tmap_bf16(&tmA, w, uint64_t(K), uint64_t(N), qmoe::kBK, qmoe::kBM));
+  QMOE_CHECK(make_tmap_bf16(&tmB, x, uint64_t(K), uint64_t(T), qmoe::kBK, qmoe::kBoxRows));
+  qmoe::GemmArgs a{};
+  a.tiles = nullptr;
+  a.dense_rows = int(T);
+  a.n_mtiles = int(N / qmoe::kBM);
+  a.num_kb = int(K / qmoe::kBK);
+  a.a_rows_per_expert = 0;
+  a.act = static_cast<__nv_bfloat16*>(out);
+  a.act_ld = int(N);
+  const int64_t units = ((T + qmoe::kBNMax - 1) / qmoe::kBNMax) * a.n_mtiles;
+  const int grid = int(std::min<int64_t>(units, num_sms(0)));
+  if (grid <= 0) return QMOE_OK;
+  QMOE_CHECK(set_smem(qmoe::grouped_gemm_kernel<qmoe::kModePlain>, C::kSmemBytes));
+  qmoe::grouped_gemm_kernel<qmoe::kModePlain><<<grid, qmoe::kGemmThreads, C::kSmemBytes, stream>>>(tmA, tmB, a);
+  return check_launch("grouped_gemm_kernel<plain>");
 }
 
 int launch_finalize(const float* acc, const void* residual, int64_t T, int64_t H, void* out,
@@ -475,6 +499,164 @@ int qmoe_blockwise_prepare(const void* x, const float* affinities, int64_t aff_r
       static_cast<const __nv_bfloat16*>(x), int(T), int(H), int(E), int(block_size),
       static_cast<__nv_bfloat16*>(x_perm), row_dst, row_w, tiles, int(max_tiles));
   return check_launch("blockwise_prepare_kernel");
+}
+
+int qmoe_linear(const void* x, const void* w, int64_t T, int64_t K, int64_t N, void* out,
+                void* stream) {
+  QMOE_REQUIRE(x && w && out, QMOE_ERR_INVALID_ARGUMENT, "linear: null pointer");
+  QMOE_REQUIRE(T >= 0 && T < (int64_t(1) << 31), QMOE_ERR_INVALID_ARGUMENT, "linear: bad T");
+  QMOE_REQUIRE(K > 0 && K % qmoe::kBK == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "linear: K %% 64 != 0");
+  QMOE_REQUIRE(N > 0 && N % qmoe::kBM == 0 && N < (int64_t(1) << 31), QMOE_ERR_UNSUPPORTED_SHAPE,
+               "linear: N %% 128 != 0");
+  QMOE_REQUIRE(aligned16(x) && aligned16(w) && aligned16(out), QMOE_ERR_MISALIGNED,
+               "linear: pointers must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  if (T == 0) return QMOE_OK;
+  return launch_linear(x, w, T, K, N, out, static_cast<cudaStream_t>(stream));
+}
+
+int qmoe_rmsnorm(const void* x, int x_is_fp32, const void* residual, const float* weight,
+                 int64_t rows, int64_t H, float eps, void* out, int out_is_fp32,
+                 void* residual_out, void* stream) {
+  QMOE_REQUIRE(x && weight && out, QMOE_ERR_INVALID_ARGUMENT, "rmsnorm: null pointer");
+  QMOE_REQUIRE(!residual || (residual_out && !x_is_fp32), QMOE_ERR_INVALID_ARGUMENT,
+               "rmsnorm: a residual needs residual_out and bf16 x");
+  QMOE_REQUIRE(rows >= 0 && rows < (int64_t(1) << 31), QMOE_ERR_INVALID_ARGUMENT, "rmsnorm: bad rows");
+  QMOE_REQUIRE(H > 0 && H % 4 == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "rmsnorm: H %% 4 != 0");
+  QMOE_REQUIRE(aligned16(x) && aligned16(weight) && aligned16(out) &&
+                   (!residual || (aligned16(residual) && aligned16(residual_out))),
+               QMOE_ERR_MISALIGNED, "rmsnorm: pointers must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  if (rows == 0) return QMOE_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = int((rows + 7) / 8);
+  const auto* res = static_cast<const __nv_bfloat16*>(residual);
+  auto* res_out = static_cast<__nv_bfloat16*>(residual_out);
+  if (x_is_fp32 && out_is_fp32)
+    qmoe::rmsnorm_kernel<float, float><<<grid, qmoe::kNormThreads, 0, s>>>(
+        static_cast<const float*>(x), nullptr, weight, int(rows), int(H), eps, static_cast<float*>(out), nullptr);
+  else if (x_is_fp32)
+    qmoe::rmsnorm_kernel<float, __nv_bfloat16><<<grid, qmoe::kNormThreads, 0, s>>>(
+        static_cast<const float*>(x), nullptr, weight, int(rows), int(H), eps,
+        static_cast<__nv_bfloat16*>(out), nullptr);
+  else if (out_is_fp32)
+    qmoe::rmsnorm_kernel<__nv_bfloat16, float><<<grid, qmoe::kNormThreads, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(x), res, weight, int(rows), int(H), eps,
+        static_cast<float*>(out), res_out);
+  else
+    qmoe::rmsnorm_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, qmoe::kNormThreads, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(x), res, weight, int(rows), int(H), eps,
+        static_cast<__nv_bfloat16*>(out), res_out);
+  return check_launch("rmsnorm_kernel");
+}
+
+int qmoe_qk_norm_rope(const void* qkv, const int32_t* positions, const int32_t* cache_slot,
+                      const float* q_norm_w, const float* k_norm_w, const float* inv_freq, int64_t T,
+                      int64_t nh, int64_t nkv, int64_t head_dim, float eps, void* q_out,
+                      void* k_cache, void* v_cache, int64_t n_slots, int64_t max_seq, void* stream) {
+  QMOE_REQUIRE(qkv && positions && q_norm_w && k_norm_w && inv_freq && q_out && k_cache && v_cache,
+               QMOE_ERR_INVALID_ARGUMENT, "qk_norm_rope: null pointer");
+  QMOE_REQUIRE(head_dim == qmoe::kQkHeadDim, QMOE_ERR_UNSUPPORTED_SHAPE,
+               "qk_norm_rope: head_dim must be 128");
+  QMOE_REQUIRE(nh > 0 && nkv > 0 && nh % nkv == 0, QMOE_ERR_INVALID_ARGUMENT, "qk_norm_rope: bad heads");
+  QMOE_REQUIRE(T >= 0 && T * (nh + 2 * nkv) < (int64_t(1) << 31), QMOE_ERR_INVALID_ARGUMENT,
+               "qk_norm_rope: bad T");
+  QMOE_REQUIRE(n_slots > 0 && max_seq > 0, QMOE_ERR_INVALID_ARGUMENT, "qk_norm_rope: bad cache shape");
+  QMOE_REQUIRE(aligned16(qkv) && aligned16(q_out) && aligned16(k_cache) && aligned16(v_cache) &&
+                   aligned16(q_norm_w) && aligned16(k_norm_w),
+               QMOE_ERR_MISALIGNED, "qk_norm_rope: pointers must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  if (T == 0) return QMOE_OK;
+  const int64_t warps = T * (nh + 2 * nkv);
+  qmoe::qk_norm_rope_kernel<<<int((warps + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(qkv), positions, cache_slot, q_norm_w, k_norm_w, inv_freq,
+      int(T), int(nh), int(nkv), eps, static_cast<__nv_bfloat16*>(q_out),
+      static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache), int(max_seq),
+      int(n_slots));
+  return check_launch("qk_norm_rope_kernel");
+}
+
+int qmoe_attention_prefill(const void* q, const void* k_cache, const void* v_cache,
+                           const int32_t* q_start, const int32_t* cache_slot, int64_t B, int64_t S,
+                           int64_t nh, int64_t nkv, int64_t head_dim, int64_t n_slots,
+                           int64_t max_seq, float scale, void* out, void* stream) {
+  QMOE_REQUIRE(q && k_cache && v_cache && q_start && out, QMOE_ERR_INVALID_ARGUMENT,
+               "attention_prefill: null pointer");
+  QMOE_REQUIRE(head_dim == qmoe::kAttnD, QMOE_ERR_UNSUPPORTED_SHAPE, "attention_prefill: head_dim must be 128");
+  QMOE_REQUIRE(nh > 0 && nkv > 0 && nh % nkv == 0 && nh <= 65535, QMOE_ERR_INVALID_ARGUMENT,
+               "attention_prefill: bad heads");
+  QMOE_REQUIRE(B >= 0 && B <= 65535 && S >= 0 && S <= max_seq && max_seq > 0 && n_slots > 0 &&
+                   (cache_slot || B <= n_slots),
+               QMOE_ERR_INVALID_ARGUMENT, "attention_prefill: bad sizes");
+  QMOE_REQUIRE(aligned16(q) && aligned16(k_cache) && aligned16(v_cache) && aligned16(out),
+               QMOE_ERR_MISALIGNED, "attention_prefill: pointers must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  if (B == 0 || S == 0) return QMOE_OK;
+  const int smem = (qmoe::kAttnBQ + 4 * qmoe::kAttnBK) * qmoe::kAttnPad * 2;
+  QMOE_CHECK(set_smem(qmoe::attn_prefill_kernel, smem));
+  const dim3 grid(static_cast<unsigned>((S + qmoe::kAttnBQ - 1) / qmoe::kAttnBQ), static_cast<unsigned>(nh),
+                  static_cast<unsigned>(B));
+  qmoe::attn_prefill_kernel<<<grid, qmoe::kAttnThreads, smem, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k_cache),
+      static_cast<const __nv_bfloat16*>(v_cache), q_start, cache_slot, int(S), int(nh), int(nkv),
+      int(max_seq), int(n_slots), scale * 1.4426950408889634f, static_cast<__nv_bfloat16*>(out));
+  return check_launch("attn_prefill_kernel");
+}
+
+int64_t qmoe_attention_decode_splits(int64_t B, int64_t nkv, int64_t max_len) {
+  if (B <= 0 || nkv <= 0 || max_len <= 0) return 1;
+  const int sms = std::max(1, num_sms(0));
+  // enough CTAs for two waves of the SMs, chunks of at least 128 keys
+  int64_t want = (2 * int64_t(sms) + B * nkv - 1) / (B * nkv);
+  int64_t most = (max_len + 127) / 128;
+  return std::max<int64_t>(1, std::min(want, most));
+}
+
+size_t qmoe_attention_decode_workspace_size(int64_t B, int64_t nh, int64_t nsplit) {
+  if (B <= 0 || nh <= 0 || nsplit <= 0) return 0;
+  return size_t(B * nh * nsplit) * (qmoe::kAttnD + 2) * sizeof(float) + 256;
+}
+
+int qmoe_attention_decode(const void* q, const void* k_cache, const void* v_cache,
+                          const int32_t* kv_len, const int32_t* cache_slot, int64_t B, int64_t nh,
+                          int64_t nkv, int64_t head_dim, int64_t n_slots, int64_t max_seq, int64_t max_len,
+                          int64_t nsplit, float scale, void* out, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  QMOE_REQUIRE(q && k_cache && v_cache && kv_len && out && workspace, QMOE_ERR_INVALID_ARGUMENT,
+               "attention_decode: null pointer");
+  QMOE_REQUIRE(head_dim == qmoe::kAttnD, QMOE_ERR_UNSUPPORTED_SHAPE, "attention_decode: head_dim must be 128");
+  QMOE_REQUIRE(nkv > 0 && nh == nkv * qmoe::kDecodeGroup, QMOE_ERR_UNSUPPORTED_SHAPE,
+               "attention_decode: needs 8 query heads per KV head");
+  QMOE_REQUIRE(B >= 0 && B <= 65535 && nkv <= 65535 && max_len >= 0 && max_len <= max_seq && nsplit >= 1 &&
+                   nsplit <= 65535 && n_slots > 0 && (cache_slot || B <= n_slots),
+               QMOE_ERR_INVALID_ARGUMENT, "attention_decode: bad sizes");
+  QMOE_REQUIRE(workspace_bytes >= qmoe_attention_decode_workspace_size(B, nh, nsplit),
+               QMOE_ERR_WORKSPACE_TOO_SMALL, "attention_decode: workspace too small");
+  QMOE_REQUIRE(aligned16(q) && aligned16(k_cache) && aligned16(v_cache) && aligned16(out) &&
+                   (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0,
+               QMOE_ERR_MISALIGNED, "attention_decode: pointers must be 16-byte aligned (workspace 256)");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  if (B == 0) return QMOE_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* part_o = static_cast<float*>(workspace);
+  float* part_ml = part_o + size_t(B * nh * nsplit) * qmoe::kAttnD;
+  const int64_t chunk = std::max<int64_t>(64, ((max_len + nsplit - 1) / nsplit + 63) / 64 * 64);
+  const int smem = 4 * qmoe::kAttnBK * qmoe::kAttnPad * 2 + 4 * qmoe::kDecodeGroup * (qmoe::kAttnD + 2) * 4;
+  QMOE_CHECK(set_smem(qmoe::attn_decode_kernel, smem));
+  const dim3 grid(static_cast<unsigned>(nsplit), static_cast<unsigned>(nkv), static_cast<unsigned>(B));
+  qmoe::attn_decode_kernel<<<grid, qmoe::kAttnThreads, smem, s>>>(
+      static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k_cache),
+      static_cast<const __nv_bfloat16*>(v_cache), kv_len, cache_slot, int(nh), int(nkv), int(max_seq),
+      int(n_slots), int(chunk), scale * 1.4426950408889634f, part_o, part_ml);
+  QMOE_CHECK(check_launch("attn_decode_kernel"));
+  qmoe::attn_decode_combine_kernel<<<int((B * nh + 7) / 8), 256, 0, s>>>(
+      part_o, part_ml, int(B), int(nh), int(nsplit), static_cast<__nv_bfloat16*>(out));
+  return check_launch("attn_decode_combine_kernel");
 }
 
 size_t qmoe_moe_forward_workspace_size(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I) {

@@ -1,0 +1,69 @@
+"""Qwen3-MoE decoder layer with the reference's forward signature.
+
+``Qwen3MoeDecoderLayer.forward(hidden_states, attention_mask=None,
+position_ids=None, past_key_value=None, padding_mask=None, **kwargs)``
+returns ``(hidden_states, present_key_value, cos_cache, sin_cache, None)``
+like NeuronQwen3MoeDecoderLayer.forward (qwen.py:378-436):
+
+    residual = x
+    h = input_layernorm(x)                       (qwen.py:408-412)
+    h, kv = self_attn(h, ...)                    (qwen.py:415-422)
+    residual = residual + h                      (qwen.py:423)
+    h = post_attention_layernorm(residual)       (qwen.py:428)
+    out = residual + mlp(h, padding_mask)[0]     (qwen.py:429-430)
+
+Here the residual add before the second norm is fused into the RMSNorm
+kernel and the final residual add into the MoE output cast.  RoPE is applied
+inside the attention kernels, so cos/sin caches are returned as None.
+``attention_mask`` is accepted for signature compatibility; attention is
+causal over each sequence's cache.  ``capture_intermediates=True`` keeps the
+post-attention residual stream and the MoE input of the last call in
+``self.last`` (for layer-by-layer parity checks).
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+from torch import nn
+
+from . import ops
+from .attention import AttnWeights, KVCache, Qwen3MoeAttention
+from .config import Qwen3MoeConfig
+from .moe import MoEWeights, Qwen3MoeSparseMoeBlock
+
+
+class Qwen3MoeDecoderLayer(nn.Module):
+    def __init__(self, cfg: Qwen3MoeConfig, layer_idx: int = 0, attn_weights: Optional[AttnWeights] = None,
+                 moe_weights: Optional[MoEWeights] = None, input_norm: Optional[torch.Tensor] = None,
+                 post_norm: Optional[torch.Tensor] = None, device="cuda", seed: int = 0):
+        super().__init__()
+        self.cfg = cfg
+        self.layer_idx = layer_idx
+        self.self_attn = Qwen3MoeAttention(cfg, attn_weights, device=device, seed=seed)
+        self.mlp = Qwen3MoeSparseMoeBlock(cfg, moe_weights, device=device, seed=seed)
+        g = torch.Generator(device=device)
+        g.manual_seed(seed * 10 + 8)
+        H = cfg.hidden_size
+        self.input_layernorm = (input_norm if input_norm is not None
+                                else 1.0 + 0.1 * torch.randn(H, generator=g, device=device)).float().contiguous()
+        self.post_attention_layernorm = (post_norm if post_norm is not None
+                                         else 1.0 + 0.1 * torch.randn(H, generator=g, device=device)).float().contiguous()
+
+    def forward(self, hidden_states: torch.Tensor, attention_mask: Optional[torch.Tensor] = None,
+                position_ids: Optional[torch.Tensor] = None, past_key_value: Optional[KVCache] = None,
+                padding_mask: Optional[torch.Tensor] = None, **kwargs):
+        B, S, H = hidden_states.shape
+        eps = self.cfg.rms_norm_eps
+        x2d = hidden_states.reshape(B * S, H).to(torch.bfloat16).contiguous()
+        h = ops.rmsnorm(x2d, self.input_layernorm, eps)
+        a, present = self.self_attn(h.reshape(B, S, H), position_ids, past_key_value)
+        h2, residual = ops.rmsnorm(a.reshape(B * S, H), self.post_attention_layernorm, eps, residual=x2d)
+        if kwargs.get("capture_intermediates"):
+            self.last = dict(attn=a.reshape(B * S, H), residual=residual, moe_in=h2)
+        if padding_mask is None:
+            out, _, _ = self.mlp._moe(h2, residual=residual)
+        else:
+            moe, _, _ = self.mlp._moe(h2)
+            out = (residual.float() + moe.float() * padding_mask.reshape(-1, 1).float()).to(torch.bfloat16)
+        return (out.reshape(B, S, H), present, None, None, None)

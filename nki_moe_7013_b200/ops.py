@@ -226,3 +226,113 @@ def moe_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate_up: torch.Tensor
     if return_routing:
         return out, idx, tw
     return out
+
+
+# ----------------------------------------------------------------------------
+# attention sub-layer
+# ----------------------------------------------------------------------------
+
+def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out (T, N) bf16 = x (T, K) @ w (N, K)^T on the tcgen05 GEMM."""
+    _need(x, "x", torch.bfloat16, 2)
+    _need(w, "w", torch.bfloat16, 2)
+    T, K = x.shape
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise ValueError("w must be (N, K)")
+    dev = x.device
+    out = out if out is not None else torch.empty((T, N), dtype=torch.bfloat16, device=dev)
+    with torch.cuda.device(dev):
+        _C.check(_C.lib().qmoe_linear(_ptr(x), _ptr(w), T, K, N, _ptr(out), _stream(dev)), "qmoe_linear")
+    return out
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: Optional[torch.Tensor] = None,
+            out_dtype=torch.bfloat16):
+    """RMSNorm over the last dim.  With ``residual`` returns (norm(x + residual),
+    x + residual) -- the decoder layer's add & norm."""
+    if x.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError("x must be bf16 or fp32")
+    _need(x, "x", None, 2)
+    _need(weight, "weight", torch.float32, 1)
+    rows, H = x.shape
+    dev = x.device
+    out = torch.empty((rows, H), dtype=out_dtype, device=dev)
+    res_out = None
+    if residual is not None:
+        _need(residual, "residual", torch.bfloat16, 2)
+        res_out = torch.empty((rows, H), dtype=torch.bfloat16, device=dev)
+    with torch.cuda.device(dev):
+        _C.check(_C.lib().qmoe_rmsnorm(_ptr(x), 1 if x.dtype == torch.float32 else 0, _ptr(residual),
+                                       _ptr(weight), rows, H, float(eps), _ptr(out),
+                                       1 if out_dtype == torch.float32 else 0, _ptr(res_out),
+                                       _stream(dev)), "qmoe_rmsnorm")
+    return out if residual is None else (out, res_out)
+
+
+def qk_norm_rope(qkv: torch.Tensor, positions: torch.Tensor, q_norm_w: torch.Tensor,
+                 k_norm_w: torch.Tensor, inv_freq: torch.Tensor, nh: int, nkv: int, eps: float,
+                 k_cache: torch.Tensor, v_cache: torch.Tensor,
+                 cache_slot: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Fused per-head QK-RMSNorm + RoPE; appends K/V into the caches.
+    Returns q (T, nh, 128) bf16."""
+    _need(qkv, "qkv", torch.bfloat16, 2)
+    _need(positions, "positions", torch.int32, 1)
+    _need(k_cache, "k_cache", torch.bfloat16, 4)
+    _need(v_cache, "v_cache", torch.bfloat16, 4)
+    if cache_slot is not None:
+        _need(cache_slot, "cache_slot", torch.int32, 1)
+    T = qkv.shape[0]
+    hd = k_cache.shape[3]
+    dev = qkv.device
+    q = torch.empty((T, nh, hd), dtype=torch.bfloat16, device=dev)
+    with torch.cuda.device(dev):
+        _C.check(_C.lib().qmoe_qk_norm_rope(
+            _ptr(qkv), _ptr(positions), _ptr(cache_slot), _ptr(q_norm_w), _ptr(k_norm_w), _ptr(inv_freq),
+            T, nh, nkv, hd, float(eps), _ptr(q), _ptr(k_cache), _ptr(v_cache), k_cache.shape[0],
+            k_cache.shape[2], _stream(dev)), "qmoe_qk_norm_rope")
+    return q
+
+
+def attention_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                      q_start: torch.Tensor, B: int, S: int, scale: Optional[float] = None,
+                      cache_slot: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Causal GQA over the cache; q (B*S, nh, 128) -> (B*S, nh*128) bf16."""
+    _need(q, "q", torch.bfloat16, 3)
+    _need(q_start, "q_start", torch.int32, 1)
+    nh, hd = q.shape[1], q.shape[2]
+    nkv, max_seq = k_cache.shape[1], k_cache.shape[2]
+    scale = hd ** -0.5 if scale is None else scale
+    dev = q.device
+    out = torch.empty((B * S, nh * hd), dtype=torch.bfloat16, device=dev)
+    with torch.cuda.device(dev):
+        _C.check(_C.lib().qmoe_attention_prefill(
+            _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(q_start), _ptr(cache_slot), B, S, nh, nkv, hd,
+            k_cache.shape[0], max_seq, float(scale), _ptr(out), _stream(dev)), "qmoe_attention_prefill")
+    return out
+
+
+def attention_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                     kv_len: torch.Tensor, max_len: int, scale: Optional[float] = None,
+                     cache_slot: Optional[torch.Tensor] = None,
+                     workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Split-KV flash-decode; q (B, nh, 128) -> (B, nh*128) bf16."""
+    _need(q, "q", torch.bfloat16, 3)
+    _need(kv_len, "kv_len", torch.int32, 1)
+    B, nh, hd = q.shape
+    nkv, max_seq = k_cache.shape[1], k_cache.shape[2]
+    scale = hd ** -0.5 if scale is None else scale
+    dev = q.device
+    lib = _C.lib()
+    nsplit = int(lib.qmoe_attention_decode_splits(B, nkv, max_len))
+    ws_bytes = int(lib.qmoe_attention_decode_workspace_size(B, nh, nsplit))
+    if workspace is None or workspace.numel() < ws_bytes:
+        workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    out = torch.empty((B, nh * hd), dtype=torch.bfloat16, device=dev)
+    with torch.cuda.device(dev):
+        _C.check(lib.qmoe_attention_decode(
+            _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(kv_len), _ptr(cache_slot), B, nh, nkv, hd,
+            k_cache.shape[0], max_seq, max_len, nsplit, float(scale), _ptr(out), _ptr(workspace),
+            workspace.numel(), _stream(dev)),
+            "qmoe_attention_decode")
+    return out

@@ -268,3 +268,95 @@ def numpy_rmsnorm_known_answer(x, weight, eps):
     variance = np.mean(x ** 2, axis=-1, keepdims=True)
     x_norm = x / np.sqrt(variance + eps)
     return x_norm * weight
+
+
+# ----------------------------------------------------------------------------
+# attention sub-layer and decoder layer (HF Qwen3MoeAttention semantics,
+# qwen.py:313-341; decoder layer qwen.py:378-436)
+# ----------------------------------------------------------------------------
+
+def rope_inv_freq(head_dim: int, theta: float) -> np.ndarray:
+    """fp32 inverse frequencies as HF / NxDI RotaryEmbedding compute them."""
+    import torch
+
+    return (1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).float() / head_dim))).numpy()
+
+
+def rope_apply(x: np.ndarray, pos: np.ndarray, inv_freq: np.ndarray) -> np.ndarray:
+    """rotate-half RoPE on (..., T, hd) with per-token positions (T,)."""
+    hd = x.shape[-1]
+    ang = pos.astype(np.float32)[:, None] * inv_freq[None, :].astype(np.float32)  # fp32 angle (as HF)
+    cos = np.cos(ang.astype(np.float64))
+    sin = np.sin(ang.astype(np.float64))
+    x1, x2 = x[..., : hd // 2], x[..., hd // 2:]
+    return np.concatenate([x1 * cos - x2 * sin, x2 * cos + x1 * sin], axis=-1)
+
+
+def attention_layer(x_bf16, wqkv_bf16, wo_bf16, q_norm_w, k_norm_w, nh: int, nkv: int, eps: float,
+                    theta: float, B: int, S: int, k_cache=None, v_cache=None, L0=None):
+    """Attention sub-layer on B sequences of S new tokens each.
+
+    ``k_cache``/``v_cache`` (B, nkv, Lmax, hd) fp32 hold bf16 values of earlier
+    tokens (rows [0, L0[b])).  Intermediates are rounded to bf16 where the GPU
+    path stores bf16 (qkv, normalised+rotated q/k, attention output).
+    Returns (out fp32 (B*S, H) before its bf16 cast, new_k, new_v)."""
+    x = bf16_bits_to_f32(as_bf16_bits(x_bf16)).astype(np.float64)
+    wqkv = bf16_bits_to_f32(as_bf16_bits(wqkv_bf16)).astype(np.float64)
+    wo = bf16_bits_to_f32(as_bf16_bits(wo_bf16)).astype(np.float64)
+    hd = 128
+    L0 = np.zeros(B, np.int64) if L0 is None else np.asarray(L0, np.int64)
+    qkv = round_to_bf16((x @ wqkv.T).astype(np.float32)).astype(np.float64)
+    qkv = qkv.reshape(B, S, nh + 2 * nkv, hd)
+    inv_freq = rope_inv_freq(hd, theta)
+    out_heads = np.zeros((B, S, nh, hd))
+    Lmax = int((L0 + S).max())
+    new_k = np.zeros((B, nkv, Lmax, hd))
+    new_v = np.zeros((B, nkv, Lmax, hd))
+    for b in range(B):
+        pos = L0[b] + np.arange(S)
+        q = qkv[b, :, :nh]
+        k = qkv[b, :, nh:nh + nkv]
+        v = qkv[b, :, nh + nkv:]
+
+        def head_norm(t, w):
+            var = np.mean(t * t, axis=-1, keepdims=True)
+            return t / np.sqrt(var + eps) * np.asarray(w, np.float64)
+
+        q = rope_apply(head_norm(q, q_norm_w).transpose(1, 0, 2), pos, inv_freq)  # (nh, S, hd)
+        k = rope_apply(head_norm(k, k_norm_w).transpose(1, 0, 2), pos, inv_freq)  # (nkv, S, hd)
+        q = round_to_bf16(q.astype(np.float32)).astype(np.float64)
+        k = round_to_bf16(k.astype(np.float32)).astype(np.float64)
+        v = v.transpose(1, 0, 2)
+        if L0[b] > 0:
+            new_k[b, :, :L0[b]] = k_cache[b, :, :L0[b]]
+            new_v[b, :, :L0[b]] = v_cache[b, :, :L0[b]]
+        new_k[b, :, L0[b]:L0[b] + S] = k
+        new_v[b, :, L0[b]:L0[b] + S] = v
+        L = L0[b] + S
+        for h in range(nh):
+            g = h // (nh // nkv)
+            sc = q[h] @ new_k[b, g, :L].T / np.sqrt(hd)  # (S, L)
+            mask = np.arange(L)[None, :] > pos[:, None]
+            sc = np.where(mask, -np.inf, sc)
+            sc = sc - sc.max(axis=1, keepdims=True)
+            p = np.exp(sc)
+            p /= p.sum(axis=1, keepdims=True)
+            out_heads[b, :, h] = p @ new_v[b, g, :L]
+    attn = round_to_bf16(out_heads.reshape(B * S, nh * hd).astype(np.float32)).astype(np.float64)
+    return (attn @ wo.T).astype(np.float32), new_k, new_v
+
+
+def decoder_layer(x_bf16, w_in, w_post, attn_args: dict, moe_args: dict, eps: float, B: int, S: int):
+    """Full decoder layer (prefill from an empty cache).  Returns fp32 (B*S, H)
+    before the final bf16 cast."""
+    import torch
+
+    x = bf16_bits_to_f32(as_bf16_bits(x_bf16))
+    h = round_to_bf16(rmsnorm(x, w_in, eps))
+    hb = torch.from_numpy(h).to(torch.bfloat16)
+    a, _, _ = attention_layer(hb, B=B, S=S, eps=eps, **attn_args)
+    a = round_to_bf16(a)
+    res2 = round_to_bf16(x + a)
+    h2 = round_to_bf16(rmsnorm(res2, w_post, eps))
+    moe = moe_block(torch.from_numpy(h2).to(torch.bfloat16), **moe_args)
+    return (res2.astype(np.float64) + moe.astype(np.float64)).astype(np.float32)
