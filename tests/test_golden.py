@@ -59,3 +59,31 @@ def test_oracle_router_matches_hf_cfg0(oracle):
     # ... and select the same experts in the same order on these inputs
     assert np.array_equal(idx, g["fp32_topk_idx"])
     np.testing.assert_allclose(w, g["fp32_topk_w"], rtol=1e-5, atol=1e-7)
+
+
+def test_oracle_attention_and_decoder_match_hf(oracle):
+    """Oracle attention (QK-norm before RoPE, rotate-half RoPE theta 1e6, GQA
+    head mapping, causal softmax) and the decoder layer against HF
+    Qwen3MoeAttention / Qwen3MoeDecoderLayer in fp32."""
+    g = np.load(os.path.join(GOLDEN, "decoder_small.npz"))
+    B, S, H, nh, nkv, E, k, I, seed = (int(v) for v in g["shape"])
+    x = normal_bf16(seed, "x", (B, S, H))
+    p = {n: normal_bf16(seed, n2, shp, sd, mu) for n, n2, shp, sd, mu in [
+        ("wq", "wq", (nh * 128, H), 0.02, 0.0), ("wk", "wk", (nkv * 128, H), 0.02, 0.0),
+        ("wv", "wv", (nkv * 128, H), 0.02, 0.0), ("wo", "wo", (H, nh * 128), 0.02, 0.0),
+        ("qn", "qn", (128,), 0.1, 1.0), ("kn", "kn", (128,), 0.1, 1.0),
+        ("ln1", "ln1", (H,), 0.1, 1.0), ("ln2", "ln2", (H,), 0.1, 1.0),
+        ("wr", "w_router", (E, H), 0.02, 0.0), ("wgu", "w_gate_up", (E, 2 * I, H), 0.02, 0.0),
+        ("wd", "w_down", (E, H, I), 0.02, 0.0)]}
+    assert _checksum(x, *p.values()) == str(g["checksum"])
+    wqkv = torch.cat([p["wq"], p["wk"], p["wv"]], 0)
+    f = lambda t: t.float().numpy()  # noqa: E731
+    attn_args = dict(wqkv_bf16=wqkv, wo_bf16=p["wo"], q_norm_w=f(p["qn"]), k_norm_w=f(p["kn"]), nh=nh,
+                     nkv=nkv, theta=1e6)
+    h = oracle.round_to_bf16(oracle.rmsnorm(f(x).reshape(B * S, H), f(p["ln1"]), 1e-6))
+    a, _, _ = oracle.attention_layer(torch.from_numpy(h).to(torch.bfloat16), B=B, S=S, eps=1e-6, **attn_args)
+    assert max_rel_err(a, g["fp32_attn"].reshape(B * S, H)) < 2e-2
+    out = oracle.decoder_layer(x.reshape(B * S, H), f(p["ln1"]), f(p["ln2"]), attn_args,
+                               dict(w_router_bf16=p["wr"], w_gate_up_bf16=p["wgu"], w_down_bf16=p["wd"], k=k),
+                               1e-6, B, S)
+    assert max_rel_err(out, g["fp32_out"].reshape(B * S, H)) < 2e-2
