@@ -9,9 +9,10 @@ SiLU*up -> down + weighted combine -> bf16 output) over the 1024 tokens, with
 inputs resident in HBM.  The 1.2 GB of expert weights are larger than L2
 (126 MB), so every step streams them from HBM again.
 
-N>1 (torchrun): every rank runs its own copy of the layer on its own 1024
-tokens (replicas; weak scaling); value = tokens of all ranks / max-over-ranks
-time.
+N>1 (torchrun): expert parallel -- rank r owns experts [r*E/N, (r+1)*E/N)
+and its own 1024 tokens; rows travel to their expert's rank and back over
+NCCL all-to-alls (weak scaling).  value = tokens of all ranks / max-over-ranks
+device time.
 
 Also reported on the same line:
   e2e          same metric through the public module API with the step's
@@ -461,10 +462,121 @@ def run_extras(cfg, weights, dev, hbm_gbs, tf_burst):
     return res
 
 
+def run_ours_ep(args):
+    """N>1: the expert-parallel MoE layer over NCCL."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from nki_moe_7013_b200 import _C
+    from nki_moe_7013_b200.config import Qwen3MoeConfig
+    from nki_moe_7013_b200.ep import ExpertParallelMoE
+    from nki_moe_7013_b200.moe import MoEWeights
+    from nki_moe_7013_b200.synth import normal_bf16_device
+
+    world = int(os.environ["WORLD_SIZE"])
+    rank = int(os.environ["RANK"])
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    _C.lib()
+    cfg = Qwen3MoeConfig()
+    T = args.tokens
+    el = E // world
+    router = normal_bf16_device(1, (E, H), 0.02, dev)
+    local = MoEWeights(router, normal_bf16_device(2000 + rank, (el, 2 * I_MOE, H), 0.02, dev),
+                       normal_bf16_device(3000 + rank, (el, H, I_MOE), 0.02, dev))
+    moe = ExpertParallelMoE(cfg, router, local)
+    x = normal_bf16_device(1000 + rank, (T, H), 1.0, dev)
+
+    def barrier():
+        dist.barrier()
+        torch.cuda.synchronize()
+
+    sampler = ClockSampler() if rank == 0 else None
+    stages = ("route", "dispatch", "experts", "combine")
+
+    def timed_run():
+        t_end = time.perf_counter() + args.clock_settle_s
+        while time.perf_counter() < t_end:
+            for _ in range(5):
+                moe(x)
+            torch.cuda.synchronize()
+        for _ in range(args.warmup):
+            moe(x)
+        evs = [{n: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for n in stages}
+               for _ in range(args.steps)]
+        barrier()
+        recv = []
+        for s_ in range(args.steps):
+            moe(x, events=evs[s_])
+            recv.append(moe.last_recv_rows)
+        barrier()
+        span = evs[0]["route"][0].elapsed_time(evs[-1]["combine"][1])
+        st = {n: statistics.mean(e[n][0].elapsed_time(e[n][1]) for e in evs) for n in stages}
+        return span, st, statistics.mean(recv)
+
+    if sampler:
+        sampler.start()
+    span_ms, stage_ms, recv_rows = timed_run()
+    clocks = sampler.stop() if sampler else None
+    t = torch.tensor([span_ms, stage_ms["experts"]], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    span_ms, experts_ms = float(t[0]), float(t[1])
+    ms_per_step = span_ms / args.steps
+    value = T * world * args.steps / (span_ms / 1e3)
+    hbm_gbs, tf_burst, _, peak_kind = load_peaks()
+    # expert stage of this rank: its el experts' weights + received rows in/out
+    exp_bytes = el * (GATE_UP_BYTES_PER_EXPERT + DOWN_BYTES_PER_EXPERT) + recv_rows * (H * 2 * 3 + I_MOE * 4)
+    achieved = exp_bytes / (experts_ms * 1e-3) / 1e9
+
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+    for _ in range(max(args.warmup, 3)):
+        y_host.copy_(moe(x_host.to(dev, non_blocking=True)), non_blocking=True)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        y_host.copy_(moe(x_host.to(dev, non_blocking=True)), non_blocking=True)
+    e1.record()
+    barrier()
+    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = T * world * args.steps / (float(te.item()) / 1e3)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded random-init weights ~N(0,0.02), activations ~N(0,1))",
+        "config": {"workload": f"qwen3-moe sparse block, expert parallel, {T} tokens per GPU",
+                   "tokens_per_gpu": T, "hidden": H, "experts": E, "experts_per_gpu": el, "top_k": K_TOP,
+                   "moe_intermediate": I_MOE, "parallelism": f"ep{world}",
+                   "l2": "inputs larger than L2: expert weights and all-to-all buffers streamed per step"},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2,
+                "api": "ExpertParallelMoE.forward(hidden_states), pinned host in/out"},
+        "gpu_launches": 11 * args.steps,
+        "stage_us": {n: round(v * 1e3, 2) for n, v in stage_ms.items()},
+        "roofline": {"bound": "hbm", "kernel": "expert stage (grouped GEMMs on the local experts)",
+                     "achieved": achieved, "peak": hbm_gbs, "unit": "GB/s", "frac": achieved / hbm_gbs,
+                     "peak_kind": peak_kind, "traffic": None, "algorithmic_bytes_per_launch": exp_bytes,
+                     "rows_received": recv_rows},
+        "clocks": clocks,
+    }
+    if rank == 0:
+        print(json.dumps(line))
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        return run_ours_ep(args)
     return run_ours(args)
 
 

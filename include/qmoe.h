@@ -271,6 +271,34 @@ QMOE_API int qmoe_attention_decode(const void* q, const void* k_cache, const voi
                                    void* out, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Expert parallelism (EP) around NCCL all-to-alls.  Rank r of n_ranks owns
+ * experts [r*e_local, (r+1)*e_local).  The reference's EP variant
+ * (qwen_with_nki.py:8148-8271) masks non-local experts and all-reduces
+ * partial outputs (qwen_with_nki.py:8173-8177); here rows travel to their
+ * expert's rank and back instead.
+ *
+ * qmoe_routing_histogram: chunk_hist (ceil(T/8), E) per-chunk expert counts
+ *   of caller-given routing (input of qmoe_moe_permute when routing does not
+ *   come from qmoe_router_topk).
+ * qmoe_ep_pack: rows grouped by destination rank, (token, slot) order kept.
+ *   chunk_hist (ceil(T/8), n_ranks) int32 scratch; send_counts (n_ranks) out;
+ *   send_x (T*k, H) bf16, send_expert (T*k) int32 (expert id local to the
+ *   destination rank), send_w (T*k) fp32 routing weight, pair_pos (T, k) int32
+ *   row of each (token, slot) in the send buffer.
+ * qmoe_ep_unpack: out (T, H) bf16 = residual + sum over slots of the
+ *   returned weighted rows y_back[pair_pos[t, j]] (fp32 sum, one cast).
+ *   H % 256 == 0.
+ * ---------------------------------------------------------------------- */
+QMOE_API int qmoe_routing_histogram(const int32_t* topk_idx, int64_t T, int64_t k, int64_t E,
+                                    int32_t* chunk_hist, void* stream);
+QMOE_API int qmoe_ep_pack(const int32_t* topk_idx, const float* topk_w, const void* x, int64_t T,
+                          int64_t H, int64_t k, int64_t e_local, int64_t n_ranks,
+                          int32_t* chunk_hist, int32_t* send_counts, void* send_x,
+                          int32_t* send_expert, float* send_w, int32_t* pair_pos, void* stream);
+QMOE_API int qmoe_ep_unpack(const void* y_back, const int32_t* pair_pos, const void* residual,
+                            int64_t T, int64_t H, int64_t k, int64_t n_back, void* out, void* stream);
+
+/* ------------------------------------------------------------------------
  * Allocation-free fused forward.  No counterpart in the reference: it exists
  * for callers that cannot allocate device memory where they run the layer --
  * plugin enqueue hooks of inference runtimes, which may only queue work on the

@@ -47,6 +47,9 @@ _SIGNATURES = {
     "qmoe_attention_decode_workspace_size": (SZ, [I64, I64, I64]),
     "qmoe_attention_decode": (I32, [P, P, P, P, P, I64, I64, I64, I64, I64, I64, I64, I64,
                                     ctypes.c_float, P, P, SZ, P]),
+    "qmoe_routing_histogram": (I32, [P, I64, I64, I64, P, P]),
+    "qmoe_ep_pack": (I32, [P, P, P, I64, I64, I64, I64, I64, P, P, P, P, P, P, P]),
+    "qmoe_ep_unpack": (I32, [P, P, P, I64, I64, I64, I64, P, P]),
     "qmoe_moe_forward_noalloc": (I32, [P, P, P, P, P, P, I64, I64, I64, I64, I64, I32, P, P, P, P]),
 }
 

@@ -1,5 +1,5 @@
 // Shared device helpers for the sm_100a kernels: bf16 conversion, mbarriers,
-// TMA (cp.async.bulk.tensor, never with cluster multicast), tcgen05 / TMEM,
+// TMA (tiled cp.async.bulk.tensor loads into this CTA only), tcgen05 / TMEM,
 // and the bounded-wait error protocol.
 #pragma once
 
@@ -115,7 +115,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 }
 
 // ---------------------------------------------------------------------------
-// TMA (tiled, 2D, no multicast)
+// TMA (tiled, 2D, one destination CTA)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* tmap, int x, int y,
                                             uint64_t* bar) {

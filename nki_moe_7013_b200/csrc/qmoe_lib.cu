@@ -15,6 +15,7 @@
 #include "attention.cuh"
 #include "blockwise.cuh"
 #include "common.cuh"
+#include "ep.cuh"
 #include "finalize.cuh"
 #include "grouped_gemm.cuh"
 #include "norm_rope.cuh"
@@ -657,6 +658,71 @@ int qmoe_attention_decode(const void* q, const void* k_cache, const void* v_cach
   qmoe::attn_decode_combine_kernel<<<int((B * nh + 7) / 8), 256, 0, s>>>(
       part_o, part_ml, int(B), int(nh), int(nsplit), static_cast<__nv_bfloat16*>(out));
   return check_launch("attn_decode_combine_kernel");
+}
+
+int qmoe_routing_histogram(const int32_t* topk_idx, int64_t T, int64_t k, int64_t E, int32_t* chunk_hist,
+                           void* stream) {
+  QMOE_REQUIRE(topk_idx && chunk_hist, QMOE_ERR_INVALID_ARGUMENT, "routing_histogram: null pointer");
+  QMOE_REQUIRE(T >= 0 && T < (int64_t(1) << 31) / 32 && k >= 1 && k <= 32 && E >= 1 && E <= 256,
+               QMOE_ERR_INVALID_ARGUMENT, "routing_histogram: bad sizes");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  const int nchunks = int((T + qmoe::kRouterChunk - 1) / qmoe::kRouterChunk);
+  if (nchunks == 0) return QMOE_OK;
+  qmoe::routing_hist_kernel<<<nchunks, qmoe::kEpThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      topk_idx, int(T), int(k), int(E), chunk_hist);
+  return check_launch("routing_hist_kernel");
+}
+
+int qmoe_ep_pack(const int32_t* topk_idx, const float* topk_w, const void* x, int64_t T, int64_t H,
+                 int64_t k, int64_t e_local, int64_t n_ranks, int32_t* chunk_hist, int32_t* send_counts,
+                 void* send_x, int32_t* send_expert, float* send_w, int32_t* pair_pos, void* stream) {
+  QMOE_REQUIRE(topk_idx && topk_w && x && chunk_hist && send_counts && send_x && send_expert && send_w &&
+                   pair_pos,
+               QMOE_ERR_INVALID_ARGUMENT, "ep_pack: null pointer");
+  QMOE_REQUIRE(T >= 0 && T < (int64_t(1) << 31) / 32 && k >= 1 && k <= 32, QMOE_ERR_INVALID_ARGUMENT,
+               "ep_pack: bad T / k");
+  QMOE_REQUIRE(n_ranks >= 1 && n_ranks <= 256 && e_local >= 1, QMOE_ERR_INVALID_ARGUMENT,
+               "ep_pack: bad n_ranks / e_local");
+  QMOE_REQUIRE(H > 0 && H % 8 == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "ep_pack: H %% 8 != 0");
+  QMOE_REQUIRE(aligned16(x) && aligned16(send_x), QMOE_ERR_MISALIGNED, "ep_pack: x / send_x not aligned");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int nchunks = int((T + qmoe::kRouterChunk - 1) / qmoe::kRouterChunk);
+  if (nchunks == 0) {
+    cudaError_t err = cudaMemsetAsync(send_counts, 0, sizeof(int32_t) * size_t(n_ranks), s);
+    if (err != cudaSuccess) return set_error(QMOE_ERR_CUDA, "ep_pack: %s", cudaGetErrorString(err));
+    return QMOE_OK;
+  }
+  qmoe::ep_dest_hist_kernel<<<nchunks, qmoe::kEpThreads, 0, s>>>(topk_idx, int(T), int(k), int(e_local),
+                                                                 int(n_ranks), chunk_hist);
+  QMOE_CHECK(check_launch("ep_dest_hist_kernel"));
+  qmoe::permute_scan_kernel<<<int(n_ranks), qmoe::kScanThreads, 0, s>>>(chunk_hist, nchunks, int(n_ranks),
+                                                                        send_counts);
+  QMOE_CHECK(check_launch("permute_scan_kernel"));
+  qmoe::ep_pack_kernel<<<nchunks, qmoe::kEpThreads, 0, s>>>(
+      topk_idx, topk_w, static_cast<const __nv_bfloat16*>(x), chunk_hist, send_counts, int(T), int(H),
+      int(k), int(e_local), int(n_ranks), static_cast<__nv_bfloat16*>(send_x), send_expert, send_w,
+      pair_pos);
+  return check_launch("ep_pack_kernel");
+}
+
+int qmoe_ep_unpack(const void* y_back, const int32_t* pair_pos, const void* residual, int64_t T,
+                   int64_t H, int64_t k, int64_t n_back, void* out, void* stream) {
+  QMOE_REQUIRE(y_back && pair_pos && out, QMOE_ERR_INVALID_ARGUMENT, "ep_unpack: null pointer");
+  QMOE_REQUIRE(T >= 0 && k >= 1 && k <= 32 && n_back >= 0, QMOE_ERR_INVALID_ARGUMENT, "ep_unpack: bad sizes");
+  QMOE_REQUIRE(H > 0 && H % 256 == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "ep_unpack: H %% 256 != 0");
+  QMOE_REQUIRE(aligned16(y_back) && aligned16(out) && (!residual || aligned16(residual)),
+               QMOE_ERR_MISALIGNED, "ep_unpack: pointers must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  const int64_t warps = T * (H / 256);
+  if (warps == 0) return QMOE_OK;
+  qmoe::ep_unpack_kernel<<<int((warps + 7) / 8), qmoe::kEpThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(y_back), pair_pos, static_cast<const __nv_bfloat16*>(residual),
+      int(T), int(H), int(k), int(n_back), static_cast<__nv_bfloat16*>(out));
+  return check_launch("ep_unpack_kernel");
 }
 
 size_t qmoe_moe_forward_workspace_size(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I) {

@@ -37,7 +37,8 @@ class MoEWeights:
 
     @property
     def num_experts(self) -> int:
-        return self.router.shape[0]
+        """Experts held here (all of them, or this rank's shard under EP)."""
+        return self.gate_up.shape[0]
 
     @property
     def hidden_size(self) -> int:
@@ -165,26 +166,18 @@ class ExpertMLPs(nn.Module):
                                  block_to_expert, int(block_size), int(num_blocks), self.w)
 
 
-def _run_routed(x: torch.Tensor, w: MoEWeights, idx: torch.Tensor, tw: torch.Tensor, k: int) -> torch.Tensor:
-    """Permutation + grouped GEMMs + combine for caller-provided routing."""
+def _run_routed(x: torch.Tensor, w: MoEWeights, idx: torch.Tensor, tw: torch.Tensor, k: int,
+                residual: Optional[torch.Tensor] = None, acc_rows: Optional[int] = None) -> torch.Tensor:
+    """Permutation + grouped GEMMs + combine for caller-provided routing
+    (idx (T, k) int32 expert ids, tw (T, k) fp32 weights)."""
     T, H = x.shape
     E = w.num_experts
-    hist = torch.zeros(((T + ops.ROUTER_CHUNK - 1) // ops.ROUTER_CHUNK, E), dtype=torch.int32,
-                       device=x.device)
-    _chunk_histogram(idx, E, hist)
+    hist = ops.routing_histogram(idx, E)
     acc = torch.empty((T, H), dtype=torch.float32, device=x.device)
     p = ops.moe_permute(idx, tw, hist, E, x=x, gather=True, acc_zero=acc)
     act = ops.grouped_gemm_gateup_swiglu(p["x_perm"], w.gate_up, p["tiles"], p["max_tiles"])
     ops.grouped_gemm_down_combine(act, w.down, p["tiles"], p["max_tiles"], p["row_token"], p["row_w"], acc)
-    return ops.combine_finalize(acc)
-
-
-def _chunk_histogram(idx: torch.Tensor, E: int, hist: torch.Tensor) -> None:
-    """Per-chunk expert histogram for caller-provided routing (device ops)."""
-    T, k = idx.shape
-    chunk = torch.arange(T, device=idx.device).div(ops.ROUTER_CHUNK, rounding_mode="floor")
-    flat = (chunk.unsqueeze(1) * E + idx.long()).reshape(-1)
-    hist.view(-1).index_add_(0, flat, torch.ones_like(flat, dtype=torch.int32))
+    return ops.combine_finalize(acc, residual)
 
 
 def blockwise_forward(hidden_states, expert_affinities_masked, token_position_to_id, block_to_expert,
@@ -216,7 +209,7 @@ class MoEPlan:
                  bias: Optional[torch.Tensor] = None):
         self.w = weights
         self.T, self.k = T, k
-        self.E, self.H, self.I = weights.num_experts, weights.hidden_size, weights.intermediate_size
+        self.E, self.H, self.I = weights.router.shape[0], weights.hidden_size, weights.intermediate_size
         self.normalize = normalize
         self.bias = bias
         dev = weights.router.device

@@ -336,3 +336,61 @@ def attention_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
             workspace.numel(), _stream(dev)),
             "qmoe_attention_decode")
     return out
+
+
+# ----------------------------------------------------------------------------
+# expert parallelism helpers
+# ----------------------------------------------------------------------------
+
+def routing_histogram(topk_idx: torch.Tensor, num_experts: int) -> torch.Tensor:
+    """Per-chunk (8 tokens) expert histogram of caller-given routing."""
+    _need(topk_idx, "topk_idx", torch.int32, 2)
+    T, k = topk_idx.shape
+    dev = topk_idx.device
+    hist = torch.empty(((T + ROUTER_CHUNK - 1) // ROUTER_CHUNK, num_experts), dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        _C.check(_C.lib().qmoe_routing_histogram(_ptr(topk_idx), T, k, num_experts, _ptr(hist), _stream(dev)),
+                 "qmoe_routing_histogram")
+    return hist
+
+
+def ep_pack(topk_idx: torch.Tensor, topk_w: torch.Tensor, x: torch.Tensor, e_local: int, n_ranks: int):
+    """Rows grouped by destination rank.  Returns dict(send_counts (n_ranks,),
+    send_x (T*k, H), send_expert (T*k,), send_w (T*k,), pair_pos (T, k))."""
+    _need(topk_idx, "topk_idx", torch.int32, 2)
+    _need(topk_w, "topk_w", torch.float32, 2)
+    _need(x, "x", torch.bfloat16, 2)
+    T, k = topk_idx.shape
+    H = x.shape[1]
+    dev = x.device
+    R = T * k
+    nchunks = (T + ROUTER_CHUNK - 1) // ROUTER_CHUNK
+    hist = torch.empty((max(nchunks, 1), n_ranks), dtype=torch.int32, device=dev)
+    out = dict(send_counts=torch.empty(n_ranks, dtype=torch.int32, device=dev),
+               send_x=torch.empty((max(R, 1), H), dtype=torch.bfloat16, device=dev),
+               send_expert=torch.empty(max(R, 1), dtype=torch.int32, device=dev),
+               send_w=torch.empty(max(R, 1), dtype=torch.float32, device=dev),
+               pair_pos=torch.empty((T, k), dtype=torch.int32, device=dev))
+    with torch.cuda.device(dev):
+        _C.check(_C.lib().qmoe_ep_pack(
+            _ptr(topk_idx), _ptr(topk_w), _ptr(x), T, H, k, e_local, n_ranks, _ptr(hist),
+            _ptr(out["send_counts"]), _ptr(out["send_x"]), _ptr(out["send_expert"]), _ptr(out["send_w"]),
+            _ptr(out["pair_pos"]), _stream(dev)), "qmoe_ep_pack")
+    return out
+
+
+def ep_unpack(y_back: torch.Tensor, pair_pos: torch.Tensor, residual: Optional[torch.Tensor] = None,
+              n_back: Optional[int] = None) -> torch.Tensor:
+    _need(y_back, "y_back", torch.bfloat16, 2)
+    _need(pair_pos, "pair_pos", torch.int32, 2)
+    T, k = pair_pos.shape
+    H = y_back.shape[1]
+    if residual is not None:
+        _need(residual, "residual", torch.bfloat16, 2)
+    dev = y_back.device
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    n_back = y_back.shape[0] if n_back is None else n_back
+    with torch.cuda.device(dev):
+        _C.check(_C.lib().qmoe_ep_unpack(_ptr(y_back), _ptr(pair_pos), _ptr(residual), T, H, k, n_back,
+                                         _ptr(out), _stream(dev)), "qmoe_ep_unpack")
+    return out

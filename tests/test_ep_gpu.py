@@ -1,0 +1,105 @@
+"""EP kernels on the GPU (bit-exact pack, unpack, routing histogram) and, when
+the box has 2+ GPUs, the NCCL expert-parallel block against the
+single-process oracle."""
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from helpers import MAX_REL, activations, max_rel_err, moe_weights, to_f32_np
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(HERE)
+
+
+@pytest.mark.parametrize("T,E,k,P", [(1, 128, 8, 8), (100, 128, 8, 2), (1024, 128, 8, 8), (37, 32, 4, 4)])
+def test_ep_pack_unpack_bit_exact(cuda_dev, oracle, T, E, k, P):
+    from ep_reference import pack_np
+
+    from nki_moe_7013_b200 import ops
+
+    H = 2048 if E == 128 else 512
+    wr = moe_weights(30 + T, E, H, 128, cuda_dev)[0]
+    x = activations(30 + T, T, H, cuda_dev)
+    idx, tw = ops.router_topk(x, wr, k)
+    pk = ops.ep_pack(idx, tw, x, E // P, P)
+    hist = ops.routing_histogram(idx, E)
+    torch.cuda.synchronize()
+    ref = pack_np(idx.cpu().numpy(), tw.cpu().numpy(), x.cpu(), E // P, P)
+    n = T * k
+    np.testing.assert_array_equal(pk["send_counts"].cpu().numpy(), ref["send_counts"])
+    np.testing.assert_array_equal(pk["pair_pos"].cpu().numpy(), ref["pair_pos"])
+    np.testing.assert_array_equal(pk["send_expert"][:n].cpu().numpy(), ref["send_expert"])
+    np.testing.assert_array_equal(pk["send_w"][:n].cpu().numpy(), ref["send_w"])
+    assert torch.equal(pk["send_x"][:n].cpu(), ref["send_x"])
+    idn = idx.cpu().numpy()
+    for c in range(hist.shape[0]):
+        np.testing.assert_array_equal(hist[c].cpu().numpy(), np.bincount(idn[8 * c:8 * c + 8].reshape(-1), minlength=E))
+    # unpack: per token, fp32 sum of its k rows plus the residual, one bf16 cast
+    y_back = activations(31 + T, n, H, cuda_dev)
+    res = activations(32 + T, T, H, cuda_dev)
+    out = ops.ep_unpack(y_back, pk["pair_pos"], res)
+    torch.cuda.synchronize()
+    yb = to_f32_np(y_back).astype(np.float64)
+    exp = yb[ref["pair_pos"]].sum(1) + to_f32_np(res)
+    assert np.array_equal(to_f32_np(out), oracle.round_to_bf16(exp.astype(np.float32)))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _nccl_worker(rank, world, port, out_dir):
+    sys.path[:0] = [REPO, HERE]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    from nki_moe_7013_b200.config import Qwen3MoeConfig
+    from nki_moe_7013_b200.ep import ExpertParallelMoE
+    from nki_moe_7013_b200.moe import MoEWeights
+    from nki_moe_7013_b200.synth import normal_bf16_device
+    from oracle import oracle
+
+    cfg = Qwen3MoeConfig()
+    E, H, I, k = cfg.num_experts, cfg.hidden_size, cfg.moe_intermediate_size, 8
+    wr = normal_bf16_device(41, (E, H), 0.02, dev)
+    wgu = normal_bf16_device(42, (E, 2 * I, H), 0.02, dev)
+    wd = normal_bf16_device(43, (E, H, I), 0.02, dev)
+    el = E // world
+    local = MoEWeights(wr, wgu[rank * el:(rank + 1) * el].contiguous(), wd[rank * el:(rank + 1) * el].contiguous())
+    T = 256
+    x = normal_bf16_device(100 + rank, (T, H), 1.0, dev)
+    moe = ExpertParallelMoE(cfg, wr, local)
+    outs = [moe(x) for _ in range(2)]
+    torch.cuda.synchronize()
+    ref = oracle.round_to_bf16(oracle.moe_block(x.cpu(), wr.cpu(), wgu.cpu(), wd.cpu(), k))
+    errs = [float(np.abs(o.float().cpu().numpy() - ref).max() / np.abs(ref).max()) for o in outs]
+    np.save(os.path.join(out_dir, f"ep{rank}.npy"), np.array(errs))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_ep_nccl_matches_single_gpu_oracle(tmp_path):
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("expert parallelism needs 2+ GPUs on the box")
+    world = 2 if n < 4 else 4
+    mp.start_processes(_nccl_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       start_method="spawn", join=True)
+    for r in range(world):
+        errs = np.load(tmp_path / f"ep{r}.npy")
+        assert np.all(errs <= MAX_REL), f"rank {r}: {errs}"
