@@ -57,7 +57,8 @@ struct GemmCfg {
   static constexpr int kTmemCols = 2 * kAccCols;
   static constexpr int kBarrierBytes = 256;
   // down epilogue: per epilogue warp a [16 rows][33] fp32 transpose buffer
-  static constexpr int kStagingBytes = kMode == kModeDown ? 4 * 16 * 33 * 4 : 0;
+  // (+ the tile's row destinations and weights, 128 x 8 bytes)
+  static constexpr int kStagingBytes = kMode == kModeDown ? 4 * 16 * 33 * 4 + 128 * 8 : 0;
   static constexpr int kSmemBytes =
       1024 /*align slack*/ + kStages * kStageBytes + kBarrierBytes + kStagingBytes;
 };
@@ -69,6 +70,8 @@ struct GemmArgs {
   int dense_rows;
   int n_mtiles;          // feature blocks per tile
   int num_kb;            // K / kBK
+  int k_splits;          // >1: each (tile, feature block) unit is split over K (down mode only;
+                         // the partial sums meet in the fp32 accumulator)
   int a_rows_per_expert; // 2I (gate/up) or H (down)
   int up_row_offset;     // I (gate/up only)
   // gate/up and plain epilogues: bf16 output rows
@@ -143,7 +146,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   const int ntiles = args.tiles ? min(args.tiles[0], args.max_tiles)
                                  : (args.dense_rows + kBNMax - 1) / kBNMax;
-  const int total_units = ntiles * args.n_mtiles;
+  const int ksplit = kMode == kModeDown ? max(1, args.k_splits) : 1;
+  const int kb_per_split = args.num_kb / ksplit;
+  const int total_units = ntiles * args.n_mtiles * ksplit;
   const TileView tv{args.tiles ? args.tiles + 1 : nullptr,
                     args.tiles ? args.tiles + 1 + args.max_tiles : nullptr,
                     args.tiles ? args.tiles + 1 + 2 * args.max_tiles : nullptr, args.dense_rows};
@@ -159,14 +164,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t issued_parity = 0;     // parity of that load's full-barrier phase
       bool ok = true;
       for (int u = blockIdx.x; ok && u < total_units; u += gridDim.x) {
-        const int tile = u / args.n_mtiles;
-        const int mt = u - tile * args.n_mtiles;
+        const int tm = u / ksplit;
+        const int ks = u - tm * ksplit;
+        const int tile = tm / args.n_mtiles;
+        const int mt = tm - tile * args.n_mtiles;
         const int e = tv.expert(tile);
         const int row0 = tv.first_row(tile);
         const int nb = (tv.nrows(tile) + kBoxRows - 1) / kBoxRows;
         const int a_row = e * args.a_rows_per_expert + mt * kBM;
         const uint32_t bytes = C::kATiles * C::kABytes + nb * kBoxRows * kBK * 2;
-        for (int kb = 0; kb < args.num_kb; ++kb) {
+        for (int kb = ks * kb_per_split; kb < (ks + 1) * kb_per_split; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, kDevErrWaitTimeoutProducer)) {
             ok = false;
             break;
@@ -209,7 +216,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int local = 0;
       bool ok = true;
       for (int u = blockIdx.x; ok && u < total_units; u += gridDim.x, ++local) {
-        const int tile = u / args.n_mtiles;
+        const int tile = (u / ksplit) / args.n_mtiles;
         const int nb = (tv.nrows(tile) + kBoxRows - 1) / kBoxRows;
         const uint32_t idesc = make_idesc_bf16(kBM, nb * kBoxRows);
         const int buf = local & 1;
@@ -221,7 +228,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_fence_after();
         const uint32_t d_gate = tmem_base + buf * C::kAccCols;
         const uint32_t d_up = d_gate + kBM;
-        for (int kb = 0; kb < args.num_kb; ++kb) {
+        for (int kb = 0; kb < kb_per_split; ++kb) {
           if (!mbar_wait_bounded(&full[stage], phase, abort_flag, kDevErrWaitTimeoutMma)) {
             ok = false;
             break;
@@ -261,20 +268,39 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ---------------- epilogue (warps 2..5) ----------------
     const int quad = warp & 3;
     const int m = quad * 32 + lane;  // feature row inside the unit = TMEM lane
+    const int et = threadIdx.x - 64;  // 0..127: epilogue thread index
+    int32_t* meta_dst = reinterpret_cast<int32_t*>(staging + 4 * 16 * 33);
+    float* meta_w = reinterpret_cast<float*>(meta_dst + 128);
     int local = 0;
     for (int u = blockIdx.x; u < total_units; u += gridDim.x, ++local) {
-      const int tile = u / args.n_mtiles;
-      const int mt = u - tile * args.n_mtiles;
+      const int tm = u / ksplit;
+      const int tile = tm / args.n_mtiles;
+      const int mt = tm - tile * args.n_mtiles;
       const int row0 = tv.first_row(tile);
       const int nrows = tv.nrows(tile);
       const int nb = (nrows + kBoxRows - 1) / kBoxRows;
       const int buf = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
+      // down: fetch the tile's row destinations / weights before waiting on the MMA
+      int my_dst = -1;
+      float my_w = 0.f;
+      if constexpr (kMode == kModeDown) {
+        if (et < nrows) {
+          my_dst = args.row_dst[row0 + et];
+          my_w = args.row_w[row0 + et];
+        }
+      }
       const bool ok =
           mbar_wait_bounded(&acc_full[buf], acc_phase, abort_flag, kDevErrWaitTimeoutEpilogue);
       // The four epilogue warps agree before going on, so a failed wait in one
-      // of them can never leave the others waiting at a named barrier.
+      // of them can never leave the others waiting at a named barrier.  This
+      // barrier also ends every read of the previous unit's row metadata.
       if (named_barrier_or(1, 128, !ok)) break;
+      if constexpr (kMode == kModeDown) {
+        meta_dst[et] = (my_dst >= 0 && my_dst < args.n_acc) ? my_dst : -1;
+        meta_w[et] = my_w;
+        named_barrier_sync(1, 128);
+      }
       tc_fence_after();
       const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) + buf * C::kAccCols;
       const int feat = mt * kBM + m;
@@ -319,10 +345,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int i = it * 4 + (lane >> 3);  // row inside the chunk
             const int n = c * 16 + i;
             if (n < nrows) {
-              const int r = row0 + n;
-              const int dst = args.row_dst[r];
-              if (dst >= 0 && dst < args.n_acc) {
-                const float wv = args.row_w[r];
+              const int dst = meta_dst[n];
+              if (dst >= 0) {
+                const float wv = meta_w[n];
                 red_add_v4_f32(args.acc + size_t(dst) * args.acc_ld + mt * kBM + quad * 32 + fq,
                                wv * wsb[i * 33 + fq], wv * wsb[i * 33 + fq + 1],
                                wv * wsb[i * 33 + fq + 2], wv * wsb[i * 33 + fq + 3]);

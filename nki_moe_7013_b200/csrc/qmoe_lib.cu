@@ -155,14 +155,44 @@ using namespace qmoe_host;
 // ---------------------------------------------------------------------------
 namespace {
 
+// Token counts up to which the router runs as logits kernel (E/8 x T/8
+// CTAs) + selection kernel instead of the fused one-CTA-per-8-tokens kernel.
+constexpr int64_t kRouterSmallMaxT = 64;
+
 int launch_router(const void* x, const void* w, const float* bias, int64_t T, int64_t H, int64_t E,
                   int64_t k, int normalize, float* logits, int32_t* topk_idx, float* topk_w,
                   int32_t* chunk_hist, cudaStream_t stream) {
   const int G = int(H / 256);
   const int nchunks = int((T + qmoe::kRouterChunk - 1) / qmoe::kRouterChunk);
-  const int smem = int(sizeof(float) * qmoe::kRouterChunk * (H + E));
   const auto* xb = static_cast<const __nv_bfloat16*>(x);
   const auto* wb = static_cast<const __nv_bfloat16*>(w);
+  if (logits != nullptr && T <= kRouterSmallMaxT) {
+    const int smem = int(sizeof(float) * qmoe::kRouterChunk * H);
+    const dim3 grid(static_cast<unsigned>((E + qmoe::kRouterSmallWarps - 1) / qmoe::kRouterSmallWarps),
+                    static_cast<unsigned>(nchunks));
+#define QMOE_ROUTER_SMALL_CASE(GG)                                                                    \
+  case GG: {                                                                                          \
+    QMOE_CHECK(set_smem(qmoe::router_logits_small_kernel<GG>, smem));                                 \
+    qmoe::router_logits_small_kernel<GG><<<grid, qmoe::kRouterSmallWarps * 32, smem, stream>>>(       \
+        xb, wb, bias, int(T), int(E), logits);                                                        \
+    break;                                                                                            \
+  }
+    switch (G) {
+      QMOE_ROUTER_SMALL_CASE(1)
+      QMOE_ROUTER_SMALL_CASE(2)
+      QMOE_ROUTER_SMALL_CASE(4)
+      QMOE_ROUTER_SMALL_CASE(8)
+      QMOE_ROUTER_SMALL_CASE(16)
+      default:
+        return set_error(QMOE_ERR_UNSUPPORTED_SHAPE, "router: H/256 = %d not in {1,2,4,8,16}", G);
+    }
+#undef QMOE_ROUTER_SMALL_CASE
+    QMOE_CHECK(check_launch("router_logits_small_kernel"));
+    qmoe::router_select_kernel<<<nchunks, qmoe::kRouterChunk * 32, 0, stream>>>(
+        logits, int(T), int(E), int(k), normalize, topk_idx, topk_w, chunk_hist);
+    return check_launch("router_select_kernel");
+  }
+  const int smem = int(sizeof(float) * qmoe::kRouterChunk * (H + E));
 #define QMOE_ROUTER_CASE(GG)                                                                   \
   case GG: {                                                                                   \
     QMOE_CHECK(set_smem(qmoe::router_topk_kernel<GG>, smem));                                  \
@@ -231,6 +261,7 @@ int launch_gemm_gateup(const void* x_perm, const void* w_gate_up, const int32_t*
   a.max_tiles = int(max_tiles);
   a.n_mtiles = int(I / qmoe::kBM);
   a.num_kb = int(H / qmoe::kBK);
+  a.k_splits = 1;
   a.a_rows_per_expert = int(2 * I);
   a.up_row_offset = int(I);
   a.act = static_cast<__nv_bfloat16*>(act);
@@ -255,6 +286,17 @@ int launch_gemm_down(const void* act, const void* w_down, const int32_t* tiles, 
   a.max_tiles = int(max_tiles);
   a.n_mtiles = int(H / qmoe::kBM);
   a.num_kb = int(I / qmoe::kBK);
+  a.k_splits = 1;
+  // Tiny batches: few (tile, feature block) units, so split K as well to put
+  // more SMs on the weight stream (the partials meet in the accumulator).
+  if (R <= 16) {
+    for (int s : {3, 2}) {
+      if (a.num_kb % s == 0) {
+        a.k_splits = s;
+        break;
+      }
+    }
+  }
   a.a_rows_per_expert = int(H);
   a.up_row_offset = 0;
   a.row_dst = row_dst;
@@ -262,7 +304,7 @@ int launch_gemm_down(const void* act, const void* w_down, const int32_t* tiles, 
   a.acc = acc;
   a.acc_ld = int(H);
   a.n_acc = int(n_acc);
-  const int64_t units = max_tiles * a.n_mtiles;
+  const int64_t units = max_tiles * a.n_mtiles * a.k_splits;
   const int grid = int(std::min<int64_t>(units, num_sms(0)));
   if (grid <= 0) return QMOE_OK;
   QMOE_CHECK(set_smem(qmoe::grouped_gemm_kernel<qmoe::kModeDown>, C::kSmemBytes));
@@ -281,6 +323,7 @@ int launch_linear(const void* x, const void* w, int64_t T, int64_t K, int64_t N,
   a.dense_rows = int(T);
   a.n_mtiles = int(N / qmoe::kBM);
   a.num_kb = int(K / qmoe::kBK);
+  a.k_splits = 1;
   a.a_rows_per_expert = 0;
   a.act = static_cast<__nv_bfloat16*>(out);
   a.act_ld = int(N);
@@ -304,7 +347,7 @@ int launch_finalize(const float* acc, const void* residual, int64_t T, int64_t H
 
 // Workspace carving for the fused forward.
 struct FwdLayout {
-  size_t chunk_hist, counts, offsets, row_token, row_w, slot_row, tiles, topk_idx, topk_w, x_perm,
+  size_t logits, chunk_hist, counts, offsets, row_token, row_w, slot_row, tiles, topk_idx, topk_w, x_perm,
       act, acc, total;
 };
 
@@ -320,6 +363,7 @@ FwdLayout fwd_layout(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I) {
     o = align256(o + bytes);
     return at;
   };
+  L.logits = take(T <= kRouterSmallMaxT ? sizeof(float) * size_t(T * E) : 0);
   L.chunk_hist = take(sizeof(int32_t) * size_t(nchunks * E));
   L.counts = take(sizeof(int32_t) * size_t(E));
   L.offsets = take(sizeof(int32_t) * size_t(E + 1));
@@ -775,7 +819,8 @@ int qmoe_moe_forward(const void* x, const void* w_router, const float* router_bi
   const int64_t R = T * k;
   const int64_t max_tiles = qmoe_max_tiles(R, E);
 
-  QMOE_CHECK(launch_router(x, w_router, router_bias, T, H, E, k, normalize, nullptr, idx, tw,
+  float* logits = T <= kRouterSmallMaxT ? reinterpret_cast<float*>(ws + L.logits) : nullptr;
+  QMOE_CHECK(launch_router(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw,
                            chunk_hist, s));
   QMOE_CHECK(launch_permute(idx, tw, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w,
                             slot_row, tiles, x_perm, acc, s));
@@ -888,7 +933,8 @@ extern "C" int qmoe_moe_forward_noalloc(const void* x, const void* w_router,
   float* acc = reinterpret_cast<float*>(ws + L.acc);
   const int64_t R = T * k;
   const int64_t max_tiles = qmoe_max_tiles(R, E);
-  QMOE_CHECK(launch_router(x, w_router, router_bias, T, H, E, k, normalize, nullptr, idx, tw,
+  float* logits = T <= kRouterSmallMaxT ? reinterpret_cast<float*>(ws + L.logits) : nullptr;
+  QMOE_CHECK(launch_router(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw,
                            chunk_hist, s));
   QMOE_CHECK(launch_permute(idx, tw, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w,
                             slot_row, tiles, x_perm, acc, s));

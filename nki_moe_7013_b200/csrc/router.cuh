@@ -72,6 +72,84 @@ __device__ __forceinline__ float warp_reduce_32_chains(const float* v, int lane)
   const float send = hi ? a[0] : a[1];
   return keep + __shfl_xor_sync(0xFFFFFFFFu, send, 1);
 }
+// Softmax over one token's E logits (`row`), top-k by logit (ties -> lower
+// expert index), L1 renormalisation of the picked probabilities; one warp.
+// Writes topk_idx/topk_w of token `tok`, optional logits, and counts the picks
+// into the shared histogram `hist`.
+__device__ __forceinline__ void select_topk_warp(const float* row, int tok, int E, int k, int normalize,
+                                                 int lane, float* __restrict__ logits_out,
+                                                 int32_t* __restrict__ topk_idx,
+                                                 float* __restrict__ topk_w, int* hist) {
+  const int per_lane = E / 32;  // <= 8
+  float lv[8];
+  float m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    lv[i] = (i < per_lane) ? row[lane + 32 * i] : -INFINITY;
+    m = fmaxf(m, lv[i]);
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+  float ex[8];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    ex[i] = (i < per_lane) ? expf(lv[i] - m) : 0.f;
+    s += ex[i];
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, off);
+  const float inv_s = 1.0f / s;
+  if (logits_out) {
+    for (int i = 0; i < per_lane; ++i) logits_out[size_t(tok) * E + lane + 32 * i] = lv[i];
+  }
+  unsigned taken = 0u;  // bit i: expert lane + 32*i already chosen
+  float chosen_p = 0.f;  // lane j (< k) keeps the probability of pick j
+  int chosen_e = 0;
+  for (int j = 0; j < k; ++j) {
+    float bv = -INFINITY;
+    int be = 0x7FFFFFFF;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (i < per_lane && !((taken >> i) & 1u)) {
+        const int ei = lane + 32 * i;
+        if (lv[i] > bv || (lv[i] == bv && ei < be)) {
+          bv = lv[i];
+          be = ei;
+        }
+      }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, off);
+      const int oe = __shfl_xor_sync(0xFFFFFFFFu, be, off);
+      if (ov > bv || (ov == bv && oe < be)) {
+        bv = ov;
+        be = oe;
+      }
+    }
+    if ((be & 31) == lane) taken |= 1u << (be >> 5);
+    const int owner = be & 31;
+    float mine = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (lane + 32 * i == be) mine = ex[i] * inv_s;
+    const float p = __shfl_sync(0xFFFFFFFFu, mine, owner);
+    if (lane == j) {
+      chosen_p = p;
+      chosen_e = be;
+    }
+  }
+  float denom = 0.f;
+  for (int j = 0; j < k; ++j) denom += __shfl_sync(0xFFFFFFFFu, chosen_p, j);
+  if (lane < k) {
+    const float wv = normalize ? chosen_p / fmaxf(denom, 1e-12f) : chosen_p;
+    topk_idx[size_t(tok) * k + lane] = chosen_e;
+    topk_w[size_t(tok) * k + lane] = wv;
+    atomicAdd(&hist[chosen_e], 1);
+  }
+}
+
 template <int G>  // G = H / 256
 __global__ void __launch_bounds__(router_warps<G>() * 32, 1)
     router_topk_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
@@ -91,7 +169,9 @@ __global__ void __launch_bounds__(router_warps<G>() * 32, 1)
   const int t0 = blockIdx.x * kRouterChunk;
   const int nt = min(kRouterChunk, T - t0);
 
-  // Stage the chunk's activations in shared memory as fp32.
+  // Stage the chunk's activations in shared memory as fp32.  Inside each
+  // 256-element group, element 8l+q is stored at (q/4)*128 + 4l + q%4 so the
+  // two float4 reads of a lane's slice are conflict-free across the warp.
   for (int i = threadIdx.x; i < kRouterChunk * (H / 8); i += kThreads) {
     const int t = i / (H / 8);
     const int c = (i % (H / 8)) * 8;
@@ -103,8 +183,10 @@ __global__ void __launch_bounds__(router_warps<G>() * 32, 1)
       hi = make_float4(bf16lo_to_f32(v.z), bf16hi_to_f32(v.z), bf16lo_to_f32(v.w),
                        bf16hi_to_f32(v.w));
     }
-    *reinterpret_cast<float4*>(xs + t * H + c) = lo;
-    *reinterpret_cast<float4*>(xs + t * H + c + 4) = hi;
+    const int gbase = t * H + (c & ~255);
+    const int sl = (c & 255) >> 3;  // lane slot inside the group
+    *reinterpret_cast<float4*>(xs + gbase + 4 * sl) = lo;
+    *reinterpret_cast<float4*>(xs + gbase + 128 + 4 * sl) = hi;
   }
   for (int i = threadIdx.x; i < 256; i += kThreads) hist[i] = 0;
   __syncthreads();
@@ -148,9 +230,9 @@ __global__ void __launch_bounds__(router_warps<G>() * 32, 1)
       }
 #pragma unroll
       for (int t = 0; t < kRouterChunk; ++t) {
-        const float* xr = xs + t * H + 256 * g + 8 * lane;
+        const float* xr = xs + t * H + 256 * g + 4 * lane;
         const float4 a = *reinterpret_cast<const float4*>(xr);
-        const float4 b = *reinterpret_cast<const float4*>(xr + 4);
+        const float4 b = *reinterpret_cast<const float4*>(xr + 128);
         const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
         for (int q = 0; q < 8; ++q)
@@ -173,88 +255,110 @@ __global__ void __launch_bounds__(router_warps<G>() * 32, 1)
   }
   __syncthreads();
 
-  // Softmax + top-k: one warp per token; lane holds experts lane + 32*i.
+  // Softmax + top-k: one warp per token.
   const int t = warp;
-  if (t < nt) {
-    const int tok = t0 + t;
-    const int per_lane = E / 32;  // <= 8
-    float lv[8];
-    float m = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      lv[i] = (i < per_lane) ? ls[t * E + lane + 32 * i] : -INFINITY;
-      m = fmaxf(m, lv[i]);
-    }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
-    float ex[8];
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      ex[i] = (i < per_lane) ? expf(lv[i] - m) : 0.f;
-      s += ex[i];
-    }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, off);
-    const float inv_s = 1.0f / s;
-
-    if (logits_out) {
-      for (int i = 0; i < per_lane; ++i) logits_out[size_t(tok) * E + lane + 32 * i] = lv[i];
-    }
-
-    unsigned taken = 0u;  // bit i: expert lane + 32*i already chosen
-    float chosen_p = 0.f;  // lane j (< k) keeps the probability of pick j
-    int chosen_e = 0;
-    for (int j = 0; j < k; ++j) {
-      // best remaining candidate of this lane: larger logit, then lower index
-      float bv = -INFINITY;
-      int be = 0x7FFFFFFF;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        if (i < per_lane && !((taken >> i) & 1u)) {
-          const int ei = lane + 32 * i;
-          if (lv[i] > bv || (lv[i] == bv && ei < be)) {
-            bv = lv[i];
-            be = ei;
-          }
-        }
-      }
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) {
-        const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, off);
-        const int oe = __shfl_xor_sync(0xFFFFFFFFu, be, off);
-        if (ov > bv || (ov == bv && oe < be)) {
-          bv = ov;
-          be = oe;
-        }
-      }
-      if ((be & 31) == lane) taken |= 1u << (be >> 5);
-      const int owner = be & 31;
-      // probability of the winner, read from its owning lane
-      float mine = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        if (lane + 32 * i == be) mine = ex[i] * inv_s;
-      const float p = __shfl_sync(0xFFFFFFFFu, mine, owner);
-      if (lane == j) {
-        chosen_p = p;
-        chosen_e = be;
-      }
-    }
-    // L1 renormalisation over the k picks, summed in pick order.
-    float denom = 0.f;
-    for (int j = 0; j < k; ++j) denom += __shfl_sync(0xFFFFFFFFu, chosen_p, j);
-    if (lane < k) {
-      const float wv = normalize ? chosen_p / fmaxf(denom, 1e-12f) : chosen_p;
-      topk_idx[size_t(tok) * k + lane] = chosen_e;
-      topk_w[size_t(tok) * k + lane] = wv;
-      atomicAdd(&hist[chosen_e], 1);
-    }
-  }
+  if (t < nt) select_topk_warp(ls + t * E, t0 + t, E, k, normalize, lane, logits_out, topk_idx, topk_w, hist);
   if (chunk_hist) {
     __syncthreads();
     for (int e = threadIdx.x; e < E; e += kThreads)
       chunk_hist[size_t(blockIdx.x) * E + e] = hist[e];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Small batches (decode): the fused kernel above would run on ceil(T/8) CTAs
+// only.  Here each warp owns ONE expert for a chunk of 8 tokens: the lane's
+// whole canonical weight slice is loaded at once (one L2 round trip), the 8
+// token chains run interleaved, and the logits go to global memory; grid =
+// (E/8 expert groups, ceil(T/8) chunks).  router_select_kernel then applies
+// softmax / top-k / renormalisation per token.  Same reduction order as the
+// fused kernel, so the logits are bit-identical.
+// ---------------------------------------------------------------------------
+constexpr int kRouterSmallWarps = 8;
+
+template <int G>
+__global__ void __launch_bounds__(kRouterSmallWarps * 32)
+    router_logits_small_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                               const float* __restrict__ bias, int T, int E, float* __restrict__ logits) {
+  constexpr int H = G * 256;
+  extern __shared__ __align__(16) float router_small_smem[];
+  float* xs = router_small_smem;  // [8][H], interleaved like the fused kernel
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = blockIdx.y * kRouterChunk;
+  const int nt = min(kRouterChunk, T - t0);
+  const int e = blockIdx.x * kRouterSmallWarps + warp;
+  // weight slice first: its loads overlap the activation staging
+  uint4 wv[G];
+  if (e < E) {
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+      wv[g] = __ldg(reinterpret_cast<const uint4*>(w + size_t(e) * H + 256 * g + 8 * lane));
+  }
+  for (int i = threadIdx.x; i < kRouterChunk * (H / 8); i += kRouterSmallWarps * 32) {
+    const int t = i / (H / 8);
+    const int c = (i % (H / 8)) * 8;
+    float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
+    if (t < nt) {
+      const uint4 v = *reinterpret_cast<const uint4*>(x + size_t(t0 + t) * H + c);
+      lo = make_float4(bf16lo_to_f32(v.x), bf16hi_to_f32(v.x), bf16lo_to_f32(v.y), bf16hi_to_f32(v.y));
+      hi = make_float4(bf16lo_to_f32(v.z), bf16hi_to_f32(v.z), bf16lo_to_f32(v.w), bf16hi_to_f32(v.w));
+    }
+    const int gbase = t * H + (c & ~255);
+    const int sl = (c & 255) >> 3;
+    *reinterpret_cast<float4*>(xs + gbase + 4 * sl) = lo;
+    *reinterpret_cast<float4*>(xs + gbase + 128 + 4 * sl) = hi;
+  }
+  __syncthreads();
+  if (e >= E) return;
+  float acc[kRouterChunk];
+#pragma unroll
+  for (int t = 0; t < kRouterChunk; ++t) acc[t] = 0.f;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const float wf[8] = {bf16lo_to_f32(wv[g].x), bf16hi_to_f32(wv[g].x), bf16lo_to_f32(wv[g].y),
+                         bf16hi_to_f32(wv[g].y), bf16lo_to_f32(wv[g].z), bf16hi_to_f32(wv[g].z),
+                         bf16lo_to_f32(wv[g].w), bf16hi_to_f32(wv[g].w)};
+#pragma unroll
+    for (int t = 0; t < kRouterChunk; ++t) {
+      const float* xr = xs + t * H + 256 * g + 4 * lane;
+      const float4 a = *reinterpret_cast<const float4*>(xr);
+      const float4 b = *reinterpret_cast<const float4*>(xr + 128);
+      acc[t] = fmaf(a.x, wf[0], acc[t]);
+      acc[t] = fmaf(a.y, wf[1], acc[t]);
+      acc[t] = fmaf(a.z, wf[2], acc[t]);
+      acc[t] = fmaf(a.w, wf[3], acc[t]);
+      acc[t] = fmaf(b.x, wf[4], acc[t]);
+      acc[t] = fmaf(b.y, wf[5], acc[t]);
+      acc[t] = fmaf(b.z, wf[6], acc[t]);
+      acc[t] = fmaf(b.w, wf[7], acc[t]);
+    }
+  }
+  const float be = bias ? bias[e] : 0.f;
+#pragma unroll
+  for (int t = 0; t < kRouterChunk; ++t) {
+    float v = acc[t];
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, off);
+    if (lane == 0 && t < nt) logits[size_t(t0 + t) * E + e] = bias ? __fadd_rn(v, be) : v;
+  }
+}
+
+// Softmax / top-k / renorm / chunk histogram from precomputed logits; one CTA
+// per chunk of 8 tokens, one warp per token.
+__global__ void __launch_bounds__(kRouterChunk * 32)
+    router_select_kernel(const float* __restrict__ logits, int T, int E, int k, int normalize,
+                         int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
+                         int32_t* __restrict__ chunk_hist) {
+  __shared__ int hist[256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  const int t0 = blockIdx.x * kRouterChunk;
+  const int t = t0 + warp;
+  if (t < T) select_topk_warp(logits + size_t(t) * E, t, E, k, normalize, lane, nullptr, topk_idx, topk_w, hist);
+  if (chunk_hist) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) chunk_hist[size_t(blockIdx.x) * E + e] = hist[e];
   }
 }
 

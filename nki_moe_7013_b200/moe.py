@@ -233,6 +233,8 @@ class MoEPlan:
         self.x_perm = torch.empty((max(R, 1), H), dtype=torch.bfloat16, device=dev)
         self.act = torch.empty((max(R, 1), I), dtype=torch.bfloat16, device=dev)
         self.acc = torch.empty((max(T, 1), H), **f32)
+        # small batches route through the logits + selection kernels
+        self.logits = torch.empty((T, E), **f32) if T <= ops.ROUTER_SMALL_MAX_T else None
         self._lib = _C.lib()
 
     def run(self, x: torch.Tensor, out: torch.Tensor, residual: Optional[torch.Tensor] = None,
@@ -248,7 +250,7 @@ class MoEPlan:
 
         mark(0)
         _C.check(lib.qmoe_router_topk(p(x), p(w.router), p(self.bias), T, H, E, k,
-                                      1 if self.normalize else 0, None, p(self.topk_idx),
+                                      1 if self.normalize else 0, p(self.logits), p(self.topk_idx),
                                       p(self.topk_w), p(self.hist), s), "router")
         mark(1)
         _C.check(lib.qmoe_moe_permute(p(self.topk_idx), p(self.topk_w), p(self.hist), p(x), T, H, E, k,

@@ -14,6 +14,7 @@ import torch
 from . import _C
 
 ROUTER_CHUNK = 8  # QMOE_ROUTER_CHUNK
+ROUTER_SMALL_MAX_T = 64  # batches up to this size take the two-kernel small-batch router
 
 
 def _ptr(t: Optional[torch.Tensor]):
@@ -55,7 +56,9 @@ def router_topk(x: torch.Tensor, w_router: torch.Tensor, k: int, normalize: bool
     dev = x.device
     idx = torch.empty((T, k), dtype=torch.int32, device=dev)
     w = torch.empty((T, k), dtype=torch.float32, device=dev)
-    logits = torch.empty((T, E), dtype=torch.float32, device=dev) if return_logits else None
+    # a logits buffer also enables the small-batch router path
+    logits = (torch.empty((T, E), dtype=torch.float32, device=dev)
+              if (return_logits or T <= ROUTER_SMALL_MAX_T) else None)
     hist = (torch.empty(((T + ROUTER_CHUNK - 1) // ROUTER_CHUNK, E), dtype=torch.int32, device=dev)
             if return_hist else None)
     with torch.cuda.device(dev):
