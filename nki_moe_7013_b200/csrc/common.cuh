@@ -42,6 +42,20 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch.  Kernels of the MoE chain are launched with
+// programmatic stream serialization: each waits for its predecessor's grid
+// (griddepcontrol.wait) before reading what it produced, and lets its own
+// dependents start launching as soon as all of its CTAs are resident.  Both
+// are no-ops for a kernel launched without the attribute.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
 // bf16 helpers
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float bf16lo_to_f32(uint32_t packed) {

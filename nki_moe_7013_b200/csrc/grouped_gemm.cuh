@@ -143,6 +143,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // everything above overlapped the previous kernel; its outputs are read below
+  griddep_wait();
+  griddep_launch_dependents();
 
   const int ntiles = args.tiles ? min(args.tiles[0], args.max_tiles)
                                  : (args.dense_rows + kBNMax - 1) / kBNMax;

@@ -64,6 +64,8 @@ __global__ void __launch_bounds__(kScanThreads)
                         int32_t* __restrict__ counts) {
   __shared__ int warp_sums[8];
   const int e = blockIdx.x;
+  griddep_wait();
+  griddep_launch_dependents();
   const int per = (nchunks + kScanThreads - 1) / kScanThreads;
   const int c0 = min(nchunks, int(threadIdx.x) * per);
   const int c1 = min(nchunks, c0 + per);
@@ -98,6 +100,8 @@ __global__ void __launch_bounds__(kScatterThreads)
   const int nt = min(kRouterChunk, T - t0);
   const int npairs = nt * k;
   const int tid = threadIdx.x;
+  griddep_wait();
+  griddep_launch_dependents();
 
   // Expert offsets: exclusive scan of counts (E <= 256).
   const int cnt = tid < E ? counts[tid] : 0;

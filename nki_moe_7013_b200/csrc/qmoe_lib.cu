@@ -11,6 +11,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <utility>
 
 #include "attention.cuh"
 #include "blockwise.cuh"
@@ -135,6 +136,27 @@ static int set_smem(Kernel k, int bytes) {
   return QMOE_OK;
 }
 
+// Kernel launch through cudaLaunchKernelEx; with `pdl` the launch allows
+// programmatic stream serialization (the kernel overlaps its predecessor's
+// tail and waits in griddepcontrol.wait before reading its outputs).
+template <typename... KArgs, typename... Args>
+static int launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                         bool pdl, const char* name, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (err != cudaSuccess) return set_error(QMOE_ERR_CUDA, "%s: %s", name, cudaGetErrorString(err));
+  return check_launch(name);
+}
+
 }  // namespace qmoe_host
 
 using namespace qmoe_host;
@@ -188,9 +210,9 @@ int launch_router(const void* x, const void* w, const float* bias, int64_t T, in
     }
 #undef QMOE_ROUTER_SMALL_CASE
     QMOE_CHECK(check_launch("router_logits_small_kernel"));
-    qmoe::router_select_kernel<<<nchunks, qmoe::kRouterChunk * 32, 0, stream>>>(
-        logits, int(T), int(E), int(k), normalize, topk_idx, topk_w, chunk_hist);
-    return check_launch("router_select_kernel");
+    return launch_kernel(qmoe::router_select_kernel, dim3(nchunks), dim3(qmoe::kRouterChunk * 32), 0, stream,
+                         true, "router_select_kernel", logits, int(T), int(E), int(k), normalize,
+                         topk_idx, topk_w, chunk_hist);
   }
   const int smem = int(sizeof(float) * qmoe::kRouterChunk * (H + E));
 #define QMOE_ROUTER_CASE(GG)                                                                   \
@@ -234,17 +256,17 @@ int launch_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chunk_
                    void* x_perm, float* acc_zero, cudaStream_t stream) {
   const int nchunks = int((T + qmoe::kRouterChunk - 1) / qmoe::kRouterChunk);
   const int64_t max_tiles = qmoe_max_tiles(T * k, E);
-  qmoe::permute_scan_kernel<<<int(E), qmoe::kScanThreads, 0, stream>>>(chunk_hist, nchunks, int(E),
-                                                                       counts);
-  QMOE_CHECK(check_launch("permute_scan_kernel"));
+  QMOE_CHECK(launch_kernel(qmoe::permute_scan_kernel, dim3(unsigned(E)), dim3(qmoe::kScanThreads), 0, stream,
+                           true, "permute_scan_kernel", chunk_hist, nchunks, int(E), counts));
   if (nchunks > 0) {
     // Enough CTAs to keep the row gather from being latency-bound.
     const int parts = x_perm ? int(std::max<int64_t>(1, std::min<int64_t>(8, (2 * num_sms(0) + nchunks - 1) / nchunks))) : 1;
-    qmoe::permute_scatter_kernel<<<dim3(nchunks, parts), qmoe::kScatterThreads, 0, stream>>>(
-        topk_idx, topk_w, chunk_hist, counts, offsets, static_cast<const __nv_bfloat16*>(x), int(T),
-        int(H), int(E), int(k), row_token, row_w, slot_row, static_cast<__nv_bfloat16*>(x_perm),
-        acc_zero, tiles, int(max_tiles));
-    QMOE_CHECK(check_launch("permute_scatter_kernel"));
+    QMOE_CHECK(launch_kernel(qmoe::permute_scatter_kernel, dim3(nchunks, parts), dim3(qmoe::kScatterThreads),
+                             0, stream, true, "permute_scatter_kernel", topk_idx, topk_w,
+                             static_cast<const int32_t*>(chunk_hist), static_cast<const int32_t*>(counts),
+                             offsets, static_cast<const __nv_bfloat16*>(x), int(T), int(H), int(E), int(k),
+                             row_token, row_w, slot_row, static_cast<__nv_bfloat16*>(x_perm), acc_zero,
+                             tiles, int(max_tiles)));
   }
   return QMOE_OK;
 }
@@ -270,8 +292,8 @@ int launch_gemm_gateup(const void* x_perm, const void* w_gate_up, const int32_t*
   const int grid = int(std::min<int64_t>(units, num_sms(0)));
   if (grid <= 0) return QMOE_OK;
   QMOE_CHECK(set_smem(qmoe::grouped_gemm_kernel<qmoe::kModeGateUp>, C::kSmemBytes));
-  qmoe::grouped_gemm_kernel<qmoe::kModeGateUp><<<grid, qmoe::kGemmThreads, C::kSmemBytes, stream>>>(tmA, tmB, a);
-  return check_launch("grouped_gemm_kernel<gate_up>");
+  return launch_kernel(qmoe::grouped_gemm_kernel<qmoe::kModeGateUp>, dim3(grid), dim3(qmoe::kGemmThreads),
+                       C::kSmemBytes, stream, true, "grouped_gemm_kernel<gate_up>", tmA, tmB, a);
 }
 
 int launch_gemm_down(const void* act, const void* w_down, const int32_t* tiles, int64_t max_tiles,
@@ -308,8 +330,8 @@ int launch_gemm_down(const void* act, const void* w_down, const int32_t* tiles, 
   const int grid = int(std::min<int64_t>(units, num_sms(0)));
   if (grid <= 0) return QMOE_OK;
   QMOE_CHECK(set_smem(qmoe::grouped_gemm_kernel<qmoe::kModeDown>, C::kSmemBytes));
-  qmoe::grouped_gemm_kernel<qmoe::kModeDown><<<grid, qmoe::kGemmThreads, C::kSmemBytes, stream>>>(tmA, tmB, a);
-  return check_launch("grouped_gemm_kernel<down>");
+  return launch_kernel(qmoe::grouped_gemm_kernel<qmoe::kModeDown>, dim3(grid), dim3(qmoe::kGemmThreads),
+                       C::kSmemBytes, stream, true, "grouped_gemm_kernel<down>", tmA, tmB, a);
 }
 
 int launch_linear(const void* x, const void* w, int64_t T, int64_t K, int64_t N, void* out,
@@ -331,8 +353,8 @@ int launch_linear(const void* x, const void* w, int64_t T, int64_t K, int64_t N,
   const int grid = int(std::min<int64_t>(units, num_sms(0)));
   if (grid <= 0) return QMOE_OK;
   QMOE_CHECK(set_smem(qmoe::grouped_gemm_kernel<qmoe::kModePlain>, C::kSmemBytes));
-  qmoe::grouped_gemm_kernel<qmoe::kModePlain><<<grid, qmoe::kGemmThreads, C::kSmemBytes, stream>>>(tmA, tmB, a);
-  return check_launch("grouped_gemm_kernel<plain>");
+  return launch_kernel(qmoe::grouped_gemm_kernel<qmoe::kModePlain>, dim3(grid), dim3(qmoe::kGemmThreads),
+                       C::kSmemBytes, stream, true, "grouped_gemm_kernel<plain>", tmA, tmB, a);
 }
 
 int launch_finalize(const float* acc, const void* residual, int64_t T, int64_t H, void* out,
@@ -340,9 +362,9 @@ int launch_finalize(const float* acc, const void* residual, int64_t T, int64_t H
   const long long n8 = (long long)(T * H / 8);
   if (n8 == 0) return QMOE_OK;
   const int grid = int(std::min<long long>((n8 + 255) / 256, (long long)num_sms(0) * 8));
-  qmoe::combine_finalize_kernel<<<grid, 256, 0, stream>>>(
-      acc, static_cast<const __nv_bfloat16*>(residual), static_cast<__nv_bfloat16*>(out), n8);
-  return check_launch("combine_finalize_kernel");
+  return launch_kernel(qmoe::combine_finalize_kernel, dim3(grid), dim3(256), 0, stream, true,
+                       "combine_finalize_kernel", acc, static_cast<const __nv_bfloat16*>(residual),
+                       static_cast<__nv_bfloat16*>(out), (long long)n8);
 }
 
 // Workspace carving for the fused forward.

@@ -168,6 +168,8 @@ __global__ void __launch_bounds__(router_warps<G>() * 32, 1)
   const int lane = threadIdx.x & 31;
   const int t0 = blockIdx.x * kRouterChunk;
   const int nt = min(kRouterChunk, T - t0);
+  griddep_wait();
+  griddep_launch_dependents();
 
   // Stage the chunk's activations in shared memory as fp32.  Inside each
   // 256-element group, element 8l+q is stored at (q/4)*128 + 4l + q%4 so the
@@ -287,6 +289,8 @@ __global__ void __launch_bounds__(kRouterSmallWarps * 32)
   const int t0 = blockIdx.y * kRouterChunk;
   const int nt = min(kRouterChunk, T - t0);
   const int e = blockIdx.x * kRouterSmallWarps + warp;
+  griddep_wait();
+  griddep_launch_dependents();
   // weight slice first: its loads overlap the activation staging
   uint4 wv[G];
   if (e < E) {
@@ -352,6 +356,8 @@ __global__ void __launch_bounds__(kRouterChunk * 32)
   __shared__ int hist[256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+  griddep_wait();
+  griddep_launch_dependents();
   __syncthreads();
   const int t0 = blockIdx.x * kRouterChunk;
   const int t = t0 + warp;
