@@ -124,15 +124,19 @@ QMOE_API int qmoe_moe_permute(const int32_t* topk_idx, const float* topk_w, int3
  * (qwen_with_nki.py:1874-1907).  TMA-fed tcgen05 MMA, fp32 accumulation in
  * TMEM, fp32 SiLU*up, one bf16 cast.
  *
- *   x_perm   (R, H)       bf16 expert-grouped rows
+ *   x        (R, H) bf16 expert-grouped rows when gather_rows is NULL; else
+ *            the source activations (x_rows, H), row r of the grouped order
+ *            being x[gather_rows[r]] (row_token of qmoe_moe_permute), read with
+ *            TMA gather4 so no permuted copy is materialised
  *   w_gate_up (E, 2I, H)  bf16
  *   tiles                 from qmoe_moe_permute (or qmoe_blockwise_prepare)
- *   act      (R, I)       bf16 out: silu(x W_gate^T) * (x W_up^T)
+ *   act      (R, I)       bf16 out: silu(x W_gate^T) * (x W_up^T), grouped order
  * Requires H % 64 == 0, I % 128 == 0.
  * ---------------------------------------------------------------------- */
-QMOE_API int qmoe_grouped_gemm_gateup_swiglu(const void* x_perm, const void* w_gate_up,
-                                    const int32_t* tiles, int64_t max_tiles, int64_t R,
-                                    int64_t H, int64_t I, int64_t E, void* act, void* stream);
+QMOE_API int qmoe_grouped_gemm_gateup_swiglu(const void* x, int64_t x_rows, const int32_t* gather_rows,
+                                             const void* w_gate_up, const int32_t* tiles,
+                                             int64_t max_tiles, int64_t R, int64_t H, int64_t I,
+                                             int64_t E, void* act, void* stream);
 
 /* ------------------------------------------------------------------------
  * K3b  grouped GEMM, down projection with the weighted combine in the

@@ -74,6 +74,9 @@ struct GemmArgs {
                          // the partial sums meet in the fp32 accumulator)
   int a_rows_per_expert; // 2I (gate/up) or H (down)
   int up_row_offset;     // I (gate/up only)
+  // gate/up: when non-null, B row r of a tile is row gather_rows[r] of the
+  // source activations (TMA gather4 from x) instead of row r of x_perm
+  const int32_t* gather_rows;
   // gate/up and plain epilogues: bf16 output rows
   __nv_bfloat16* act;
   int act_ld;
@@ -157,56 +160,92 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     args.tiles ? args.tiles + 1 + 2 * args.max_tiles : nullptr, args.dense_rows};
 
   if (warp == 0) {
-    if (lane == 0) {
-      // ---------------- TMA producer ----------------
-      const uint64_t pol_w = policy_evict_first();
-      const uint64_t pol_x = policy_evict_last();
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t issued_mask = 0;       // stages holding a load issued by this thread
-      uint32_t issued_parity = 0;     // parity of that load's full-barrier phase
-      bool ok = true;
-      for (int u = blockIdx.x; ok && u < total_units; u += gridDim.x) {
-        const int tm = u / ksplit;
-        const int ks = u - tm * ksplit;
-        const int tile = tm / args.n_mtiles;
-        const int mt = tm - tile * args.n_mtiles;
-        const int e = tv.expert(tile);
-        const int row0 = tv.first_row(tile);
-        const int nb = (tv.nrows(tile) + kBoxRows - 1) / kBoxRows;
-        const int a_row = e * args.a_rows_per_expert + mt * kBM;
-        const uint32_t bytes = C::kATiles * C::kABytes + nb * kBoxRows * kBK * 2;
-        for (int kb = ks * kb_per_split; kb < (ks + 1) * kb_per_split; ++kb) {
-          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, kDevErrWaitTimeoutProducer)) {
+    // ---------------- TMA producer (warp 0) ----------------
+    // Lane 0 waits on the ring and issues the weight loads; with a gather,
+    // every lane then issues one gather4 of 4 activation rows.
+    const uint64_t pol_w = policy_evict_first();
+    const uint64_t pol_x = policy_evict_last();
+    const bool gather = kGateUp && args.gather_rows != nullptr;
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued_mask = 0;       // stages holding a load issued by this warp
+    uint32_t issued_parity = 0;     // parity of that load's full-barrier phase
+    bool ok = gather || lane == 0;  // box path: only lane 0 runs the loop
+    for (int u = blockIdx.x; ok && u < total_units; u += gridDim.x) {
+      const int tm = u / ksplit;
+      const int ks = u - tm * ksplit;
+      const int tile = tm / args.n_mtiles;
+      const int mt = tm - tile * args.n_mtiles;
+      const int e = tv.expert(tile);
+      const int row0 = tv.first_row(tile);
+      const int nrows = tv.nrows(tile);
+      const int nb = (nrows + kBoxRows - 1) / kBoxRows;
+      const int a_row = e * args.a_rows_per_expert + mt * kBM;
+      const int n_g4 = (nrows + 3) / 4;
+      int src[4] = {0, 0, 0, 0};
+      if (gather && lane < n_g4) {
+        const int last = args.gather_rows[row0 + nrows - 1];  // filler for rows past the tile
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int r = lane * 4 + q;
+          src[q] = r < nrows ? args.gather_rows[row0 + r] : last;
+        }
+      }
+      const uint32_t bytes = C::kATiles * C::kABytes +
+                             (gather ? n_g4 * 4 * kBK * 2 : nb * kBoxRows * kBK * 2);
+      for (int kb = ks * kb_per_split; kb < (ks + 1) * kb_per_split; ++kb) {
+        uint8_t* sb = stages + stage * C::kStageBytes;
+        uint8_t* bs = sb + C::kATiles * C::kABytes;
+        if (!gather) {
+          // box path: lane 0 alone runs the ring (no per-stage warp sync)
+          if (lane == 0) {
+            if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, kDevErrWaitTimeoutProducer)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[stage], bytes);
+            tma_load_2d_hint(sb, &tmA, kb * kBK, a_row, &full[stage], pol_w);
+            if (kGateUp)
+              tma_load_2d_hint(sb + C::kABytes, &tmA, kb * kBK, a_row + args.up_row_offset,
+                               &full[stage], pol_w);
+            for (int b = 0; b < nb; ++b)
+              tma_load_2d_hint(bs + b * (kBoxRows * kBK * 2), &tmB, kb * kBK, row0 + b * kBoxRows,
+                               &full[stage], pol_x);
+          }
+        } else {
+          int w_ok = 1;
+          if (lane == 0)
+            w_ok = mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, kDevErrWaitTimeoutProducer);
+          if (!__shfl_sync(0xFFFFFFFFu, w_ok, 0)) {
             ok = false;
             break;
           }
-          uint8_t* sb = stages + stage * C::kStageBytes;
-          mbar_arrive_expect_tx(&full[stage], bytes);
-          tma_load_2d_hint(sb, &tmA, kb * kBK, a_row, &full[stage], pol_w);
-          if (kGateUp)
-            tma_load_2d_hint(sb + C::kABytes, &tmA, kb * kBK, a_row + args.up_row_offset,
-                             &full[stage], pol_w);
-          uint8_t* bs = sb + C::kATiles * C::kABytes;
-          for (int b = 0; b < nb; ++b)
-            tma_load_2d_hint(bs + b * (kBoxRows * kBK * 2), &tmB, kb * kBK, row0 + b * kBoxRows,
-                             &full[stage], pol_x);
-          issued_mask |= 1u << stage;
-          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-          if (++stage == C::kStages) {
-            stage = 0;
-            phase ^= 1u;
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&full[stage], bytes);
+            tma_load_2d_hint(sb, &tmA, kb * kBK, a_row, &full[stage], pol_w);
+            tma_load_2d_hint(sb + C::kABytes, &tmA, kb * kBK, a_row + args.up_row_offset, &full[stage],
+                             pol_w);
           }
+          __syncwarp();  // the expect_tx above precedes every gather's complete_tx
+          if (lane < n_g4)
+            tma_gather4_hint(bs + lane * 4 * (kBK * 2), &tmB, kb * kBK, src[0], src[1], src[2], src[3],
+                             &full[stage], pol_x);
+        }
+        issued_mask |= 1u << stage;
+        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+        if (++stage == C::kStages) {
+          stage = 0;
+          phase ^= 1u;
         }
       }
-      if (!ok) {
-        // Let every load this thread issued land before the CTA's smem goes away.
-        for (int s = 0; s < C::kStages; ++s) {
-          if ((issued_mask >> s) & 1u) {
-            const unsigned long long t0 = globaltimer_ns();
-            while (!mbar_try_wait(&full[s], (issued_parity >> s) & 1u)) {
-              if (globaltimer_ns() - t0 > kWaitLimitNs) break;
-            }
+    }
+    if (!ok && lane == 0) {
+      // Let every load this warp issued land before the CTA's smem goes away.
+      for (int s = 0; s < C::kStages; ++s) {
+        if ((issued_mask >> s) & 1u) {
+          const unsigned long long t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full[s], (issued_parity >> s) & 1u)) {
+            if (globaltimer_ns() - t0 > kWaitLimitNs) break;
           }
         }
       }

@@ -180,6 +180,11 @@ namespace {
 // Token counts up to which the router runs as logits kernel (E/8 x T/8
 // CTAs) + selection kernel instead of the fused one-CTA-per-8-tokens kernel.
 constexpr int64_t kRouterSmallMaxT = 64;
+// Token counts up to which the gate/up GEMM gathers token rows itself (TMA
+// gather4) instead of reading a permuted copy: at decode sizes the copy costs
+// more than it saves; for prefill, 16-row boxes of the copy feed the tensor
+// core faster than 4-row gathers.
+constexpr int64_t kGatherMaxT = 64;
 
 int launch_router(const void* x, const void* w, const float* bias, int64_t T, int64_t H, int64_t E,
                   int64_t k, int normalize, float* logits, int32_t* topk_idx, float* topk_w,
@@ -271,13 +276,18 @@ int launch_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chunk_
   return QMOE_OK;
 }
 
-int launch_gemm_gateup(const void* x_perm, const void* w_gate_up, const int32_t* tiles,
-                       int64_t max_tiles, int64_t R, int64_t H, int64_t I, int64_t E, void* act,
-                       cudaStream_t stream) {
+// x: x_perm (R rows, permuted) when gather_rows is null, else the source
+// activations (x_rows rows) gathered by gather_rows[r] with TMA gather4.
+int launch_gemm_gateup(const void* x, int64_t x_rows, const int32_t* gather_rows, const void* w_gate_up,
+                       const int32_t* tiles, int64_t max_tiles, int64_t R, int64_t H, int64_t I, int64_t E,
+                       void* act, cudaStream_t stream) {
   using C = qmoe::GemmCfg<qmoe::kModeGateUp>;
   CUtensorMap tmA, tmB;
   QMOE_CHECK(make_tmap_bf16(&tmA, w_gate_up, uint64_t(H), uint64_t(E * 2 * I), qmoe::kBK, qmoe::kBM));
-  QMOE_CHECK(make_tmap_bf16(&tmB, x_perm, uint64_t(H), uint64_t(R), qmoe::kBK, qmoe::kBoxRows));
+  if (gather_rows)
+    QMOE_CHECK(make_tmap_bf16(&tmB, x, uint64_t(H), uint64_t(x_rows), qmoe::kBK, 1));
+  else
+    QMOE_CHECK(make_tmap_bf16(&tmB, x, uint64_t(H), uint64_t(R), qmoe::kBK, qmoe::kBoxRows));
   qmoe::GemmArgs a{};
   a.tiles = tiles;
   a.max_tiles = int(max_tiles);
@@ -286,6 +296,7 @@ int launch_gemm_gateup(const void* x_perm, const void* w_gate_up, const int32_t*
   a.k_splits = 1;
   a.a_rows_per_expert = int(2 * I);
   a.up_row_offset = int(I);
+  a.gather_rows = gather_rows;
   a.act = static_cast<__nv_bfloat16*>(act);
   a.act_ld = int(I);
   const int64_t units = max_tiles * a.n_mtiles;
@@ -395,7 +406,7 @@ FwdLayout fwd_layout(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I) {
   L.tiles = take(sizeof(int32_t) * size_t(1 + 3 * qmoe_max_tiles(R, E)));
   L.topk_idx = take(sizeof(int32_t) * size_t(R));
   L.topk_w = take(sizeof(float) * size_t(R));
-  L.x_perm = take(2 * size_t(R * H));
+  L.x_perm = take(T > kGatherMaxT ? 2 * size_t(R * H) : 0);
   L.act = take(2 * size_t(R * I));
   L.acc = take(sizeof(float) * size_t(T * H));
   L.total = o;
@@ -482,21 +493,23 @@ int qmoe_moe_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chun
                         row_w, slot_row, tiles, x_perm, acc_zero, static_cast<cudaStream_t>(stream));
 }
 
-int qmoe_grouped_gemm_gateup_swiglu(const void* x_perm, const void* w_gate_up,
-                                    const int32_t* tiles, int64_t max_tiles, int64_t R, int64_t H,
-                                    int64_t I, int64_t E, void* act, void* stream) {
-  QMOE_REQUIRE(x_perm && w_gate_up && tiles && act, QMOE_ERR_INVALID_ARGUMENT, "gate_up: null pointer");
+int qmoe_grouped_gemm_gateup_swiglu(const void* x, int64_t x_rows, const int32_t* gather_rows,
+                                    const void* w_gate_up, const int32_t* tiles, int64_t max_tiles,
+                                    int64_t R, int64_t H, int64_t I, int64_t E, void* act, void* stream) {
+  QMOE_REQUIRE(x && w_gate_up && tiles && act, QMOE_ERR_INVALID_ARGUMENT, "gate_up: null pointer");
   QMOE_REQUIRE(R >= 0 && R < (int64_t(1) << 31), QMOE_ERR_INVALID_ARGUMENT, "gate_up: bad R");
+  QMOE_REQUIRE(!gather_rows || (x_rows > 0 && x_rows < (int64_t(1) << 31)), QMOE_ERR_INVALID_ARGUMENT,
+               "gate_up: bad x_rows for a gather");
   QMOE_REQUIRE(H > 0 && H % qmoe::kBK == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "gate_up: H %% 64 != 0");
   QMOE_REQUIRE(I > 0 && I % qmoe::kBM == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "gate_up: I %% 128 != 0");
   QMOE_REQUIRE(E > 0 && E * 2 * I < (int64_t(1) << 31), QMOE_ERR_UNSUPPORTED_SHAPE, "gate_up: E too large");
   QMOE_REQUIRE(max_tiles >= 0 && max_tiles < (int64_t(1) << 24), QMOE_ERR_INVALID_ARGUMENT, "gate_up: bad max_tiles");
-  QMOE_REQUIRE(aligned16(x_perm) && aligned16(w_gate_up) && aligned16(act), QMOE_ERR_MISALIGNED,
+  QMOE_REQUIRE(aligned16(x) && aligned16(w_gate_up) && aligned16(act), QMOE_ERR_MISALIGNED,
                "gate_up: pointers must be 16-byte aligned");
   DeviceInfo* d = nullptr;
   QMOE_CHECK(device_info(&d));
   if (R == 0) return QMOE_OK;
-  return launch_gemm_gateup(x_perm, w_gate_up, tiles, max_tiles, R, H, I, E, act,
+  return launch_gemm_gateup(x, x_rows, gather_rows, w_gate_up, tiles, max_tiles, R, H, I, E, act,
                             static_cast<cudaStream_t>(stream));
 }
 
@@ -835,7 +848,7 @@ int qmoe_moe_forward(const void* x, const void* w_router, const float* router_bi
   int32_t* tiles = reinterpret_cast<int32_t*>(ws + L.tiles);
   int32_t* idx = topk_idx ? topk_idx : reinterpret_cast<int32_t*>(ws + L.topk_idx);
   float* tw = topk_w ? topk_w : reinterpret_cast<float*>(ws + L.topk_w);
-  void* x_perm = ws + L.x_perm;
+  void* x_perm = T > kGatherMaxT ? ws + L.x_perm : nullptr;
   void* act = ws + L.act;
   float* acc = reinterpret_cast<float*>(ws + L.acc);
   const int64_t R = T * k;
@@ -846,7 +859,10 @@ int qmoe_moe_forward(const void* x, const void* w_router, const float* router_bi
                            chunk_hist, s));
   QMOE_CHECK(launch_permute(idx, tw, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w,
                             slot_row, tiles, x_perm, acc, s));
-  QMOE_CHECK(launch_gemm_gateup(x_perm, w_gate_up, tiles, max_tiles, R, H, I, E, act, s));
+  if (x_perm)
+    QMOE_CHECK(launch_gemm_gateup(x_perm, R, nullptr, w_gate_up, tiles, max_tiles, R, H, I, E, act, s));
+  else
+    QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, s));
   QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s));
   return launch_finalize(acc, residual, T, H, out, s);
 }
@@ -950,7 +966,7 @@ extern "C" int qmoe_moe_forward_noalloc(const void* x, const void* w_router,
   int32_t* tiles = reinterpret_cast<int32_t*>(ws + L.tiles);
   int32_t* idx = topk_idx ? topk_idx : reinterpret_cast<int32_t*>(ws + L.topk_idx);
   float* tw = topk_w ? topk_w : reinterpret_cast<float*>(ws + L.topk_w);
-  void* x_perm = ws + L.x_perm;
+  void* x_perm = T > kGatherMaxT ? ws + L.x_perm : nullptr;
   void* act = ws + L.act;
   float* acc = reinterpret_cast<float*>(ws + L.acc);
   const int64_t R = T * k;
@@ -960,7 +976,10 @@ extern "C" int qmoe_moe_forward_noalloc(const void* x, const void* w_router,
                            chunk_hist, s));
   QMOE_CHECK(launch_permute(idx, tw, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w,
                             slot_row, tiles, x_perm, acc, s));
-  QMOE_CHECK(launch_gemm_gateup(x_perm, w_gate_up, tiles, max_tiles, R, H, I, E, act, s));
+  if (x_perm)
+    QMOE_CHECK(launch_gemm_gateup(x_perm, R, nullptr, w_gate_up, tiles, max_tiles, R, H, I, E, act, s));
+  else
+    QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, s));
   QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s));
   return launch_finalize(acc, residual, T, H, out, s);
 }

@@ -174,8 +174,12 @@ def _run_routed(x: torch.Tensor, w: MoEWeights, idx: torch.Tensor, tw: torch.Ten
     E = w.num_experts
     hist = ops.routing_histogram(idx, E)
     acc = torch.empty((T, H), dtype=torch.float32, device=x.device)
-    p = ops.moe_permute(idx, tw, hist, E, x=x, gather=True, acc_zero=acc)
-    act = ops.grouped_gemm_gateup_swiglu(p["x_perm"], w.gate_up, p["tiles"], p["max_tiles"])
+    if T > ops.GATHER_MAX_T:
+        p = ops.moe_permute(idx, tw, hist, E, x=x, gather=True, acc_zero=acc)
+        act = ops.grouped_gemm_gateup_swiglu(p["x_perm"], w.gate_up, p["tiles"], p["max_tiles"])
+    else:
+        p = ops.moe_permute(idx, tw, hist, E, x=x, gather=False, acc_zero=acc)
+        act = ops.grouped_gemm_gateup_swiglu(x, w.gate_up, p["tiles"], p["max_tiles"], gather_rows=p["row_token"])
     ops.grouped_gemm_down_combine(act, w.down, p["tiles"], p["max_tiles"], p["row_token"], p["row_w"], acc)
     return ops.combine_finalize(acc, residual)
 
@@ -230,9 +234,11 @@ class MoEPlan:
         self.row_w = torch.empty(max(R, 1), **f32)
         self.slot_row = torch.empty((T, k), **i32)
         self.tiles = torch.empty(1 + 3 * self.max_tiles, **i32)
-        self.x_perm = torch.empty((max(R, 1), H), dtype=torch.bfloat16, device=dev)
         self.act = torch.empty((max(R, 1), I), dtype=torch.bfloat16, device=dev)
         self.acc = torch.empty((max(T, 1), H), **f32)
+        # prefill sizes read a permuted copy of the rows; decode sizes gather
+        self.x_perm = (torch.empty((max(R, 1), H), dtype=torch.bfloat16, device=dev)
+                       if T > ops.GATHER_MAX_T else None)
         # small batches route through the logits + selection kernels
         self.logits = torch.empty((T, E), **f32) if T <= ops.ROUTER_SMALL_MAX_T else None
         self._lib = _C.lib()
@@ -258,9 +264,13 @@ class MoEPlan:
                                       p(self.slot_row), p(self.tiles), p(self.x_perm), p(self.acc), s),
                  "permute")
         mark(2)
-        _C.check(lib.qmoe_grouped_gemm_gateup_swiglu(p(self.x_perm), p(w.gate_up), p(self.tiles),
-                                                     self.max_tiles, R, H, I, E, p(self.act), s),
-                 "gate_up")
+        if self.x_perm is not None:
+            _C.check(lib.qmoe_grouped_gemm_gateup_swiglu(p(self.x_perm), R, None, p(w.gate_up), p(self.tiles),
+                                                         self.max_tiles, R, H, I, E, p(self.act), s), "gate_up")
+        else:
+            _C.check(lib.qmoe_grouped_gemm_gateup_swiglu(p(x), T, p(self.row_token), p(w.gate_up),
+                                                         p(self.tiles), self.max_tiles, R, H, I, E, p(self.act),
+                                                         s), "gate_up")
         mark(3)
         _C.check(lib.qmoe_grouped_gemm_down_combine(p(self.act), p(w.down), p(self.tiles), self.max_tiles,
                                                     p(self.row_token), p(self.row_w), R, H, I, E,

@@ -15,6 +15,7 @@ from . import _C
 
 ROUTER_CHUNK = 8  # QMOE_ROUTER_CHUNK
 ROUTER_SMALL_MAX_T = 64  # batches up to this size take the two-kernel small-batch router
+GATHER_MAX_T = 64  # batches up to this size gather token rows inside the gate/up GEMM
 
 
 def _ptr(t: Optional[torch.Tensor]):
@@ -110,23 +111,30 @@ def moe_permute(topk_idx: torch.Tensor, topk_w: torch.Tensor, chunk_hist: torch.
                 slot_row=slot_row, tiles=tiles, max_tiles=mt, x_perm=x_perm)
 
 
-def grouped_gemm_gateup_swiglu(x_perm: torch.Tensor, w_gate_up: torch.Tensor, tiles: torch.Tensor,
-                               max_tiles_: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """K3a.  x_perm (R,H) bf16, w_gate_up (E,2I,H) bf16 -> act (R,I) bf16."""
-    _need(x_perm, "x_perm", torch.bfloat16, 2)
+def grouped_gemm_gateup_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, tiles: torch.Tensor,
+                               max_tiles_: int, out: Optional[torch.Tensor] = None,
+                               gather_rows: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """K3a.  act (R, I) bf16 = SiLU(x W_gate^T) * (x W_up^T) in grouped order.
+    ``x`` is x_perm (R, H), or with ``gather_rows`` (R,) int32 the source
+    activations whose row gather_rows[r] is grouped row r."""
+    _need(x, "x", torch.bfloat16, 2)
     _need(w_gate_up, "w_gate_up", torch.bfloat16, 3)
     _need(tiles, "tiles", torch.int32, 1)
-    R, H = x_perm.shape
+    rows, H = x.shape
+    R = rows
+    if gather_rows is not None:
+        _need(gather_rows, "gather_rows", torch.int32, 1)
+        R = gather_rows.shape[0]
     E, I2, H2 = w_gate_up.shape
     if H2 != H or I2 % 2:
-        raise ValueError("w_gate_up must be (E, 2I, H) matching x_perm")
+        raise ValueError("w_gate_up must be (E, 2I, H) matching x")
     I = I2 // 2
-    dev = x_perm.device
+    dev = x.device
     act = out if out is not None else torch.empty((R, I), dtype=torch.bfloat16, device=dev)
     with torch.cuda.device(dev):
         _C.check(_C.lib().qmoe_grouped_gemm_gateup_swiglu(
-            _ptr(x_perm), _ptr(w_gate_up), _ptr(tiles), max_tiles_, R, H, I, E, _ptr(act),
-            _stream(dev)), "qmoe_grouped_gemm_gateup_swiglu")
+            _ptr(x), rows, _ptr(gather_rows), _ptr(w_gate_up), _ptr(tiles), max_tiles_, R, H, I, E,
+            _ptr(act), _stream(dev)), "qmoe_grouped_gemm_gateup_swiglu")
     return act
 
 

@@ -43,7 +43,7 @@ def test_host_side_validation_needs_no_gpu(lib):
     st = lib.qmoe_router_topk(p, p, None, 4, 2048, 32, 33, 1, None, p, p, None, None)
     assert st == -1
     # I not a multiple of 128
-    st = lib.qmoe_grouped_gemm_gateup_swiglu(p, p, p, 10, 8, 2048, 100, 128, p, None)
+    st = lib.qmoe_grouped_gemm_gateup_swiglu(p, 0, None, p, p, 10, 8, 2048, 100, 128, p, None)
     assert st == -2
     # misaligned pointer
     st = lib.qmoe_combine_finalize(p + 4, None, 2, 64, p, None)
@@ -54,6 +54,8 @@ def test_workspace_size_query(lib):
     small = lib.qmoe_moe_forward_workspace_size(1, 2048, 128, 8, 768)
     big = lib.qmoe_moe_forward_workspace_size(1024, 2048, 128, 8, 768)
     assert 0 < small < big
-    # dominated by x_perm (T*k*H bf16) + act (T*k*I bf16) + fp32 accumulator (T*H)
+    # prefill sizes: permuted rows (T*k*H bf16) + act (T*k*I bf16) + fp32
+    # accumulator (T*H); decode sizes gather token rows inside the GEMM
     assert big >= 1024 * 8 * 2048 * 2 + 1024 * 8 * 768 * 2 + 1024 * 2048 * 4
+    assert lib.qmoe_moe_forward_workspace_size(64, 2048, 128, 8, 768) < 64 * 8 * 2048 * 2
     assert lib.qmoe_max_tiles(8192, 128) == 128 + 64 + 1

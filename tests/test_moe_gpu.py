@@ -64,8 +64,11 @@ def test_grouped_gemms_vs_oracle(cuda_dev, oracle, T, H, E, k, I):
     acc = torch.empty((T, H), dtype=torch.float32, device=cuda_dev)
     p = ops.moe_permute(idx, w, hist, E, x=x, gather=True, acc_zero=acc)
     act = ops.grouped_gemm_gateup_swiglu(p["x_perm"], wgu, p["tiles"], p["max_tiles"])
+    # the gathered form (TMA gather4 straight from x) gives the same activations
+    act_g = ops.grouped_gemm_gateup_swiglu(x, wgu, p["tiles"], p["max_tiles"], gather_rows=p["row_token"])
     ops.grouped_gemm_down_combine(act, wd, p["tiles"], p["max_tiles"], p["row_token"], p["row_w"], acc)
     torch.cuda.synchronize()
+    assert torch.equal(act, act_g)
     from nki_moe_7013_b200 import _C
 
     assert _C.device_error() == 0
