@@ -527,7 +527,7 @@ def run_ours_ep(args):
 
     from nki_moe_7013_b200 import _C
     from nki_moe_7013_b200.config import Qwen3MoeConfig
-    from nki_moe_7013_b200.ep import ExpertParallelMoE
+    from nki_moe_7013_b200.ep import PeerExpertParallelMoE
     from nki_moe_7013_b200.moe import MoEWeights
     from nki_moe_7013_b200.synth import normal_bf16_device
 
@@ -544,7 +544,7 @@ def run_ours_ep(args):
     router = normal_bf16_device(1, (E, H), 0.02, dev)
     local = MoEWeights(router, normal_bf16_device(2000 + rank, (el, 2 * I_MOE, H), 0.02, dev),
                        normal_bf16_device(3000 + rank, (el, H, I_MOE), 0.02, dev))
-    moe = ExpertParallelMoE(cfg, router, local)
+    moe = PeerExpertParallelMoE(cfg, router, local, max_tokens=T)
     x = normal_bf16_device(1000 + rank, (T, H), 1.0, dev)
 
     def barrier():
@@ -552,7 +552,6 @@ def run_ours_ep(args):
         torch.cuda.synchronize()
 
     sampler = ClockSampler() if rank == 0 else None
-    stages = ("route", "dispatch", "experts", "combine")
 
     def timed_run():
         t_end = time.perf_counter() + args.clock_settle_s
@@ -562,31 +561,31 @@ def run_ours_ep(args):
             torch.cuda.synchronize()
         for _ in range(args.warmup):
             moe(x)
-        evs = [{n: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for n in stages}
-               for _ in range(args.steps)]
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
-        recv = []
-        for s_ in range(args.steps):
-            moe(x, events=evs[s_])
-            recv.append(moe.last_recv_rows)
+        e0.record()
+        for _ in range(args.steps):
+            moe(x)
+        e1.record()
         barrier()
-        span = evs[0]["route"][0].elapsed_time(evs[-1]["combine"][1])
-        st = {n: statistics.mean(e[n][0].elapsed_time(e[n][1]) for e in evs) for n in stages}
-        return span, st, statistics.mean(recv)
+        return e0.elapsed_time(e1)
 
     if sampler:
         sampler.start()
-    span_ms, stage_ms, recv_rows = timed_run()
+    span_ms = timed_run()
     clocks = sampler.stop() if sampler else None
-    t = torch.tensor([span_ms, stage_ms["experts"]], dtype=torch.float64, device=dev)
+    t = torch.tensor([span_ms], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    span_ms, experts_ms = float(t[0]), float(t[1])
+    span_ms = float(t[0])
     ms_per_step = span_ms / args.steps
     value = T * world * args.steps / (span_ms / 1e3)
     hbm_gbs, tf_burst, _, peak_kind = load_peaks()
-    # expert stage of this rank: its el experts' weights + received rows in/out
-    exp_bytes = el * (GATE_UP_BYTES_PER_EXPERT + DOWN_BYTES_PER_EXPERT) + recv_rows * (H * 2 * 3 + I_MOE * 4)
-    achieved = exp_bytes / (experts_ms * 1e-3) / 1e9
+    # bytes each rank must stream per step: its experts' weights, plus the
+    # rows it sends and receives over NVLink (k rows of H bf16 per token)
+    recv_rows = int(moe.recv_rows.item())
+    exp_bytes = el * (GATE_UP_BYTES_PER_EXPERT + DOWN_BYTES_PER_EXPERT) + recv_rows * (H * 2 * 2 + I_MOE * 4)
+    achieved = exp_bytes / (ms_per_step * 1e-3) / 1e9
+    nvlink_bytes = 2 * T * K_TOP * H * 2 * (world - 1) / world  # dispatch + return, remote share
 
     x_host = x.cpu().pin_memory()
     y_host = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
@@ -612,17 +611,20 @@ def run_ours_ep(args):
                    "moe_intermediate": I_MOE, "parallelism": f"ep{world}",
                    "l2": "inputs larger than L2: expert weights and all-to-all buffers streamed per step"},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2,
-                "api": "ExpertParallelMoE.forward(hidden_states), pinned host in/out"},
-        "gpu_launches": 11 * args.steps,
-        "stage_us": {n: round(v * 1e3, 2) for n, v in stage_ms.items()},
-        "roofline": {"bound": "hbm", "kernel": "expert stage (grouped GEMMs on the local experts)",
+                "api": "PeerExpertParallelMoE.forward(hidden_states), pinned host in/out"},
+        "gpu_launches": 12 * args.steps,
+        "roofline": {"bound": "hbm", "kernel": "whole EP step (local experts' weights + rows in/out)",
                      "achieved": achieved, "peak": hbm_gbs, "unit": "GB/s", "frac": achieved / hbm_gbs,
-                     "peak_kind": peak_kind, "traffic": None, "algorithmic_bytes_per_launch": exp_bytes,
-                     "rows_received": recv_rows},
+                     "peak_kind": peak_kind, "traffic": None, "algorithmic_bytes_per_step": exp_bytes,
+                     "rows_received": recv_rows,
+                     "nvlink_gb_per_step": nvlink_bytes / 1e9,
+                     "nvlink_gbs": nvlink_bytes / (ms_per_step * 1e-3) / 1e9},
         "clocks": clocks,
     }
     if rank == 0:
         print(json.dumps(line))
+    dist.barrier()
+    moe.close()
     dist.barrier()
     dist.destroy_process_group()
     return 0

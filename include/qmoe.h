@@ -290,8 +290,8 @@ QMOE_API int qmoe_attention_decode(const void* q, const void* k_cache, const voi
  *   destination rank), send_w (T*k) fp32 routing weight, pair_pos (T, k) int32
  *   row of each (token, slot) in the send buffer.
  * qmoe_ep_unpack: out (T, H) bf16 = residual + sum over slots of the
- *   returned weighted rows y_back[pair_pos[t, j]] (fp32 sum, one cast).
- *   H % 256 == 0.
+ *   returned weighted rows y_back[pair_pos[t, j]] (fp32 sum, one cast);
+ *   pair_pos NULL means row t*k + j.  H % 256 == 0.
  * ---------------------------------------------------------------------- */
 QMOE_API int qmoe_routing_histogram(const int32_t* topk_idx, int64_t T, int64_t k, int64_t E,
                                     int32_t* chunk_hist, void* stream);
@@ -301,6 +301,56 @@ QMOE_API int qmoe_ep_pack(const int32_t* topk_idx, const float* topk_w, const vo
                           int32_t* send_expert, float* send_w, int32_t* pair_pos, void* stream);
 QMOE_API int qmoe_ep_unpack(const void* y_back, const int32_t* pair_pos, const void* residual,
                             int64_t T, int64_t H, int64_t k, int64_t n_back, void* out, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Expert parallelism over peer memory (one node, NVLink / NVSwitch), with no
+ * host synchronisation: the whole EP step is stream-ordered kernels.
+ * Replaces the EP variant of qwen_with_nki.py:8148-8271 (masked local
+ * experts + world all-reduce) with row exchange through mapped peer buffers.
+ *
+ * qmoe_ipc_export / qmoe_ipc_import / qmoe_ipc_close: CUDA IPC of a
+ *   caller-allocated device buffer.  export gives a 64-byte handle of the
+ *   allocation holding `ptr` and ptr's offset inside it; import maps a peer's
+ *   handle (peer access enabled lazily) and returns the pointer at `offset`
+ *   plus the mapping base for close.
+ * qmoe_ep_ctrl_words: int32 words of one rank's control block (two parity
+ *   halves of [N x E counts | 3 x N flags]); zero it once before first use.
+ * qmoe_ep_exchange_counts: one CTA.  Writes this rank's per-expert row
+ *   counts (from qmoe_moe_permute) into every peer's control block, flags
+ *   them, waits (bounded) for every rank's counts, then writes dest_base (E):
+ *   the first row of this rank's rows of expert e in e's owner's receive
+ *   buffer; the tile list of the local experts over this rank's receive
+ *   buffer (expert ids local, 0..e_local-1); and recv_rows[0].
+ * qmoe_ep_dispatch: copies every (token, slot) row of x straight into the
+ *   owner's receive buffer (peer_recv_x[d] + (parity*cap_rows + row)*H) with
+ *   meta {weight bits, source rank, token*k + slot, 0} (int4 per row).
+ * qmoe_ep_signal_wait: one warp; flag `kind` (1 dispatch, 2 combine) of this
+ *   rank in every peer, then wait (bounded) for every rank's flag.
+ * qmoe_grouped_gemm_down_return: K3b whose epilogue stores each weighted bf16
+ *   row into the SOURCE rank's return buffer: peer_ret[src] + (ret_row0 +
+ *   token*k + slot)*H (the combine, fused into the GEMM, over peer memory).
+ * Arrays of peer pointers (peer_ctrl, peer_recv_x, ...) are device arrays
+ *   of n_ranks pointers.  A time-out records device error 5 and returns.
+ * ---------------------------------------------------------------------- */
+QMOE_API int qmoe_ipc_export(const void* ptr, void* handle_out, int64_t* offset_out);
+QMOE_API int qmoe_ipc_import(const void* handle, int64_t offset, void** ptr_out, void** base_out);
+QMOE_API int qmoe_ipc_close(void* base);
+QMOE_API int64_t qmoe_ep_ctrl_words(int64_t n_ranks, int64_t E);
+QMOE_API int qmoe_ep_exchange_counts(const int32_t* counts, int* const* peer_ctrl, int* my_ctrl, int64_t me,
+                                     int64_t n_ranks, int64_t E, int64_t e_local, int64_t parity,
+                                     int64_t epoch, int32_t* dest_base, int32_t* tiles, int64_t max_tiles,
+                                     int32_t* recv_rows, int64_t cap_rows, void* stream);
+QMOE_API int qmoe_ep_dispatch(const void* x, const int32_t* topk_idx, const float* topk_w,
+                              const int32_t* slot_row, const int32_t* offsets, const int32_t* dest_base,
+                              void* const* peer_recv_x, void* const* peer_recv_meta, int64_t T, int64_t k,
+                              int64_t H, int64_t e_local, int64_t me, int64_t parity, int64_t cap_rows,
+                              void* stream);
+QMOE_API int qmoe_ep_signal_wait(int* const* peer_ctrl, int* my_ctrl, int64_t n_ranks, int64_t E,
+                                 int64_t me, int64_t parity, int64_t kind, int64_t epoch, void* stream);
+QMOE_API int qmoe_grouped_gemm_down_return(const void* act, const void* w_down, const int32_t* tiles,
+                                           int64_t max_tiles, const void* row_meta, void* const* peer_ret,
+                                           int64_t ret_row0, int64_t n_ret_rows, int64_t n_ranks, int64_t R,
+                                           int64_t H, int64_t I, int64_t E, void* stream);
 
 /* ------------------------------------------------------------------------
  * Allocation-free fused forward.  No counterpart in the reference: it exists

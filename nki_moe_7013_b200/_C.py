@@ -50,6 +50,14 @@ _SIGNATURES = {
     "qmoe_routing_histogram": (I32, [P, I64, I64, I64, P, P]),
     "qmoe_ep_pack": (I32, [P, P, P, I64, I64, I64, I64, I64, P, P, P, P, P, P, P]),
     "qmoe_ep_unpack": (I32, [P, P, P, I64, I64, I64, I64, P, P]),
+    "qmoe_ipc_export": (I32, [P, P, ctypes.POINTER(ctypes.c_int64)]),
+    "qmoe_ipc_import": (I32, [P, I64, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)]),
+    "qmoe_ipc_close": (I32, [P]),
+    "qmoe_ep_ctrl_words": (I64, [I64, I64]),
+    "qmoe_ep_exchange_counts": (I32, [P, P, P, I64, I64, I64, I64, I64, I64, P, P, I64, P, I64, P]),
+    "qmoe_ep_dispatch": (I32, [P, P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, I64, P]),
+    "qmoe_ep_signal_wait": (I32, [P, P, I64, I64, I64, I64, I64, I64, P]),
+    "qmoe_grouped_gemm_down_return": (I32, [P, P, P, I64, P, P, I64, I64, I64, I64, I64, I64, I64, P]),
     "qmoe_moe_forward_noalloc": (I32, [P, P, P, P, P, P, I64, I64, I64, I64, I64, I32, P, P, P, P]),
 }
 

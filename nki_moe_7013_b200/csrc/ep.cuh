@@ -140,7 +140,7 @@ __global__ void __launch_bounds__(kEpThreads)
   const int col = (gw - t * slabs) * 256 + lane * 8;
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   for (int j = 0; j < k; ++j) {
-    const int r = pair_pos[size_t(t) * k + j];
+    const int r = pair_pos ? pair_pos[size_t(t) * k + j] : t * k + j;
     if (r < 0 || r >= n_back) {
       if (r >= n_back) record_device_error(kDevErrBadIndex);
       continue;

@@ -1,0 +1,205 @@
+// Expert parallelism over peer memory (NVLink / NVSwitch), no host sync.
+//
+// Every rank maps its peers' EP buffers (CUDA IPC) and a step runs as:
+//
+//   1. ep_exchange_counts (1 CTA): my per-expert row counts -> row `me` of
+//      every peer's count matrix, then a flag; wait for all N rows; derive
+//        dest_base[e]  first row of my rows of expert e in the receive buffer
+//                      of e's rank (rows there are grouped by expert, then by
+//                      source rank, then by token),
+//        the tile list of my local experts over my receive buffer, and the
+//        number of rows I receive;
+//   2. ep_dispatch: each (token, slot) row of x goes straight from x into the
+//      destination rank's receive buffer (peer stores), with its routing
+//      weight and its return address (source rank, token*k + slot);
+//   3. ep_signal_wait: flag every peer "my rows are in your buffer", wait for
+//      everyone's flag;
+//   4. grouped gate/up + down GEMMs on the receive buffer; the down epilogue
+//      writes each weighted bf16 row back into the SOURCE rank's return
+//      buffer through peer stores (the combine, fused into the GEMM);
+//   5. ep_signal_wait again ("your rows are back"), then ep_unpack sums the k
+//      returned rows of every token in fp32.
+//
+// Receive / return buffers and the control block have two halves used on
+// alternate steps (parity), so a fast rank can never overwrite data a peer
+// is still reading: writing parity p of step i+2 requires the peer's step
+// i+2 counts, which the peer publishes only after finishing step i.
+//
+// Every cross-GPU wait is bounded (kWaitLimitNs); on time-out the kernel
+// records a device error and returns.  No cluster-multicast load anywhere.
+#pragma once
+
+#include "common.cuh"
+
+namespace qmoe {
+
+// Control block of one rank (int32 words); per parity half:
+//   counts[N][E] | flag_counts[N] | flag_dispatch[N] | flag_combine[N]
+__host__ __device__ __forceinline__ size_t ep_ctrl_words_per_parity(int N, int E) {
+  return size_t(N) * E + 3 * size_t(N);
+}
+enum EpFlagKind : int { kEpFlagCounts = 0, kEpFlagDispatch = 1, kEpFlagCombine = 2 };
+
+__device__ __forceinline__ size_t ep_flag_word(int N, int E, int p, int kind, int s) {
+  return p * ep_ctrl_words_per_parity(N, E) + size_t(N) * E + size_t(kind) * N + s;
+}
+
+__device__ __forceinline__ void st_release_sys(int* ptr, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* ptr) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
+// Spin (bounded) until *flag >= epoch.  Returns false and records `code` on
+// time-out.
+__device__ __forceinline__ bool ep_wait_flag(const int* flag, int epoch, unsigned int code) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (ld_acquire_sys(flag) < epoch) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      record_device_error(code);
+      return false;
+    }
+    __nanosleep(100);
+  }
+  return true;
+}
+
+constexpr unsigned int kDevErrPeerTimeout = 5;
+
+// Write `epoch` into flag (kind, p, me) of every peer, then wait until every
+// peer has written flag (kind, p, s) of mine.  One warp.
+__device__ __forceinline__ bool ep_signal_and_wait(int* const* peer_ctrl, int* my_ctrl, int N, int E, int me,
+                                                   int p, int kind, int epoch) {
+  const int lane = threadIdx.x & 31;
+  __threadfence_system();
+  __syncwarp();
+  for (int d = lane; d < N; d += 32) st_release_sys(peer_ctrl[d] + ep_flag_word(N, E, p, kind, me), epoch);
+  bool ok = true;
+  for (int s = lane; s < N; s += 32) ok &= ep_wait_flag(my_ctrl + ep_flag_word(N, E, p, kind, s), epoch, kDevErrPeerTimeout);
+  ok = __all_sync(0xFFFFFFFFu, ok);
+  __threadfence_system();
+  return ok;
+}
+
+// ---------------------------------------------------------------------------
+// 1. count exchange (one CTA of 256 threads; E <= 256, N <= 32)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+    ep_exchange_counts_kernel(const int32_t* __restrict__ counts, int* const* __restrict__ peer_ctrl,
+                              int* __restrict__ my_ctrl, int me, int N, int E, int e_local, int p, int epoch,
+                              int32_t* __restrict__ dest_base, int32_t* __restrict__ tiles, int max_tiles,
+                              int32_t* __restrict__ recv_rows, int cap_rows) {
+  __shared__ int tot[256];
+  __shared__ int expert_off[257];
+  __shared__ int ok_s;
+  const int tid = threadIdx.x;
+  griddep_wait();
+  // my counts row into every peer's matrix
+  for (int i = tid; i < N * E; i += blockDim.x) {
+    const int d = i / E, e = i - d * E;
+    peer_ctrl[d][size_t(p) * ep_ctrl_words_per_parity(N, E) + size_t(me) * E + e] = counts[e];
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (tid < 32) {
+    const bool ok = ep_signal_and_wait(peer_ctrl, my_ctrl, N, E, me, p, kEpFlagCounts, epoch);
+    if (tid == 0) ok_s = ok;
+  }
+  __syncthreads();
+  if (!ok_s) {
+    // leave an empty tile list and zero received rows so later kernels do nothing
+    if (tid == 0) {
+      tiles[0] = 0;
+      recv_rows[0] = 0;
+    }
+    return;
+  }
+  const volatile int* M = my_ctrl + size_t(p) * ep_ctrl_words_per_parity(N, E);
+  for (int e = tid; e < E; e += blockDim.x) {
+    int t = 0;
+    for (int s = 0; s < N; ++s) t += M[s * E + e];
+    tot[e] = t;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    // row offset of each expert inside its owner's receive buffer
+    for (int d = 0; d < N; ++d) {
+      int o = 0;
+      for (int e = d * e_local; e < (d + 1) * e_local; ++e) {
+        expert_off[e] = o;
+        o += tot[e];
+      }
+      if (d == me) recv_rows[0] = o;
+    }
+    // tiles of my local experts
+    int nt = 0;
+    for (int le = 0; le < e_local; ++le) {
+      const int e = me * e_local + le;
+      for (int r = 0; r < tot[e]; r += 128) {
+        if (nt < max_tiles) {
+          tiles[1 + nt] = le;
+          tiles[1 + max_tiles + nt] = expert_off[e] + r;
+          tiles[1 + 2 * max_tiles + nt] = min(128, tot[e] - r);
+        }
+        ++nt;
+      }
+    }
+    tiles[0] = min(nt, max_tiles);
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += blockDim.x) {
+    int before = 0;
+    for (int s = 0; s < me; ++s) before += M[s * E + e];
+    const int b = expert_off[e] + before;
+    dest_base[e] = b;
+    if (b + counts[e] > cap_rows) record_device_error(kDevErrBadIndex);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 2. dispatch: one warp per (token, slot) row, grid-stride
+//   recv row meta = {weight bits, source rank, token*k + slot, 0}
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+    ep_dispatch_kernel(const __nv_bfloat16* __restrict__ x, const int32_t* __restrict__ topk_idx,
+                       const float* __restrict__ topk_w, const int32_t* __restrict__ slot_row,
+                       const int32_t* __restrict__ offsets, const int32_t* __restrict__ dest_base,
+                       __nv_bfloat16* const* __restrict__ peer_recv_x, int4* const* __restrict__ peer_recv_meta,
+                       int T, int k, int H, int e_local, int me, int p, int cap_rows) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (blockDim.x / 32);
+  const int vec = H / 8;  // 16-byte vectors per row
+  for (int i = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); i < T * k; i += warps) {
+    const int t = i / k;
+    const int e = topk_idx[i];
+    const int d = e / e_local;
+    const int row = dest_base[e] + (slot_row[i] - offsets[e]);
+    if (row < 0 || row >= cap_rows) {
+      if (lane == 0) record_device_error(kDevErrBadIndex);
+      continue;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(x + size_t(t) * H);
+    uint4* dst = reinterpret_cast<uint4*>(peer_recv_x[d] + (size_t(p) * cap_rows + row) * H);
+    for (int v = lane; v < vec; v += 32) dst[v] = src[v];
+    if (lane == 0)
+      peer_recv_meta[d][size_t(p) * cap_rows + row] = make_int4(__float_as_int(topk_w[i]), me, i, 0);
+  }
+  __threadfence_system();
+}
+
+// ---------------------------------------------------------------------------
+// 3. signal + wait (one warp)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(32)
+    ep_signal_wait_kernel(int* const* __restrict__ peer_ctrl, int* __restrict__ my_ctrl, int N, int E, int me,
+                          int p, int kind, int epoch) {
+  griddep_wait();
+  ep_signal_and_wait(peer_ctrl, my_ctrl, N, E, me, p, kind, epoch);
+}
+
+}  // namespace qmoe

@@ -43,6 +43,7 @@ enum GemmMode : int {
   kModeDown = 0,    // weighted rows reduced into an fp32 accumulator (combine)
   kModeGateUp = 1,  // two accumulators (gate, up) -> bf16 SiLU(gate)*up
   kModePlain = 2,   // one accumulator -> bf16 store (dense projections)
+  kModeDownReturn = 3,  // weighted bf16 rows stored into the source rank's return buffer (EP)
 };
 
 template <int kMode>
@@ -57,8 +58,9 @@ struct GemmCfg {
   static constexpr int kTmemCols = 2 * kAccCols;
   static constexpr int kBarrierBytes = 256;
   // down epilogue: per epilogue warp a [16 rows][33] fp32 transpose buffer
-  // (+ the tile's row destinations and weights, 128 x 8 bytes)
-  static constexpr int kStagingBytes = kMode == kModeDown ? 4 * 16 * 33 * 4 + 128 * 8 : 0;
+  // (+ the tile's row destinations, weights and source ranks, 128 x 12 bytes)
+  static constexpr bool kDownLike = kMode == kModeDown || kMode == kModeDownReturn;
+  static constexpr int kStagingBytes = kDownLike ? 4 * 16 * 33 * 4 + 128 * 12 : 0;
   static constexpr int kSmemBytes =
       1024 /*align slack*/ + kStages * kStageBytes + kBarrierBytes + kStagingBytes;
 };
@@ -86,6 +88,12 @@ struct GemmArgs {
   float* acc;
   int acc_ld;
   int n_acc;
+  // down-return (EP): per row {weight bits, source rank, return row, 0}; the
+  // output row goes to peer_ret[source] + (ret_row0 + return row) * acc_ld
+  const int4* row_meta;
+  __nv_bfloat16* const* peer_ret;
+  int ret_row0;
+  int n_ranks;
 };
 
 // Tile accessors: the device-built tile list, or a dense row range.
@@ -313,6 +321,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int et = threadIdx.x - 64;  // 0..127: epilogue thread index
     int32_t* meta_dst = reinterpret_cast<int32_t*>(staging + 4 * 16 * 33);
     float* meta_w = reinterpret_cast<float*>(meta_dst + 128);
+    int32_t* meta_src = meta_dst + 256;
     int local = 0;
     for (int u = blockIdx.x; u < total_units; u += gridDim.x, ++local) {
       const int tm = u / ksplit;
@@ -324,12 +333,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int buf = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       // down: fetch the tile's row destinations / weights before waiting on the MMA
-      int my_dst = -1;
+      int my_dst = -1, my_src = 0;
       float my_w = 0.f;
       if constexpr (kMode == kModeDown) {
         if (et < nrows) {
           my_dst = args.row_dst[row0 + et];
           my_w = args.row_w[row0 + et];
+        }
+      } else if constexpr (kMode == kModeDownReturn) {
+        if (et < nrows) {
+          const int4 mt4 = args.row_meta[row0 + et];
+          my_w = __int_as_float(mt4.x);
+          my_src = (mt4.y >= 0 && mt4.y < args.n_ranks) ? mt4.y : -1;
+          my_dst = my_src >= 0 ? mt4.z : -1;
         }
       }
       const bool ok =
@@ -341,6 +357,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if constexpr (kMode == kModeDown) {
         meta_dst[et] = (my_dst >= 0 && my_dst < args.n_acc) ? my_dst : -1;
         meta_w[et] = my_w;
+        named_barrier_sync(1, 128);
+      } else if constexpr (kMode == kModeDownReturn) {
+        meta_dst[et] = (my_dst >= 0 && my_dst < args.n_acc) ? my_dst : -1;
+        meta_w[et] = my_w;
+        meta_src[et] = my_src;
         named_barrier_sync(1, 128);
       }
       tc_fence_after();
@@ -390,9 +411,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               const int dst = meta_dst[n];
               if (dst >= 0) {
                 const float wv = meta_w[n];
-                red_add_v4_f32(args.acc + size_t(dst) * args.acc_ld + mt * kBM + quad * 32 + fq,
-                               wv * wsb[i * 33 + fq], wv * wsb[i * 33 + fq + 1],
-                               wv * wsb[i * 33 + fq + 2], wv * wsb[i * 33 + fq + 3]);
+                if constexpr (kMode == kModeDownReturn) {
+                  // weighted row segment straight into the source rank's return buffer
+                  __nv_bfloat16* ret = args.peer_ret[meta_src[n]] +
+                                       (size_t(args.ret_row0) + dst) * args.acc_ld + mt * kBM + quad * 32 + fq;
+                  const __nv_bfloat162 lo = __floats2bfloat162_rn(wv * wsb[i * 33 + fq], wv * wsb[i * 33 + fq + 1]);
+                  const __nv_bfloat162 hi =
+                      __floats2bfloat162_rn(wv * wsb[i * 33 + fq + 2], wv * wsb[i * 33 + fq + 3]);
+                  uint2 pk;
+                  pk.x = *reinterpret_cast<const uint32_t*>(&lo);
+                  pk.y = *reinterpret_cast<const uint32_t*>(&hi);
+                  *reinterpret_cast<uint2*>(ret) = pk;
+                } else {
+                  red_add_v4_f32(args.acc + size_t(dst) * args.acc_ld + mt * kBM + quad * 32 + fq,
+                                 wv * wsb[i * 33 + fq], wv * wsb[i * 33 + fq + 1],
+                                 wv * wsb[i * 33 + fq + 2], wv * wsb[i * 33 + fq + 3]);
+                }
               }
             }
           }
@@ -404,6 +438,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   }
 
+  if constexpr (kMode == kModeDownReturn) __threadfence_system();  // peer stores before the next signal
   __syncthreads();
   if (warp == 1) {
     __syncwarp();

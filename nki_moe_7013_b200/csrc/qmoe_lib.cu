@@ -17,6 +17,7 @@
 #include "blockwise.cuh"
 #include "common.cuh"
 #include "ep.cuh"
+#include "ep_p2p.cuh"
 #include "finalize.cuh"
 #include "grouped_gemm.cuh"
 #include "norm_rope.cuh"
@@ -789,7 +790,7 @@ int qmoe_ep_pack(const int32_t* topk_idx, const float* topk_w, const void* x, in
 
 int qmoe_ep_unpack(const void* y_back, const int32_t* pair_pos, const void* residual, int64_t T,
                    int64_t H, int64_t k, int64_t n_back, void* out, void* stream) {
-  QMOE_REQUIRE(y_back && pair_pos && out, QMOE_ERR_INVALID_ARGUMENT, "ep_unpack: null pointer");
+  QMOE_REQUIRE(y_back && out, QMOE_ERR_INVALID_ARGUMENT, "ep_unpack: null pointer");
   QMOE_REQUIRE(T >= 0 && k >= 1 && k <= 32 && n_back >= 0, QMOE_ERR_INVALID_ARGUMENT, "ep_unpack: bad sizes");
   QMOE_REQUIRE(H > 0 && H % 256 == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "ep_unpack: H %% 256 != 0");
   QMOE_REQUIRE(aligned16(y_back) && aligned16(out) && (!residual || aligned16(residual)),
@@ -802,6 +803,153 @@ int qmoe_ep_unpack(const void* y_back, const int32_t* pair_pos, const void* resi
       static_cast<const __nv_bfloat16*>(y_back), pair_pos, static_cast<const __nv_bfloat16*>(residual),
       int(T), int(H), int(k), int(n_back), static_cast<__nv_bfloat16*>(out));
   return check_launch("ep_unpack_kernel");
+}
+
+// ---------------------------------------------------------------------------
+// CUDA IPC of caller-allocated buffers (the peer-memory EP path)
+// ---------------------------------------------------------------------------
+typedef CUresult (*GetAddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+int qmoe_ipc_export(const void* ptr, void* handle_out, int64_t* offset_out) {
+  QMOE_REQUIRE(ptr && handle_out && offset_out, QMOE_ERR_INVALID_ARGUMENT, "ipc_export: null pointer");
+  static GetAddressRangeFn range_fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      range_fn = reinterpret_cast<GetAddressRangeFn>(p);
+  });
+  QMOE_REQUIRE(range_fn, QMOE_ERR_CUDA, "ipc_export: cuMemGetAddressRange unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  CUresult r = range_fn(&base, &size, reinterpret_cast<CUdeviceptr>(ptr));
+  QMOE_REQUIRE(r == CUDA_SUCCESS, QMOE_ERR_CUDA, "ipc_export: cuMemGetAddressRange failed (%d)", int(r));
+  cudaIpcMemHandle_t h;
+  cudaError_t err = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  QMOE_REQUIRE(err == cudaSuccess, QMOE_ERR_CUDA, "ipc_export: %s", cudaGetErrorString(err));
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  memcpy(handle_out, &h, sizeof(h));
+  *offset_out = int64_t(reinterpret_cast<uintptr_t>(ptr) - uintptr_t(base));
+  return QMOE_OK;
+}
+
+int qmoe_ipc_import(const void* handle, int64_t offset, void** ptr_out, void** base_out) {
+  QMOE_REQUIRE(handle && ptr_out && base_out && offset >= 0, QMOE_ERR_INVALID_ARGUMENT, "ipc_import: bad argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  cudaError_t err = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  QMOE_REQUIRE(err == cudaSuccess, QMOE_ERR_CUDA, "ipc_import: %s", cudaGetErrorString(err));
+  *base_out = base;
+  *ptr_out = static_cast<uint8_t*>(base) + offset;
+  return QMOE_OK;
+}
+
+int qmoe_ipc_close(void* base) {
+  QMOE_REQUIRE(base, QMOE_ERR_INVALID_ARGUMENT, "ipc_close: null pointer");
+  cudaError_t err = cudaIpcCloseMemHandle(base);
+  QMOE_REQUIRE(err == cudaSuccess, QMOE_ERR_CUDA, "ipc_close: %s", cudaGetErrorString(err));
+  return QMOE_OK;
+}
+
+int64_t qmoe_ep_ctrl_words(int64_t n_ranks, int64_t E) {
+  if (n_ranks <= 0 || E <= 0) return 0;
+  return 2 * int64_t(qmoe::ep_ctrl_words_per_parity(int(n_ranks), int(E)));
+}
+
+int qmoe_ep_exchange_counts(const int32_t* counts, int* const* peer_ctrl, int* my_ctrl, int64_t me,
+                            int64_t n_ranks, int64_t E, int64_t e_local, int64_t parity, int64_t epoch,
+                            int32_t* dest_base, int32_t* tiles, int64_t max_tiles, int32_t* recv_rows,
+                            int64_t cap_rows, void* stream) {
+  QMOE_REQUIRE(counts && peer_ctrl && my_ctrl && dest_base && tiles && recv_rows, QMOE_ERR_INVALID_ARGUMENT,
+               "ep_exchange_counts: null pointer");
+  QMOE_REQUIRE(n_ranks >= 1 && n_ranks <= 32 && me >= 0 && me < n_ranks && E >= 1 && E <= 256 &&
+                   e_local >= 1 && e_local * n_ranks == E && (parity == 0 || parity == 1) && epoch > 0 &&
+                   epoch < (int64_t(1) << 31) && max_tiles > 0 && cap_rows > 0 && cap_rows < (int64_t(1) << 31),
+               QMOE_ERR_INVALID_ARGUMENT, "ep_exchange_counts: bad sizes");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  return launch_kernel(qmoe::ep_exchange_counts_kernel, dim3(1), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                       true, "ep_exchange_counts_kernel", counts, peer_ctrl, my_ctrl, int(me), int(n_ranks),
+                       int(E), int(e_local), int(parity), int(epoch), dest_base, tiles, int(max_tiles),
+                       recv_rows, int(cap_rows));
+}
+
+int qmoe_ep_dispatch(const void* x, const int32_t* topk_idx, const float* topk_w, const int32_t* slot_row,
+                     const int32_t* offsets, const int32_t* dest_base, void* const* peer_recv_x,
+                     void* const* peer_recv_meta, int64_t T, int64_t k, int64_t H, int64_t e_local, int64_t me,
+                     int64_t parity, int64_t cap_rows, void* stream) {
+  QMOE_REQUIRE(x && topk_idx && topk_w && slot_row && offsets && dest_base && peer_recv_x && peer_recv_meta,
+               QMOE_ERR_INVALID_ARGUMENT, "ep_dispatch: null pointer");
+  QMOE_REQUIRE(T >= 0 && k >= 1 && k <= 32 && T * k < (int64_t(1) << 31) && H > 0 && H % 8 == 0 &&
+                   e_local >= 1 && (parity == 0 || parity == 1) && cap_rows > 0,
+               QMOE_ERR_INVALID_ARGUMENT, "ep_dispatch: bad sizes");
+  QMOE_REQUIRE(aligned16(x), QMOE_ERR_MISALIGNED, "ep_dispatch: x not 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  if (T == 0) return QMOE_OK;
+  const int grid = int(std::min<int64_t>((T * k + 7) / 8, 4 * int64_t(d->sms)));
+  return launch_kernel(qmoe::ep_dispatch_kernel, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream), true,
+                       "ep_dispatch_kernel", static_cast<const __nv_bfloat16*>(x), topk_idx, topk_w, slot_row,
+                       offsets, dest_base, reinterpret_cast<__nv_bfloat16* const*>(peer_recv_x),
+                       reinterpret_cast<int4* const*>(peer_recv_meta), int(T), int(k), int(H), int(e_local),
+                       int(me), int(parity), int(cap_rows));
+}
+
+int qmoe_ep_signal_wait(int* const* peer_ctrl, int* my_ctrl, int64_t n_ranks, int64_t E, int64_t me,
+                        int64_t parity, int64_t kind, int64_t epoch, void* stream) {
+  QMOE_REQUIRE(peer_ctrl && my_ctrl, QMOE_ERR_INVALID_ARGUMENT, "ep_signal_wait: null pointer");
+  QMOE_REQUIRE(n_ranks >= 1 && n_ranks <= 32 && me >= 0 && me < n_ranks && (parity == 0 || parity == 1) &&
+                   kind >= 0 && kind <= 2 && epoch > 0 && E >= 1,
+               QMOE_ERR_INVALID_ARGUMENT, "ep_signal_wait: bad arguments");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  return launch_kernel(qmoe::ep_signal_wait_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), true,
+                       "ep_signal_wait_kernel", peer_ctrl, my_ctrl, int(n_ranks), int(E), int(me), int(parity),
+                       int(kind), int(epoch));
+}
+
+int qmoe_grouped_gemm_down_return(const void* act, const void* w_down, const int32_t* tiles, int64_t max_tiles,
+                                  const void* row_meta, void* const* peer_ret, int64_t ret_row0,
+                                  int64_t n_ret_rows, int64_t n_ranks, int64_t R, int64_t H, int64_t I,
+                                  int64_t E, void* stream) {
+  QMOE_REQUIRE(act && w_down && tiles && row_meta && peer_ret, QMOE_ERR_INVALID_ARGUMENT,
+               "down_return: null pointer");
+  QMOE_REQUIRE(R >= 0 && R < (int64_t(1) << 31) && H > 0 && H % qmoe::kBM == 0 && I > 0 && I % qmoe::kBK == 0 &&
+                   E > 0 && E * H < (int64_t(1) << 31) && n_ret_rows > 0 && ret_row0 >= 0 && n_ranks >= 1 &&
+                   max_tiles >= 0 && max_tiles < (int64_t(1) << 24),
+               QMOE_ERR_INVALID_ARGUMENT, "down_return: bad sizes");
+  QMOE_REQUIRE(aligned16(act) && aligned16(w_down) && aligned16(row_meta), QMOE_ERR_MISALIGNED,
+               "down_return: pointers must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  if (R == 0) return QMOE_OK;
+  using C = qmoe::GemmCfg<qmoe::kModeDownReturn>;
+  CUtensorMap tmA, tmB;
+  QMOE_CHECK(make_tmap_bf16(&tmA, w_down, uint64_t(I), uint64_t(E * H), qmoe::kBK, qmoe::kBM));
+  QMOE_CHECK(make_tmap_bf16(&tmB, act, uint64_t(I), uint64_t(R), qmoe::kBK, qmoe::kBoxRows));
+  qmoe::GemmArgs a{};
+  a.tiles = tiles;
+  a.max_tiles = int(max_tiles);
+  a.n_mtiles = int(H / qmoe::kBM);
+  a.num_kb = int(I / qmoe::kBK);
+  a.k_splits = 1;
+  a.a_rows_per_expert = int(H);
+  a.acc_ld = int(H);
+  a.n_acc = int(n_ret_rows);
+  a.row_meta = static_cast<const int4*>(row_meta);
+  a.peer_ret = reinterpret_cast<__nv_bfloat16* const*>(peer_ret);
+  a.ret_row0 = int(ret_row0);
+  a.n_ranks = int(n_ranks);
+  const int64_t units = max_tiles * a.n_mtiles;
+  const int grid = int(std::min<int64_t>(units, d->sms));
+  if (grid <= 0) return QMOE_OK;
+  QMOE_CHECK(set_smem(qmoe::grouped_gemm_kernel<qmoe::kModeDownReturn>, C::kSmemBytes));
+  return launch_kernel(qmoe::grouped_gemm_kernel<qmoe::kModeDownReturn>, dim3(grid), dim3(qmoe::kGemmThreads),
+                       C::kSmemBytes, static_cast<cudaStream_t>(stream), true, "grouped_gemm_kernel<down_return>",
+                       tmA, tmB, a);
 }
 
 size_t qmoe_moe_forward_workspace_size(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I) {

@@ -23,6 +23,7 @@ CUDA kernels (``CudaEPKernels``) and NCCL.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Optional
 
 import torch
@@ -120,4 +121,132 @@ class ExpertParallelMoE(nn.Module):
         res = None if residual is None else residual.reshape(-1, H).to(torch.bfloat16).contiguous()
         out = kn.unpack(y_back, pk["pair_pos"], res)
         mark("combine", 1)
+        return out.reshape(shape)
+
+
+class PeerExpertParallelMoE(nn.Module):
+    """Expert-parallel block whose exchange runs through peer memory inside
+    one node (CUDA IPC mappings over NVLink / NVSwitch) with no host sync, so
+    a step is a fixed sequence of stream-ordered kernels (graph-capturable).
+
+    Kernels per step: router, permutation (counts / offsets / slot rows),
+    count exchange, dispatch (rows of x straight into the owners' receive
+    buffers, already grouped by expert), signal/wait, gate/up GEMM on the
+    receive buffer, down GEMM whose epilogue stores the weighted rows into the
+    source ranks' return buffers, signal/wait, unpack.
+
+    Buffers (identical shapes on every rank, two parity halves each):
+    receive rows (P*max_tokens*k, H), their meta, return rows
+    (max_tokens*k, H), and the control block (counts + flags)."""
+
+    def __init__(self, cfg: Qwen3MoeConfig, router_weight: torch.Tensor, local: MoEWeights,
+                 max_tokens: int, group=None):
+        super().__init__()
+        from . import _C
+
+        self._lib = _C.lib()
+        self.cfg = cfg
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        E, H, I, k = cfg.num_experts, cfg.hidden_size, cfg.moe_intermediate_size, cfg.num_experts_per_tok
+        if E % self.world:
+            raise ValueError("num_experts must divide evenly over the ranks")
+        self.E, self.H, self.I, self.k = E, H, I, k
+        self.e_local = E // self.world
+        if local.gate_up.shape[0] != self.e_local:
+            raise ValueError("local expert weights do not match E / world")
+        self.router_weight = router_weight
+        self.local = local
+        self.router_bias: Optional[torch.Tensor] = None
+        self.max_tokens = max_tokens
+        dev = router_weight.device
+        self.device = dev
+        self.cap = self.world * max_tokens * k          # receive rows per parity
+        self.ret_rows = max_tokens * k                  # return rows per parity
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.recv_x = torch.empty((2 * self.cap, H), dtype=torch.bfloat16, device=dev)
+        self.recv_meta = torch.zeros((2 * self.cap, 4), **i32)
+        self.ret = torch.empty((2 * self.ret_rows, H), dtype=torch.bfloat16, device=dev)
+        self.ctrl = torch.zeros(int(self._lib.qmoe_ep_ctrl_words(self.world, E)), **i32)
+        self.dest_base = torch.empty(E, **i32)
+        self.max_tiles = self.e_local + self.cap // 128 + 1
+        self.tiles = torch.zeros(1 + 3 * self.max_tiles, **i32)
+        self.recv_rows = torch.zeros(1, **i32)
+        self.act = torch.empty((self.cap, I), dtype=torch.bfloat16, device=dev)
+        torch.cuda.synchronize(dev)
+        self._imported = []
+        names = ("recv_x", "recv_meta", "ret", "ctrl")
+        mine = {}
+        for n in names:
+            h = ctypes.create_string_buffer(64)
+            off = ctypes.c_int64(0)
+            _C.check(self._lib.qmoe_ipc_export(getattr(self, n).data_ptr(), h, ctypes.byref(off)),
+                     "qmoe_ipc_export")
+            mine[n] = (h.raw, off.value)
+        gathered = [None] * self.world
+        dist.all_gather_object(gathered, mine, group=group)
+        ptrs = {n: [] for n in names}
+        for r in range(self.world):
+            for n in names:
+                if r == self.rank:
+                    ptrs[n].append(getattr(self, n).data_ptr())
+                    continue
+                handle, off = gathered[r][n]
+                p = ctypes.c_void_p()
+                base = ctypes.c_void_p()
+                _C.check(self._lib.qmoe_ipc_import(handle, off, ctypes.byref(p), ctypes.byref(base)),
+                         "qmoe_ipc_import")
+                self._imported.append(base.value)
+                ptrs[n].append(p.value)
+        self.peer = {n: torch.tensor(ptrs[n], dtype=torch.int64, device=dev) for n in names}
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=group)
+        self.epoch = 0
+
+    def close(self):
+        """Unmap the peers' buffers (all ranks should be done with the exchange)."""
+        from . import _C
+
+        torch.cuda.synchronize(self.device)
+        for base in self._imported:
+            _C.check(self._lib.qmoe_ipc_close(base), "qmoe_ipc_close")
+        self._imported = []
+
+    def forward(self, hidden_states: torch.Tensor, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+        from . import _C
+
+        shape = hidden_states.shape
+        H, E, k, I = self.H, self.E, self.k, self.I
+        x = hidden_states.reshape(-1, H).to(torch.bfloat16).contiguous()
+        T = x.shape[0]
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed max_tokens={self.max_tokens} of the EP buffers")
+        lib, pt = self._lib, ops._ptr
+        s = torch.cuda.current_stream(self.device).cuda_stream
+        self.epoch += 1
+        par, ep = self.epoch & 1, self.epoch
+        idx, tw, hist = ops.router_topk(x, self.router_weight, k, bias=self.router_bias, return_hist=True)
+        perm = ops.moe_permute(idx, tw, hist, E)
+        _C.check(lib.qmoe_ep_exchange_counts(
+            pt(perm["counts"]), pt(self.peer["ctrl"]), pt(self.ctrl), self.rank, self.world, E, self.e_local,
+            par, ep, pt(self.dest_base), pt(self.tiles), self.max_tiles, pt(self.recv_rows), self.cap, s),
+            "qmoe_ep_exchange_counts")
+        _C.check(lib.qmoe_ep_dispatch(
+            pt(x), pt(idx), pt(tw), pt(perm["slot_row"]), pt(perm["offsets"]), pt(self.dest_base),
+            pt(self.peer["recv_x"]), pt(self.peer["recv_meta"]), T, k, H, self.e_local, self.rank, par,
+            self.cap, s), "qmoe_ep_dispatch")
+        _C.check(lib.qmoe_ep_signal_wait(pt(self.peer["ctrl"]), pt(self.ctrl), self.world, E, self.rank, par, 1,
+                                         ep, s), "qmoe_ep_signal_wait")
+        recv_x = self.recv_x[par * self.cap:(par + 1) * self.cap]
+        ops.grouped_gemm_gateup_swiglu(recv_x, self.local.gate_up, self.tiles, self.max_tiles, out=self.act)
+        _C.check(lib.qmoe_grouped_gemm_down_return(
+            pt(self.act), pt(self.local.down), pt(self.tiles), self.max_tiles,
+            pt(self.recv_meta[par * self.cap:]), pt(self.peer["ret"]), par * self.ret_rows, self.ret_rows,
+            self.world, self.cap, H, I, self.e_local, s), "qmoe_grouped_gemm_down_return")
+        _C.check(lib.qmoe_ep_signal_wait(pt(self.peer["ctrl"]), pt(self.ctrl), self.world, E, self.rank, par, 2,
+                                         ep, s), "qmoe_ep_signal_wait")
+        y_back = self.ret[par * self.ret_rows:par * self.ret_rows + T * k]
+        res = None if residual is None else residual.reshape(-1, H).to(torch.bfloat16).contiguous()
+        out = ops.ep_unpack(y_back, None, res, T=T, k=k)
         return out.reshape(shape)

@@ -390,11 +390,16 @@ def ep_pack(topk_idx: torch.Tensor, topk_w: torch.Tensor, x: torch.Tensor, e_loc
     return out
 
 
-def ep_unpack(y_back: torch.Tensor, pair_pos: torch.Tensor, residual: Optional[torch.Tensor] = None,
-              n_back: Optional[int] = None) -> torch.Tensor:
+def ep_unpack(y_back: torch.Tensor, pair_pos: Optional[torch.Tensor], residual: Optional[torch.Tensor] = None,
+              n_back: Optional[int] = None, T: Optional[int] = None, k: Optional[int] = None) -> torch.Tensor:
+    """out[t] = residual[t] + sum_j y_back[pair_pos[t, j]] (fp32 sum).  With
+    pair_pos None the rows are t*k + j (pass T and k)."""
     _need(y_back, "y_back", torch.bfloat16, 2)
-    _need(pair_pos, "pair_pos", torch.int32, 2)
-    T, k = pair_pos.shape
+    if pair_pos is not None:
+        _need(pair_pos, "pair_pos", torch.int32, 2)
+        T, k = pair_pos.shape
+    elif T is None or k is None:
+        raise ValueError("T and k are needed without pair_pos")
     H = y_back.shape[1]
     if residual is not None:
         _need(residual, "residual", torch.bfloat16, 2)

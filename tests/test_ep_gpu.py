@@ -1,6 +1,6 @@
 """EP kernels on the GPU (bit-exact pack, unpack, routing histogram) and, when
-the box has 2+ GPUs, the NCCL expert-parallel block against the
-single-process oracle."""
+the box has 2+ GPUs, the NCCL and the peer-memory expert-parallel blocks
+against the single-process oracle."""
 import os
 import socket
 import sys
@@ -81,14 +81,27 @@ def _nccl_worker(rank, world, port, out_dir):
     wd = normal_bf16_device(43, (E, H, I), 0.02, dev)
     el = E // world
     local = MoEWeights(wr, wgu[rank * el:(rank + 1) * el].contiguous(), wd[rank * el:(rank + 1) * el].contiguous())
+    from nki_moe_7013_b200 import _C
+    from nki_moe_7013_b200.ep import PeerExpertParallelMoE
+
     T = 256
     x = normal_bf16_device(100 + rank, (T, H), 1.0, dev)
     moe = ExpertParallelMoE(cfg, wr, local)
     outs = [moe(x) for _ in range(2)]
+    # the peer-memory path: three steps (both parities, then reuse), a
+    # smaller batch on the last one, and a residual
+    peer = PeerExpertParallelMoE(cfg, wr, local, max_tokens=T)
+    res = normal_bf16_device(200 + rank, (T, H), 1.0, dev)
+    outs += [peer(x), peer(x, residual=res), peer(x[: T // 2])]
     torch.cuda.synchronize()
-    ref = oracle.round_to_bf16(oracle.moe_block(x.cpu(), wr.cpu(), wgu.cpu(), wd.cpu(), k))
-    errs = [float(np.abs(o.float().cpu().numpy() - ref).max() / np.abs(ref).max()) for o in outs]
+    assert _C.device_error() == 0
+    moe_ref = oracle.moe_block(x.cpu(), wr.cpu(), wgu.cpu(), wd.cpu(), k)
+    ref = oracle.round_to_bf16(moe_ref)
+    refs = [ref, ref, ref, moe_ref + res.float().cpu().numpy(), ref[: T // 2]]
+    errs = [float(np.abs(o.float().cpu().numpy() - r).max() / np.abs(r).max()) for o, r in zip(outs, refs)]
     np.save(os.path.join(out_dir, f"ep{rank}.npy"), np.array(errs))
+    dist.barrier()
+    peer.close()
     dist.barrier()
     dist.destroy_process_group()
 
