@@ -455,6 +455,7 @@ def run_extras(cfg, weights, dev, hbm_gbs, tf_burst):
 
     res = {}
     dec = {}
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 2x L2
     for B in (1, 8, 32, 64):
         plan = MoEPlan(weights, B, K_TOP)
         x = normal_bf16_device(77 + B, (B, H), 1.0, dev)
@@ -471,19 +472,31 @@ def run_extras(cfg, weights, dev, hbm_gbs, tf_burst):
         for _ in range(5):
             g.replay()
         torch.cuda.synchronize()
-        n = 200
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(n):
+        # The experts one small batch hits can fit in L2 (8 x 9.4 MB at B=1),
+        # so L2 is flushed before every replay and each replay is timed alone.
+        n = 50
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        for i in range(n):
+            flush.zero_()
+            ev[i][0].record()
             g.replay()
-        e1.record()
+            ev[i][1].record()
         torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) * 1e3 / n
+        us = statistics.median(a.elapsed_time(b) for a, b in ev) * 1e3
+        # the same layer without the graph, an event between stages
+        st = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(n)]
+        for i in range(n):
+            flush.zero_()
+            plan.run(x, out, events=st[i])
+        torch.cuda.synchronize()
+        stage = [statistics.median(st[i][j].elapsed_time(st[i][j + 1]) for i in range(n)) * 1e3 for j in range(5)]
         U = int((plan.counts.cpu() > 0).sum().item())
         byts = U * (GATE_UP_BYTES_PER_EXPERT + DOWN_BYTES_PER_EXPERT) + E * H * 2 + 4 * B * H + 8 * B * K_TOP
         dec[str(B)] = {"us_per_layer": round(us, 2), "tokens_per_s": B / (us * 1e-6),
-                       "experts_hit": U, "hbm_frac": byts / (us * 1e-6) / 1e9 / hbm_gbs}
+                       "experts_hit": U, "hbm_frac": byts / (us * 1e-6) / 1e9 / hbm_gbs,
+                       "stage_us_eager": dict(zip(MoEPlan.STAGES, [round(v, 1) for v in stage]))}
         del g
+    del flush
     res["decode_moe_layer_cuda_graph"] = dec
 
     T = 16384

@@ -131,12 +131,21 @@ QMOE_API int qmoe_moe_permute(const int32_t* topk_idx, const float* topk_w, int3
  *   w_gate_up (E, 2I, H)  bf16
  *   tiles                 from qmoe_moe_permute (or qmoe_blockwise_prepare)
  *   act      (R, I)       bf16 out: silu(x W_gate^T) * (x W_up^T), grouped order
+ *   split_ws optional scratch of qmoe_grouped_gemm_gateup_split_workspace_size()
+ *            bytes (or NULL).  With it, decode-sized calls (R <= 128) whose
+ *            tiles all hold <= 16 rows split K over up to 4 CTAs per unit so
+ *            that more SMs stream weights; the splits' fp32 partials are added
+ *            in a fixed order (deterministic).  It must be zero-filled before
+ *            its first use; every completed launch leaves it zero-filled again.
+ *            Calls sharing one split_ws must not overlap on the GPU.
  * Requires H % 64 == 0, I % 128 == 0.
  * ---------------------------------------------------------------------- */
+QMOE_API size_t qmoe_grouped_gemm_gateup_split_workspace_size(void);
 QMOE_API int qmoe_grouped_gemm_gateup_swiglu(const void* x, int64_t x_rows, const int32_t* gather_rows,
                                              const void* w_gate_up, const int32_t* tiles,
                                              int64_t max_tiles, int64_t R, int64_t H, int64_t I,
-                                             int64_t E, void* act, void* stream);
+                                             int64_t E, void* act, void* split_ws, size_t split_ws_bytes,
+                                             void* stream);
 
 /* ------------------------------------------------------------------------
  * K3b  grouped GEMM, down projection with the weighted combine in the

@@ -25,6 +25,14 @@
 // K3b (down) multiplies each column (row r of the tile) by row_w[r] and adds
 // it into the fp32 accumulator row row_dst[r] (the weighted combine) with
 // 16-byte vector reductions.
+//
+// Split K.  With few units (decode batches) a unit's K range can be split
+// over several CTAs so that more SMs stream weights.  Down: the partial sums
+// meet in the fp32 accumulator (the combine is linear).  Gate/up (SiLU is
+// not): each split stores its fp32 gate/up partials in a scratch slot and
+// bumps the unit's arrival counter; the last CTA to arrive adds the S
+// partials in split order (so the result does not depend on which CTA came
+// last), applies SiLU(gate)*up and resets the counter to zero.
 #pragma once
 
 #include "common.cuh"
@@ -37,6 +45,11 @@ constexpr int kBNMax = 128;    // token rows per tile
 constexpr int kBoxRows = 16;   // rows per activation TMA box
 constexpr int kUmmaK = 16;     // k per tcgen05.mma (bf16)
 constexpr int kGemmThreads = 192;
+// gate/up split-K scratch: kSplitSlots partial slots of [2][16 rows][128
+// features] fp32, then kSplitSlots arrival counters
+constexpr int kSplitSlots = 256;
+constexpr int kSplitSlotFloats = 2 * kBoxRows * kBM;
+constexpr size_t kSplitWorkspaceBytes = size_t(kSplitSlots) * kSplitSlotFloats * 4 + kSplitSlots * 4;
 
 // Epilogue modes of the one GEMM kernel.
 enum GemmMode : int {
@@ -72,8 +85,13 @@ struct GemmArgs {
   int dense_rows;
   int n_mtiles;          // feature blocks per tile
   int num_kb;            // K / kBK
-  int k_splits;          // >1: each (tile, feature block) unit is split over K (down mode only;
-                         // the partial sums meet in the fp32 accumulator)
+  int k_splits;          // down: >1 splits each (tile, feature block) unit over K (the
+                         // partial sums meet in the fp32 accumulator)
+  // gate/up: split-K scratch (kSplitWorkspaceBytes; counters zero on entry,
+  // left zero on exit) and the most splits to use; the kernel picks the
+  // count from the tile list (splits only when every tile has <= 16 rows)
+  float* split_ws;
+  int max_k_splits;
   int a_rows_per_expert; // 2I (gate/up) or H (down)
   int up_row_offset;     // I (gate/up only)
   // gate/up: when non-null, B row r of a tile is row gather_rows[r] of the
@@ -109,6 +127,63 @@ struct TileView {
   }
 };
 
+// Gate/up split count for this launch: as many splits (<= max_k_splits) as
+// fit the grid once, only when every tile has at most 16 rows.
+__device__ __forceinline__ int gateup_k_splits(const GemmArgs& a, const TileView& tv, int ntiles) {
+  if (a.split_ws == nullptr || a.max_k_splits < 2 || ntiles <= 0) return 1;
+  const int units = ntiles * a.n_mtiles;
+  int s = min(a.max_k_splits, min(int(gridDim.x), kSplitSlots) / units);
+  s = min(s, a.num_kb);
+  if (s < 2) return 1;
+  for (int t = 0; t < ntiles; ++t)
+    if (tv.nrows(t) > kBoxRows) return 1;
+  return s;
+}
+
+// Gate/up split-K fix-up, run by the 128 epilogue threads of one unit (tm,
+// ks) after loading this split's partials into g / u (feature m, 16 rows).
+// Stores them into slot (tm, ks), counts the arrival, and returns true in
+// the CTA that arrived last, with g / u replaced by the sums over the splits
+// in split order.
+__device__ __forceinline__ bool gateup_split_reduce(const GemmArgs& a, int tm, int ks, int nsplit, int m, int et,
+                                                    float (&g)[16], float (&u)[16], volatile int* last_s) {
+  float* slots = a.split_ws;
+  int* arrivals = reinterpret_cast<int*>(slots + size_t(kSplitSlots) * kSplitSlotFloats);
+  float* mine = slots + size_t(tm * nsplit + ks) * kSplitSlotFloats;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    __stcg(mine + i * kBM + m, g[i]);
+    __stcg(mine + (16 + i) * kBM + m, u[i]);
+  }
+  __threadfence();
+  named_barrier_sync(1, 128);
+  if (et == 0) {
+    const int last = atomicAdd(arrivals + tm, 1) == nsplit - 1;
+    if (last) arrivals[tm] = 0;  // every split has arrived: ready for the next launch
+    *last_s = last;
+  }
+  named_barrier_sync(1, 128);
+  if (!*last_s) return false;
+  __threadfence();
+  float gs[16], us[16];
+  for (int s = 0; s < nsplit; ++s) {
+    const float* p = slots + size_t(tm * nsplit + s) * kSplitSlotFloats;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float gv = s == ks ? g[i] : __ldcg(p + i * kBM + m);
+      const float uv = s == ks ? u[i] : __ldcg(p + (16 + i) * kBM + m);
+      gs[i] = s == 0 ? gv : gs[i] + gv;
+      us[i] = s == 0 ? uv : us[i] + uv;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    g[i] = gs[i];
+    u[i] = us[i];
+  }
+  return true;
+}
+
 template <int kMode>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -116,6 +191,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   using C = GemmCfg<kMode>;
   constexpr bool kGateUp = C::kGateUp;
   extern __shared__ uint8_t gemm_smem_raw[];
+  __shared__ int split_last;
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(gemm_smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
@@ -160,12 +236,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   const int ntiles = args.tiles ? min(args.tiles[0], args.max_tiles)
                                  : (args.dense_rows + kBNMax - 1) / kBNMax;
-  const int ksplit = kMode == kModeDown ? max(1, args.k_splits) : 1;
-  const int kb_per_split = args.num_kb / ksplit;
-  const int total_units = ntiles * args.n_mtiles * ksplit;
   const TileView tv{args.tiles ? args.tiles + 1 : nullptr,
                     args.tiles ? args.tiles + 1 + args.max_tiles : nullptr,
                     args.tiles ? args.tiles + 1 + 2 * args.max_tiles : nullptr, args.dense_rows};
+  int ksplit = 1;
+  if constexpr (kMode == kModeDown) ksplit = max(1, min(args.k_splits, args.num_kb));
+  if constexpr (kGateUp) ksplit = gateup_k_splits(args, tv, ntiles);
+  const int total_units = ntiles * args.n_mtiles * ksplit;
 
   if (warp == 0) {
     // ---------------- TMA producer (warp 0) ----------------
@@ -201,7 +278,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       const uint32_t bytes = C::kATiles * C::kABytes +
                              (gather ? n_g4 * 4 * kBK * 2 : nb * kBoxRows * kBK * 2);
-      for (int kb = ks * kb_per_split; kb < (ks + 1) * kb_per_split; ++kb) {
+      const int kb_end = (ks + 1) * args.num_kb / ksplit;
+      for (int kb = ks * args.num_kb / ksplit; kb < kb_end; ++kb) {
         uint8_t* sb = stages + stage * C::kStageBytes;
         uint8_t* bs = sb + C::kATiles * C::kABytes;
         if (!gather) {
@@ -267,6 +345,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool ok = true;
       for (int u = blockIdx.x; ok && u < total_units; u += gridDim.x, ++local) {
         const int tile = (u / ksplit) / args.n_mtiles;
+        const int ks = u % ksplit;
+        const int n_kb = (ks + 1) * args.num_kb / ksplit - ks * args.num_kb / ksplit;
         const int nb = (tv.nrows(tile) + kBoxRows - 1) / kBoxRows;
         const uint32_t idesc = make_idesc_bf16(kBM, nb * kBoxRows);
         const int buf = local & 1;
@@ -278,7 +358,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_fence_after();
         const uint32_t d_gate = tmem_base + buf * C::kAccCols;
         const uint32_t d_up = d_gate + kBM;
-        for (int kb = 0; kb < kb_per_split; ++kb) {
+        for (int kb = 0; kb < n_kb; ++kb) {
           if (!mbar_wait_bounded(&full[stage], phase, abort_flag, kDevErrWaitTimeoutMma)) {
             ok = false;
             break;
@@ -382,13 +462,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           uint32_t up[16];
           tmem_ld_32x32b_x16(taddr + kBM + c * 16, up);
           tmem_ld_wait();
+          float g[16], uv[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            g[i] = __uint_as_float(v[i]);
+            uv[i] = __uint_as_float(up[i]);
+          }
+          // split K (one 16-row chunk per unit): only the last split finishes
+          if (ksplit > 1 && !gateup_split_reduce(args, tm, u - tm * ksplit, ksplit, m, et, g, uv, &split_last))
+            break;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int n = c * 16 + i;
             if (n < nrows) {
-              const float g = __uint_as_float(v[i]);
-              const float uval = __uint_as_float(up[i]);
-              const float h = g / (1.0f + __expf(-g)) * uval;
+              const float h = g[i] / (1.0f + __expf(-g[i])) * uv[i];
               args.act[size_t(row0 + n) * args.act_ld + feat] = __float2bfloat16_rn(h);
             }
           }

@@ -89,7 +89,8 @@ __global__ void __launch_bounds__(kScatterThreads)
                            const __nv_bfloat16* __restrict__ x, int T, int H, int E, int k,
                            int32_t* __restrict__ row_token, float* __restrict__ row_w,
                            int32_t* __restrict__ slot_row, __nv_bfloat16* __restrict__ x_perm,
-                           float* __restrict__ acc_zero, int32_t* __restrict__ tiles, int max_tiles) {
+                           float* __restrict__ acc_zero, int32_t* __restrict__ tiles, int max_tiles,
+                           int32_t* __restrict__ zero_words, int n_zero_words) {
   __shared__ unsigned mask[256];
   __shared__ int off_s[256];
   __shared__ int pos_s[kScatterThreads];
@@ -132,6 +133,8 @@ __global__ void __launch_bounds__(kScatterThreads)
       tiles[0] = min(tot_tiles, max_tiles);
     }
   }
+  if (c == 0 && part == 0)
+    for (int i = tid; i < n_zero_words; i += kScatterThreads) zero_words[i] = 0;
   for (int i = tid; i < E; i += kScatterThreads) mask[i] = 0u;
   __syncthreads();
   int e = -1;

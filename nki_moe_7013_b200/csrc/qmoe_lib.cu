@@ -186,6 +186,11 @@ constexpr int64_t kRouterSmallMaxT = 64;
 // more than it saves; for prefill, 16-row boxes of the copy feed the tensor
 // core faster than 4-row gathers.
 constexpr int64_t kGatherMaxT = 64;
+// Routed rows up to which the gate/up GEMM may split K (given a scratch), and
+// the most splits.  Splits pay when the units leave SMs idle: at one token
+// (8 rows) 48 units of a 148-SM B200 become 144.
+constexpr int64_t kGateUpSplitMaxR = 128;
+constexpr int kGateUpMaxSplits = 4;
 
 int launch_router(const void* x, const void* w, const float* bias, int64_t T, int64_t H, int64_t E,
                   int64_t k, int normalize, float* logits, int32_t* topk_idx, float* topk_w,
@@ -259,7 +264,8 @@ int check_router_args(const void* x, const void* w, int64_t T, int64_t H, int64_
 int launch_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chunk_hist, const void* x,
                    int64_t T, int64_t H, int64_t E, int64_t k, int32_t* counts, int32_t* offsets,
                    int32_t* row_token, float* row_w, int32_t* slot_row, int32_t* tiles,
-                   void* x_perm, float* acc_zero, cudaStream_t stream) {
+                   void* x_perm, float* acc_zero, cudaStream_t stream, int32_t* zero_words = nullptr,
+                   int n_zero_words = 0) {
   const int nchunks = int((T + qmoe::kRouterChunk - 1) / qmoe::kRouterChunk);
   const int64_t max_tiles = qmoe_max_tiles(T * k, E);
   QMOE_CHECK(launch_kernel(qmoe::permute_scan_kernel, dim3(unsigned(E)), dim3(qmoe::kScanThreads), 0, stream,
@@ -272,7 +278,7 @@ int launch_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chunk_
                              static_cast<const int32_t*>(chunk_hist), static_cast<const int32_t*>(counts),
                              offsets, static_cast<const __nv_bfloat16*>(x), int(T), int(H), int(E), int(k),
                              row_token, row_w, slot_row, static_cast<__nv_bfloat16*>(x_perm), acc_zero,
-                             tiles, int(max_tiles)));
+                             tiles, int(max_tiles), zero_words, n_zero_words));
   }
   return QMOE_OK;
 }
@@ -281,7 +287,7 @@ int launch_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chunk_
 // activations (x_rows rows) gathered by gather_rows[r] with TMA gather4.
 int launch_gemm_gateup(const void* x, int64_t x_rows, const int32_t* gather_rows, const void* w_gate_up,
                        const int32_t* tiles, int64_t max_tiles, int64_t R, int64_t H, int64_t I, int64_t E,
-                       void* act, cudaStream_t stream) {
+                       void* act, void* split_ws, cudaStream_t stream) {
   using C = qmoe::GemmCfg<qmoe::kModeGateUp>;
   CUtensorMap tmA, tmB;
   QMOE_CHECK(make_tmap_bf16(&tmA, w_gate_up, uint64_t(H), uint64_t(E * 2 * I), qmoe::kBK, qmoe::kBM));
@@ -300,7 +306,10 @@ int launch_gemm_gateup(const void* x, int64_t x_rows, const int32_t* gather_rows
   a.gather_rows = gather_rows;
   a.act = static_cast<__nv_bfloat16*>(act);
   a.act_ld = int(I);
-  const int64_t units = max_tiles * a.n_mtiles;
+  // decode sizes: let the kernel split K when its units leave SMs idle
+  a.split_ws = R <= kGateUpSplitMaxR ? static_cast<float*>(split_ws) : nullptr;
+  a.max_k_splits = a.split_ws ? kGateUpMaxSplits : 1;
+  const int64_t units = max_tiles * a.n_mtiles * a.max_k_splits;
   const int grid = int(std::min<int64_t>(units, num_sms(0)));
   if (grid <= 0) return QMOE_OK;
   QMOE_CHECK(set_smem(qmoe::grouped_gemm_kernel<qmoe::kModeGateUp>, C::kSmemBytes));
@@ -382,7 +391,7 @@ int launch_finalize(const float* acc, const void* residual, int64_t T, int64_t H
 // Workspace carving for the fused forward.
 struct FwdLayout {
   size_t logits, chunk_hist, counts, offsets, row_token, row_w, slot_row, tiles, topk_idx, topk_w, x_perm,
-      act, acc, total;
+      act, acc, split, total;
 };
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -410,6 +419,7 @@ FwdLayout fwd_layout(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I) {
   L.x_perm = take(T > kGatherMaxT ? 2 * size_t(R * H) : 0);
   L.act = take(2 * size_t(R * I));
   L.acc = take(sizeof(float) * size_t(T * H));
+  L.split = take(T * k <= kGateUpSplitMaxR ? qmoe::kSplitWorkspaceBytes : 0);
   L.total = o;
   return L;
 }
@@ -494,9 +504,12 @@ int qmoe_moe_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chun
                         row_w, slot_row, tiles, x_perm, acc_zero, static_cast<cudaStream_t>(stream));
 }
 
+size_t qmoe_grouped_gemm_gateup_split_workspace_size(void) { return qmoe::kSplitWorkspaceBytes; }
+
 int qmoe_grouped_gemm_gateup_swiglu(const void* x, int64_t x_rows, const int32_t* gather_rows,
                                     const void* w_gate_up, const int32_t* tiles, int64_t max_tiles,
-                                    int64_t R, int64_t H, int64_t I, int64_t E, void* act, void* stream) {
+                                    int64_t R, int64_t H, int64_t I, int64_t E, void* act, void* split_ws,
+                                    size_t split_ws_bytes, void* stream) {
   QMOE_REQUIRE(x && w_gate_up && tiles && act, QMOE_ERR_INVALID_ARGUMENT, "gate_up: null pointer");
   QMOE_REQUIRE(R >= 0 && R < (int64_t(1) << 31), QMOE_ERR_INVALID_ARGUMENT, "gate_up: bad R");
   QMOE_REQUIRE(!gather_rows || (x_rows > 0 && x_rows < (int64_t(1) << 31)), QMOE_ERR_INVALID_ARGUMENT,
@@ -507,10 +520,13 @@ int qmoe_grouped_gemm_gateup_swiglu(const void* x, int64_t x_rows, const int32_t
   QMOE_REQUIRE(max_tiles >= 0 && max_tiles < (int64_t(1) << 24), QMOE_ERR_INVALID_ARGUMENT, "gate_up: bad max_tiles");
   QMOE_REQUIRE(aligned16(x) && aligned16(w_gate_up) && aligned16(act), QMOE_ERR_MISALIGNED,
                "gate_up: pointers must be 16-byte aligned");
+  QMOE_REQUIRE(!split_ws || split_ws_bytes >= qmoe::kSplitWorkspaceBytes, QMOE_ERR_WORKSPACE_TOO_SMALL,
+               "gate_up: split workspace %zu < required %zu bytes", split_ws_bytes, qmoe::kSplitWorkspaceBytes);
+  QMOE_REQUIRE(!split_ws || aligned16(split_ws), QMOE_ERR_MISALIGNED, "gate_up: split workspace not 16-byte aligned");
   DeviceInfo* d = nullptr;
   QMOE_CHECK(device_info(&d));
   if (R == 0) return QMOE_OK;
-  return launch_gemm_gateup(x, x_rows, gather_rows, w_gate_up, tiles, max_tiles, R, H, I, E, act,
+  return launch_gemm_gateup(x, x_rows, gather_rows, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws,
                             static_cast<cudaStream_t>(stream));
 }
 
@@ -999,18 +1015,24 @@ int qmoe_moe_forward(const void* x, const void* w_router, const float* router_bi
   void* x_perm = T > kGatherMaxT ? ws + L.x_perm : nullptr;
   void* act = ws + L.act;
   float* acc = reinterpret_cast<float*>(ws + L.acc);
+  float* split_ws = T * k <= kGateUpSplitMaxR ? reinterpret_cast<float*>(ws + L.split) : nullptr;
+  int32_t* split_counters = split_ws ? reinterpret_cast<int32_t*>(split_ws + size_t(qmoe::kSplitSlots) *
+                                                                               qmoe::kSplitSlotFloats)
+                                     : nullptr;
   const int64_t R = T * k;
   const int64_t max_tiles = qmoe_max_tiles(R, E);
 
   float* logits = T <= kRouterSmallMaxT ? reinterpret_cast<float*>(ws + L.logits) : nullptr;
   QMOE_CHECK(launch_router(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw,
                            chunk_hist, s));
+  // the permutation also zeroes the gate/up split counters (the workspace
+  // may hold anything on entry)
   QMOE_CHECK(launch_permute(idx, tw, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w,
-                            slot_row, tiles, x_perm, acc, s));
+                            slot_row, tiles, x_perm, acc, s, split_counters, split_counters ? qmoe::kSplitSlots : 0));
   if (x_perm)
-    QMOE_CHECK(launch_gemm_gateup(x_perm, R, nullptr, w_gate_up, tiles, max_tiles, R, H, I, E, act, s));
+    QMOE_CHECK(launch_gemm_gateup(x_perm, R, nullptr, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s));
   else
-    QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, s));
+    QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s));
   QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s));
   return launch_finalize(acc, residual, T, H, out, s);
 }
@@ -1117,17 +1139,23 @@ extern "C" int qmoe_moe_forward_noalloc(const void* x, const void* w_router,
   void* x_perm = T > kGatherMaxT ? ws + L.x_perm : nullptr;
   void* act = ws + L.act;
   float* acc = reinterpret_cast<float*>(ws + L.acc);
+  float* split_ws = T * k <= kGateUpSplitMaxR ? reinterpret_cast<float*>(ws + L.split) : nullptr;
+  int32_t* split_counters = split_ws ? reinterpret_cast<int32_t*>(split_ws + size_t(qmoe::kSplitSlots) *
+                                                                               qmoe::kSplitSlotFloats)
+                                     : nullptr;
   const int64_t R = T * k;
   const int64_t max_tiles = qmoe_max_tiles(R, E);
   float* logits = T <= kRouterSmallMaxT ? reinterpret_cast<float*>(ws + L.logits) : nullptr;
   QMOE_CHECK(launch_router(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw,
                            chunk_hist, s));
+  // the permutation also zeroes the gate/up split counters (the workspace
+  // may hold anything on entry)
   QMOE_CHECK(launch_permute(idx, tw, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w,
-                            slot_row, tiles, x_perm, acc, s));
+                            slot_row, tiles, x_perm, acc, s, split_counters, split_counters ? qmoe::kSplitSlots : 0));
   if (x_perm)
-    QMOE_CHECK(launch_gemm_gateup(x_perm, R, nullptr, w_gate_up, tiles, max_tiles, R, H, I, E, act, s));
+    QMOE_CHECK(launch_gemm_gateup(x_perm, R, nullptr, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s));
   else
-    QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, s));
+    QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s));
   QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s));
   return launch_finalize(acc, residual, T, H, out, s);
 }

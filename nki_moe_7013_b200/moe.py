@@ -179,7 +179,9 @@ def _run_routed(x: torch.Tensor, w: MoEWeights, idx: torch.Tensor, tw: torch.Ten
         act = ops.grouped_gemm_gateup_swiglu(p["x_perm"], w.gate_up, p["tiles"], p["max_tiles"])
     else:
         p = ops.moe_permute(idx, tw, hist, E, x=x, gather=False, acc_zero=acc)
-        act = ops.grouped_gemm_gateup_swiglu(x, w.gate_up, p["tiles"], p["max_tiles"], gather_rows=p["row_token"])
+        split = ops.gateup_split_workspace(x.device) if T * k <= ops.GATEUP_SPLIT_MAX_R else None
+        act = ops.grouped_gemm_gateup_swiglu(x, w.gate_up, p["tiles"], p["max_tiles"], gather_rows=p["row_token"],
+                                             split_ws=split)
     ops.grouped_gemm_down_combine(act, w.down, p["tiles"], p["max_tiles"], p["row_token"], p["row_w"], acc)
     return ops.combine_finalize(acc, residual)
 
@@ -241,6 +243,9 @@ class MoEPlan:
                        if T > ops.GATHER_MAX_T else None)
         # small batches route through the logits + selection kernels
         self.logits = torch.empty((T, E), **f32) if T <= ops.ROUTER_SMALL_MAX_T else None
+        # decode sizes: the gate/up GEMM may split K (zero-filled scratch)
+        self.split_ws = ops.gateup_split_workspace(dev) if R <= ops.GATEUP_SPLIT_MAX_R else None
+        self._split_bytes = 0 if self.split_ws is None else self.split_ws.numel()
         self._lib = _C.lib()
 
     def run(self, x: torch.Tensor, out: torch.Tensor, residual: Optional[torch.Tensor] = None,
@@ -266,11 +271,12 @@ class MoEPlan:
         mark(2)
         if self.x_perm is not None:
             _C.check(lib.qmoe_grouped_gemm_gateup_swiglu(p(self.x_perm), R, None, p(w.gate_up), p(self.tiles),
-                                                         self.max_tiles, R, H, I, E, p(self.act), s), "gate_up")
+                                                         self.max_tiles, R, H, I, E, p(self.act),
+                                                         p(self.split_ws), self._split_bytes, s), "gate_up")
         else:
             _C.check(lib.qmoe_grouped_gemm_gateup_swiglu(p(x), T, p(self.row_token), p(w.gate_up),
                                                          p(self.tiles), self.max_tiles, R, H, I, E, p(self.act),
-                                                         s), "gate_up")
+                                                         p(self.split_ws), self._split_bytes, s), "gate_up")
         mark(3)
         _C.check(lib.qmoe_grouped_gemm_down_combine(p(self.act), p(w.down), p(self.tiles), self.max_tiles,
                                                     p(self.row_token), p(self.row_w), R, H, I, E,

@@ -16,6 +16,7 @@ from . import _C
 ROUTER_CHUNK = 8  # QMOE_ROUTER_CHUNK
 ROUTER_SMALL_MAX_T = 64  # batches up to this size take the two-kernel small-batch router
 GATHER_MAX_T = 64  # batches up to this size gather token rows inside the gate/up GEMM
+GATEUP_SPLIT_MAX_R = 128  # routed rows up to which the gate/up GEMM may split K
 
 
 def _ptr(t: Optional[torch.Tensor]):
@@ -111,12 +112,22 @@ def moe_permute(topk_idx: torch.Tensor, topk_w: torch.Tensor, chunk_hist: torch.
                 slot_row=slot_row, tiles=tiles, max_tiles=mt, x_perm=x_perm)
 
 
+def gateup_split_workspace(device) -> torch.Tensor:
+    """Zero-filled scratch that lets decode-sized gate/up calls split K over
+    several CTAs (``split_ws`` of grouped_gemm_gateup_swiglu); every launch
+    leaves it zero-filled.  Calls that share one must not overlap on the GPU."""
+    n = int(_C.lib().qmoe_grouped_gemm_gateup_split_workspace_size())
+    return torch.zeros(n, dtype=torch.uint8, device=device)
+
+
 def grouped_gemm_gateup_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, tiles: torch.Tensor,
                                max_tiles_: int, out: Optional[torch.Tensor] = None,
-                               gather_rows: Optional[torch.Tensor] = None) -> torch.Tensor:
+                               gather_rows: Optional[torch.Tensor] = None,
+                               split_ws: Optional[torch.Tensor] = None) -> torch.Tensor:
     """K3a.  act (R, I) bf16 = SiLU(x W_gate^T) * (x W_up^T) in grouped order.
     ``x`` is x_perm (R, H), or with ``gather_rows`` (R,) int32 the source
-    activations whose row gather_rows[r] is grouped row r."""
+    activations whose row gather_rows[r] is grouped row r.  ``split_ws``
+    (from gateup_split_workspace) lets R <= 128 calls split K."""
     _need(x, "x", torch.bfloat16, 2)
     _need(w_gate_up, "w_gate_up", torch.bfloat16, 3)
     _need(tiles, "tiles", torch.int32, 1)
@@ -134,7 +145,8 @@ def grouped_gemm_gateup_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, tiles: 
     with torch.cuda.device(dev):
         _C.check(_C.lib().qmoe_grouped_gemm_gateup_swiglu(
             _ptr(x), rows, _ptr(gather_rows), _ptr(w_gate_up), _ptr(tiles), max_tiles_, R, H, I, E,
-            _ptr(act), _stream(dev)), "qmoe_grouped_gemm_gateup_swiglu")
+            _ptr(act), _ptr(split_ws), 0 if split_ws is None else split_ws.numel() * split_ws.element_size(),
+            _stream(dev)), "qmoe_grouped_gemm_gateup_swiglu")
     return act
 
 
