@@ -412,7 +412,7 @@ def run_ours(args):
                 "d2h_bytes_per_step": T * H * 2,
                 "api": "Qwen3MoeSparseMoeBlock.forward(hidden_states)[0], pinned host in/out, "
                        "uploads and downloads on their own streams overlapping compute"},
-        "gpu_launches": MoEPlan.LAUNCHES_PER_RUN * args.steps,
+        "gpu_launches": plan.launches_per_run * args.steps,
         "stage_us": dict(zip(MoEPlan.STAGES, [round(s * 1e3, 2) for s in stage_ms])),
         "stage_note": "per-kernel CUDA-event times from a second pass of the K steps with an event "
                       "between every kernel; value uses events at the ends of the timed region only",

@@ -111,6 +111,20 @@ QMOE_API int qmoe_router_topk(const void* x, const void* w_router, const float* 
  * Rows of one expert are ordered by ascending token id.  Bit-exact.
  * ---------------------------------------------------------------------- */
 QMOE_API int64_t qmoe_max_tiles(int64_t rows, int64_t E);
+
+/* ------------------------------------------------------------------------
+ * K1 + K2 for decode batches (T <= 16, E <= 128) in one launch (a cluster
+ * of 8 CTAs):
+ * the outputs of qmoe_router_topk (logits, topk_idx, topk_w) and of
+ * qmoe_moe_permute (counts, offsets, row_token, row_w, slot_row, tiles,
+ * acc_zero) with identical values; no chunk histogram, no x_perm (decode
+ * sizes gather rows inside the gate/up GEMM).  logits (T, E) fp32 is
+ * required (scratch).  Replaces the same reference stages as those two.
+ * ---------------------------------------------------------------------- */
+QMOE_API int qmoe_route_small(const void* x, const void* w_router, const float* bias, int64_t T, int64_t H,
+                              int64_t E, int64_t k, int normalize, float* logits, int32_t* topk_idx,
+                              float* topk_w, int32_t* counts, int32_t* offsets, int32_t* row_token,
+                              float* row_w, int32_t* slot_row, int32_t* tiles, float* acc_zero, void* stream);
 QMOE_API int qmoe_moe_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chunk_hist,
                      const void* x, int64_t T, int64_t H, int64_t E, int64_t k,
                      int32_t* counts, int32_t* offsets, int32_t* row_token, float* row_w,

@@ -22,6 +22,7 @@
 #include "grouped_gemm.cuh"
 #include "norm_rope.cuh"
 #include "permute.cuh"
+#include "route_small.cuh"
 #include "router.cuh"
 
 // ---------------------------------------------------------------------------
@@ -244,6 +245,59 @@ int launch_router(const void* x, const void* w, const float* bias, int64_t T, in
   }
 #undef QMOE_ROUTER_CASE
   return check_launch("router_topk_kernel");
+}
+
+size_t route_small_smem(int64_t T, int64_t H, int64_t E, int64_t k) {
+  const size_t rows = 2 * size_t((T + 3) & ~int64_t(3)) * size_t(H);
+  const size_t sel = 4 * size_t(T * E) + 8 * size_t(T * k);
+  return std::max(rows, sel);
+}
+
+// Router + permutation for T <= kRouteSmallMaxT: one cluster of
+// kRouteSmallCtas CTAs (route_small_kernel).
+int launch_route_small(const void* x, const void* w, const float* bias, int64_t T, int64_t H, int64_t E,
+                       int64_t k, int normalize, float* logits, int32_t* topk_idx, float* topk_w,
+                       int32_t* counts, int32_t* offsets, int32_t* row_token, float* row_w, int32_t* slot_row,
+                       int32_t* tiles, int64_t max_tiles, float* acc_zero, cudaStream_t stream,
+                       int32_t* zero_words = nullptr, int n_zero_words = 0) {
+  const int G = int(H / 256);
+  const int smem = int(route_small_smem(T, H, E, k));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(qmoe::kRouteSmallCtas);
+  cfg.blockDim = dim3(unsigned(E / qmoe::kRouteSmallCtas * 32));
+  cfg.dynamicSmemBytes = size_t(smem);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = qmoe::kRouteSmallCtas;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  const auto* wb = static_cast<const __nv_bfloat16*>(w);
+  cudaError_t err = cudaSuccess;
+#define QMOE_ROUTE_SMALL_CASE(GG)                                                                        \
+  case GG:                                                                                               \
+    QMOE_CHECK(set_smem(qmoe::route_small_kernel<GG>, smem));                                            \
+    err = cudaLaunchKernelEx(&cfg, qmoe::route_small_kernel<GG>, xb, wb, bias, int(T), int(E), int(k),   \
+                             normalize, logits, topk_idx, topk_w, counts, offsets, row_token, row_w,     \
+                             slot_row, tiles, int(max_tiles), acc_zero, zero_words, n_zero_words);       \
+    break;
+  switch (G) {
+    QMOE_ROUTE_SMALL_CASE(1)
+    QMOE_ROUTE_SMALL_CASE(2)
+    QMOE_ROUTE_SMALL_CASE(4)
+    QMOE_ROUTE_SMALL_CASE(8)
+    QMOE_ROUTE_SMALL_CASE(16)
+    default:
+      return set_error(QMOE_ERR_UNSUPPORTED_SHAPE, "route_small: H/256 = %d not in {1,2,4,8,16}", G);
+  }
+#undef QMOE_ROUTE_SMALL_CASE
+  if (err != cudaSuccess) return set_error(QMOE_ERR_CUDA, "route_small_kernel: %s", cudaGetErrorString(err));
+  return check_launch("route_small_kernel");
 }
 
 int check_router_args(const void* x, const void* w, int64_t T, int64_t H, int64_t E, int64_t k,
@@ -502,6 +556,26 @@ int qmoe_moe_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chun
   QMOE_CHECK(device_info(&d));
   return launch_permute(topk_idx, topk_w, chunk_hist, x, T, H, E, k, counts, offsets, row_token,
                         row_w, slot_row, tiles, x_perm, acc_zero, static_cast<cudaStream_t>(stream));
+}
+
+int qmoe_route_small(const void* x, const void* w_router, const float* bias, int64_t T, int64_t H, int64_t E,
+                     int64_t k, int normalize, float* logits, int32_t* topk_idx, float* topk_w, int32_t* counts,
+                     int32_t* offsets, int32_t* row_token, float* row_w, int32_t* slot_row, int32_t* tiles,
+                     float* acc_zero, void* stream) {
+  QMOE_CHECK(check_router_args(x, w_router, T, H, E, k, topk_idx, topk_w));
+  QMOE_REQUIRE(logits && counts && offsets && row_token && row_w && slot_row && tiles, QMOE_ERR_INVALID_ARGUMENT,
+               "route_small: null pointer");
+  QMOE_REQUIRE(T <= qmoe::kRouteSmallMaxT, QMOE_ERR_UNSUPPORTED_SHAPE, "route_small: T=%lld > %d", (long long)T,
+               qmoe::kRouteSmallMaxT);
+  QMOE_REQUIRE(E <= qmoe::kRouteSmallMaxE, QMOE_ERR_UNSUPPORTED_SHAPE, "route_small: E=%lld > %d", (long long)E,
+               qmoe::kRouteSmallMaxE);
+  QMOE_REQUIRE(!acc_zero || aligned16(acc_zero), QMOE_ERR_MISALIGNED, "route_small: acc not 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  if (T == 0) return QMOE_OK;
+  return launch_route_small(x, w_router, bias, T, H, E, k, normalize, logits, topk_idx, topk_w, counts, offsets,
+                            row_token, row_w, slot_row, tiles, qmoe_max_tiles(T * k, E), acc_zero,
+                            static_cast<cudaStream_t>(stream));
 }
 
 size_t qmoe_grouped_gemm_gateup_split_workspace_size(void) { return qmoe::kSplitWorkspaceBytes; }
@@ -1023,12 +1097,21 @@ int qmoe_moe_forward(const void* x, const void* w_router, const float* router_bi
   const int64_t max_tiles = qmoe_max_tiles(R, E);
 
   float* logits = T <= kRouterSmallMaxT ? reinterpret_cast<float*>(ws + L.logits) : nullptr;
-  QMOE_CHECK(launch_router(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw,
-                           chunk_hist, s));
-  // the permutation also zeroes the gate/up split counters (the workspace
-  // may hold anything on entry)
-  QMOE_CHECK(launch_permute(idx, tw, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w,
-                            slot_row, tiles, x_perm, acc, s, split_counters, split_counters ? qmoe::kSplitSlots : 0));
+  if (T <= qmoe::kRouteSmallMaxT && E <= qmoe::kRouteSmallMaxE) {
+    // decode sizes: router + permutation in one launch, which also zeroes
+    // the gate/up split counters (the workspace may hold anything on entry)
+    QMOE_CHECK(launch_route_small(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw, counts,
+                                  offsets, row_token, row_w, slot_row, tiles, max_tiles, acc, s, split_counters,
+                                  split_counters ? qmoe::kSplitSlots : 0));
+  } else {
+    QMOE_CHECK(launch_router(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw,
+                             chunk_hist, s));
+    // the permutation also zeroes the gate/up split counters (the workspace
+    // may hold anything on entry)
+    QMOE_CHECK(launch_permute(idx, tw, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w,
+                              slot_row, tiles, x_perm, acc, s, split_counters,
+                              split_counters ? qmoe::kSplitSlots : 0));
+  }
   if (x_perm)
     QMOE_CHECK(launch_gemm_gateup(x_perm, R, nullptr, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s));
   else
@@ -1146,12 +1229,21 @@ extern "C" int qmoe_moe_forward_noalloc(const void* x, const void* w_router,
   const int64_t R = T * k;
   const int64_t max_tiles = qmoe_max_tiles(R, E);
   float* logits = T <= kRouterSmallMaxT ? reinterpret_cast<float*>(ws + L.logits) : nullptr;
-  QMOE_CHECK(launch_router(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw,
-                           chunk_hist, s));
-  // the permutation also zeroes the gate/up split counters (the workspace
-  // may hold anything on entry)
-  QMOE_CHECK(launch_permute(idx, tw, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w,
-                            slot_row, tiles, x_perm, acc, s, split_counters, split_counters ? qmoe::kSplitSlots : 0));
+  if (T <= qmoe::kRouteSmallMaxT && E <= qmoe::kRouteSmallMaxE) {
+    // decode sizes: router + permutation in one launch, which also zeroes
+    // the gate/up split counters (the workspace may hold anything on entry)
+    QMOE_CHECK(launch_route_small(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw, counts,
+                                  offsets, row_token, row_w, slot_row, tiles, max_tiles, acc, s, split_counters,
+                                  split_counters ? qmoe::kSplitSlots : 0));
+  } else {
+    QMOE_CHECK(launch_router(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw,
+                             chunk_hist, s));
+    // the permutation also zeroes the gate/up split counters (the workspace
+    // may hold anything on entry)
+    QMOE_CHECK(launch_permute(idx, tw, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w,
+                              slot_row, tiles, x_perm, acc, s, split_counters,
+                              split_counters ? qmoe::kSplitSlots : 0));
+  }
   if (x_perm)
     QMOE_CHECK(launch_gemm_gateup(x_perm, R, nullptr, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s));
   else

@@ -243,6 +243,8 @@ class MoEPlan:
                        if T > ops.GATHER_MAX_T else None)
         # small batches route through the logits + selection kernels
         self.logits = torch.empty((T, E), **f32) if T <= ops.ROUTER_SMALL_MAX_T else None
+        # decode sizes: router + permutation in one launch
+        self.route_small = T <= ops.ROUTE_SMALL_MAX_T and E <= ops.ROUTE_SMALL_MAX_E
         # decode sizes: the gate/up GEMM may split K (zero-filled scratch)
         self.split_ws = ops.gateup_split_workspace(dev) if R <= ops.GATEUP_SPLIT_MAX_R else None
         self._split_bytes = 0 if self.split_ws is None else self.split_ws.numel()
@@ -260,14 +262,21 @@ class MoEPlan:
                 events[i].record()
 
         mark(0)
-        _C.check(lib.qmoe_router_topk(p(x), p(w.router), p(self.bias), T, H, E, k,
-                                      1 if self.normalize else 0, p(self.logits), p(self.topk_idx),
-                                      p(self.topk_w), p(self.hist), s), "router")
-        mark(1)
-        _C.check(lib.qmoe_moe_permute(p(self.topk_idx), p(self.topk_w), p(self.hist), p(x), T, H, E, k,
-                                      p(self.counts), p(self.offsets), p(self.row_token), p(self.row_w),
-                                      p(self.slot_row), p(self.tiles), p(self.x_perm), p(self.acc), s),
-                 "permute")
+        if self.route_small:
+            _C.check(lib.qmoe_route_small(p(x), p(w.router), p(self.bias), T, H, E, k, 1 if self.normalize else 0,
+                                          p(self.logits), p(self.topk_idx), p(self.topk_w), p(self.counts),
+                                          p(self.offsets), p(self.row_token), p(self.row_w), p(self.slot_row),
+                                          p(self.tiles), p(self.acc), s), "route_small")
+            mark(1)
+        else:
+            _C.check(lib.qmoe_router_topk(p(x), p(w.router), p(self.bias), T, H, E, k,
+                                          1 if self.normalize else 0, p(self.logits), p(self.topk_idx),
+                                          p(self.topk_w), p(self.hist), s), "router")
+            mark(1)
+            _C.check(lib.qmoe_moe_permute(p(self.topk_idx), p(self.topk_w), p(self.hist), p(x), T, H, E, k,
+                                          p(self.counts), p(self.offsets), p(self.row_token), p(self.row_w),
+                                          p(self.slot_row), p(self.tiles), p(self.x_perm), p(self.acc), s),
+                     "permute")
         mark(2)
         if self.x_perm is not None:
             _C.check(lib.qmoe_grouped_gemm_gateup_swiglu(p(self.x_perm), R, None, p(w.gate_up), p(self.tiles),
@@ -286,4 +295,13 @@ class MoEPlan:
         mark(5)
         return out
 
-    LAUNCHES_PER_RUN = 6  # router, scan, scatter, gate/up, down, finalize
+    LAUNCHES_PER_RUN = 6  # router, scan, scatter, gate/up, down, finalize (T > 64)
+
+    @property
+    def launches_per_run(self) -> int:
+        """Kernels one run launches: route_small (1) or router (2 when
+        T <= 64: logits + selection) + scan + scatter, then gate/up, down,
+        finalize."""
+        if self.route_small:
+            return 4
+        return (7 if self.T <= ops.ROUTER_SMALL_MAX_T else 6)

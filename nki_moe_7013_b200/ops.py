@@ -17,6 +17,8 @@ ROUTER_CHUNK = 8  # QMOE_ROUTER_CHUNK
 ROUTER_SMALL_MAX_T = 64  # batches up to this size take the two-kernel small-batch router
 GATHER_MAX_T = 64  # batches up to this size gather token rows inside the gate/up GEMM
 GATEUP_SPLIT_MAX_R = 128  # routed rows up to which the gate/up GEMM may split K
+ROUTE_SMALL_MAX_T = 16  # batches up to this size (E <= 128) route + permute in one launch
+ROUTE_SMALL_MAX_E = 128
 
 
 def _ptr(t: Optional[torch.Tensor]):
@@ -73,6 +75,37 @@ def router_topk(x: torch.Tensor, w_router: torch.Tensor, k: int, normalize: bool
     if return_hist:
         out.append(hist)
     return tuple(out)
+
+
+def route_small(x: torch.Tensor, w_router: torch.Tensor, k: int, normalize: bool = True,
+                bias: Optional[torch.Tensor] = None, acc_zero: Optional[torch.Tensor] = None):
+    """K1 + K2 in one launch for T <= ROUTE_SMALL_MAX_T tokens (E <= 128).
+    Returns a dict with the router outputs (topk_idx, topk_w, logits) and the
+    permutation outputs (counts, offsets, row_token, row_w, slot_row, tiles,
+    max_tiles); ``acc_zero`` (T, H) fp32 is zero-filled."""
+    _need(x, "x", torch.bfloat16, 2)
+    _need(w_router, "w_router", torch.bfloat16, 2)
+    T, H = x.shape
+    E = w_router.shape[0]
+    if bias is not None:
+        _need(bias, "bias", torch.float32, 1)
+    dev = x.device
+    R = T * k
+    mt = max_tiles(R, E)
+    i32 = dict(dtype=torch.int32, device=dev)
+    f32 = dict(dtype=torch.float32, device=dev)
+    out = dict(topk_idx=torch.empty((T, k), **i32), topk_w=torch.empty((T, k), **f32),
+               logits=torch.empty((T, E), **f32), counts=torch.empty(E, **i32),
+               offsets=torch.empty(E + 1, **i32), row_token=torch.empty(max(R, 1), **i32),
+               row_w=torch.empty(max(R, 1), **f32), slot_row=torch.empty((T, k), **i32),
+               tiles=torch.zeros(1 + 3 * mt, **i32), max_tiles=mt)
+    with torch.cuda.device(dev):
+        _C.check(_C.lib().qmoe_route_small(
+            _ptr(x), _ptr(w_router), _ptr(bias), T, H, E, k, 1 if normalize else 0, _ptr(out["logits"]),
+            _ptr(out["topk_idx"]), _ptr(out["topk_w"]), _ptr(out["counts"]), _ptr(out["offsets"]),
+            _ptr(out["row_token"]), _ptr(out["row_w"]), _ptr(out["slot_row"]), _ptr(out["tiles"]),
+            _ptr(acc_zero), _stream(dev)), "qmoe_route_small")
+    return out
 
 
 def moe_permute(topk_idx: torch.Tensor, topk_w: torch.Tensor, chunk_hist: torch.Tensor,

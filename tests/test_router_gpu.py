@@ -4,7 +4,7 @@ import numpy as np
 import pytest
 import torch
 
-from helpers import activations
+from helpers import activations, moe_weights
 
 pytestmark = pytest.mark.gpu
 
@@ -69,3 +69,36 @@ def test_router_bias_and_unnormalized(cuda_dev, oracle):
     assert np.array_equal(logits.view(np.uint32), ref_logits.view(np.uint32))
     assert np.array_equal(idx, ref_idx)
     np.testing.assert_allclose(w, ref_w, rtol=2e-6, atol=1e-8)
+
+
+@pytest.mark.parametrize("T,H,E,k", [(1, 2048, 128, 8), (2, 2048, 128, 8), (5, 256, 32, 4), (16, 2048, 128, 8),
+                                     (7, 4096, 64, 8), (16, 512, 128, 1), (3, 1024, 32, 32)])
+def test_route_small_matches_router_and_permute(cuda_dev, oracle, T, H, E, k):
+    """The one-launch decode route (router + permutation in a cluster) gives
+    the oracle's routing and rows bit for bit, and zero-fills the accumulator."""
+    from nki_moe_7013_b200 import ops
+
+    wr = moe_weights(50 + T, E, H, 128, cuda_dev)[0]
+    x = activations(50 + T, T, H, cuda_dev)
+    acc = torch.full((T, H), 3.0, dtype=torch.float32, device=cuda_dev)
+    r = ops.route_small(x, wr, k, acc_zero=acc)
+    torch.cuda.synchronize()
+    ref_logits, ref_idx, ref_w = oracle.router(x.cpu(), wr.cpu(), k, True)
+    assert np.array_equal(r["logits"].cpu().numpy().view(np.uint32), ref_logits.view(np.uint32))
+    assert np.array_equal(r["topk_idx"].cpu().numpy(), ref_idx)
+    np.testing.assert_allclose(r["topk_w"].cpu().numpy(), ref_w, rtol=2e-6, atol=1e-7)
+    # identical to the separate kernels
+    idx, w, hist = ops.router_topk(x, wr, k, return_hist=True)
+    p = ops.moe_permute(idx, w, hist, E, x=x, gather=False)
+    torch.cuda.synchronize()
+    assert torch.equal(r["topk_w"], w)
+    for key in ("counts", "offsets", "row_token", "row_w", "slot_row"):
+        assert torch.equal(r[key], p[key]), key
+    nt = int(p["tiles"][0])
+    mt = p["max_tiles"]
+    assert int(r["tiles"][0]) == nt
+    for part in range(3):
+        assert torch.equal(r["tiles"][1 + part * mt:1 + part * mt + nt], p["tiles"][1 + part * mt:1 + part * mt + nt])
+    assert torch.count_nonzero(acc).item() == 0
+    ref = oracle.permute(idx.cpu().numpy(), E)
+    np.testing.assert_array_equal(r["row_token"].cpu().numpy(), ref["row_token"])
