@@ -145,6 +145,11 @@ QMOE_API int qmoe_moe_permute(const int32_t* topk_idx, const float* topk_w, int3
  *   w_gate_up (E, 2I, H)  bf16
  *   tiles                 from qmoe_moe_permute (or qmoe_blockwise_prepare)
  *   act      (R, I)       bf16 out: silu(x W_gate^T) * (x W_up^T), grouped order
+ *   max_tile_rows         an upper bound on the rows of any tile (1..128; other
+ *            values mean 128).  Tiles of <= 16 rows (decode) run a
+ *            configuration with a deeper weight pipeline; a tile larger than
+ *            a bound <= 16 is refused on the device (device error 4).  Rows
+ *            routed by qmoe_router_topk satisfy max_tile_rows = min(T, 128).
  *   split_ws optional scratch of qmoe_grouped_gemm_gateup_split_workspace_size()
  *            bytes (or NULL).  With it, decode-sized calls (R <= 128) whose
  *            tiles all hold <= 16 rows split K over up to 4 CTAs per unit so
@@ -157,9 +162,9 @@ QMOE_API int qmoe_moe_permute(const int32_t* topk_idx, const float* topk_w, int3
 QMOE_API size_t qmoe_grouped_gemm_gateup_split_workspace_size(void);
 QMOE_API int qmoe_grouped_gemm_gateup_swiglu(const void* x, int64_t x_rows, const int32_t* gather_rows,
                                              const void* w_gate_up, const int32_t* tiles,
-                                             int64_t max_tiles, int64_t R, int64_t H, int64_t I,
-                                             int64_t E, void* act, void* split_ws, size_t split_ws_bytes,
-                                             void* stream);
+                                             int64_t max_tiles, int64_t max_tile_rows, int64_t R, int64_t H,
+                                             int64_t I, int64_t E, void* act, void* split_ws,
+                                             size_t split_ws_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
  * K3b  grouped GEMM, down projection with the weighted combine in the
@@ -169,6 +174,7 @@ QMOE_API int qmoe_grouped_gemm_gateup_swiglu(const void* x, int64_t x_rows, cons
  *
  *   act     (R, I)   bf16
  *   w_down  (E, H, I) bf16
+ *   max_tile_rows    as for qmoe_grouped_gemm_gateup_swiglu
  *   row_dst (R)      int32: destination row in acc; rows < 0 are skipped
  *   row_w   (R)      fp32 weight
  *   acc     (n_acc, H) fp32, accumulated into (fp32 atomic adds, so the
@@ -176,7 +182,7 @@ QMOE_API int qmoe_grouped_gemm_gateup_swiglu(const void* x, int64_t x_rows, cons
  * Requires H % 128 == 0, I % 64 == 0.
  * ---------------------------------------------------------------------- */
 QMOE_API int qmoe_grouped_gemm_down_combine(const void* act, const void* w_down, const int32_t* tiles,
-                                   int64_t max_tiles, const int32_t* row_dst,
+                                   int64_t max_tiles, int64_t max_tile_rows, const int32_t* row_dst,
                                    const float* row_w, int64_t R, int64_t H, int64_t I,
                                    int64_t E, float* acc, int64_t n_acc, void* stream);
 

@@ -59,14 +59,19 @@ enum GemmMode : int {
   kModeDownReturn = 3,  // weighted bf16 rows stored into the source rank's return buffer (EP)
 };
 
-template <int kMode>
+// kSmall: every tile has at most 16 rows (decode batches).  The activation
+// slot of a stage shrinks to 16 rows, which leaves room for more stages --
+// more weight bytes in flight per SM, which is what bounds a GEMM that
+// streams a few experts.
+template <int kMode, bool kSmall = false>
 struct GemmCfg {
   static constexpr bool kGateUp = kMode == kModeGateUp;
   static constexpr int kATiles = kGateUp ? 2 : 1;
   static constexpr int kABytes = kBM * kBK * 2;           // 16 KB
-  static constexpr int kBBytes = kBNMax * kBK * 2;        // 16 KB
+  static constexpr int kBRows = kSmall ? kBoxRows : kBNMax;
+  static constexpr int kBBytes = kBRows * kBK * 2;        // 16 KB (2 KB small)
   static constexpr int kStageBytes = kATiles * kABytes + kBBytes;
-  static constexpr int kStages = kGateUp ? 4 : 6;
+  static constexpr int kStages = kGateUp ? (kSmall ? 6 : 4) : (kSmall ? 11 : 6);
   static constexpr int kAccCols = kGateUp ? 256 : 128;    // TMEM columns per accumulator buffer
   static constexpr int kTmemCols = 2 * kAccCols;
   static constexpr int kBarrierBytes = 256;
@@ -129,15 +134,11 @@ struct TileView {
 
 // Gate/up split count for this launch: as many splits (<= max_k_splits) as
 // fit the grid once, only when every tile has at most 16 rows.
-__device__ __forceinline__ int gateup_k_splits(const GemmArgs& a, const TileView& tv, int ntiles) {
-  if (a.split_ws == nullptr || a.max_k_splits < 2 || ntiles <= 0) return 1;
+__device__ __forceinline__ int gateup_k_splits(const GemmArgs& a, int ntiles, int max_rows) {
+  if (a.split_ws == nullptr || a.max_k_splits < 2 || ntiles <= 0 || max_rows > kBoxRows) return 1;
   const int units = ntiles * a.n_mtiles;
-  int s = min(a.max_k_splits, min(int(gridDim.x), kSplitSlots) / units);
-  s = min(s, a.num_kb);
-  if (s < 2) return 1;
-  for (int t = 0; t < ntiles; ++t)
-    if (tv.nrows(t) > kBoxRows) return 1;
-  return s;
+  const int s = min(min(a.max_k_splits, a.num_kb), min(int(gridDim.x), kSplitSlots) / units);
+  return s < 2 ? 1 : s;
 }
 
 // Gate/up split-K fix-up, run by the 128 epilogue threads of one unit (tm,
@@ -184,11 +185,11 @@ __device__ __forceinline__ bool gateup_split_reduce(const GemmArgs& a, int tm, i
   return true;
 }
 
-template <int kMode>
+template <int kMode, bool kSmall = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
-  using C = GemmCfg<kMode>;
+  using C = GemmCfg<kMode, kSmall>;
   constexpr bool kGateUp = C::kGateUp;
   extern __shared__ uint8_t gemm_smem_raw[];
   __shared__ int split_last;
@@ -234,14 +235,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   griddep_wait();
   griddep_launch_dependents();
 
-  const int ntiles = args.tiles ? min(args.tiles[0], args.max_tiles)
-                                 : (args.dense_rows + kBNMax - 1) / kBNMax;
+  int ntiles = args.tiles ? min(args.tiles[0], args.max_tiles) : (args.dense_rows + kBNMax - 1) / kBNMax;
   const TileView tv{args.tiles ? args.tiles + 1 : nullptr,
                     args.tiles ? args.tiles + 1 + args.max_tiles : nullptr,
                     args.tiles ? args.tiles + 1 + 2 * args.max_tiles : nullptr, args.dense_rows};
+  // Largest tile (every warp scans the row counts in parallel): the small
+  // configuration holds 16 rows per stage, and gate/up splits K only over
+  // one-chunk tiles.
+  int max_rows = kBNMax;
+  if (kSmall || (kGateUp && args.split_ws != nullptr && args.max_k_splits > 1)) {
+    max_rows = 0;
+    for (int t = lane; t < ntiles; t += 32) max_rows = max(max_rows, tv.nrows(t));
+    max_rows = __reduce_max_sync(0xFFFFFFFFu, max_rows);
+  }
+  if (kSmall && max_rows > kBoxRows) {
+    if (threadIdx.x == 0) record_device_error(kDevErrBadIndex);
+    ntiles = 0;  // refuse the launch rather than overrun a stage
+  }
   int ksplit = 1;
-  if constexpr (kMode == kModeDown) ksplit = max(1, min(args.k_splits, args.num_kb));
-  if constexpr (kGateUp) ksplit = gateup_k_splits(args, tv, ntiles);
+  if constexpr (kMode == kModeDown) {
+    // as many splits (<= k_splits) as the grid runs at once
+    const int units = max(1, ntiles * args.n_mtiles);
+    ksplit = max(1, min(min(args.k_splits, args.num_kb), int(gridDim.x) / units));
+  }
+  if constexpr (kGateUp) ksplit = gateup_k_splits(args, ntiles, max_rows);
   const int total_units = ntiles * args.n_mtiles * ksplit;
 
   if (warp == 0) {

@@ -227,12 +227,12 @@ int launch_router(const void* x, const void* w, const float* bias, int64_t T, in
                          topk_idx, topk_w, chunk_hist);
   }
   const int smem = int(sizeof(float) * qmoe::kRouterChunk * (H + E));
-#define QMOE_ROUTER_CASE(GG)                                                                   \
-  case GG: {                                                                                   \
-    QMOE_CHECK(set_smem(qmoe::router_topk_kernel<GG>, smem));                                  \
-    qmoe::router_topk_kernel<GG><<<nchunks, qmoe::router_warps<GG>() * 32, smem, stream>>>(   \
-        xb, wb, bias, int(T), int(E), int(k), normalize, logits, topk_idx, topk_w, chunk_hist); \
-    break;                                                                                     \
+#define QMOE_ROUTER_CASE(GG)                                                                                \
+  case GG: {                                                                                                \
+    QMOE_CHECK(set_smem(qmoe::router_topk_kernel<GG>, smem));                                               \
+    return launch_kernel(qmoe::router_topk_kernel<GG>, dim3(nchunks), dim3(qmoe::router_warps<GG>() * 32), \
+                         size_t(smem), stream, true, "router_topk_kernel", xb, wb, bias, int(T), int(E),     \
+                         int(k), normalize, logits, topk_idx, topk_w, chunk_hist);                          \
   }
   switch (G) {
     QMOE_ROUTER_CASE(1)
@@ -244,7 +244,6 @@ int launch_router(const void* x, const void* w, const float* bias, int64_t T, in
       return set_error(QMOE_ERR_UNSUPPORTED_SHAPE, "router: H/256 = %d not in {1,2,4,8,16}", G);
   }
 #undef QMOE_ROUTER_CASE
-  return check_launch("router_topk_kernel");
 }
 
 size_t route_small_smem(int64_t T, int64_t H, int64_t E, int64_t k) {
@@ -337,12 +336,25 @@ int launch_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chunk_
   return QMOE_OK;
 }
 
+// One grouped-GEMM launch in the normal or the small-tile configuration.
+template <int kMode, bool kSmall>
+int launch_gemm_cfg(const CUtensorMap& tmA, const CUtensorMap& tmB, const qmoe::GemmArgs& a, int grid,
+                    cudaStream_t stream, const char* name) {
+  using C = qmoe::GemmCfg<kMode, kSmall>;
+  QMOE_CHECK(set_smem(qmoe::grouped_gemm_kernel<kMode, kSmall>, C::kSmemBytes));
+  return launch_kernel(qmoe::grouped_gemm_kernel<kMode, kSmall>, dim3(grid), dim3(qmoe::kGemmThreads),
+                       C::kSmemBytes, stream, true, name, tmA, tmB, a);
+}
+
+// Tiles of at most this many rows take the small configuration.
+constexpr int64_t kSmallTileRows = qmoe::kBoxRows;
+
 // x: x_perm (R rows, permuted) when gather_rows is null, else the source
 // activations (x_rows rows) gathered by gather_rows[r] with TMA gather4.
+// max_tile_rows: an upper bound on the rows of any tile.
 int launch_gemm_gateup(const void* x, int64_t x_rows, const int32_t* gather_rows, const void* w_gate_up,
                        const int32_t* tiles, int64_t max_tiles, int64_t R, int64_t H, int64_t I, int64_t E,
-                       void* act, void* split_ws, cudaStream_t stream) {
-  using C = qmoe::GemmCfg<qmoe::kModeGateUp>;
+                       void* act, void* split_ws, cudaStream_t stream, int64_t max_tile_rows = qmoe::kBNMax) {
   CUtensorMap tmA, tmB;
   QMOE_CHECK(make_tmap_bf16(&tmA, w_gate_up, uint64_t(H), uint64_t(E * 2 * I), qmoe::kBK, qmoe::kBM));
   if (gather_rows)
@@ -366,15 +378,15 @@ int launch_gemm_gateup(const void* x, int64_t x_rows, const int32_t* gather_rows
   const int64_t units = max_tiles * a.n_mtiles * a.max_k_splits;
   const int grid = int(std::min<int64_t>(units, num_sms(0)));
   if (grid <= 0) return QMOE_OK;
-  QMOE_CHECK(set_smem(qmoe::grouped_gemm_kernel<qmoe::kModeGateUp>, C::kSmemBytes));
-  return launch_kernel(qmoe::grouped_gemm_kernel<qmoe::kModeGateUp>, dim3(grid), dim3(qmoe::kGemmThreads),
-                       C::kSmemBytes, stream, true, "grouped_gemm_kernel<gate_up>", tmA, tmB, a);
+  if (std::min(max_tile_rows, R) <= kSmallTileRows)
+    return launch_gemm_cfg<qmoe::kModeGateUp, true>(tmA, tmB, a, grid, stream, "grouped_gemm_kernel<gate_up,small>");
+  return launch_gemm_cfg<qmoe::kModeGateUp, false>(tmA, tmB, a, grid, stream, "grouped_gemm_kernel<gate_up>");
 }
 
 int launch_gemm_down(const void* act, const void* w_down, const int32_t* tiles, int64_t max_tiles,
                      const int32_t* row_dst, const float* row_w, int64_t R, int64_t H, int64_t I,
-                     int64_t E, float* acc, int64_t n_acc, cudaStream_t stream) {
-  using C = qmoe::GemmCfg<qmoe::kModeDown>;
+                     int64_t E, float* acc, int64_t n_acc, cudaStream_t stream,
+                     int64_t max_tile_rows = qmoe::kBNMax) {
   CUtensorMap tmA, tmB;
   QMOE_CHECK(make_tmap_bf16(&tmA, w_down, uint64_t(I), uint64_t(E * H), qmoe::kBK, qmoe::kBM));
   QMOE_CHECK(make_tmap_bf16(&tmB, act, uint64_t(I), uint64_t(R), qmoe::kBK, qmoe::kBoxRows));
@@ -384,16 +396,10 @@ int launch_gemm_down(const void* act, const void* w_down, const int32_t* tiles, 
   a.n_mtiles = int(H / qmoe::kBM);
   a.num_kb = int(I / qmoe::kBK);
   a.k_splits = 1;
-  // Tiny batches: few (tile, feature block) units, so split K as well to put
-  // more SMs on the weight stream (the partials meet in the accumulator).
-  if (R <= 16) {
-    for (int s : {3, 2}) {
-      if (a.num_kb % s == 0) {
-        a.k_splits = s;
-        break;
-      }
-    }
-  }
+  // Tiny batches: the kernel may split K (up to 3 ways, no more than the
+  // grid holds at once) to put more SMs on the weight stream; the partials
+  // meet in the accumulator.
+  if (R <= 16) a.k_splits = 3;
   a.a_rows_per_expert = int(H);
   a.up_row_offset = 0;
   a.row_dst = row_dst;
@@ -404,9 +410,9 @@ int launch_gemm_down(const void* act, const void* w_down, const int32_t* tiles, 
   const int64_t units = max_tiles * a.n_mtiles * a.k_splits;
   const int grid = int(std::min<int64_t>(units, num_sms(0)));
   if (grid <= 0) return QMOE_OK;
-  QMOE_CHECK(set_smem(qmoe::grouped_gemm_kernel<qmoe::kModeDown>, C::kSmemBytes));
-  return launch_kernel(qmoe::grouped_gemm_kernel<qmoe::kModeDown>, dim3(grid), dim3(qmoe::kGemmThreads),
-                       C::kSmemBytes, stream, true, "grouped_gemm_kernel<down>", tmA, tmB, a);
+  if (std::min(max_tile_rows, R) <= kSmallTileRows)
+    return launch_gemm_cfg<qmoe::kModeDown, true>(tmA, tmB, a, grid, stream, "grouped_gemm_kernel<down,small>");
+  return launch_gemm_cfg<qmoe::kModeDown, false>(tmA, tmB, a, grid, stream, "grouped_gemm_kernel<down>");
 }
 
 int launch_linear(const void* x, const void* w, int64_t T, int64_t K, int64_t N, void* out,
@@ -582,8 +588,8 @@ size_t qmoe_grouped_gemm_gateup_split_workspace_size(void) { return qmoe::kSplit
 
 int qmoe_grouped_gemm_gateup_swiglu(const void* x, int64_t x_rows, const int32_t* gather_rows,
                                     const void* w_gate_up, const int32_t* tiles, int64_t max_tiles,
-                                    int64_t R, int64_t H, int64_t I, int64_t E, void* act, void* split_ws,
-                                    size_t split_ws_bytes, void* stream) {
+                                    int64_t max_tile_rows, int64_t R, int64_t H, int64_t I, int64_t E,
+                                    void* act, void* split_ws, size_t split_ws_bytes, void* stream) {
   QMOE_REQUIRE(x && w_gate_up && tiles && act, QMOE_ERR_INVALID_ARGUMENT, "gate_up: null pointer");
   QMOE_REQUIRE(R >= 0 && R < (int64_t(1) << 31), QMOE_ERR_INVALID_ARGUMENT, "gate_up: bad R");
   QMOE_REQUIRE(!gather_rows || (x_rows > 0 && x_rows < (int64_t(1) << 31)), QMOE_ERR_INVALID_ARGUMENT,
@@ -601,11 +607,13 @@ int qmoe_grouped_gemm_gateup_swiglu(const void* x, int64_t x_rows, const int32_t
   QMOE_CHECK(device_info(&d));
   if (R == 0) return QMOE_OK;
   return launch_gemm_gateup(x, x_rows, gather_rows, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws,
-                            static_cast<cudaStream_t>(stream));
+                            static_cast<cudaStream_t>(stream),
+                            max_tile_rows >= 1 && max_tile_rows <= qmoe::kBNMax ? max_tile_rows : qmoe::kBNMax);
 }
 
 int qmoe_grouped_gemm_down_combine(const void* act, const void* w_down, const int32_t* tiles,
-                                   int64_t max_tiles, const int32_t* row_dst, const float* row_w,
+                                   int64_t max_tiles, int64_t max_tile_rows, const int32_t* row_dst,
+                                   const float* row_w,
                                    int64_t R, int64_t H, int64_t I, int64_t E, float* acc,
                                    int64_t n_acc, void* stream) {
   QMOE_REQUIRE(act && w_down && tiles && row_dst && row_w && acc, QMOE_ERR_INVALID_ARGUMENT,
@@ -621,7 +629,8 @@ int qmoe_grouped_gemm_down_combine(const void* act, const void* w_down, const in
   QMOE_CHECK(device_info(&d));
   if (R == 0) return QMOE_OK;
   return launch_gemm_down(act, w_down, tiles, max_tiles, row_dst, row_w, R, H, I, E, acc, n_acc,
-                          static_cast<cudaStream_t>(stream));
+                          static_cast<cudaStream_t>(stream),
+                          max_tile_rows >= 1 && max_tile_rows <= qmoe::kBNMax ? max_tile_rows : qmoe::kBNMax);
 }
 
 int qmoe_combine_finalize(const float* acc, const void* residual, int64_t T, int64_t H, void* out,
@@ -1095,6 +1104,8 @@ int qmoe_moe_forward(const void* x, const void* w_router, const float* router_bi
                                      : nullptr;
   const int64_t R = T * k;
   const int64_t max_tiles = qmoe_max_tiles(R, E);
+  // a token's k experts are distinct, so no expert gets more than T rows
+  const int64_t tile_rows = std::min<int64_t>(T, qmoe::kBNMax);
 
   float* logits = T <= kRouterSmallMaxT ? reinterpret_cast<float*>(ws + L.logits) : nullptr;
   if (T <= qmoe::kRouteSmallMaxT && E <= qmoe::kRouteSmallMaxE) {
@@ -1113,10 +1124,12 @@ int qmoe_moe_forward(const void* x, const void* w_router, const float* router_bi
                               split_counters ? qmoe::kSplitSlots : 0));
   }
   if (x_perm)
-    QMOE_CHECK(launch_gemm_gateup(x_perm, R, nullptr, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s));
+    QMOE_CHECK(launch_gemm_gateup(x_perm, R, nullptr, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s,
+                                  tile_rows));
   else
-    QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s));
-  QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s));
+    QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s,
+                                  tile_rows));
+  QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s, tile_rows));
   return launch_finalize(acc, residual, T, H, out, s);
 }
 
@@ -1228,6 +1241,8 @@ extern "C" int qmoe_moe_forward_noalloc(const void* x, const void* w_router,
                                      : nullptr;
   const int64_t R = T * k;
   const int64_t max_tiles = qmoe_max_tiles(R, E);
+  // a token's k experts are distinct, so no expert gets more than T rows
+  const int64_t tile_rows = std::min<int64_t>(T, qmoe::kBNMax);
   float* logits = T <= kRouterSmallMaxT ? reinterpret_cast<float*>(ws + L.logits) : nullptr;
   if (T <= qmoe::kRouteSmallMaxT && E <= qmoe::kRouteSmallMaxE) {
     // decode sizes: router + permutation in one launch, which also zeroes
@@ -1245,9 +1260,11 @@ extern "C" int qmoe_moe_forward_noalloc(const void* x, const void* w_router,
                               split_counters ? qmoe::kSplitSlots : 0));
   }
   if (x_perm)
-    QMOE_CHECK(launch_gemm_gateup(x_perm, R, nullptr, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s));
+    QMOE_CHECK(launch_gemm_gateup(x_perm, R, nullptr, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s,
+                                  tile_rows));
   else
-    QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s));
-  QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s));
+    QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s,
+                                  tile_rows));
+  QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s, tile_rows));
   return launch_finalize(acc, residual, T, H, out, s);
 }

@@ -243,6 +243,8 @@ class MoEPlan:
                        if T > ops.GATHER_MAX_T else None)
         # small batches route through the logits + selection kernels
         self.logits = torch.empty((T, E), **f32) if T <= ops.ROUTER_SMALL_MAX_T else None
+        # a token's k experts are distinct: no tile holds more than T rows
+        self.tile_rows = min(T, 128)
         # decode sizes: router + permutation in one launch
         self.route_small = T <= ops.ROUTE_SMALL_MAX_T and E <= ops.ROUTE_SMALL_MAX_E
         # decode sizes: the gate/up GEMM may split K (zero-filled scratch)
@@ -280,15 +282,16 @@ class MoEPlan:
         mark(2)
         if self.x_perm is not None:
             _C.check(lib.qmoe_grouped_gemm_gateup_swiglu(p(self.x_perm), R, None, p(w.gate_up), p(self.tiles),
-                                                         self.max_tiles, R, H, I, E, p(self.act),
+                                                         self.max_tiles, self.tile_rows, R, H, I, E, p(self.act),
                                                          p(self.split_ws), self._split_bytes, s), "gate_up")
         else:
             _C.check(lib.qmoe_grouped_gemm_gateup_swiglu(p(x), T, p(self.row_token), p(w.gate_up),
-                                                         p(self.tiles), self.max_tiles, R, H, I, E, p(self.act),
-                                                         p(self.split_ws), self._split_bytes, s), "gate_up")
+                                                         p(self.tiles), self.max_tiles, self.tile_rows, R, H, I, E,
+                                                         p(self.act), p(self.split_ws), self._split_bytes, s),
+                     "gate_up")
         mark(3)
         _C.check(lib.qmoe_grouped_gemm_down_combine(p(self.act), p(w.down), p(self.tiles), self.max_tiles,
-                                                    p(self.row_token), p(self.row_w), R, H, I, E,
+                                                    self.tile_rows, p(self.row_token), p(self.row_w), R, H, I, E,
                                                     p(self.acc), T, s), "down")
         mark(4)
         _C.check(lib.qmoe_combine_finalize(p(self.acc), p(residual), T, H, p(out), s), "finalize")

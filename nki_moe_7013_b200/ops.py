@@ -156,11 +156,13 @@ def gateup_split_workspace(device) -> torch.Tensor:
 def grouped_gemm_gateup_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, tiles: torch.Tensor,
                                max_tiles_: int, out: Optional[torch.Tensor] = None,
                                gather_rows: Optional[torch.Tensor] = None,
-                               split_ws: Optional[torch.Tensor] = None) -> torch.Tensor:
+                               split_ws: Optional[torch.Tensor] = None, max_tile_rows: int = 128) -> torch.Tensor:
     """K3a.  act (R, I) bf16 = SiLU(x W_gate^T) * (x W_up^T) in grouped order.
     ``x`` is x_perm (R, H), or with ``gather_rows`` (R,) int32 the source
     activations whose row gather_rows[r] is grouped row r.  ``split_ws``
-    (from gateup_split_workspace) lets R <= 128 calls split K."""
+    (from gateup_split_workspace) lets R <= 128 calls split K.
+    ``max_tile_rows``: a bound on the rows of any tile (min(T, 128) for
+    router-built tiles); <= 16 selects the decode configuration."""
     _need(x, "x", torch.bfloat16, 2)
     _need(w_gate_up, "w_gate_up", torch.bfloat16, 3)
     _need(tiles, "tiles", torch.int32, 1)
@@ -177,7 +179,7 @@ def grouped_gemm_gateup_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, tiles: 
     act = out if out is not None else torch.empty((R, I), dtype=torch.bfloat16, device=dev)
     with torch.cuda.device(dev):
         _C.check(_C.lib().qmoe_grouped_gemm_gateup_swiglu(
-            _ptr(x), rows, _ptr(gather_rows), _ptr(w_gate_up), _ptr(tiles), max_tiles_, R, H, I, E,
+            _ptr(x), rows, _ptr(gather_rows), _ptr(w_gate_up), _ptr(tiles), max_tiles_, max_tile_rows, R, H, I, E,
             _ptr(act), _ptr(split_ws), 0 if split_ws is None else split_ws.numel() * split_ws.element_size(),
             _stream(dev)), "qmoe_grouped_gemm_gateup_swiglu")
     return act
@@ -185,8 +187,9 @@ def grouped_gemm_gateup_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, tiles: 
 
 def grouped_gemm_down_combine(act: torch.Tensor, w_down: torch.Tensor, tiles: torch.Tensor,
                               max_tiles_: int, row_dst: torch.Tensor, row_w: torch.Tensor,
-                              acc: torch.Tensor) -> torch.Tensor:
-    """K3b.  acc[row_dst[r]] += row_w[r] * act[r] @ W_down[e]^T (fp32, in place)."""
+                              acc: torch.Tensor, max_tile_rows: int = 128) -> torch.Tensor:
+    """K3b.  acc[row_dst[r]] += row_w[r] * act[r] @ W_down[e]^T (fp32, in place).
+    ``max_tile_rows`` as for grouped_gemm_gateup_swiglu."""
     _need(act, "act", torch.bfloat16, 2)
     _need(w_down, "w_down", torch.bfloat16, 3)
     _need(tiles, "tiles", torch.int32, 1)
@@ -200,7 +203,7 @@ def grouped_gemm_down_combine(act: torch.Tensor, w_down: torch.Tensor, tiles: to
     dev = act.device
     with torch.cuda.device(dev):
         _C.check(_C.lib().qmoe_grouped_gemm_down_combine(
-            _ptr(act), _ptr(w_down), _ptr(tiles), max_tiles_, _ptr(row_dst), _ptr(row_w),
+            _ptr(act), _ptr(w_down), _ptr(tiles), max_tiles_, max_tile_rows, _ptr(row_dst), _ptr(row_w),
             R, H, I, E, _ptr(acc), acc.shape[0], _stream(dev)), "qmoe_grouped_gemm_down_combine")
     return acc
 

@@ -43,10 +43,10 @@ def test_host_side_validation_needs_no_gpu(lib):
     st = lib.qmoe_router_topk(p, p, None, 4, 2048, 32, 33, 1, None, p, p, None, None)
     assert st == -1
     # I not a multiple of 128
-    st = lib.qmoe_grouped_gemm_gateup_swiglu(p, 0, None, p, p, 10, 8, 2048, 100, 128, p, None, 0, None)
+    st = lib.qmoe_grouped_gemm_gateup_swiglu(p, 0, None, p, p, 10, 128, 8, 2048, 100, 128, p, None, 0, None)
     assert st == -2
     # split-K scratch smaller than the query says
-    st = lib.qmoe_grouped_gemm_gateup_swiglu(p, 0, None, p, p, 10, 8, 2048, 768, 128, p, p, 64, None)
+    st = lib.qmoe_grouped_gemm_gateup_swiglu(p, 0, None, p, p, 10, 128, 8, 2048, 768, 128, p, p, 64, None)
     assert st == -4 and lib.qmoe_grouped_gemm_gateup_split_workspace_size() > 64
     # misaligned pointer
     st = lib.qmoe_combine_finalize(p + 4, None, 2, 64, p, None)

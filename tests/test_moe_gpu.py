@@ -109,6 +109,61 @@ def test_gateup_split_k(cuda_dev, oracle, T, H, E, k, I):
     assert err <= MAX_REL, f"split-K act max rel err {err:.3e}"
 
 
+@pytest.mark.parametrize("T,gather", [(1, True), (4, True), (16, True), (9, False)])
+def test_small_tile_configuration(cuda_dev, oracle, T, gather):
+    """Tiles of <= 16 rows (max_tile_rows <= 16) run the deeper-pipeline
+    configuration of both GEMMs; results equal the normal configuration's
+    (same k order, same epilogue), and a tile larger than the promised bound
+    is refused on the device with error 4 instead of being computed."""
+    from nki_moe_7013_b200 import _C, ops
+
+    H, E, k, I = 2048, 128, 8, 768
+    wr, wgu, wd = moe_weights(5, E, H, I, cuda_dev)
+    x = activations(60 + T, T, H, cuda_dev)
+    idx, w, hist = _routing(cuda_dev, x, wr, k)
+    p = ops.moe_permute(idx, w, hist, E, x=x, gather=not gather)
+    src = dict(x=x, gather_rows=p["row_token"]) if gather else dict(x=p["x_perm"])
+    outs = []
+    for rows in (128, T):
+        act = ops.grouped_gemm_gateup_swiglu(src["x"], wgu, p["tiles"], p["max_tiles"],
+                                             gather_rows=src.get("gather_rows"), max_tile_rows=rows)
+        acc = torch.zeros((T, H), dtype=torch.float32, device=cuda_dev)
+        ops.grouped_gemm_down_combine(act, wd, p["tiles"], p["max_tiles"], p["row_token"], p["row_w"], acc,
+                                      max_tile_rows=rows)
+        outs.append((act, acc))
+    torch.cuda.synchronize()
+    assert _C.device_error() == 0
+    assert torch.equal(outs[0][0], outs[1][0])
+    assert max_rel_err(outs[1][1].cpu().numpy(), outs[0][1].cpu().numpy()) <= 1e-5
+    ref_out, _ = oracle.moe_block(x.cpu(), wr.cpu(), wgu.cpu(), wd.cpu(), k, return_intermediates=True)
+    assert max_rel_err(outs[1][1].cpu().numpy(), ref_out) <= MAX_REL
+
+
+def test_small_tile_configuration_refuses_larger_tiles(cuda_dev):
+    """A caller that promises tiles of <= 16 rows but passes a 32-row tile
+    gets device error 4 and untouched outputs, never an overrun stage."""
+    from nki_moe_7013_b200 import _C, ops
+
+    H, E, k, I, T = 2048, 128, 8, 768, 32
+    wr, wgu, wd = moe_weights(6, E, H, I, cuda_dev)
+    x = activations(6, 1, H, cuda_dev).repeat(T, 1).contiguous()  # identical tokens: 32 rows per expert
+    idx, w, hist = _routing(cuda_dev, x, wr, k)
+    p = ops.moe_permute(idx, w, hist, E, x=x, gather=False)
+    assert int(p["counts"].max()) == T
+    act = torch.full((T * k, I), 7.0, dtype=torch.bfloat16, device=cuda_dev)
+    ops.grouped_gemm_gateup_swiglu(x, wgu, p["tiles"], p["max_tiles"], gather_rows=p["row_token"],
+                                   max_tile_rows=16, out=act)
+    torch.cuda.synchronize()
+    assert _C.device_error() == 4
+    assert bool((act == 7.0).all())
+    acc = torch.full((T, H), 5.0, dtype=torch.float32, device=cuda_dev)
+    ops.grouped_gemm_down_combine(act, wd, p["tiles"], p["max_tiles"], p["row_token"], p["row_w"], acc,
+                                  max_tile_rows=16)
+    torch.cuda.synchronize()
+    assert _C.device_error() == 4
+    assert bool((acc == 5.0).all())
+
+
 @pytest.mark.parametrize("T", [1, 2, 8, 64, 128, 1024])
 def test_moe_forward_cfg0_shapes(cuda_dev, oracle, T):
     from nki_moe_7013_b200 import ops
