@@ -175,14 +175,21 @@ QMOE_API int qmoe_grouped_gemm_gateup_swiglu(const void* x, int64_t x_rows, cons
  *   act     (R, I)   bf16
  *   w_down  (E, H, I) bf16
  *   max_tile_rows    as for qmoe_grouped_gemm_gateup_swiglu
+ *   flags   QMOE_GEMM_TILES_READY: tiles were complete before the previous
+ *                    operation on the stream started (e.g. this call follows
+ *                    qmoe_grouped_gemm_gateup_swiglu on the same tiles).  With
+ *                    tiles of <= 16 rows the kernel then streams its first
+ *                    weight tiles while that previous kernel still runs.
  *   row_dst (R)      int32: destination row in acc; rows < 0 are skipped
  *   row_w   (R)      fp32 weight
  *   acc     (n_acc, H) fp32, accumulated into (fp32 atomic adds, so the
  *                    order of the k contributions of a row is not fixed)
  * Requires H % 128 == 0, I % 64 == 0.
  * ---------------------------------------------------------------------- */
+#define QMOE_GEMM_TILES_READY 1
 QMOE_API int qmoe_grouped_gemm_down_combine(const void* act, const void* w_down, const int32_t* tiles,
-                                   int64_t max_tiles, int64_t max_tile_rows, const int32_t* row_dst,
+                                   int64_t max_tiles, int64_t max_tile_rows, int64_t flags,
+                                   const int32_t* row_dst,
                                    const float* row_w, int64_t R, int64_t H, int64_t I,
                                    int64_t E, float* acc, int64_t n_acc, void* stream);
 

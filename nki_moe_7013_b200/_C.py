@@ -33,7 +33,7 @@ _SIGNATURES = {
     "qmoe_grouped_gemm_gateup_split_workspace_size": (SZ, []),
     "qmoe_route_small": (I32, [P, P, P, I64, I64, I64, I64, I32, P, P, P, P, P, P, P, P, P, P, P]),
     "qmoe_grouped_gemm_gateup_swiglu": (I32, [P, I64, P, P, P, I64, I64, I64, I64, I64, I64, P, P, SZ, P]),
-    "qmoe_grouped_gemm_down_combine": (I32, [P, P, P, I64, I64, P, P, I64, I64, I64, I64, P, I64, P]),
+    "qmoe_grouped_gemm_down_combine": (I32, [P, P, P, I64, I64, I64, P, P, I64, I64, I64, I64, P, I64, P]),
     "qmoe_blockwise_max_tiles": (I64, [I64, I64]),
     "qmoe_blockwise_prepare": (I32, [P, P, I64, P, P, I64, I64, I64, I64, I64, P, P, P, P, P]),
     "qmoe_combine_finalize": (I32, [P, P, I64, I64, P, P]),

@@ -41,6 +41,25 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
   return t;
 }
 
+// Optional timeline instrumentation (build with -DQMOE_TRACE): kernels stamp
+// %globaltimer at a few points per CTA into g_qmoe_trace[kernel][cta][event],
+// read back with qmoe_trace_read.  Compiled out otherwise.
+// kernel slots: 0 router / route_small, 1 gate/up, 2 down, 3 finalize,
+// 4 permute scan, 5 permute scatter
+constexpr int kTraceKernels = 6, kTraceCtas = 160, kTraceEvents = 8;
+#ifdef QMOE_TRACE
+__device__ unsigned long long g_qmoe_trace[kTraceKernels * kTraceCtas * kTraceEvents];
+#define QMOE_TRACE_AT(kid, ev)                                                                   \
+  do {                                                                                           \
+    if (blockIdx.x < kTraceCtas) g_qmoe_trace[((kid) * kTraceCtas + blockIdx.x) * kTraceEvents + (ev)] = \
+        globaltimer_ns();                                                                        \
+  } while (0)
+#else
+#define QMOE_TRACE_AT(kid, ev) \
+  do {                         \
+  } while (0)
+#endif
+
 // ---------------------------------------------------------------------------
 // Programmatic dependent launch.  Kernels of the MoE chain are launched with
 // programmatic stream serialization: each waits for its predecessor's grid

@@ -9,8 +9,10 @@ namespace qmoe {
 __global__ void __launch_bounds__(256)
     combine_finalize_kernel(const float* __restrict__ acc, const __nv_bfloat16* __restrict__ residual,
                             __nv_bfloat16* __restrict__ out, long long n_vec8) {
+  if (threadIdx.x == 0) QMOE_TRACE_AT(3, 0);
   griddep_wait();
   griddep_launch_dependents();
+  if (threadIdx.x == 0) QMOE_TRACE_AT(3, 1);
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n_vec8;
        i += (long long)gridDim.x * blockDim.x) {
     const float4 a = reinterpret_cast<const float4*>(acc)[2 * i];
@@ -34,6 +36,7 @@ __global__ void __launch_bounds__(256)
     }
     reinterpret_cast<uint4*>(out)[i] = o;
   }
+  if (threadIdx.x == 0) QMOE_TRACE_AT(3, 2);
 }
 
 }  // namespace qmoe

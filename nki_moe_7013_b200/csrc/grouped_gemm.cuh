@@ -45,6 +45,11 @@ constexpr int kBNMax = 128;    // token rows per tile
 constexpr int kBoxRows = 16;   // rows per activation TMA box
 constexpr int kUmmaK = 16;     // k per tcgen05.mma (bf16)
 constexpr int kGemmThreads = 192;
+// GemmArgs::flags: the tile list was complete before the previous kernel on
+// the stream started (true for the down GEMM after a gate/up GEMM on the same
+// tiles), so a small-tile down GEMM may read it and stream weights before its
+// dependency wait.
+constexpr int kGemmTilesReady = 1;
 // gate/up split-K scratch: kSplitSlots partial slots of [2][16 rows][128
 // features] fp32, then kSplitSlots arrival counters
 constexpr int kSplitSlots = 256;
@@ -59,10 +64,11 @@ enum GemmMode : int {
   kModeDownReturn = 3,  // weighted bf16 rows stored into the source rank's return buffer (EP)
 };
 
-// kSmall: every tile has at most 16 rows (decode batches).  The activation
-// slot of a stage shrinks to 16 rows, which leaves room for more stages --
-// more weight bytes in flight per SM, which is what bounds a GEMM that
-// streams a few experts.
+// kSmall: every tile has at most 16 rows (decode batches).  A stage's
+// activation slot and the TMEM accumulators shrink to 16 rows, so that a
+// gate/up CTA and a down CTA fit on one SM together (shared memory and TMEM):
+// the down GEMM, launched while the gate/up GEMM still runs, streams its
+// weights into its ring before the gate/up results it multiplies exist.
 template <int kMode, bool kSmall = false>
 struct GemmCfg {
   static constexpr bool kGateUp = kMode == kModeGateUp;
@@ -71,9 +77,10 @@ struct GemmCfg {
   static constexpr int kBRows = kSmall ? kBoxRows : kBNMax;
   static constexpr int kBBytes = kBRows * kBK * 2;        // 16 KB (2 KB small)
   static constexpr int kStageBytes = kATiles * kABytes + kBBytes;
-  static constexpr int kStages = kGateUp ? (kSmall ? 6 : 4) : (kSmall ? 11 : 6);
-  static constexpr int kAccCols = kGateUp ? 256 : 128;    // TMEM columns per accumulator buffer
-  static constexpr int kTmemCols = 2 * kAccCols;
+  static constexpr int kStages = kGateUp ? (kSmall ? 3 : 4) : (kSmall ? 5 : 6);
+  static constexpr int kUpCol = kSmall ? kBoxRows : kBM;  // TMEM column of the up accumulator
+  static constexpr int kAccCols = kGateUp ? 2 * kUpCol : kBRows;  // TMEM columns per accumulator buffer
+  static constexpr int kTmemCols = 2 * kAccCols < 32 ? 32 : 2 * kAccCols;
   static constexpr int kBarrierBytes = 256;
   // down epilogue: per epilogue warp a [16 rows][33] fp32 transpose buffer
   // (+ the tile's row destinations, weights and source ranks, 128 x 12 bytes)
@@ -97,6 +104,7 @@ struct GemmArgs {
   // count from the tile list (splits only when every tile has <= 16 rows)
   float* split_ws;
   int max_k_splits;
+  int flags;             // kGemmTilesReady
   int a_rows_per_expert; // 2I (gate/up) or H (down)
   int up_row_offset;     // I (gate/up only)
   // gate/up: when non-null, B row r of a tile is row gather_rows[r] of the
@@ -119,16 +127,21 @@ struct GemmArgs {
   int n_ranks;
 };
 
-// Tile accessors: the device-built tile list, or a dense row range.
+// Tile accessors: the device-built tile list (its first kTileCache entries
+// copied to shared memory), or a dense row range.
+constexpr int kTileCache = 32;
 struct TileView {
   const int32_t* exp;
   const int32_t* row0;
   const int32_t* rows;
   int dense_rows;
-  __device__ __forceinline__ int expert(int t) const { return exp ? exp[t] : 0; }
-  __device__ __forceinline__ int first_row(int t) const { return exp ? row0[t] : t * kBNMax; }
+  const int4* cache;  // {expert, first row, rows, 0} of tiles [0, kTileCache)
+  __device__ __forceinline__ int expert(int t) const { return exp ? (t < kTileCache ? cache[t].x : exp[t]) : 0; }
+  __device__ __forceinline__ int first_row(int t) const {
+    return exp ? (t < kTileCache ? cache[t].y : row0[t]) : t * kBNMax;
+  }
   __device__ __forceinline__ int nrows(int t) const {
-    return exp ? rows[t] : min(kBNMax, dense_rows - t * kBNMax);
+    return exp ? (t < kTileCache ? cache[t].z : rows[t]) : min(kBNMax, dense_rows - t * kBNMax);
   }
 };
 
@@ -185,6 +198,42 @@ __device__ __forceinline__ bool gateup_split_reduce(const GemmArgs& a, int tm, i
   return true;
 }
 
+// Down GEMM, small tiles, tile list ready: issue the weight loads of the
+// first ring stages before the dependency wait (one warp reads the tile list
+// through L2; lane 0 issues).  Each stage's full barrier is armed with the
+// stage's whole byte count (weights + activation rows); the activation loads
+// follow in the main loop.  Returns the number of stages issued (lane 0; 0
+// elsewhere, and 0 when some tile is too large for the small configuration,
+// which the main path then refuses).
+template <typename C>
+__device__ __forceinline__ int down_pre_issue(const GemmArgs& a, const CUtensorMap* tmA, uint8_t* stages,
+                                              uint64_t* full, int lane) {
+  const int nt = min(__ldcg(a.tiles), a.max_tiles);
+  const int32_t* t_exp = a.tiles + 1;
+  const int32_t* t_rows = a.tiles + 1 + 2 * a.max_tiles;
+  int mr = 0;
+  for (int t = lane; t < nt; t += 32) mr = max(mr, __ldcg(t_rows + t));
+  mr = __reduce_max_sync(0xFFFFFFFFu, mr);
+  if (mr > kBoxRows || nt <= 0 || lane != 0) return 0;
+  const int units = nt * a.n_mtiles;
+  const int ksplit = max(1, min(min(a.k_splits, a.num_kb), int(gridDim.x) / units));
+  const int total = units * ksplit;
+  const uint64_t pol_w = policy_evict_first();
+  int n = 0;
+  for (int u = blockIdx.x; u < total && n < C::kStages; u += gridDim.x) {
+    const int tm = u / ksplit, ks = u - tm * ksplit;
+    const int tile = tm / a.n_mtiles, mt = tm - tile * a.n_mtiles;
+    const int a_row = __ldcg(t_exp + tile) * a.a_rows_per_expert + mt * kBM;
+    const uint32_t bytes = C::kABytes + kBoxRows * kBK * 2;  // one 16-row box (<= 16 rows)
+    const int kb_end = (ks + 1) * a.num_kb / ksplit;
+    for (int kb = ks * a.num_kb / ksplit; kb < kb_end && n < C::kStages; ++kb, ++n) {
+      mbar_arrive_expect_tx(&full[n], bytes);
+      tma_load_2d_hint(stages + n * C::kStageBytes, tmA, kb * kBK, a_row, &full[n], pol_w);
+    }
+  }
+  return n;
+}
+
 template <int kMode, bool kSmall = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -193,6 +242,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   constexpr bool kGateUp = C::kGateUp;
   extern __shared__ uint8_t gemm_smem_raw[];
   __shared__ int split_last;
+  __shared__ int4 tile_cache[kTileCache];
+  __shared__ int tile_meta[2];  // tile count, largest tile
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(gemm_smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
@@ -207,6 +258,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  constexpr int kTid = kMode == kModeGateUp ? 1 : kMode == kModeDown ? 2 : -1;  // trace slot
+  if constexpr (kTid >= 0) if (threadIdx.x == 0) QMOE_TRACE_AT(kTid, 0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
@@ -231,23 +284,51 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Small-tile down GEMM with a tile list that predates the previous kernel:
+  // the producer fills its ring with weight tiles now, while the previous
+  // kernel (the gate/up GEMM producing this GEMM's activations) still runs;
+  // their activation tiles follow after the wait.  Metadata is read through
+  // L2 (ld.global.cg) since this precedes the wait.
+  int n_pre = 0;
+  if constexpr (kSmall && kMode == kModeDown) {
+    if ((args.flags & kGemmTilesReady) && args.tiles != nullptr && warp == 0)
+      n_pre = down_pre_issue<C>(args, &tmA, stages, full, lane);
+  }
   // everything above overlapped the previous kernel; its outputs are read below
   griddep_wait();
   griddep_launch_dependents();
+  if constexpr (kTid >= 0) if (threadIdx.x == 0) QMOE_TRACE_AT(kTid, 1);
 
-  int ntiles = args.tiles ? min(args.tiles[0], args.max_tiles) : (args.dense_rows + kBNMax - 1) / kBNMax;
   const TileView tv{args.tiles ? args.tiles + 1 : nullptr,
                     args.tiles ? args.tiles + 1 + args.max_tiles : nullptr,
-                    args.tiles ? args.tiles + 1 + 2 * args.max_tiles : nullptr, args.dense_rows};
-  // Largest tile (every warp scans the row counts in parallel): the small
-  // configuration holds 16 rows per stage, and gate/up splits K only over
-  // one-chunk tiles.
-  int max_rows = kBNMax;
-  if (kSmall || (kGateUp && args.split_ws != nullptr && args.max_k_splits > 1)) {
-    max_rows = 0;
-    for (int t = lane; t < ntiles; t += 32) max_rows = max(max_rows, tv.nrows(t));
-    max_rows = __reduce_max_sync(0xFFFFFFFFu, max_rows);
+                    args.tiles ? args.tiles + 1 + 2 * args.max_tiles : nullptr, args.dense_rows, tile_cache};
+  // Tile metadata in one round trip: warp 0 reads the count and the first
+  // kTileCache tiles together (lane l: tile l), keeps them in shared memory
+  // and finds the largest tile (the small configuration holds 16 rows per
+  // stage; gate/up splits K only over one-chunk tiles).
+  if (warp == 0) {
+    int nt, mr;
+    if (args.tiles) {
+      const int cnt = args.tiles[0];
+      int4 c = make_int4(0, 0, 0, 0);
+      if (lane < args.max_tiles) c = make_int4(tv.exp[lane], tv.row0[lane], tv.rows[lane], 0);
+      nt = min(cnt, args.max_tiles);
+      tile_cache[lane] = c;
+      mr = lane < nt ? c.z : 0;
+      for (int t = lane + kTileCache; t < nt; t += 32) mr = max(mr, tv.rows[t]);
+      mr = __reduce_max_sync(0xFFFFFFFFu, mr);
+    } else {
+      nt = (args.dense_rows + kBNMax - 1) / kBNMax;
+      mr = min(kBNMax, args.dense_rows);
+    }
+    if (lane == 0) {
+      tile_meta[0] = nt;
+      tile_meta[1] = mr;
+    }
   }
+  __syncthreads();
+  int ntiles = tile_meta[0];
+  const int max_rows = tile_meta[1];
   if (kSmall && max_rows > kBoxRows) {
     if (threadIdx.x == 0) record_device_error(kDevErrBadIndex);
     ntiles = 0;  // refuse the launch rather than overrun a stage
@@ -273,6 +354,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t issued_mask = 0;       // stages holding a load issued by this warp
     uint32_t issued_parity = 0;     // parity of that load's full-barrier phase
     bool ok = gather || lane == 0;  // box path: only lane 0 runs the loop
+    int step = 0;                   // (unit, k-block) steps issued so far
+    if (lane == 0)
+      for (int s = 0; s < n_pre; ++s) issued_mask |= 1u << s;  // pre-issued: phase 0
     for (int u = blockIdx.x; ok && u < total_units; u += gridDim.x) {
       const int tm = u / ksplit;
       const int ks = u - tm * ksplit;
@@ -302,15 +386,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (!gather) {
           // box path: lane 0 alone runs the ring (no per-stage warp sync)
           if (lane == 0) {
-            if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, kDevErrWaitTimeoutProducer)) {
-              ok = false;
-              break;
-            }
-            mbar_arrive_expect_tx(&full[stage], bytes);
-            tma_load_2d_hint(sb, &tmA, kb * kBK, a_row, &full[stage], pol_w);
-            if (kGateUp)
-              tma_load_2d_hint(sb + C::kABytes, &tmA, kb * kBK, a_row + args.up_row_offset,
-                               &full[stage], pol_w);
+            if (step >= n_pre) {
+              if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, kDevErrWaitTimeoutProducer)) {
+                ok = false;
+                break;
+              }
+              mbar_arrive_expect_tx(&full[stage], bytes);
+              tma_load_2d_hint(sb, &tmA, kb * kBK, a_row, &full[stage], pol_w);
+              if (kGateUp)
+                tma_load_2d_hint(sb + C::kABytes, &tmA, kb * kBK, a_row + args.up_row_offset,
+                                 &full[stage], pol_w);
+            }  // else: weights and the byte count were issued before the wait
             for (int b = 0; b < nb; ++b)
               tma_load_2d_hint(bs + b * (kBoxRows * kBK * 2), &tmB, kb * kBK, row0 + b * kBoxRows,
                                &full[stage], pol_x);
@@ -334,8 +420,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tma_gather4_hint(bs + lane * 4 * (kBK * 2), &tmB, kb * kBK, src[0], src[1], src[2], src[3],
                              &full[stage], pol_x);
         }
+        if constexpr (kTid >= 0) if (step == 0 && lane == 0) QMOE_TRACE_AT(kTid, 2);
         issued_mask |= 1u << stage;
         issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+        ++step;
         if (++stage == C::kStages) {
           stage = 0;
           phase ^= 1u;
@@ -374,12 +462,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_gate = tmem_base + buf * C::kAccCols;
-        const uint32_t d_up = d_gate + kBM;
+        const uint32_t d_up = d_gate + C::kUpCol;
         for (int kb = 0; kb < n_kb; ++kb) {
           if (!mbar_wait_bounded(&full[stage], phase, abort_flag, kDevErrWaitTimeoutMma)) {
             ok = false;
             break;
           }
+          if constexpr (kTid >= 0) if (local == 0 && kb == 0) QMOE_TRACE_AT(kTid, 3);
           tc_fence_after();
           const uint32_t sb = smem_u32(stages + stage * C::kStageBytes);
           const uint32_t bsb = sb + C::kATiles * C::kABytes;
@@ -401,6 +490,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (!ok) break;
         umma_commit(&acc_full[buf]);
       }
+      if constexpr (kTid >= 0) QMOE_TRACE_AT(kTid, 4);
       // Drain: every MMA issued above has completed once this barrier fires.
       umma_commit(drain);
       const unsigned long long t0 = globaltimer_ns();
@@ -447,6 +537,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       const bool ok =
           mbar_wait_bounded(&acc_full[buf], acc_phase, abort_flag, kDevErrWaitTimeoutEpilogue);
+      if constexpr (kTid >= 0) if (local == 0 && et == 0) QMOE_TRACE_AT(kTid, 5);
       // The four epilogue warps agree before going on, so a failed wait in one
       // of them can never leave the others waiting at a named barrier.  This
       // barrier also ends every read of the previous unit's row metadata.
@@ -477,7 +568,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         } else if constexpr (kGateUp) {
           uint32_t up[16];
-          tmem_ld_32x32b_x16(taddr + kBM + c * 16, up);
+          tmem_ld_32x32b_x16(taddr + C::kUpCol + c * 16, up);
           tmem_ld_wait();
           float g[16], uv[16];
 #pragma unroll
@@ -542,8 +633,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   }
 
+  if constexpr (kTid >= 0) if (threadIdx.x == 64) QMOE_TRACE_AT(kTid, 6);
   if constexpr (kMode == kModeDownReturn) __threadfence_system();  // peer stores before the next signal
   __syncthreads();
+  if constexpr (kTid >= 0) if (threadIdx.x == 0) QMOE_TRACE_AT(kTid, 7);
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();

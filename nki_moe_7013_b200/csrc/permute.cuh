@@ -64,6 +64,7 @@ __global__ void __launch_bounds__(kScanThreads)
                         int32_t* __restrict__ counts) {
   __shared__ int warp_sums[8];
   const int e = blockIdx.x;
+  if (threadIdx.x == 0) QMOE_TRACE_AT(4, 0);
   griddep_wait();
   griddep_launch_dependents();
   const int per = (nchunks + kScanThreads - 1) / kScanThreads;
@@ -79,6 +80,7 @@ __global__ void __launch_bounds__(kScanThreads)
     run += v;
   }
   if (threadIdx.x == 0) counts[e] = total;
+  if (threadIdx.x == 0) QMOE_TRACE_AT(4, 3);
 }
 
 // One CTA per router chunk (8 tokens); gridDim.y CTAs share the row gather.
@@ -101,6 +103,7 @@ __global__ void __launch_bounds__(kScatterThreads)
   const int nt = min(kRouterChunk, T - t0);
   const int npairs = nt * k;
   const int tid = threadIdx.x;
+  if (threadIdx.x == 0 && blockIdx.y == 0) QMOE_TRACE_AT(5, 0);
   griddep_wait();
   griddep_launch_dependents();
 
@@ -198,6 +201,7 @@ __global__ void __launch_bounds__(kScatterThreads)
       *reinterpret_cast<float4*>(acc_zero + size_t(t0 + tl) * H + cc) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
+  if (threadIdx.x == 0 && blockIdx.y == 0) QMOE_TRACE_AT(5, 3);
 }
 
 }  // namespace qmoe

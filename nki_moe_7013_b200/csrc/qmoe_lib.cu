@@ -248,8 +248,7 @@ int launch_router(const void* x, const void* w, const float* bias, int64_t T, in
 
 size_t route_small_smem(int64_t T, int64_t H, int64_t E, int64_t k) {
   const size_t rows = 2 * size_t((T + 3) & ~int64_t(3)) * size_t(H);
-  const size_t sel = 4 * size_t(T * E) + 8 * size_t(T * k);
-  return std::max(rows, sel);
+  return rows + 4 * size_t(T * E) + 8 * size_t(T * k);
 }
 
 // Router + permutation for T <= kRouteSmallMaxT: one cluster of
@@ -386,7 +385,7 @@ int launch_gemm_gateup(const void* x, int64_t x_rows, const int32_t* gather_rows
 int launch_gemm_down(const void* act, const void* w_down, const int32_t* tiles, int64_t max_tiles,
                      const int32_t* row_dst, const float* row_w, int64_t R, int64_t H, int64_t I,
                      int64_t E, float* acc, int64_t n_acc, cudaStream_t stream,
-                     int64_t max_tile_rows = qmoe::kBNMax) {
+                     int64_t max_tile_rows = qmoe::kBNMax, int flags = 0) {
   CUtensorMap tmA, tmB;
   QMOE_CHECK(make_tmap_bf16(&tmA, w_down, uint64_t(I), uint64_t(E * H), qmoe::kBK, qmoe::kBM));
   QMOE_CHECK(make_tmap_bf16(&tmB, act, uint64_t(I), uint64_t(R), qmoe::kBK, qmoe::kBoxRows));
@@ -407,6 +406,7 @@ int launch_gemm_down(const void* act, const void* w_down, const int32_t* tiles, 
   a.acc = acc;
   a.acc_ld = int(H);
   a.n_acc = int(n_acc);
+  a.flags = flags;
   const int64_t units = max_tiles * a.n_mtiles * a.k_splits;
   const int grid = int(std::min<int64_t>(units, num_sms(0)));
   if (grid <= 0) return QMOE_OK;
@@ -612,8 +612,8 @@ int qmoe_grouped_gemm_gateup_swiglu(const void* x, int64_t x_rows, const int32_t
 }
 
 int qmoe_grouped_gemm_down_combine(const void* act, const void* w_down, const int32_t* tiles,
-                                   int64_t max_tiles, int64_t max_tile_rows, const int32_t* row_dst,
-                                   const float* row_w,
+                                   int64_t max_tiles, int64_t max_tile_rows, int64_t flags,
+                                   const int32_t* row_dst, const float* row_w,
                                    int64_t R, int64_t H, int64_t I, int64_t E, float* acc,
                                    int64_t n_acc, void* stream) {
   QMOE_REQUIRE(act && w_down && tiles && row_dst && row_w && acc, QMOE_ERR_INVALID_ARGUMENT,
@@ -630,7 +630,8 @@ int qmoe_grouped_gemm_down_combine(const void* act, const void* w_down, const in
   if (R == 0) return QMOE_OK;
   return launch_gemm_down(act, w_down, tiles, max_tiles, row_dst, row_w, R, H, I, E, acc, n_acc,
                           static_cast<cudaStream_t>(stream),
-                          max_tile_rows >= 1 && max_tile_rows <= qmoe::kBNMax ? max_tile_rows : qmoe::kBNMax);
+                          max_tile_rows >= 1 && max_tile_rows <= qmoe::kBNMax ? max_tile_rows : qmoe::kBNMax,
+                          (flags & QMOE_GEMM_TILES_READY) ? qmoe::kGemmTilesReady : 0);
 }
 
 int qmoe_combine_finalize(const float* acc, const void* residual, int64_t T, int64_t H, void* out,
@@ -1129,9 +1130,23 @@ int qmoe_moe_forward(const void* x, const void* w_router, const float* router_bi
   else
     QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s,
                                   tile_rows));
-  QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s, tile_rows));
+  // the tile list comes from the routing kernels, before the gate/up GEMM
+  QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s, tile_rows,
+                              qmoe::kGemmTilesReady));
   return launch_finalize(acc, residual, T, H, out, s);
 }
+
+#ifdef QMOE_TRACE
+// Trace build only (not part of the public header): copies the timeline
+// stamps out and clears them.
+QMOE_API int qmoe_trace_read(void* host, size_t bytes) {
+  const size_t n = std::min(bytes, sizeof(qmoe::g_qmoe_trace));
+  if (cudaMemcpyFromSymbol(host, qmoe::g_qmoe_trace, n) != cudaSuccess) return QMOE_ERR_CUDA;
+  static unsigned long long zeros[qmoe::kTraceKernels * qmoe::kTraceCtas * qmoe::kTraceEvents];
+  if (cudaMemcpyToSymbol(qmoe::g_qmoe_trace, zeros, sizeof(zeros)) != cudaSuccess) return QMOE_ERR_CUDA;
+  return QMOE_OK;
+}
+#endif
 
 }  // extern "C"
 
@@ -1265,6 +1280,8 @@ extern "C" int qmoe_moe_forward_noalloc(const void* x, const void* w_router,
   else
     QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s,
                                   tile_rows));
-  QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s, tile_rows));
+  // the tile list comes from the routing kernels, before the gate/up GEMM
+  QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s, tile_rows,
+                              qmoe::kGemmTilesReady));
   return launch_finalize(acc, residual, T, H, out, s);
 }

@@ -9,7 +9,9 @@
 //               expert, all tokens) in the canonical order of the fused router
 //               (lane l owns elements [8l, 8l+8) of each 256-element group,
 //               group-major FMA from +0, xor butterfly 16..1), writes them to
-//               `logits`, and zeroes its slice of the combine accumulator;
+//               `logits` and into CTA 0's shared memory (distributed shared
+//               memory of the cluster), and zeroes its slice of the combine
+//               accumulator;
 //   cluster barrier (release / acquire);
 //   CTA 0       softmax + top-k + renorm per token (select_topk_warp, as the
 //               other router kernels), then the stable expert-grouped
@@ -66,9 +68,12 @@ __global__ void __launch_bounds__(kRouteSmallMaxE / kRouteSmallCtas * 32, 1)
                        float* __restrict__ acc_zero, int32_t* __restrict__ zero_words, int n_zero_words) {
   constexpr int H = G * 256;
   extern __shared__ __align__(16) uint8_t route_small_smem[];
-  // [Tpad][H] bf16 token rows; reused by CTA 0 after the logits as
-  // [T][E] fp32 logits, [T*k] picks and [T*k] weights
+  // [Tpad][H] bf16 token rows | [T][E] fp32 logits (CTA 0's copy is filled by
+  // every CTA) | [T*k] picks | [T*k] weights
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(route_small_smem);
+  float* ls = reinterpret_cast<float*>(route_small_smem + 2 * size_t((T + 3) & ~3) * (G * 256));
+  int* idx_s = reinterpret_cast<int*>(ls + T * E);
+  float* w_s = reinterpret_cast<float*>(idx_s + T * k);
   __shared__ int hist[256];
   __shared__ int off_s[256];
   __shared__ int tile_s[256];
@@ -76,8 +81,10 @@ __global__ void __launch_bounds__(kRouteSmallMaxE / kRouteSmallCtas * 32, 1)
   const int cta = blockIdx.x;  // the grid is one cluster
   const int e_per = E / kRouteSmallCtas;
   const int Tpad = (T + 3) & ~3;
+  if (threadIdx.x == 0) QMOE_TRACE_AT(0, 0);
   griddep_wait();
   griddep_launch_dependents();
+  if (threadIdx.x == 0) QMOE_TRACE_AT(0, 1);
 
   // this warp's expert: its canonical weight slice, one load per group
   const int e = cta * e_per + warp;
@@ -93,6 +100,9 @@ __global__ void __launch_bounds__(kRouteSmallMaxE / kRouteSmallCtas * 32, 1)
   }
   if (cta == kRouteSmallCtas - 1)
     for (int i = threadIdx.x; i < n_zero_words; i += blockDim.x) zero_words[i] = 0;
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+  uint32_t ls_cta0;  // CTA 0's logits array in the cluster's shared window
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ls_cta0) : "r"(smem_u32(ls)), "r"(0));
   if (acc_zero) {
     const int n4 = T * (H / 4);
     for (int i = cta * blockDim.x + threadIdx.x; i < n4; i += kRouteSmallCtas * blockDim.x)
@@ -127,20 +137,20 @@ __global__ void __launch_bounds__(kRouteSmallMaxE / kRouteSmallCtas * 32, 1)
       float v = acc[tt];
 #pragma unroll
       for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, off);
-      if (lane == 0 && t0 + tt < T) logits[size_t(t0 + tt) * E + e] = bias ? __fadd_rn(v, be) : v;
+      if (lane == 0 && t0 + tt < T) {
+        const float lg = bias ? __fadd_rn(v, be) : v;
+        logits[size_t(t0 + tt) * E + e] = lg;
+        asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ls_cta0 + 4u * uint32_t((t0 + tt) * E + e)), "f"(lg)
+                     : "memory");
+      }
     }
   }
   __threadfence();
   cluster_sync_all();
+  if (threadIdx.x == 0) QMOE_TRACE_AT(0, 2);
   if (cta != 0) return;
 
-  // ---- CTA 0: selection ----
-  float* ls = reinterpret_cast<float*>(route_small_smem);           // [T][E]
-  int* idx_s = reinterpret_cast<int*>(ls + T * E);                   // [T*k]
-  float* w_s = reinterpret_cast<float*>(idx_s + T * k);              // [T*k]
-  for (int i = threadIdx.x; i < T * E; i += blockDim.x) ls[i] = __ldcg(logits + i);
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
-  __syncthreads();
+  // ---- CTA 0: selection (the logits are in its shared memory now) ----
   const int nwarps = blockDim.x >> 5;
   for (int t = warp; t < T; t += nwarps) select_topk_warp(ls + t * E, t, E, k, normalize, lane, nullptr, idx_s, w_s, hist);
   __syncthreads();
@@ -193,6 +203,7 @@ __global__ void __launch_bounds__(kRouteSmallMaxE / kRouteSmallCtas * 32, 1)
     row_w[pos] = w_s[p];
     slot_row[p] = pos;
   }
+  if (threadIdx.x == 0) QMOE_TRACE_AT(0, 3);
 }
 
 }  // namespace qmoe

@@ -76,20 +76,32 @@ __device__ __forceinline__ float warp_reduce_32_chains(const float* v, int lane)
 // expert index), L1 renormalisation of the picked probabilities; one warp.
 // Writes topk_idx/topk_w of token `tok`, optional logits, and counts the picks
 // into the shared histogram `hist`.
+// Order-preserving map of a finite float to an unsigned key (larger float ->
+// larger key; -0.0 maps like +0.0, as the float comparison treats them).
+__device__ __forceinline__ unsigned int float_order_key(float f) {
+  unsigned int u = __float_as_uint(f);
+  if (u == 0x80000000u) u = 0u;
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float float_from_order_key(unsigned int key) {
+  return __uint_as_float((key & 0x80000000u) ? (key & 0x7FFFFFFFu) : ~key);
+}
+
 __device__ __forceinline__ void select_topk_warp(const float* row, int tok, int E, int k, int normalize,
                                                  int lane, float* __restrict__ logits_out,
                                                  int32_t* __restrict__ topk_idx,
                                                  float* __restrict__ topk_w, int* hist) {
   const int per_lane = E / 32;  // <= 8
   float lv[8];
-  float m = -INFINITY;
+  unsigned int key[8];  // 0: no expert in this slot (below every finite logit's key)
+  unsigned int kmax = 0u;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     lv[i] = (i < per_lane) ? row[lane + 32 * i] : -INFINITY;
-    m = fmaxf(m, lv[i]);
+    key[i] = (i < per_lane) ? float_order_key(lv[i]) : 0u;
+    kmax = max(kmax, key[i]);
   }
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+  const float m = float_from_order_key(__reduce_max_sync(0xFFFFFFFFu, kmax));
   float ex[8];
   float s = 0.f;
 #pragma unroll
@@ -103,32 +115,24 @@ __device__ __forceinline__ void select_topk_warp(const float* row, int tok, int 
   if (logits_out) {
     for (int i = 0; i < per_lane; ++i) logits_out[size_t(tok) * E + lane + 32 * i] = lv[i];
   }
-  unsigned taken = 0u;  // bit i: expert lane + 32*i already chosen
+  // k rounds: the largest remaining logit (warp max of the keys), then the
+  // lowest expert index holding it (warp min) -- ties go to the lower index.
+  // A chosen expert's key is cleared to 0.
   float chosen_p = 0.f;  // lane j (< k) keeps the probability of pick j
   int chosen_e = 0;
   for (int j = 0; j < k; ++j) {
-    float bv = -INFINITY;
-    int be = 0x7FFFFFFF;
+    unsigned int lk = 0u;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      if (i < per_lane && !((taken >> i) & 1u)) {
-        const int ei = lane + 32 * i;
-        if (lv[i] > bv || (lv[i] == bv && ei < be)) {
-          bv = lv[i];
-          be = ei;
-        }
-      }
-    }
+    for (int i = 0; i < 8; ++i) lk = max(lk, key[i]);
+    const unsigned int bk = __reduce_max_sync(0xFFFFFFFFu, lk);
+    int li = 0x7FFFFFFF;
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) {
-      const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, off);
-      const int oe = __shfl_xor_sync(0xFFFFFFFFu, be, off);
-      if (ov > bv || (ov == bv && oe < be)) {
-        bv = ov;
-        be = oe;
-      }
-    }
-    if ((be & 31) == lane) taken |= 1u << (be >> 5);
+    for (int i = 7; i >= 0; --i)
+      if (key[i] == bk && bk != 0u) li = lane + 32 * i;
+    const int be = __reduce_min_sync(0xFFFFFFFFu, li);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (lane + 32 * i == be) key[i] = 0u;
     const int owner = be & 31;
     float mine = 0.f;
 #pragma unroll
@@ -168,8 +172,10 @@ __global__ void __launch_bounds__(router_warps<G>() * 32, 1)
   const int lane = threadIdx.x & 31;
   const int t0 = blockIdx.x * kRouterChunk;
   const int nt = min(kRouterChunk, T - t0);
+  if (threadIdx.x == 0) QMOE_TRACE_AT(0, 0);
   griddep_wait();
   griddep_launch_dependents();
+  if (threadIdx.x == 0) QMOE_TRACE_AT(0, 1);
 
   // Stage the chunk's activations in shared memory as fp32.  Inside each
   // 256-element group, element 8l+q is stored at (q/4)*128 + 4l + q%4 so the
@@ -265,6 +271,7 @@ __global__ void __launch_bounds__(router_warps<G>() * 32, 1)
     for (int e = threadIdx.x; e < E; e += kThreads)
       chunk_hist[size_t(blockIdx.x) * E + e] = hist[e];
   }
+  if (threadIdx.x == 0) QMOE_TRACE_AT(0, 3);
 }
 
 // ---------------------------------------------------------------------------

@@ -182,7 +182,8 @@ def _run_routed(x: torch.Tensor, w: MoEWeights, idx: torch.Tensor, tw: torch.Ten
         split = ops.gateup_split_workspace(x.device) if T * k <= ops.GATEUP_SPLIT_MAX_R else None
         act = ops.grouped_gemm_gateup_swiglu(x, w.gate_up, p["tiles"], p["max_tiles"], gather_rows=p["row_token"],
                                              split_ws=split)
-    ops.grouped_gemm_down_combine(act, w.down, p["tiles"], p["max_tiles"], p["row_token"], p["row_w"], acc)
+    ops.grouped_gemm_down_combine(act, w.down, p["tiles"], p["max_tiles"], p["row_token"], p["row_w"], acc,
+                                  tiles_ready=True)
     return ops.combine_finalize(acc, residual)
 
 
@@ -290,8 +291,9 @@ class MoEPlan:
                                                          p(self.act), p(self.split_ws), self._split_bytes, s),
                      "gate_up")
         mark(3)
+        # tiles come from the routing kernels, before the gate/up GEMM
         _C.check(lib.qmoe_grouped_gemm_down_combine(p(self.act), p(w.down), p(self.tiles), self.max_tiles,
-                                                    self.tile_rows, p(self.row_token), p(self.row_w), R, H, I, E,
+                                                    self.tile_rows, 1, p(self.row_token), p(self.row_w), R, H, I, E,
                                                     p(self.acc), T, s), "down")
         mark(4)
         _C.check(lib.qmoe_combine_finalize(p(self.acc), p(residual), T, H, p(out), s), "finalize")

@@ -187,9 +187,12 @@ def grouped_gemm_gateup_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, tiles: 
 
 def grouped_gemm_down_combine(act: torch.Tensor, w_down: torch.Tensor, tiles: torch.Tensor,
                               max_tiles_: int, row_dst: torch.Tensor, row_w: torch.Tensor,
-                              acc: torch.Tensor, max_tile_rows: int = 128) -> torch.Tensor:
+                              acc: torch.Tensor, max_tile_rows: int = 128,
+                              tiles_ready: bool = False) -> torch.Tensor:
     """K3b.  acc[row_dst[r]] += row_w[r] * act[r] @ W_down[e]^T (fp32, in place).
-    ``max_tile_rows`` as for grouped_gemm_gateup_swiglu."""
+    ``max_tile_rows`` as for grouped_gemm_gateup_swiglu.  ``tiles_ready``:
+    the tile list was complete before the previous kernel on the stream began
+    (QMOE_GEMM_TILES_READY), e.g. right after the gate/up GEMM on the same tiles."""
     _need(act, "act", torch.bfloat16, 2)
     _need(w_down, "w_down", torch.bfloat16, 3)
     _need(tiles, "tiles", torch.int32, 1)
@@ -203,7 +206,8 @@ def grouped_gemm_down_combine(act: torch.Tensor, w_down: torch.Tensor, tiles: to
     dev = act.device
     with torch.cuda.device(dev):
         _C.check(_C.lib().qmoe_grouped_gemm_down_combine(
-            _ptr(act), _ptr(w_down), _ptr(tiles), max_tiles_, max_tile_rows, _ptr(row_dst), _ptr(row_w),
+            _ptr(act), _ptr(w_down), _ptr(tiles), max_tiles_, max_tile_rows, 1 if tiles_ready else 0,
+            _ptr(row_dst), _ptr(row_w),
             R, H, I, E, _ptr(acc), acc.shape[0], _stream(dev)), "qmoe_grouped_gemm_down_combine")
     return acc
 

@@ -128,8 +128,10 @@ def test_small_tile_configuration(cuda_dev, oracle, T, gather):
         act = ops.grouped_gemm_gateup_swiglu(src["x"], wgu, p["tiles"], p["max_tiles"],
                                              gather_rows=src.get("gather_rows"), max_tile_rows=rows)
         acc = torch.zeros((T, H), dtype=torch.float32, device=cuda_dev)
+        # the small configuration also streams weights before its dependency
+        # wait (the tile list predates the gate/up launch)
         ops.grouped_gemm_down_combine(act, wd, p["tiles"], p["max_tiles"], p["row_token"], p["row_w"], acc,
-                                      max_tile_rows=rows)
+                                      max_tile_rows=rows, tiles_ready=rows < 128)
         outs.append((act, acc))
     torch.cuda.synchronize()
     assert _C.device_error() == 0
@@ -158,7 +160,7 @@ def test_small_tile_configuration_refuses_larger_tiles(cuda_dev):
     assert bool((act == 7.0).all())
     acc = torch.full((T, H), 5.0, dtype=torch.float32, device=cuda_dev)
     ops.grouped_gemm_down_combine(act, wd, p["tiles"], p["max_tiles"], p["row_token"], p["row_w"], acc,
-                                  max_tile_rows=16)
+                                  max_tile_rows=16, tiles_ready=True)
     torch.cuda.synchronize()
     assert _C.device_error() == 4
     assert bool((acc == 5.0).all())
