@@ -293,13 +293,14 @@ def run_ours(args):
         span_ms = e_start.elapsed_time(e_end)
         # stage pass: the same K steps again with an event between every
         # kernel, for the per-kernel durations (roofline) and the breakdown
-        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(args.steps)]
+        ns = len(plan.stages)
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(ns + 1)] for _ in range(args.steps)]
         barrier()
         for s_ in range(args.steps):
             plan.run(x, out, events=ev[s_])
         barrier()
         stage_ms = [statistics.mean(ev[s_][i].elapsed_time(ev[s_][i + 1]) for s_ in range(args.steps))
-                    for i in range(5)]
+                    for i in range(ns)]
         return span_ms, stage_ms
 
     if sampler:
@@ -324,9 +325,19 @@ def run_ours(args):
     U = int((counts > 0).sum().item())
     R = T * K_TOP
     hbm_gbs, tf_burst, tf_sust, peak_kind = load_peaks()
-    gate_up_bytes = U * GATE_UP_BYTES_PER_EXPERT + R * H * 2 + R * I_MOE * 2
-    gate_up_us = stage_ms[2] * 1e3
-    achieved = gate_up_bytes / (gate_up_us * 1e-6) / 1e9
+    if plan.fused:
+        # dominant kernel: gate/up + down in one persistent kernel.  Bytes:
+        # the hit experts' weights (9,437,184 B each), the permuted rows in,
+        # the SwiGLU activations out and back in, the fp32 combine rows.
+        kern_name = "moe_fused_kernel (gate/up + down)"
+        kern_bytes = (U * (GATE_UP_BYTES_PER_EXPERT + DOWN_BYTES_PER_EXPERT) + R * H * 2 + 2 * R * I_MOE * 2
+                      + T * H * 4)
+        kern_us = stage_ms[plan.stages.index("experts")] * 1e3
+    else:
+        kern_name = "grouped_gemm_kernel<gate_up>"
+        kern_bytes = U * GATE_UP_BYTES_PER_EXPERT + R * H * 2 + R * I_MOE * 2
+        kern_us = stage_ms[plan.stages.index("gate_up")] * 1e3
+    achieved = kern_bytes / (kern_us * 1e-6) / 1e9
     layer_bytes = U * (GATE_UP_BYTES_PER_EXPERT + DOWN_BYTES_PER_EXPERT) + E * H * 2 + 4 * T * H + 8 * T * K_TOP
     layer_gbs = layer_bytes / (ms_per_step * 1e-3) / 1e9
 
@@ -393,7 +404,7 @@ def run_ours(args):
     try:
         with open(os.path.join(REPO, "profiles", "ncu_traffic.json")) as f:
             tr = json.load(f)
-        ent = tr.get(f"gate_up_T{T}")
+        ent = tr.get(f"{'experts' if plan.fused else 'gate_up'}_T{T}")
         if ent:
             traffic = float(ent["dram_bytes_per_launch"])
     except Exception:
@@ -413,13 +424,13 @@ def run_ours(args):
                 "api": "Qwen3MoeSparseMoeBlock.forward(hidden_states)[0], pinned host in/out, "
                        "uploads and downloads on their own streams overlapping compute"},
         "gpu_launches": plan.launches_per_run * args.steps,
-        "stage_us": dict(zip(MoEPlan.STAGES, [round(s * 1e3, 2) for s in stage_ms])),
+        "stage_us": dict(zip(plan.stages, [round(s * 1e3, 2) for s in stage_ms])),
         "stage_note": "per-kernel CUDA-event times from a second pass of the K steps with an event "
                       "between every kernel; value uses events at the ends of the timed region only",
-        "roofline": {"bound": "hbm", "kernel": "grouped_gemm_kernel<gate_up>",
+        "roofline": {"bound": "hbm", "kernel": kern_name,
                      "achieved": achieved, "peak": hbm_gbs, "unit": "GB/s", "frac": achieved / hbm_gbs,
                      "peak_kind": peak_kind, "traffic": traffic,
-                     "algorithmic_bytes_per_launch": gate_up_bytes, "experts_hit": U},
+                     "algorithmic_bytes_per_launch": kern_bytes, "experts_hit": U},
         "layer_roofline": {"bound": "hbm", "achieved": layer_gbs, "peak": hbm_gbs, "unit": "GB/s",
                            "frac": layer_gbs / hbm_gbs, "algorithmic_bytes_per_step": layer_bytes},
         "clocks": clocks,
@@ -484,17 +495,18 @@ def run_extras(cfg, weights, dev, hbm_gbs, tf_burst):
         torch.cuda.synchronize()
         us = statistics.median(a.elapsed_time(b) for a, b in ev) * 1e3
         # the same layer without the graph, an event between stages
-        st = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(n)]
+        ns = len(plan.stages)
+        st = [[torch.cuda.Event(enable_timing=True) for _ in range(ns + 1)] for _ in range(n)]
         for i in range(n):
             flush.zero_()
             plan.run(x, out, events=st[i])
         torch.cuda.synchronize()
-        stage = [statistics.median(st[i][j].elapsed_time(st[i][j + 1]) for i in range(n)) * 1e3 for j in range(5)]
+        stage = [statistics.median(st[i][j].elapsed_time(st[i][j + 1]) for i in range(n)) * 1e3 for j in range(ns)]
         U = int((plan.counts.cpu() > 0).sum().item())
         byts = U * (GATE_UP_BYTES_PER_EXPERT + DOWN_BYTES_PER_EXPERT) + E * H * 2 + 4 * B * H + 8 * B * K_TOP
         dec[str(B)] = {"us_per_layer": round(us, 2), "tokens_per_s": B / (us * 1e-6),
                        "experts_hit": U, "hbm_frac": byts / (us * 1e-6) / 1e9 / hbm_gbs,
-                       "stage_us_eager": dict(zip(MoEPlan.STAGES, [round(v, 1) for v in stage]))}
+                       "stage_us_eager": dict(zip(plan.stages, [round(v, 1) for v in stage]))}
         del g
     del flush
     res["decode_moe_layer_cuda_graph"] = dec
@@ -514,19 +526,21 @@ def run_extras(cfg, weights, dev, hbm_gbs, tf_burst):
     e1.record()
     torch.cuda.synchronize()
     total_ms = e0.elapsed_time(e1) / 10
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(10)]
+    ns = len(plan.stages)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(ns + 1)] for _ in range(10)]
     torch.cuda.synchronize()
     for s in range(10):
         plan.run(x, out, events=ev[s])
     torch.cuda.synchronize()
-    stage = [statistics.mean(ev[s][i].elapsed_time(ev[s][i + 1]) for s in range(10)) for i in range(5)]
+    stage = [statistics.mean(ev[s][i].elapsed_time(ev[s][i + 1]) for s in range(10)) for i in range(ns)]
     counts = plan.counts.cpu()
     flops_gemm = T * 6 * K_TOP * H * I_MOE
+    gemm_ms = sum(v for name, v in zip(plan.stages, stage) if name in ("experts", "gate_up", "down"))
     res["cfg4_zipf_T16384"] = {
         "ms_per_layer": round(total_ms, 3), "tokens_per_s": T / (total_ms * 1e-3),
-        "stage_us": dict(zip(MoEPlan.STAGES, [round(v * 1e3, 1) for v in stage])),
-        "expert_gemm_tflops": flops_gemm / ((stage[2] + stage[3]) * 1e-3) / 1e12,
-        "tensor_frac": flops_gemm / ((stage[2] + stage[3]) * 1e-3) / 1e12 / tf_burst,
+        "stage_us": dict(zip(plan.stages, [round(v * 1e3, 1) for v in stage])),
+        "expert_gemm_tflops": flops_gemm / (gemm_ms * 1e-3) / 1e12,
+        "tensor_frac": flops_gemm / (gemm_ms * 1e-3) / 1e12 / tf_burst,
         "max_expert_rows": int(counts.max().item()), "mean_expert_rows": float(counts.float().mean().item()),
     }
     return res

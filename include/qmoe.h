@@ -108,6 +108,9 @@ QMOE_API int qmoe_router_topk(const void* x, const void* w_router, const float* 
  *   x_perm  (T*k, H)  bf16 out or NULL
  *   acc_zero (T, H)   fp32 or NULL: zero-filled here (the down-projection
  *                     accumulator of the fused forward)
+ *   zero_words (n_zero_words) int32 or NULL: zero-filled here (scratch that a
+ *                     later kernel needs zeroed, e.g. the done counters of
+ *                     qmoe_moe_experts)
  * Rows of one expert are ordered by ascending token id.  Bit-exact.
  * ---------------------------------------------------------------------- */
 QMOE_API int64_t qmoe_max_tiles(int64_t rows, int64_t E);
@@ -129,7 +132,7 @@ QMOE_API int qmoe_moe_permute(const int32_t* topk_idx, const float* topk_w, int3
                      const void* x, int64_t T, int64_t H, int64_t E, int64_t k,
                      int32_t* counts, int32_t* offsets, int32_t* row_token, float* row_w,
                      int32_t* slot_row, int32_t* tiles, void* x_perm, float* acc_zero,
-                     void* stream);
+                     int32_t* zero_words, int64_t n_zero_words, void* stream);
 
 /* ------------------------------------------------------------------------
  * K3a  grouped GEMM, gate/up projection fused with SiLU(gate)*up.
@@ -187,6 +190,26 @@ QMOE_API int qmoe_grouped_gemm_gateup_swiglu(const void* x, int64_t x_rows, cons
  * Requires H % 128 == 0, I % 64 == 0.
  * ---------------------------------------------------------------------- */
 #define QMOE_GEMM_TILES_READY 1
+/* ------------------------------------------------------------------------
+ * K3a + K3b in one persistent kernel, for prefill sizes: every gate/up unit
+ * then every down unit of the tiles, one CTA per SM; a CTA out of gate/up
+ * work starts down units (of tiles whose activations are complete) while
+ * others finish, so the two GEMMs leave no tail or start-up gap between them.
+ * Same results as qmoe_grouped_gemm_gateup_swiglu (x = x_perm) followed by
+ * qmoe_grouped_gemm_down_combine.
+ *   x_perm (R, H), w_gate_up (E, 2I, H), w_down (E, H, I) bf16; tiles /
+ *   max_tiles, row_dst, row_w as for those two; act (R, I) bf16 scratch (the
+ *   SwiGLU activations); acc (n_acc, H) fp32, accumulated into;
+ *   done    int32[max_tiles + 1] zero-filled before the call (e.g. by
+ *           qmoe_moe_permute's zero_words): per-tile counters and the unit
+ *           counter of the dynamic schedule; left non-zero.
+ * Requires H % 128 == 0, I % 128 == 0.
+ * ---------------------------------------------------------------------- */
+QMOE_API int qmoe_moe_experts(const void* x_perm, const void* w_gate_up, const void* w_down, const int32_t* tiles,
+                              int64_t max_tiles, const int32_t* row_dst, const float* row_w, int64_t R, int64_t H,
+                              int64_t I, int64_t E, void* act, float* acc, int64_t n_acc, int32_t* done,
+                              void* stream);
+
 QMOE_API int qmoe_grouped_gemm_down_combine(const void* act, const void* w_down, const int32_t* tiles,
                                    int64_t max_tiles, int64_t max_tile_rows, int64_t flags,
                                    const int32_t* row_dst,

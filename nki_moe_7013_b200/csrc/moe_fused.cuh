@@ -1,0 +1,419 @@
+// K3a + K3b in ONE persistent kernel (prefill sizes).
+//
+// The separate gate/up and down launches leave two gaps at a layer's core:
+// the gate/up grid's last partial wave (a 1024-token layer has ~5.3 waves of
+// 1 MB weight units: the last CTAs finish ~20 us after the median one), and
+// the down kernel's start-up after the whole gate/up grid has drained.  Here
+// the unit list is every gate/up unit (tile-major) followed by every down
+// unit (tile-major), run by one CTA per SM that draws units in order from a
+// global atomic counter: a CTA out of gate/up work moves straight on to down
+// units while others finish theirs, and the dynamic draw balances the unequal
+// units (a gate/up unit streams ~5x the bytes of a down unit, so a static deal
+// would leave the CTAs that drew an extra gate/up unit a unit behind).
+//
+// Dependency: down unit (tile t, feature block f) multiplies the activations
+// of tile t, which the n_mt_gu gate/up units of tile t write.  Each gate/up
+// unit's epilogue bumps done[t] after its stores (fenced); the producer of a
+// down unit waits (bounded) for done[t] == n_mt_gu before loading those
+// activation rows with TMA.  Deadlock-free: units are drawn in order, so a
+// down unit is drawn only after every gate/up unit has been drawn by a CTA
+// that is running it (gate/up units wait on nothing), and the grid (one CTA
+// per SM) is co-resident.
+// Down weights do not depend on anything, so the wait only gates the
+// activation loads of the unit's first stage.
+//
+// Pipeline, warp roles, TMEM double-buffering, swizzles and epilogues are
+// those of grouped_gemm_kernel (gate/up: two accumulators, SiLU(gate)*up;
+// down: weighted rows reduced into the fp32 combine accumulator).  The
+// producer draws each unit from the counter and passes it to the MMA and
+// epilogue warps through a small shared-memory queue (kUnitQueue slots, full
+// / empty mbarriers); -1 ends the stream.
+#pragma once
+
+#include "common.cuh"
+#include "grouped_gemm.cuh"
+
+namespace qmoe {
+
+struct FusedCfg {
+  static constexpr int kABytes = kBM * kBK * 2;              // 16 KB
+  static constexpr int kBBytes = kBNMax * kBK * 2;           // 16 KB
+  static constexpr int kStageBytes = 2 * kABytes + kBBytes;  // gate/up stage; a down stage uses A + B
+  static constexpr int kStages = 4;
+  static constexpr int kAccCols = 256;                       // gate [0,128) up [128,256); down [0,128)
+  static constexpr int kTmemCols = 512;
+  static constexpr int kBarrierBytes = 256;
+  static constexpr int kUnitQueue = 4;
+  static constexpr int kStagingBytes = 4 * 16 * 33 * 4 + 128 * 12;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes + kStagingBytes;
+};
+
+struct FusedArgs {
+  const int32_t* tiles;  // [0] = ntiles, then expert[max_tiles], row0[max_tiles], nrows[max_tiles]
+  int max_tiles;
+  int n_mt_gu, n_mt_dn;      // feature blocks: I / 128 and H / 128
+  int num_kb_gu, num_kb_dn;  // k blocks: H / 64 and I / 64
+  int a_rows_gu;             // 2I
+  int up_off;                // I
+  int a_rows_dn;             // H
+  __nv_bfloat16* act;        // (R, I)
+  int act_ld;
+  const int32_t* row_dst;
+  const float* row_w;
+  float* acc;
+  int acc_ld;
+  int n_acc;
+  int* done;  // [max_tiles + 1]: gate/up units finished per tile, then the unit
+              // counter; all zero on entry
+};
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait for a tile's activations; false (and a device error) on time-out.
+__device__ __forceinline__ bool wait_tile_done(const int* done, int target, volatile int* abort_flag) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (ld_acquire_gpu(done) < target) {
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      record_device_error(kDevErrWaitTimeoutProducer);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  // the activation rows were written through the generic proxy by other SMs;
+  // order them before this thread's TMA (async proxy) loads
+  asm volatile("fence.proxy.async;" ::: "memory");
+  return true;
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    moe_fused_kernel(const __grid_constant__ CUtensorMap tmA_gu, const __grid_constant__ CUtensorMap tmB_gu,
+                     const __grid_constant__ CUtensorMap tmA_dn, const __grid_constant__ CUtensorMap tmB_dn,
+                     const FusedArgs args) {
+  using C = FusedCfg;
+  extern __shared__ uint8_t fused_smem_raw[];
+  __shared__ int4 tile_cache[kTileCache];
+  __shared__ int tile_meta[2];
+  __shared__ int unit_q[FusedCfg::kUnitQueue];
+  __shared__ __align__(8) uint64_t uq_full[FusedCfg::kUnitQueue];
+  __shared__ __align__(8) uint64_t uq_empty[FusedCfg::kUnitQueue];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(fused_smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* acc_full = empty + C::kStages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;       // [2]
+  uint64_t* drain = acc_empty + 2;          // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* staging = reinterpret_cast<float*>(smem + C::kStages * C::kStageBytes + C::kBarrierBytes);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    QMOE_TRACE_AT(1, 0);
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    mbar_init(drain, 1);
+    for (int q = 0; q < C::kUnitQueue; ++q) {
+      mbar_init(&uq_full[q], 1);
+      mbar_init(&uq_empty[q], 2);  // the MMA issuer and the epilogue
+    }
+    *abort_flag = 0;
+    fence_mbarrier_init();
+    prefetch_tmap(&tmA_gu);
+    prefetch_tmap(&tmB_gu);
+    prefetch_tmap(&tmA_dn);
+    prefetch_tmap(&tmB_dn);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();
+  griddep_launch_dependents();
+  if (threadIdx.x == 0) QMOE_TRACE_AT(1, 1);
+
+  const TileView tv{args.tiles + 1, args.tiles + 1 + args.max_tiles, args.tiles + 1 + 2 * args.max_tiles, 0,
+                    tile_cache};
+  if (warp == 0) {
+    const int cnt = args.tiles[0];
+    int4 c = make_int4(0, 0, 0, 0);
+    if (lane < args.max_tiles) c = make_int4(tv.exp[lane], tv.row0[lane], tv.rows[lane], 0);
+    tile_cache[lane] = c;
+    if (lane == 0) tile_meta[0] = min(cnt, args.max_tiles);
+  }
+  __syncthreads();
+  const int ntiles = tile_meta[0];
+  const int units_gu = ntiles * args.n_mt_gu;
+  const int total_units = units_gu + ntiles * args.n_mt_dn;
+  // unit u -> (gate/up?, tile, feature block)
+  auto unit_of = [&](int u, bool& gu, int& tile, int& mt) {
+    gu = u < units_gu;
+    const int v = gu ? u : u - units_gu;
+    const int n = gu ? args.n_mt_gu : args.n_mt_dn;
+    tile = v / n;
+    mt = v - tile * n;
+  };
+
+  if (warp == 0) {
+    // ---------------- TMA producer (lane 0) ----------------
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_x = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      bool first = true;
+      int* counter = args.done + args.max_tiles;
+      for (int i = 0;; ++i) {
+        const int q = i % C::kUnitQueue;
+        if (!mbar_wait_bounded(&uq_empty[q], ((i / C::kUnitQueue) & 1) ^ 1u, abort_flag,
+                               kDevErrWaitTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        int u = ok ? atomicAdd(counter, 1) : -1;
+        if (u >= total_units) u = -1;
+        unit_q[q] = u;
+        mbar_arrive(&uq_full[q]);
+        if (u < 0) break;
+        bool gu;
+        int tile, mt;
+        unit_of(u, gu, tile, mt);
+        const int e = tv.expert(tile);
+        const int row0 = tv.first_row(tile);
+        const int nb = (tv.nrows(tile) + kBoxRows - 1) / kBoxRows;
+        if (!gu && !wait_tile_done(args.done + tile, args.n_mt_gu, abort_flag)) {
+          ok = false;
+          continue;  // the next slot carries the end marker
+        }
+        const CUtensorMap* ta = gu ? &tmA_gu : &tmA_dn;
+        const CUtensorMap* tb = gu ? &tmB_gu : &tmB_dn;
+        const int a_row = gu ? e * args.a_rows_gu + mt * kBM : e * args.a_rows_dn + mt * kBM;
+        const int nkb = gu ? args.num_kb_gu : args.num_kb_dn;
+        const uint32_t bytes = (gu ? 2 : 1) * C::kABytes + nb * kBoxRows * kBK * 2;
+        for (int kb = 0; kb < nkb; ++kb) {
+          uint8_t* sb = stages + stage * C::kStageBytes;
+          uint8_t* bs = sb + 2 * C::kABytes;
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, kDevErrWaitTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], bytes);
+          tma_load_2d_hint(sb, ta, kb * kBK, a_row, &full[stage], pol_w);
+          if (gu) tma_load_2d_hint(sb + C::kABytes, ta, kb * kBK, a_row + args.up_off, &full[stage], pol_w);
+          for (int b = 0; b < nb; ++b)
+            tma_load_2d_hint(bs + b * (kBoxRows * kBK * 2), tb, kb * kBK, row0 + b * kBoxRows, &full[stage],
+                             pol_x);
+          if (first) {
+            QMOE_TRACE_AT(1, 2);
+            first = false;
+          }
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        for (int s = 0; s < C::kStages; ++s) {
+          if ((issued_mask >> s) & 1u) {
+            const unsigned long long t0 = globaltimer_ns();
+            while (!mbar_try_wait(&full[s], (issued_parity >> s) & 1u)) {
+              if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int local = 0; ok; ++local) {
+        const int q = local % C::kUnitQueue;
+        if (!mbar_wait_bounded(&uq_full[q], (local / C::kUnitQueue) & 1, abort_flag, kDevErrWaitTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        const int u = unit_q[q];
+        mbar_arrive(&uq_empty[q]);
+        if (u < 0) break;
+        bool gu;
+        int tile, mt;
+        unit_of(u, gu, tile, mt);
+        const int nb = (tv.nrows(tile) + kBoxRows - 1) / kBoxRows;
+        const uint32_t idesc = make_idesc_bf16(kBM, nb * kBoxRows);
+        const int nkb = gu ? args.num_kb_gu : args.num_kb_dn;
+        const int buf = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait_bounded(&acc_empty[buf], acc_phase ^ 1u, abort_flag, kDevErrWaitTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d0 = tmem_base + buf * C::kAccCols;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait_bounded(&full[stage], phase, abort_flag, kDevErrWaitTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          if (local == 0 && kb == 0) QMOE_TRACE_AT(1, 3);
+          tc_fence_after();
+          const uint32_t sb = smem_u32(stages + stage * C::kStageBytes);
+          const uint32_t bsb = sb + 2 * C::kABytes;
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k) {
+            const uint32_t accum = (kb | k) != 0 ? 1u : 0u;
+            const uint64_t bdesc = make_sw128_desc(bsb + k * kUmmaK * 2);
+            umma_bf16(d0, make_sw128_desc(sb + k * kUmmaK * 2), bdesc, idesc, accum);
+            if (gu) umma_bf16(d0 + kBM, make_sw128_desc(sb + C::kABytes + k * kUmmaK * 2), bdesc, idesc, accum);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[buf]);
+      }
+      if (!ok) *abort_flag = 1;
+      QMOE_TRACE_AT(1, 4);
+      umma_commit(drain);
+      const unsigned long long t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain, 0)) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          record_device_error(kDevErrWaitTimeoutMma);
+          break;
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quad = warp & 3;
+    const int m = quad * 32 + lane;  // feature row inside the unit = TMEM lane
+    const int et = threadIdx.x - 64;
+    int32_t* meta_dst = reinterpret_cast<int32_t*>(staging + 4 * 16 * 33);
+    float* meta_w = reinterpret_cast<float*>(meta_dst + 128);
+    for (int local = 0;; ++local) {
+      const int q = local % C::kUnitQueue;
+      const bool got = mbar_wait_bounded(&uq_full[q], (local / C::kUnitQueue) & 1, abort_flag,
+                                         kDevErrWaitTimeoutEpilogue);
+      const int u = got ? unit_q[q] : -1;
+      // all four warps have the unit (or give up together) before the slot is released
+      if (named_barrier_or(1, 128, !got)) break;
+      if (et == 0) mbar_arrive(&uq_empty[q]);
+      if (u < 0) break;
+      bool gu;
+      int tile, mt;
+      unit_of(u, gu, tile, mt);
+      const int row0 = tv.first_row(tile);
+      const int nrows = tv.nrows(tile);
+      const int nb = (nrows + kBoxRows - 1) / kBoxRows;
+      const int buf = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      int my_dst = -1;
+      float my_w = 0.f;
+      if (!gu && et < nrows) {
+        my_dst = args.row_dst[row0 + et];
+        my_w = args.row_w[row0 + et];
+      }
+      const bool ok = mbar_wait_bounded(&acc_full[buf], acc_phase, abort_flag, kDevErrWaitTimeoutEpilogue);
+      if (named_barrier_or(1, 128, !ok)) break;
+      if (local == 0 && et == 0) QMOE_TRACE_AT(1, 5);
+      if (!gu) {
+        meta_dst[et] = (my_dst >= 0 && my_dst < args.n_acc) ? my_dst : -1;
+        meta_w[et] = my_w;
+        named_barrier_sync(1, 128);
+      }
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) + buf * C::kAccCols;
+      const int feat = mt * kBM + m;
+      for (int c = 0; c < nb; ++c) {
+        uint32_t v[16];
+        tmem_ld_32x32b_x16(taddr + c * 16, v);
+        if (gu) {
+          uint32_t up[16];
+          tmem_ld_32x32b_x16(taddr + kBM + c * 16, up);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int n = c * 16 + i;
+            if (n < nrows) {
+              const float g = __uint_as_float(v[i]);
+              const float h = g / (1.0f + __expf(-g)) * __uint_as_float(up[i]);
+              args.act[size_t(row0 + n) * args.act_ld + feat] = __float2bfloat16_rn(h);
+            }
+          }
+        } else {
+          tmem_ld_wait();
+          // transpose through shared memory: a lane then holds 4 consecutive
+          // features of one row, added with one 16-byte vector reduction
+          float* wsb = staging + (warp - 2) * (16 * 33);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) wsb[i * 33 + lane] = __uint_as_float(v[i]);
+          __syncwarp();
+          const int fq = (lane & 7) * 4;
+#pragma unroll
+          for (int it = 0; it < 4; ++it) {
+            const int i = it * 4 + (lane >> 3);
+            const int n = c * 16 + i;
+            if (n < nrows) {
+              const int dst = meta_dst[n];
+              if (dst >= 0) {
+                const float wv = meta_w[n];
+                red_add_v4_f32(args.acc + size_t(dst) * args.acc_ld + mt * kBM + quad * 32 + fq,
+                               wv * wsb[i * 33 + fq], wv * wsb[i * 33 + fq + 1], wv * wsb[i * 33 + fq + 2],
+                               wv * wsb[i * 33 + fq + 3]);
+              }
+            }
+          }
+          __syncwarp();
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
+      if (gu) {
+        // publish this unit's activation rows to the down units of the tile
+        asm volatile("fence.proxy.async;" ::: "memory");
+        __threadfence();
+        named_barrier_sync(1, 128);
+        if (et == 0) atomicAdd(args.done + tile, 1);
+      }
+    }
+    if (threadIdx.x == 64) QMOE_TRACE_AT(1, 6);
+  }
+
+  __syncthreads();
+  if (threadIdx.x == 0) QMOE_TRACE_AT(1, 7);
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+}  // namespace qmoe

@@ -20,6 +20,7 @@
 #include "ep_p2p.cuh"
 #include "finalize.cuh"
 #include "grouped_gemm.cuh"
+#include "moe_fused.cuh"
 #include "norm_rope.cuh"
 #include "permute.cuh"
 #include "route_small.cuh"
@@ -415,6 +416,43 @@ int launch_gemm_down(const void* act, const void* w_down, const int32_t* tiles, 
   return launch_gemm_cfg<qmoe::kModeDown, false>(tmA, tmB, a, grid, stream, "grouped_gemm_kernel<down>");
 }
 
+// Gate/up + down in one persistent kernel (prefill sizes, permuted rows).
+int launch_moe_fused(const void* x_perm, const void* w_gate_up, const void* w_down, const int32_t* tiles,
+                     int64_t max_tiles, const int32_t* row_dst, const float* row_w, int64_t R, int64_t H,
+                     int64_t I, int64_t E, void* act, float* acc, int64_t n_acc, int32_t* done,
+                     cudaStream_t stream) {
+  using C = qmoe::FusedCfg;
+  CUtensorMap ta_gu, tb_gu, ta_dn, tb_dn;
+  QMOE_CHECK(make_tmap_bf16(&ta_gu, w_gate_up, uint64_t(H), uint64_t(E * 2 * I), qmoe::kBK, qmoe::kBM));
+  QMOE_CHECK(make_tmap_bf16(&tb_gu, x_perm, uint64_t(H), uint64_t(R), qmoe::kBK, qmoe::kBoxRows));
+  QMOE_CHECK(make_tmap_bf16(&ta_dn, w_down, uint64_t(I), uint64_t(E * H), qmoe::kBK, qmoe::kBM));
+  QMOE_CHECK(make_tmap_bf16(&tb_dn, act, uint64_t(I), uint64_t(R), qmoe::kBK, qmoe::kBoxRows));
+  qmoe::FusedArgs a{};
+  a.tiles = tiles;
+  a.max_tiles = int(max_tiles);
+  a.n_mt_gu = int(I / qmoe::kBM);
+  a.n_mt_dn = int(H / qmoe::kBM);
+  a.num_kb_gu = int(H / qmoe::kBK);
+  a.num_kb_dn = int(I / qmoe::kBK);
+  a.a_rows_gu = int(2 * I);
+  a.up_off = int(I);
+  a.a_rows_dn = int(H);
+  a.act = static_cast<__nv_bfloat16*>(act);
+  a.act_ld = int(I);
+  a.row_dst = row_dst;
+  a.row_w = row_w;
+  a.acc = acc;
+  a.acc_ld = int(H);
+  a.n_acc = int(n_acc);
+  a.done = done;
+  const int64_t units = max_tiles * (a.n_mt_gu + a.n_mt_dn);
+  const int grid = int(std::min<int64_t>(units, num_sms(0)));
+  if (grid <= 0) return QMOE_OK;
+  QMOE_CHECK(set_smem(qmoe::moe_fused_kernel, C::kSmemBytes));
+  return launch_kernel(qmoe::moe_fused_kernel, dim3(grid), dim3(qmoe::kGemmThreads), C::kSmemBytes, stream, true,
+                       "moe_fused_kernel", ta_gu, tb_gu, ta_dn, tb_dn, a);
+}
+
 int launch_linear(const void* x, const void* w, int64_t T, int64_t K, int64_t N, void* out,
                   cudaStream_t stream) {
   using C = qmoe::GemmCfg<qmoe::kModePlain>;
@@ -451,7 +489,7 @@ int launch_finalize(const float* acc, const void* residual, int64_t T, int64_t H
 // Workspace carving for the fused forward.
 struct FwdLayout {
   size_t logits, chunk_hist, counts, offsets, row_token, row_w, slot_row, tiles, topk_idx, topk_w, x_perm,
-      act, acc, split, total;
+      act, acc, split, done, total;
 };
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -480,6 +518,7 @@ FwdLayout fwd_layout(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I) {
   L.act = take(2 * size_t(R * I));
   L.acc = take(sizeof(float) * size_t(T * H));
   L.split = take(T * k <= kGateUpSplitMaxR ? qmoe::kSplitWorkspaceBytes : 0);
+  L.done = take(T > kGatherMaxT ? sizeof(int32_t) * size_t(qmoe_max_tiles(R, E) + 1) : 0);
   L.total = o;
   return L;
 }
@@ -543,7 +582,10 @@ int qmoe_router_topk(const void* x, const void* w_router, const float* bias, int
 int qmoe_moe_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chunk_hist,
                      const void* x, int64_t T, int64_t H, int64_t E, int64_t k, int32_t* counts,
                      int32_t* offsets, int32_t* row_token, float* row_w, int32_t* slot_row,
-                     int32_t* tiles, void* x_perm, float* acc_zero, void* stream) {
+                     int32_t* tiles, void* x_perm, float* acc_zero, int32_t* zero_words, int64_t n_zero_words,
+                     void* stream) {
+  QMOE_REQUIRE(!zero_words == (n_zero_words == 0) && n_zero_words >= 0 && n_zero_words < (int64_t(1) << 24),
+               QMOE_ERR_INVALID_ARGUMENT, "permute: bad zero_words / n_zero_words");
   QMOE_REQUIRE(topk_idx && topk_w && chunk_hist && counts && offsets && row_token && row_w &&
                    slot_row && tiles,
                QMOE_ERR_INVALID_ARGUMENT, "permute: null pointer");
@@ -561,7 +603,8 @@ int qmoe_moe_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chun
   DeviceInfo* d = nullptr;
   QMOE_CHECK(device_info(&d));
   return launch_permute(topk_idx, topk_w, chunk_hist, x, T, H, E, k, counts, offsets, row_token,
-                        row_w, slot_row, tiles, x_perm, acc_zero, static_cast<cudaStream_t>(stream));
+                        row_w, slot_row, tiles, x_perm, acc_zero, static_cast<cudaStream_t>(stream), zero_words,
+                        int(n_zero_words));
 }
 
 int qmoe_route_small(const void* x, const void* w_router, const float* bias, int64_t T, int64_t H, int64_t E,
@@ -632,6 +675,28 @@ int qmoe_grouped_gemm_down_combine(const void* act, const void* w_down, const in
                           static_cast<cudaStream_t>(stream),
                           max_tile_rows >= 1 && max_tile_rows <= qmoe::kBNMax ? max_tile_rows : qmoe::kBNMax,
                           (flags & QMOE_GEMM_TILES_READY) ? qmoe::kGemmTilesReady : 0);
+}
+
+int qmoe_moe_experts(const void* x_perm, const void* w_gate_up, const void* w_down, const int32_t* tiles,
+                     int64_t max_tiles, const int32_t* row_dst, const float* row_w, int64_t R, int64_t H, int64_t I,
+                     int64_t E, void* act, float* acc, int64_t n_acc, int32_t* done, void* stream) {
+  QMOE_REQUIRE(x_perm && w_gate_up && w_down && tiles && row_dst && row_w && act && acc && done,
+               QMOE_ERR_INVALID_ARGUMENT, "moe_experts: null pointer");
+  QMOE_REQUIRE(R >= 0 && R < (int64_t(1) << 31), QMOE_ERR_INVALID_ARGUMENT, "moe_experts: bad R");
+  QMOE_REQUIRE(H > 0 && H % qmoe::kBM == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "moe_experts: H %% 128 != 0");
+  QMOE_REQUIRE(I > 0 && I % qmoe::kBM == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "moe_experts: I %% 128 != 0");
+  QMOE_REQUIRE(E > 0 && E * 2 * I < (int64_t(1) << 31) && E * H < (int64_t(1) << 31), QMOE_ERR_UNSUPPORTED_SHAPE,
+               "moe_experts: E too large");
+  QMOE_REQUIRE(n_acc >= 0 && n_acc * H < (int64_t(1) << 40), QMOE_ERR_INVALID_ARGUMENT, "moe_experts: bad n_acc");
+  QMOE_REQUIRE(max_tiles >= 0 && max_tiles < (int64_t(1) << 24), QMOE_ERR_INVALID_ARGUMENT,
+               "moe_experts: bad max_tiles");
+  QMOE_REQUIRE(aligned16(x_perm) && aligned16(w_gate_up) && aligned16(w_down) && aligned16(act), QMOE_ERR_MISALIGNED,
+               "moe_experts: pointers must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  if (R == 0) return QMOE_OK;
+  return launch_moe_fused(x_perm, w_gate_up, w_down, tiles, max_tiles, row_dst, row_w, R, H, I, E, act, acc, n_acc,
+                          done, static_cast<cudaStream_t>(stream));
 }
 
 int qmoe_combine_finalize(const float* acc, const void* residual, int64_t T, int64_t H, void* out,
@@ -1100,6 +1165,7 @@ int qmoe_moe_forward(const void* x, const void* w_router, const float* router_bi
   void* act = ws + L.act;
   float* acc = reinterpret_cast<float*>(ws + L.acc);
   float* split_ws = T * k <= kGateUpSplitMaxR ? reinterpret_cast<float*>(ws + L.split) : nullptr;
+  int32_t* done = x_perm ? reinterpret_cast<int32_t*>(ws + L.done) : nullptr;
   int32_t* split_counters = split_ws ? reinterpret_cast<int32_t*>(split_ws + size_t(qmoe::kSplitSlots) *
                                                                                qmoe::kSplitSlotFloats)
                                      : nullptr;
@@ -1118,21 +1184,24 @@ int qmoe_moe_forward(const void* x, const void* w_router, const float* router_bi
   } else {
     QMOE_CHECK(launch_router(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw,
                              chunk_hist, s));
-    // the permutation also zeroes the gate/up split counters (the workspace
-    // may hold anything on entry)
+    // the permutation also zeroes the gate/up split counters or the fused
+    // kernel's tile counters (the workspace may hold anything on entry)
+    int32_t* zero = x_perm ? done : split_counters;
+    const int n_zero = x_perm ? int(max_tiles + 1) : (split_counters ? qmoe::kSplitSlots : 0);
     QMOE_CHECK(launch_permute(idx, tw, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w,
-                              slot_row, tiles, x_perm, acc, s, split_counters,
-                              split_counters ? qmoe::kSplitSlots : 0));
+                              slot_row, tiles, x_perm, acc, s, zero, n_zero));
   }
-  if (x_perm)
-    QMOE_CHECK(launch_gemm_gateup(x_perm, R, nullptr, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s,
-                                  tile_rows));
-  else
+  if (x_perm) {
+    // prefill: gate/up and down in one persistent kernel
+    QMOE_CHECK(launch_moe_fused(x_perm, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, act,
+                                acc, T, done, s));
+  } else {
     QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s,
                                   tile_rows));
-  // the tile list comes from the routing kernels, before the gate/up GEMM
-  QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s, tile_rows,
-                              qmoe::kGemmTilesReady));
+    // the tile list comes from the routing kernels, before the gate/up GEMM
+    QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s,
+                                tile_rows, qmoe::kGemmTilesReady));
+  }
   return launch_finalize(acc, residual, T, H, out, s);
 }
 
@@ -1251,6 +1320,7 @@ extern "C" int qmoe_moe_forward_noalloc(const void* x, const void* w_router,
   void* act = ws + L.act;
   float* acc = reinterpret_cast<float*>(ws + L.acc);
   float* split_ws = T * k <= kGateUpSplitMaxR ? reinterpret_cast<float*>(ws + L.split) : nullptr;
+  int32_t* done = x_perm ? reinterpret_cast<int32_t*>(ws + L.done) : nullptr;
   int32_t* split_counters = split_ws ? reinterpret_cast<int32_t*>(split_ws + size_t(qmoe::kSplitSlots) *
                                                                                qmoe::kSplitSlotFloats)
                                      : nullptr;
@@ -1268,20 +1338,23 @@ extern "C" int qmoe_moe_forward_noalloc(const void* x, const void* w_router,
   } else {
     QMOE_CHECK(launch_router(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw,
                              chunk_hist, s));
-    // the permutation also zeroes the gate/up split counters (the workspace
-    // may hold anything on entry)
+    // the permutation also zeroes the gate/up split counters or the fused
+    // kernel's tile counters (the workspace may hold anything on entry)
+    int32_t* zero = x_perm ? done : split_counters;
+    const int n_zero = x_perm ? int(max_tiles + 1) : (split_counters ? qmoe::kSplitSlots : 0);
     QMOE_CHECK(launch_permute(idx, tw, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w,
-                              slot_row, tiles, x_perm, acc, s, split_counters,
-                              split_counters ? qmoe::kSplitSlots : 0));
+                              slot_row, tiles, x_perm, acc, s, zero, n_zero));
   }
-  if (x_perm)
-    QMOE_CHECK(launch_gemm_gateup(x_perm, R, nullptr, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s,
-                                  tile_rows));
-  else
+  if (x_perm) {
+    // prefill: gate/up and down in one persistent kernel
+    QMOE_CHECK(launch_moe_fused(x_perm, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, act,
+                                acc, T, done, s));
+  } else {
     QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s,
                                   tile_rows));
-  // the tile list comes from the routing kernels, before the gate/up GEMM
-  QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s, tile_rows,
-                              qmoe::kGemmTilesReady));
+    // the tile list comes from the routing kernels, before the gate/up GEMM
+    QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s,
+                                tile_rows, qmoe::kGemmTilesReady));
+  }
   return launch_finalize(acc, residual, T, H, out, s);
 }

@@ -176,7 +176,9 @@ def _run_routed(x: torch.Tensor, w: MoEWeights, idx: torch.Tensor, tw: torch.Ten
     acc = torch.empty((T, H), dtype=torch.float32, device=x.device)
     if T > ops.GATHER_MAX_T:
         p = ops.moe_permute(idx, tw, hist, E, x=x, gather=True, acc_zero=acc)
-        act = ops.grouped_gemm_gateup_swiglu(p["x_perm"], w.gate_up, p["tiles"], p["max_tiles"])
+        ops.moe_experts(p["x_perm"], w.gate_up, w.down, p["tiles"], p["max_tiles"], p["row_token"], p["row_w"],
+                        acc, p["done"])
+        return ops.combine_finalize(acc, residual)
     else:
         p = ops.moe_permute(idx, tw, hist, E, x=x, gather=False, acc_zero=acc)
         split = ops.gateup_split_workspace(x.device) if T * k <= ops.GATEUP_SPLIT_MAX_R else None
@@ -205,12 +207,14 @@ def blockwise_forward(hidden_states, expert_affinities_masked, token_position_to
 class MoEPlan:
     """Preallocated buffers + direct C-ABI launches for a fixed (T, H, E, k, I).
 
-    ``run(x, out, residual=None, events=None)``: when ``events`` is a list of 6
-    CUDA events, they are recorded before the router and after each of the
-    five stages (router, permute-scan+scatter, gate/up, down, finalize), on the
-    current stream."""
+    ``run(x, out, residual=None, events=None)``: when ``events`` is a list of
+    len(self.stages) + 1 CUDA events, they are recorded before the first
+    kernel and after each stage, on the current stream.  Stages: router,
+    permute (scan + scatter), gate_up, down, finalize; prefill sizes run
+    gate/up and down as one kernel ("experts")."""
 
     STAGES = ("router", "permute", "gate_up", "down", "finalize")
+    STAGES_FUSED = ("router", "permute", "experts", "finalize")
 
     def __init__(self, weights: MoEWeights, T: int, k: int, normalize: bool = True,
                  bias: Optional[torch.Tensor] = None):
@@ -242,6 +246,11 @@ class MoEPlan:
         # prefill sizes read a permuted copy of the rows; decode sizes gather
         self.x_perm = (torch.empty((max(R, 1), H), dtype=torch.bfloat16, device=dev)
                        if T > ops.GATHER_MAX_T else None)
+        # prefill sizes: gate/up and down run as one persistent kernel, whose
+        # per-tile counters the permutation zero-fills
+        self.fused = self.x_perm is not None
+        self.done = torch.zeros(self.max_tiles + 1, **i32) if self.fused else None
+        self.stages = self.STAGES_FUSED if self.fused else self.STAGES
         # small batches route through the logits + selection kernels
         self.logits = torch.empty((T, E), **f32) if T <= ops.ROUTER_SMALL_MAX_T else None
         # a token's k experts are distinct: no tile holds more than T rows
@@ -278,9 +287,18 @@ class MoEPlan:
             mark(1)
             _C.check(lib.qmoe_moe_permute(p(self.topk_idx), p(self.topk_w), p(self.hist), p(x), T, H, E, k,
                                           p(self.counts), p(self.offsets), p(self.row_token), p(self.row_w),
-                                          p(self.slot_row), p(self.tiles), p(self.x_perm), p(self.acc), s),
+                                          p(self.slot_row), p(self.tiles), p(self.x_perm), p(self.acc),
+                                          p(self.done), self.max_tiles + 1 if self.fused else 0, s),
                      "permute")
         mark(2)
+        if self.fused:
+            _C.check(lib.qmoe_moe_experts(p(self.x_perm), p(w.gate_up), p(w.down), p(self.tiles), self.max_tiles,
+                                          p(self.row_token), p(self.row_w), R, H, I, E, p(self.act), p(self.acc), T,
+                                          p(self.done), s), "experts")
+            mark(3)
+            _C.check(lib.qmoe_combine_finalize(p(self.acc), p(residual), T, H, p(out), s), "finalize")
+            mark(4)
+            return out
         if self.x_perm is not None:
             _C.check(lib.qmoe_grouped_gemm_gateup_swiglu(p(self.x_perm), R, None, p(w.gate_up), p(self.tiles),
                                                          self.max_tiles, self.tile_rows, R, H, I, E, p(self.act),
@@ -309,4 +327,6 @@ class MoEPlan:
         finalize."""
         if self.route_small:
             return 4
+        if self.fused:
+            return 5
         return (7 if self.T <= ops.ROUTER_SMALL_MAX_T else 6)

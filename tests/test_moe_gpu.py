@@ -166,6 +166,35 @@ def test_small_tile_configuration_refuses_larger_tiles(cuda_dev):
     assert bool((acc == 5.0).all())
 
 
+@pytest.mark.parametrize("T,H,E,k,I", [(65, 2048, 128, 8, 768), (1024, 2048, 128, 8, 768), (300, 512, 32, 8, 256),
+                                       (2048, 256, 64, 4, 128), (777, 1024, 256, 8, 384)])
+def test_moe_experts_fused_matches_separate_gemms(cuda_dev, oracle, T, H, E, k, I):
+    """The persistent gate/up -> down kernel gives the separate kernels'
+    activations bit for bit and the same combine (fp32 atomics: order only)."""
+    from nki_moe_7013_b200 import _C, ops
+
+    wr, wgu, wd = moe_weights(7, E, H, I, cuda_dev)
+    x = activations(70 + T, T, H, cuda_dev)
+    idx, w, hist = _routing(cuda_dev, x, wr, k)
+    acc_f = torch.empty((T, H), dtype=torch.float32, device=cuda_dev)
+    p = ops.moe_permute(idx, w, hist, E, x=x, gather=True, acc_zero=acc_f)
+    act_f = torch.empty((T * k, I), dtype=torch.bfloat16, device=cuda_dev)
+    ops.moe_experts(p["x_perm"], wgu, wd, p["tiles"], p["max_tiles"], p["row_token"], p["row_w"], acc_f,
+                    p["done"], act=act_f)
+    act = ops.grouped_gemm_gateup_swiglu(p["x_perm"], wgu, p["tiles"], p["max_tiles"])
+    acc = torch.zeros((T, H), dtype=torch.float32, device=cuda_dev)
+    ops.grouped_gemm_down_combine(act, wd, p["tiles"], p["max_tiles"], p["row_token"], p["row_w"], acc)
+    torch.cuda.synchronize()
+    assert _C.device_error() == 0
+    assert torch.equal(act_f, act)
+    assert max_rel_err(acc_f.cpu().numpy(), acc.cpu().numpy()) <= 1e-5
+    # every tile's counter reached the number of gate/up feature blocks
+    nt = int(p["tiles"][0])
+    assert bool((p["done"][:nt] == I // 128).all())
+    ref_out, _ = oracle.moe_block(x.cpu(), wr.cpu(), wgu.cpu(), wd.cpu(), k, return_intermediates=True)
+    assert max_rel_err(acc_f.cpu().numpy(), ref_out) <= MAX_REL
+
+
 @pytest.mark.parametrize("T", [1, 2, 8, 64, 128, 1024])
 def test_moe_forward_cfg0_shapes(cuda_dev, oracle, T):
     from nki_moe_7013_b200 import ops
