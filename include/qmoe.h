@@ -195,9 +195,12 @@ QMOE_API int qmoe_grouped_gemm_gateup_swiglu(const void* x, int64_t x_rows, cons
  * then every down unit of the tiles, one CTA per SM; a CTA out of gate/up
  * work starts down units (of tiles whose activations are complete) while
  * others finish, so the two GEMMs leave no tail or start-up gap between them.
- * Same results as qmoe_grouped_gemm_gateup_swiglu (x = x_perm) followed by
+ * Same results as qmoe_grouped_gemm_gateup_swiglu followed by
  * qmoe_grouped_gemm_down_combine.
- *   x_perm (R, H), w_gate_up (E, 2I, H), w_down (E, H, I) bf16; tiles /
+ *   x, x_rows, gather_rows   as for qmoe_grouped_gemm_gateup_swiglu: the
+ *           permuted rows (R, H), or the token rows (x_rows, H) gathered by
+ *           gather_rows (row_token) with TMA gather4 -- no permuted copy;
+ *   w_gate_up (E, 2I, H), w_down (E, H, I) bf16; tiles /
  *   max_tiles, row_dst, row_w as for those two; act (R, I) bf16 scratch (the
  *   SwiGLU activations); acc (n_acc, H) fp32, accumulated into;
  *   done    int32[max_tiles + 1] zero-filled before the call (e.g. by
@@ -205,10 +208,10 @@ QMOE_API int qmoe_grouped_gemm_gateup_swiglu(const void* x, int64_t x_rows, cons
  *           counter of the dynamic schedule; left non-zero.
  * Requires H % 128 == 0, I % 128 == 0.
  * ---------------------------------------------------------------------- */
-QMOE_API int qmoe_moe_experts(const void* x_perm, const void* w_gate_up, const void* w_down, const int32_t* tiles,
-                              int64_t max_tiles, const int32_t* row_dst, const float* row_w, int64_t R, int64_t H,
-                              int64_t I, int64_t E, void* act, float* acc, int64_t n_acc, int32_t* done,
-                              void* stream);
+QMOE_API int qmoe_moe_experts(const void* x, int64_t x_rows, const int32_t* gather_rows, const void* w_gate_up,
+                              const void* w_down, const int32_t* tiles, int64_t max_tiles, const int32_t* row_dst,
+                              const float* row_w, int64_t R, int64_t H, int64_t I, int64_t E, void* act, float* acc,
+                              int64_t n_acc, int32_t* done, void* stream);
 
 QMOE_API int qmoe_grouped_gemm_down_combine(const void* act, const void* w_down, const int32_t* tiles,
                                    int64_t max_tiles, int64_t max_tile_rows, int64_t flags,

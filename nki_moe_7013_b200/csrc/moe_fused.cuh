@@ -22,6 +22,9 @@
 // Down weights do not depend on anything, so the wait only gates the
 // activation loads of the unit's first stage.
 //
+// Gate/up rows come from the permuted copy of the tokens (16-row boxes) or
+// straight from the token rows (TMA gather4 by row_token; no copy to write).
+//
 // Pipeline, warp roles, TMEM double-buffering, swizzles and epilogues are
 // those of grouped_gemm_kernel (gate/up: two accumulators, SiLU(gate)*up;
 // down: weighted rows reduced into the fp32 combine accumulator).  The
@@ -65,6 +68,9 @@ struct FusedArgs {
   int n_acc;
   int* done;  // [max_tiles + 1]: gate/up units finished per tile, then the unit
               // counter; all zero on entry
+  // non-null: gate/up row r of a tile is token row gather_rows[r] of x (TMA
+  // gather4; tmB_gu maps x with 1-row boxes), else row r of the permuted copy
+  const int32_t* gather_rows;
 };
 
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
@@ -171,8 +177,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     mt = v - tile * n;
   };
 
-  if (warp == 0) {
-    // ---------------- TMA producer (lane 0) ----------------
+  if (warp == 0 && args.gather_rows == nullptr) {
+    // ---------------- TMA producer, permuted rows (lane 0 alone) ----------------
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
       const uint64_t pol_x = policy_evict_last();
@@ -242,6 +248,118 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             while (!mbar_try_wait(&full[s], (issued_parity >> s) & 1u)) {
               if (globaltimer_ns() - t0 > kWaitLimitNs) break;
             }
+          }
+        }
+      }
+    }
+  } else if (warp == 0) {
+    // ---------------- TMA producer, gathered rows (warp 0) ----------------
+    // Lane 0 draws units, waits on the ring and issues the weight loads (and
+    // the activation boxes of down units); for gate/up units each lane
+    // issues one gather4 of 4 token rows per stage.
+    const uint64_t pol_w = policy_evict_first();
+    const uint64_t pol_x = policy_evict_last();
+    const bool gather = args.gather_rows != nullptr;
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued_mask = 0, issued_parity = 0;
+    bool ok = true;
+    bool first = true;
+    int* counter = args.done + args.max_tiles;
+    for (int i = 0;; ++i) {
+      const int q = i % C::kUnitQueue;
+      int u = -1;
+      int got = 1;
+      if (lane == 0) {
+        if (!mbar_wait_bounded(&uq_empty[q], ((i / C::kUnitQueue) & 1) ^ 1u, abort_flag,
+                               kDevErrWaitTimeoutProducer)) {
+          got = 0;
+        } else {
+          u = ok ? atomicAdd(counter, 1) : -1;
+          if (u >= total_units) u = -1;
+          unit_q[q] = u;
+          mbar_arrive(&uq_full[q]);
+        }
+      }
+      got = __shfl_sync(0xFFFFFFFFu, got, 0);
+      u = __shfl_sync(0xFFFFFFFFu, u, 0);
+      if (!got) {
+        ok = false;
+        break;
+      }
+      if (u < 0) break;
+      bool gu;
+      int tile, mt;
+      unit_of(u, gu, tile, mt);
+      const int e = tv.expert(tile);
+      const int row0 = tv.first_row(tile);
+      const int nrows = tv.nrows(tile);
+      const int nb = (nrows + kBoxRows - 1) / kBoxRows;
+      if (!gu) {
+        int dep = 1;
+        if (lane == 0) dep = wait_tile_done(args.done + tile, args.n_mt_gu, abort_flag);
+        if (!__shfl_sync(0xFFFFFFFFu, dep, 0)) {
+          ok = false;
+          continue;  // the next slot carries the end marker
+        }
+      }
+      const bool g4 = gu && gather;
+      const int n_g4 = (nrows + 3) / 4;
+      int src[4] = {0, 0, 0, 0};
+      if (g4 && lane < n_g4) {
+        const int last = args.gather_rows[row0 + nrows - 1];  // filler for rows past the tile
+#pragma unroll
+        for (int r = 0; r < 4; ++r) src[r] = lane * 4 + r < nrows ? args.gather_rows[row0 + lane * 4 + r] : last;
+      }
+      const CUtensorMap* ta = gu ? &tmA_gu : &tmA_dn;
+      const CUtensorMap* tb = gu ? &tmB_gu : &tmB_dn;
+      const int a_row = gu ? e * args.a_rows_gu + mt * kBM : e * args.a_rows_dn + mt * kBM;
+      const int nkb = gu ? args.num_kb_gu : args.num_kb_dn;
+      const uint32_t bytes =
+          (gu ? 2 : 1) * C::kABytes + (g4 ? n_g4 * 4 * kBK * 2 : nb * kBoxRows * kBK * 2);
+      for (int kb = 0; kb < nkb; ++kb) {
+        uint8_t* sb = stages + stage * C::kStageBytes;
+        uint8_t* bs = sb + 2 * C::kABytes;
+        int w_ok = 1;
+        if (lane == 0) {
+          w_ok = mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, kDevErrWaitTimeoutProducer);
+          if (w_ok) {
+            mbar_arrive_expect_tx(&full[stage], bytes);
+            tma_load_2d_hint(sb, ta, kb * kBK, a_row, &full[stage], pol_w);
+            if (gu) tma_load_2d_hint(sb + C::kABytes, ta, kb * kBK, a_row + args.up_off, &full[stage], pol_w);
+            if (!g4)
+              for (int b = 0; b < nb; ++b)
+                tma_load_2d_hint(bs + b * (kBoxRows * kBK * 2), tb, kb * kBK, row0 + b * kBoxRows,
+                                 &full[stage], pol_x);
+            if (first) {
+              QMOE_TRACE_AT(1, 2);
+              first = false;
+            }
+          }
+        }
+        if (!__shfl_sync(0xFFFFFFFFu, w_ok, 0)) {
+          ok = false;
+          break;
+        }
+        // the expect_tx above precedes every gather's complete_tx
+        if (g4 && lane < n_g4)
+          tma_gather4_hint(bs + lane * 4 * (kBK * 2), tb, kb * kBK, src[0], src[1], src[2], src[3], &full[stage],
+                           pol_x);
+        issued_mask |= 1u << stage;
+        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+        if (++stage == C::kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    if (!ok && lane == 0) {
+      *abort_flag = 1;
+      for (int s = 0; s < C::kStages; ++s) {
+        if ((issued_mask >> s) & 1u) {
+          const unsigned long long t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full[s], (issued_parity >> s) & 1u)) {
+            if (globaltimer_ns() - t0 > kWaitLimitNs) break;
           }
         }
       }

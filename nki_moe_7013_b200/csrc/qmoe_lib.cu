@@ -188,6 +188,13 @@ constexpr int64_t kRouterSmallMaxT = 64;
 // more than it saves; for prefill, 16-row boxes of the copy feed the tensor
 // core faster than 4-row gathers.
 constexpr int64_t kGatherMaxT = 64;
+// Above kGatherMaxT tokens gate/up and down run as one persistent kernel
+// (moe_fused_kernel) on the permuted copy of the rows: measured on B200 the
+// copy plus 16-row boxes beats gathering token rows in the kernel (gather4,
+// 4 rows per instruction) from 256 tokens up, and ties below.  The kernel
+// keeps the gather form (qmoe_moe_experts with gather_rows) for callers
+// without a copy.
+constexpr int64_t kFusedGatherMaxT = kGatherMaxT;
 // Routed rows up to which the gate/up GEMM may split K (given a scratch), and
 // the most splits.  Splits pay when the units leave SMs idle: at one token
 // (8 rows) 48 units of a 148-SM B200 become 144.
@@ -416,15 +423,20 @@ int launch_gemm_down(const void* act, const void* w_down, const int32_t* tiles, 
   return launch_gemm_cfg<qmoe::kModeDown, false>(tmA, tmB, a, grid, stream, "grouped_gemm_kernel<down>");
 }
 
-// Gate/up + down in one persistent kernel (prefill sizes, permuted rows).
-int launch_moe_fused(const void* x_perm, const void* w_gate_up, const void* w_down, const int32_t* tiles,
-                     int64_t max_tiles, const int32_t* row_dst, const float* row_w, int64_t R, int64_t H,
-                     int64_t I, int64_t E, void* act, float* acc, int64_t n_acc, int32_t* done,
-                     cudaStream_t stream) {
+// Gate/up + down in one persistent kernel (prefill sizes).  x: the permuted
+// rows (R) when gather_rows is null, else the token rows (x_rows) gathered by
+// gather_rows[r].
+int launch_moe_fused(const void* x, int64_t x_rows, const int32_t* gather_rows, const void* w_gate_up,
+                     const void* w_down, const int32_t* tiles, int64_t max_tiles, const int32_t* row_dst,
+                     const float* row_w, int64_t R, int64_t H, int64_t I, int64_t E, void* act, float* acc,
+                     int64_t n_acc, int32_t* done, cudaStream_t stream) {
   using C = qmoe::FusedCfg;
   CUtensorMap ta_gu, tb_gu, ta_dn, tb_dn;
   QMOE_CHECK(make_tmap_bf16(&ta_gu, w_gate_up, uint64_t(H), uint64_t(E * 2 * I), qmoe::kBK, qmoe::kBM));
-  QMOE_CHECK(make_tmap_bf16(&tb_gu, x_perm, uint64_t(H), uint64_t(R), qmoe::kBK, qmoe::kBoxRows));
+  if (gather_rows)
+    QMOE_CHECK(make_tmap_bf16(&tb_gu, x, uint64_t(H), uint64_t(x_rows), qmoe::kBK, 1));
+  else
+    QMOE_CHECK(make_tmap_bf16(&tb_gu, x, uint64_t(H), uint64_t(R), qmoe::kBK, qmoe::kBoxRows));
   QMOE_CHECK(make_tmap_bf16(&ta_dn, w_down, uint64_t(I), uint64_t(E * H), qmoe::kBK, qmoe::kBM));
   QMOE_CHECK(make_tmap_bf16(&tb_dn, act, uint64_t(I), uint64_t(R), qmoe::kBK, qmoe::kBoxRows));
   qmoe::FusedArgs a{};
@@ -445,6 +457,7 @@ int launch_moe_fused(const void* x_perm, const void* w_gate_up, const void* w_do
   a.acc_ld = int(H);
   a.n_acc = int(n_acc);
   a.done = done;
+  a.gather_rows = gather_rows;
   const int64_t units = max_tiles * (a.n_mt_gu + a.n_mt_dn);
   const int grid = int(std::min<int64_t>(units, num_sms(0)));
   if (grid <= 0) return QMOE_OK;
@@ -514,7 +527,7 @@ FwdLayout fwd_layout(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I) {
   L.tiles = take(sizeof(int32_t) * size_t(1 + 3 * qmoe_max_tiles(R, E)));
   L.topk_idx = take(sizeof(int32_t) * size_t(R));
   L.topk_w = take(sizeof(float) * size_t(R));
-  L.x_perm = take(T > kGatherMaxT ? 2 * size_t(R * H) : 0);
+  L.x_perm = take(T > kFusedGatherMaxT ? 2 * size_t(R * H) : 0);
   L.act = take(2 * size_t(R * I));
   L.acc = take(sizeof(float) * size_t(T * H));
   L.split = take(T * k <= kGateUpSplitMaxR ? qmoe::kSplitWorkspaceBytes : 0);
@@ -677,12 +690,15 @@ int qmoe_grouped_gemm_down_combine(const void* act, const void* w_down, const in
                           (flags & QMOE_GEMM_TILES_READY) ? qmoe::kGemmTilesReady : 0);
 }
 
-int qmoe_moe_experts(const void* x_perm, const void* w_gate_up, const void* w_down, const int32_t* tiles,
-                     int64_t max_tiles, const int32_t* row_dst, const float* row_w, int64_t R, int64_t H, int64_t I,
-                     int64_t E, void* act, float* acc, int64_t n_acc, int32_t* done, void* stream) {
-  QMOE_REQUIRE(x_perm && w_gate_up && w_down && tiles && row_dst && row_w && act && acc && done,
+int qmoe_moe_experts(const void* x, int64_t x_rows, const int32_t* gather_rows, const void* w_gate_up,
+                     const void* w_down, const int32_t* tiles, int64_t max_tiles, const int32_t* row_dst,
+                     const float* row_w, int64_t R, int64_t H, int64_t I, int64_t E, void* act, float* acc,
+                     int64_t n_acc, int32_t* done, void* stream) {
+  QMOE_REQUIRE(x && w_gate_up && w_down && tiles && row_dst && row_w && act && acc && done,
                QMOE_ERR_INVALID_ARGUMENT, "moe_experts: null pointer");
   QMOE_REQUIRE(R >= 0 && R < (int64_t(1) << 31), QMOE_ERR_INVALID_ARGUMENT, "moe_experts: bad R");
+  QMOE_REQUIRE(!gather_rows || (x_rows > 0 && x_rows < (int64_t(1) << 31)), QMOE_ERR_INVALID_ARGUMENT,
+               "moe_experts: bad x_rows for a gather");
   QMOE_REQUIRE(H > 0 && H % qmoe::kBM == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "moe_experts: H %% 128 != 0");
   QMOE_REQUIRE(I > 0 && I % qmoe::kBM == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "moe_experts: I %% 128 != 0");
   QMOE_REQUIRE(E > 0 && E * 2 * I < (int64_t(1) << 31) && E * H < (int64_t(1) << 31), QMOE_ERR_UNSUPPORTED_SHAPE,
@@ -690,13 +706,13 @@ int qmoe_moe_experts(const void* x_perm, const void* w_gate_up, const void* w_do
   QMOE_REQUIRE(n_acc >= 0 && n_acc * H < (int64_t(1) << 40), QMOE_ERR_INVALID_ARGUMENT, "moe_experts: bad n_acc");
   QMOE_REQUIRE(max_tiles >= 0 && max_tiles < (int64_t(1) << 24), QMOE_ERR_INVALID_ARGUMENT,
                "moe_experts: bad max_tiles");
-  QMOE_REQUIRE(aligned16(x_perm) && aligned16(w_gate_up) && aligned16(w_down) && aligned16(act), QMOE_ERR_MISALIGNED,
+  QMOE_REQUIRE(aligned16(x) && aligned16(w_gate_up) && aligned16(w_down) && aligned16(act), QMOE_ERR_MISALIGNED,
                "moe_experts: pointers must be 16-byte aligned");
   DeviceInfo* d = nullptr;
   QMOE_CHECK(device_info(&d));
   if (R == 0) return QMOE_OK;
-  return launch_moe_fused(x_perm, w_gate_up, w_down, tiles, max_tiles, row_dst, row_w, R, H, I, E, act, acc, n_acc,
-                          done, static_cast<cudaStream_t>(stream));
+  return launch_moe_fused(x, x_rows, gather_rows, w_gate_up, w_down, tiles, max_tiles, row_dst, row_w, R, H, I, E,
+                          act, acc, n_acc, done, static_cast<cudaStream_t>(stream));
 }
 
 int qmoe_combine_finalize(const float* acc, const void* residual, int64_t T, int64_t H, void* out,
@@ -1161,11 +1177,12 @@ int qmoe_moe_forward(const void* x, const void* w_router, const float* router_bi
   int32_t* tiles = reinterpret_cast<int32_t*>(ws + L.tiles);
   int32_t* idx = topk_idx ? topk_idx : reinterpret_cast<int32_t*>(ws + L.topk_idx);
   float* tw = topk_w ? topk_w : reinterpret_cast<float*>(ws + L.topk_w);
-  void* x_perm = T > kGatherMaxT ? ws + L.x_perm : nullptr;
+  const bool fused = T > kGatherMaxT;
+  void* x_perm = T > kFusedGatherMaxT ? ws + L.x_perm : nullptr;
   void* act = ws + L.act;
   float* acc = reinterpret_cast<float*>(ws + L.acc);
   float* split_ws = T * k <= kGateUpSplitMaxR ? reinterpret_cast<float*>(ws + L.split) : nullptr;
-  int32_t* done = x_perm ? reinterpret_cast<int32_t*>(ws + L.done) : nullptr;
+  int32_t* done = fused ? reinterpret_cast<int32_t*>(ws + L.done) : nullptr;
   int32_t* split_counters = split_ws ? reinterpret_cast<int32_t*>(split_ws + size_t(qmoe::kSplitSlots) *
                                                                                qmoe::kSplitSlotFloats)
                                      : nullptr;
@@ -1186,15 +1203,19 @@ int qmoe_moe_forward(const void* x, const void* w_router, const float* router_bi
                              chunk_hist, s));
     // the permutation also zeroes the gate/up split counters or the fused
     // kernel's tile counters (the workspace may hold anything on entry)
-    int32_t* zero = x_perm ? done : split_counters;
-    const int n_zero = x_perm ? int(max_tiles + 1) : (split_counters ? qmoe::kSplitSlots : 0);
+    int32_t* zero = fused ? done : split_counters;
+    const int n_zero = fused ? int(max_tiles + 1) : (split_counters ? qmoe::kSplitSlots : 0);
     QMOE_CHECK(launch_permute(idx, tw, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w,
                               slot_row, tiles, x_perm, acc, s, zero, n_zero));
   }
-  if (x_perm) {
+  if (fused) {
     // prefill: gate/up and down in one persistent kernel
-    QMOE_CHECK(launch_moe_fused(x_perm, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, act,
-                                acc, T, done, s));
+    if (x_perm)
+      QMOE_CHECK(launch_moe_fused(x_perm, R, nullptr, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H,
+                                  I, E, act, acc, T, done, s));
+    else
+      QMOE_CHECK(launch_moe_fused(x, T, row_token, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H, I,
+                                  E, act, acc, T, done, s));
   } else {
     QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s,
                                   tile_rows));
@@ -1316,11 +1337,12 @@ extern "C" int qmoe_moe_forward_noalloc(const void* x, const void* w_router,
   int32_t* tiles = reinterpret_cast<int32_t*>(ws + L.tiles);
   int32_t* idx = topk_idx ? topk_idx : reinterpret_cast<int32_t*>(ws + L.topk_idx);
   float* tw = topk_w ? topk_w : reinterpret_cast<float*>(ws + L.topk_w);
-  void* x_perm = T > kGatherMaxT ? ws + L.x_perm : nullptr;
+  const bool fused = T > kGatherMaxT;
+  void* x_perm = T > kFusedGatherMaxT ? ws + L.x_perm : nullptr;
   void* act = ws + L.act;
   float* acc = reinterpret_cast<float*>(ws + L.acc);
   float* split_ws = T * k <= kGateUpSplitMaxR ? reinterpret_cast<float*>(ws + L.split) : nullptr;
-  int32_t* done = x_perm ? reinterpret_cast<int32_t*>(ws + L.done) : nullptr;
+  int32_t* done = fused ? reinterpret_cast<int32_t*>(ws + L.done) : nullptr;
   int32_t* split_counters = split_ws ? reinterpret_cast<int32_t*>(split_ws + size_t(qmoe::kSplitSlots) *
                                                                                qmoe::kSplitSlotFloats)
                                      : nullptr;
@@ -1340,15 +1362,19 @@ extern "C" int qmoe_moe_forward_noalloc(const void* x, const void* w_router,
                              chunk_hist, s));
     // the permutation also zeroes the gate/up split counters or the fused
     // kernel's tile counters (the workspace may hold anything on entry)
-    int32_t* zero = x_perm ? done : split_counters;
-    const int n_zero = x_perm ? int(max_tiles + 1) : (split_counters ? qmoe::kSplitSlots : 0);
+    int32_t* zero = fused ? done : split_counters;
+    const int n_zero = fused ? int(max_tiles + 1) : (split_counters ? qmoe::kSplitSlots : 0);
     QMOE_CHECK(launch_permute(idx, tw, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w,
                               slot_row, tiles, x_perm, acc, s, zero, n_zero));
   }
-  if (x_perm) {
+  if (fused) {
     // prefill: gate/up and down in one persistent kernel
-    QMOE_CHECK(launch_moe_fused(x_perm, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, act,
-                                acc, T, done, s));
+    if (x_perm)
+      QMOE_CHECK(launch_moe_fused(x_perm, R, nullptr, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H,
+                                  I, E, act, acc, T, done, s));
+    else
+      QMOE_CHECK(launch_moe_fused(x, T, row_token, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H, I,
+                                  E, act, acc, T, done, s));
   } else {
     QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s,
                                   tile_rows));

@@ -175,9 +175,14 @@ def _run_routed(x: torch.Tensor, w: MoEWeights, idx: torch.Tensor, tw: torch.Ten
     hist = ops.routing_histogram(idx, E)
     acc = torch.empty((T, H), dtype=torch.float32, device=x.device)
     if T > ops.GATHER_MAX_T:
-        p = ops.moe_permute(idx, tw, hist, E, x=x, gather=True, acc_zero=acc)
-        ops.moe_experts(p["x_perm"], w.gate_up, w.down, p["tiles"], p["max_tiles"], p["row_token"], p["row_w"],
-                        acc, p["done"])
+        copy = T > ops.FUSED_GATHER_MAX_T
+        p = ops.moe_permute(idx, tw, hist, E, x=x, gather=copy, acc_zero=acc)
+        if copy:
+            ops.moe_experts(p["x_perm"], w.gate_up, w.down, p["tiles"], p["max_tiles"], p["row_token"], p["row_w"],
+                            acc, p["done"])
+        else:
+            ops.moe_experts(x, w.gate_up, w.down, p["tiles"], p["max_tiles"], p["row_token"], p["row_w"], acc,
+                            p["done"], gather_rows=p["row_token"])
         return ops.combine_finalize(acc, residual)
     else:
         p = ops.moe_permute(idx, tw, hist, E, x=x, gather=False, acc_zero=acc)
@@ -217,7 +222,7 @@ class MoEPlan:
     STAGES_FUSED = ("router", "permute", "experts", "finalize")
 
     def __init__(self, weights: MoEWeights, T: int, k: int, normalize: bool = True,
-                 bias: Optional[torch.Tensor] = None):
+                 bias: Optional[torch.Tensor] = None, prefill_gather: Optional[bool] = None):
         self.w = weights
         self.T, self.k = T, k
         self.E, self.H, self.I = weights.router.shape[0], weights.hidden_size, weights.intermediate_size
@@ -244,11 +249,14 @@ class MoEPlan:
         self.act = torch.empty((max(R, 1), I), dtype=torch.bfloat16, device=dev)
         self.acc = torch.empty((max(T, 1), H), **f32)
         # prefill sizes read a permuted copy of the rows; decode sizes gather
-        self.x_perm = (torch.empty((max(R, 1), H), dtype=torch.bfloat16, device=dev)
-                       if T > ops.GATHER_MAX_T else None)
         # prefill sizes: gate/up and down run as one persistent kernel, whose
-        # per-tile counters the permutation zero-fills
-        self.fused = self.x_perm is not None
+        # per-tile counters the permutation zero-fills; its gate/up rows come
+        # from a permuted copy or (prefill_gather) straight from the tokens
+        self.fused = T > ops.GATHER_MAX_T
+        if prefill_gather is None:
+            prefill_gather = T <= ops.FUSED_GATHER_MAX_T
+        self.x_perm = (torch.empty((max(R, 1), H), dtype=torch.bfloat16, device=dev)
+                       if self.fused and not prefill_gather else None)
         self.done = torch.zeros(self.max_tiles + 1, **i32) if self.fused else None
         self.stages = self.STAGES_FUSED if self.fused else self.STAGES
         # small batches route through the logits + selection kernels
@@ -292,9 +300,13 @@ class MoEPlan:
                      "permute")
         mark(2)
         if self.fused:
-            _C.check(lib.qmoe_moe_experts(p(self.x_perm), p(w.gate_up), p(w.down), p(self.tiles), self.max_tiles,
-                                          p(self.row_token), p(self.row_w), R, H, I, E, p(self.act), p(self.acc), T,
-                                          p(self.done), s), "experts")
+            if self.x_perm is not None:
+                src, src_rows, gather = self.x_perm, R, None
+            else:
+                src, src_rows, gather = x, T, self.row_token
+            _C.check(lib.qmoe_moe_experts(p(src), src_rows, p(gather), p(w.gate_up), p(w.down), p(self.tiles),
+                                          self.max_tiles, p(self.row_token), p(self.row_w), R, H, I, E, p(self.act),
+                                          p(self.acc), T, p(self.done), s), "experts")
             mark(3)
             _C.check(lib.qmoe_combine_finalize(p(self.acc), p(residual), T, H, p(out), s), "finalize")
             mark(4)

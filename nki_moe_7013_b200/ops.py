@@ -16,6 +16,7 @@ from . import _C
 ROUTER_CHUNK = 8  # QMOE_ROUTER_CHUNK
 ROUTER_SMALL_MAX_T = 64  # batches up to this size take the two-kernel small-batch router
 GATHER_MAX_T = 64  # batches up to this size gather token rows inside the gate/up GEMM
+FUSED_GATHER_MAX_T = GATHER_MAX_T  # the fused experts kernel reads the permuted copy (faster from 256 tokens)
 GATEUP_SPLIT_MAX_R = 128  # routed rows up to which the gate/up GEMM may split K
 ROUTE_SMALL_MAX_T = 16  # batches up to this size (E <= 128) route + permute in one launch
 ROUTE_SMALL_MAX_E = 128
@@ -111,9 +112,8 @@ def route_small(x: torch.Tensor, w_router: torch.Tensor, k: int, normalize: bool
 def moe_permute(topk_idx: torch.Tensor, topk_w: torch.Tensor, chunk_hist: torch.Tensor,
                 num_experts: int, x: Optional[torch.Tensor] = None, gather: bool = True,
                 acc_zero: Optional[torch.Tensor] = None):
-    """K2.  ``chunk_hist`` is overwritten.  Returns a dict of device tensors;
-    with a permuted copy (``gather``) also ``done``, the zero-filled tile
-    counters moe_experts needs."""
+    """K2.  ``chunk_hist`` is overwritten.  Returns a dict of device tensors,
+    among them ``done``: the zero-filled counters moe_experts needs."""
     _need(topk_idx, "topk_idx", torch.int32, 2)
     _need(topk_w, "topk_w", torch.float32, 2)
     _need(chunk_hist, "chunk_hist", torch.int32, 2)
@@ -138,41 +138,49 @@ def moe_permute(topk_idx: torch.Tensor, topk_w: torch.Tensor, chunk_hist: torch.
     row_w = torch.empty(R, dtype=torch.float32, device=dev)
     slot_row = torch.empty((T, k), dtype=torch.int32, device=dev)
     tiles = torch.empty(1 + 3 * mt, dtype=torch.int32, device=dev)
-    done = torch.empty(mt + 1, dtype=torch.int32, device=dev) if x_perm is not None else None
+    done = torch.empty(mt + 1, dtype=torch.int32, device=dev)
     with torch.cuda.device(dev):
         _C.check(_C.lib().qmoe_moe_permute(
             _ptr(topk_idx), _ptr(topk_w), _ptr(chunk_hist), _ptr(x), T, H, E, k,
             _ptr(counts), _ptr(offsets), _ptr(row_token), _ptr(row_w), _ptr(slot_row),
-            _ptr(tiles), _ptr(x_perm), _ptr(acc_zero), _ptr(done), 0 if done is None else mt + 1,
+            _ptr(tiles), _ptr(x_perm), _ptr(acc_zero), _ptr(done), mt + 1,
             _stream(dev)), "qmoe_moe_permute")
     return dict(counts=counts, offsets=offsets, row_token=row_token, row_w=row_w,
                 slot_row=slot_row, tiles=tiles, max_tiles=mt, x_perm=x_perm, done=done)
 
 
-def moe_experts(x_perm: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor, tiles: torch.Tensor,
+def moe_experts(x: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor, tiles: torch.Tensor,
                 max_tiles_: int, row_dst: torch.Tensor, row_w: torch.Tensor, acc: torch.Tensor,
-                done: torch.Tensor, act: Optional[torch.Tensor] = None) -> torch.Tensor:
+                done: torch.Tensor, act: Optional[torch.Tensor] = None,
+                gather_rows: Optional[torch.Tensor] = None) -> torch.Tensor:
     """K3a + K3b in one persistent kernel (prefill): acc[row_dst[r]] +=
-    row_w[r] * SwiGLU(x_perm[r]) @ W_down[e]^T.  ``done`` (max_tiles + 1,)
-    int32 must be zero-filled (moe_permute's ``done``).  Returns acc."""
-    _need(x_perm, "x_perm", torch.bfloat16, 2)
+    row_w[r] * SwiGLU(x_r) @ W_down[e]^T, x_r = x_perm[r] (``x`` = the
+    permuted rows) or x[gather_rows[r]] (``x`` = the token rows).  ``done``
+    (max_tiles + 1,) int32 must be zero-filled (moe_permute's ``done``).
+    Returns acc."""
+    _need(x, "x", torch.bfloat16, 2)
     _need(w_gate_up, "w_gate_up", torch.bfloat16, 3)
     _need(w_down, "w_down", torch.bfloat16, 3)
     _need(tiles, "tiles", torch.int32, 1)
     _need(acc, "acc", torch.float32, 2)
     _need(done, "done", torch.int32, 1)
-    R, H = x_perm.shape
+    rows, H = x.shape
+    R = rows
+    if gather_rows is not None:
+        _need(gather_rows, "gather_rows", torch.int32, 1)
+        R = gather_rows.shape[0]
     E, I2, H2 = w_gate_up.shape
     I = I2 // 2
     if H2 != H or tuple(w_down.shape) != (E, H, I) or acc.shape[1] != H:
         raise ValueError("moe_experts: weight / activation shapes do not match")
-    dev = x_perm.device
+    dev = x.device
     if act is None:
         act = torch.empty((max(R, 1), I), dtype=torch.bfloat16, device=dev)
     with torch.cuda.device(dev):
         _C.check(_C.lib().qmoe_moe_experts(
-            _ptr(x_perm), _ptr(w_gate_up), _ptr(w_down), _ptr(tiles), max_tiles_, _ptr(row_dst), _ptr(row_w),
-            R, H, I, E, _ptr(act), _ptr(acc), acc.shape[0], _ptr(done), _stream(dev)), "qmoe_moe_experts")
+            _ptr(x), rows, _ptr(gather_rows), _ptr(w_gate_up), _ptr(w_down), _ptr(tiles), max_tiles_,
+            _ptr(row_dst), _ptr(row_w), R, H, I, E, _ptr(act), _ptr(acc), acc.shape[0], _ptr(done), _stream(dev)),
+            "qmoe_moe_experts")
     return acc
 
 

@@ -184,10 +184,18 @@ def test_moe_experts_fused_matches_separate_gemms(cuda_dev, oracle, T, H, E, k, 
     act = ops.grouped_gemm_gateup_swiglu(p["x_perm"], wgu, p["tiles"], p["max_tiles"])
     acc = torch.zeros((T, H), dtype=torch.float32, device=cuda_dev)
     ops.grouped_gemm_down_combine(act, wd, p["tiles"], p["max_tiles"], p["row_token"], p["row_w"], acc)
+    # the same kernel gathering token rows itself (no permuted copy)
+    done_g = torch.zeros_like(p["done"])
+    acc_g = torch.zeros((T, H), dtype=torch.float32, device=cuda_dev)
+    act_g = torch.empty_like(act_f)
+    ops.moe_experts(x, wgu, wd, p["tiles"], p["max_tiles"], p["row_token"], p["row_w"], acc_g, done_g, act=act_g,
+                    gather_rows=p["row_token"])
     torch.cuda.synchronize()
     assert _C.device_error() == 0
     assert torch.equal(act_f, act)
+    assert torch.equal(act_g, act)
     assert max_rel_err(acc_f.cpu().numpy(), acc.cpu().numpy()) <= 1e-5
+    assert max_rel_err(acc_g.cpu().numpy(), acc.cpu().numpy()) <= 1e-5
     # every tile's counter reached the number of gate/up feature blocks
     nt = int(p["tiles"][0])
     assert bool((p["done"][:nt] == I // 128).all())
