@@ -222,7 +222,8 @@ class MoEPlan:
     STAGES_FUSED = ("router", "permute", "experts", "finalize")
 
     def __init__(self, weights: MoEWeights, T: int, k: int, normalize: bool = True,
-                 bias: Optional[torch.Tensor] = None, prefill_gather: Optional[bool] = None):
+                 bias: Optional[torch.Tensor] = None, prefill_gather: Optional[bool] = None,
+                 fused: Optional[bool] = None):
         self.w = weights
         self.T, self.k = T, k
         self.E, self.H, self.I = weights.router.shape[0], weights.hidden_size, weights.intermediate_size
@@ -252,11 +253,11 @@ class MoEPlan:
         # prefill sizes: gate/up and down run as one persistent kernel, whose
         # per-tile counters the permutation zero-fills; its gate/up rows come
         # from a permuted copy or (prefill_gather) straight from the tokens
-        self.fused = T > ops.GATHER_MAX_T
+        self.fused = T > ops.GATHER_MAX_T if fused is None else (bool(fused) and T > ops.GATHER_MAX_T)
         if prefill_gather is None:
             prefill_gather = T <= ops.FUSED_GATHER_MAX_T
         self.x_perm = (torch.empty((max(R, 1), H), dtype=torch.bfloat16, device=dev)
-                       if self.fused and not prefill_gather else None)
+                       if T > ops.GATHER_MAX_T and not (self.fused and prefill_gather) else None)
         self.done = torch.zeros(self.max_tiles + 1, **i32) if self.fused else None
         self.stages = self.STAGES_FUSED if self.fused else self.STAGES
         # small batches route through the logits + selection kernels
