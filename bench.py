@@ -510,6 +510,7 @@ def run_extras(cfg, weights, dev, hbm_gbs, tf_burst):
         del g
     del flush
     res["decode_moe_layer_cuda_graph"] = dec
+    res["decode_step_cfg2"] = run_decode_model(cfg, dev, hbm_gbs)
 
     T = 16384
     bias = zipf_expert_bias(0, E).to(dev)
@@ -544,6 +545,49 @@ def run_extras(cfg, weights, dev, hbm_gbs, tf_burst):
         "max_expert_rows": int(counts.max().item()), "mean_expert_rows": float(counts.float().mean().item()),
     }
     return res
+
+
+def run_decode_model(cfg, dev, hbm_gbs, batches=(1, 8, 32, 64), context=4096):
+    """Config 2: the 48-layer model (random weights ~N(0,0.02), vocab 151,936)
+    decoding one token per sequence per step with 4,096 cached tokens per
+    sequence (~N(0,1)); the whole step (embedding, 48 layers, final norm, LM
+    head, greedy pick) replays as one CUDA graph.  60 GB of weights: no step
+    finds its weights in L2."""
+    import torch
+
+    from nki_moe_7013_b200.model import DecodeSession, Qwen3MoeModel
+
+    model = Qwen3MoeModel(cfg, device=dev, seed=1)
+    nl, V = len(model.layers), model.vocab_size
+    attn_bytes = sum(l.self_attn.w.wqkv.numel() + l.self_attn.w.wo.numel() for l in model.layers) * 2
+    out = {}
+    for B in batches:
+        sess = DecodeSession(model, B, context=context, max_new=64, seed=B)
+        sess.capture()
+        for _ in range(2):
+            sess.step()
+        torch.cuda.synchronize()
+        n = 10
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            sess.step()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / n
+        U = sum(int((p.counts > 0).sum().item()) for p in sess.plans)
+        kv_len = context + sess.steps_done
+        byts = (U * (GATE_UP_BYTES_PER_EXPERT + DOWN_BYTES_PER_EXPERT) + nl * E * H * 2 + attn_bytes
+                + V * H * 2 + nl * B * cfg.num_key_value_heads * kv_len * cfg.head_dim * 2 * 2)
+        out[str(B)] = {"ms_per_step": round(ms, 3), "tokens_per_s": B / (ms * 1e-3),
+                       "experts_hit_per_layer": round(U / nl, 1), "hbm_bytes_per_step": byts,
+                       "hbm_frac": byts / (ms * 1e-3) / 1e9 / hbm_gbs}
+        sess.release()
+        del sess
+        torch.cuda.empty_cache()
+    return {"layers": nl, "vocab": V, "context": context, "per_batch": out,
+            "note": "one CUDA graph per step: embedding, 48 x (norm, QKV, QK-norm+RoPE+append, split-KV "
+                    "attention, O proj, add&norm, MoE), final norm, LM head, greedy pick"}
 
 
 def run_ours_ep(args):

@@ -249,6 +249,14 @@ QMOE_API int qmoe_combine_finalize(const float* acc, const void* residual, int64
                           void* out, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Token embedding lookup: out[i, :] = table[ids[i], :], table (V, H) bf16.
+ * Replaces the reference's embedding kernel (qwen_with_nki.py:1541-1578).
+ * An id outside [0, V) yields a zero row and device error 4.  H % 8 == 0.
+ * ---------------------------------------------------------------------- */
+QMOE_API int qmoe_embedding_gather(const void* table, int64_t V, int64_t H, const int32_t* ids, int64_t n,
+                                   void* out, void* stream);
+
+/* ------------------------------------------------------------------------
  * Fused sparse-MoE block forward: K1 -> K2 -> K3a -> K3b -> finalize.
  * Replaces the module call self.mlp(hidden_states, padding_mask)[0]
  * (qwen.py:429) for the routed-expert MoE of Qwen3.

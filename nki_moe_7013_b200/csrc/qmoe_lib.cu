@@ -715,6 +715,23 @@ int qmoe_moe_experts(const void* x, int64_t x_rows, const int32_t* gather_rows, 
                           act, acc, n_acc, done, static_cast<cudaStream_t>(stream));
 }
 
+int qmoe_embedding_gather(const void* table, int64_t V, int64_t H, const int32_t* ids, int64_t n, void* out,
+                          void* stream) {
+  QMOE_REQUIRE(table && ids && out, QMOE_ERR_INVALID_ARGUMENT, "embedding: null pointer");
+  QMOE_REQUIRE(V > 0 && V < (int64_t(1) << 31) && n >= 0 && n < (int64_t(1) << 31), QMOE_ERR_INVALID_ARGUMENT,
+               "embedding: bad V or n");
+  QMOE_REQUIRE(H > 0 && H % 8 == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "embedding: H %% 8 != 0");
+  QMOE_REQUIRE(aligned16(table) && aligned16(out), QMOE_ERR_MISALIGNED, "embedding: pointers must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  if (n == 0) return QMOE_OK;
+  const long long total = (long long)n * (H / 8);
+  const int grid = int(std::min<long long>((total + 255) / 256, (long long)d->sms * 8));
+  return launch_kernel(qmoe::embedding_gather_kernel, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                       true, "embedding_gather_kernel", static_cast<const uint4*>(table), ids, int(n), int(V),
+                       int(H / 8), static_cast<uint4*>(out));
+}
+
 int qmoe_combine_finalize(const float* acc, const void* residual, int64_t T, int64_t H, void* out,
                           void* stream) {
   QMOE_REQUIRE(acc && out, QMOE_ERR_INVALID_ARGUMENT, "finalize: null pointer");

@@ -1,0 +1,156 @@
+"""Qwen3-MoE decoder stack and its decode step (config 2).
+
+``Qwen3MoeModel`` is the reference model's forward (qwen.py:439-477):
+token embedding -> ``num_hidden_layers`` decoder layers -> final RMSNorm ->
+LM head, with the embedding lookup and the LM head on this library's kernels
+(they replace the reference's NKI embedding and LM-head kernels,
+qwen_with_nki.py:1541-1578 and 1766-1805).  ``forward`` is the eager module
+path (host-side cache lengths, any number of new tokens).
+
+``DecodeSession`` runs B sequences one token per step with static shapes:
+positions, cache lengths and the next tokens live on the device and advance
+on the device, so a whole step -- 48 layers of RMSNorm, QKV projection, QK
+norm + RoPE + cache append, split-KV decode attention, O projection, add &
+norm, the MoE block, then the final norm, the LM head and a greedy pick --
+captures into one CUDA graph and replays without the host.
+"""
+from __future__ import annotations
+
+from typing import List, Optional
+
+import torch
+
+from . import ops
+from .attention import KVCache
+from .config import Qwen3MoeConfig
+from .decoder import Qwen3MoeDecoderLayer
+from .moe import MoEPlan
+
+
+class Qwen3MoeModel:
+    def __init__(self, cfg: Qwen3MoeConfig, num_layers: Optional[int] = None, vocab_size: Optional[int] = None,
+                 device="cuda", seed: int = 0, std: float = 0.02):
+        from .synth import normal_bf16_device
+
+        self.cfg = cfg
+        self.device = torch.device(device)
+        L = cfg.num_hidden_layers if num_layers is None else num_layers
+        V = cfg.vocab_size if vocab_size is None else vocab_size
+        H = cfg.hidden_size
+        self.vocab_size = V
+        self.embed = normal_bf16_device(seed * 1000 + 1, (V, H), std, self.device)
+        self.layers: List[Qwen3MoeDecoderLayer] = [
+            Qwen3MoeDecoderLayer(cfg, layer_idx=l, device=self.device, seed=seed * 1000 + 10 + l) for l in range(L)]
+        g = torch.Generator(device=self.device)
+        g.manual_seed(seed * 1000 + 3)
+        self.norm = (1.0 + 0.1 * torch.randn(H, generator=g, device=self.device)).float().contiguous()
+        self.lm_head = normal_bf16_device(seed * 1000 + 2, (V, H), std, self.device)
+
+    def new_caches(self, n_slots: int, max_seq: int) -> List[KVCache]:
+        return [layer.self_attn.new_cache(n_slots, max_seq) for layer in self.layers]
+
+    def forward(self, input_ids: torch.Tensor, past_key_values: Optional[List[KVCache]] = None):
+        """input_ids (B, S) -> (logits (B, S, V) bf16, caches); the eager path
+        through the decoder-layer modules."""
+        B, S = input_ids.shape
+        H = self.cfg.hidden_size
+        caches = past_key_values if past_key_values is not None else self.new_caches(B, S)
+        x = ops.embedding(input_ids.reshape(-1).to(torch.int32).contiguous(), self.embed).reshape(B, S, H)
+        for layer, cache in zip(self.layers, caches):
+            x = layer(x, past_key_value=cache)[0]
+        h = ops.rmsnorm(x.reshape(B * S, H), self.norm, self.cfg.rms_norm_eps)
+        logits = ops.linear(h, self.lm_head)
+        return logits.reshape(B, S, self.vocab_size), caches
+
+
+class DecodeSession:
+    """B sequences, one new token each per ``step()``, static shapes.
+
+    The caches hold ``context`` tokens per sequence on entry (config 2 fills
+    them with ~N(0,1) values) and room for ``max_new`` more.  ``tokens`` (B,)
+    int32 on the device is the input of the next step and is overwritten with
+    its greedy output; ``logits`` (B, V) bf16 holds the last step's logits."""
+
+    def __init__(self, model: Qwen3MoeModel, batch: int, context: int, max_new: int, seed: int = 0,
+                 fill_random: bool = True):
+        cfg = model.cfg
+        dev = model.device
+        self.model = model
+        self.B = batch
+        self.max_seq = context + max_new
+        self.caches = model.new_caches(batch, self.max_seq)
+        if fill_random:
+            for l, c in enumerate(self.caches):
+                c.fill_random(context, seed=seed * 100 + l)
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.positions = torch.full((batch,), context, **i32)   # position of the next token
+        self.kv_len = self.positions + 1                        # cache length once it is appended
+        self.slots = torch.arange(batch, **i32)
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed * 100 + 99)
+        self.tokens = torch.randint(0, model.vocab_size, (batch,), generator=g, device=dev, dtype=torch.int32)
+        self.plans = [MoEPlan(layer.mlp.weights, batch, cfg.num_experts_per_tok) for layer in model.layers]
+        lib_splits = ops._C.lib().qmoe_attention_decode_splits(batch, cfg.num_key_value_heads, self.max_seq)
+        ws = ops._C.lib().qmoe_attention_decode_workspace_size(batch, cfg.num_attention_heads, int(lib_splits))
+        self.attn_ws = torch.empty(max(int(ws), 1), dtype=torch.uint8, device=dev)
+        H = cfg.hidden_size
+        self.x = [torch.empty((batch, H), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        self.logits = torch.empty((batch, model.vocab_size), dtype=torch.bfloat16, device=dev)
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.steps_done = 0
+
+    def _layer(self, l: int, x: torch.Tensor, out: torch.Tensor) -> None:
+        cfg = self.model.cfg
+        layer = self.model.layers[l]
+        attn = layer.self_attn
+        cache = self.caches[l]
+        eps = cfg.rms_norm_eps
+        h = ops.rmsnorm(x, layer.input_layernorm, eps)
+        qkv = ops.linear(h, attn.w.wqkv)
+        q = ops.qk_norm_rope(qkv, self.positions, attn.w.q_norm, attn.w.k_norm, attn.inv_freq,
+                             cfg.num_attention_heads, cfg.num_key_value_heads, eps, cache.k, cache.v,
+                             cache_slot=self.slots)
+        a = ops.attention_decode(q, cache.k, cache.v, self.kv_len, self.max_seq, workspace=self.attn_ws)
+        o = ops.linear(a, attn.w.wo)
+        h2, residual = ops.rmsnorm(o, layer.post_attention_layernorm, eps, residual=x)
+        self.plans[l].run(h2, out, residual=residual)
+
+    def step(self) -> torch.Tensor:
+        """One decode step on the current stream (or the captured graph)."""
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._step_kernels()
+        self.steps_done += 1
+        return self.tokens
+
+    def _step_kernels(self) -> None:
+        m = self.model
+        x = ops.embedding(self.tokens, m.embed, out=self.x[0])
+        for l in range(len(m.layers)):
+            out = self.x[(l + 1) & 1]
+            self._layer(l, x, out)
+            x = out
+        hf = ops.rmsnorm(x, m.norm, m.cfg.rms_norm_eps)
+        ops.linear(hf, m.lm_head, out=self.logits)
+        self.tokens.copy_(torch.argmax(self.logits, dim=-1).to(torch.int32))
+        self.positions.add_(1)
+        self.kv_len.add_(1)
+
+    def capture(self) -> None:
+        """Capture one step into a CUDA graph (run one eager step first so
+        every kernel's attributes are set outside the capture)."""
+        dev = self.model.device
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            self._step_kernels()
+            self.steps_done += 1
+        torch.cuda.current_stream(dev).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._step_kernels()
+        self.graph = g
+
+    def release(self) -> None:
+        self.graph = None

@@ -291,6 +291,21 @@ def combine_finalize(acc: torch.Tensor, residual: Optional[torch.Tensor] = None,
     return out
 
 
+def embedding(ids: torch.Tensor, table: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[i] = table[ids[i]] (bf16 rows); ids outside [0, V) give zero rows
+    and device error 4."""
+    _need(ids, "ids", torch.int32, 1)
+    _need(table, "table", torch.bfloat16, 2)
+    V, H = table.shape
+    n = ids.shape[0]
+    dev = table.device
+    out = out if out is not None else torch.empty((n, H), dtype=torch.bfloat16, device=dev)
+    with torch.cuda.device(dev):
+        _C.check(_C.lib().qmoe_embedding_gather(_ptr(table), V, H, _ptr(ids), n, _ptr(out), _stream(dev)),
+                 "qmoe_embedding_gather")
+    return out
+
+
 def moe_forward_workspace_size(T: int, H: int, E: int, k: int, I: int) -> int:
     return int(_C.lib().qmoe_moe_forward_workspace_size(T, H, E, k, I))
 
