@@ -59,6 +59,9 @@ def parse_args():
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
     ap.add_argument("--clock-settle-s", type=float, default=1.0,
                     help="untimed load before warm-up so clocks settle and get sampled")
+    ap.add_argument("--decode-model", type=int, default=0, metavar="LAYERS",
+                    help="profiling aid: only run the config-2 decode step of a LAYERS-layer model "
+                         "(--tokens = batch) for --steps graph replays and print its time")
     return ap.parse_args()
 
 
@@ -701,8 +704,35 @@ def run_ours_ep(args):
     return 0
 
 
+def run_decode_model_only(args):
+    import torch
+
+    from nki_moe_7013_b200.config import Qwen3MoeConfig
+    from nki_moe_7013_b200.model import DecodeSession, Qwen3MoeModel
+
+    dev = torch.device("cuda", 0)
+    model = Qwen3MoeModel(Qwen3MoeConfig(), num_layers=args.decode_model, device=dev, seed=1)
+    sess = DecodeSession(model, args.tokens, context=4096, max_new=args.steps + args.warmup + 4, seed=1)
+    sess.capture()
+    for _ in range(args.warmup):
+        sess.step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        sess.step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / max(args.steps, 1)
+    print(json.dumps({"decode_model_layers": args.decode_model, "batch": args.tokens, "ms_per_step": ms,
+                      "us_per_layer": ms * 1e3 / args.decode_model}))
+    return 0
+
+
 def main():
     args = parse_args()
+    if args.decode_model:
+        return run_decode_model_only(args)
     if args.impl == "reference":
         return run_reference(args)
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:

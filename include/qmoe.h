@@ -276,10 +276,16 @@ QMOE_API int qmoe_moe_forward(const void* x, const void* w_router, const float* 
  * Dense projection out (T, N) bf16 = x (T, K) . w (N, K)^T, the nn.Linear
  * convention, on the same TMA + tcgen05 pipeline as the expert GEMMs (one
  * "expert", dense row tiles).  Replaces the QKV and o_proj projections of
- * NeuronAttentionBase (qwen.py:313-341).  Requires K % 64 == 0, N % 128 == 0.
+ * NeuronAttentionBase (qwen.py:313-341) and the LM head (the reference's
+ * NKI LM-head kernel, qwen_with_nki.py:1766-1805).  Requires K % 64 == 0,
+ * N % 128 == 0.  Decode rows (T <= 16) run a deep-ring configuration; with
+ * split_ws (qmoe_grouped_gemm_gateup_split_workspace_size() bytes, zero-filled
+ * before first use, left zero-filled, calls sharing it must not overlap on
+ * the GPU) K is also split over up to 8 CTAs per 128 features when that puts
+ * more SMs on the weight stream (fixed-order fp32 fix-up).
  * ---------------------------------------------------------------------- */
 QMOE_API int qmoe_linear(const void* x, const void* w, int64_t T, int64_t K, int64_t N, void* out,
-                         void* stream);
+                         void* split_ws, size_t split_ws_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
  * K4  RMSNorm: out = x * rsqrt(mean(x^2) + eps) * weight, fp32 math, one

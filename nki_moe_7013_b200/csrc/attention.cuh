@@ -292,6 +292,8 @@ __global__ void __launch_bounds__(kAttnThreads)
   const int nsplit = gridDim.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tq = lane & 3;
+  griddep_wait();
+  griddep_launch_dependents();
   int L = kv_len[b];
   const int slot_raw = cache_slot ? cache_slot[b] : b;
   const bool bad = L < 0 || L > max_seq || slot_raw < 0 || slot_raw >= n_slots;  // block-uniform
@@ -419,18 +421,28 @@ __global__ void __launch_bounds__(kAttnThreads)
 __global__ void __launch_bounds__(256)
     attn_decode_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
                                int B, int nh, int nsplit, __nv_bfloat16* __restrict__ out) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (gw >= B * nh) return;
   const size_t base_idx = size_t(gw) * nsplit;
+  // the splits' maxima and sums: lane s takes splits s, s+32, ... (one round
+  // trip), then warp reductions
   float M = -INFINITY;
-  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, part_ml[(base_idx + s) * 2]);
+  for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, part_ml[(base_idx + s) * 2]);
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, off));
   const float mb = M == -INFINITY ? 0.f : M;
   float L = 0.f;
+  for (int s = lane; s < nsplit; s += 32)
+    L += part_ml[(base_idx + s) * 2 + 1] * exp2f(part_ml[(base_idx + s) * 2] - mb);
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) L += __shfl_xor_sync(0xFFFFFFFFu, L, off);
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
   for (int s = 0; s < nsplit; ++s) {
     const float sc = exp2f(part_ml[(base_idx + s) * 2] - mb);
-    L += part_ml[(base_idx + s) * 2 + 1] * sc;
     const float4 v = *reinterpret_cast<const float4*>(part_o + (base_idx + s) * kAttnD + lane * 4);
     acc[0] += v.x * sc;
     acc[1] += v.y * sc;

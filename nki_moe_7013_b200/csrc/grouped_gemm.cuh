@@ -77,7 +77,9 @@ struct GemmCfg {
   static constexpr int kBRows = kSmall ? kBoxRows : kBNMax;
   static constexpr int kBBytes = kBRows * kBK * 2;        // 16 KB (2 KB small)
   static constexpr int kStageBytes = kATiles * kABytes + kBBytes;
-  static constexpr int kStages = kGateUp ? (kSmall ? 3 : 4) : (kSmall ? 5 : 6);
+  // small plain GEMMs (decode projections) run alone: the deepest ring
+  static constexpr int kStages =
+      kGateUp ? (kSmall ? 3 : 4) : kMode == kModePlain ? (kSmall ? 10 : 6) : (kSmall ? 5 : 6);
   static constexpr int kUpCol = kSmall ? kBoxRows : kBM;  // TMEM column of the up accumulator
   static constexpr int kAccCols = kGateUp ? 2 * kUpCol : kBRows;  // TMEM columns per accumulator buffer
   static constexpr int kTmemCols = 2 * kAccCols < 32 ? 32 : 2 * kAccCols;
@@ -154,11 +156,12 @@ __device__ __forceinline__ int gateup_k_splits(const GemmArgs& a, int ntiles, in
   return s < 2 ? 1 : s;
 }
 
-// Gate/up split-K fix-up, run by the 128 epilogue threads of one unit (tm,
-// ks) after loading this split's partials into g / u (feature m, 16 rows).
-// Stores them into slot (tm, ks), counts the arrival, and returns true in
-// the CTA that arrived last, with g / u replaced by the sums over the splits
-// in split order.
+// Split-K fix-up, run by the 128 epilogue threads of one unit (tm, ks) after
+// loading this split's partials into g (and u for gate/up: kTwo) -- feature
+// m, 16 rows.  Stores them into slot (tm, ks), counts the arrival, and
+// returns true in the CTA that arrived last, with g / u replaced by the sums
+// over the splits in split order.
+template <bool kTwo = true>
 __device__ __forceinline__ bool gateup_split_reduce(const GemmArgs& a, int tm, int ks, int nsplit, int m, int et,
                                                     float (&g)[16], float (&u)[16], volatile int* last_s) {
   float* slots = a.split_ws;
@@ -167,7 +170,7 @@ __device__ __forceinline__ bool gateup_split_reduce(const GemmArgs& a, int tm, i
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     __stcg(mine + i * kBM + m, g[i]);
-    __stcg(mine + (16 + i) * kBM + m, u[i]);
+    if (kTwo) __stcg(mine + (16 + i) * kBM + m, u[i]);
   }
   __threadfence();
   named_barrier_sync(1, 128);
@@ -185,7 +188,7 @@ __device__ __forceinline__ bool gateup_split_reduce(const GemmArgs& a, int tm, i
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const float gv = s == ks ? g[i] : __ldcg(p + i * kBM + m);
-      const float uv = s == ks ? u[i] : __ldcg(p + (16 + i) * kBM + m);
+      const float uv = !kTwo ? 0.f : s == ks ? u[i] : __ldcg(p + (16 + i) * kBM + m);
       gs[i] = s == 0 ? gv : gs[i] + gv;
       us[i] = s == 0 ? uv : us[i] + uv;
     }
@@ -339,7 +342,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int units = max(1, ntiles * args.n_mtiles);
     ksplit = max(1, min(min(args.k_splits, args.num_kb), int(gridDim.x) / units));
   }
-  if constexpr (kGateUp) ksplit = gateup_k_splits(args, ntiles, max_rows);
+  if constexpr (kGateUp || kMode == kModePlain) ksplit = gateup_k_splits(args, ntiles, max_rows);
   const int total_units = ntiles * args.n_mtiles * ksplit;
 
   if (warp == 0) {
@@ -560,11 +563,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tmem_ld_32x32b_x16(taddr + c * 16, v);
         if constexpr (kMode == kModePlain) {
           tmem_ld_wait();
+          float g[16], unused[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) g[i] = __uint_as_float(v[i]);
+          // split K (one 16-row chunk per unit): only the last split stores
+          if (ksplit > 1 && !gateup_split_reduce<false>(args, tm, u - tm * ksplit, ksplit, m, et, g, unused,
+                                                         &split_last))
+            break;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int n = c * 16 + i;
-            if (n < nrows)
-              args.act[size_t(row0 + n) * args.act_ld + feat] = __float2bfloat16_rn(__uint_as_float(v[i]));
+            if (n < nrows) args.act[size_t(row0 + n) * args.act_ld + feat] = __float2bfloat16_rn(g[i]);
           }
         } else if constexpr (kGateUp) {
           uint32_t up[16];

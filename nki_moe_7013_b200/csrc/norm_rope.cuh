@@ -22,62 +22,73 @@ constexpr int kNormThreads = 256;  // 8 rows per CTA, one warp per row
 
 // x (rows, H) bf16 or fp32; residual (rows, H) bf16 or null.  With a
 // residual, s = bf16(x + residual) is written to residual_out and normalised.
-template <typename Tin, typename Tout>
+// One warp per row; lane l handles elements [128c + 4l, 128c + 4l + 4) for
+// c < kChunks (kChunks * 128 >= H), all loaded before any is used so a row
+// costs one memory round trip; the values stay in registers for the scaling.
+template <typename Tin, typename Tout, int kChunks>
 __global__ void __launch_bounds__(kNormThreads)
     rmsnorm_kernel(const Tin* __restrict__ x, const __nv_bfloat16* __restrict__ residual,
                    const float* __restrict__ w, int rows, int H, float eps, Tout* __restrict__ y,
                    __nv_bfloat16* __restrict__ residual_out) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (kNormThreads / 32) + warp;
   if (row >= rows) return;
   const Tin* xr = x + size_t(row) * H;
-  float ss = 0.f;
-  // pass 1: sum of squares (and the fused residual add)
-  for (int c = lane * 4; c < H; c += 128) {
-    float v[4];
-    if constexpr (sizeof(Tin) == 4) {
-      const float4 a = *reinterpret_cast<const float4*>(xr + c);
-      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-    } else {
-      const uint2 a = *reinterpret_cast<const uint2*>(xr + c);
-      v[0] = bf16lo_to_f32(a.x); v[1] = bf16hi_to_f32(a.x);
-      v[2] = bf16lo_to_f32(a.y); v[3] = bf16hi_to_f32(a.y);
+  float v[kChunks][4];
+#pragma unroll
+  for (int i = 0; i < kChunks; ++i) {
+    const int c = i * 128 + lane * 4;
+    v[i][0] = v[i][1] = v[i][2] = v[i][3] = 0.f;
+    if (c < H) {
+      if constexpr (sizeof(Tin) == 4) {
+        const float4 a = *reinterpret_cast<const float4*>(xr + c);
+        v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
+      } else {
+        const uint2 a = *reinterpret_cast<const uint2*>(xr + c);
+        v[i][0] = bf16lo_to_f32(a.x); v[i][1] = bf16hi_to_f32(a.x);
+        v[i][2] = bf16lo_to_f32(a.y); v[i][3] = bf16hi_to_f32(a.y);
+      }
     }
-    if (residual) {
-      const uint2 r = *reinterpret_cast<const uint2*>(residual + size_t(row) * H + c);
-      const __nv_bfloat162 s0 = __floats2bfloat162_rn(v[0] + bf16lo_to_f32(r.x), v[1] + bf16hi_to_f32(r.x));
-      const __nv_bfloat162 s1 = __floats2bfloat162_rn(v[2] + bf16lo_to_f32(r.y), v[3] + bf16hi_to_f32(r.y));
-      uint2 o;
-      o.x = *reinterpret_cast<const uint32_t*>(&s0);
-      o.y = *reinterpret_cast<const uint32_t*>(&s1);
-      *reinterpret_cast<uint2*>(residual_out + size_t(row) * H + c) = o;
-      v[0] = bf16lo_to_f32(o.x); v[1] = bf16hi_to_f32(o.x);
-      v[2] = bf16lo_to_f32(o.y); v[3] = bf16hi_to_f32(o.y);
-    }
-    ss += v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
   }
+  if (residual) {
+    uint2 rr[kChunks];
+#pragma unroll
+    for (int i = 0; i < kChunks; ++i) {
+      const int c = i * 128 + lane * 4;
+      if (c < H) rr[i] = *reinterpret_cast<const uint2*>(residual + size_t(row) * H + c);
+    }
+#pragma unroll
+    for (int i = 0; i < kChunks; ++i) {
+      const int c = i * 128 + lane * 4;
+      if (c < H) {
+        const __nv_bfloat162 s0 = __floats2bfloat162_rn(v[i][0] + bf16lo_to_f32(rr[i].x),
+                                                        v[i][1] + bf16hi_to_f32(rr[i].x));
+        const __nv_bfloat162 s1 = __floats2bfloat162_rn(v[i][2] + bf16lo_to_f32(rr[i].y),
+                                                        v[i][3] + bf16hi_to_f32(rr[i].y));
+        uint2 o;
+        o.x = *reinterpret_cast<const uint32_t*>(&s0);
+        o.y = *reinterpret_cast<const uint32_t*>(&s1);
+        *reinterpret_cast<uint2*>(residual_out + size_t(row) * H + c) = o;
+        v[i][0] = bf16lo_to_f32(o.x); v[i][1] = bf16hi_to_f32(o.x);
+        v[i][2] = bf16lo_to_f32(o.y); v[i][3] = bf16hi_to_f32(o.y);
+      }
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kChunks; ++i) ss += v[i][0] * v[i][0] + v[i][1] * v[i][1] + v[i][2] * v[i][2] + v[i][3] * v[i][3];
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, off);
   const float r = rsqrtf(ss / float(H) + eps);
-  __syncwarp();
-  // pass 2: scale (reads back the row; L1-resident)
-  for (int c = lane * 4; c < H; c += 128) {
-    float v[4];
-    if (residual) {
-      const uint2 a = *reinterpret_cast<const uint2*>(residual_out + size_t(row) * H + c);
-      v[0] = bf16lo_to_f32(a.x); v[1] = bf16hi_to_f32(a.x);
-      v[2] = bf16lo_to_f32(a.y); v[3] = bf16hi_to_f32(a.y);
-    } else if constexpr (sizeof(Tin) == 4) {
-      const float4 a = *reinterpret_cast<const float4*>(xr + c);
-      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-    } else {
-      const uint2 a = *reinterpret_cast<const uint2*>(xr + c);
-      v[0] = bf16lo_to_f32(a.x); v[1] = bf16hi_to_f32(a.x);
-      v[2] = bf16lo_to_f32(a.y); v[3] = bf16hi_to_f32(a.y);
-    }
+#pragma unroll
+  for (int i = 0; i < kChunks; ++i) {
+    const int c = i * 128 + lane * 4;
+    if (c >= H) continue;
     const float4 wv = *reinterpret_cast<const float4*>(w + c);
-    const float o0 = v[0] * r * wv.x, o1 = v[1] * r * wv.y, o2 = v[2] * r * wv.z, o3 = v[3] * r * wv.w;
+    const float o0 = v[i][0] * r * wv.x, o1 = v[i][1] * r * wv.y, o2 = v[i][2] * r * wv.z, o3 = v[i][3] * r * wv.w;
     if constexpr (sizeof(Tout) == 4) {
       *reinterpret_cast<float4*>(y + size_t(row) * H + c) = make_float4(o0, o1, o2, o3);
     } else {
@@ -104,6 +115,8 @@ __global__ void __launch_bounds__(256)
                         int nkv, float eps, __nv_bfloat16* __restrict__ q_out,
                         __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache,
                         int max_seq, int n_slots) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int nheads = nh + 2 * nkv;

@@ -466,9 +466,27 @@ int launch_moe_fused(const void* x, int64_t x_rows, const int32_t* gather_rows, 
                        "moe_fused_kernel", ta_gu, tb_gu, ta_dn, tb_dn, a);
 }
 
+// RMSNorm launch with the row held in registers: kChunks 128-element chunks
+// per warp (H <= 4096).
+template <typename Tin, typename Tout>
+int launch_rmsnorm(int chunks, int grid, cudaStream_t s, const Tin* x, const __nv_bfloat16* res, const float* w,
+                   int rows, int H, float eps, Tout* y, __nv_bfloat16* res_out) {
+#define QMOE_RMSNORM_CASE(CH)                                                                               \
+  if (chunks <= CH)                                                                                         \
+    return launch_kernel(qmoe::rmsnorm_kernel<Tin, Tout, CH>, dim3(grid), dim3(qmoe::kNormThreads), 0, s, true, \
+                         "rmsnorm_kernel", x, res, w, rows, H, eps, y, res_out);
+  QMOE_RMSNORM_CASE(1)
+  QMOE_RMSNORM_CASE(2)
+  QMOE_RMSNORM_CASE(4)
+  QMOE_RMSNORM_CASE(8)
+  QMOE_RMSNORM_CASE(16)
+  QMOE_RMSNORM_CASE(32)
+#undef QMOE_RMSNORM_CASE
+  return set_error(QMOE_ERR_UNSUPPORTED_SHAPE, "rmsnorm: H=%d > 4096", H);
+}
+
 int launch_linear(const void* x, const void* w, int64_t T, int64_t K, int64_t N, void* out,
-                  cudaStream_t stream) {
-  using C = qmoe::GemmCfg<qmoe::kModePlain>;
+                  cudaStream_t stream, void* split_ws = nullptr) {
   CUtensorMap tmA, tmB;
   QMOE_CHECK(make_tmap_bf16(&tmA, w, uint64_t(K), uint64_t(N), qmoe::kBK, qmoe::kBM));
   QMOE_CHECK(make_tmap_bf16(&tmB, x, uint64_t(K), uint64_t(T), qmoe::kBK, qmoe::kBoxRows));
@@ -481,12 +499,17 @@ int launch_linear(const void* x, const void* w, int64_t T, int64_t K, int64_t N,
   a.a_rows_per_expert = 0;
   a.act = static_cast<__nv_bfloat16*>(out);
   a.act_ld = int(N);
-  const int64_t units = ((T + qmoe::kBNMax - 1) / qmoe::kBNMax) * a.n_mtiles;
+  // decode rows (<= 16): the deep-ring small configuration, and K split over
+  // up to 8 CTAs per feature block when a scratch is given
+  const bool small = T <= kSmallTileRows;
+  a.split_ws = small ? static_cast<float*>(split_ws) : nullptr;
+  a.max_k_splits = a.split_ws ? 8 : 1;
+  const int64_t units = ((T + qmoe::kBNMax - 1) / qmoe::kBNMax) * a.n_mtiles * a.max_k_splits;
   const int grid = int(std::min<int64_t>(units, num_sms(0)));
   if (grid <= 0) return QMOE_OK;
-  QMOE_CHECK(set_smem(qmoe::grouped_gemm_kernel<qmoe::kModePlain>, C::kSmemBytes));
-  return launch_kernel(qmoe::grouped_gemm_kernel<qmoe::kModePlain>, dim3(grid), dim3(qmoe::kGemmThreads),
-                       C::kSmemBytes, stream, true, "grouped_gemm_kernel<plain>", tmA, tmB, a);
+  if (small)
+    return launch_gemm_cfg<qmoe::kModePlain, true>(tmA, tmB, a, grid, stream, "grouped_gemm_kernel<plain,small>");
+  return launch_gemm_cfg<qmoe::kModePlain, false>(tmA, tmB, a, grid, stream, "grouped_gemm_kernel<plain>");
 }
 
 int launch_finalize(const float* acc, const void* residual, int64_t T, int64_t H, void* out,
@@ -780,8 +803,8 @@ int qmoe_blockwise_prepare(const void* x, const float* affinities, int64_t aff_r
   return check_launch("blockwise_prepare_kernel");
 }
 
-int qmoe_linear(const void* x, const void* w, int64_t T, int64_t K, int64_t N, void* out,
-                void* stream) {
+int qmoe_linear(const void* x, const void* w, int64_t T, int64_t K, int64_t N, void* out, void* split_ws,
+                size_t split_ws_bytes, void* stream) {
   QMOE_REQUIRE(x && w && out, QMOE_ERR_INVALID_ARGUMENT, "linear: null pointer");
   QMOE_REQUIRE(T >= 0 && T < (int64_t(1) << 31), QMOE_ERR_INVALID_ARGUMENT, "linear: bad T");
   QMOE_REQUIRE(K > 0 && K % qmoe::kBK == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "linear: K %% 64 != 0");
@@ -789,10 +812,13 @@ int qmoe_linear(const void* x, const void* w, int64_t T, int64_t K, int64_t N, v
                "linear: N %% 128 != 0");
   QMOE_REQUIRE(aligned16(x) && aligned16(w) && aligned16(out), QMOE_ERR_MISALIGNED,
                "linear: pointers must be 16-byte aligned");
+  QMOE_REQUIRE(!split_ws || split_ws_bytes >= qmoe::kSplitWorkspaceBytes, QMOE_ERR_WORKSPACE_TOO_SMALL,
+               "linear: split workspace %zu < required %zu bytes", split_ws_bytes, qmoe::kSplitWorkspaceBytes);
+  QMOE_REQUIRE(!split_ws || aligned16(split_ws), QMOE_ERR_MISALIGNED, "linear: split workspace not aligned");
   DeviceInfo* d = nullptr;
   QMOE_CHECK(device_info(&d));
   if (T == 0) return QMOE_OK;
-  return launch_linear(x, w, T, K, N, out, static_cast<cudaStream_t>(stream));
+  return launch_linear(x, w, T, K, N, out, static_cast<cudaStream_t>(stream), split_ws);
 }
 
 int qmoe_rmsnorm(const void* x, int x_is_fp32, const void* residual, const float* weight,
@@ -802,7 +828,8 @@ int qmoe_rmsnorm(const void* x, int x_is_fp32, const void* residual, const float
   QMOE_REQUIRE(!residual || (residual_out && !x_is_fp32), QMOE_ERR_INVALID_ARGUMENT,
                "rmsnorm: a residual needs residual_out and bf16 x");
   QMOE_REQUIRE(rows >= 0 && rows < (int64_t(1) << 31), QMOE_ERR_INVALID_ARGUMENT, "rmsnorm: bad rows");
-  QMOE_REQUIRE(H > 0 && H % 4 == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "rmsnorm: H %% 4 != 0");
+  QMOE_REQUIRE(H > 0 && H % 4 == 0 && H <= 4096, QMOE_ERR_UNSUPPORTED_SHAPE,
+               "rmsnorm: H must be a multiple of 4 and <= 4096");
   QMOE_REQUIRE(aligned16(x) && aligned16(weight) && aligned16(out) &&
                    (!residual || (aligned16(residual) && aligned16(residual_out))),
                QMOE_ERR_MISALIGNED, "rmsnorm: pointers must be 16-byte aligned");
@@ -813,22 +840,19 @@ int qmoe_rmsnorm(const void* x, int x_is_fp32, const void* residual, const float
   const int grid = int((rows + 7) / 8);
   const auto* res = static_cast<const __nv_bfloat16*>(residual);
   auto* res_out = static_cast<__nv_bfloat16*>(residual_out);
+  const int chunks = int((H + 127) / 128);
   if (x_is_fp32 && out_is_fp32)
-    qmoe::rmsnorm_kernel<float, float><<<grid, qmoe::kNormThreads, 0, s>>>(
-        static_cast<const float*>(x), nullptr, weight, int(rows), int(H), eps, static_cast<float*>(out), nullptr);
-  else if (x_is_fp32)
-    qmoe::rmsnorm_kernel<float, __nv_bfloat16><<<grid, qmoe::kNormThreads, 0, s>>>(
-        static_cast<const float*>(x), nullptr, weight, int(rows), int(H), eps,
-        static_cast<__nv_bfloat16*>(out), nullptr);
-  else if (out_is_fp32)
-    qmoe::rmsnorm_kernel<__nv_bfloat16, float><<<grid, qmoe::kNormThreads, 0, s>>>(
-        static_cast<const __nv_bfloat16*>(x), res, weight, int(rows), int(H), eps,
-        static_cast<float*>(out), res_out);
-  else
-    qmoe::rmsnorm_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, qmoe::kNormThreads, 0, s>>>(
-        static_cast<const __nv_bfloat16*>(x), res, weight, int(rows), int(H), eps,
-        static_cast<__nv_bfloat16*>(out), res_out);
-  return check_launch("rmsnorm_kernel");
+    return launch_rmsnorm<float, float>(chunks, grid, s, static_cast<const float*>(x), nullptr, weight, int(rows),
+                                        int(H), eps, static_cast<float*>(out), nullptr);
+  if (x_is_fp32)
+    return launch_rmsnorm<float, __nv_bfloat16>(chunks, grid, s, static_cast<const float*>(x), nullptr, weight,
+                                                int(rows), int(H), eps, static_cast<__nv_bfloat16*>(out), nullptr);
+  if (out_is_fp32)
+    return launch_rmsnorm<__nv_bfloat16, float>(chunks, grid, s, static_cast<const __nv_bfloat16*>(x), res, weight,
+                                                int(rows), int(H), eps, static_cast<float*>(out), res_out);
+  return launch_rmsnorm<__nv_bfloat16, __nv_bfloat16>(chunks, grid, s, static_cast<const __nv_bfloat16*>(x), res,
+                                                      weight, int(rows), int(H), eps,
+                                                      static_cast<__nv_bfloat16*>(out), res_out);
 }
 
 int qmoe_qk_norm_rope(const void* qkv, const int32_t* positions, const int32_t* cache_slot,
@@ -850,12 +874,12 @@ int qmoe_qk_norm_rope(const void* qkv, const int32_t* positions, const int32_t* 
   QMOE_CHECK(device_info(&d));
   if (T == 0) return QMOE_OK;
   const int64_t warps = T * (nh + 2 * nkv);
-  qmoe::qk_norm_rope_kernel<<<int((warps + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(qkv), positions, cache_slot, q_norm_w, k_norm_w, inv_freq,
-      int(T), int(nh), int(nkv), eps, static_cast<__nv_bfloat16*>(q_out),
-      static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache), int(max_seq),
-      int(n_slots));
-  return check_launch("qk_norm_rope_kernel");
+  return launch_kernel(qmoe::qk_norm_rope_kernel, dim3(unsigned((warps + 7) / 8)), dim3(256), 0,
+                       static_cast<cudaStream_t>(stream), true, "qk_norm_rope_kernel",
+                       static_cast<const __nv_bfloat16*>(qkv), positions, cache_slot, q_norm_w, k_norm_w, inv_freq,
+                       int(T), int(nh), int(nkv), eps, static_cast<__nv_bfloat16*>(q_out),
+                       static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache), int(max_seq),
+                       int(n_slots));
 }
 
 int qmoe_attention_prefill(const void* q, const void* k_cache, const void* v_cache,
@@ -928,14 +952,15 @@ int qmoe_attention_decode(const void* q, const void* k_cache, const void* v_cach
   const int smem = 4 * qmoe::kAttnBK * qmoe::kAttnPad * 2 + 4 * qmoe::kDecodeGroup * (qmoe::kAttnD + 2) * 4;
   QMOE_CHECK(set_smem(qmoe::attn_decode_kernel, smem));
   const dim3 grid(static_cast<unsigned>(nsplit), static_cast<unsigned>(nkv), static_cast<unsigned>(B));
-  qmoe::attn_decode_kernel<<<grid, qmoe::kAttnThreads, smem, s>>>(
-      static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k_cache),
-      static_cast<const __nv_bfloat16*>(v_cache), kv_len, cache_slot, int(nh), int(nkv), int(max_seq),
-      int(n_slots), int(chunk), scale * 1.4426950408889634f, part_o, part_ml);
-  QMOE_CHECK(check_launch("attn_decode_kernel"));
-  qmoe::attn_decode_combine_kernel<<<int((B * nh + 7) / 8), 256, 0, s>>>(
-      part_o, part_ml, int(B), int(nh), int(nsplit), static_cast<__nv_bfloat16*>(out));
-  return check_launch("attn_decode_combine_kernel");
+  QMOE_CHECK(launch_kernel(qmoe::attn_decode_kernel, grid, dim3(qmoe::kAttnThreads), size_t(smem), s, true,
+                           "attn_decode_kernel", static_cast<const __nv_bfloat16*>(q),
+                           static_cast<const __nv_bfloat16*>(k_cache), static_cast<const __nv_bfloat16*>(v_cache),
+                           kv_len, cache_slot, int(nh), int(nkv), int(max_seq), int(n_slots), int(chunk),
+                           scale * 1.4426950408889634f, part_o, part_ml));
+  return launch_kernel(qmoe::attn_decode_combine_kernel, dim3(unsigned((B * nh + 7) / 8)), dim3(256), 0, s, true,
+                       "attn_decode_combine_kernel", static_cast<const float*>(part_o),
+                       static_cast<const float*>(part_ml), int(B), int(nh), int(nsplit),
+                       static_cast<__nv_bfloat16*>(out));
 }
 
 int qmoe_routing_histogram(const int32_t* topk_idx, int64_t T, int64_t k, int64_t E, int32_t* chunk_hist,

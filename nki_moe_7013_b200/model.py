@@ -72,7 +72,7 @@ class DecodeSession:
     its greedy output; ``logits`` (B, V) bf16 holds the last step's logits."""
 
     def __init__(self, model: Qwen3MoeModel, batch: int, context: int, max_new: int, seed: int = 0,
-                 fill_random: bool = True):
+                 fill_random: bool = True, split_k: bool = True):
         cfg = model.cfg
         dev = model.device
         self.model = model
@@ -93,6 +93,8 @@ class DecodeSession:
         lib_splits = ops._C.lib().qmoe_attention_decode_splits(batch, cfg.num_key_value_heads, self.max_seq)
         ws = ops._C.lib().qmoe_attention_decode_workspace_size(batch, cfg.num_attention_heads, int(lib_splits))
         self.attn_ws = torch.empty(max(int(ws), 1), dtype=torch.uint8, device=dev)
+        # split-K scratch of the decode projections (one launch at a time uses it)
+        self.split_ws = ops.gateup_split_workspace(dev) if (split_k and batch <= 16) else None
         H = cfg.hidden_size
         self.x = [torch.empty((batch, H), dtype=torch.bfloat16, device=dev) for _ in range(2)]
         self.logits = torch.empty((batch, model.vocab_size), dtype=torch.bfloat16, device=dev)
@@ -106,12 +108,12 @@ class DecodeSession:
         cache = self.caches[l]
         eps = cfg.rms_norm_eps
         h = ops.rmsnorm(x, layer.input_layernorm, eps)
-        qkv = ops.linear(h, attn.w.wqkv)
+        qkv = ops.linear(h, attn.w.wqkv, split_ws=self.split_ws)
         q = ops.qk_norm_rope(qkv, self.positions, attn.w.q_norm, attn.w.k_norm, attn.inv_freq,
                              cfg.num_attention_heads, cfg.num_key_value_heads, eps, cache.k, cache.v,
                              cache_slot=self.slots)
         a = ops.attention_decode(q, cache.k, cache.v, self.kv_len, self.max_seq, workspace=self.attn_ws)
-        o = ops.linear(a, attn.w.wo)
+        o = ops.linear(a, attn.w.wo, split_ws=self.split_ws)
         h2, residual = ops.rmsnorm(o, layer.post_attention_layernorm, eps, residual=x)
         self.plans[l].run(h2, out, residual=residual)
 
@@ -132,7 +134,7 @@ class DecodeSession:
             self._layer(l, x, out)
             x = out
         hf = ops.rmsnorm(x, m.norm, m.cfg.rms_norm_eps)
-        ops.linear(hf, m.lm_head, out=self.logits)
+        ops.linear(hf, m.lm_head, out=self.logits, split_ws=self.split_ws)
         self.tokens.copy_(torch.argmax(self.logits, dim=-1).to(torch.int32))
         self.positions.add_(1)
         self.kv_len.add_(1)

@@ -349,8 +349,10 @@ def moe_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate_up: torch.Tensor
 # attention sub-layer
 # ----------------------------------------------------------------------------
 
-def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """out (T, N) bf16 = x (T, K) @ w (N, K)^T on the tcgen05 GEMM."""
+def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
+           split_ws: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out (T, N) bf16 = x (T, K) @ w (N, K)^T on the tcgen05 GEMM.  With
+    ``split_ws`` (gateup_split_workspace) decode-sized calls may split K."""
     _need(x, "x", torch.bfloat16, 2)
     _need(w, "w", torch.bfloat16, 2)
     T, K = x.shape
@@ -360,7 +362,9 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None)
     dev = x.device
     out = out if out is not None else torch.empty((T, N), dtype=torch.bfloat16, device=dev)
     with torch.cuda.device(dev):
-        _C.check(_C.lib().qmoe_linear(_ptr(x), _ptr(w), T, K, N, _ptr(out), _stream(dev)), "qmoe_linear")
+        _C.check(_C.lib().qmoe_linear(_ptr(x), _ptr(w), T, K, N, _ptr(out), _ptr(split_ws),
+                                      0 if split_ws is None else split_ws.numel() * split_ws.element_size(),
+                                      _stream(dev)), "qmoe_linear")
     return out
 
 

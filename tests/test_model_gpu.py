@@ -43,7 +43,9 @@ def test_decode_step_matches_module_path(cuda_dev, oracle, B):
 
     model = _small_model(cuda_dev)
     ctx = 64
-    sess = DecodeSession(model, B, context=ctx, max_new=8, seed=5)
+    # projections without split K: the module path runs them unsplit, and a
+    # different fp32 summation order could flip a near-tie in the routing
+    sess = DecodeSession(model, B, context=ctx, max_new=8, seed=5, split_k=False)
     # the module path on copies of the same caches (host-side lengths = ctx)
     caches = []
     for c in sess.caches:
