@@ -192,10 +192,11 @@ __global__ void __launch_bounds__(kScatterThreads)
         if (dst[u] >= 0) *reinterpret_cast<uint4*>(x_perm + size_t(dst[u]) * H + col[u]) = val[u];
     }
   }
-  if (acc_zero && part == 0) {
+  if (acc_zero) {
+    // the chunk's accumulator rows, split across the chunk's CTAs
     const int vec_per_row = H / 4;
     const int total_v = nt * vec_per_row;
-    for (int v = tid; v < total_v; v += kScatterThreads) {
+    for (int v = part * kScatterThreads + tid; v < total_v; v += kScatterThreads * gridDim.y) {
       const int tl = v / vec_per_row;
       const int cc = (v % vec_per_row) * 4;
       *reinterpret_cast<float4*>(acc_zero + size_t(t0 + tl) * H + cc) = make_float4(0.f, 0.f, 0.f, 0.f);

@@ -332,7 +332,7 @@ int launch_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chunk_
                            true, "permute_scan_kernel", chunk_hist, nchunks, int(E), counts));
   if (nchunks > 0) {
     // Enough CTAs to keep the row gather from being latency-bound.
-    const int parts = x_perm ? int(std::max<int64_t>(1, std::min<int64_t>(8, (2 * num_sms(0) + nchunks - 1) / nchunks))) : 1;
+    const int parts = x_perm ? int(std::max<int64_t>(1, std::min<int64_t>(8, (4 * num_sms(0) + nchunks - 1) / nchunks))) : 1;
     QMOE_CHECK(launch_kernel(qmoe::permute_scatter_kernel, dim3(nchunks, parts), dim3(qmoe::kScatterThreads),
                              0, stream, true, "permute_scatter_kernel", topk_idx, topk_w,
                              static_cast<const int32_t*>(chunk_hist), static_cast<const int32_t*>(counts),
