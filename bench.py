@@ -578,7 +578,7 @@ def run_decode_model(cfg, dev, hbm_gbs, batches=(1, 8, 32, 64), context=4096):
         e1.record()
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / n
-        U = sum(int((p.counts > 0).sum().item()) for p in sess.plans)
+        U = sum(p.experts_hit() for p in sess.plans)
         kv_len = context + sess.steps_done
         byts = (U * (GATE_UP_BYTES_PER_EXPERT + DOWN_BYTES_PER_EXPERT) + nl * E * H * 2 + attn_bytes
                 + V * H * 2 + nl * B * cfg.num_key_value_heads * kv_len * cfg.head_dim * 2 * 2)

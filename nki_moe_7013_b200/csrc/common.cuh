@@ -180,6 +180,66 @@ __device__ __forceinline__ void tma_gather4_hint(void* smem_dst, const CUtensorM
       : "memory");
 }
 
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// One grid-wide barrier of a co-resident grid (at most one CTA per SM, all
+// launched): every CTA arrives once on *counter (zero before the launch) and
+// waits, bounded, for the others.  Every thread's earlier global writes and
+// reductions are visible grid-wide afterwards.  Returns false (device error
+// `code` recorded) if the others did not arrive within the wait limit.
+__device__ __forceinline__ bool grid_barrier_once(int* counter, unsigned int code) {
+  __shared__ int arrived_ok;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    atomicAdd(counter, 1);
+    int good = 1;
+    const unsigned long long t0 = globaltimer_ns();
+    while (ld_acquire_gpu(counter) < int(gridDim.x)) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        record_device_error(code);
+        good = 0;
+        break;
+      }
+      __nanosleep(128);
+    }
+    arrived_ok = good;
+  }
+  __syncthreads();
+  return arrived_ok != 0;
+}
+
+// Combine finalisation of 8 features: out = bf16(acc [+ residual]), fp32
+// sum, one rounding.  acc is read through L2 (it may have been reduced into
+// by other SMs in the same kernel).
+__device__ __forceinline__ void finalize_vec8(const float* __restrict__ acc, const __nv_bfloat16* __restrict__ residual,
+                                              __nv_bfloat16* __restrict__ out, long long i) {
+  const float4 a = __ldcg(reinterpret_cast<const float4*>(acc) + 2 * i);
+  const float4 b = __ldcg(reinterpret_cast<const float4*>(acc) + 2 * i + 1);
+  float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  if (residual) {
+    const uint4 r = reinterpret_cast<const uint4*>(residual)[i];
+    const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[2 * j] += __uint_as_float(rw[j] << 16);
+      v[2 * j + 1] += __uint_as_float(rw[j] & 0xFFFF0000u);
+    }
+  }
+  uint4 o;
+  uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const __nv_bfloat162 p = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+    ow[j] = *reinterpret_cast<const uint32_t*>(&p);
+  }
+  reinterpret_cast<uint4*>(out)[i] = o;
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }

@@ -14,28 +14,8 @@ __global__ void __launch_bounds__(256)
   griddep_launch_dependents();
   if (threadIdx.x == 0) QMOE_TRACE_AT(3, 1);
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n_vec8;
-       i += (long long)gridDim.x * blockDim.x) {
-    const float4 a = reinterpret_cast<const float4*>(acc)[2 * i];
-    const float4 b = reinterpret_cast<const float4*>(acc)[2 * i + 1];
-    float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    if (residual) {
-      const uint4 r = reinterpret_cast<const uint4*>(residual)[i];
-      const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        v[2 * j] += bf16lo_to_f32(rw[j]);
-        v[2 * j + 1] += bf16hi_to_f32(rw[j]);
-      }
-    }
-    uint4 o;
-    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const __nv_bfloat162 p = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
-      ow[j] = *reinterpret_cast<const uint32_t*>(&p);
-    }
-    reinterpret_cast<uint4*>(out)[i] = o;
-  }
+       i += (long long)gridDim.x * blockDim.x)
+    finalize_vec8(acc, residual, out, i);
   if (threadIdx.x == 0) QMOE_TRACE_AT(3, 2);
 }
 

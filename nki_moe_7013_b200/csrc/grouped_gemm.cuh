@@ -50,11 +50,13 @@ constexpr int kGemmThreads = 192;
 // tiles), so a small-tile down GEMM may read it and stream weights before its
 // dependency wait.
 constexpr int kGemmTilesReady = 1;
-// gate/up split-K scratch: kSplitSlots partial slots of [2][16 rows][128
-// features] fp32, then kSplitSlots arrival counters
+// split-K scratch: kSplitSlots partial slots of [2][16 rows][128 features]
+// fp32, then kSplitSlots arrival counters and 4 spare words (word kSplitSlots:
+// the grid-barrier counter of the fused decode finalisation)
 constexpr int kSplitSlots = 256;
 constexpr int kSplitSlotFloats = 2 * kBoxRows * kBM;
-constexpr size_t kSplitWorkspaceBytes = size_t(kSplitSlots) * kSplitSlotFloats * 4 + kSplitSlots * 4;
+constexpr int kSplitCounterWords = kSplitSlots + 4;
+constexpr size_t kSplitWorkspaceBytes = size_t(kSplitSlots) * kSplitSlotFloats * 4 + kSplitCounterWords * 4;
 
 // Epilogue modes of the one GEMM kernel.
 enum GemmMode : int {
@@ -107,6 +109,12 @@ struct GemmArgs {
   float* split_ws;
   int max_k_splits;
   int flags;             // kGemmTilesReady
+  // down: when fin_out is set, after one grid-wide barrier on *grid_bar (zero
+  // before the launch) every CTA finalises a slice of the combine --
+  // fin_out = bf16(acc + fin_residual), the finalize kernel folded in
+  const __nv_bfloat16* fin_residual;
+  __nv_bfloat16* fin_out;
+  int* grid_bar;
   int a_rows_per_expert; // 2I (gate/up) or H (down)
   int up_row_offset;     // I (gate/up only)
   // gate/up: when non-null, B row r of a tile is row gather_rows[r] of the
@@ -650,6 +658,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+  if constexpr (kMode == kModeDown) {
+    if (args.fin_out != nullptr && grid_barrier_once(args.grid_bar, kDevErrWaitTimeoutEpilogue)) {
+      const long long n8 = (long long)args.n_acc * args.acc_ld / 8;
+      for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8;
+           i += (long long)gridDim.x * blockDim.x)
+        finalize_vec8(args.acc, args.fin_residual, args.fin_out, i);
+    }
   }
 }
 

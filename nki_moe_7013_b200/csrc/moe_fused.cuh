@@ -66,18 +66,17 @@ struct FusedArgs {
   float* acc;
   int acc_ld;
   int n_acc;
-  int* done;  // [max_tiles + 1]: gate/up units finished per tile, then the unit
-              // counter; all zero on entry
+  int* done;  // [max_tiles + 2]: gate/up units finished per tile, the unit
+              // counter, the grid-barrier counter; all zero on entry
+  // when fin_out is set, after one grid-wide barrier on done[max_tiles + 1]
+  // every CTA finalises a slice of the combine: fin_out = bf16(acc +
+  // fin_residual) -- the finalize kernel folded in
+  const __nv_bfloat16* fin_residual;
+  __nv_bfloat16* fin_out;
   // non-null: gate/up row r of a tile is token row gather_rows[r] of x (TMA
   // gather4; tmB_gu maps x with 1-row boxes), else row r of the permuted copy
   const int32_t* gather_rows;
 };
-
-__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 
 // Bounded wait for a tile's activations; false (and a device error) on time-out.
 __device__ __forceinline__ bool wait_tile_done(const int* done, int target, volatile int* abort_flag) {
@@ -531,6 +530,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+  if (args.fin_out != nullptr && grid_barrier_once(args.done + args.max_tiles + 1, kDevErrWaitTimeoutEpilogue)) {
+    const long long n8 = (long long)args.n_acc * args.acc_ld / 8;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8;
+         i += (long long)gridDim.x * blockDim.x)
+      finalize_vec8(args.acc, args.fin_residual, args.fin_out, i);
   }
 }
 

@@ -393,7 +393,8 @@ int launch_gemm_gateup(const void* x, int64_t x_rows, const int32_t* gather_rows
 int launch_gemm_down(const void* act, const void* w_down, const int32_t* tiles, int64_t max_tiles,
                      const int32_t* row_dst, const float* row_w, int64_t R, int64_t H, int64_t I,
                      int64_t E, float* acc, int64_t n_acc, cudaStream_t stream,
-                     int64_t max_tile_rows = qmoe::kBNMax, int flags = 0) {
+                     int64_t max_tile_rows = qmoe::kBNMax, int flags = 0, const void* fin_residual = nullptr,
+                     void* fin_out = nullptr, int32_t* grid_bar = nullptr) {
   CUtensorMap tmA, tmB;
   QMOE_CHECK(make_tmap_bf16(&tmA, w_down, uint64_t(I), uint64_t(E * H), qmoe::kBK, qmoe::kBM));
   QMOE_CHECK(make_tmap_bf16(&tmB, act, uint64_t(I), uint64_t(R), qmoe::kBK, qmoe::kBoxRows));
@@ -415,6 +416,9 @@ int launch_gemm_down(const void* act, const void* w_down, const int32_t* tiles, 
   a.acc_ld = int(H);
   a.n_acc = int(n_acc);
   a.flags = flags;
+  a.fin_residual = static_cast<const __nv_bfloat16*>(fin_residual);
+  a.fin_out = static_cast<__nv_bfloat16*>(fin_out);
+  a.grid_bar = grid_bar;
   const int64_t units = max_tiles * a.n_mtiles * a.k_splits;
   const int grid = int(std::min<int64_t>(units, num_sms(0)));
   if (grid <= 0) return QMOE_OK;
@@ -429,7 +433,8 @@ int launch_gemm_down(const void* act, const void* w_down, const int32_t* tiles, 
 int launch_moe_fused(const void* x, int64_t x_rows, const int32_t* gather_rows, const void* w_gate_up,
                      const void* w_down, const int32_t* tiles, int64_t max_tiles, const int32_t* row_dst,
                      const float* row_w, int64_t R, int64_t H, int64_t I, int64_t E, void* act, float* acc,
-                     int64_t n_acc, int32_t* done, cudaStream_t stream) {
+                     int64_t n_acc, int32_t* done, cudaStream_t stream, const void* fin_residual = nullptr,
+                     void* fin_out = nullptr) {
   using C = qmoe::FusedCfg;
   CUtensorMap ta_gu, tb_gu, ta_dn, tb_dn;
   QMOE_CHECK(make_tmap_bf16(&ta_gu, w_gate_up, uint64_t(H), uint64_t(E * 2 * I), qmoe::kBK, qmoe::kBM));
@@ -458,6 +463,8 @@ int launch_moe_fused(const void* x, int64_t x_rows, const int32_t* gather_rows, 
   a.n_acc = int(n_acc);
   a.done = done;
   a.gather_rows = gather_rows;
+  a.fin_residual = static_cast<const __nv_bfloat16*>(fin_residual);
+  a.fin_out = static_cast<__nv_bfloat16*>(fin_out);
   const int64_t units = max_tiles * (a.n_mt_gu + a.n_mt_dn);
   const int grid = int(std::min<int64_t>(units, num_sms(0)));
   if (grid <= 0) return QMOE_OK;
@@ -554,7 +561,7 @@ FwdLayout fwd_layout(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I) {
   L.act = take(2 * size_t(R * I));
   L.acc = take(sizeof(float) * size_t(T * H));
   L.split = take(T * k <= kGateUpSplitMaxR ? qmoe::kSplitWorkspaceBytes : 0);
-  L.done = take(T > kGatherMaxT ? sizeof(int32_t) * size_t(qmoe_max_tiles(R, E) + 1) : 0);
+  L.done = take(T > kGatherMaxT ? sizeof(int32_t) * size_t(qmoe_max_tiles(R, E) + 2) : 0);
   L.total = o;
   return L;
 }
@@ -1239,32 +1246,35 @@ int qmoe_moe_forward(const void* x, const void* w_router, const float* router_bi
     // the gate/up split counters (the workspace may hold anything on entry)
     QMOE_CHECK(launch_route_small(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw, counts,
                                   offsets, row_token, row_w, slot_row, tiles, max_tiles, acc, s, split_counters,
-                                  split_counters ? qmoe::kSplitSlots : 0));
+                                  split_counters ? qmoe::kSplitCounterWords : 0));
   } else {
     QMOE_CHECK(launch_router(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw,
                              chunk_hist, s));
     // the permutation also zeroes the gate/up split counters or the fused
     // kernel's tile counters (the workspace may hold anything on entry)
     int32_t* zero = fused ? done : split_counters;
-    const int n_zero = fused ? int(max_tiles + 1) : (split_counters ? qmoe::kSplitSlots : 0);
+    const int n_zero = fused ? int(max_tiles + 2) : (split_counters ? qmoe::kSplitCounterWords : 0);
     QMOE_CHECK(launch_permute(idx, tw, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w,
                               slot_row, tiles, x_perm, acc, s, zero, n_zero));
   }
   if (fused) {
-    // prefill: gate/up and down in one persistent kernel
+    // prefill: gate/up and down in one persistent kernel, which also
+    // finalises the combine after a grid-wide barrier
     if (x_perm)
-      QMOE_CHECK(launch_moe_fused(x_perm, R, nullptr, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H,
-                                  I, E, act, acc, T, done, s));
-    else
-      QMOE_CHECK(launch_moe_fused(x, T, row_token, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H, I,
-                                  E, act, acc, T, done, s));
-  } else {
-    QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s,
-                                  tile_rows));
-    // the tile list comes from the routing kernels, before the gate/up GEMM
-    QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s,
-                                tile_rows, qmoe::kGemmTilesReady));
+      return launch_moe_fused(x_perm, R, nullptr, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H, I,
+                              E, act, acc, T, done, s, residual, out);
+    return launch_moe_fused(x, T, row_token, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, act,
+                            acc, T, done, s, residual, out);
   }
+  QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s,
+                                tile_rows));
+  // the tile list comes from the routing kernels, before the gate/up GEMM;
+  // with the split scratch (decode sizes) the down GEMM finalises too
+  if (split_counters)
+    return launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s, tile_rows,
+                            qmoe::kGemmTilesReady, residual, out, split_counters + qmoe::kSplitSlots);
+  QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s, tile_rows,
+                              qmoe::kGemmTilesReady));
   return launch_finalize(acc, residual, T, H, out, s);
 }
 
@@ -1398,31 +1408,34 @@ extern "C" int qmoe_moe_forward_noalloc(const void* x, const void* w_router,
     // the gate/up split counters (the workspace may hold anything on entry)
     QMOE_CHECK(launch_route_small(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw, counts,
                                   offsets, row_token, row_w, slot_row, tiles, max_tiles, acc, s, split_counters,
-                                  split_counters ? qmoe::kSplitSlots : 0));
+                                  split_counters ? qmoe::kSplitCounterWords : 0));
   } else {
     QMOE_CHECK(launch_router(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw,
                              chunk_hist, s));
     // the permutation also zeroes the gate/up split counters or the fused
     // kernel's tile counters (the workspace may hold anything on entry)
     int32_t* zero = fused ? done : split_counters;
-    const int n_zero = fused ? int(max_tiles + 1) : (split_counters ? qmoe::kSplitSlots : 0);
+    const int n_zero = fused ? int(max_tiles + 2) : (split_counters ? qmoe::kSplitCounterWords : 0);
     QMOE_CHECK(launch_permute(idx, tw, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w,
                               slot_row, tiles, x_perm, acc, s, zero, n_zero));
   }
   if (fused) {
-    // prefill: gate/up and down in one persistent kernel
+    // prefill: gate/up and down in one persistent kernel, which also
+    // finalises the combine after a grid-wide barrier
     if (x_perm)
-      QMOE_CHECK(launch_moe_fused(x_perm, R, nullptr, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H,
-                                  I, E, act, acc, T, done, s));
-    else
-      QMOE_CHECK(launch_moe_fused(x, T, row_token, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H, I,
-                                  E, act, acc, T, done, s));
-  } else {
-    QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s,
-                                  tile_rows));
-    // the tile list comes from the routing kernels, before the gate/up GEMM
-    QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s,
-                                tile_rows, qmoe::kGemmTilesReady));
+      return launch_moe_fused(x_perm, R, nullptr, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H, I,
+                              E, act, acc, T, done, s, residual, out);
+    return launch_moe_fused(x, T, row_token, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, act,
+                            acc, T, done, s, residual, out);
   }
+  QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s,
+                                tile_rows));
+  // the tile list comes from the routing kernels, before the gate/up GEMM;
+  // with the split scratch (decode sizes) the down GEMM finalises too
+  if (split_counters)
+    return launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s, tile_rows,
+                            qmoe::kGemmTilesReady, residual, out, split_counters + qmoe::kSplitSlots);
+  QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s, tile_rows,
+                              qmoe::kGemmTilesReady));
   return launch_finalize(acc, residual, T, H, out, s);
 }

@@ -212,11 +212,14 @@ def blockwise_forward(hidden_states, expert_affinities_masked, token_position_to
 class MoEPlan:
     """Preallocated buffers + direct C-ABI launches for a fixed (T, H, E, k, I).
 
-    ``run(x, out, residual=None, events=None)``: when ``events`` is a list of
-    len(self.stages) + 1 CUDA events, they are recorded before the first
-    kernel and after each stage, on the current stream.  Stages: router,
-    permute (scan + scatter), gate_up, down, finalize; prefill sizes run
-    gate/up and down as one kernel ("experts")."""
+    ``run(x, out, residual=None)`` is one ``qmoe_moe_forward`` call (the
+    library's fused forward on a preallocated workspace).  ``run(..., events)``
+    runs the same kernels through the per-stage entry points instead and
+    records the CUDA events (len(self.stages) + 1) before the first kernel and
+    after each stage, on the current stream.  Stages: router, permute (scan +
+    scatter), gate_up, down, finalize; prefill sizes run gate/up and down as
+    one kernel ("experts").  The fused forward folds the finalize into the
+    last kernel."""
 
     STAGES = ("router", "permute", "gate_up", "down", "finalize")
     STAGES_FUSED = ("router", "permute", "experts", "finalize")
@@ -260,6 +263,8 @@ class MoEPlan:
                        if T > ops.GATHER_MAX_T and not (self.fused and prefill_gather) else None)
         self.done = torch.zeros(self.max_tiles + 1, **i32) if self.fused else None
         self.stages = self.STAGES_FUSED if self.fused else self.STAGES
+        self.ws_bytes = int(_C.lib().qmoe_moe_forward_workspace_size(T, H, E, k, I))
+        self.workspace = torch.empty(max(self.ws_bytes, 256), dtype=torch.uint8, device=dev)
         # small batches route through the logits + selection kernels
         self.logits = torch.empty((T, E), **f32) if T <= ops.ROUTER_SMALL_MAX_T else None
         # a token's k experts are distinct: no tile holds more than T rows
@@ -277,6 +282,11 @@ class MoEPlan:
         s = torch.cuda.current_stream(self.device).cuda_stream
         T, H, E, k, I, R = self.T, self.H, self.E, self.k, self.I, self.R
         w = self.w
+        if events is None:
+            _C.check(lib.qmoe_moe_forward(p(x), p(w.router), p(self.bias), p(w.gate_up), p(w.down), p(residual),
+                                          T, H, E, k, I, 1 if self.normalize else 0, p(out), p(self.topk_idx),
+                                          p(self.topk_w), p(self.workspace), self.ws_bytes, s), "moe_forward")
+            return out
 
         def mark(i):
             if events is not None:
@@ -333,13 +343,17 @@ class MoEPlan:
 
     LAUNCHES_PER_RUN = 6  # router, scan, scatter, gate/up, down, finalize (T > 64)
 
+    def experts_hit(self) -> int:
+        """Distinct experts the last run routed to."""
+        return int(torch.unique(self.topk_idx).numel())
+
     @property
     def launches_per_run(self) -> int:
         """Kernels one run launches: route_small (1) or router (2 when
         T <= 64: logits + selection) + scan + scatter, then gate/up, down,
         finalize."""
         if self.route_small:
-            return 4
+            return 3  # route, gate/up, down (+ finalize folded in)
         if self.fused:
-            return 5
+            return 4  # router, scan, scatter, experts (+ finalize folded in)
         return (7 if self.T <= ops.ROUTER_SMALL_MAX_T else 6)
