@@ -594,7 +594,7 @@ def run_decode_model(cfg, dev, hbm_gbs, batches=(1, 8, 32, 64), context=4096):
 
 
 def run_ours_ep(args):
-    """N>1: the expert-parallel MoE layer over NCCL."""
+    """N>1: the expert-parallel MoE layer over peer memory (NCCL for set-up)."""
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -620,6 +620,11 @@ def run_ours_ep(args):
                        normal_bf16_device(3000 + rank, (el, H, I_MOE), 0.02, dev))
     moe = PeerExpertParallelMoE(cfg, router, local, max_tokens=T)
     x = normal_bf16_device(1000 + rank, (T, H), 1.0, dev)
+    for _ in range(2):
+        moe(x)  # eager steps: every kernel's attributes set before capture
+    torch.cuda.synchronize()
+    moe.capture(x)  # one CUDA graph per parity; each step replays one
+    x_static = moe.static_input()
 
     def barrier():
         dist.barrier()
@@ -628,18 +633,18 @@ def run_ours_ep(args):
     sampler = ClockSampler() if rank == 0 else None
 
     def timed_run():
-        t_end = time.perf_counter() + args.clock_settle_s
-        while time.perf_counter() < t_end:
-            for _ in range(5):
-                moe(x)
-            torch.cuda.synchronize()
+        # load phase: the same number of steps on every rank (each step's
+        # exchange waits for every peer's same step), about clock_settle_s
+        for _ in range(int(args.clock_settle_s * 3000)):
+            moe.replay()
+        torch.cuda.synchronize()
         for _ in range(args.warmup):
-            moe(x)
+            moe.replay()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
         e0.record()
         for _ in range(args.steps):
-            moe(x)
+            moe.replay()
         e1.record()
         barrier()
         return e0.elapsed_time(e1)
@@ -648,6 +653,15 @@ def run_ours_ep(args):
         sampler.start()
     span_ms = timed_run()
     clocks = sampler.stop() if sampler else None
+    # stage pass (eager steps, an event between stages; every rank does it)
+    ns = len(PeerExpertParallelMoE.STAGES)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(ns + 1)] for _ in range(10)]
+    barrier()
+    for i in range(10):
+        moe(x, events=evs[i])
+    barrier()
+    stage_us = {name: round(statistics.median(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(10)) * 1e3, 1)
+                for j, name in enumerate(PeerExpertParallelMoE.STAGES)}
     t = torch.tensor([span_ms], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     span_ms = float(t[0])
@@ -663,13 +677,18 @@ def run_ours_ep(args):
 
     x_host = x.cpu().pin_memory()
     y_host = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        x_static.copy_(x_host, non_blocking=True)
+        y_host.copy_(moe.replay(), non_blocking=True)
+
     for _ in range(max(args.warmup, 3)):
-        y_host.copy_(moe(x_host.to(dev, non_blocking=True)), non_blocking=True)
+        e2e_step()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        y_host.copy_(moe(x_host.to(dev, non_blocking=True)), non_blocking=True)
+        e2e_step()
     e1.record()
     barrier()
     te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
@@ -685,8 +704,9 @@ def run_ours_ep(args):
                    "moe_intermediate": I_MOE, "parallelism": f"ep{world}",
                    "l2": "inputs larger than L2: expert weights and all-to-all buffers streamed per step"},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2,
-                "api": "PeerExpertParallelMoE.forward(hidden_states), pinned host in/out"},
-        "gpu_launches": 12 * args.steps,
+                "api": "PeerExpertParallelMoE step (CUDA graph replay of its forward), pinned host in/out"},
+        "gpu_launches": 9 * args.steps,
+        "stage_us_rank0": stage_us,
         "roofline": {"bound": "hbm", "kernel": "whole EP step (local experts' weights + rows in/out)",
                      "achieved": achieved, "peak": hbm_gbs, "unit": "GB/s", "frac": achieved / hbm_gbs,
                      "peak_kind": peak_kind, "traffic": None, "algorithmic_bytes_per_step": exp_bytes,

@@ -390,18 +390,30 @@ QMOE_API int qmoe_ep_unpack(const void* y_back, const int32_t* pair_pos, const v
  *   handle (peer access enabled lazily) and returns the pointer at `offset`
  *   plus the mapping base for close.
  * qmoe_ep_ctrl_words: int32 words of one rank's control block (two parity
- *   halves of [N x E counts | 3 x N flags]); zero it once before first use.
+ *   halves of [N x E counts | 3 x N flags], then the rank's step counter);
+ *   zero it once before first use.
+ * Epochs: every step of a rank has epoch = step number (1, 2, ...) and uses
+ *   the buffer halves of parity epoch & 1.  Pass the epoch explicitly, or 0
+ *   to take it from the step counter (then the kind-2 signal advances the
+ *   counter, and each parity's step is one fixed, graph-capturable sequence
+ *   of calls).  A parity that does not match the epoch is device error 4.
  * qmoe_ep_exchange_counts: one CTA.  Writes this rank's per-expert row
  *   counts (from qmoe_moe_permute) into every peer's control block, flags
  *   them, waits (bounded) for every rank's counts, then writes dest_base (E):
  *   the first row of this rank's rows of expert e in e's owner's receive
  *   buffer; the tile list of the local experts over this rank's receive
- *   buffer (expert ids local, 0..e_local-1); and recv_rows[0].
+ *   buffer (expert ids local, 0..e_local-1); and recv_rows[0]; and zero-fills
+ *   zero_words (n_zero_words int32, or NULL / 0).
  * qmoe_ep_dispatch: copies every (token, slot) row of x straight into the
  *   owner's receive buffer (peer_recv_x[d] + (parity*cap_rows + row)*H) with
  *   meta {weight bits, source rank, token*k + slot, 0} (int4 per row).
  * qmoe_ep_signal_wait: one warp; flag `kind` (1 dispatch, 2 combine) of this
- *   rank in every peer, then wait (bounded) for every rank's flag.
+ *   rank in every peer, then wait (bounded) for every rank's flag; kind 2
+ *   with epoch 0 then advances the step counter.
+ * qmoe_moe_experts_return: gate/up + down in one persistent kernel (as
+ *   qmoe_moe_experts, x = the receive rows) whose down epilogue stores into
+ *   the source ranks' return buffers as qmoe_grouped_gemm_down_return does;
+ *   done int32[max_tiles + 2] zero (qmoe_ep_exchange_counts' zero_words).
  * qmoe_grouped_gemm_down_return: K3b whose epilogue stores each weighted bf16
  *   row into the SOURCE rank's return buffer: peer_ret[src] + (ret_row0 +
  *   token*k + slot)*H (the combine, fused into the GEMM, over peer memory).
@@ -415,7 +427,8 @@ QMOE_API int64_t qmoe_ep_ctrl_words(int64_t n_ranks, int64_t E);
 QMOE_API int qmoe_ep_exchange_counts(const int32_t* counts, int* const* peer_ctrl, int* my_ctrl, int64_t me,
                                      int64_t n_ranks, int64_t E, int64_t e_local, int64_t parity,
                                      int64_t epoch, int32_t* dest_base, int32_t* tiles, int64_t max_tiles,
-                                     int32_t* recv_rows, int64_t cap_rows, void* stream);
+                                     int32_t* recv_rows, int64_t cap_rows, int32_t* zero_words,
+                                     int64_t n_zero_words, void* stream);
 QMOE_API int qmoe_ep_dispatch(const void* x, const int32_t* topk_idx, const float* topk_w,
                               const int32_t* slot_row, const int32_t* offsets, const int32_t* dest_base,
                               void* const* peer_recv_x, void* const* peer_recv_meta, int64_t T, int64_t k,
@@ -423,6 +436,10 @@ QMOE_API int qmoe_ep_dispatch(const void* x, const int32_t* topk_idx, const floa
                               void* stream);
 QMOE_API int qmoe_ep_signal_wait(int* const* peer_ctrl, int* my_ctrl, int64_t n_ranks, int64_t E,
                                  int64_t me, int64_t parity, int64_t kind, int64_t epoch, void* stream);
+QMOE_API int qmoe_moe_experts_return(const void* x, const void* w_gate_up, const void* w_down, const int32_t* tiles,
+                                     int64_t max_tiles, const void* row_meta, void* const* peer_ret,
+                                     int64_t ret_row0, int64_t n_ret_rows, int64_t n_ranks, int64_t R, int64_t H,
+                                     int64_t I, int64_t E, void* act, int32_t* done, void* stream);
 QMOE_API int qmoe_grouped_gemm_down_return(const void* act, const void* w_down, const int32_t* tiles,
                                            int64_t max_tiles, const void* row_meta, void* const* peer_ret,
                                            int64_t ret_row0, int64_t n_ret_rows, int64_t n_ranks, int64_t R,

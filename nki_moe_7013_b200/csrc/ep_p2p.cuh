@@ -25,6 +25,13 @@
 // is still reading: writing parity p of step i+2 requires the peer's step
 // i+2 counts, which the peer publishes only after finishing step i.
 //
+// Step epochs: the flags carry the step number (epoch), so a flag from an
+// older step never satisfies a newer wait.  A caller passes the epoch, or 0
+// to use the rank's own device-side step counter (the last word of its
+// control block, advanced by the step's final signal kernel): then a step is
+// a fixed sequence of kernels with fixed arguments per parity, and two CUDA
+// graphs (one per parity) replay the steps alternately.
+//
 // Every cross-GPU wait is bounded (kWaitLimitNs); on time-out the kernel
 // records a device error and returns.  No cluster-multicast load anywhere.
 #pragma once
@@ -39,6 +46,20 @@ __host__ __device__ __forceinline__ size_t ep_ctrl_words_per_parity(int N, int E
   return size_t(N) * E + 3 * size_t(N);
 }
 enum EpFlagKind : int { kEpFlagCounts = 0, kEpFlagDispatch = 1, kEpFlagCombine = 2 };
+
+// Index of the device-side step counter (after both parity halves).
+__host__ __device__ __forceinline__ size_t ep_step_word(int N, int E) { return 2 * ep_ctrl_words_per_parity(N, E); }
+
+// The step's epoch: the caller's, or (epoch == 0) the device counter + 1.
+// Its parity must be p (the caller's buffers); false + device error if not.
+__device__ __forceinline__ bool ep_resolve_epoch(const int* my_ctrl, int N, int E, int p, int& epoch) {
+  if (epoch == 0) epoch = *reinterpret_cast<const volatile int*>(my_ctrl + ep_step_word(N, E)) + 1;
+  if ((epoch & 1) != p) {
+    record_device_error(kDevErrBadIndex);
+    return false;
+  }
+  return true;
+}
 
 __device__ __forceinline__ size_t ep_flag_word(int N, int E, int p, int kind, int s) {
   return p * ep_ctrl_words_per_parity(N, E) + size_t(N) * E + size_t(kind) * N + s;
@@ -91,12 +112,22 @@ __global__ void __launch_bounds__(256)
     ep_exchange_counts_kernel(const int32_t* __restrict__ counts, int* const* __restrict__ peer_ctrl,
                               int* __restrict__ my_ctrl, int me, int N, int E, int e_local, int p, int epoch,
                               int32_t* __restrict__ dest_base, int32_t* __restrict__ tiles, int max_tiles,
-                              int32_t* __restrict__ recv_rows, int cap_rows) {
+                              int32_t* __restrict__ recv_rows, int cap_rows, int32_t* __restrict__ zero_words,
+                              int n_zero_words) {
   __shared__ int tot[256];
   __shared__ int expert_off[257];
   __shared__ int ok_s;
   const int tid = threadIdx.x;
   griddep_wait();
+  // scratch the step's expert kernel needs zeroed (its tile counters)
+  for (int i = tid; i < n_zero_words; i += blockDim.x) zero_words[i] = 0;
+  if (!ep_resolve_epoch(my_ctrl, N, E, p, epoch)) {
+    if (tid == 0) {
+      tiles[0] = 0;
+      recv_rows[0] = 0;
+    }
+    return;
+  }
   // my counts row into every peer's matrix
   for (int i = tid; i < N * E; i += blockDim.x) {
     const int d = i / E, e = i - d * E;
@@ -199,7 +230,11 @@ __global__ void __launch_bounds__(32)
     ep_signal_wait_kernel(int* const* __restrict__ peer_ctrl, int* __restrict__ my_ctrl, int N, int E, int me,
                           int p, int kind, int epoch) {
   griddep_wait();
-  ep_signal_and_wait(peer_ctrl, my_ctrl, N, E, me, p, kind, epoch);
+  const bool device_epoch = epoch == 0;
+  if (!ep_resolve_epoch(my_ctrl, N, E, p, epoch)) return;
+  const bool ok = ep_signal_and_wait(peer_ctrl, my_ctrl, N, E, me, p, kind, epoch);
+  // the step's last wait: advance the device step counter
+  if (ok && device_epoch && kind == kEpFlagCombine && threadIdx.x == 0) my_ctrl[ep_step_word(N, E)] = epoch;
 }
 
 }  // namespace qmoe

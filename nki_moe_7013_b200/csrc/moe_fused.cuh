@@ -73,6 +73,13 @@ struct FusedArgs {
   // fin_residual) -- the finalize kernel folded in
   const __nv_bfloat16* fin_residual;
   __nv_bfloat16* fin_out;
+  // expert-parallel return (kReturn): per row {weight bits, source rank,
+  // return row, 0}; the weighted bf16 row goes to peer_ret[source] +
+  // (ret_row0 + return row) * acc_ld instead of the fp32 accumulator
+  const int4* row_meta;
+  __nv_bfloat16* const* peer_ret;
+  int ret_row0;
+  int n_ranks;
   // non-null: gate/up row r of a tile is token row gather_rows[r] of x (TMA
   // gather4; tmB_gu maps x with 1-row boxes), else row r of the permuted copy
   const int32_t* gather_rows;
@@ -95,6 +102,7 @@ __device__ __forceinline__ bool wait_tile_done(const int* done, int target, vola
   return true;
 }
 
+template <bool kReturn = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     moe_fused_kernel(const __grid_constant__ CUtensorMap tmA_gu, const __grid_constant__ CUtensorMap tmB_gu,
                      const __grid_constant__ CUtensorMap tmA_dn, const __grid_constant__ CUtensorMap tmB_dn,
@@ -435,6 +443,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int et = threadIdx.x - 64;
     int32_t* meta_dst = reinterpret_cast<int32_t*>(staging + 4 * 16 * 33);
     float* meta_w = reinterpret_cast<float*>(meta_dst + 128);
+    int32_t* meta_src = meta_dst + 256;
     for (int local = 0;; ++local) {
       const int q = local % C::kUnitQueue;
       const bool got = mbar_wait_bounded(&uq_full[q], (local / C::kUnitQueue) & 1, abort_flag,
@@ -452,11 +461,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int nb = (nrows + kBoxRows - 1) / kBoxRows;
       const int buf = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      int my_dst = -1;
+      int my_dst = -1, my_src = 0;
       float my_w = 0.f;
       if (!gu && et < nrows) {
-        my_dst = args.row_dst[row0 + et];
-        my_w = args.row_w[row0 + et];
+        if constexpr (kReturn) {
+          const int4 m4 = args.row_meta[row0 + et];
+          my_w = __int_as_float(m4.x);
+          my_src = (m4.y >= 0 && m4.y < args.n_ranks) ? m4.y : -1;
+          my_dst = my_src >= 0 ? m4.z : -1;
+        } else {
+          my_dst = args.row_dst[row0 + et];
+          my_w = args.row_w[row0 + et];
+        }
       }
       const bool ok = mbar_wait_bounded(&acc_full[buf], acc_phase, abort_flag, kDevErrWaitTimeoutEpilogue);
       if (named_barrier_or(1, 128, !ok)) break;
@@ -464,6 +480,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!gu) {
         meta_dst[et] = (my_dst >= 0 && my_dst < args.n_acc) ? my_dst : -1;
         meta_w[et] = my_w;
+        meta_src[et] = my_src;
         named_barrier_sync(1, 128);
       }
       tc_fence_after();
@@ -502,9 +519,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               const int dst = meta_dst[n];
               if (dst >= 0) {
                 const float wv = meta_w[n];
-                red_add_v4_f32(args.acc + size_t(dst) * args.acc_ld + mt * kBM + quad * 32 + fq,
-                               wv * wsb[i * 33 + fq], wv * wsb[i * 33 + fq + 1], wv * wsb[i * 33 + fq + 2],
-                               wv * wsb[i * 33 + fq + 3]);
+                if constexpr (kReturn) {
+                  // weighted row segment straight into the source rank's return buffer
+                  __nv_bfloat16* ret = args.peer_ret[meta_src[n]] + (size_t(args.ret_row0) + dst) * args.acc_ld +
+                                       mt * kBM + quad * 32 + fq;
+                  const __nv_bfloat162 lo = __floats2bfloat162_rn(wv * wsb[i * 33 + fq], wv * wsb[i * 33 + fq + 1]);
+                  const __nv_bfloat162 hi =
+                      __floats2bfloat162_rn(wv * wsb[i * 33 + fq + 2], wv * wsb[i * 33 + fq + 3]);
+                  uint2 pk;
+                  pk.x = *reinterpret_cast<const uint32_t*>(&lo);
+                  pk.y = *reinterpret_cast<const uint32_t*>(&hi);
+                  *reinterpret_cast<uint2*>(ret) = pk;
+                } else {
+                  red_add_v4_f32(args.acc + size_t(dst) * args.acc_ld + mt * kBM + quad * 32 + fq,
+                                 wv * wsb[i * 33 + fq], wv * wsb[i * 33 + fq + 1], wv * wsb[i * 33 + fq + 2],
+                                 wv * wsb[i * 33 + fq + 3]);
+                }
               }
             }
           }
@@ -524,6 +554,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (threadIdx.x == 64) QMOE_TRACE_AT(1, 6);
   }
 
+  if constexpr (kReturn) __threadfence_system();  // peer stores before the step's next signal
   __syncthreads();
   if (threadIdx.x == 0) QMOE_TRACE_AT(1, 7);
   if (warp == 1) {
@@ -531,7 +562,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, C::kTmemCols);
   }
-  if (args.fin_out != nullptr && grid_barrier_once(args.done + args.max_tiles + 1, kDevErrWaitTimeoutEpilogue)) {
+  if (!kReturn && args.fin_out != nullptr &&
+      grid_barrier_once(args.done + args.max_tiles + 1, kDevErrWaitTimeoutEpilogue)) {
     const long long n8 = (long long)args.n_acc * args.acc_ld / 8;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8;
          i += (long long)gridDim.x * blockDim.x)

@@ -434,7 +434,8 @@ int launch_moe_fused(const void* x, int64_t x_rows, const int32_t* gather_rows, 
                      const void* w_down, const int32_t* tiles, int64_t max_tiles, const int32_t* row_dst,
                      const float* row_w, int64_t R, int64_t H, int64_t I, int64_t E, void* act, float* acc,
                      int64_t n_acc, int32_t* done, cudaStream_t stream, const void* fin_residual = nullptr,
-                     void* fin_out = nullptr) {
+                     void* fin_out = nullptr, const void* row_meta = nullptr, void* const* peer_ret = nullptr,
+                     int64_t ret_row0 = 0, int64_t n_ranks = 0) {
   using C = qmoe::FusedCfg;
   CUtensorMap ta_gu, tb_gu, ta_dn, tb_dn;
   QMOE_CHECK(make_tmap_bf16(&ta_gu, w_gate_up, uint64_t(H), uint64_t(E * 2 * I), qmoe::kBK, qmoe::kBM));
@@ -465,12 +466,21 @@ int launch_moe_fused(const void* x, int64_t x_rows, const int32_t* gather_rows, 
   a.gather_rows = gather_rows;
   a.fin_residual = static_cast<const __nv_bfloat16*>(fin_residual);
   a.fin_out = static_cast<__nv_bfloat16*>(fin_out);
+  a.row_meta = static_cast<const int4*>(row_meta);
+  a.peer_ret = reinterpret_cast<__nv_bfloat16* const*>(peer_ret);
+  a.ret_row0 = int(ret_row0);
+  a.n_ranks = int(n_ranks);
   const int64_t units = max_tiles * (a.n_mt_gu + a.n_mt_dn);
   const int grid = int(std::min<int64_t>(units, num_sms(0)));
   if (grid <= 0) return QMOE_OK;
-  QMOE_CHECK(set_smem(qmoe::moe_fused_kernel, C::kSmemBytes));
-  return launch_kernel(qmoe::moe_fused_kernel, dim3(grid), dim3(qmoe::kGemmThreads), C::kSmemBytes, stream, true,
-                       "moe_fused_kernel", ta_gu, tb_gu, ta_dn, tb_dn, a);
+  if (a.peer_ret != nullptr) {
+    QMOE_CHECK(set_smem(qmoe::moe_fused_kernel<true>, C::kSmemBytes));
+    return launch_kernel(qmoe::moe_fused_kernel<true>, dim3(grid), dim3(qmoe::kGemmThreads), C::kSmemBytes, stream,
+                         true, "moe_fused_kernel<return>", ta_gu, tb_gu, ta_dn, tb_dn, a);
+  }
+  QMOE_CHECK(set_smem(qmoe::moe_fused_kernel<false>, C::kSmemBytes));
+  return launch_kernel(qmoe::moe_fused_kernel<false>, dim3(grid), dim3(qmoe::kGemmThreads), C::kSmemBytes, stream,
+                       true, "moe_fused_kernel", ta_gu, tb_gu, ta_dn, tb_dn, a);
 }
 
 // RMSNorm launch with the row held in registers: kChunks 128-element chunks
@@ -1086,17 +1096,19 @@ int qmoe_ipc_close(void* base) {
 
 int64_t qmoe_ep_ctrl_words(int64_t n_ranks, int64_t E) {
   if (n_ranks <= 0 || E <= 0) return 0;
-  return 2 * int64_t(qmoe::ep_ctrl_words_per_parity(int(n_ranks), int(E)));
+  return int64_t(qmoe::ep_step_word(int(n_ranks), int(E))) + 4;  // both halves + the step counter
 }
 
 int qmoe_ep_exchange_counts(const int32_t* counts, int* const* peer_ctrl, int* my_ctrl, int64_t me,
                             int64_t n_ranks, int64_t E, int64_t e_local, int64_t parity, int64_t epoch,
                             int32_t* dest_base, int32_t* tiles, int64_t max_tiles, int32_t* recv_rows,
-                            int64_t cap_rows, void* stream) {
+                            int64_t cap_rows, int32_t* zero_words, int64_t n_zero_words, void* stream) {
+  QMOE_REQUIRE(!zero_words == (n_zero_words == 0) && n_zero_words >= 0 && n_zero_words < (int64_t(1) << 24),
+               QMOE_ERR_INVALID_ARGUMENT, "ep_exchange_counts: bad zero_words");
   QMOE_REQUIRE(counts && peer_ctrl && my_ctrl && dest_base && tiles && recv_rows, QMOE_ERR_INVALID_ARGUMENT,
                "ep_exchange_counts: null pointer");
   QMOE_REQUIRE(n_ranks >= 1 && n_ranks <= 32 && me >= 0 && me < n_ranks && E >= 1 && E <= 256 &&
-                   e_local >= 1 && e_local * n_ranks == E && (parity == 0 || parity == 1) && epoch > 0 &&
+                   e_local >= 1 && e_local * n_ranks == E && (parity == 0 || parity == 1) && epoch >= 0 &&
                    epoch < (int64_t(1) << 31) && max_tiles > 0 && cap_rows > 0 && cap_rows < (int64_t(1) << 31),
                QMOE_ERR_INVALID_ARGUMENT, "ep_exchange_counts: bad sizes");
   DeviceInfo* d = nullptr;
@@ -1104,7 +1116,7 @@ int qmoe_ep_exchange_counts(const int32_t* counts, int* const* peer_ctrl, int* m
   return launch_kernel(qmoe::ep_exchange_counts_kernel, dim3(1), dim3(256), 0, static_cast<cudaStream_t>(stream),
                        true, "ep_exchange_counts_kernel", counts, peer_ctrl, my_ctrl, int(me), int(n_ranks),
                        int(E), int(e_local), int(parity), int(epoch), dest_base, tiles, int(max_tiles),
-                       recv_rows, int(cap_rows));
+                       recv_rows, int(cap_rows), zero_words, int(n_zero_words));
 }
 
 int qmoe_ep_dispatch(const void* x, const int32_t* topk_idx, const float* topk_w, const int32_t* slot_row,
@@ -1132,13 +1144,33 @@ int qmoe_ep_signal_wait(int* const* peer_ctrl, int* my_ctrl, int64_t n_ranks, in
                         int64_t parity, int64_t kind, int64_t epoch, void* stream) {
   QMOE_REQUIRE(peer_ctrl && my_ctrl, QMOE_ERR_INVALID_ARGUMENT, "ep_signal_wait: null pointer");
   QMOE_REQUIRE(n_ranks >= 1 && n_ranks <= 32 && me >= 0 && me < n_ranks && (parity == 0 || parity == 1) &&
-                   kind >= 0 && kind <= 2 && epoch > 0 && E >= 1,
+                   kind >= 0 && kind <= 2 && epoch >= 0 && epoch < (int64_t(1) << 31) && E >= 1,
                QMOE_ERR_INVALID_ARGUMENT, "ep_signal_wait: bad arguments");
   DeviceInfo* d = nullptr;
   QMOE_CHECK(device_info(&d));
   return launch_kernel(qmoe::ep_signal_wait_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), true,
                        "ep_signal_wait_kernel", peer_ctrl, my_ctrl, int(n_ranks), int(E), int(me), int(parity),
                        int(kind), int(epoch));
+}
+
+int qmoe_moe_experts_return(const void* x, const void* w_gate_up, const void* w_down, const int32_t* tiles,
+                            int64_t max_tiles, const void* row_meta, void* const* peer_ret, int64_t ret_row0,
+                            int64_t n_ret_rows, int64_t n_ranks, int64_t R, int64_t H, int64_t I, int64_t E,
+                            void* act, int32_t* done, void* stream) {
+  QMOE_REQUIRE(x && w_gate_up && w_down && tiles && row_meta && peer_ret && act && done, QMOE_ERR_INVALID_ARGUMENT,
+               "moe_experts_return: null pointer");
+  QMOE_REQUIRE(R >= 0 && R < (int64_t(1) << 31) && H > 0 && H % qmoe::kBM == 0 && I > 0 && I % qmoe::kBM == 0 &&
+                   E > 0 && E * 2 * I < (int64_t(1) << 31) && E * H < (int64_t(1) << 31) && n_ret_rows > 0 &&
+                   ret_row0 >= 0 && n_ranks >= 1 && max_tiles >= 0 && max_tiles < (int64_t(1) << 24),
+               QMOE_ERR_INVALID_ARGUMENT, "moe_experts_return: bad sizes");
+  QMOE_REQUIRE(aligned16(x) && aligned16(w_gate_up) && aligned16(w_down) && aligned16(act) && aligned16(row_meta),
+               QMOE_ERR_MISALIGNED, "moe_experts_return: pointers must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  if (R == 0) return QMOE_OK;
+  return launch_moe_fused(x, R, nullptr, w_gate_up, w_down, tiles, max_tiles, nullptr, nullptr, R, H, I, E, act,
+                          nullptr, n_ret_rows, done, static_cast<cudaStream_t>(stream), nullptr, nullptr, row_meta,
+                          peer_ret, ret_row0, n_ranks);
 }
 
 int qmoe_grouped_gemm_down_return(const void* act, const void* w_down, const int32_t* tiles, int64_t max_tiles,

@@ -127,17 +127,24 @@ class ExpertParallelMoE(nn.Module):
 class PeerExpertParallelMoE(nn.Module):
     """Expert-parallel block whose exchange runs through peer memory inside
     one node (CUDA IPC mappings over NVLink / NVSwitch) with no host sync, so
-    a step is a fixed sequence of stream-ordered kernels (graph-capturable).
+    a step is a fixed sequence of stream-ordered kernels.
 
     Kernels per step: router, permutation (counts / offsets / slot rows),
     count exchange, dispatch (rows of x straight into the owners' receive
-    buffers, already grouped by expert), signal/wait, gate/up GEMM on the
-    receive buffer, down GEMM whose epilogue stores the weighted rows into the
-    source ranks' return buffers, signal/wait, unpack.
+    buffers, already grouped by expert), signal/wait, gate/up + down in one
+    persistent kernel on the receive buffer whose down epilogue stores the
+    weighted rows into the source ranks' return buffers, signal/wait, unpack.
 
     Buffers (identical shapes on every rank, two parity halves each):
     receive rows (P*max_tokens*k, H), their meta, return rows
-    (max_tokens*k, H), and the control block (counts + flags)."""
+    (max_tokens*k, H), and the control block (counts + flags + the rank's
+    step counter).  The kernels take the step's epoch from the device-side
+    step counter, so each parity's step has fixed arguments: ``capture``
+    records one CUDA graph per parity and ``replay`` runs the next step with
+    no host work beyond the graph launch.  Every rank must run the same steps
+    in the same order (each step's exchange waits for every peer's step of
+    the same number); a rank that runs an extra step waits out the bounded
+    wait limit and records device error 5."""
 
     def __init__(self, cfg: Qwen3MoeConfig, router_weight: torch.Tensor, local: MoEWeights,
                  max_tokens: int, group=None):
@@ -165,6 +172,7 @@ class PeerExpertParallelMoE(nn.Module):
         self.cap = self.world * max_tokens * k          # receive rows per parity
         self.ret_rows = max_tokens * k                  # return rows per parity
         i32 = dict(dtype=torch.int32, device=dev)
+        f32 = dict(dtype=torch.float32, device=dev)
         self.recv_x = torch.empty((2 * self.cap, H), dtype=torch.bfloat16, device=dev)
         self.recv_meta = torch.zeros((2 * self.cap, 4), **i32)
         self.ret = torch.empty((2 * self.ret_rows, H), dtype=torch.bfloat16, device=dev)
@@ -174,6 +182,21 @@ class PeerExpertParallelMoE(nn.Module):
         self.tiles = torch.zeros(1 + 3 * self.max_tiles, **i32)
         self.recv_rows = torch.zeros(1, **i32)
         self.act = torch.empty((self.cap, I), dtype=torch.bfloat16, device=dev)
+        # counters of the fused expert kernel (zeroed each step by the exchange)
+        self.done = torch.zeros(self.max_tiles + 2, **i32)
+        # routing / permutation buffers of the local tokens (max_tokens)
+        R = max_tokens * k
+        nchunks = (max_tokens + ops.ROUTER_CHUNK - 1) // ops.ROUTER_CHUNK
+        self.topk_idx = torch.empty((max_tokens, k), **i32)
+        self.topk_w = torch.empty((max_tokens, k), **f32)
+        self.hist = torch.empty((max(nchunks, 1), E), **i32)
+        self.counts = torch.empty(E, **i32)
+        self.offsets = torch.empty(E + 1, **i32)
+        self.row_token = torch.empty(max(R, 1), **i32)
+        self.row_w = torch.empty(max(R, 1), **f32)
+        self.slot_row = torch.empty((max_tokens, k), **i32)
+        self.perm_tiles = torch.empty(1 + 3 * ops.max_tiles(R, E), **i32)
+        self.logits = torch.empty((max_tokens, E), **f32)
         torch.cuda.synchronize(dev)
         self._imported = []
         names = ("recv_x", "recv_meta", "ret", "ctrl")
@@ -202,51 +225,115 @@ class PeerExpertParallelMoE(nn.Module):
         self.peer = {n: torch.tensor(ptrs[n], dtype=torch.int64, device=dev) for n in names}
         torch.cuda.synchronize(dev)
         dist.barrier(group=group)
-        self.epoch = 0
+        self.steps = 0        # steps issued (the device counter follows in stream order)
+        self._graphs = None   # (graph of parity 0, graph of parity 1)
+        self._static = None
 
     def close(self):
         """Unmap the peers' buffers (all ranks should be done with the exchange)."""
         from . import _C
 
         torch.cuda.synchronize(self.device)
+        self._graphs = None
         for base in self._imported:
             _C.check(self._lib.qmoe_ipc_close(base), "qmoe_ipc_close")
         self._imported = []
 
-    def forward(self, hidden_states: torch.Tensor, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    STAGES = ("router", "permute", "exchange", "dispatch", "experts", "return_wait", "unpack")
+
+    def _issue(self, x: torch.Tensor, residual: Optional[torch.Tensor], out: torch.Tensor, par: int,
+               events=None) -> None:
+        """The step's kernels for parity `par` on the current stream (epochs
+        from the device step counter).  ``events``: len(STAGES) + 1 CUDA
+        events recorded before the first kernel and after each stage."""
         from . import _C
 
-        shape = hidden_states.shape
-        H, E, k, I = self.H, self.E, self.k, self.I
-        x = hidden_states.reshape(-1, H).to(torch.bfloat16).contiguous()
+        def mark(i):
+            if events is not None:
+                events[i].record()
+
+        mark(0)
         T = x.shape[0]
-        if T > self.max_tokens:
-            raise ValueError(f"{T} tokens exceed max_tokens={self.max_tokens} of the EP buffers")
+        H, E, k, I = self.H, self.E, self.k, self.I
         lib, pt = self._lib, ops._ptr
         s = torch.cuda.current_stream(self.device).cuda_stream
-        self.epoch += 1
-        par, ep = self.epoch & 1, self.epoch
-        idx, tw, hist = ops.router_topk(x, self.router_weight, k, bias=self.router_bias, return_hist=True)
-        perm = ops.moe_permute(idx, tw, hist, E)
+        logits = self.logits if T <= ops.ROUTER_SMALL_MAX_T else None
+        _C.check(lib.qmoe_router_topk(pt(x), pt(self.router_weight), pt(self.router_bias), T, H, E, k, 1,
+                                      pt(logits), pt(self.topk_idx), pt(self.topk_w), pt(self.hist), s),
+                 "qmoe_router_topk")
+        mark(1)
+        _C.check(lib.qmoe_moe_permute(pt(self.topk_idx), pt(self.topk_w), pt(self.hist), None, T, H, E, k,
+                                      pt(self.counts), pt(self.offsets), pt(self.row_token), pt(self.row_w),
+                                      pt(self.slot_row), pt(self.perm_tiles), None, None, None, 0, s),
+                 "qmoe_moe_permute")
+        mark(2)
         _C.check(lib.qmoe_ep_exchange_counts(
-            pt(perm["counts"]), pt(self.peer["ctrl"]), pt(self.ctrl), self.rank, self.world, E, self.e_local,
-            par, ep, pt(self.dest_base), pt(self.tiles), self.max_tiles, pt(self.recv_rows), self.cap, s),
-            "qmoe_ep_exchange_counts")
+            pt(self.counts), pt(self.peer["ctrl"]), pt(self.ctrl), self.rank, self.world, E, self.e_local,
+            par, 0, pt(self.dest_base), pt(self.tiles), self.max_tiles, pt(self.recv_rows), self.cap,
+            pt(self.done), self.max_tiles + 2, s), "qmoe_ep_exchange_counts")
+        mark(3)
         _C.check(lib.qmoe_ep_dispatch(
-            pt(x), pt(idx), pt(tw), pt(perm["slot_row"]), pt(perm["offsets"]), pt(self.dest_base),
+            pt(x), pt(self.topk_idx), pt(self.topk_w), pt(self.slot_row), pt(self.offsets), pt(self.dest_base),
             pt(self.peer["recv_x"]), pt(self.peer["recv_meta"]), T, k, H, self.e_local, self.rank, par,
             self.cap, s), "qmoe_ep_dispatch")
         _C.check(lib.qmoe_ep_signal_wait(pt(self.peer["ctrl"]), pt(self.ctrl), self.world, E, self.rank, par, 1,
-                                         ep, s), "qmoe_ep_signal_wait")
+                                         0, s), "qmoe_ep_signal_wait")
+        mark(4)
         recv_x = self.recv_x[par * self.cap:(par + 1) * self.cap]
-        ops.grouped_gemm_gateup_swiglu(recv_x, self.local.gate_up, self.tiles, self.max_tiles, out=self.act)
-        _C.check(lib.qmoe_grouped_gemm_down_return(
-            pt(self.act), pt(self.local.down), pt(self.tiles), self.max_tiles,
+        # gate/up + down in one persistent kernel; its down epilogue stores
+        # each weighted row into the source rank's return buffer
+        _C.check(lib.qmoe_moe_experts_return(
+            pt(recv_x), pt(self.local.gate_up), pt(self.local.down), pt(self.tiles), self.max_tiles,
             pt(self.recv_meta[par * self.cap:]), pt(self.peer["ret"]), par * self.ret_rows, self.ret_rows,
-            self.world, self.cap, H, I, self.e_local, s), "qmoe_grouped_gemm_down_return")
+            self.world, self.cap, H, I, self.e_local, pt(self.act), pt(self.done), s), "qmoe_moe_experts_return")
+        mark(5)
         _C.check(lib.qmoe_ep_signal_wait(pt(self.peer["ctrl"]), pt(self.ctrl), self.world, E, self.rank, par, 2,
-                                         ep, s), "qmoe_ep_signal_wait")
+                                         0, s), "qmoe_ep_signal_wait")
+        mark(6)
         y_back = self.ret[par * self.ret_rows:par * self.ret_rows + T * k]
-        res = None if residual is None else residual.reshape(-1, H).to(torch.bfloat16).contiguous()
-        out = ops.ep_unpack(y_back, None, res, T=T, k=k)
+        _C.check(lib.qmoe_ep_unpack(pt(y_back), None, pt(residual), T, H, k, T * k, pt(out), s),
+                 "qmoe_ep_unpack")
+        mark(7)
+
+    def forward(self, hidden_states: torch.Tensor, residual: Optional[torch.Tensor] = None,
+                events=None) -> torch.Tensor:
+        shape = hidden_states.shape
+        x = hidden_states.reshape(-1, self.H).to(torch.bfloat16).contiguous()
+        T = x.shape[0]
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed max_tokens={self.max_tokens} of the EP buffers")
+        res = None if residual is None else residual.reshape(-1, self.H).to(torch.bfloat16).contiguous()
+        out = torch.empty((T, self.H), dtype=torch.bfloat16, device=self.device)
+        self.steps += 1
+        self._issue(x, res, out, self.steps & 1, events)
         return out.reshape(shape)
+
+    def capture(self, hidden_states: torch.Tensor, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Record one CUDA graph per parity over static copies of the inputs;
+        returns the static output that every ``replay`` overwrites.  Every
+        rank captures with the same shapes (no kernel runs during capture)."""
+        x = hidden_states.reshape(-1, self.H).to(torch.bfloat16).contiguous().clone()
+        T = x.shape[0]
+        res = None if residual is None else residual.reshape(-1, self.H).to(torch.bfloat16).contiguous().clone()
+        out = torch.empty((T, self.H), dtype=torch.bfloat16, device=self.device)
+        graphs = []
+        for par in (0, 1):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._issue(x, res, out, par)
+            graphs.append(g)
+        self._graphs = tuple(graphs)
+        self._static = (x, res, out)
+        return out
+
+    def replay(self) -> torch.Tensor:
+        """Run the next step from the captured graphs (inputs: the static
+        buffers ``capture`` returned alongside, ``static_input()``)."""
+        if self._graphs is None:
+            raise RuntimeError("capture() first")
+        self.steps += 1
+        self._graphs[self.steps & 1].replay()
+        return self._static[2]
+
+    def static_input(self) -> torch.Tensor:
+        return self._static[0]

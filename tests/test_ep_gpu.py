@@ -93,11 +93,14 @@ def _nccl_worker(rank, world, port, out_dir):
     peer = PeerExpertParallelMoE(cfg, wr, local, max_tokens=T)
     res = normal_bf16_device(200 + rank, (T, H), 1.0, dev)
     outs += [peer(x), peer(x, residual=res), peer(x[: T // 2])]
+    # graph replays (one graph per parity), after the eager steps
+    peer.capture(x)
+    outs += [peer.replay().clone(), peer.replay().clone()]
     torch.cuda.synchronize()
     assert _C.device_error() == 0
     moe_ref = oracle.moe_block(x.cpu(), wr.cpu(), wgu.cpu(), wd.cpu(), k)
     ref = oracle.round_to_bf16(moe_ref)
-    refs = [ref, ref, ref, moe_ref + res.float().cpu().numpy(), ref[: T // 2]]
+    refs = [ref, ref, ref, moe_ref + res.float().cpu().numpy(), ref[: T // 2], ref, ref]
     errs = [float(np.abs(o.float().cpu().numpy() - r).max() / np.abs(r).max()) for o, r in zip(outs, refs)]
     np.save(os.path.join(out_dir, f"ep{rank}.npy"), np.array(errs))
     dist.barrier()
