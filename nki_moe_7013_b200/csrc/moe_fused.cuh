@@ -22,6 +22,20 @@
 // Down weights do not depend on anything, so the wait only gates the
 // activation loads of the unit's first stage.
 //
+// Unit shapes: a gate/up unit is 128 gate + the matching 128 up features of
+// one tile (two accumulators sharing the row operand); a down unit is 256
+// output features of one tile (two 128-feature accumulators sharing the
+// activation rows) when H is a multiple of 256, else 128.  Every stage then
+// carries two 16 KB weight tiles and the rows: 8 MMAs per 48 KB instead of 4
+// per 32 KB for single-tile down units, and the activation rows are read
+// half as often.
+//
+// The producer claims the unit after the one it is loading as soon as it has
+// claimed that one, so the counter's round trip overlaps a unit's loads
+// instead of draining the ring between units.  (Deadlock-free as above: a CTA
+// holding an unstarted unit is working on an earlier-drawn one, and only down
+// units wait -- on gate/up units, all of which were drawn before them.)
+//
 // Gate/up rows come from the permuted copy of the tokens (16-row boxes) or
 // straight from the token rows (TMA gather4 by row_token; no copy to write).
 //
@@ -54,7 +68,8 @@ struct FusedCfg {
 struct FusedArgs {
   const int32_t* tiles;  // [0] = ntiles, then expert[max_tiles], row0[max_tiles], nrows[max_tiles]
   int max_tiles;
-  int n_mt_gu, n_mt_dn;      // feature blocks: I / 128 and H / 128
+  int n_mt_gu, n_mt_dn;      // units per tile: I / 128 and H / (128 * (1 + dn_two))
+  int dn_two;                // 1: a down unit covers 256 features (two accumulators)
   int num_kb_gu, num_kb_dn;  // k blocks: H / 64 and I / 64
   int a_rows_gu;             // 2I
   int up_off;                // I
@@ -195,6 +210,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool ok = true;
       bool first = true;
       int* counter = args.done + args.max_tiles;
+      int next_u = -2;  // -2: nothing claimed ahead yet
       for (int i = 0;; ++i) {
         const int q = i % C::kUnitQueue;
         if (!mbar_wait_bounded(&uq_empty[q], ((i / C::kUnitQueue) & 1) ^ 1u, abort_flag,
@@ -202,8 +218,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           ok = false;
           break;
         }
-        int u = ok ? atomicAdd(counter, 1) : -1;
-        if (u >= total_units) u = -1;
+        int u = next_u == -2 ? atomicAdd(counter, 1) : next_u;
+        if (!ok || u >= total_units) u = -1;
+        next_u = u >= 0 ? atomicAdd(counter, 1) : -1;
         unit_q[q] = u;
         mbar_arrive(&uq_full[q]);
         if (u < 0) break;
@@ -219,9 +236,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         const CUtensorMap* ta = gu ? &tmA_gu : &tmA_dn;
         const CUtensorMap* tb = gu ? &tmB_gu : &tmB_dn;
-        const int a_row = gu ? e * args.a_rows_gu + mt * kBM : e * args.a_rows_dn + mt * kBM;
+        const bool two_a = gu || args.dn_two;
+        const int a_row = gu ? e * args.a_rows_gu + mt * kBM : e * args.a_rows_dn + mt * kBM * (1 + args.dn_two);
+        const int a2_row = a_row + (gu ? args.up_off : kBM);
         const int nkb = gu ? args.num_kb_gu : args.num_kb_dn;
-        const uint32_t bytes = (gu ? 2 : 1) * C::kABytes + nb * kBoxRows * kBK * 2;
+        const uint32_t bytes = (two_a ? 2 : 1) * C::kABytes + nb * kBoxRows * kBK * 2;
         for (int kb = 0; kb < nkb; ++kb) {
           uint8_t* sb = stages + stage * C::kStageBytes;
           uint8_t* bs = sb + 2 * C::kABytes;
@@ -231,7 +250,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           mbar_arrive_expect_tx(&full[stage], bytes);
           tma_load_2d_hint(sb, ta, kb * kBK, a_row, &full[stage], pol_w);
-          if (gu) tma_load_2d_hint(sb + C::kABytes, ta, kb * kBK, a_row + args.up_off, &full[stage], pol_w);
+          if (two_a) tma_load_2d_hint(sb + C::kABytes, ta, kb * kBK, a2_row, &full[stage], pol_w);
           for (int b = 0; b < nb; ++b)
             tma_load_2d_hint(bs + b * (kBoxRows * kBK * 2), tb, kb * kBK, row0 + b * kBoxRows, &full[stage],
                              pol_x);
@@ -273,6 +292,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     bool ok = true;
     bool first = true;
     int* counter = args.done + args.max_tiles;
+    int next_u = -2;  // lane 0: the unit claimed ahead (-2: none yet)
     for (int i = 0;; ++i) {
       const int q = i % C::kUnitQueue;
       int u = -1;
@@ -282,8 +302,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                kDevErrWaitTimeoutProducer)) {
           got = 0;
         } else {
-          u = ok ? atomicAdd(counter, 1) : -1;
-          if (u >= total_units) u = -1;
+          u = next_u == -2 ? atomicAdd(counter, 1) : next_u;
+          if (!ok || u >= total_units) u = -1;
+          next_u = u >= 0 ? atomicAdd(counter, 1) : -1;
           unit_q[q] = u;
           mbar_arrive(&uq_full[q]);
         }
@@ -320,10 +341,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       const CUtensorMap* ta = gu ? &tmA_gu : &tmA_dn;
       const CUtensorMap* tb = gu ? &tmB_gu : &tmB_dn;
-      const int a_row = gu ? e * args.a_rows_gu + mt * kBM : e * args.a_rows_dn + mt * kBM;
+      const bool two_a = gu || args.dn_two;
+      const int a_row = gu ? e * args.a_rows_gu + mt * kBM : e * args.a_rows_dn + mt * kBM * (1 + args.dn_two);
+      const int a2_row = a_row + (gu ? args.up_off : kBM);
       const int nkb = gu ? args.num_kb_gu : args.num_kb_dn;
       const uint32_t bytes =
-          (gu ? 2 : 1) * C::kABytes + (g4 ? n_g4 * 4 * kBK * 2 : nb * kBoxRows * kBK * 2);
+          (two_a ? 2 : 1) * C::kABytes + (g4 ? n_g4 * 4 * kBK * 2 : nb * kBoxRows * kBK * 2);
       for (int kb = 0; kb < nkb; ++kb) {
         uint8_t* sb = stages + stage * C::kStageBytes;
         uint8_t* bs = sb + 2 * C::kABytes;
@@ -333,7 +356,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (w_ok) {
             mbar_arrive_expect_tx(&full[stage], bytes);
             tma_load_2d_hint(sb, ta, kb * kBK, a_row, &full[stage], pol_w);
-            if (gu) tma_load_2d_hint(sb + C::kABytes, ta, kb * kBK, a_row + args.up_off, &full[stage], pol_w);
+            if (two_a) tma_load_2d_hint(sb + C::kABytes, ta, kb * kBK, a2_row, &full[stage], pol_w);
             if (!g4)
               for (int b = 0; b < nb; ++b)
                 tma_load_2d_hint(bs + b * (kBoxRows * kBK * 2), tb, kb * kBK, row0 + b * kBoxRows,
@@ -392,6 +415,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int nb = (tv.nrows(tile) + kBoxRows - 1) / kBoxRows;
         const uint32_t idesc = make_idesc_bf16(kBM, nb * kBoxRows);
         const int nkb = gu ? args.num_kb_gu : args.num_kb_dn;
+        const bool two_a = gu || args.dn_two;
         const int buf = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait_bounded(&acc_empty[buf], acc_phase ^ 1u, abort_flag, kDevErrWaitTimeoutMma)) {
@@ -414,7 +438,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint32_t accum = (kb | k) != 0 ? 1u : 0u;
             const uint64_t bdesc = make_sw128_desc(bsb + k * kUmmaK * 2);
             umma_bf16(d0, make_sw128_desc(sb + k * kUmmaK * 2), bdesc, idesc, accum);
-            if (gu) umma_bf16(d0 + kBM, make_sw128_desc(sb + C::kABytes + k * kUmmaK * 2), bdesc, idesc, accum);
+            if (two_a) umma_bf16(d0 + kBM, make_sw128_desc(sb + C::kABytes + k * kUmmaK * 2), bdesc, idesc, accum);
           }
           umma_commit(&empty[stage]);
           if (++stage == C::kStages) {
@@ -503,42 +527,47 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
           }
         } else {
-          tmem_ld_wait();
-          // transpose through shared memory: a lane then holds 4 consecutive
-          // features of one row, added with one 16-byte vector reduction
-          float* wsb = staging + (warp - 2) * (16 * 33);
+          for (int h = 0; h <= args.dn_two; ++h) {  // the unit's 128-feature halves
+            if (h) tmem_ld_32x32b_x16(taddr + kBM + c * 16, v);
+            tmem_ld_wait();
+            // transpose through shared memory: a lane then holds 4 consecutive
+            // features of one row, added with one 16-byte vector reduction
+            float* wsb = staging + (warp - 2) * (16 * 33);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) wsb[i * 33 + lane] = __uint_as_float(v[i]);
-          __syncwarp();
-          const int fq = (lane & 7) * 4;
+            for (int i = 0; i < 16; ++i) wsb[i * 33 + lane] = __uint_as_float(v[i]);
+            __syncwarp();
+            const int fq = (lane & 7) * 4;
+            const int fcol = (mt * (1 + args.dn_two) + h) * kBM + quad * 32 + fq;
 #pragma unroll
-          for (int it = 0; it < 4; ++it) {
-            const int i = it * 4 + (lane >> 3);
-            const int n = c * 16 + i;
-            if (n < nrows) {
-              const int dst = meta_dst[n];
-              if (dst >= 0) {
-                const float wv = meta_w[n];
-                if constexpr (kReturn) {
-                  // weighted row segment straight into the source rank's return buffer
-                  __nv_bfloat16* ret = args.peer_ret[meta_src[n]] + (size_t(args.ret_row0) + dst) * args.acc_ld +
-                                       mt * kBM + quad * 32 + fq;
-                  const __nv_bfloat162 lo = __floats2bfloat162_rn(wv * wsb[i * 33 + fq], wv * wsb[i * 33 + fq + 1]);
-                  const __nv_bfloat162 hi =
-                      __floats2bfloat162_rn(wv * wsb[i * 33 + fq + 2], wv * wsb[i * 33 + fq + 3]);
-                  uint2 pk;
-                  pk.x = *reinterpret_cast<const uint32_t*>(&lo);
-                  pk.y = *reinterpret_cast<const uint32_t*>(&hi);
-                  *reinterpret_cast<uint2*>(ret) = pk;
-                } else {
-                  red_add_v4_f32(args.acc + size_t(dst) * args.acc_ld + mt * kBM + quad * 32 + fq,
-                                 wv * wsb[i * 33 + fq], wv * wsb[i * 33 + fq + 1], wv * wsb[i * 33 + fq + 2],
-                                 wv * wsb[i * 33 + fq + 3]);
+            for (int it = 0; it < 4; ++it) {
+              const int i = it * 4 + (lane >> 3);
+              const int n = c * 16 + i;
+              if (n < nrows) {
+                const int dst = meta_dst[n];
+                if (dst >= 0) {
+                  const float wv = meta_w[n];
+                  if constexpr (kReturn) {
+                    // weighted row segment straight into the source rank's return buffer
+                    __nv_bfloat16* ret =
+                        args.peer_ret[meta_src[n]] + (size_t(args.ret_row0) + dst) * args.acc_ld + fcol;
+                    const __nv_bfloat162 lo =
+                        __floats2bfloat162_rn(wv * wsb[i * 33 + fq], wv * wsb[i * 33 + fq + 1]);
+                    const __nv_bfloat162 hi =
+                        __floats2bfloat162_rn(wv * wsb[i * 33 + fq + 2], wv * wsb[i * 33 + fq + 3]);
+                    uint2 pk;
+                    pk.x = *reinterpret_cast<const uint32_t*>(&lo);
+                    pk.y = *reinterpret_cast<const uint32_t*>(&hi);
+                    *reinterpret_cast<uint2*>(ret) = pk;
+                  } else {
+                    red_add_v4_f32(args.acc + size_t(dst) * args.acc_ld + fcol,
+                                   wv * wsb[i * 33 + fq], wv * wsb[i * 33 + fq + 1], wv * wsb[i * 33 + fq + 2],
+                                   wv * wsb[i * 33 + fq + 3]);
+                  }
                 }
               }
             }
+            __syncwarp();
           }
-          __syncwarp();
         }
       }
       tc_fence_before();

@@ -449,7 +449,8 @@ int launch_moe_fused(const void* x, int64_t x_rows, const int32_t* gather_rows, 
   a.tiles = tiles;
   a.max_tiles = int(max_tiles);
   a.n_mt_gu = int(I / qmoe::kBM);
-  a.n_mt_dn = int(H / qmoe::kBM);
+  a.dn_two = H % (2 * qmoe::kBM) == 0 ? 1 : 0;
+  a.n_mt_dn = int(H / (qmoe::kBM * (1 + a.dn_two)));
   a.num_kb_gu = int(H / qmoe::kBK);
   a.num_kb_dn = int(I / qmoe::kBK);
   a.a_rows_gu = int(2 * I);
