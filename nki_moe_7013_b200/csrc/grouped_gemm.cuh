@@ -340,7 +340,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   int ntiles = tile_meta[0];
   const int max_rows = tile_meta[1];
-  if (kSmall && max_rows > kBoxRows) {
+  if (max_rows > C::kBRows) {
     if (threadIdx.x == 0) record_device_error(kDevErrBadIndex);
     ntiles = 0;  // refuse the launch rather than overrun a stage
   }

@@ -39,6 +39,9 @@
 // Gate/up rows come from the permuted copy of the tokens (16-row boxes) or
 // straight from the token rows (TMA gather4 by row_token; no copy to write).
 //
+// A tile outside its limits (more than 128 rows, or rows outside [0, R)) is
+// skipped by every warp role with device error 4, never loaded into a stage.
+//
 // Pipeline, warp roles, TMEM double-buffering, swizzles and epilogues are
 // those of grouped_gemm_kernel (gate/up: two accumulators, SiLU(gate)*up;
 // down: weighted rows reduced into the fp32 combine accumulator).  The
@@ -53,21 +56,23 @@
 namespace qmoe {
 
 struct FusedCfg {
+  static constexpr int kMaxRows = kBNMax;                    // rows of a tile
   static constexpr int kABytes = kBM * kBK * 2;              // 16 KB
-  static constexpr int kBBytes = kBNMax * kBK * 2;           // 16 KB
-  static constexpr int kStageBytes = 2 * kABytes + kBBytes;  // gate/up stage; a down stage uses A + B
+  static constexpr int kBBytes = kMaxRows * kBK * 2;         // 16 KB
+  static constexpr int kStageBytes = 2 * kABytes + kBBytes;  // two weight tiles + the rows
   static constexpr int kStages = 4;
-  static constexpr int kAccCols = 256;                       // gate [0,128) up [128,256); down [0,128)
+  static constexpr int kAccCols = 256;                       // one TMEM buffer: two 128-column accumulators
   static constexpr int kTmemCols = 512;
   static constexpr int kBarrierBytes = 256;
   static constexpr int kUnitQueue = 4;
-  static constexpr int kStagingBytes = 4 * 16 * 33 * 4 + 128 * 12;
+  static constexpr int kStagingBytes = 4 * 16 * 33 * 4 + kMaxRows * 12;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes + kStagingBytes;
 };
 
 struct FusedArgs {
   const int32_t* tiles;  // [0] = ntiles, then expert[max_tiles], row0[max_tiles], nrows[max_tiles]
   int max_tiles;
+  int n_rows;            // R: rows of the permuted operands (a tile outside [0, R) is refused)
   int n_mt_gu, n_mt_dn;      // units per tile: I / 128 and H / (128 * (1 + dn_two))
   int dn_two;                // 1: a down unit covers 256 features (two accumulators)
   int num_kb_gu, num_kb_dn;  // k blocks: H / 64 and I / 64
@@ -117,6 +122,31 @@ __device__ __forceinline__ bool wait_tile_done(const int* done, int target, vola
   return true;
 }
 
+// One unit's shape, derived identically by the producer, MMA and epilogue
+// warps.  rows == 0: a tile outside its limits -- the unit is skipped by all
+// three (a gate/up unit still counts as done for its tile's down units).
+struct FusedUnit {
+  bool gu;      // gate/up (else down)
+  int tile, mt;
+  int e, row0, rows, nb;  // expert, first row, rows, 16-row boxes
+  bool two;     // two accumulators (gate + up, or two 128-feature halves)
+};
+
+// TMEM buffer sequence of the MMA and epilogue warps: each unit that is not
+// skipped takes buffer `next` (256 columns) and flips it; uses(b) counts the
+// buffer's completed uses (its barrier phases).
+struct AccSeq {
+  int next = 0;
+  uint32_t u0 = 0u, u1 = 0u;
+  __device__ __forceinline__ uint32_t uses(int b) const { return b ? u1 : u0; }
+  __device__ __forceinline__ void bump(int b) {
+    if (b)
+      ++u1;
+    else
+      ++u0;
+  }
+};
+
 template <bool kReturn = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     moe_fused_kernel(const __grid_constant__ CUtensorMap tmA_gu, const __grid_constant__ CUtensorMap tmB_gu,
@@ -126,9 +156,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   extern __shared__ uint8_t fused_smem_raw[];
   __shared__ int4 tile_cache[kTileCache];
   __shared__ int tile_meta[2];
-  __shared__ int unit_q[FusedCfg::kUnitQueue];
-  __shared__ __align__(8) uint64_t uq_full[FusedCfg::kUnitQueue];
-  __shared__ __align__(8) uint64_t uq_empty[FusedCfg::kUnitQueue];
+  __shared__ int unit_q[C::kUnitQueue];
+  __shared__ __align__(8) uint64_t uq_full[C::kUnitQueue];
+  __shared__ __align__(8) uint64_t uq_empty[C::kUnitQueue];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(fused_smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
@@ -190,13 +220,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int ntiles = tile_meta[0];
   const int units_gu = ntiles * args.n_mt_gu;
   const int total_units = units_gu + ntiles * args.n_mt_dn;
-  // unit u -> (gate/up?, tile, feature block)
-  auto unit_of = [&](int u, bool& gu, int& tile, int& mt) {
-    gu = u < units_gu;
-    const int v = gu ? u : u - units_gu;
-    const int n = gu ? args.n_mt_gu : args.n_mt_dn;
-    tile = v / n;
-    mt = v - tile * n;
+  // unit u -> (gate/up?, tile, feature block) and its shape
+  auto unit_of = [&](int u) {
+    FusedUnit f;
+    f.gu = u < units_gu;
+    const int v = f.gu ? u : u - units_gu;
+    const int n = f.gu ? args.n_mt_gu : args.n_mt_dn;
+    f.tile = v / n;
+    f.mt = v - f.tile * n;
+    f.e = tv.expert(f.tile);
+    f.row0 = tv.first_row(f.tile);
+    f.rows = tv.nrows(f.tile);
+    if (f.rows < 0 || f.rows > C::kMaxRows || f.row0 < 0 || f.row0 > args.n_rows - f.rows) f.rows = 0;
+    f.nb = (f.rows + kBoxRows - 1) / kBoxRows;
+    f.two = f.gu || args.dn_two;
+    return f;
   };
 
   if (warp == 0 && args.gather_rows == nullptr) {
@@ -224,19 +262,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         unit_q[q] = u;
         mbar_arrive(&uq_full[q]);
         if (u < 0) break;
-        bool gu;
-        int tile, mt;
-        unit_of(u, gu, tile, mt);
-        const int e = tv.expert(tile);
-        const int row0 = tv.first_row(tile);
-        const int nb = (tv.nrows(tile) + kBoxRows - 1) / kBoxRows;
+        const FusedUnit f = unit_of(u);
+        if (f.rows == 0) {
+          record_device_error(kDevErrBadIndex);
+          continue;
+        }
+        const bool gu = f.gu;
+        const int tile = f.tile, mt = f.mt, e = f.e, row0 = f.row0, nb = f.nb;
         if (!gu && !wait_tile_done(args.done + tile, args.n_mt_gu, abort_flag)) {
           ok = false;
           continue;  // the next slot carries the end marker
         }
         const CUtensorMap* ta = gu ? &tmA_gu : &tmA_dn;
         const CUtensorMap* tb = gu ? &tmB_gu : &tmB_dn;
-        const bool two_a = gu || args.dn_two;
+        const bool two_a = f.two;
         const int a_row = gu ? e * args.a_rows_gu + mt * kBM : e * args.a_rows_dn + mt * kBM * (1 + args.dn_two);
         const int a2_row = a_row + (gu ? args.up_off : kBM);
         const int nkb = gu ? args.num_kb_gu : args.num_kb_dn;
@@ -316,13 +355,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       if (u < 0) break;
-      bool gu;
-      int tile, mt;
-      unit_of(u, gu, tile, mt);
-      const int e = tv.expert(tile);
-      const int row0 = tv.first_row(tile);
-      const int nrows = tv.nrows(tile);
-      const int nb = (nrows + kBoxRows - 1) / kBoxRows;
+      const FusedUnit f = unit_of(u);
+      if (f.rows == 0) {
+        if (lane == 0) record_device_error(kDevErrBadIndex);
+        continue;
+      }
+      const bool gu = f.gu;
+      const int tile = f.tile, mt = f.mt, e = f.e, row0 = f.row0, nrows = f.rows, nb = f.nb;
       if (!gu) {
         int dep = 1;
         if (lane == 0) dep = wait_tile_done(args.done + tile, args.n_mt_gu, abort_flag);
@@ -341,7 +380,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       const CUtensorMap* ta = gu ? &tmA_gu : &tmA_dn;
       const CUtensorMap* tb = gu ? &tmB_gu : &tmB_dn;
-      const bool two_a = gu || args.dn_two;
+      const bool two_a = f.two;
       const int a_row = gu ? e * args.a_rows_gu + mt * kBM : e * args.a_rows_dn + mt * kBM * (1 + args.dn_two);
       const int a2_row = a_row + (gu ? args.up_off : kBM);
       const int nkb = gu ? args.num_kb_gu : args.num_kb_dn;
@@ -400,6 +439,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      AccSeq acc;
       for (int local = 0; ok; ++local) {
         const int q = local % C::kUnitQueue;
         if (!mbar_wait_bounded(&uq_full[q], (local / C::kUnitQueue) & 1, abort_flag, kDevErrWaitTimeoutMma)) {
@@ -409,21 +449,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int u = unit_q[q];
         mbar_arrive(&uq_empty[q]);
         if (u < 0) break;
-        bool gu;
-        int tile, mt;
-        unit_of(u, gu, tile, mt);
-        const int nb = (tv.nrows(tile) + kBoxRows - 1) / kBoxRows;
-        const uint32_t idesc = make_idesc_bf16(kBM, nb * kBoxRows);
-        const int nkb = gu ? args.num_kb_gu : args.num_kb_dn;
-        const bool two_a = gu || args.dn_two;
-        const int buf = local & 1;
-        const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait_bounded(&acc_empty[buf], acc_phase ^ 1u, abort_flag, kDevErrWaitTimeoutMma)) {
+        const FusedUnit f = unit_of(u);
+        if (f.rows == 0) continue;
+        const uint32_t idesc = make_idesc_bf16(kBM, f.nb * kBoxRows);
+        const int nkb = f.gu ? args.num_kb_gu : args.num_kb_dn;
+        const bool two_a = f.two;
+        const int buf = acc.next;
+        if (!mbar_wait_bounded(&acc_empty[buf], (acc.uses(buf) & 1u) ^ 1u, abort_flag, kDevErrWaitTimeoutMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d0 = tmem_base + buf * C::kAccCols;
+        const uint32_t d1 = d0 + kBM;
         for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait_bounded(&full[stage], phase, abort_flag, kDevErrWaitTimeoutMma)) {
             ok = false;
@@ -438,7 +476,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint32_t accum = (kb | k) != 0 ? 1u : 0u;
             const uint64_t bdesc = make_sw128_desc(bsb + k * kUmmaK * 2);
             umma_bf16(d0, make_sw128_desc(sb + k * kUmmaK * 2), bdesc, idesc, accum);
-            if (two_a) umma_bf16(d0 + kBM, make_sw128_desc(sb + C::kABytes + k * kUmmaK * 2), bdesc, idesc, accum);
+            if (two_a) umma_bf16(d1, make_sw128_desc(sb + C::kABytes + k * kUmmaK * 2), bdesc, idesc, accum);
           }
           umma_commit(&empty[stage]);
           if (++stage == C::kStages) {
@@ -448,6 +486,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         if (!ok) break;
         umma_commit(&acc_full[buf]);
+        acc.bump(buf);
+        acc.next = buf ^ 1;
       }
       if (!ok) *abort_flag = 1;
       QMOE_TRACE_AT(1, 4);
@@ -466,8 +506,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int m = quad * 32 + lane;  // feature row inside the unit = TMEM lane
     const int et = threadIdx.x - 64;
     int32_t* meta_dst = reinterpret_cast<int32_t*>(staging + 4 * 16 * 33);
-    float* meta_w = reinterpret_cast<float*>(meta_dst + 128);
-    int32_t* meta_src = meta_dst + 256;
+    float* meta_w = reinterpret_cast<float*>(meta_dst + C::kMaxRows);
+    int32_t* meta_src = meta_dst + 2 * C::kMaxRows;
+    AccSeq acc;
     for (int local = 0;; ++local) {
       const int q = local % C::kUnitQueue;
       const bool got = mbar_wait_bounded(&uq_full[q], (local / C::kUnitQueue) & 1, abort_flag,
@@ -477,14 +518,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (named_barrier_or(1, 128, !got)) break;
       if (et == 0) mbar_arrive(&uq_empty[q]);
       if (u < 0) break;
-      bool gu;
-      int tile, mt;
-      unit_of(u, gu, tile, mt);
-      const int row0 = tv.first_row(tile);
-      const int nrows = tv.nrows(tile);
-      const int nb = (nrows + kBoxRows - 1) / kBoxRows;
-      const int buf = local & 1;
-      const uint32_t acc_phase = (local >> 1) & 1;
+      const FusedUnit f = unit_of(u);
+      if (f.rows == 0) continue;  // skipped by every role
+      const bool gu = f.gu;
+      const int tile = f.tile, mt = f.mt, row0 = f.row0, nrows = f.rows, nb = f.nb;
+      const int buf = acc.next;
       int my_dst = -1, my_src = 0;
       float my_w = 0.f;
       if (!gu && et < nrows) {
@@ -498,7 +536,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           my_w = args.row_w[row0 + et];
         }
       }
-      const bool ok = mbar_wait_bounded(&acc_full[buf], acc_phase, abort_flag, kDevErrWaitTimeoutEpilogue);
+      const bool ok = mbar_wait_bounded(&acc_full[buf], acc.uses(buf) & 1u, abort_flag, kDevErrWaitTimeoutEpilogue);
       if (named_barrier_or(1, 128, !ok)) break;
       if (local == 0 && et == 0) QMOE_TRACE_AT(1, 5);
       if (!gu) {
@@ -509,13 +547,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       tc_fence_after();
       const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) + buf * C::kAccCols;
+      const uint32_t tsecond = kBM;
       const int feat = mt * kBM + m;
       for (int c = 0; c < nb; ++c) {
         uint32_t v[16];
         tmem_ld_32x32b_x16(taddr + c * 16, v);
         if (gu) {
           uint32_t up[16];
-          tmem_ld_32x32b_x16(taddr + kBM + c * 16, up);
+          tmem_ld_32x32b_x16(taddr + tsecond + c * 16, up);
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
@@ -528,7 +567,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         } else {
           for (int h = 0; h <= args.dn_two; ++h) {  // the unit's 128-feature halves
-            if (h) tmem_ld_32x32b_x16(taddr + kBM + c * 16, v);
+            if (h) tmem_ld_32x32b_x16(taddr + tsecond + c * 16, v);
             tmem_ld_wait();
             // transpose through shared memory: a lane then holds 4 consecutive
             // features of one row, added with one 16-byte vector reduction
@@ -572,6 +611,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
+      acc.bump(buf);
+      acc.next = buf ^ 1;
       if (gu) {
         // publish this unit's activation rows to the down units of the tile
         asm volatile("fence.proxy.async;" ::: "memory");

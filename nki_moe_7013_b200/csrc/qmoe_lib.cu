@@ -448,6 +448,7 @@ int launch_moe_fused(const void* x, int64_t x_rows, const int32_t* gather_rows, 
   qmoe::FusedArgs a{};
   a.tiles = tiles;
   a.max_tiles = int(max_tiles);
+  a.n_rows = int(R);
   a.n_mt_gu = int(I / qmoe::kBM);
   a.dn_two = H % (2 * qmoe::kBM) == 0 ? 1 : 0;
   a.n_mt_dn = int(H / (qmoe::kBM * (1 + a.dn_two)));
@@ -575,6 +576,73 @@ FwdLayout fwd_layout(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I) {
   L.done = take(T > kGatherMaxT ? sizeof(int32_t) * size_t(qmoe_max_tiles(R, E) + 2) : 0);
   L.total = o;
   return L;
+}
+
+// The MoE forward on a workspace laid out by fwd_layout (shapes checked by
+// the caller): routing, permutation, experts and the combine.
+int moe_forward_on(const void* x, const void* w_router, const float* router_bias, const void* w_gate_up,
+                   const void* w_down, const void* residual, int64_t T, int64_t H, int64_t E, int64_t k, int64_t I,
+                   int normalize, void* out, int32_t* topk_idx, float* topk_w, uint8_t* ws, const FwdLayout& L,
+                   cudaStream_t s) {
+  int32_t* chunk_hist = reinterpret_cast<int32_t*>(ws + L.chunk_hist);
+  int32_t* counts = reinterpret_cast<int32_t*>(ws + L.counts);
+  int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
+  int32_t* row_token = reinterpret_cast<int32_t*>(ws + L.row_token);
+  float* row_w = reinterpret_cast<float*>(ws + L.row_w);
+  int32_t* slot_row = reinterpret_cast<int32_t*>(ws + L.slot_row);
+  int32_t* tiles = reinterpret_cast<int32_t*>(ws + L.tiles);
+  int32_t* idx = topk_idx ? topk_idx : reinterpret_cast<int32_t*>(ws + L.topk_idx);
+  float* tw = topk_w ? topk_w : reinterpret_cast<float*>(ws + L.topk_w);
+  const bool fused = T > kGatherMaxT;
+  void* x_perm = T > kFusedGatherMaxT ? ws + L.x_perm : nullptr;
+  void* act = ws + L.act;
+  float* acc = reinterpret_cast<float*>(ws + L.acc);
+  float* split_ws = T * k <= kGateUpSplitMaxR ? reinterpret_cast<float*>(ws + L.split) : nullptr;
+  int32_t* done = fused ? reinterpret_cast<int32_t*>(ws + L.done) : nullptr;
+  int32_t* split_counters = split_ws ? reinterpret_cast<int32_t*>(split_ws + size_t(qmoe::kSplitSlots) *
+                                                                               qmoe::kSplitSlotFloats)
+                                     : nullptr;
+  const int64_t R = T * k;
+  const int64_t max_tiles = qmoe_max_tiles(R, E);
+  // a token's k experts are distinct, so no expert gets more than T rows
+  const int64_t tile_rows = std::min<int64_t>(T, qmoe::kBNMax);
+
+  float* logits = T <= kRouterSmallMaxT ? reinterpret_cast<float*>(ws + L.logits) : nullptr;
+  if (T <= qmoe::kRouteSmallMaxT && E <= qmoe::kRouteSmallMaxE) {
+    // decode sizes: router + permutation in one launch, which also zeroes
+    // the gate/up split counters (the workspace may hold anything on entry)
+    QMOE_CHECK(launch_route_small(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw, counts,
+                                  offsets, row_token, row_w, slot_row, tiles, max_tiles, acc, s, split_counters,
+                                  split_counters ? qmoe::kSplitCounterWords : 0));
+  } else {
+    QMOE_CHECK(launch_router(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw,
+                             chunk_hist, s));
+    // the permutation also zeroes the gate/up split counters or the fused
+    // kernel's tile counters (the workspace may hold anything on entry)
+    int32_t* zero = fused ? done : split_counters;
+    const int n_zero = fused ? int(max_tiles + 2) : (split_counters ? qmoe::kSplitCounterWords : 0);
+    QMOE_CHECK(launch_permute(idx, tw, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w,
+                              slot_row, tiles, x_perm, acc, s, zero, n_zero));
+  }
+  if (fused) {
+    // prefill: gate/up and down in one persistent kernel, which also
+    // finalises the combine after a grid-wide barrier
+    if (x_perm)
+      return launch_moe_fused(x_perm, R, nullptr, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H, I,
+                              E, act, acc, T, done, s, residual, out);
+    return launch_moe_fused(x, T, row_token, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, act,
+                            acc, T, done, s, residual, out);
+  }
+  QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s,
+                                tile_rows));
+  // the tile list comes from the routing kernels, before the gate/up GEMM;
+  // with the split scratch (decode sizes) the down GEMM finalises too
+  if (split_counters)
+    return launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s, tile_rows,
+                            qmoe::kGemmTilesReady, residual, out, split_counters + qmoe::kSplitSlots);
+  QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s, tile_rows,
+                              qmoe::kGemmTilesReady));
+  return launch_finalize(acc, residual, T, H, out, s);
 }
 
 }  // namespace
@@ -1248,67 +1316,8 @@ int qmoe_moe_forward(const void* x, const void* w_router, const float* router_bi
   DeviceInfo* d = nullptr;
   QMOE_CHECK(device_info(&d));
   if (T == 0) return QMOE_OK;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
-  int32_t* chunk_hist = reinterpret_cast<int32_t*>(ws + L.chunk_hist);
-  int32_t* counts = reinterpret_cast<int32_t*>(ws + L.counts);
-  int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
-  int32_t* row_token = reinterpret_cast<int32_t*>(ws + L.row_token);
-  float* row_w = reinterpret_cast<float*>(ws + L.row_w);
-  int32_t* slot_row = reinterpret_cast<int32_t*>(ws + L.slot_row);
-  int32_t* tiles = reinterpret_cast<int32_t*>(ws + L.tiles);
-  int32_t* idx = topk_idx ? topk_idx : reinterpret_cast<int32_t*>(ws + L.topk_idx);
-  float* tw = topk_w ? topk_w : reinterpret_cast<float*>(ws + L.topk_w);
-  const bool fused = T > kGatherMaxT;
-  void* x_perm = T > kFusedGatherMaxT ? ws + L.x_perm : nullptr;
-  void* act = ws + L.act;
-  float* acc = reinterpret_cast<float*>(ws + L.acc);
-  float* split_ws = T * k <= kGateUpSplitMaxR ? reinterpret_cast<float*>(ws + L.split) : nullptr;
-  int32_t* done = fused ? reinterpret_cast<int32_t*>(ws + L.done) : nullptr;
-  int32_t* split_counters = split_ws ? reinterpret_cast<int32_t*>(split_ws + size_t(qmoe::kSplitSlots) *
-                                                                               qmoe::kSplitSlotFloats)
-                                     : nullptr;
-  const int64_t R = T * k;
-  const int64_t max_tiles = qmoe_max_tiles(R, E);
-  // a token's k experts are distinct, so no expert gets more than T rows
-  const int64_t tile_rows = std::min<int64_t>(T, qmoe::kBNMax);
-
-  float* logits = T <= kRouterSmallMaxT ? reinterpret_cast<float*>(ws + L.logits) : nullptr;
-  if (T <= qmoe::kRouteSmallMaxT && E <= qmoe::kRouteSmallMaxE) {
-    // decode sizes: router + permutation in one launch, which also zeroes
-    // the gate/up split counters (the workspace may hold anything on entry)
-    QMOE_CHECK(launch_route_small(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw, counts,
-                                  offsets, row_token, row_w, slot_row, tiles, max_tiles, acc, s, split_counters,
-                                  split_counters ? qmoe::kSplitCounterWords : 0));
-  } else {
-    QMOE_CHECK(launch_router(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw,
-                             chunk_hist, s));
-    // the permutation also zeroes the gate/up split counters or the fused
-    // kernel's tile counters (the workspace may hold anything on entry)
-    int32_t* zero = fused ? done : split_counters;
-    const int n_zero = fused ? int(max_tiles + 2) : (split_counters ? qmoe::kSplitCounterWords : 0);
-    QMOE_CHECK(launch_permute(idx, tw, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w,
-                              slot_row, tiles, x_perm, acc, s, zero, n_zero));
-  }
-  if (fused) {
-    // prefill: gate/up and down in one persistent kernel, which also
-    // finalises the combine after a grid-wide barrier
-    if (x_perm)
-      return launch_moe_fused(x_perm, R, nullptr, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H, I,
-                              E, act, acc, T, done, s, residual, out);
-    return launch_moe_fused(x, T, row_token, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, act,
-                            acc, T, done, s, residual, out);
-  }
-  QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s,
-                                tile_rows));
-  // the tile list comes from the routing kernels, before the gate/up GEMM;
-  // with the split scratch (decode sizes) the down GEMM finalises too
-  if (split_counters)
-    return launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s, tile_rows,
-                            qmoe::kGemmTilesReady, residual, out, split_counters + qmoe::kSplitSlots);
-  QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s, tile_rows,
-                              qmoe::kGemmTilesReady));
-  return launch_finalize(acc, residual, T, H, out, s);
+  return moe_forward_on(x, w_router, router_bias, w_gate_up, w_down, residual, T, H, E, k, I, normalize, out,
+                        topk_idx, topk_w, static_cast<uint8_t*>(workspace), L, static_cast<cudaStream_t>(stream));
 }
 
 #ifdef QMOE_TRACE
@@ -1411,64 +1420,6 @@ extern "C" int qmoe_moe_forward_noalloc(const void* x, const void* w_router,
   void* scratch = nullptr;
   QMOE_CHECK(noalloc_scratch(&scratch));
   if (T == 0) return QMOE_OK;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  uint8_t* ws = static_cast<uint8_t*>(scratch);
-  int32_t* chunk_hist = reinterpret_cast<int32_t*>(ws + L.chunk_hist);
-  int32_t* counts = reinterpret_cast<int32_t*>(ws + L.counts);
-  int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
-  int32_t* row_token = reinterpret_cast<int32_t*>(ws + L.row_token);
-  float* row_w = reinterpret_cast<float*>(ws + L.row_w);
-  int32_t* slot_row = reinterpret_cast<int32_t*>(ws + L.slot_row);
-  int32_t* tiles = reinterpret_cast<int32_t*>(ws + L.tiles);
-  int32_t* idx = topk_idx ? topk_idx : reinterpret_cast<int32_t*>(ws + L.topk_idx);
-  float* tw = topk_w ? topk_w : reinterpret_cast<float*>(ws + L.topk_w);
-  const bool fused = T > kGatherMaxT;
-  void* x_perm = T > kFusedGatherMaxT ? ws + L.x_perm : nullptr;
-  void* act = ws + L.act;
-  float* acc = reinterpret_cast<float*>(ws + L.acc);
-  float* split_ws = T * k <= kGateUpSplitMaxR ? reinterpret_cast<float*>(ws + L.split) : nullptr;
-  int32_t* done = fused ? reinterpret_cast<int32_t*>(ws + L.done) : nullptr;
-  int32_t* split_counters = split_ws ? reinterpret_cast<int32_t*>(split_ws + size_t(qmoe::kSplitSlots) *
-                                                                               qmoe::kSplitSlotFloats)
-                                     : nullptr;
-  const int64_t R = T * k;
-  const int64_t max_tiles = qmoe_max_tiles(R, E);
-  // a token's k experts are distinct, so no expert gets more than T rows
-  const int64_t tile_rows = std::min<int64_t>(T, qmoe::kBNMax);
-  float* logits = T <= kRouterSmallMaxT ? reinterpret_cast<float*>(ws + L.logits) : nullptr;
-  if (T <= qmoe::kRouteSmallMaxT && E <= qmoe::kRouteSmallMaxE) {
-    // decode sizes: router + permutation in one launch, which also zeroes
-    // the gate/up split counters (the workspace may hold anything on entry)
-    QMOE_CHECK(launch_route_small(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw, counts,
-                                  offsets, row_token, row_w, slot_row, tiles, max_tiles, acc, s, split_counters,
-                                  split_counters ? qmoe::kSplitCounterWords : 0));
-  } else {
-    QMOE_CHECK(launch_router(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw,
-                             chunk_hist, s));
-    // the permutation also zeroes the gate/up split counters or the fused
-    // kernel's tile counters (the workspace may hold anything on entry)
-    int32_t* zero = fused ? done : split_counters;
-    const int n_zero = fused ? int(max_tiles + 2) : (split_counters ? qmoe::kSplitCounterWords : 0);
-    QMOE_CHECK(launch_permute(idx, tw, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w,
-                              slot_row, tiles, x_perm, acc, s, zero, n_zero));
-  }
-  if (fused) {
-    // prefill: gate/up and down in one persistent kernel, which also
-    // finalises the combine after a grid-wide barrier
-    if (x_perm)
-      return launch_moe_fused(x_perm, R, nullptr, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H, I,
-                              E, act, acc, T, done, s, residual, out);
-    return launch_moe_fused(x, T, row_token, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, act,
-                            acc, T, done, s, residual, out);
-  }
-  QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s,
-                                tile_rows));
-  // the tile list comes from the routing kernels, before the gate/up GEMM;
-  // with the split scratch (decode sizes) the down GEMM finalises too
-  if (split_counters)
-    return launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s, tile_rows,
-                            qmoe::kGemmTilesReady, residual, out, split_counters + qmoe::kSplitSlots);
-  QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s, tile_rows,
-                              qmoe::kGemmTilesReady));
-  return launch_finalize(acc, residual, T, H, out, s);
+  return moe_forward_on(x, w_router, router_bias, w_gate_up, w_down, residual, T, H, E, k, I, normalize, out,
+                        topk_idx, topk_w, static_cast<uint8_t*>(scratch), L, static_cast<cudaStream_t>(stream));
 }

@@ -113,7 +113,9 @@ __device__ __forceinline__ void select_topk_warp(const float* row, int tok, int 
   for (int off = 16; off >= 1; off >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, off);
   const float inv_s = 1.0f / s;
   if (logits_out) {
-    for (int i = 0; i < per_lane; ++i) logits_out[size_t(tok) * E + lane + 32 * i] = lv[i];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < per_lane) logits_out[size_t(tok) * E + lane + 32 * i] = lv[i];
   }
   // k rounds: the largest remaining logit (warp max of the keys), then the
   // lowest expert index holding it (warp min) -- ties go to the lower index.

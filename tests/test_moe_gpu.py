@@ -166,6 +166,35 @@ def test_small_tile_configuration_refuses_larger_tiles(cuda_dev):
     assert bool((acc == 5.0).all())
 
 
+def test_oversized_tiles_refused(cuda_dev):
+    """A tile list with a tile of more than 128 rows: the grouped GEMMs refuse
+    the launch (device error 4, outputs untouched); the fused kernel skips
+    that tile's units (device error 4) and completes every other tile -- no
+    stage is ever overrun."""
+    from nki_moe_7013_b200 import _C, ops
+
+    H, E, k, I, T = 2048, 128, 8, 768, 1024
+    wr, wgu, wd = moe_weights(4, E, H, I, cuda_dev)
+    x = activations(4, T, H, cuda_dev)
+    idx, w, hist = _routing(cuda_dev, x, wr, k)
+    p = ops.moe_permute(idx, w, hist, E, x=x, gather=True)
+    mt = p["max_tiles"]
+    nt = int(p["tiles"][0])
+    bad = p["tiles"].clone()
+    bad[1 + 2 * mt] = 200  # tile 0 (rows from 0) claims 200 rows
+    act = torch.full((T * k, I), 7.0, dtype=torch.bfloat16, device=cuda_dev)
+    ops.grouped_gemm_gateup_swiglu(p["x_perm"], wgu, bad, mt, out=act)
+    torch.cuda.synchronize()
+    assert _C.device_error() == 4
+    assert bool((act == 7.0).all())
+    acc = torch.zeros((T, H), dtype=torch.float32, device=cuda_dev)
+    ops.moe_experts(p["x_perm"], wgu, wd, bad, mt, p["row_token"], p["row_w"], acc, p["done"], act=act)
+    torch.cuda.synchronize()
+    assert _C.device_error() == 4
+    assert int(p["done"][0]) == 0
+    assert bool((p["done"][1:nt] == I // 128).all())
+
+
 @pytest.mark.parametrize("T,H,E,k,I", [(65, 2048, 128, 8, 768), (1024, 2048, 128, 8, 768), (300, 512, 32, 8, 256),
                                        (2048, 256, 64, 4, 128), (777, 1024, 256, 8, 384)])
 def test_moe_experts_fused_matches_separate_gemms(cuda_dev, oracle, T, H, E, k, I):
