@@ -235,12 +235,19 @@ int launch_router(const void* x, const void* w, const float* bias, int64_t T, in
                          topk_idx, topk_w, chunk_hist);
   }
   const int smem = int(sizeof(float) * qmoe::kRouterChunk * (H + E));
-#define QMOE_ROUTER_CASE(GG)                                                                                \
-  case GG: {                                                                                                \
-    QMOE_CHECK(set_smem(qmoe::router_topk_kernel<GG>, smem));                                               \
-    return launch_kernel(qmoe::router_topk_kernel<GG>, dim3(nchunks), dim3(qmoe::router_warps<GG>() * 32), \
-                         size_t(smem), stream, true, "router_topk_kernel", xb, wb, bias, int(T), int(E),     \
-                         int(k), normalize, logits, topk_idx, topk_w, chunk_hist);                          \
+  // more chunks than SMs: 8-warp CTAs, two per SM (H < 4096)
+  const bool pairs = nchunks > num_sms(0);
+#define QMOE_ROUTER_LAUNCH(GG, W)                                                                            \
+  {                                                                                                          \
+    QMOE_CHECK(set_smem(qmoe::router_topk_kernel<GG, W>, smem));                                             \
+    return launch_kernel(qmoe::router_topk_kernel<GG, W>, dim3(nchunks), dim3((W) * 32), size_t(smem), stream, \
+                         true, "router_topk_kernel", xb, wb, bias, int(T), int(E), int(k), normalize, logits,  \
+                         topk_idx, topk_w, chunk_hist);                                                      \
+  }
+#define QMOE_ROUTER_CASE(GG)                                            \
+  case GG: {                                                            \
+    if (pairs && GG < 16) QMOE_ROUTER_LAUNCH(GG, 8)                     \
+    QMOE_ROUTER_LAUNCH(GG, qmoe::router_warps<GG>())                    \
   }
   switch (G) {
     QMOE_ROUTER_CASE(1)
@@ -252,6 +259,7 @@ int launch_router(const void* x, const void* w, const float* bias, int64_t T, in
       return set_error(QMOE_ERR_UNSUPPORTED_SHAPE, "router: H/256 = %d not in {1,2,4,8,16}", G);
   }
 #undef QMOE_ROUTER_CASE
+#undef QMOE_ROUTER_LAUNCH
 }
 
 size_t route_small_smem(int64_t T, int64_t H, int64_t E, int64_t k) {

@@ -22,9 +22,13 @@ constexpr int kRouterChunk = QMOE_ROUTER_CHUNK;  // tokens per CTA (= histogram 
 constexpr int kRouterTE = 4;                       // experts per register tile
 // Warps per router CTA: 16 (two 4-expert tiles each for E=128) keeps enough
 // warps resident to hide the L2 latency of the weight stream; H = 4096 uses 8
-// so its larger register footprint fits.
+// so its larger register footprint fits.  Batches of more chunks than SMs
+// use 8-warp CTAs, two per SM: one CTA's staging and top-k phases (half its
+// warps idle) then overlap the other's logit FMAs.
 template <int G>
 constexpr int router_warps() { return G >= 16 ? 8 : 16; }
+template <int G, int kWarps>
+constexpr int router_ctas_per_sm() { return (G < 16 && kWarps == 8) ? 2 : 1; }
 static_assert(kRouterChunk * kRouterTE == 32, "one reduced chain per lane");
 
 // Sums v[0..31] of every lane across the warp; returns in lane l the total of
@@ -156,15 +160,15 @@ __device__ __forceinline__ void select_topk_warp(const float* row, int tok, int 
   }
 }
 
-template <int G>  // G = H / 256
-__global__ void __launch_bounds__(router_warps<G>() * 32, 1)
+template <int G, int kWarps = router_warps<G>()>  // G = H / 256
+__global__ void __launch_bounds__(kWarps * 32, router_ctas_per_sm<G, kWarps>())
     router_topk_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                        const float* __restrict__ bias, int T, int E, int k, int normalize,
                        float* __restrict__ logits_out, int32_t* __restrict__ topk_idx,
                        float* __restrict__ topk_w, int32_t* __restrict__ chunk_hist) {
   constexpr int H = G * 256;
-  constexpr int kThreads = router_warps<G>() * 32;
-  static_assert(kRouterChunk <= router_warps<G>(), "one warp per token in the top-k phase");
+  constexpr int kThreads = kWarps * 32;
+  static_assert(kRouterChunk <= kWarps, "one warp per token in the top-k phase");
   extern __shared__ __align__(16) float router_smem[];
   float* xs = router_smem;                        // [kRouterChunk][H]
   float* ls = router_smem + kRouterChunk * H;     // [kRouterChunk][E]
@@ -206,7 +210,7 @@ __global__ void __launch_bounds__(router_warps<G>() * 32, 1)
   // independent fp32 chains per lane (token t x expert j), each accumulating
   // the lane's canonical slice group-major.  Weights stream from L2 one group
   // ahead; activations come from shared memory.
-  for (int tile = warp; tile < E / kRouterTE; tile += router_warps<G>()) {
+  for (int tile = warp; tile < E / kRouterTE; tile += kWarps) {
     const int e0 = tile * kRouterTE;
     const __nv_bfloat16* wp = w + size_t(e0) * H + 8 * lane;
     float acc[kRouterChunk][kRouterTE];

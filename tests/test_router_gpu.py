@@ -18,8 +18,10 @@ def _run(x, wr, k, bias=None, normalize=True):
     return idx.cpu().numpy(), w.cpu().numpy(), logits.cpu().numpy(), hist.cpu().numpy()
 
 
+# 2000 and 1300 tokens: more chunks than SMs, the two-CTAs-per-SM configuration
 @pytest.mark.parametrize("T,H,E,k", [(1, 2048, 128, 8), (7, 256, 32, 4), (128, 2048, 128, 8),
-                                     (1000, 2048, 128, 8), (33, 512, 64, 8), (9, 4096, 256, 32)])
+                                     (1000, 2048, 128, 8), (33, 512, 64, 8), (9, 4096, 256, 32),
+                                     (2000, 2048, 128, 8), (1300, 512, 64, 8)])
 def test_router_matches_oracle(cuda_dev, oracle, T, H, E, k):
     from nki_moe_7013_b200.synth import normal_bf16_device
 
