@@ -351,6 +351,43 @@ int launch_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chunk_
   return QMOE_OK;
 }
 
+// Router + scan + scatter in one launch (nchunks <= SMs, T > kRouterSmallMaxT):
+// route_permute_kernel.  barrier: one int32 of scratch, cleared here first.
+int launch_route_permute(const void* x, const void* w, const float* bias, int64_t T, int64_t H, int64_t E,
+                         int64_t k, int normalize, int32_t* topk_idx, float* topk_w, int32_t* chunk_hist,
+                         int32_t* counts, int32_t* offsets, int32_t* row_token, float* row_w, int32_t* slot_row,
+                         int32_t* tiles, int64_t max_tiles, void* x_perm, float* acc_zero, int32_t* zero_words,
+                         int n_zero_words, int* barrier, cudaStream_t stream) {
+  const int G = int(H / 256);
+  const int nchunks = int((T + qmoe::kRouterChunk - 1) / qmoe::kRouterChunk);
+  if (nchunks <= 0) return QMOE_OK;
+  const cudaError_t err = cudaMemsetAsync(barrier, 0, sizeof(int), stream);
+  if (err != cudaSuccess) return set_error(QMOE_ERR_CUDA, "route_permute barrier: %s", cudaGetErrorString(err));
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  const auto* wb = static_cast<const __nv_bfloat16*>(w);
+  auto* xp = static_cast<__nv_bfloat16*>(x_perm);
+#define QMOE_ROUTE_PERMUTE_CASE(GG)                                                                               \
+  case GG: {                                                                                                      \
+    constexpr int kThreads = qmoe::router_warps<GG>() * 32;                                                       \
+    const int smem = qmoe::route_permute_smem_bytes(int(H), int(E), kThreads);                                   \
+    QMOE_CHECK(set_smem(qmoe::route_permute_kernel<GG>, smem));                                                   \
+    return launch_kernel(qmoe::route_permute_kernel<GG>, dim3(nchunks), dim3(kThreads), size_t(smem), stream,     \
+                         true, "route_permute_kernel", xb, wb, bias, int(T), int(E), int(k), normalize, topk_idx, \
+                         topk_w, chunk_hist, counts, offsets, row_token, row_w, slot_row, xp, acc_zero, tiles,     \
+                         int(max_tiles), zero_words, n_zero_words, barrier);                                      \
+  }
+  switch (G) {
+    QMOE_ROUTE_PERMUTE_CASE(1)
+    QMOE_ROUTE_PERMUTE_CASE(2)
+    QMOE_ROUTE_PERMUTE_CASE(4)
+    QMOE_ROUTE_PERMUTE_CASE(8)
+    QMOE_ROUTE_PERMUTE_CASE(16)
+    default:
+      return set_error(QMOE_ERR_UNSUPPORTED_SHAPE, "route_permute: H/256 = %d not in {1,2,4,8,16}", G);
+  }
+#undef QMOE_ROUTE_PERMUTE_CASE
+}
+
 // One grouped-GEMM launch in the normal or the small-tile configuration.
 template <int kMode, bool kSmall>
 int launch_gemm_cfg(const CUtensorMap& tmA, const CUtensorMap& tmB, const qmoe::GemmArgs& a, int grid,
@@ -552,7 +589,7 @@ int launch_finalize(const float* acc, const void* residual, int64_t T, int64_t H
 // Workspace carving for the fused forward.
 struct FwdLayout {
   size_t logits, chunk_hist, counts, offsets, row_token, row_w, slot_row, tiles, topk_idx, topk_w, x_perm,
-      act, acc, split, done, total;
+      act, acc, split, done, route_barrier, total;
 };
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -582,6 +619,7 @@ FwdLayout fwd_layout(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I) {
   L.acc = take(sizeof(float) * size_t(T * H));
   L.split = take(T * k <= kGateUpSplitMaxR ? qmoe::kSplitWorkspaceBytes : 0);
   L.done = take(T > kGatherMaxT ? sizeof(int32_t) * size_t(qmoe_max_tiles(R, E) + 2) : 0);
+  L.route_barrier = take(T > kRouterSmallMaxT ? sizeof(int32_t) : 0);
   L.total = o;
   return L;
 }
@@ -616,12 +654,20 @@ int moe_forward_on(const void* x, const void* w_router, const float* router_bias
   const int64_t tile_rows = std::min<int64_t>(T, qmoe::kBNMax);
 
   float* logits = T <= kRouterSmallMaxT ? reinterpret_cast<float*>(ws + L.logits) : nullptr;
+  const int64_t nchunks = (T + qmoe::kRouterChunk - 1) / qmoe::kRouterChunk;
   if (T <= qmoe::kRouteSmallMaxT && E <= qmoe::kRouteSmallMaxE) {
     // decode sizes: router + permutation in one launch, which also zeroes
     // the gate/up split counters (the workspace may hold anything on entry)
     QMOE_CHECK(launch_route_small(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw, counts,
                                   offsets, row_token, row_w, slot_row, tiles, max_tiles, acc, s, split_counters,
                                   split_counters ? qmoe::kSplitCounterWords : 0));
+  } else if (fused && nchunks <= num_sms(0)) {
+    // prefill batches of at most one router chunk per SM: router, scan and
+    // scatter in one launch (one grid-wide barrier), which also zeroes the
+    // fused kernel's tile counters
+    QMOE_CHECK(launch_route_permute(x, w_router, router_bias, T, H, E, k, normalize, idx, tw, chunk_hist, counts,
+                                    offsets, row_token, row_w, slot_row, tiles, max_tiles, x_perm, acc, done,
+                                    int(max_tiles + 2), reinterpret_cast<int*>(ws + L.route_barrier), s));
   } else {
     QMOE_CHECK(launch_router(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw,
                              chunk_hist, s));

@@ -160,28 +160,24 @@ __device__ __forceinline__ void select_topk_warp(const float* row, int tok, int 
   }
 }
 
-template <int G, int kWarps = router_warps<G>()>  // G = H / 256
-__global__ void __launch_bounds__(kWarps * 32, router_ctas_per_sm<G, kWarps>())
-    router_topk_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
-                       const float* __restrict__ bias, int T, int E, int k, int normalize,
-                       float* __restrict__ logits_out, int32_t* __restrict__ topk_idx,
-                       float* __restrict__ topk_w, int32_t* __restrict__ chunk_hist) {
+// The router for one chunk of kRouterChunk tokens (kWarps warps): fp32
+// logits in the canonical order, softmax, top-k, renormalisation; writes
+// topk_idx / topk_w (and logits_out) of its tokens and leaves the chunk's
+// expert histogram in hist[0, E) (shared), synchronised.  xs: kRouterChunk*H
+// floats and ls: kRouterChunk*E floats of shared memory.
+template <int G, int kWarps>
+__device__ __forceinline__ void router_chunk(int chunk, const __nv_bfloat16* __restrict__ x,
+                                             const __nv_bfloat16* __restrict__ w, const float* __restrict__ bias,
+                                             int T, int E, int k, int normalize, float* __restrict__ logits_out,
+                                             int32_t* __restrict__ topk_idx, float* __restrict__ topk_w, float* xs,
+                                             float* ls, int* hist) {
   constexpr int H = G * 256;
   constexpr int kThreads = kWarps * 32;
   static_assert(kRouterChunk <= kWarps, "one warp per token in the top-k phase");
-  extern __shared__ __align__(16) float router_smem[];
-  float* xs = router_smem;                        // [kRouterChunk][H]
-  float* ls = router_smem + kRouterChunk * H;     // [kRouterChunk][E]
-  __shared__ int hist[256];
-
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int t0 = blockIdx.x * kRouterChunk;
+  const int t0 = chunk * kRouterChunk;
   const int nt = min(kRouterChunk, T - t0);
-  if (threadIdx.x == 0) QMOE_TRACE_AT(0, 0);
-  griddep_wait();
-  griddep_launch_dependents();
-  if (threadIdx.x == 0) QMOE_TRACE_AT(0, 1);
 
   // Stage the chunk's activations in shared memory as fp32.  Inside each
   // 256-element group, element 8l+q is stored at (q/4)*128 + 4l + q%4 so the
@@ -272,11 +268,25 @@ __global__ void __launch_bounds__(kWarps * 32, router_ctas_per_sm<G, kWarps>())
   // Softmax + top-k: one warp per token.
   const int t = warp;
   if (t < nt) select_topk_warp(ls + t * E, t0 + t, E, k, normalize, lane, logits_out, topk_idx, topk_w, hist);
-  if (chunk_hist) {
-    __syncthreads();
-    for (int e = threadIdx.x; e < E; e += kThreads)
-      chunk_hist[size_t(blockIdx.x) * E + e] = hist[e];
-  }
+  __syncthreads();
+}
+
+template <int G, int kWarps = router_warps<G>()>  // G = H / 256
+__global__ void __launch_bounds__(kWarps * 32, router_ctas_per_sm<G, kWarps>())
+    router_topk_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                       const float* __restrict__ bias, int T, int E, int k, int normalize,
+                       float* __restrict__ logits_out, int32_t* __restrict__ topk_idx,
+                       float* __restrict__ topk_w, int32_t* __restrict__ chunk_hist) {
+  extern __shared__ __align__(16) float router_smem[];
+  __shared__ int hist[256];
+  if (threadIdx.x == 0) QMOE_TRACE_AT(0, 0);
+  griddep_wait();
+  griddep_launch_dependents();
+  if (threadIdx.x == 0) QMOE_TRACE_AT(0, 1);
+  router_chunk<G, kWarps>(blockIdx.x, x, w, bias, T, E, k, normalize, logits_out, topk_idx, topk_w, router_smem,
+                          router_smem + kRouterChunk * G * 256, hist);
+  if (chunk_hist)
+    for (int e = threadIdx.x; e < E; e += kWarps * 32) chunk_hist[size_t(blockIdx.x) * E + e] = hist[e];
   if (threadIdx.x == 0) QMOE_TRACE_AT(0, 3);
 }
 

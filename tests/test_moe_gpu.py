@@ -249,6 +249,25 @@ def test_moe_forward_cfg0_shapes(cuda_dev, oracle, T):
     assert err <= MAX_REL, f"moe_forward max rel err {err:.3e}"
 
 
+@pytest.mark.parametrize("T,H,E,k,I", [(1184, 256, 32, 4, 128), (300, 1024, 256, 8, 256), (65, 512, 64, 2, 128),
+                                       (700, 4096, 128, 8, 128), (1185, 512, 32, 8, 128)])
+def test_moe_forward_route_permute_shapes(cuda_dev, oracle, T, H, E, k, I):
+    """Prefill batches of at most one router chunk per SM route and permute in
+    one launch (grid-wide barrier); 1185 tokens (149 chunks) take the separate
+    kernels.  Routing bit-exact, output within the activation tolerance."""
+    from nki_moe_7013_b200 import _C, ops
+
+    wr, wgu, wd = moe_weights(12, E, H, I, cuda_dev)
+    x = activations(12 + T, T, H, cuda_dev)
+    out, idx, tw = ops.moe_forward(x, wr, wgu, wd, k, return_routing=True)
+    torch.cuda.synchronize()
+    assert _C.device_error() == 0
+    ref_out, inter = oracle.moe_block(x.cpu(), wr.cpu(), wgu.cpu(), wd.cpu(), k, return_intermediates=True)
+    assert np.array_equal(idx.cpu().numpy(), inter["topk_idx"])
+    np.testing.assert_allclose(tw.cpu().numpy(), inter["topk_w"], rtol=2e-6, atol=1e-7)
+    assert max_rel_err(to_f32_np(out), oracle.round_to_bf16(ref_out)) <= MAX_REL
+
+
 def test_moe_forward_residual_and_determinism(cuda_dev, oracle):
     from nki_moe_7013_b200 import ops
 
