@@ -16,8 +16,10 @@
 //                  chunk that chose the same expert (popcount of a bitmask)
 //                  plus the chunk prefix, so rows inside an expert follow
 //                  ascending token id -- deterministic and bit-exact.  The CTA
-//                  then gathers its tokens' activation rows into x_perm and
-//                  zero-fills their rows of the fp32 combine accumulator.
+//                  then copies its tokens' activation rows into x_perm (TMA
+//                  bulk loads of the chunk's 8 token rows into shared memory,
+//                  one bulk store per (token, slot) row) and zero-fills their
+//                  rows of the fp32 combine accumulator.
 //   route_permute kernel (batches of at most one chunk per SM): the router
 //                  and both kernels above in one launch -- every CTA routes
 //                  its chunk, publishes the chunk histogram, waits at one
@@ -178,52 +180,58 @@ __device__ __forceinline__ void permute_chunk_rows(int c, int T, int E, int k, c
   __syncthreads();
 }
 
-// The chunk's activation rows into x_perm (pos_s from permute_chunk_rows) and
-// its rows of the combine accumulator zero-filled; this CTA takes share
-// `part` of `nparts`.
-__device__ __forceinline__ void permute_chunk_copy(int c, int part, int nparts, int T, int H, int k,
-                                                   const int* pos_s, const __nv_bfloat16* __restrict__ x,
-                                                   __nv_bfloat16* __restrict__ x_perm, float* __restrict__ acc_zero) {
-  const int tid = threadIdx.x;
+// The chunk's rows of the combine accumulator zero-filled; this CTA takes
+// share `part` of `nparts`.
+__device__ __forceinline__ void permute_chunk_zero_acc(int c, int part, int nparts, int T, int H,
+                                                       float* __restrict__ acc_zero) {
+  if (!acc_zero) return;
   const int t0 = c * kRouterChunk;
   const int nt = min(kRouterChunk, T - t0);
-  const int npairs = nt * k;
-  if (x_perm) {
-    // 4 independent 16-byte copies in flight per thread
-    const int vec_per_row = H / 8;
-    const int total_v = npairs * vec_per_row;
-    const int stride = blockDim.x * nparts;
-    for (int v0 = part * blockDim.x + tid; v0 < total_v; v0 += 4 * stride) {
-      uint4 val[4];
-      int dst[4], col[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int v = v0 + u * stride;
-        dst[u] = -1;
-        if (v < total_v) {
-          const int p = v / vec_per_row;
-          col[u] = (v - p * vec_per_row) * 8;
-          dst[u] = pos_s[p];
-          if (dst[u] >= 0) val[u] = *reinterpret_cast<const uint4*>(x + size_t(t0 + p / k) * H + col[u]);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        if (dst[u] >= 0) *reinterpret_cast<uint4*>(x_perm + size_t(dst[u]) * H + col[u]) = val[u];
-    }
+  const int vec_per_row = H / 4;
+  const int total_v = nt * vec_per_row;
+  for (int v = part * blockDim.x + threadIdx.x; v < total_v; v += blockDim.x * nparts) {
+    const int tl = v / vec_per_row;
+    const int cc = (v % vec_per_row) * 4;
+    *reinterpret_cast<float4*>(acc_zero + size_t(t0 + tl) * H + cc) = make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  if (acc_zero) {
-    const int vec_per_row = H / 4;
-    const int total_v = nt * vec_per_row;
-    for (int v = part * blockDim.x + tid; v < total_v; v += blockDim.x * nparts) {
-      const int tl = v / vec_per_row;
-      const int cc = (v % vec_per_row) * 4;
-      *reinterpret_cast<float4*>(acc_zero + size_t(t0 + tl) * H + cc) = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// The chunk's (token, slot) rows of this CTA's share into x_perm with one
+// bulk store each, from the token rows (rows_s, bf16, loaded on rows_bar);
+// every thread that issued waits for its store.  Thread 0 also waits for the
+// row loads when it issues nothing, so no load outlives the CTA.
+__device__ __forceinline__ void permute_chunk_bulk_rows(int c, int part, int nparts, int T, int H, int k,
+                                                        const int* pos_s, const __nv_bfloat16* rows_s,
+                                                        uint64_t* rows_bar, int* rows_abort,
+                                                        __nv_bfloat16* __restrict__ x_perm) {
+  const int tid = threadIdx.x;
+  const int npairs = min(kRouterChunk, T - c * kRouterChunk) * k;
+  const bool mine = tid < npairs && tid % nparts == part;
+  if (mine || tid == 0) {
+    const bool rows_in = mbar_wait_bounded(rows_bar, 0, rows_abort, kDevErrWaitTimeoutProducer);
+    const int pos = mine ? pos_s[tid] : -1;
+    if (rows_in && pos >= 0) {
+      bulk_store(x_perm + size_t(pos) * H, rows_s + (tid / k) * H, H * 2);
+      bulk_commit_group();
+      bulk_wait_all();
     }
   }
 }
 
-// One CTA per router chunk (8 tokens); gridDim.y CTAs share the row gather.
+// Thread 0: bulk loads of the chunk's token rows into rows_s (bf16) on
+// rows_bar (initialised here).
+__device__ __forceinline__ void permute_chunk_load_rows(int c, int T, int H, const __nv_bfloat16* __restrict__ x,
+                                                        __nv_bfloat16* rows_s, uint64_t* rows_bar, int* rows_abort) {
+  const int nt = min(kRouterChunk, T - c * kRouterChunk);
+  *rows_abort = 0;
+  mbar_init(rows_bar, 1);
+  fence_mbarrier_init();
+  mbar_arrive_expect_tx(rows_bar, uint32_t(nt) * H * 2);
+  for (int t = 0; t < nt; ++t) bulk_load(rows_s + t * H, x + size_t(c * kRouterChunk + t) * H, H * 2, rows_bar);
+}
+
+// One CTA per router chunk (8 tokens); gridDim.y CTAs share the row copy.
+// Dynamic shared memory: kRouterChunk * H bf16 when x_perm is set.
 __global__ void __launch_bounds__(kScatterThreads)
     permute_scatter_kernel(const int32_t* __restrict__ topk_idx, const float* __restrict__ topk_w,
                            const int32_t* __restrict__ chunk_prefix,
@@ -233,16 +241,22 @@ __global__ void __launch_bounds__(kScatterThreads)
                            int32_t* __restrict__ slot_row, __nv_bfloat16* __restrict__ x_perm,
                            float* __restrict__ acc_zero, int32_t* __restrict__ tiles, int max_tiles,
                            int32_t* __restrict__ zero_words, int n_zero_words) {
+  extern __shared__ __align__(16) __nv_bfloat16 scatter_rows_s[];
   __shared__ unsigned mask[256];
   __shared__ int off_s[256];
   __shared__ int pos_s[kScatterThreads];
   __shared__ int warp_sums[32];
+  __shared__ __align__(8) uint64_t rows_bar;
+  __shared__ int rows_abort;
   const int c = blockIdx.x;
   const int part = blockIdx.y;
   const int tid = threadIdx.x;
   if (threadIdx.x == 0 && blockIdx.y == 0) QMOE_TRACE_AT(5, 0);
   griddep_wait();
   griddep_launch_dependents();
+  // x is an input of the layer, not of the router: its rows can be in flight
+  // while the offsets and ranks are worked out
+  if (x_perm && tid == 0) permute_chunk_load_rows(c, T, H, x, scatter_rows_s, &rows_bar, &rows_abort);
 
   const bool lead = c == 0 && part == 0;
   permute_offsets(tid < E ? counts[tid] : 0, E, lead, off_s, warp_sums, nullptr, offsets, tiles, max_tiles);
@@ -252,7 +266,9 @@ __global__ void __launch_bounds__(kScatterThreads)
   permute_chunk_rows(
       c, T, E, k, topk_idx, topk_w, off_s, [&](int e) { return pre_row[e]; }, part == 0, row_token, row_w,
       slot_row, mask, pos_s);
-  permute_chunk_copy(c, part, gridDim.y, T, H, k, pos_s, x, x_perm, acc_zero);
+  permute_chunk_zero_acc(c, part, gridDim.y, T, H, acc_zero);
+  if (x_perm)
+    permute_chunk_bulk_rows(c, part, gridDim.y, T, H, k, pos_s, scatter_rows_s, &rows_bar, &rows_abort, x_perm);
   if (threadIdx.x == 0 && blockIdx.y == 0) QMOE_TRACE_AT(5, 3);
 }
 
@@ -294,7 +310,6 @@ __global__ void __launch_bounds__(router_warps<G>() * 32, 1)
   __shared__ int rows_abort;
   const int c = blockIdx.x;
   const int tid = threadIdx.x;
-  const int nt = min(kRouterChunk, T - c * kRouterChunk);
   __nv_bfloat16* rows_s = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(router_smem) +
                                                            route_permute_stage_bytes(H, E, kThreads));
   if (tid == 0) QMOE_TRACE_AT(0, 0);
@@ -303,11 +318,7 @@ __global__ void __launch_bounds__(router_warps<G>() * 32, 1)
   if (tid == 0) {
     QMOE_TRACE_AT(0, 1);
     // the chunk's token rows, bf16, for the bulk stores after the barrier
-    rows_abort = 0;
-    mbar_init(&rows_bar, 1);
-    fence_mbarrier_init();
-    mbar_arrive_expect_tx(&rows_bar, uint32_t(nt) * H * 2);
-    for (int t = 0; t < nt; ++t) bulk_load(rows_s + t * H, x + size_t(c * kRouterChunk + t) * H, H * 2, &rows_bar);
+    permute_chunk_load_rows(c, T, H, x, rows_s, &rows_bar, &rows_abort);
   }
   router_chunk<G, kWarps>(c, x, w, bias, T, E, k, normalize, nullptr, topk_idx, topk_w, router_smem,
                           router_smem + kRouterChunk * H, hist);
@@ -364,17 +375,9 @@ __global__ void __launch_bounds__(router_warps<G>() * 32, 1)
   permute_chunk_rows(
       c, T, E, k, topk_idx, topk_w, off_s, [&](int e) { return pre_s[e]; }, true, row_token, row_w, slot_row, mask,
       pos_s);
-  permute_chunk_copy(c, 0, 1, T, H, k, pos_s, x, nullptr, acc_zero);
-  // one bulk store per (token, slot) row; every thread that issued waits for
-  // its store to complete before the CTA's shared memory goes away
-  if (tid < nt * k) {
-    const bool rows_in = mbar_wait_bounded(&rows_bar, 0, &rows_abort, kDevErrWaitTimeoutProducer);
-    const int pos = pos_s[tid];
-    if (rows_in && x_perm != nullptr && pos >= 0) {
-      bulk_store(x_perm + size_t(pos) * H, rows_s + (tid / k) * H, H * 2);
-      bulk_commit_group();
-      bulk_wait_all();
-    }
+  permute_chunk_zero_acc(c, 0, 1, T, H, acc_zero);
+  if (x_perm) {
+    permute_chunk_bulk_rows(c, 0, 1, T, H, k, pos_s, rows_s, &rows_bar, &rows_abort, x_perm);
   } else if (tid == 0) {
     mbar_wait_bounded(&rows_bar, 0, &rows_abort, kDevErrWaitTimeoutProducer);
   }

@@ -341,8 +341,11 @@ int launch_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chunk_
   if (nchunks > 0) {
     // Enough CTAs to keep the row gather from being latency-bound.
     const int parts = x_perm ? int(std::max<int64_t>(1, std::min<int64_t>(8, (4 * num_sms(0) + nchunks - 1) / nchunks))) : 1;
+    // the chunk's token rows in shared memory for the bulk row copy
+    const int smem = x_perm ? int(2 * qmoe::kRouterChunk * H) : 0;
+    QMOE_CHECK(set_smem(qmoe::permute_scatter_kernel, smem));
     QMOE_CHECK(launch_kernel(qmoe::permute_scatter_kernel, dim3(nchunks, parts), dim3(qmoe::kScatterThreads),
-                             0, stream, true, "permute_scatter_kernel", topk_idx, topk_w,
+                             size_t(smem), stream, true, "permute_scatter_kernel", topk_idx, topk_w,
                              static_cast<const int32_t*>(chunk_hist), static_cast<const int32_t*>(counts),
                              offsets, static_cast<const __nv_bfloat16*>(x), int(T), int(H), int(E), int(k),
                              row_token, row_w, slot_row, static_cast<__nv_bfloat16*>(x_perm), acc_zero,
