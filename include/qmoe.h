@@ -135,6 +135,23 @@ QMOE_API int qmoe_moe_permute(const int32_t* topk_idx, const float* topk_w, int3
                      int32_t* zero_words, int64_t n_zero_words, void* stream);
 
 /* ------------------------------------------------------------------------
+ * K1 + K2 in one call: the outputs of qmoe_router_topk (topk_idx, topk_w)
+ * followed by qmoe_moe_permute, identical values.  Prefill batches with at
+ * most one router chunk (8 tokens) per SM and T > 64 run as ONE launch: each
+ * CTA routes its chunk, publishes its histogram, waits at a grid-wide barrier,
+ * then sums the histograms into the counts and its own chunk prefix and
+ * permutes its chunk (rows copied with TMA bulk copies).  Other sizes run the
+ * two kernels.  chunk_hist ((T+7)/8, E) int32 scratch, 16-byte aligned (it
+ * keeps the raw chunk histograms on the one-launch path, the prefixes
+ * otherwise); barrier: one int32 of device scratch, cleared by the call.
+ * ---------------------------------------------------------------------- */
+QMOE_API int qmoe_route_permute(const void* x, const void* w_router, const float* bias, int64_t T, int64_t H,
+                                int64_t E, int64_t k, int normalize, int32_t* topk_idx, float* topk_w,
+                                int32_t* chunk_hist, int32_t* counts, int32_t* offsets, int32_t* row_token,
+                                float* row_w, int32_t* slot_row, int32_t* tiles, void* x_perm, float* acc_zero,
+                                int32_t* zero_words, int64_t n_zero_words, int32_t* barrier, void* stream);
+
+/* ------------------------------------------------------------------------
  * K3a  grouped GEMM, gate/up projection fused with SiLU(gate)*up.
  * Replaces _nki_cte_moe_left_gate_up_kernel (qwen_with_nki.py:5341-5369) and
  * the decode gate/up stage of _nki_batched_moe_kernel

@@ -30,6 +30,7 @@ _SIGNATURES = {
     "qmoe_router_topk": (I32, [P, P, P, I64, I64, I64, I64, I32, P, P, P, P, P]),
     "qmoe_max_tiles": (I64, [I64, I64]),
     "qmoe_moe_permute": (I32, [P, P, P, P, I64, I64, I64, I64, P, P, P, P, P, P, P, P, P, I64, P]),
+    "qmoe_route_permute": (I32, [P, P, P, I64, I64, I64, I64, I32, P, P, P, P, P, P, P, P, P, P, P, P, I64, P, P]),
     "qmoe_moe_experts": (I32, [P, I64, P, P, P, P, I64, P, P, I64, I64, I64, I64, P, P, I64, P, P]),
     "qmoe_grouped_gemm_gateup_split_workspace_size": (SZ, []),
     "qmoe_route_small": (I32, [P, P, P, I64, I64, I64, I64, I32, P, P, P, P, P, P, P, P, P, P, P]),

@@ -758,11 +758,13 @@ int qmoe_router_topk(const void* x, const void* w_router, const float* bias, int
                        chunk_hist, static_cast<cudaStream_t>(stream));
 }
 
-int qmoe_moe_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chunk_hist,
-                     const void* x, int64_t T, int64_t H, int64_t E, int64_t k, int32_t* counts,
-                     int32_t* offsets, int32_t* row_token, float* row_w, int32_t* slot_row,
-                     int32_t* tiles, void* x_perm, float* acc_zero, int32_t* zero_words, int64_t n_zero_words,
-                     void* stream) {
+}  // extern "C"
+
+namespace {
+int check_permute_args(const int32_t* topk_idx, const float* topk_w, const int32_t* chunk_hist, const void* x,
+                       int64_t T, int64_t H, int64_t E, int64_t k, const int32_t* counts, const int32_t* offsets,
+                       const int32_t* row_token, const float* row_w, const int32_t* slot_row, const int32_t* tiles,
+                       const void* x_perm, const float* acc_zero, const int32_t* zero_words, int64_t n_zero_words) {
   QMOE_REQUIRE(!zero_words == (n_zero_words == 0) && n_zero_words >= 0 && n_zero_words < (int64_t(1) << 24),
                QMOE_ERR_INVALID_ARGUMENT, "permute: bad zero_words / n_zero_words");
   QMOE_REQUIRE(topk_idx && topk_w && chunk_hist && counts && offsets && row_token && row_w &&
@@ -779,11 +781,48 @@ int qmoe_moe_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chun
                  "permute: x / x_perm null or not 16-byte aligned");
     QMOE_REQUIRE(!acc_zero || aligned16(acc_zero), QMOE_ERR_MISALIGNED, "permute: acc not aligned");
   }
+  return QMOE_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int qmoe_moe_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chunk_hist,
+                     const void* x, int64_t T, int64_t H, int64_t E, int64_t k, int32_t* counts,
+                     int32_t* offsets, int32_t* row_token, float* row_w, int32_t* slot_row,
+                     int32_t* tiles, void* x_perm, float* acc_zero, int32_t* zero_words, int64_t n_zero_words,
+                     void* stream) {
+  QMOE_CHECK(check_permute_args(topk_idx, topk_w, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w,
+                                slot_row, tiles, x_perm, acc_zero, zero_words, n_zero_words));
   DeviceInfo* d = nullptr;
   QMOE_CHECK(device_info(&d));
   return launch_permute(topk_idx, topk_w, chunk_hist, x, T, H, E, k, counts, offsets, row_token,
                         row_w, slot_row, tiles, x_perm, acc_zero, static_cast<cudaStream_t>(stream), zero_words,
                         int(n_zero_words));
+}
+
+int qmoe_route_permute(const void* x, const void* w_router, const float* bias, int64_t T, int64_t H, int64_t E,
+                       int64_t k, int normalize, int32_t* topk_idx, float* topk_w, int32_t* chunk_hist,
+                       int32_t* counts, int32_t* offsets, int32_t* row_token, float* row_w, int32_t* slot_row,
+                       int32_t* tiles, void* x_perm, float* acc_zero, int32_t* zero_words, int64_t n_zero_words,
+                       int32_t* barrier, void* stream) {
+  QMOE_CHECK(check_router_args(x, w_router, T, H, E, k, topk_idx, topk_w));
+  QMOE_CHECK(check_permute_args(topk_idx, topk_w, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w,
+                                slot_row, tiles, x_perm, acc_zero, zero_words, n_zero_words));
+  QMOE_REQUIRE(barrier && (reinterpret_cast<uintptr_t>(chunk_hist) & 15u) == 0, QMOE_ERR_INVALID_ARGUMENT,
+               "route_permute: null barrier or chunk_hist not 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  if (T == 0) return QMOE_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t nchunks = (T + qmoe::kRouterChunk - 1) / qmoe::kRouterChunk;
+  if (T > kRouterSmallMaxT && nchunks <= num_sms(0))
+    return launch_route_permute(x, w_router, bias, T, H, E, k, normalize, topk_idx, topk_w, chunk_hist, counts,
+                                offsets, row_token, row_w, slot_row, tiles, qmoe_max_tiles(T * k, E), x_perm,
+                                acc_zero, zero_words, int(n_zero_words), barrier, s);
+  QMOE_CHECK(launch_router(x, w_router, bias, T, H, E, k, normalize, nullptr, topk_idx, topk_w, chunk_hist, s));
+  return launch_permute(topk_idx, topk_w, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w, slot_row,
+                        tiles, x_perm, acc_zero, s, zero_words, int(n_zero_words));
 }
 
 int qmoe_route_small(const void* x, const void* w_router, const float* bias, int64_t T, int64_t H, int64_t E,

@@ -223,6 +223,7 @@ class MoEPlan:
 
     STAGES = ("router", "permute", "gate_up", "down", "finalize")
     STAGES_FUSED = ("router", "permute", "experts", "finalize")
+    STAGES_ROUTED = ("route", "experts", "finalize")  # router + permutation in one launch
 
     def __init__(self, weights: MoEWeights, T: int, k: int, normalize: bool = True,
                  bias: Optional[torch.Tensor] = None, prefill_gather: Optional[bool] = None,
@@ -262,7 +263,14 @@ class MoEPlan:
         self.x_perm = (torch.empty((max(R, 1), H), dtype=torch.bfloat16, device=dev)
                        if T > ops.GATHER_MAX_T and not (self.fused and prefill_gather) else None)
         self.done = torch.zeros(self.max_tiles + 1, **i32) if self.fused else None
-        self.stages = self.STAGES_FUSED if self.fused else self.STAGES
+        # prefill batches of at most one router chunk per SM route and permute
+        # in one launch (the library forward does the same)
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        self.route_permute = (self.fused and self.x_perm is not None and T > ops.ROUTER_SMALL_MAX_T
+                              and nchunks <= sms)
+        self.route_barrier = torch.zeros(1, **i32) if self.route_permute else None
+        self.stages = (self.STAGES_ROUTED if self.route_permute else
+                       self.STAGES_FUSED if self.fused else self.STAGES)
         self.ws_bytes = int(_C.lib().qmoe_moe_forward_workspace_size(T, H, E, k, I))
         self.workspace = torch.empty(max(self.ws_bytes, 256), dtype=torch.uint8, device=dev)
         # small batches route through the logits + selection kernels
@@ -288,28 +296,39 @@ class MoEPlan:
                                           p(self.topk_w), p(self.workspace), self.ws_bytes, s), "moe_forward")
             return out
 
-        def mark(i):
-            if events is not None:
-                events[i].record()
+        n_marked = [0]
 
-        mark(0)
+        def mark():  # the event after the next stage
+            if events is not None:
+                events[n_marked[0]].record()
+            n_marked[0] += 1
+
+        mark()
         if self.route_small:
             _C.check(lib.qmoe_route_small(p(x), p(w.router), p(self.bias), T, H, E, k, 1 if self.normalize else 0,
                                           p(self.logits), p(self.topk_idx), p(self.topk_w), p(self.counts),
                                           p(self.offsets), p(self.row_token), p(self.row_w), p(self.slot_row),
                                           p(self.tiles), p(self.acc), s), "route_small")
-            mark(1)
+            mark()
+            mark()
+        elif self.route_permute:
+            _C.check(lib.qmoe_route_permute(p(x), p(w.router), p(self.bias), T, H, E, k, 1 if self.normalize else 0,
+                                            p(self.topk_idx), p(self.topk_w), p(self.hist), p(self.counts),
+                                            p(self.offsets), p(self.row_token), p(self.row_w), p(self.slot_row),
+                                            p(self.tiles), p(self.x_perm), p(self.acc), p(self.done),
+                                            self.max_tiles + 1, p(self.route_barrier), s), "route")
+            mark()
         else:
             _C.check(lib.qmoe_router_topk(p(x), p(w.router), p(self.bias), T, H, E, k,
                                           1 if self.normalize else 0, p(self.logits), p(self.topk_idx),
                                           p(self.topk_w), p(self.hist), s), "router")
-            mark(1)
+            mark()
             _C.check(lib.qmoe_moe_permute(p(self.topk_idx), p(self.topk_w), p(self.hist), p(x), T, H, E, k,
                                           p(self.counts), p(self.offsets), p(self.row_token), p(self.row_w),
                                           p(self.slot_row), p(self.tiles), p(self.x_perm), p(self.acc),
                                           p(self.done), self.max_tiles + 1 if self.fused else 0, s),
                      "permute")
-        mark(2)
+            mark()
         if self.fused:
             if self.x_perm is not None:
                 src, src_rows, gather = self.x_perm, R, None
@@ -318,9 +337,9 @@ class MoEPlan:
             _C.check(lib.qmoe_moe_experts(p(src), src_rows, p(gather), p(w.gate_up), p(w.down), p(self.tiles),
                                           self.max_tiles, p(self.row_token), p(self.row_w), R, H, I, E, p(self.act),
                                           p(self.acc), T, p(self.done), s), "experts")
-            mark(3)
+            mark()
             _C.check(lib.qmoe_combine_finalize(p(self.acc), p(residual), T, H, p(out), s), "finalize")
-            mark(4)
+            mark()
             return out
         if self.x_perm is not None:
             _C.check(lib.qmoe_grouped_gemm_gateup_swiglu(p(self.x_perm), R, None, p(w.gate_up), p(self.tiles),
@@ -331,14 +350,14 @@ class MoEPlan:
                                                          p(self.tiles), self.max_tiles, self.tile_rows, R, H, I, E,
                                                          p(self.act), p(self.split_ws), self._split_bytes, s),
                      "gate_up")
-        mark(3)
+        mark()
         # tiles come from the routing kernels, before the gate/up GEMM
         _C.check(lib.qmoe_grouped_gemm_down_combine(p(self.act), p(w.down), p(self.tiles), self.max_tiles,
                                                     self.tile_rows, 1, p(self.row_token), p(self.row_w), R, H, I, E,
                                                     p(self.acc), T, s), "down")
-        mark(4)
+        mark()
         _C.check(lib.qmoe_combine_finalize(p(self.acc), p(residual), T, H, p(out), s), "finalize")
-        mark(5)
+        mark()
         return out
 
     LAUNCHES_PER_RUN = 6  # router, scan, scatter, gate/up, down, finalize (T > 64)
@@ -354,6 +373,8 @@ class MoEPlan:
         finalize."""
         if self.route_small:
             return 3  # route, gate/up, down (+ finalize folded in)
+        if self.route_permute:
+            return 2  # route + permutation, experts (+ finalize folded in)
         if self.fused:
             return 4  # router, scan, scatter, experts (+ finalize folded in)
         return (7 if self.T <= ops.ROUTER_SMALL_MAX_T else 6)

@@ -149,6 +149,41 @@ def moe_permute(topk_idx: torch.Tensor, topk_w: torch.Tensor, chunk_hist: torch.
                 slot_row=slot_row, tiles=tiles, max_tiles=mt, x_perm=x_perm, done=done)
 
 
+def route_permute(x: torch.Tensor, w_router: torch.Tensor, k: int, normalize: bool = True,
+                  bias: Optional[torch.Tensor] = None, gather: bool = True,
+                  acc_zero: Optional[torch.Tensor] = None):
+    """K1 + K2 in one call (one launch for prefill batches of at most one
+    router chunk per SM): the outputs of router_topk followed by moe_permute,
+    as moe_permute's dict plus topk_idx / topk_w."""
+    _need(x, "x", torch.bfloat16, 2)
+    _need(w_router, "w_router", torch.bfloat16, 2)
+    T, H = x.shape
+    E = w_router.shape[0]
+    R = T * k
+    dev = x.device
+    i32 = dict(dtype=torch.int32, device=dev)
+    mt = max_tiles(R, E)
+    out = dict(topk_idx=torch.empty((T, k), **i32), topk_w=torch.empty((T, k), dtype=torch.float32, device=dev),
+               chunk_hist=torch.empty((max((T + ROUTER_CHUNK - 1) // ROUTER_CHUNK, 1), E), **i32),
+               counts=torch.empty(E, **i32), offsets=torch.empty(E + 1, **i32), row_token=torch.empty(R, **i32),
+               row_w=torch.empty(R, dtype=torch.float32, device=dev), slot_row=torch.empty((T, k), **i32),
+               tiles=torch.empty(1 + 3 * mt, **i32), max_tiles=mt, done=torch.empty(mt + 1, **i32),
+               x_perm=torch.empty((R, H), dtype=torch.bfloat16, device=dev) if gather else None)
+    barrier = torch.empty(1, **i32)
+    if acc_zero is not None:
+        _need(acc_zero, "acc_zero", torch.float32, 2)
+    if bias is not None:
+        _need(bias, "bias", torch.float32, 1)
+    with torch.cuda.device(dev):
+        _C.check(_C.lib().qmoe_route_permute(
+            _ptr(x), _ptr(w_router), _ptr(bias), T, H, E, k, 1 if normalize else 0, _ptr(out["topk_idx"]),
+            _ptr(out["topk_w"]), _ptr(out["chunk_hist"]), _ptr(out["counts"]), _ptr(out["offsets"]),
+            _ptr(out["row_token"]), _ptr(out["row_w"]), _ptr(out["slot_row"]), _ptr(out["tiles"]),
+            _ptr(out["x_perm"]), _ptr(acc_zero), _ptr(out["done"]), mt + 1, _ptr(barrier), _stream(dev)),
+            "qmoe_route_permute")
+    return out
+
+
 def moe_experts(x: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor, tiles: torch.Tensor,
                 max_tiles_: int, row_dst: torch.Tensor, row_w: torch.Tensor, acc: torch.Tensor,
                 done: torch.Tensor, act: Optional[torch.Tensor] = None,

@@ -104,3 +104,35 @@ def test_route_small_matches_router_and_permute(cuda_dev, oracle, T, H, E, k):
     assert torch.count_nonzero(acc).item() == 0
     ref = oracle.permute(idx.cpu().numpy(), E)
     np.testing.assert_array_equal(r["row_token"].cpu().numpy(), ref["row_token"])
+
+
+@pytest.mark.parametrize("T,H,E,k", [(1000, 2048, 128, 8), (65, 512, 64, 4), (1184, 256, 32, 8), (1300, 2048, 128, 8),
+                                     (300, 4096, 256, 8)])
+def test_route_permute_matches_router_and_permute(cuda_dev, oracle, T, H, E, k):
+    """Router + permutation in one call (one launch up to one router chunk per
+    SM, 1300 tokens: the two kernels) gives the separate kernels' outputs bit
+    for bit, and zero-fills the accumulator and the counters."""
+    from nki_moe_7013_b200 import _C, ops
+
+    wr = moe_weights(60 + T, E, H, 128, cuda_dev)[0]
+    x = activations(60 + T, T, H, cuda_dev)
+    acc = torch.full((T, H), 3.0, dtype=torch.float32, device=cuda_dev)
+    r = ops.route_permute(x, wr, k, acc_zero=acc)
+    r2 = ops.route_permute(x, wr, k)  # a second call on fresh (uninitialised) outputs
+    idx, w, hist = ops.router_topk(x, wr, k, return_hist=True)
+    p = ops.moe_permute(idx, w, hist, E, x=x, gather=True)
+    torch.cuda.synchronize()
+    assert _C.device_error() == 0
+    assert torch.equal(r["topk_idx"], idx) and torch.equal(r["topk_w"], w)
+    for key in ("counts", "offsets", "row_token", "row_w", "slot_row", "x_perm"):
+        assert torch.equal(r[key], p[key]), key
+        assert torch.equal(r2[key], p[key]), key
+    nt = int(p["tiles"][0])
+    mt = p["max_tiles"]
+    assert int(r["tiles"][0]) == nt
+    for part in range(3):
+        assert torch.equal(r["tiles"][1 + part * mt:1 + part * mt + nt], p["tiles"][1 + part * mt:1 + part * mt + nt])
+    assert torch.count_nonzero(acc).item() == 0
+    assert torch.count_nonzero(r2["done"]).item() == 0
+    ref = oracle.permute(idx.cpu().numpy(), E)
+    np.testing.assert_array_equal(r["row_token"].cpu().numpy(), ref["row_token"])
