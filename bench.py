@@ -705,7 +705,7 @@ def run_ours_ep(args):
                    "l2": "inputs larger than L2: expert weights and all-to-all buffers streamed per step"},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2,
                 "api": "PeerExpertParallelMoE step (CUDA graph replay of its forward), pinned host in/out"},
-        "gpu_launches": 9 * args.steps,
+        "gpu_launches": moe.launches_per_step(T) * args.steps,
         "stage_us_rank0": stage_us,
         "roofline": {"bound": "hbm", "kernel": "whole EP step (local experts' weights + rows in/out)",
                      "achieved": achieved, "peak": hbm_gbs, "unit": "GB/s", "frac": achieved / hbm_gbs,

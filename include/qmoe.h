@@ -143,7 +143,9 @@ QMOE_API int qmoe_moe_permute(const int32_t* topk_idx, const float* topk_w, int3
  * permutes its chunk (rows copied with TMA bulk copies).  Other sizes run the
  * two kernels.  chunk_hist ((T+7)/8, E) int32 scratch, 16-byte aligned (it
  * keeps the raw chunk histograms on the one-launch path, the prefixes
- * otherwise); barrier: one int32 of device scratch, cleared by the call.
+ * otherwise); barrier: two int32 of device scratch, zero-filled before the
+ * first call; every completed call leaves them zero again (a call that
+ * records a wait time-out may not: zero them again before the next).
  * ---------------------------------------------------------------------- */
 QMOE_API int qmoe_route_permute(const void* x, const void* w_router, const float* bias, int64_t T, int64_t H,
                                 int64_t E, int64_t k, int normalize, int32_t* topk_idx, float* topk_w,

@@ -284,9 +284,11 @@ __host__ __device__ constexpr int route_permute_smem_bytes(int H, int E, int thr
 
 // Router + permutation in one launch for nchunks <= SMs (see the header
 // comment).  chunk_hist (nchunks, E) int32 scratch receives the raw chunk
-// histograms; barrier: one int32, zero on entry (the grid-wide barrier's
-// arrival counter).  Writes what router_topk + scan + scatter write except
-// the per-chunk prefixes (chunk_hist keeps the histograms).
+// histograms; barrier: two int32 (arrivals, departures of the grid-wide
+// barrier), zero on entry -- the last CTA through resets both, so a launch
+// that completes leaves them zero for the next.  Writes what router_topk +
+// scan + scatter write except the per-chunk prefixes (chunk_hist keeps the
+// histograms).
 template <int G>
 __global__ void __launch_bounds__(router_warps<G>() * 32, 1)
     route_permute_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
@@ -315,20 +317,27 @@ __global__ void __launch_bounds__(router_warps<G>() * 32, 1)
   if (tid == 0) QMOE_TRACE_AT(0, 0);
   griddep_wait();
   griddep_launch_dependents();
-  if (tid == 0) {
-    QMOE_TRACE_AT(0, 1);
-    // the chunk's token rows, bf16, for the bulk stores after the barrier
-    permute_chunk_load_rows(c, T, H, x, rows_s, &rows_bar, &rows_abort);
-  }
+  const bool copy_rows = x_perm != nullptr;
+  if (tid == 0) QMOE_TRACE_AT(0, 1);
+  // the chunk's token rows, bf16, for the bulk stores after the barrier
+  if (copy_rows && tid == 0) permute_chunk_load_rows(c, T, H, x, rows_s, &rows_bar, &rows_abort);
   router_chunk<G, kWarps>(c, x, w, bias, T, E, k, normalize, nullptr, topk_idx, topk_w, router_smem,
                           router_smem + kRouterChunk * H, hist);
   for (int e = tid; e < E; e += kThreads) chunk_hist[size_t(c) * E + e] = hist[e];
   if (!grid_barrier_once(barrier, kDevErrWaitTimeoutProducer)) {
     // the row loads land before the CTA leaves
-    if (tid == 0) mbar_wait_bounded(&rows_bar, 0, &rows_abort, kDevErrWaitTimeoutProducer);
+    if (copy_rows && tid == 0) mbar_wait_bounded(&rows_bar, 0, &rows_abort, kDevErrWaitTimeoutProducer);
     return;
   }
-  if (tid == 0) QMOE_TRACE_AT(0, 2);
+  // every CTA has passed the wait once its departure is counted: the last one
+  // clears the barrier for the next launch
+  if (tid == 0) {
+    QMOE_TRACE_AT(0, 2);
+    if (atomicAdd(barrier + 1, 1) == int(gridDim.x) - 1) {
+      barrier[0] = 0;
+      barrier[1] = 0;
+    }
+  }
 
   // Every chunk's histogram is out: this chunk's prefix and the counts.  A
   // thread sums 4 experts over a strided subset of the chunks (16-byte loads
@@ -376,11 +385,7 @@ __global__ void __launch_bounds__(router_warps<G>() * 32, 1)
       c, T, E, k, topk_idx, topk_w, off_s, [&](int e) { return pre_s[e]; }, true, row_token, row_w, slot_row, mask,
       pos_s);
   permute_chunk_zero_acc(c, 0, 1, T, H, acc_zero);
-  if (x_perm) {
-    permute_chunk_bulk_rows(c, 0, 1, T, H, k, pos_s, rows_s, &rows_bar, &rows_abort, x_perm);
-  } else if (tid == 0) {
-    mbar_wait_bounded(&rows_bar, 0, &rows_abort, kDevErrWaitTimeoutProducer);
-  }
+  if (copy_rows) permute_chunk_bulk_rows(c, 0, 1, T, H, k, pos_s, rows_s, &rows_bar, &rows_abort, x_perm);
   if (tid == 0) QMOE_TRACE_AT(0, 3);
 }
 

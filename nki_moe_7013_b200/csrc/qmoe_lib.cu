@@ -355,17 +355,20 @@ int launch_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chunk_
 }
 
 // Router + scan + scatter in one launch (nchunks <= SMs, T > kRouterSmallMaxT):
-// route_permute_kernel.  barrier: one int32 of scratch, cleared here first.
+// route_permute_kernel.  barrier: two int32 of scratch; zero on entry (every
+// completed launch leaves them zero), or cleared here first with `clear`.
 int launch_route_permute(const void* x, const void* w, const float* bias, int64_t T, int64_t H, int64_t E,
                          int64_t k, int normalize, int32_t* topk_idx, float* topk_w, int32_t* chunk_hist,
                          int32_t* counts, int32_t* offsets, int32_t* row_token, float* row_w, int32_t* slot_row,
                          int32_t* tiles, int64_t max_tiles, void* x_perm, float* acc_zero, int32_t* zero_words,
-                         int n_zero_words, int* barrier, cudaStream_t stream) {
+                         int n_zero_words, int* barrier, cudaStream_t stream, bool clear) {
   const int G = int(H / 256);
   const int nchunks = int((T + qmoe::kRouterChunk - 1) / qmoe::kRouterChunk);
   if (nchunks <= 0) return QMOE_OK;
-  const cudaError_t err = cudaMemsetAsync(barrier, 0, sizeof(int), stream);
-  if (err != cudaSuccess) return set_error(QMOE_ERR_CUDA, "route_permute barrier: %s", cudaGetErrorString(err));
+  if (clear) {
+    const cudaError_t err = cudaMemsetAsync(barrier, 0, 2 * sizeof(int), stream);
+    if (err != cudaSuccess) return set_error(QMOE_ERR_CUDA, "route_permute barrier: %s", cudaGetErrorString(err));
+  }
   const auto* xb = static_cast<const __nv_bfloat16*>(x);
   const auto* wb = static_cast<const __nv_bfloat16*>(w);
   auto* xp = static_cast<__nv_bfloat16*>(x_perm);
@@ -622,7 +625,7 @@ FwdLayout fwd_layout(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I) {
   L.acc = take(sizeof(float) * size_t(T * H));
   L.split = take(T * k <= kGateUpSplitMaxR ? qmoe::kSplitWorkspaceBytes : 0);
   L.done = take(T > kGatherMaxT ? sizeof(int32_t) * size_t(qmoe_max_tiles(R, E) + 2) : 0);
-  L.route_barrier = take(T > kRouterSmallMaxT ? sizeof(int32_t) : 0);
+  L.route_barrier = take(T > kRouterSmallMaxT ? 2 * sizeof(int32_t) : 0);
   L.total = o;
   return L;
 }
@@ -670,7 +673,7 @@ int moe_forward_on(const void* x, const void* w_router, const float* router_bias
     // fused kernel's tile counters
     QMOE_CHECK(launch_route_permute(x, w_router, router_bias, T, H, E, k, normalize, idx, tw, chunk_hist, counts,
                                     offsets, row_token, row_w, slot_row, tiles, max_tiles, x_perm, acc, done,
-                                    int(max_tiles + 2), reinterpret_cast<int*>(ws + L.route_barrier), s));
+                                    int(max_tiles + 2), reinterpret_cast<int*>(ws + L.route_barrier), s, true));
   } else {
     QMOE_CHECK(launch_router(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw,
                              chunk_hist, s));
@@ -819,7 +822,7 @@ int qmoe_route_permute(const void* x, const void* w_router, const float* bias, i
   if (T > kRouterSmallMaxT && nchunks <= num_sms(0))
     return launch_route_permute(x, w_router, bias, T, H, E, k, normalize, topk_idx, topk_w, chunk_hist, counts,
                                 offsets, row_token, row_w, slot_row, tiles, qmoe_max_tiles(T * k, E), x_perm,
-                                acc_zero, zero_words, int(n_zero_words), barrier, s);
+                                acc_zero, zero_words, int(n_zero_words), barrier, s, false);
   QMOE_CHECK(launch_router(x, w_router, bias, T, H, E, k, normalize, nullptr, topk_idx, topk_w, chunk_hist, s));
   return launch_permute(topk_idx, topk_w, chunk_hist, x, T, H, E, k, counts, offsets, row_token, row_w, slot_row,
                         tiles, x_perm, acc_zero, s, zero_words, int(n_zero_words));

@@ -196,7 +196,8 @@ class PeerExpertParallelMoE(nn.Module):
         self.row_w = torch.empty(max(R, 1), **f32)
         self.slot_row = torch.empty((max_tokens, k), **i32)
         self.perm_tiles = torch.empty(1 + 3 * ops.max_tiles(R, E), **i32)
-        self.logits = torch.empty((max_tokens, E), **f32)
+        self.route_barrier = torch.zeros(2, **i32)  # left zero by every completed route
+        self._sms = torch.cuda.get_device_properties(dev).multi_processor_count
         torch.cuda.synchronize(dev)
         self._imported = []
         names = ("recv_x", "recv_meta", "ret", "ctrl")
@@ -239,7 +240,15 @@ class PeerExpertParallelMoE(nn.Module):
             _C.check(self._lib.qmoe_ipc_close(base), "qmoe_ipc_close")
         self._imported = []
 
-    STAGES = ("router", "permute", "exchange", "dispatch", "experts", "return_wait", "unpack")
+    STAGES = ("route", "exchange", "dispatch", "experts", "return_wait", "unpack")
+
+    def launches_per_step(self, T: int) -> int:
+        """Kernels one step launches: route (router + permutation: one launch
+        up to one router chunk per SM and T > 64, else router + scan +
+        scatter), count exchange, dispatch, signal, experts, signal, unpack."""
+        nchunks = (T + ops.ROUTER_CHUNK - 1) // ops.ROUTER_CHUNK
+        one = T > ops.ROUTER_SMALL_MAX_T and nchunks <= self._sms
+        return (1 if one else 3) + 6
 
     def _issue(self, x: torch.Tensor, residual: Optional[torch.Tensor], out: torch.Tensor, par: int,
                events=None) -> None:
@@ -257,28 +266,25 @@ class PeerExpertParallelMoE(nn.Module):
         H, E, k, I = self.H, self.E, self.k, self.I
         lib, pt = self._lib, ops._ptr
         s = torch.cuda.current_stream(self.device).cuda_stream
-        logits = self.logits if T <= ops.ROUTER_SMALL_MAX_T else None
-        _C.check(lib.qmoe_router_topk(pt(x), pt(self.router_weight), pt(self.router_bias), T, H, E, k, 1,
-                                      pt(logits), pt(self.topk_idx), pt(self.topk_w), pt(self.hist), s),
-                 "qmoe_router_topk")
+        # router + permutation of the local tokens (one launch at prefill sizes)
+        _C.check(lib.qmoe_route_permute(pt(x), pt(self.router_weight), pt(self.router_bias), T, H, E, k, 1,
+                                        pt(self.topk_idx), pt(self.topk_w), pt(self.hist), pt(self.counts),
+                                        pt(self.offsets), pt(self.row_token), pt(self.row_w), pt(self.slot_row),
+                                        pt(self.perm_tiles), None, None, None, 0, pt(self.route_barrier), s),
+                 "qmoe_route_permute")
         mark(1)
-        _C.check(lib.qmoe_moe_permute(pt(self.topk_idx), pt(self.topk_w), pt(self.hist), None, T, H, E, k,
-                                      pt(self.counts), pt(self.offsets), pt(self.row_token), pt(self.row_w),
-                                      pt(self.slot_row), pt(self.perm_tiles), None, None, None, 0, s),
-                 "qmoe_moe_permute")
-        mark(2)
         _C.check(lib.qmoe_ep_exchange_counts(
             pt(self.counts), pt(self.peer["ctrl"]), pt(self.ctrl), self.rank, self.world, E, self.e_local,
             par, 0, pt(self.dest_base), pt(self.tiles), self.max_tiles, pt(self.recv_rows), self.cap,
             pt(self.done), self.max_tiles + 2, s), "qmoe_ep_exchange_counts")
-        mark(3)
+        mark(2)
         _C.check(lib.qmoe_ep_dispatch(
             pt(x), pt(self.topk_idx), pt(self.topk_w), pt(self.slot_row), pt(self.offsets), pt(self.dest_base),
             pt(self.peer["recv_x"]), pt(self.peer["recv_meta"]), T, k, H, self.e_local, self.rank, par,
             self.cap, s), "qmoe_ep_dispatch")
         _C.check(lib.qmoe_ep_signal_wait(pt(self.peer["ctrl"]), pt(self.ctrl), self.world, E, self.rank, par, 1,
                                          0, s), "qmoe_ep_signal_wait")
-        mark(4)
+        mark(3)
         recv_x = self.recv_x[par * self.cap:(par + 1) * self.cap]
         # gate/up + down in one persistent kernel; its down epilogue stores
         # each weighted row into the source rank's return buffer
@@ -286,14 +292,14 @@ class PeerExpertParallelMoE(nn.Module):
             pt(recv_x), pt(self.local.gate_up), pt(self.local.down), pt(self.tiles), self.max_tiles,
             pt(self.recv_meta[par * self.cap:]), pt(self.peer["ret"]), par * self.ret_rows, self.ret_rows,
             self.world, self.cap, H, I, self.e_local, pt(self.act), pt(self.done), s), "qmoe_moe_experts_return")
-        mark(5)
+        mark(4)
         _C.check(lib.qmoe_ep_signal_wait(pt(self.peer["ctrl"]), pt(self.ctrl), self.world, E, self.rank, par, 2,
                                          0, s), "qmoe_ep_signal_wait")
-        mark(6)
+        mark(5)
         y_back = self.ret[par * self.ret_rows:par * self.ret_rows + T * k]
         _C.check(lib.qmoe_ep_unpack(pt(y_back), None, pt(residual), T, H, k, T * k, pt(out), s),
                  "qmoe_ep_unpack")
-        mark(7)
+        mark(6)
 
     def forward(self, hidden_states: torch.Tensor, residual: Optional[torch.Tensor] = None,
                 events=None) -> torch.Tensor:

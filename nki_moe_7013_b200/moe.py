@@ -268,7 +268,7 @@ class MoEPlan:
         sms = torch.cuda.get_device_properties(dev).multi_processor_count
         self.route_permute = (self.fused and self.x_perm is not None and T > ops.ROUTER_SMALL_MAX_T
                               and nchunks <= sms)
-        self.route_barrier = torch.zeros(1, **i32) if self.route_permute else None
+        self.route_barrier = torch.zeros(2, **i32) if self.route_permute else None
         self.stages = (self.STAGES_ROUTED if self.route_permute else
                        self.STAGES_FUSED if self.fused else self.STAGES)
         self.ws_bytes = int(_C.lib().qmoe_moe_forward_workspace_size(T, H, E, k, I))

@@ -169,7 +169,7 @@ def route_permute(x: torch.Tensor, w_router: torch.Tensor, k: int, normalize: bo
                row_w=torch.empty(R, dtype=torch.float32, device=dev), slot_row=torch.empty((T, k), **i32),
                tiles=torch.empty(1 + 3 * mt, **i32), max_tiles=mt, done=torch.empty(mt + 1, **i32),
                x_perm=torch.empty((R, H), dtype=torch.bfloat16, device=dev) if gather else None)
-    barrier = torch.empty(1, **i32)
+    barrier = torch.zeros(2, **i32)
     if acc_zero is not None:
         _need(acc_zero, "acc_zero", torch.float32, 2)
     if bias is not None:
@@ -181,6 +181,7 @@ def route_permute(x: torch.Tensor, w_router: torch.Tensor, k: int, normalize: bo
             _ptr(out["row_token"]), _ptr(out["row_w"]), _ptr(out["slot_row"]), _ptr(out["tiles"]),
             _ptr(out["x_perm"]), _ptr(acc_zero), _ptr(out["done"]), mt + 1, _ptr(barrier), _stream(dev)),
             "qmoe_route_permute")
+    out["barrier"] = barrier
     return out
 
 

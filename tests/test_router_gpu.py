@@ -119,6 +119,7 @@ def test_route_permute_matches_router_and_permute(cuda_dev, oracle, T, H, E, k):
     acc = torch.full((T, H), 3.0, dtype=torch.float32, device=cuda_dev)
     r = ops.route_permute(x, wr, k, acc_zero=acc)
     r2 = ops.route_permute(x, wr, k)  # a second call on fresh (uninitialised) outputs
+    r3 = ops.route_permute(x, wr, k, gather=False)  # no permuted copy (the expert-parallel step)
     idx, w, hist = ops.router_topk(x, wr, k, return_hist=True)
     p = ops.moe_permute(idx, w, hist, E, x=x, gather=True)
     torch.cuda.synchronize()
@@ -127,6 +128,8 @@ def test_route_permute_matches_router_and_permute(cuda_dev, oracle, T, H, E, k):
     for key in ("counts", "offsets", "row_token", "row_w", "slot_row", "x_perm"):
         assert torch.equal(r[key], p[key]), key
         assert torch.equal(r2[key], p[key]), key
+        if key != "x_perm":
+            assert torch.equal(r3[key], p[key]), key
     nt = int(p["tiles"][0])
     mt = p["max_tiles"]
     assert int(r["tiles"][0]) == nt
@@ -134,5 +137,6 @@ def test_route_permute_matches_router_and_permute(cuda_dev, oracle, T, H, E, k):
         assert torch.equal(r["tiles"][1 + part * mt:1 + part * mt + nt], p["tiles"][1 + part * mt:1 + part * mt + nt])
     assert torch.count_nonzero(acc).item() == 0
     assert torch.count_nonzero(r2["done"]).item() == 0
+    assert torch.count_nonzero(r["barrier"]).item() == 0  # left zero for the next call
     ref = oracle.permute(idx.cpu().numpy(), E)
     np.testing.assert_array_equal(r["row_token"].cpu().numpy(), ref["row_token"])
