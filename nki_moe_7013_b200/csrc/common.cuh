@@ -369,6 +369,11 @@ __device__ __forceinline__ void bulk_commit_group() {
 __device__ __forceinline__ void bulk_wait_read_le1() {
   asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
 }
+// Wait until every committed bulk group has finished reading shared memory
+// (the global writes complete on their own; a dependent grid sees them).
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
 __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }

@@ -26,10 +26,9 @@
 //                  grid-wide barrier (all CTAs are resident), then sums the
 //                  published histograms into the counts and its own chunk
 //                  prefix and does its chunk's scatter.  Same outputs, bit
-//                  for bit, as router_topk + scan + scatter.  Its row copy
-//                  goes through the TMA engine: the chunk's token rows are
-//                  bulk-loaded into shared memory while the CTA routes, and
-//                  every (token, slot) row is one bulk store into x_perm.
+//                  for bit, as router_topk + scan + scatter.  The chunk's
+//                  token rows are bulk-loaded into shared memory while the
+//                  CTA routes; each permuted row is one bulk store.
 #pragma once
 
 #include "common.cuh"
@@ -198,8 +197,11 @@ __device__ __forceinline__ void permute_chunk_zero_acc(int c, int part, int npar
 
 // The chunk's (token, slot) rows of this CTA's share into x_perm with one
 // bulk store each, from the token rows (rows_s, bf16, loaded on rows_bar);
-// every thread that issued waits for its store.  Thread 0 also waits for the
-// row loads when it issues nothing, so no load outlives the CTA.
+// every thread that issued waits until its store has read shared memory (the
+// writes complete on their own; the next grid sees them).  Thread 0 also
+// waits for the row loads when it issues nothing, so no load outlives the
+// CTA.  (The copy is bound by the aggregate write rate, ~5.6 TB/s for the
+// 1,024-token layer's 33.5 MB: 16-byte stores from every thread were slower.)
 __device__ __forceinline__ void permute_chunk_bulk_rows(int c, int part, int nparts, int T, int H, int k,
                                                         const int* pos_s, const __nv_bfloat16* rows_s,
                                                         uint64_t* rows_bar, int* rows_abort,
@@ -213,7 +215,7 @@ __device__ __forceinline__ void permute_chunk_bulk_rows(int c, int part, int npa
     if (rows_in && pos >= 0) {
       bulk_store(x_perm + size_t(pos) * H, rows_s + (tid / k) * H, H * 2);
       bulk_commit_group();
-      bulk_wait_all();
+      bulk_wait_read_all();
     }
   }
 }
@@ -351,23 +353,35 @@ __global__ void __launch_bounds__(router_warps<G>() * 32, 1)
     const int col4 = tid % E4;
     const int rg = tid / E4;
     int4 tot = make_int4(0, 0, 0, 0), pre = tot;
-    for (int r = rg; r < int(gridDim.x); r += n_rg) {
-      const int4 h = __ldcg(reinterpret_cast<const int4*>(chunk_hist + size_t(r) * E) + col4);
-      tot.x += h.x;
-      tot.y += h.y;
-      tot.z += h.z;
-      tot.w += h.w;
-      if (r < c) {
-        pre.x += h.x;
-        pre.y += h.y;
-        pre.z += h.z;
-        pre.w += h.w;
+    // eight rows' loads in flight at a time
+    for (int r0 = rg; r0 < int(gridDim.x); r0 += 8 * n_rg) {
+      int4 h[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int r = r0 + u * n_rg;
+        h[u] = r < int(gridDim.x) ? __ldcg(reinterpret_cast<const int4*>(chunk_hist + size_t(r) * E) + col4)
+                                  : make_int4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int r = r0 + u * n_rg;
+        tot.x += h[u].x;
+        tot.y += h[u].y;
+        tot.z += h[u].z;
+        tot.w += h[u].w;
+        if (r < c) {
+          pre.x += h[u].x;
+          pre.y += h[u].y;
+          pre.z += h[u].z;
+          pre.w += h[u].w;
+        }
       }
     }
     reinterpret_cast<int4*>(part_tot + rg * E)[col4] = tot;
     reinterpret_cast<int4*>(part_pre + rg * E)[col4] = pre;
   }
   __syncthreads();
+  if (tid == 0) QMOE_TRACE_AT(0, 4);
   int cnt = 0;
   if (tid < E) {
     int p = 0;
@@ -379,12 +393,15 @@ __global__ void __launch_bounds__(router_warps<G>() * 32, 1)
   }
   const bool lead = c == 0;
   permute_offsets(cnt, E, lead, off_s, warp_sums, counts, offsets, tiles, max_tiles);
+  if (tid == 0) QMOE_TRACE_AT(0, 5);
   if (lead)
     for (int i = tid; i < n_zero_words; i += kThreads) zero_words[i] = 0;
   permute_chunk_rows(
       c, T, E, k, topk_idx, topk_w, off_s, [&](int e) { return pre_s[e]; }, true, row_token, row_w, slot_row, mask,
       pos_s);
+  if (tid == 0) QMOE_TRACE_AT(0, 6);
   permute_chunk_zero_acc(c, 0, 1, T, H, acc_zero);
+  if (tid == 0) QMOE_TRACE_AT(0, 7);
   if (copy_rows) permute_chunk_bulk_rows(c, 0, 1, T, H, k, pos_s, rows_s, &rows_bar, &rows_abort, x_perm);
   if (tid == 0) QMOE_TRACE_AT(0, 3);
 }
