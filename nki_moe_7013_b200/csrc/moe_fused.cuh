@@ -32,7 +32,10 @@
 //
 // The producer claims the unit after the one it is loading as soon as it has
 // claimed that one, so the counter's round trip overlaps a unit's loads
-// instead of draining the ring between units.  (Deadlock-free as above: a CTA
+// instead of draining the ring between units.  A CTA's first unit is its
+// blockIdx.x (no atomic before the first loads); the counter hands out units
+// from gridDim.x on.  (Every CTA is resident, so units are still taken in
+// order by running CTAs.)  (Deadlock-free as above: a CTA
 // holding an unstarted unit is working on an earlier-drawn one, and only down
 // units wait -- on gate/up units, all of which were drawn before them.)
 //
@@ -256,9 +259,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           ok = false;
           break;
         }
-        int u = next_u == -2 ? atomicAdd(counter, 1) : next_u;
+        int u = next_u == -2 ? int(blockIdx.x) : next_u;
         if (!ok || u >= total_units) u = -1;
-        next_u = u >= 0 ? atomicAdd(counter, 1) : -1;
+        next_u = u >= 0 ? int(gridDim.x) + atomicAdd(counter, 1) : -1;
         unit_q[q] = u;
         mbar_arrive(&uq_full[q]);
         if (u < 0) break;
@@ -341,9 +344,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                kDevErrWaitTimeoutProducer)) {
           got = 0;
         } else {
-          u = next_u == -2 ? atomicAdd(counter, 1) : next_u;
+          u = next_u == -2 ? int(blockIdx.x) : next_u;
           if (!ok || u >= total_units) u = -1;
-          next_u = u >= 0 ? atomicAdd(counter, 1) : -1;
+          next_u = u >= 0 ? int(gridDim.x) + atomicAdd(counter, 1) : -1;
           unit_q[q] = u;
           mbar_arrive(&uq_full[q]);
         }
