@@ -155,20 +155,52 @@ struct TileView {
   }
 };
 
-// Gate/up split count for this launch: as many splits (<= max_k_splits) as
-// fit the grid once, only when every tile has at most 16 rows.
-__device__ __forceinline__ int gateup_k_splits(const GemmArgs& a, int ntiles, int max_rows) {
-  if (a.split_ws == nullptr || a.max_k_splits < 2 || ntiles <= 0 || max_rows > kBoxRows) return 1;
-  const int units = ntiles * a.n_mtiles;
-  const int s = min(min(a.max_k_splits, a.num_kb), min(int(gridDim.x), kSplitSlots) / units);
-  return s < 2 ? 1 : s;
+// Work items of a launch.  Units (tile x feature block) fill whole grid
+// waves unsplit (n_full of them); each unit of the last, partial wave is
+// split over `split` CTAs along K, so the last wave keeps every SM busy
+// instead of a few (decode: 312 gate/up units on 148 SMs ran 3 units deep,
+// now 2 + 4 quarter units).  Item u (CTA u % grid, wave u / grid) is unit
+// tm, split ks of nsplit.
+struct WorkPlan {
+  int n_full;  // unsplit units
+  int split;   // splits of each remaining unit
+  int total;   // work items
+  __device__ __forceinline__ void item(int u, int& tm, int& ks, int& nsplit) const {
+    if (u < n_full) {
+      tm = u;
+      ks = 0;
+      nsplit = 1;
+    } else {
+      const int j = u - n_full;
+      tm = n_full + j / split;
+      ks = j - (j / split) * split;
+      nsplit = split;
+    }
+  }
+};
+
+// Gate/up and plain launches: split the last partial wave's units over up to
+// max_k_splits CTAs each (only when every tile has at most 16 rows and a
+// scratch is given: the fixed-order fix-up needs one slot per split).
+__device__ __forceinline__ WorkPlan gateup_work_plan(const GemmArgs& a, int ntiles, int max_rows) {
+  const int units = max(0, ntiles) * a.n_mtiles;
+  WorkPlan p{units, 1, units};
+  if (a.split_ws == nullptr || a.max_k_splits < 2 || units <= 0 || max_rows > kBoxRows) return p;
+  const int grid = int(gridDim.x);
+  const int n_full = (units / grid) * grid;
+  const int tail = units - n_full;
+  if (tail == 0) return p;
+  const int s = min(min(a.max_k_splits, a.num_kb), min(grid, kSplitSlots) / tail);
+  if (s < 2) return p;
+  return WorkPlan{n_full, s, n_full + tail * s};
 }
 
-// Split-K fix-up, run by the 128 epilogue threads of one unit (tm, ks) after
-// loading this split's partials into g (and u for gate/up: kTwo) -- feature
-// m, 16 rows.  Stores them into slot (tm, ks), counts the arrival, and
-// returns true in the CTA that arrived last, with g / u replaced by the sums
-// over the splits in split order.
+// Split-K fix-up, run by the 128 epilogue threads of one split unit (tm, ks)
+// after loading this split's partials into g (and u for gate/up: kTwo) --
+// feature m, 16 rows.  tm: the unit's index among the split units.  Stores
+// them into slot (tm, ks), counts the arrival, and returns true in the CTA
+// that arrived last, with g / u replaced by the sums over the splits in
+// split order.
 template <bool kTwo = true>
 __device__ __forceinline__ bool gateup_split_reduce(const GemmArgs& a, int tm, int ks, int nsplit, int m, int et,
                                                     float (&g)[16], float (&u)[16], volatile int* last_s) {
@@ -344,14 +376,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (threadIdx.x == 0) record_device_error(kDevErrBadIndex);
     ntiles = 0;  // refuse the launch rather than overrun a stage
   }
-  int ksplit = 1;
+  WorkPlan plan{ntiles * args.n_mtiles, 1, ntiles * args.n_mtiles};
   if constexpr (kMode == kModeDown) {
-    // as many splits (<= k_splits) as the grid runs at once
+    // as many splits (<= k_splits) of every unit as the grid runs at once
+    // (the splits' partials meet in the fp32 accumulator)
     const int units = max(1, ntiles * args.n_mtiles);
-    ksplit = max(1, min(min(args.k_splits, args.num_kb), int(gridDim.x) / units));
+    const int ksplit = max(1, min(min(args.k_splits, args.num_kb), int(gridDim.x) / units));
+    plan = WorkPlan{0, ksplit, ntiles * args.n_mtiles * ksplit};
   }
-  if constexpr (kGateUp || kMode == kModePlain) ksplit = gateup_k_splits(args, ntiles, max_rows);
-  const int total_units = ntiles * args.n_mtiles * ksplit;
+  if constexpr (kGateUp || kMode == kModePlain) plan = gateup_work_plan(args, ntiles, max_rows);
+  const int total_units = plan.total;
 
   if (warp == 0) {
     // ---------------- TMA producer (warp 0) ----------------
@@ -369,8 +403,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0)
       for (int s = 0; s < n_pre; ++s) issued_mask |= 1u << s;  // pre-issued: phase 0
     for (int u = blockIdx.x; ok && u < total_units; u += gridDim.x) {
-      const int tm = u / ksplit;
-      const int ks = u - tm * ksplit;
+      int tm, ks, nsplit;
+      plan.item(u, tm, ks, nsplit);
       const int tile = tm / args.n_mtiles;
       const int mt = tm - tile * args.n_mtiles;
       const int e = tv.expert(tile);
@@ -390,8 +424,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       const uint32_t bytes = C::kATiles * C::kABytes +
                              (gather ? n_g4 * 4 * kBK * 2 : nb * kBoxRows * kBK * 2);
-      const int kb_end = (ks + 1) * args.num_kb / ksplit;
-      for (int kb = ks * args.num_kb / ksplit; kb < kb_end; ++kb) {
+      const int kb_end = (ks + 1) * args.num_kb / nsplit;
+      for (int kb = ks * args.num_kb / nsplit; kb < kb_end; ++kb) {
         uint8_t* sb = stages + stage * C::kStageBytes;
         uint8_t* bs = sb + C::kATiles * C::kABytes;
         if (!gather) {
@@ -460,9 +494,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int local = 0;
       bool ok = true;
       for (int u = blockIdx.x; ok && u < total_units; u += gridDim.x, ++local) {
-        const int tile = (u / ksplit) / args.n_mtiles;
-        const int ks = u % ksplit;
-        const int n_kb = (ks + 1) * args.num_kb / ksplit - ks * args.num_kb / ksplit;
+        int tm, ks, nsplit;
+        plan.item(u, tm, ks, nsplit);
+        const int tile = tm / args.n_mtiles;
+        const int n_kb = (ks + 1) * args.num_kb / nsplit - ks * args.num_kb / nsplit;
         const int nb = (tv.nrows(tile) + kBoxRows - 1) / kBoxRows;
         const uint32_t idesc = make_idesc_bf16(kBM, nb * kBoxRows);
         const int buf = local & 1;
@@ -522,7 +557,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int32_t* meta_src = meta_dst + 256;
     int local = 0;
     for (int u = blockIdx.x; u < total_units; u += gridDim.x, ++local) {
-      const int tm = u / ksplit;
+      int tm, ks, nsplit;
+      plan.item(u, tm, ks, nsplit);
+      const int su = tm - plan.n_full;  // split unit (slots, arrival counter)
       const int tile = tm / args.n_mtiles;
       const int mt = tm - tile * args.n_mtiles;
       const int row0 = tv.first_row(tile);
@@ -575,8 +612,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int i = 0; i < 16; ++i) g[i] = __uint_as_float(v[i]);
           // split K (one 16-row chunk per unit): only the last split stores
-          if (ksplit > 1 && !gateup_split_reduce<false>(args, tm, u - tm * ksplit, ksplit, m, et, g, unused,
-                                                         &split_last))
+          if (nsplit > 1 && !gateup_split_reduce<false>(args, su, ks, nsplit, m, et, g, unused, &split_last))
             break;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
@@ -594,7 +630,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             uv[i] = __uint_as_float(up[i]);
           }
           // split K (one 16-row chunk per unit): only the last split finishes
-          if (ksplit > 1 && !gateup_split_reduce(args, tm, u - tm * ksplit, ksplit, m, et, g, uv, &split_last))
+          if (nsplit > 1 && !gateup_split_reduce(args, su, ks, nsplit, m, et, g, uv, &split_last))
             break;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
