@@ -195,6 +195,12 @@ constexpr int64_t kGatherMaxT = 64;
 // keeps the gather form (qmoe_moe_experts with gather_rows) for callers
 // without a copy.
 constexpr int64_t kFusedGatherMaxT = kGatherMaxT;
+// Above kFusedMinT tokens the forward runs the experts as the persistent
+// fused kernel (dynamic units, per-tile dependencies, no split-K; decode
+// sizes gather the token rows): measured on B200 it beats the split-K gate/up
+// and down kernels from 3 tokens up (-10 % at 4, 8 and 16 tokens) and ties at
+// 2; at 1 token (48 gate/up units) the splits keep more SMs streaming.
+constexpr int64_t kFusedMinT = 2;
 // Routed rows up to which the gate/up GEMM may split K (given a scratch), and
 // the most splits.  Splits pay when the units leave SMs idle: at one token
 // (8 rows) 48 units of a 148-SM B200 become 144.
@@ -624,7 +630,7 @@ FwdLayout fwd_layout(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I) {
   L.act = take(2 * size_t(R * I));
   L.acc = take(sizeof(float) * size_t(T * H));
   L.split = take(T * k <= kGateUpSplitMaxR ? qmoe::kSplitWorkspaceBytes : 0);
-  L.done = take(T > kGatherMaxT ? sizeof(int32_t) * size_t(qmoe_max_tiles(R, E) + 2) : 0);
+  L.done = take(T > kFusedMinT ? sizeof(int32_t) * size_t(qmoe_max_tiles(R, E) + 2) : 0);
   L.route_barrier = take(T > kRouterSmallMaxT ? 2 * sizeof(int32_t) : 0);
   L.total = o;
   return L;
@@ -645,7 +651,7 @@ int moe_forward_on(const void* x, const void* w_router, const float* router_bias
   int32_t* tiles = reinterpret_cast<int32_t*>(ws + L.tiles);
   int32_t* idx = topk_idx ? topk_idx : reinterpret_cast<int32_t*>(ws + L.topk_idx);
   float* tw = topk_w ? topk_w : reinterpret_cast<float*>(ws + L.topk_w);
-  const bool fused = T > kGatherMaxT;
+  const bool fused = T > kFusedMinT;
   void* x_perm = T > kFusedGatherMaxT ? ws + L.x_perm : nullptr;
   void* act = ws + L.act;
   float* acc = reinterpret_cast<float*>(ws + L.acc);
@@ -665,8 +671,9 @@ int moe_forward_on(const void* x, const void* w_router, const float* router_bias
     // decode sizes: router + permutation in one launch, which also zeroes
     // the gate/up split counters (the workspace may hold anything on entry)
     QMOE_CHECK(launch_route_small(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw, counts,
-                                  offsets, row_token, row_w, slot_row, tiles, max_tiles, acc, s, split_counters,
-                                  split_counters ? qmoe::kSplitCounterWords : 0));
+                                  offsets, row_token, row_w, slot_row, tiles, max_tiles, acc, s,
+                                  fused ? done : split_counters,
+                                  fused ? int(max_tiles + 2) : split_counters ? qmoe::kSplitCounterWords : 0));
   } else if (fused && nchunks <= num_sms(0)) {
     // prefill batches of at most one router chunk per SM: router, scan and
     // scatter in one launch (one grid-wide barrier), which also zeroes the

@@ -174,7 +174,7 @@ def _run_routed(x: torch.Tensor, w: MoEWeights, idx: torch.Tensor, tw: torch.Ten
     E = w.num_experts
     hist = ops.routing_histogram(idx, E)
     acc = torch.empty((T, H), dtype=torch.float32, device=x.device)
-    if T > ops.GATHER_MAX_T:
+    if T > ops.FUSED_MIN_T:
         copy = T > ops.FUSED_GATHER_MAX_T
         p = ops.moe_permute(idx, tw, hist, E, x=x, gather=copy, acc_zero=acc)
         if copy:
@@ -217,9 +217,9 @@ class MoEPlan:
     runs the same kernels through the per-stage entry points instead and
     records the CUDA events (len(self.stages) + 1) before the first kernel and
     after each stage, on the current stream.  Stages: router, permute (scan +
-    scatter), gate_up, down, finalize; prefill sizes run gate/up and down as
-    one kernel ("experts").  The fused forward folds the finalize into the
-    last kernel."""
+    scatter), gate_up, down, finalize; batches of more than ops.FUSED_MIN_T
+    tokens run gate/up and down as one kernel ("experts").  The fused forward
+    folds the finalize into the last kernel."""
 
     STAGES = ("router", "permute", "gate_up", "down", "finalize")
     STAGES_FUSED = ("router", "permute", "experts", "finalize")
@@ -257,7 +257,7 @@ class MoEPlan:
         # prefill sizes: gate/up and down run as one persistent kernel, whose
         # per-tile counters the permutation zero-fills; its gate/up rows come
         # from a permuted copy or (prefill_gather) straight from the tokens
-        self.fused = T > ops.GATHER_MAX_T if fused is None else (bool(fused) and T > ops.GATHER_MAX_T)
+        self.fused = T > ops.FUSED_MIN_T if fused is None else (bool(fused) and T > ops.FUSED_MIN_T)
         if prefill_gather is None:
             prefill_gather = T <= ops.FUSED_GATHER_MAX_T
         self.x_perm = (torch.empty((max(R, 1), H), dtype=torch.bfloat16, device=dev)
@@ -309,6 +309,8 @@ class MoEPlan:
                                           p(self.logits), p(self.topk_idx), p(self.topk_w), p(self.counts),
                                           p(self.offsets), p(self.row_token), p(self.row_w), p(self.slot_row),
                                           p(self.tiles), p(self.acc), s), "route_small")
+            if self.fused:
+                self.done.zero_()  # the library forward has the route kernel zero them
             mark()
             mark()
         elif self.route_permute:
@@ -372,7 +374,7 @@ class MoEPlan:
         T <= 64: logits + selection) + scan + scatter, then gate/up, down,
         finalize."""
         if self.route_small:
-            return 3  # route, gate/up, down (+ finalize folded in)
+            return 2 if self.fused else 3  # route, experts / gate/up + down (+ finalize folded in)
         if self.route_permute:
             return 2  # route + permutation, experts (+ finalize folded in)
         if self.fused:

@@ -17,6 +17,7 @@ ROUTER_CHUNK = 8  # QMOE_ROUTER_CHUNK
 ROUTER_SMALL_MAX_T = 64  # batches up to this size take the two-kernel small-batch router
 GATHER_MAX_T = 64  # batches up to this size gather token rows inside the gate/up GEMM
 FUSED_GATHER_MAX_T = GATHER_MAX_T  # the fused experts kernel reads the permuted copy (faster from 256 tokens)
+FUSED_MIN_T = 2  # above this many tokens the forward runs the experts as the fused persistent kernel
 GATEUP_SPLIT_MAX_R = 128  # routed rows up to which the gate/up GEMM may split K
 ROUTE_SMALL_MAX_T = 16  # batches up to this size (E <= 128) route + permute in one launch
 ROUTE_SMALL_MAX_E = 128
