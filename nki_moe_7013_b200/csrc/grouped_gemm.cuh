@@ -55,7 +55,11 @@ constexpr int kGemmTilesReady = 1;
 // the grid-barrier counter of the fused decode finalisation)
 constexpr int kSplitSlots = 256;
 constexpr int kSplitSlotFloats = 2 * kBoxRows * kBM;
-constexpr int kSplitCounterWords = kSplitSlots + 4;
+// Per-tile unit counters of the decode forward (the down GEMM starts a tile
+// once its gate/up units are done), after the arrival counters and spares.
+constexpr int kSplitTileDoneWords = 260;
+constexpr int kSplitTileDoneOffset = kSplitSlots + 4;
+constexpr int kSplitCounterWords = kSplitTileDoneOffset + kSplitTileDoneWords;
 constexpr size_t kSplitWorkspaceBytes = size_t(kSplitSlots) * kSplitSlotFloats * 4 + kSplitCounterWords * 4;
 
 // Epilogue modes of the one GEMM kernel.
@@ -109,6 +113,13 @@ struct GemmArgs {
   float* split_ws;
   int max_k_splits;
   int flags;             // kGemmTilesReady
+  // gate/up: when non-null, each finished unit (after its activation rows are
+  // written; the last split of a split unit) adds 1 to tile_done[tile].
+  // down: when non-null, a tile's activation rows are loaded once
+  // tile_done[tile] reaches tile_done_target (bounded wait) -- instead of
+  // waiting for the whole previous grid, which runs concurrently.
+  int* tile_done;
+  int tile_done_target;
   // down: when fin_out is set, after one grid-wide barrier on *grid_bar (zero
   // before the launch) every CTA finalises a slice of the combine --
   // fin_out = bf16(acc + fin_residual), the finalize kernel folded in
@@ -154,6 +165,23 @@ struct TileView {
     return exp ? (t < kTileCache ? cache[t].z : rows[t]) : min(kBNMax, dense_rows - t * kBNMax);
   }
 };
+
+// Bounded wait for a tile's activations; false (and a device error) on time-out.
+__device__ __forceinline__ bool wait_tile_done(const int* done, int target, volatile int* abort_flag) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (ld_acquire_gpu(done) < target) {
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      record_device_error(kDevErrWaitTimeoutProducer);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  // the activation rows were written through the generic proxy by other SMs;
+  // order them before this thread's TMA (async proxy) loads
+  asm volatile("fence.proxy.async;" ::: "memory");
+  return true;
+}
 
 // Work items of a launch.  Units (tile x feature block) fill whole grid
 // waves unsplit (n_full of them); each unit of the last, partial wave is
@@ -338,7 +366,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       n_pre = down_pre_issue<C>(args, &tmA, stages, full, lane);
   }
   // everything above overlapped the previous kernel; its outputs are read below
-  griddep_wait();
+  // (a down GEMM with per-tile counters waits per tile in its producer instead)
+  if (!(kMode == kModeDown && args.tile_done != nullptr)) griddep_wait();
   griddep_launch_dependents();
   if constexpr (kTid >= 0) if (threadIdx.x == 0) QMOE_TRACE_AT(kTid, 1);
 
@@ -424,6 +453,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       const uint32_t bytes = C::kATiles * C::kABytes +
                              (gather ? n_g4 * 4 * kBK * 2 : nb * kBoxRows * kBK * 2);
+      if constexpr (kMode == kModeDown) {
+        if (args.tile_done != nullptr && lane == 0 &&
+            !wait_tile_done(args.tile_done + tile, args.tile_done_target, abort_flag)) {
+          ok = false;
+          break;
+        }
+      }
       const int kb_end = (ks + 1) * args.num_kb / nsplit;
       for (int kb = ks * args.num_kb / nsplit; kb < kb_end; ++kb) {
         uint8_t* sb = stages + stage * C::kStageBytes;
@@ -683,6 +719,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
+      if constexpr (kGateUp) {
+        if (args.tile_done != nullptr && (nsplit == 1 || split_last)) {
+          // publish the unit's activation rows to the down GEMM's producer
+          asm volatile("fence.proxy.async;" ::: "memory");
+          __threadfence();
+          named_barrier_sync(1, 128);
+          if (et == 0) atomicAdd(args.tile_done + tile, 1);
+        }
+      }
     }
   }
 

@@ -108,22 +108,6 @@ struct FusedArgs {
   const int32_t* gather_rows;
 };
 
-// Bounded wait for a tile's activations; false (and a device error) on time-out.
-__device__ __forceinline__ bool wait_tile_done(const int* done, int target, volatile int* abort_flag) {
-  const unsigned long long t0 = globaltimer_ns();
-  while (ld_acquire_gpu(done) < target) {
-    if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
-      record_device_error(kDevErrWaitTimeoutProducer);
-      return false;
-    }
-    __nanosleep(64);
-  }
-  // the activation rows were written through the generic proxy by other SMs;
-  // order them before this thread's TMA (async proxy) loads
-  asm volatile("fence.proxy.async;" ::: "memory");
-  return true;
-}
 
 // One unit's shape, derived identically by the producer, MMA and epilogue
 // warps.  rows == 0: a tile outside its limits -- the unit is skipped by all

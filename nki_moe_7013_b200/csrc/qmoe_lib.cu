@@ -418,7 +418,8 @@ constexpr int64_t kSmallTileRows = qmoe::kBoxRows;
 // max_tile_rows: an upper bound on the rows of any tile.
 int launch_gemm_gateup(const void* x, int64_t x_rows, const int32_t* gather_rows, const void* w_gate_up,
                        const int32_t* tiles, int64_t max_tiles, int64_t R, int64_t H, int64_t I, int64_t E,
-                       void* act, void* split_ws, cudaStream_t stream, int64_t max_tile_rows = qmoe::kBNMax) {
+                       void* act, void* split_ws, cudaStream_t stream, int64_t max_tile_rows = qmoe::kBNMax,
+                       int32_t* tile_done = nullptr) {
   CUtensorMap tmA, tmB;
   QMOE_CHECK(make_tmap_bf16(&tmA, w_gate_up, uint64_t(H), uint64_t(E * 2 * I), qmoe::kBK, qmoe::kBM));
   if (gather_rows)
@@ -439,6 +440,7 @@ int launch_gemm_gateup(const void* x, int64_t x_rows, const int32_t* gather_rows
   // decode sizes: let the kernel split K when its units leave SMs idle
   a.split_ws = R <= kGateUpSplitMaxR ? static_cast<float*>(split_ws) : nullptr;
   a.max_k_splits = a.split_ws ? kGateUpMaxSplits : 1;
+  a.tile_done = tile_done;
   const int64_t units = max_tiles * a.n_mtiles * a.max_k_splits;
   const int grid = int(std::min<int64_t>(units, num_sms(0)));
   if (grid <= 0) return QMOE_OK;
@@ -451,7 +453,7 @@ int launch_gemm_down(const void* act, const void* w_down, const int32_t* tiles, 
                      const int32_t* row_dst, const float* row_w, int64_t R, int64_t H, int64_t I,
                      int64_t E, float* acc, int64_t n_acc, cudaStream_t stream,
                      int64_t max_tile_rows = qmoe::kBNMax, int flags = 0, const void* fin_residual = nullptr,
-                     void* fin_out = nullptr, int32_t* grid_bar = nullptr) {
+                     void* fin_out = nullptr, int32_t* grid_bar = nullptr, int32_t* tile_done = nullptr) {
   CUtensorMap tmA, tmB;
   QMOE_CHECK(make_tmap_bf16(&tmA, w_down, uint64_t(I), uint64_t(E * H), qmoe::kBK, qmoe::kBM));
   QMOE_CHECK(make_tmap_bf16(&tmB, act, uint64_t(I), uint64_t(R), qmoe::kBK, qmoe::kBoxRows));
@@ -476,6 +478,9 @@ int launch_gemm_down(const void* act, const void* w_down, const int32_t* tiles, 
   a.fin_residual = static_cast<const __nv_bfloat16*>(fin_residual);
   a.fin_out = static_cast<__nv_bfloat16*>(fin_out);
   a.grid_bar = grid_bar;
+  // per-tile counters of the gate/up GEMM (its I / 128 units per tile)
+  a.tile_done = tile_done;
+  a.tile_done_target = int(I / qmoe::kBM);
   const int64_t units = max_tiles * a.n_mtiles * a.k_splits;
   const int grid = int(std::min<int64_t>(units, num_sms(0)));
   if (grid <= 0) return QMOE_OK;
@@ -700,13 +705,19 @@ int moe_forward_on(const void* x, const void* w_router, const float* router_bias
     return launch_moe_fused(x, T, row_token, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, act,
                             acc, T, done, s, residual, out);
   }
+  // with the split scratch (decode sizes) the gate/up GEMM counts finished
+  // units per tile there, so the down GEMM starts each tile as soon as its
+  // activations are written rather than after the whole gate/up grid
+  int32_t* tile_done = split_counters && max_tiles <= qmoe::kSplitTileDoneWords
+                           ? split_counters + qmoe::kSplitTileDoneOffset
+                           : nullptr;
   QMOE_CHECK(launch_gemm_gateup(x, T, row_token, w_gate_up, tiles, max_tiles, R, H, I, E, act, split_ws, s,
-                                tile_rows));
+                                tile_rows, tile_done));
   // the tile list comes from the routing kernels, before the gate/up GEMM;
   // with the split scratch (decode sizes) the down GEMM finalises too
   if (split_counters)
     return launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s, tile_rows,
-                            qmoe::kGemmTilesReady, residual, out, split_counters + qmoe::kSplitSlots);
+                            qmoe::kGemmTilesReady, residual, out, split_counters + qmoe::kSplitSlots, tile_done);
   QMOE_CHECK(launch_gemm_down(act, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, acc, T, s, tile_rows,
                               qmoe::kGemmTilesReady));
   return launch_finalize(acc, residual, T, H, out, s);
