@@ -46,6 +46,22 @@ class Qwen3MoeModel:
         self.norm = (1.0 + 0.1 * torch.randn(H, generator=g, device=self.device)).float().contiguous()
         self.lm_head = normal_bf16_device(seed * 1000 + 2, (V, H), std, self.device)
 
+    @classmethod
+    def from_parts(cls, cfg: Qwen3MoeConfig, embed: torch.Tensor, layers: List[Qwen3MoeDecoderLayer],
+                   norm: torch.Tensor, lm_head: torch.Tensor) -> "Qwen3MoeModel":
+        """A model from given weights (e.g. a checkpoint: checkpoint.load_model):
+        embed (V, H) bf16, the decoder layers, final norm (H,) fp32, LM head
+        (V, H) bf16 -- no random initialisation."""
+        m = cls.__new__(cls)
+        m.cfg = cfg
+        m.device = embed.device
+        m.vocab_size = embed.shape[0]
+        m.embed = embed
+        m.layers = list(layers)
+        m.norm = norm
+        m.lm_head = lm_head
+        return m
+
     def new_caches(self, n_slots: int, max_seq: int) -> List[KVCache]:
         return [layer.self_attn.new_cache(n_slots, max_seq) for layer in self.layers]
 
