@@ -470,7 +470,9 @@ def run_extras(cfg, weights, dev, hbm_gbs, tf_burst):
     res = {}
     dec = {}
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 2x L2
-    for B in (1, 8, 32, 64):
+    # 5 and 40 tokens: speculative-decoding verify steps (1 and 8 sequences x
+    # 5 tokens), between decode and prefill
+    for B in (1, 5, 8, 32, 40, 64):
         plan = MoEPlan(weights, B, K_TOP)
         x = normal_bf16_device(77 + B, (B, H), 1.0, dev)
         out = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
@@ -510,6 +512,8 @@ def run_extras(cfg, weights, dev, hbm_gbs, tf_burst):
         dec[str(B)] = {"us_per_layer": round(us, 2), "tokens_per_s": B / (us * 1e-6),
                        "experts_hit": U, "hbm_frac": byts / (us * 1e-6) / 1e9 / hbm_gbs,
                        "stage_us_eager": dict(zip(plan.stages, [round(v, 1) for v in stage]))}
+        if B in (5, 40):
+            dec[str(B)]["shape"] = f"spec-verify step: {B // 5} sequence(s) x 5 tokens"
         del g
     del flush
     res["decode_moe_layer_cuda_graph"] = dec

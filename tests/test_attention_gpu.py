@@ -89,7 +89,9 @@ def _attn_weights(cuda_dev, H, nh, nkv, seed):
     return wqkv, wo, qn, kn
 
 
-@pytest.mark.parametrize("B,S,L0", [(1, 1024, 0), (2, 200, 0), (2, 70, 37), (3, 1, 100)])
+# (2, 5, 4096) / (4, 5, 300): speculative-decoding verify shapes -- 5 new
+# tokens per sequence on top of a filled cache
+@pytest.mark.parametrize("B,S,L0", [(1, 1024, 0), (2, 200, 0), (2, 70, 37), (3, 1, 100), (2, 5, 4096), (4, 5, 300)])
 def test_attention_layer_vs_oracle(cuda_dev, oracle, B, S, L0):
     """Projection -> QK-norm/RoPE/cache append -> prefill or decode -> o_proj,
     continuing a cache that already holds L0 tokens per sequence."""
