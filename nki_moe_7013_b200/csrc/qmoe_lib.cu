@@ -636,7 +636,9 @@ FwdLayout fwd_layout(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I) {
   L.acc = take(sizeof(float) * size_t(T * H));
   L.split = take(T * k <= kGateUpSplitMaxR ? qmoe::kSplitWorkspaceBytes : 0);
   L.done = take(T > kFusedMinT ? sizeof(int32_t) * size_t(qmoe_max_tiles(R, E) + 2) : 0);
-  L.route_barrier = take(T > kRouterSmallMaxT ? 2 * sizeof(int32_t) : 0);
+  // the one-launch route + permutation (and its two barrier words) serves
+  // every fused batch that the decode route kernel does not
+  L.route_barrier = take(T > kFusedMinT ? 2 * sizeof(int32_t) : 0);
   L.total = o;
   return L;
 }

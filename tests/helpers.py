@@ -39,3 +39,19 @@ def activations(seed: int, T: int, H: int, device):
     if str(device).startswith("cuda"):
         return normal_bf16_device(seed * 10 + 4, (T, H), 1.0, device)
     return normal_bf16(seed, "x", (T, H), 1.0)
+
+
+def assert_within_one_ulp(actual: torch.Tensor, expected: torch.Tensor, what: str = "") -> None:
+    """bf16 results of the same arithmetic whose fp32 sums were added in a
+    different order: every element within one bf16 ulp of the other (2^-7 of
+    its magnitude), nothing more.  A missed, doubled or overwritten
+    contribution is far larger."""
+    a = actual.float()
+    e = expected.float()
+    tol = e.abs() * 2.0 ** -7 + 1e-6
+    bad = (a - e).abs() > tol
+    n = int(bad.sum())
+    if n:
+        i = torch.nonzero(bad)[0].tolist()
+        raise AssertionError(f"{what}: {n} elements differ by more than one bf16 ulp, first at {i}: "
+                             f"{float(a[tuple(i)])} vs {float(e[tuple(i)])}")

@@ -302,3 +302,54 @@ def test_moe_forward_zipf_skew(cuda_dev, oracle):
     assert counts.max() > 4 * counts.mean()  # the skew is real: several 128-row tiles per hot expert
     err = max_rel_err(to_f32_np(out), oracle.round_to_bf16(ref_out))
     assert err <= MAX_REL
+
+
+@pytest.mark.parametrize("T,H,E,k,I", [(1, 2048, 128, 8, 768), (2, 2048, 128, 8, 768), (3, 2048, 128, 8, 768),
+                                       (16, 2048, 128, 8, 768), (17, 2048, 128, 8, 768), (24, 2048, 128, 8, 768),
+                                       (64, 2048, 128, 8, 768), (65, 2048, 128, 8, 768), (300, 2048, 128, 8, 768),
+                                       (1200, 2048, 128, 8, 768), (5, 1024, 256, 8, 256), (40, 1024, 256, 8, 256)])
+def test_forward_stays_inside_its_workspace(cuda_dev, T, H, E, k, I):
+    """qmoe_moe_forward writes nothing past the workspace size it reports, on
+    every routing path (decode route kernel, one-launch route + permutation,
+    separate router and permutation kernels): a guard of pattern bytes after
+    the workspace stays untouched.  (The one-launch route's two barrier words
+    once sat outside the layout for 17-64 tokens and zeroed the 8 bytes after
+    the workspace.)"""
+    from nki_moe_7013_b200 import _C, ops
+
+    guard = 1 << 16
+    wr, wgu, wd = moe_weights(95 + T, E, H, I, cuda_dev)
+    x = activations(95 + T, T, H, cuda_dev)
+    res = activations(96 + T, T, H, cuda_dev)
+    nb = ops.moe_forward_workspace_size(T, H, E, k, I)
+    ws = torch.full((nb + guard,), 0x5A, dtype=torch.uint8, device=cuda_dev)
+    out = ops.moe_forward(x, wr, wgu, wd, k, residual=res, workspace=ws)
+    torch.cuda.synchronize()
+    assert _C.device_error() == 0
+    assert int((ws[nb:] != 0x5A).sum()) == 0, "moe_forward wrote past its workspace"
+    assert torch.isfinite(out.float()).all()
+
+
+@pytest.mark.parametrize("T", [1, 2, 3, 17, 24, 40, 100, 300])
+def test_moe_forward_repeatable_on_dirty_workspace(cuda_dev, T):
+    """Repeated forwards on workspaces pre-filled with NaN, huge and zero
+    bytes, routing kept in the workspace: every output within one bf16 ulp of
+    the first (the combine adds in arrival order) and of a call that returns
+    its routing.  Catches reads of unwritten scratch and cross-CTA ordering
+    faults."""
+    from helpers import assert_within_one_ulp
+    from nki_moe_7013_b200 import _C, ops
+
+    H, E, k, I = 2048, 128, 8, 768
+    wr, wgu, wd = moe_weights(90 + T, E, H, I, cuda_dev)
+    x = activations(90 + T, T, H, cuda_dev)
+    res = activations(91 + T, T, H, cuda_dev)
+    ref, _, _ = ops.moe_forward(x, wr, wgu, wd, k, residual=res, return_routing=True)
+    nb = ops.moe_forward_workspace_size(T, H, E, k, I)
+    for i, fill in enumerate([0xFF, 0x7F, 0x00, 0x3F] * 3):
+        ws = torch.full((nb,), fill, dtype=torch.uint8, device=cuda_dev)
+        out = ops.moe_forward(x, wr, wgu, wd, k, residual=res, workspace=ws)
+        torch.cuda.synchronize()
+        assert not torch.isnan(out).any()
+        assert_within_one_ulp(out, ref, f"T={T} run {i}")
+    assert _C.device_error() == 0

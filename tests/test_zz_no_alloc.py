@@ -45,7 +45,7 @@ def _forward_noalloc(lib, x, wr, wgu, wd, res, stream):
     return out, idx, tw
 
 
-@pytest.mark.parametrize("T", [1, 64, 150])
+@pytest.mark.parametrize("T", [1, 24, 64, 150])
 def test_noalloc_matches_workspace_forward_twice(cuda_dev, T):
     from nki_moe_7013_b200 import _C
 
