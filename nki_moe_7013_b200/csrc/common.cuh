@@ -180,6 +180,22 @@ __device__ __forceinline__ void tma_gather4_hint(void* smem_dst, const CUtensorM
       : "memory");
 }
 
+// Release / acquire-release adds at GPU scope.  A thread that publishes a
+// flag for the stores of its whole CTA (or warp group) issues one of these
+// after the CTA-level barrier that follows those stores: the barrier orders
+// the other threads' stores before this thread's release, so a reader that
+// acquires the flag sees them.
+__device__ __forceinline__ int atom_add_release_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.release.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   int v;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -196,7 +212,7 @@ __device__ __forceinline__ bool grid_barrier_once(int* counter, unsigned int cod
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
-    atomicAdd(counter, 1);
+    atom_add_release_gpu(counter, 1);
     int good = 1;
     const unsigned long long t0 = globaltimer_ns();
     while (ld_acquire_gpu(counter) < int(gridDim.x)) {

@@ -243,7 +243,7 @@ __device__ __forceinline__ bool gateup_split_reduce(const GemmArgs& a, int tm, i
   __threadfence();
   named_barrier_sync(1, 128);
   if (et == 0) {
-    const int last = atomicAdd(arrivals + tm, 1) == nsplit - 1;
+    const int last = atom_add_acq_rel_gpu(arrivals + tm, 1) == nsplit - 1;
     if (last) arrivals[tm] = 0;  // every split has arrived: ready for the next launch
     *last_s = last;
   }
@@ -725,7 +725,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           asm volatile("fence.proxy.async;" ::: "memory");
           __threadfence();
           named_barrier_sync(1, 128);
-          if (et == 0) atomicAdd(args.tile_done + tile, 1);
+          if (et == 0) atom_add_release_gpu(args.tile_done + tile, 1);
         }
       }
     }

@@ -605,7 +605,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         asm volatile("fence.proxy.async;" ::: "memory");
         __threadfence();
         named_barrier_sync(1, 128);
-        if (et == 0) atomicAdd(args.done + tile, 1);
+        if (et == 0) atom_add_release_gpu(args.done + tile, 1);
       }
     }
     if (threadIdx.x == 64) QMOE_TRACE_AT(1, 6);
