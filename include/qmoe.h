@@ -292,6 +292,35 @@ QMOE_API int qmoe_moe_forward(const void* x, const void* w_router, const float* 
                      size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Fused MoE block: the decoder layer's post-attention add & norm, the MoE
+ * and the residual add in one call -- replaces qwen.py:423-430 (residual
+ * add, post_attention_layernorm, self.mlp, residual add) and the reference's
+ * fused RMSNorm + router + MoE kernels (qwen_with_nki.py:2184-2374,
+ * 8518-8711; the router reads the post-norm tensor, qwen_with_nki.py:8583-8588):
+ *
+ *   s   = bf16(x + residual)                              -> residual_out
+ *   h   = bf16(s * rsqrt(mean(s^2) + eps) * norm_weight)  -> moe_in_out
+ *   out = bf16(s + MoE(h))
+ *
+ *   x, residual (T, H) bf16; norm_weight (H) fp32; out (T, H) bf16
+ *   moe_in_out / residual_out (T, H) bf16 outputs may be NULL (then they live
+ *   in the workspace); topk_idx / topk_w as in qmoe_moe_forward
+ *   workspace of qmoe_moe_block_forward_workspace_size() bytes, 256-byte aligned
+ *
+ * s and h equal qmoe_rmsnorm's outputs bit for bit and out equals
+ * qmoe_moe_forward(h, ..., residual = s).  At decode sizes (T <= 16,
+ * E <= 128) the add & norm runs inside the routing kernel: one launch fewer
+ * than qmoe_rmsnorm + qmoe_moe_forward.
+ * ---------------------------------------------------------------------- */
+QMOE_API size_t qmoe_moe_block_forward_workspace_size(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I);
+QMOE_API int qmoe_moe_block_forward(const void* x, const void* residual, const float* norm_weight, float eps,
+                                    const void* w_router, const float* router_bias, const void* w_gate_up,
+                                    const void* w_down, int64_t T, int64_t H, int64_t E, int64_t k, int64_t I,
+                                    int normalize, void* out, void* moe_in_out, void* residual_out,
+                                    int32_t* topk_idx, float* topk_w, void* workspace,
+                                    size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
  * Dense projection out (T, N) bf16 = x (T, K) . w (N, K)^T, the nn.Linear
  * convention, on the same TMA + tcgen05 pipeline as the expert GEMMs (one
  * "expert", dense row tiles).  Replaces the QKV and o_proj projections of

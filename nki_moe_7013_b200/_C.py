@@ -42,6 +42,9 @@ _SIGNATURES = {
     "qmoe_embedding_gather": (I32, [P, I64, I64, P, I64, P, P]),
     "qmoe_moe_forward_workspace_size": (SZ, [I64, I64, I64, I64, I64]),
     "qmoe_moe_forward": (I32, [P, P, P, P, P, P, I64, I64, I64, I64, I64, I32, P, P, P, P, SZ, P]),
+    "qmoe_moe_block_forward_workspace_size": (SZ, [I64, I64, I64, I64, I64]),
+    "qmoe_moe_block_forward": (I32, [P, P, P, ctypes.c_float, P, P, P, P, I64, I64, I64, I64, I64, I32, P, P, P,
+                                     P, P, P, SZ, P]),
     "qmoe_linear": (I32, [P, P, I64, I64, I64, P, P, SZ, P]),
     "qmoe_rmsnorm": (I32, [P, I32, P, P, I64, I64, ctypes.c_float, P, I32, P, P]),
     "qmoe_qk_norm_rope": (I32, [P, P, P, P, P, P, I64, I64, I64, I64, ctypes.c_float, P, P, P, I64,

@@ -84,6 +84,18 @@ __device__ __forceinline__ float bf16hi_to_f32(uint32_t packed) {
   return __uint_as_float(packed & 0xFFFF0000u);
 }
 
+// One step of an RMSNorm sum of squares: ss + (((a*a + b*b) + c*c) + d*d)
+// with the rounding fixed (one multiply, three fused multiply-adds, one add),
+// so every kernel that normalises a row in the same lane layout gets the
+// same bits whatever the compiler would contract.
+__device__ __forceinline__ float sumsq4(float ss, float a, float b, float c, float d) {
+  float q = __fmul_rn(a, a);
+  q = __fmaf_rn(b, b, q);
+  q = __fmaf_rn(c, c, q);
+  q = __fmaf_rn(d, d, q);
+  return __fadd_rn(ss, q);
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -102,6 +114,10 @@ __device__ __forceinline__ void fence_mbarrier_init() {
 
 __device__ __forceinline__ void fence_proxy_async_shared() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {

@@ -79,7 +79,7 @@ __global__ void __launch_bounds__(kNormThreads)
   }
   float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < kChunks; ++i) ss += v[i][0] * v[i][0] + v[i][1] * v[i][1] + v[i][2] * v[i][2] + v[i][3] * v[i][3];
+  for (int i = 0; i < kChunks; ++i) ss = sumsq4(ss, v[i][0], v[i][1], v[i][2], v[i][3]);
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, off);
   const float r = rsqrtf(ss / float(H) + eps);
@@ -88,7 +88,8 @@ __global__ void __launch_bounds__(kNormThreads)
     const int c = i * 128 + lane * 4;
     if (c >= H) continue;
     const float4 wv = *reinterpret_cast<const float4*>(w + c);
-    const float o0 = v[i][0] * r * wv.x, o1 = v[i][1] * r * wv.y, o2 = v[i][2] * r * wv.z, o3 = v[i][3] * r * wv.w;
+    const float o0 = __fmul_rn(__fmul_rn(v[i][0], r), wv.x), o1 = __fmul_rn(__fmul_rn(v[i][1], r), wv.y),
+                o2 = __fmul_rn(__fmul_rn(v[i][2], r), wv.z), o3 = __fmul_rn(__fmul_rn(v[i][3], r), wv.w);
     if constexpr (sizeof(Tout) == 4) {
       *reinterpret_cast<float4*>(y + size_t(row) * H + c) = make_float4(o0, o1, o2, o3);
     } else {

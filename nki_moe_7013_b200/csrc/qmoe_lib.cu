@@ -279,7 +279,8 @@ int launch_route_small(const void* x, const void* w, const float* bias, int64_t 
                        int64_t k, int normalize, float* logits, int32_t* topk_idx, float* topk_w,
                        int32_t* counts, int32_t* offsets, int32_t* row_token, float* row_w, int32_t* slot_row,
                        int32_t* tiles, int64_t max_tiles, float* acc_zero, cudaStream_t stream,
-                       int32_t* zero_words = nullptr, int n_zero_words = 0) {
+                       int32_t* zero_words = nullptr, int n_zero_words = 0,
+                       const qmoe::RouteNorm& nrm = qmoe::RouteNorm{}) {
   const int G = int(H / 256);
   const int smem = int(route_small_smem(T, H, E, k));
   cudaLaunchConfig_t cfg = {};
@@ -304,7 +305,7 @@ int launch_route_small(const void* x, const void* w, const float* bias, int64_t 
     QMOE_CHECK(set_smem(qmoe::route_small_kernel<GG>, smem));                                            \
     err = cudaLaunchKernelEx(&cfg, qmoe::route_small_kernel<GG>, xb, wb, bias, int(T), int(E), int(k),   \
                              normalize, logits, topk_idx, topk_w, counts, offsets, row_token, row_w,     \
-                             slot_row, tiles, int(max_tiles), acc_zero, zero_words, n_zero_words);       \
+                             slot_row, tiles, int(max_tiles), acc_zero, zero_words, n_zero_words, nrm);  \
     break;
   switch (G) {
     QMOE_ROUTE_SMALL_CASE(1)
@@ -606,12 +607,14 @@ int launch_finalize(const float* acc, const void* residual, int64_t T, int64_t H
 // Workspace carving for the fused forward.
 struct FwdLayout {
   size_t logits, chunk_hist, counts, offsets, row_token, row_w, slot_row, tiles, topk_idx, topk_w, x_perm,
-      act, acc, split, done, route_barrier, total;
+      act, acc, split, done, route_barrier, norm_h, norm_res, total;
 };
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-FwdLayout fwd_layout(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I) {
+// with_norm: room for the add & norm outputs (qmoe_moe_block_forward callers
+// that do not take them).
+FwdLayout fwd_layout(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I, bool with_norm = false) {
   FwdLayout L{};
   const int64_t R = T * k;
   const int64_t nchunks = (T + qmoe::kRouterChunk - 1) / qmoe::kRouterChunk;
@@ -639,16 +642,50 @@ FwdLayout fwd_layout(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I) {
   // the one-launch route + permutation (and its two barrier words) serves
   // every fused batch that the decode route kernel does not
   L.route_barrier = take(T > kFusedMinT ? 2 * sizeof(int32_t) : 0);
+  L.norm_h = take(with_norm ? 2 * size_t(T * H) : 0);
+  L.norm_res = take(with_norm ? 2 * size_t(T * H) : 0);
   L.total = o;
   return L;
 }
 
+// The decoder layer's add & norm in front of the MoE block (qwen.py:423,
+// 428): s = bf16(a + res) -> res_out, h = bf16(rmsnorm(s) * w) -> h_out; the
+// MoE block reads h and its output adds s.
+struct AddNorm {
+  const void* a;
+  const void* res;
+  const float* w;
+  float eps;
+  void* h_out;
+  void* res_out;
+};
+
 // The MoE forward on a workspace laid out by fwd_layout (shapes checked by
-// the caller): routing, permutation, experts and the combine.
+// the caller): routing, permutation, experts and the combine.  With `an`, x
+// and residual are ignored: the add & norm runs first (inside the decode
+// route kernel when that kernel routes the batch) and the block reads its
+// outputs.
 int moe_forward_on(const void* x, const void* w_router, const float* router_bias, const void* w_gate_up,
                    const void* w_down, const void* residual, int64_t T, int64_t H, int64_t E, int64_t k, int64_t I,
                    int normalize, void* out, int32_t* topk_idx, float* topk_w, uint8_t* ws, const FwdLayout& L,
-                   cudaStream_t s) {
+                   cudaStream_t s, const AddNorm* an = nullptr) {
+  const bool small_route = T <= qmoe::kRouteSmallMaxT && E <= qmoe::kRouteSmallMaxE;
+  qmoe::RouteNorm rn{};
+  if (an) {
+    using bf16 = __nv_bfloat16;
+    x = an->h_out;
+    residual = an->res_out;
+    if (small_route) {
+      rn = qmoe::RouteNorm{static_cast<const bf16*>(an->a), static_cast<const bf16*>(an->res), an->w, an->eps,
+                           static_cast<bf16*>(an->h_out), static_cast<bf16*>(an->res_out)};
+    } else {
+      const int st = launch_rmsnorm<bf16, bf16>(int((H + 127) / 128), int((T + 7) / 8), s,
+                                                static_cast<const bf16*>(an->a), static_cast<const bf16*>(an->res),
+                                                an->w, int(T), int(H), an->eps, static_cast<bf16*>(an->h_out),
+                                                static_cast<bf16*>(an->res_out));
+      if (st != QMOE_OK) return st;
+    }
+  }
   int32_t* chunk_hist = reinterpret_cast<int32_t*>(ws + L.chunk_hist);
   int32_t* counts = reinterpret_cast<int32_t*>(ws + L.counts);
   int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
@@ -674,13 +711,14 @@ int moe_forward_on(const void* x, const void* w_router, const float* router_bias
 
   float* logits = T <= kRouterSmallMaxT ? reinterpret_cast<float*>(ws + L.logits) : nullptr;
   const int64_t nchunks = (T + qmoe::kRouterChunk - 1) / qmoe::kRouterChunk;
-  if (T <= qmoe::kRouteSmallMaxT && E <= qmoe::kRouteSmallMaxE) {
-    // decode sizes: router + permutation in one launch, which also zeroes
-    // the gate/up split counters (the workspace may hold anything on entry)
+  if (small_route) {
+    // decode sizes: router + permutation (and the add & norm) in one launch,
+    // which also zeroes the gate/up split counters (the workspace may hold
+    // anything on entry)
     QMOE_CHECK(launch_route_small(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw, counts,
                                   offsets, row_token, row_w, slot_row, tiles, max_tiles, acc, s,
                                   fused ? done : split_counters,
-                                  fused ? int(max_tiles + 2) : split_counters ? qmoe::kSplitCounterWords : 0));
+                                  fused ? int(max_tiles + 2) : split_counters ? qmoe::kSplitCounterWords : 0, rn));
   } else if (fused && nchunks <= num_sms(0)) {
     // prefill batches of at most one router chunk per SM: router, scan and
     // scatter in one launch (one grid-wide barrier), which also zeroes the
@@ -1437,6 +1475,47 @@ int qmoe_moe_forward(const void* x, const void* w_router, const float* router_bi
   if (T == 0) return QMOE_OK;
   return moe_forward_on(x, w_router, router_bias, w_gate_up, w_down, residual, T, H, E, k, I, normalize, out,
                         topk_idx, topk_w, static_cast<uint8_t*>(workspace), L, static_cast<cudaStream_t>(stream));
+}
+
+size_t qmoe_moe_block_forward_workspace_size(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I) {
+  if (T < 0 || H <= 0 || E <= 0 || k <= 0 || I <= 0) return 0;
+  return fwd_layout(T, H, E, k, I, true).total;
+}
+
+int qmoe_moe_block_forward(const void* x, const void* residual, const float* norm_weight, float eps,
+                           const void* w_router, const float* router_bias, const void* w_gate_up,
+                           const void* w_down, int64_t T, int64_t H, int64_t E, int64_t k, int64_t I,
+                           int normalize, void* out, void* moe_in_out, void* residual_out, int32_t* topk_idx,
+                           float* topk_w, void* workspace, size_t workspace_bytes, void* stream) {
+  QMOE_REQUIRE(x && residual && norm_weight && w_router && w_gate_up && w_down && out, QMOE_ERR_INVALID_ARGUMENT,
+               "moe_block_forward: null pointer");
+  QMOE_REQUIRE(T >= 0 && T < (int64_t(1) << 31) / 32, QMOE_ERR_INVALID_ARGUMENT, "moe_block_forward: bad T");
+  QMOE_REQUIRE(H > 0 && H % 256 == 0 && H <= 4096, QMOE_ERR_UNSUPPORTED_SHAPE,
+               "moe_block_forward: H=%lld must be a multiple of 256 and <= 4096", (long long)H);
+  QMOE_REQUIRE(E >= 32 && E <= 256 && E % 32 == 0, QMOE_ERR_UNSUPPORTED_SHAPE,
+               "moe_block_forward: E=%lld must be a multiple of 32 in [32, 256]", (long long)E);
+  QMOE_REQUIRE(k >= 1 && k <= E && k <= 32, QMOE_ERR_INVALID_ARGUMENT, "moe_block_forward: k invalid");
+  QMOE_REQUIRE(I > 0 && I % qmoe::kBM == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "moe_block_forward: I %% 128 != 0");
+  QMOE_REQUIRE(E * 2 * I < (int64_t(1) << 31) && E * H < (int64_t(1) << 31), QMOE_ERR_UNSUPPORTED_SHAPE,
+               "moe_block_forward: weights too large");
+  QMOE_REQUIRE(aligned16(x) && aligned16(residual) && aligned16(norm_weight) && aligned16(w_router) &&
+                   aligned16(w_gate_up) && aligned16(w_down) && aligned16(out) &&
+                   (!moe_in_out || aligned16(moe_in_out)) && (!residual_out || aligned16(residual_out)),
+               QMOE_ERR_MISALIGNED, "moe_block_forward: pointers must be 16-byte aligned");
+  const FwdLayout L = fwd_layout(T, H, E, k, I, true);
+  QMOE_REQUIRE(workspace || L.total == 0, QMOE_ERR_INVALID_ARGUMENT, "moe_block_forward: null workspace");
+  QMOE_REQUIRE(workspace_bytes >= L.total, QMOE_ERR_WORKSPACE_TOO_SMALL,
+               "moe_block_forward: workspace %zu < required %zu bytes", workspace_bytes, L.total);
+  QMOE_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255u) == 0, QMOE_ERR_MISALIGNED,
+               "moe_block_forward: workspace must be 256-byte aligned");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  if (T == 0) return QMOE_OK;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const AddNorm an{x, residual, norm_weight, eps, moe_in_out ? moe_in_out : ws + L.norm_h,
+                   residual_out ? residual_out : ws + L.norm_res};
+  return moe_forward_on(nullptr, w_router, router_bias, w_gate_up, w_down, nullptr, T, H, E, k, I, normalize, out,
+                        topk_idx, topk_w, ws, L, static_cast<cudaStream_t>(stream), &an);
 }
 
 #ifdef QMOE_TRACE

@@ -12,8 +12,11 @@ like NeuronQwen3MoeDecoderLayer.forward (qwen.py:378-436):
     h = post_attention_layernorm(residual)       (qwen.py:428)
     out = residual + mlp(h, padding_mask)[0]     (qwen.py:429-430)
 
-Here the residual add before the second norm is fused into the RMSNorm
-kernel and the final residual add into the MoE output cast.  RoPE is applied
+Here the residual add before the second norm, the norm, the MoE block and
+the final residual add are one library call (``qmoe_moe_block_forward``; at
+decode sizes the add & norm runs inside the MoE's routing kernel).  With a
+``padding_mask`` the masked MoE output needs the norm's outputs first, so
+that path runs the add & norm and the MoE block as two calls.  RoPE is applied
 inside the attention kernels, so cos/sin caches are returned as None.
 ``attention_mask`` is accepted for signature compatibility; attention is
 causal over each sequence's cache.  ``capture_intermediates=True`` keeps the
@@ -58,12 +61,17 @@ class Qwen3MoeDecoderLayer(nn.Module):
         x2d = hidden_states.reshape(B * S, H).to(torch.bfloat16).contiguous()
         h = ops.rmsnorm(x2d, self.input_layernorm, eps)
         a, present = self.self_attn(h.reshape(B, S, H), position_ids, past_key_value)
-        h2, residual = ops.rmsnorm(a.reshape(B * S, H), self.post_attention_layernorm, eps, residual=x2d)
-        if kwargs.get("capture_intermediates"):
-            self.last = dict(attn=a.reshape(B * S, H), residual=residual, moe_in=h2)
+        a2d = a.reshape(B * S, H)
         if padding_mask is None:
-            out, _, _ = self.mlp._moe(h2, residual=residual)
+            capture = bool(kwargs.get("capture_intermediates"))
+            h2 = torch.empty_like(x2d) if capture else None
+            residual = torch.empty_like(x2d) if capture else None
+            out = self.mlp._block(a2d, x2d, self.post_attention_layernorm, eps, moe_in_out=h2,
+                                  residual_out=residual)
         else:
+            h2, residual = ops.rmsnorm(a2d, self.post_attention_layernorm, eps, residual=x2d)
             moe, _, _ = self.mlp._moe(h2)
             out = (residual.float() + moe.float() * padding_mask.reshape(-1, 1).float()).to(torch.bfloat16)
+        if kwargs.get("capture_intermediates"):
+            self.last = dict(attn=a2d, residual=residual, moe_in=h2)
         return (out.reshape(B, S, H), present, None, None, None)

@@ -11,7 +11,7 @@ path (host-side cache lengths, any number of new tokens).
 positions, cache lengths and the next tokens live on the device and advance
 on the device, so a whole step -- 48 layers of RMSNorm, QKV projection, QK
 norm + RoPE + cache append, split-KV decode attention, O projection, add &
-norm, the MoE block, then the final norm, the LM head and a greedy pick --
+norm fused into the MoE block, then the final norm, the LM head and a greedy pick --
 captures into one CUDA graph and replays without the host.
 """
 from __future__ import annotations
@@ -130,8 +130,9 @@ class DecodeSession:
                              cache_slot=self.slots)
         a = ops.attention_decode(q, cache.k, cache.v, self.kv_len, self.max_seq, workspace=self.attn_ws)
         o = ops.linear(a, attn.w.wo, split_ws=self.split_ws)
-        h2, residual = ops.rmsnorm(o, layer.post_attention_layernorm, eps, residual=x)
-        self.plans[l].run(h2, out, residual=residual)
+        # add & norm + MoE + residual add (decode sizes: the add & norm runs
+        # inside the routing kernel)
+        self.plans[l].run_block(o, x, layer.post_attention_layernorm, eps, out)
 
     def step(self) -> torch.Tensor:
         """One decode step on the current stream (or the captured graph)."""

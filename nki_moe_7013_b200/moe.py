@@ -108,6 +108,18 @@ class Qwen3MoeSparseMoeBlock(nn.Module):
                                normalize=self.normalize, residual=residual, bias=self.router_bias,
                                workspace=self._workspace, return_routing=True)
 
+    def _block(self, x2d: torch.Tensor, residual: torch.Tensor, norm_weight: torch.Tensor, eps: float,
+               moe_in_out: Optional[torch.Tensor] = None, residual_out: Optional[torch.Tensor] = None):
+        """add & norm + this block + residual add (ops.moe_block_forward)."""
+        T, H = x2d.shape
+        ws = ops.moe_block_forward_workspace_size(T, H, self.cfg.num_experts, self.top_k,
+                                                  self.cfg.moe_intermediate_size)
+        if self._workspace is None or self._workspace.numel() < ws or self._workspace.device != x2d.device:
+            self._workspace = torch.empty(max(ws, 1), dtype=torch.uint8, device=x2d.device)
+        return ops.moe_block_forward(x2d, residual, norm_weight, eps, self.router_weight, self.gate_up, self.down,
+                                     self.top_k, normalize=self.normalize, bias=self.router_bias,
+                                     workspace=self._workspace, moe_in_out=moe_in_out, residual_out=residual_out)
+
     def forward(self, hidden_states: torch.Tensor, padding_mask: Optional[torch.Tensor] = None):
         shape = hidden_states.shape
         x2d = hidden_states.reshape(-1, shape[-1]).to(torch.bfloat16).contiguous()
@@ -272,7 +284,8 @@ class MoEPlan:
         self.stages = (self.STAGES_ROUTED if self.route_permute else
                        self.STAGES_FUSED if self.fused else self.STAGES)
         self.ws_bytes = int(_C.lib().qmoe_moe_forward_workspace_size(T, H, E, k, I))
-        self.workspace = torch.empty(max(self.ws_bytes, 256), dtype=torch.uint8, device=dev)
+        self.block_ws_bytes = int(_C.lib().qmoe_moe_block_forward_workspace_size(T, H, E, k, I))
+        self.workspace = torch.empty(max(self.ws_bytes, self.block_ws_bytes, 256), dtype=torch.uint8, device=dev)
         # small batches route through the logits + selection kernels
         self.logits = torch.empty((T, E), **f32) if T <= ops.ROUTER_SMALL_MAX_T else None
         # a token's k experts are distinct: no tile holds more than T rows
@@ -360,6 +373,23 @@ class MoEPlan:
         mark()
         _C.check(lib.qmoe_combine_finalize(p(self.acc), p(residual), T, H, p(out), s), "finalize")
         mark()
+        return out
+
+    def run_block(self, x: torch.Tensor, residual: torch.Tensor, norm_weight: torch.Tensor, eps: float,
+                  out: torch.Tensor, moe_in_out: Optional[torch.Tensor] = None,
+                  residual_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """The decoder layer's post-attention add & norm, this block and the
+        residual add (one ``qmoe_moe_block_forward`` call): out = s + MoE(h)
+        with s = bf16(x + residual), h = rmsnorm(s) * norm_weight.  At decode
+        sizes the add & norm runs inside the routing kernel."""
+        lib, p = self._lib, ops._ptr
+        s = torch.cuda.current_stream(self.device).cuda_stream
+        w = self.w
+        _C.check(lib.qmoe_moe_block_forward(p(x), p(residual), p(norm_weight), float(eps), p(w.router), p(self.bias),
+                                            p(w.gate_up), p(w.down), self.T, self.H, self.E, self.k, self.I,
+                                            1 if self.normalize else 0, p(out), p(moe_in_out), p(residual_out),
+                                            p(self.topk_idx), p(self.topk_w), p(self.workspace),
+                                            self.workspace.numel(), s), "moe_block_forward")
         return out
 
     LAUNCHES_PER_RUN = 6  # router, scan, scatter, gate/up, down, finalize (T > 64)

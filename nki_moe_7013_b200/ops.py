@@ -382,6 +382,54 @@ def moe_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate_up: torch.Tensor
     return out
 
 
+def moe_block_forward_workspace_size(T: int, H: int, E: int, k: int, I: int) -> int:
+    return int(_C.lib().qmoe_moe_block_forward_workspace_size(T, H, E, k, I))
+
+
+def moe_block_forward(x: torch.Tensor, residual: torch.Tensor, norm_weight: torch.Tensor, eps: float,
+                      w_router: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor, k: int,
+                      normalize: bool = True, bias: Optional[torch.Tensor] = None,
+                      workspace: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                      moe_in_out: Optional[torch.Tensor] = None, residual_out: Optional[torch.Tensor] = None,
+                      return_routing: bool = False):
+    """The decoder layer's post-attention add & norm + MoE block + residual
+    add in one library call (qwen.py:423-430): s = bf16(x + residual),
+    h = rmsnorm(s) * norm_weight, out = bf16(s + MoE(h)).  ``moe_in_out`` /
+    ``residual_out`` receive h and s when given.  Returns out (T, H) bf16
+    [, topk_idx (T, k) int32, topk_w (T, k) fp32]."""
+    _need(x, "x", torch.bfloat16, 2)
+    _need(residual, "residual", torch.bfloat16, 2)
+    _need(norm_weight, "norm_weight", torch.float32, 1)
+    _need(w_router, "w_router", torch.bfloat16, 2)
+    _need(w_gate_up, "w_gate_up", torch.bfloat16, 3)
+    _need(w_down, "w_down", torch.bfloat16, 3)
+    for name, t in (("moe_in_out", moe_in_out), ("residual_out", residual_out)):
+        if t is not None:
+            _need(t, name, torch.bfloat16, 2)
+    if bias is not None:
+        _need(bias, "bias", torch.float32, 1)
+    T, H = x.shape
+    if tuple(residual.shape) != (T, H) or norm_weight.numel() != H:
+        raise ValueError("residual must match x and norm_weight must have H elements")
+    E = w_router.shape[0]
+    I = w_down.shape[2]
+    dev = x.device
+    ws_bytes = moe_block_forward_workspace_size(T, H, E, k, I)
+    if workspace is None or workspace.numel() < ws_bytes:
+        workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    out = out if out is not None else torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    idx = torch.empty((T, k), dtype=torch.int32, device=dev) if return_routing else None
+    tw = torch.empty((T, k), dtype=torch.float32, device=dev) if return_routing else None
+    with torch.cuda.device(dev):
+        _C.check(_C.lib().qmoe_moe_block_forward(
+            _ptr(x), _ptr(residual), _ptr(norm_weight), float(eps), _ptr(w_router), _ptr(bias), _ptr(w_gate_up),
+            _ptr(w_down), T, H, E, k, I, 1 if normalize else 0, _ptr(out), _ptr(moe_in_out), _ptr(residual_out),
+            _ptr(idx), _ptr(tw), _ptr(workspace), workspace.numel(), _stream(dev)), "qmoe_moe_block_forward")
+    if return_routing:
+        return out, idx, tw
+    return out
+
+
 # ----------------------------------------------------------------------------
 # attention sub-layer
 # ----------------------------------------------------------------------------

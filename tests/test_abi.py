@@ -62,3 +62,28 @@ def test_workspace_size_query(lib):
     assert big >= 1024 * 8 * 2048 * 2 + 1024 * 8 * 768 * 2 + 1024 * 2048 * 4
     assert lib.qmoe_moe_forward_workspace_size(64, 2048, 128, 8, 768) < 64 * 8 * 2048 * 2
     assert lib.qmoe_max_tiles(8192, 128) == 128 + 64 + 1
+    # the fused block adds room for the add & norm outputs (2 x T*H bf16)
+    for T in (1, 16, 1024):
+        plain = lib.qmoe_moe_forward_workspace_size(T, 2048, 128, 8, 768)
+        block = lib.qmoe_moe_block_forward_workspace_size(T, 2048, 128, 8, 768)
+        assert block >= plain + 2 * 2 * T * 2048
+
+
+def test_block_forward_validation_needs_no_gpu(lib):
+    buf = ctypes.create_string_buffer(64)
+    p = ctypes.addressof(buf)
+    f = ctypes.c_float(1e-6)
+
+    def call(x, res, w, H, I, ws_bytes, h_out=None):
+        return lib.qmoe_moe_block_forward(x, res, w, f, p, None, p, p, 4, H, 128, 8, I, 1, p, h_out, None, None,
+                                          None, p, ws_bytes, None)
+    # no residual / no norm weight
+    assert call(p, None, p, 2048, 768, 1 << 30) == -1 and b"null" in lib.qmoe_last_error()
+    assert call(p, p, None, 2048, 768, 1 << 30) == -1
+    # unsupported hidden size; I not a multiple of 128
+    assert call(p, p, p, 300, 768, 1 << 30) == -2
+    assert call(p, p, p, 2048, 100, 1 << 30) == -2
+    # a workspace smaller than the query says
+    assert call(p, p, p, 2048, 768, 64) == -4
+    # misaligned optional output
+    assert call(p, p, p, 2048, 768, 1 << 30, h_out=p + 4) == -3
