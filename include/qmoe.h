@@ -307,10 +307,9 @@ QMOE_API int qmoe_moe_forward(const void* x, const void* w_router, const float* 
  *   in the workspace); topk_idx / topk_w as in qmoe_moe_forward
  *   workspace of qmoe_moe_block_forward_workspace_size() bytes, 256-byte aligned
  *
- * s and h equal qmoe_rmsnorm's outputs bit for bit and out equals
- * qmoe_moe_forward(h, ..., residual = s).  At decode sizes (T <= 16,
- * E <= 128) the add & norm runs inside the routing kernel: one launch fewer
- * than qmoe_rmsnorm + qmoe_moe_forward.
+ * s and h are qmoe_rmsnorm's outputs (the same kernel) and out equals
+ * qmoe_moe_forward(h, ..., residual = s): the same launches as those two
+ * calls, on one workspace, behind one entry point.
  * ---------------------------------------------------------------------- */
 QMOE_API size_t qmoe_moe_block_forward_workspace_size(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I);
 QMOE_API int qmoe_moe_block_forward(const void* x, const void* residual, const float* norm_weight, float eps,

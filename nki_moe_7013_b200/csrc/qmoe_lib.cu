@@ -279,8 +279,7 @@ int launch_route_small(const void* x, const void* w, const float* bias, int64_t 
                        int64_t k, int normalize, float* logits, int32_t* topk_idx, float* topk_w,
                        int32_t* counts, int32_t* offsets, int32_t* row_token, float* row_w, int32_t* slot_row,
                        int32_t* tiles, int64_t max_tiles, float* acc_zero, cudaStream_t stream,
-                       int32_t* zero_words = nullptr, int n_zero_words = 0,
-                       const qmoe::RouteNorm& nrm = qmoe::RouteNorm{}) {
+                       int32_t* zero_words = nullptr, int n_zero_words = 0) {
   const int G = int(H / 256);
   const int smem = int(route_small_smem(T, H, E, k));
   cudaLaunchConfig_t cfg = {};
@@ -305,7 +304,7 @@ int launch_route_small(const void* x, const void* w, const float* bias, int64_t 
     QMOE_CHECK(set_smem(qmoe::route_small_kernel<GG>, smem));                                            \
     err = cudaLaunchKernelEx(&cfg, qmoe::route_small_kernel<GG>, xb, wb, bias, int(T), int(E), int(k),   \
                              normalize, logits, topk_idx, topk_w, counts, offsets, row_token, row_w,     \
-                             slot_row, tiles, int(max_tiles), acc_zero, zero_words, n_zero_words, nrm);  \
+                             slot_row, tiles, int(max_tiles), acc_zero, zero_words, n_zero_words);       \
     break;
   switch (G) {
     QMOE_ROUTE_SMALL_CASE(1)
@@ -662,29 +661,25 @@ struct AddNorm {
 
 // The MoE forward on a workspace laid out by fwd_layout (shapes checked by
 // the caller): routing, permutation, experts and the combine.  With `an`, x
-// and residual are ignored: the add & norm runs first (inside the decode
-// route kernel when that kernel routes the batch) and the block reads its
-// outputs.
+// and residual are ignored: the add & norm kernel runs first and the block
+// reads its outputs.  (Folding the add & norm into the decode route kernel
+// measured slower: that kernel's 8-CTA cluster then follows the whole-GPU
+// O projection directly and waits for eight free SMs of one GPC; behind
+// the small norm kernel it is placed while the norm runs.)
 int moe_forward_on(const void* x, const void* w_router, const float* router_bias, const void* w_gate_up,
                    const void* w_down, const void* residual, int64_t T, int64_t H, int64_t E, int64_t k, int64_t I,
                    int normalize, void* out, int32_t* topk_idx, float* topk_w, uint8_t* ws, const FwdLayout& L,
                    cudaStream_t s, const AddNorm* an = nullptr) {
   const bool small_route = T <= qmoe::kRouteSmallMaxT && E <= qmoe::kRouteSmallMaxE;
-  qmoe::RouteNorm rn{};
   if (an) {
     using bf16 = __nv_bfloat16;
     x = an->h_out;
     residual = an->res_out;
-    if (small_route) {
-      rn = qmoe::RouteNorm{static_cast<const bf16*>(an->a), static_cast<const bf16*>(an->res), an->w, an->eps,
-                           static_cast<bf16*>(an->h_out), static_cast<bf16*>(an->res_out)};
-    } else {
-      const int st = launch_rmsnorm<bf16, bf16>(int((H + 127) / 128), int((T + 7) / 8), s,
-                                                static_cast<const bf16*>(an->a), static_cast<const bf16*>(an->res),
-                                                an->w, int(T), int(H), an->eps, static_cast<bf16*>(an->h_out),
-                                                static_cast<bf16*>(an->res_out));
-      if (st != QMOE_OK) return st;
-    }
+    const int st = launch_rmsnorm<bf16, bf16>(int((H + 127) / 128), int((T + 7) / 8), s,
+                                              static_cast<const bf16*>(an->a), static_cast<const bf16*>(an->res),
+                                              an->w, int(T), int(H), an->eps, static_cast<bf16*>(an->h_out),
+                                              static_cast<bf16*>(an->res_out));
+    if (st != QMOE_OK) return st;
   }
   int32_t* chunk_hist = reinterpret_cast<int32_t*>(ws + L.chunk_hist);
   int32_t* counts = reinterpret_cast<int32_t*>(ws + L.counts);
@@ -712,13 +707,12 @@ int moe_forward_on(const void* x, const void* w_router, const float* router_bias
   float* logits = T <= kRouterSmallMaxT ? reinterpret_cast<float*>(ws + L.logits) : nullptr;
   const int64_t nchunks = (T + qmoe::kRouterChunk - 1) / qmoe::kRouterChunk;
   if (small_route) {
-    // decode sizes: router + permutation (and the add & norm) in one launch,
-    // which also zeroes the gate/up split counters (the workspace may hold
-    // anything on entry)
+    // decode sizes: router + permutation in one launch, which also zeroes
+    // the gate/up split counters (the workspace may hold anything on entry)
     QMOE_CHECK(launch_route_small(x, w_router, router_bias, T, H, E, k, normalize, logits, idx, tw, counts,
                                   offsets, row_token, row_w, slot_row, tiles, max_tiles, acc, s,
                                   fused ? done : split_counters,
-                                  fused ? int(max_tiles + 2) : split_counters ? qmoe::kSplitCounterWords : 0, rn));
+                                  fused ? int(max_tiles + 2) : split_counters ? qmoe::kSplitCounterWords : 0));
   } else if (fused && nchunks <= num_sms(0)) {
     // prefill batches of at most one router chunk per SM: router, scan and
     // scatter in one launch (one grid-wide barrier), which also zeroes the

@@ -20,18 +20,6 @@
 //
 // Outputs match router_topk + moe_permute bit for bit (routing, rows, tiles);
 // the per-chunk histogram is not produced.
-//
-// With a RouteNorm the kernel also does the decoder layer's post-attention
-// add & norm in front of the router (qwen.py:423 and 428): every CTA forms
-// s = bf16(a + res) and h = bf16(rmsnorm(s) * w) for all T rows in its shared
-// memory (the rows are a few KB; recomputing them beats a cluster exchange),
-// CTA t % kRouteSmallCtas writes row t of s and h to global memory for the
-// expert GEMMs and the residual of the combine, and the router reads h.  Lane
-// layout and rounding are rmsnorm_kernel's, so h and s equal that kernel's
-// outputs bit for bit.
-//
-// The router weights do not depend on the previous kernel, so each warp
-// issues its loads before the programmatic-launch wait.
 #pragma once
 
 #include "common.cuh"
@@ -43,16 +31,6 @@ constexpr int kRouteSmallCtas = 8;    // one cluster (portable size)
 constexpr int kRouteSmallMaxT = 16;   // tokens per launch
 constexpr int kRouteSmallMaxE = 128;  // experts: one warp each, E/8 warps per CTA
 constexpr int kRouteSmallTileRows = 128;
-
-// The add & norm in front of the router (null w: none; the kernel reads x).
-struct RouteNorm {
-  const __nv_bfloat16* a;    // (T, H) sub-layer output
-  const __nv_bfloat16* res;  // (T, H) residual stream
-  const float* w;            // (H) norm weight
-  float eps;
-  __nv_bfloat16* h_out;      // (T, H) normalised rows (the MoE input)
-  __nv_bfloat16* res_out;    // (T, H) s = bf16(a + res)
-};
 
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -79,67 +57,6 @@ __device__ __forceinline__ int warp_exclusive_scan_smem(int* v, int n, int lane)
   return __shfl_sync(0xFFFFFFFFu, incl, 31);
 }
 
-__device__ __forceinline__ uint2 pack_bf16x4(float a, float b, float c, float d) {
-  const __nv_bfloat162 lo = __floats2bfloat162_rn(a, b);
-  const __nv_bfloat162 hi = __floats2bfloat162_rn(c, d);
-  uint2 o;
-  o.x = *reinterpret_cast<const uint32_t*>(&lo);
-  o.y = *reinterpret_cast<const uint32_t*>(&hi);
-  return o;
-}
-
-// Rows t = warp, warp + nwarps, ... < T of s = bf16(a + res) and
-// h = bf16(s * rsqrt(mean(s^2) + eps) * w) into xs (h) and, for the rows this
-// CTA owns, into res_out (s) and h_out (h).  One warp per row; lane l holds
-// elements [128c + 4l, 128c + 4l + 4) of every 128-element chunk c, as in
-// rmsnorm_kernel; s goes through xs between the two passes (it is exactly
-// representable there), which keeps registers for the router weights.
-template <int G>
-__device__ __forceinline__ void route_add_norm_rows(const RouteNorm& nrm, __nv_bfloat16* xs, int T, int cta,
-                                                    int warp, int nwarps, int lane) {
-  constexpr int H = G * 256;
-  constexpr int kC = 2 * G;             // 128-element chunks per row
-  constexpr int kB = kC < 8 ? kC : 8;   // chunks loaded per round trip
-  for (int t = warp; t < T; t += nwarps) {
-    const bool own = t % kRouteSmallCtas == cta;
-    const size_t row = size_t(t) * H + 4 * lane;
-    float ss = 0.f;
-#pragma unroll
-    for (int c0 = 0; c0 < kC; c0 += kB) {
-      uint2 av[kB], rv[kB];
-#pragma unroll
-      for (int i = 0; i < kB; ++i) {
-        av[i] = *reinterpret_cast<const uint2*>(nrm.a + row + (c0 + i) * 128);
-        rv[i] = *reinterpret_cast<const uint2*>(nrm.res + row + (c0 + i) * 128);
-      }
-#pragma unroll
-      for (int i = 0; i < kB; ++i) {
-        const uint2 o = pack_bf16x4(bf16lo_to_f32(av[i].x) + bf16lo_to_f32(rv[i].x),
-                                    bf16hi_to_f32(av[i].x) + bf16hi_to_f32(rv[i].x),
-                                    bf16lo_to_f32(av[i].y) + bf16lo_to_f32(rv[i].y),
-                                    bf16hi_to_f32(av[i].y) + bf16hi_to_f32(rv[i].y));
-        *reinterpret_cast<uint2*>(xs + row + (c0 + i) * 128) = o;
-        if (own) *reinterpret_cast<uint2*>(nrm.res_out + row + (c0 + i) * 128) = o;
-        ss = sumsq4(ss, bf16lo_to_f32(o.x), bf16hi_to_f32(o.x), bf16lo_to_f32(o.y), bf16hi_to_f32(o.y));
-      }
-    }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, off);
-    const float r = rsqrtf(ss / float(H) + nrm.eps);
-#pragma unroll 4
-    for (int c = 0; c < kC; ++c) {
-      const uint2 sv = *reinterpret_cast<const uint2*>(xs + row + c * 128);
-      const float4 wv = *reinterpret_cast<const float4*>(nrm.w + c * 128 + 4 * lane);
-      const uint2 o = pack_bf16x4(__fmul_rn(__fmul_rn(bf16lo_to_f32(sv.x), r), wv.x),
-                                  __fmul_rn(__fmul_rn(bf16hi_to_f32(sv.x), r), wv.y),
-                                  __fmul_rn(__fmul_rn(bf16lo_to_f32(sv.y), r), wv.z),
-                                  __fmul_rn(__fmul_rn(bf16hi_to_f32(sv.y), r), wv.w));
-      *reinterpret_cast<uint2*>(xs + row + c * 128) = o;
-      if (own) *reinterpret_cast<uint2*>(nrm.h_out + row + c * 128) = o;
-    }
-  }
-}
-
 template <int G>  // G = H / 256
 __global__ void __launch_bounds__(kRouteSmallMaxE / kRouteSmallCtas * 32, 1)
     route_small_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
@@ -148,8 +65,7 @@ __global__ void __launch_bounds__(kRouteSmallMaxE / kRouteSmallCtas * 32, 1)
                        int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
                        int32_t* __restrict__ row_token, float* __restrict__ row_w,
                        int32_t* __restrict__ slot_row, int32_t* __restrict__ tiles, int max_tiles,
-                       float* __restrict__ acc_zero, int32_t* __restrict__ zero_words, int n_zero_words,
-                       RouteNorm nrm) {
+                       float* __restrict__ acc_zero, int32_t* __restrict__ zero_words, int n_zero_words) {
   constexpr int H = G * 256;
   extern __shared__ __align__(16) uint8_t route_small_smem[];
   // [Tpad][H] bf16 token rows | [T][E] fp32 logits (CTA 0's copy is filled by
@@ -166,24 +82,17 @@ __global__ void __launch_bounds__(kRouteSmallMaxE / kRouteSmallCtas * 32, 1)
   const int e_per = E / kRouteSmallCtas;
   const int Tpad = (T + 3) & ~3;
   if (threadIdx.x == 0) QMOE_TRACE_AT(0, 0);
-  // this warp's expert: its canonical weight slice, one load per group (the
-  // weights are not written by the previous kernel)
+  griddep_wait();
+  griddep_launch_dependents();
+  if (threadIdx.x == 0) QMOE_TRACE_AT(0, 1);
+
+  // this warp's expert: its canonical weight slice, one load per group
   const int e = cta * e_per + warp;
   uint4 wv[G];
 #pragma unroll
   for (int g = 0; g < G; ++g)
     wv[g] = __ldg(reinterpret_cast<const uint4*>(w + size_t(e) * H + 256 * g + 8 * lane));
-  griddep_wait();
-  griddep_launch_dependents();
-  if (threadIdx.x == 0) QMOE_TRACE_AT(0, 1);
-
-  if (nrm.w) {
-    route_add_norm_rows<G>(nrm, xs, T, cta, warp, int(blockDim.x >> 5), lane);
-    uint4* pad = reinterpret_cast<uint4*>(xs + size_t(T) * H);
-    for (int i = threadIdx.x; i < (Tpad - T) * (H / 8); i += blockDim.x) pad[i] = make_uint4(0u, 0u, 0u, 0u);
-    // h is read next by the expert GEMMs' tensor-memory-access loads
-    fence_proxy_async_global();
-  } else {
+  {
     const uint4* src = reinterpret_cast<const uint4*>(x);
     uint4* dst = reinterpret_cast<uint4*>(xs);
     const int n = T * (H / 8), npad = Tpad * (H / 8);

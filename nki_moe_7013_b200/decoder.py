@@ -13,8 +13,7 @@ like NeuronQwen3MoeDecoderLayer.forward (qwen.py:378-436):
     out = residual + mlp(h, padding_mask)[0]     (qwen.py:429-430)
 
 Here the residual add before the second norm, the norm, the MoE block and
-the final residual add are one library call (``qmoe_moe_block_forward``; at
-decode sizes the add & norm runs inside the MoE's routing kernel).  With a
+the final residual add are one library call (``qmoe_moe_block_forward``).  With a
 ``padding_mask`` the masked MoE output needs the norm's outputs first, so
 that path runs the add & norm and the MoE block as two calls.  RoPE is applied
 inside the attention kernels, so cos/sin caches are returned as None.

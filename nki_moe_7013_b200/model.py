@@ -11,7 +11,7 @@ path (host-side cache lengths, any number of new tokens).
 positions, cache lengths and the next tokens live on the device and advance
 on the device, so a whole step -- 48 layers of RMSNorm, QKV projection, QK
 norm + RoPE + cache append, split-KV decode attention, O projection, add &
-norm fused into the MoE block, then the final norm, the LM head and a greedy pick --
+norm and the MoE block (one library call), then the final norm, the LM head and a greedy pick --
 captures into one CUDA graph and replays without the host.
 """
 from __future__ import annotations
@@ -130,8 +130,7 @@ class DecodeSession:
                              cache_slot=self.slots)
         a = ops.attention_decode(q, cache.k, cache.v, self.kv_len, self.max_seq, workspace=self.attn_ws)
         o = ops.linear(a, attn.w.wo, split_ws=self.split_ws)
-        # add & norm + MoE + residual add (decode sizes: the add & norm runs
-        # inside the routing kernel)
+        # add & norm + MoE + residual add, one library call
         self.plans[l].run_block(o, x, layer.post_attention_layernorm, eps, out)
 
     def step(self) -> torch.Tensor:

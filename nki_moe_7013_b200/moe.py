@@ -380,8 +380,7 @@ class MoEPlan:
                   residual_out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """The decoder layer's post-attention add & norm, this block and the
         residual add (one ``qmoe_moe_block_forward`` call): out = s + MoE(h)
-        with s = bf16(x + residual), h = rmsnorm(s) * norm_weight.  At decode
-        sizes the add & norm runs inside the routing kernel."""
+        with s = bf16(x + residual), h = rmsnorm(s) * norm_weight."""
         lib, p = self._lib, ops._ptr
         s = torch.cuda.current_stream(self.device).cuda_stream
         w = self.w

@@ -3,8 +3,7 @@ library call).  Its add & norm outputs equal the standalone RMSNorm kernel's
 bit for bit and are checked against the oracle; its routing equals
 moe_forward's on those rows bit for bit; its output is within the
 activation tolerance of the oracle's block on the same rows and within one
-bf16 ulp of the two-call path.  Decode sizes (T <= 16) run the add & norm
-inside the routing kernel, larger batches in front of it."""
+bf16 ulp of the two-call path, at decode and prefill sizes."""
 import numpy as np
 import pytest
 import torch
