@@ -24,6 +24,7 @@
 #include "norm_rope.cuh"
 #include "permute.cuh"
 #include "route_small.cuh"
+#include "gemv.cuh"
 #include "router.cuh"
 
 // ---------------------------------------------------------------------------
@@ -566,8 +567,81 @@ int launch_rmsnorm(int chunks, int grid, cudaStream_t s, const Tin* x, const __n
   return set_error(QMOE_ERR_UNSUPPORTED_SHAPE, "rmsnorm: H=%d > 4096", H);
 }
 
+// Decode-row projection on the CUDA cores (gemv.cuh): T <= kGemvMaxT rows,
+// K of 1024, 2048 or 4096, weights up to kGemvMaxWeightElems.
+constexpr int64_t kGemvMaxWeightElems = int64_t(32) << 20;  // 64 MB of bf16
+
+bool linear_rows_applies(int64_t T, int64_t K, int64_t N) {
+  return T >= 1 && T <= qmoe::kGemvMaxT && (K == 1024 || K == 2048 || K == 4096) && N * K <= kGemvMaxWeightElems;
+}
+
+int launch_linear_rows(const void* x, const void* w, int64_t T, int64_t K, int64_t N, void* out,
+                       cudaStream_t stream) {
+  const int TT = T <= 1 ? 1 : T <= 2 ? 2 : 4;
+  const int smem = int(TT * K * 2);
+  const dim3 grid(unsigned((N + qmoe::kGemvWarps - 1) / qmoe::kGemvWarps));
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  const auto* wb = static_cast<const __nv_bfloat16*>(w);
+  auto* ob = static_cast<__nv_bfloat16*>(out);
+#define QMOE_GEMV_CASE(KC, TTV)                                                                            \
+  if (K == 256 * (KC) && TT == (TTV)) {                                                                    \
+    QMOE_CHECK(set_smem(qmoe::linear_rows_kernel<KC, TTV>, smem));                                        \
+    return launch_kernel(qmoe::linear_rows_kernel<KC, TTV>, grid, dim3(qmoe::kGemvWarps * 32), size_t(smem), \
+                         stream, true, "linear_rows_kernel", xb, wb, int(T), int(N), ob);                  \
+  }
+#define QMOE_GEMV_KC(KC) QMOE_GEMV_CASE(KC, 1) QMOE_GEMV_CASE(KC, 2) QMOE_GEMV_CASE(KC, 4)
+  QMOE_GEMV_KC(4)
+  QMOE_GEMV_KC(8)
+  QMOE_GEMV_KC(16)
+#undef QMOE_GEMV_KC
+#undef QMOE_GEMV_CASE
+  return set_error(QMOE_ERR_UNSUPPORTED_SHAPE, "linear_rows: K=%lld T=%lld", (long long)K, (long long)T);
+}
+
+// Expert GEMMs of a 1-2 token step on the CUDA cores (gemv.cuh).
+bool expert_rows_applies(int64_t T, int64_t H, int64_t k, int64_t I) {
+  return T >= 1 && T <= qmoe::kExpertRowsMaxT && (H == 1024 || H == 2048) && I % 256 == 0 &&
+         I / 256 <= 4 && T * k <= qmoe::kExpertRowsMaxR && T * k * I * 2 <= 96 * 1024;
+}
+
+int launch_expert_rows(const void* x, const int32_t* row_token, const float* row_w, const void* w_gate_up,
+                       const void* w_down, const int32_t* tiles, int64_t max_tiles, int64_t R, int64_t H,
+                       int64_t I, int64_t E, int64_t T, void* act, const void* residual, void* out,
+                       cudaStream_t s) {
+  using bf16 = __nv_bfloat16;
+  const dim3 block(qmoe::kGemvWarps * 32);
+  const dim3 grid_gu(unsigned(std::min<int64_t>(2 * num_sms(0), max_tiles * (I / qmoe::kGemvWarps))));
+  int st = QMOE_OK;
+#define QMOE_GU_CASE(KC)                                                                                          \
+  if (H == 256 * (KC))                                                                                             \
+    st = launch_kernel(qmoe::expert_gateup_rows_kernel<KC>, grid_gu, block, 0, s, true, "expert_gateup_rows_kernel", \
+                       static_cast<const bf16*>(x), row_token, static_cast<const bf16*>(w_gate_up), tiles,          \
+                       int(max_tiles), int(R), int(I), int(E), int(T), static_cast<bf16*>(act));
+  QMOE_GU_CASE(4)
+  QMOE_GU_CASE(8)
+#undef QMOE_GU_CASE
+  if (st != QMOE_OK) return st;
+  const int smem = int(R * I * 2);
+  const dim3 grid_dn(unsigned(std::min<int64_t>(2 * num_sms(0), (H + qmoe::kGemvWarps - 1) / qmoe::kGemvWarps)));
+#define QMOE_DN_CASE(IC)                                                                                          \
+  if (I == 256 * (IC)) {                                                                                           \
+    QMOE_CHECK(set_smem(qmoe::expert_down_rows_kernel<IC>, smem));                                                 \
+    return launch_kernel(qmoe::expert_down_rows_kernel<IC>, grid_dn, block, size_t(smem), s, true,                 \
+                         "expert_down_rows_kernel", static_cast<const bf16*>(act), static_cast<const bf16*>(w_down), \
+                         tiles, int(max_tiles), row_token, row_w, int(R), int(H), int(E), int(T),                    \
+                         static_cast<const bf16*>(residual), static_cast<bf16*>(out));                               \
+  }
+  QMOE_DN_CASE(1)
+  QMOE_DN_CASE(2)
+  QMOE_DN_CASE(3)
+  QMOE_DN_CASE(4)
+#undef QMOE_DN_CASE
+  return set_error(QMOE_ERR_UNSUPPORTED_SHAPE, "expert rows: I=%lld", (long long)I);
+}
+
 int launch_linear(const void* x, const void* w, int64_t T, int64_t K, int64_t N, void* out,
                   cudaStream_t stream, void* split_ws = nullptr) {
+  if (linear_rows_applies(T, K, N)) return launch_linear_rows(x, w, T, K, N, out, stream);
   CUtensorMap tmA, tmB;
   QMOE_CHECK(make_tmap_bf16(&tmA, w, uint64_t(K), uint64_t(N), qmoe::kBK, qmoe::kBM));
   QMOE_CHECK(make_tmap_bf16(&tmB, x, uint64_t(K), uint64_t(T), qmoe::kBK, qmoe::kBoxRows));
@@ -739,6 +813,11 @@ int moe_forward_on(const void* x, const void* w_router, const float* router_bias
     return launch_moe_fused(x, T, row_token, w_gate_up, w_down, tiles, max_tiles, row_token, row_w, R, H, I, E, act,
                             acc, T, done, s, residual, out);
   }
+  // 1-2 tokens: the expert GEMMs are matrix-vector products, run on the CUDA
+  // cores; the down kernel also adds the residual and writes the output
+  if (expert_rows_applies(T, H, k, I))
+    return launch_expert_rows(x, row_token, row_w, w_gate_up, w_down, tiles, max_tiles, R, H, I, E, T, act,
+                              residual, out, s);
   // with the split scratch (decode sizes) the gate/up GEMM counts finished
   // units per tile there, so the down GEMM starts each tile as soon as its
   // activations are written rather than after the whole gate/up grid

@@ -76,6 +76,28 @@ def test_linear_decode_split_k(cuda_dev, T, K, N):
     assert max_rel_err(to_f32_np(runs[0]), ref) < 1e-2
 
 
+@pytest.mark.parametrize("T,K,N", [(1, 2048, 5120), (2, 4096, 2048), (3, 1024, 384), (4, 2048, 1024),
+                                   (4, 4096, 2048), (5, 2048, 5120)])
+def test_linear_decode_rows(cuda_dev, T, K, N):
+    """Decode rows (T <= 4) run the CUDA-core projection (5 rows: the
+    tensor-core kernel): within the tolerance of an fp64 reference,
+    run-to-run identical, and within the same tolerance of the tensor-core
+    path (a 9-row call whose first T rows are these)."""
+    from nki_moe_7013_b200 import _C, ops
+
+    x9 = activations(T + K + 1, 9, K, cuda_dev)
+    x = x9[:T].contiguous()
+    w = (activations(N + 3, N, K, cuda_dev) * 0.02).to(torch.bfloat16).contiguous()
+    runs = [ops.linear(x, w) for _ in range(2)]
+    tc = ops.linear(x9, w)[:T]
+    torch.cuda.synchronize()
+    assert _C.device_error() == 0
+    assert torch.equal(runs[0], runs[1])
+    ref = to_f32_np(x).astype(np.float64) @ to_f32_np(w).astype(np.float64).T
+    assert max_rel_err(to_f32_np(runs[0]), ref) < 1e-2
+    assert max_rel_err(to_f32_np(runs[0]), to_f32_np(tc)) < 1e-2
+
+
 def _attn_weights(cuda_dev, H, nh, nkv, seed):
     from nki_moe_7013_b200.synth import normal_bf16_device
 

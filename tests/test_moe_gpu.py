@@ -353,3 +353,32 @@ def test_moe_forward_repeatable_on_dirty_workspace(cuda_dev, T):
         assert not torch.isnan(out).any()
         assert_within_one_ulp(out, ref, f"T={T} run {i}")
     assert _C.device_error() == 0
+
+
+@pytest.mark.parametrize("T,H,E,k,I", [(1, 2048, 128, 8, 768), (2, 2048, 128, 8, 768), (1, 4096, 64, 8, 256),
+                                       (2, 1024, 32, 32, 512), (2, 2048, 256, 8, 768)])
+def test_decode_expert_rows_match_tensor_core_path(cuda_dev, oracle, T, H, E, k, I):
+    """1-2 token forwards run the expert GEMMs on the CUDA cores (the down
+    kernel also adds the residual and writes the output): routing identical,
+    output within the activation tolerance of the oracle and of the
+    tensor-core kernels on the same routing (MoEPlan's per-stage path), and
+    run-to-run identical (no atomics)."""
+    from nki_moe_7013_b200 import _C, ops
+    from nki_moe_7013_b200.moe import MoEPlan, MoEWeights
+
+    wr, wgu, wd = moe_weights(110 + T, E, H, I, cuda_dev)
+    x = activations(110 + T, T, H, cuda_dev)
+    res = activations(111 + T, T, H, cuda_dev)
+    outs = [ops.moe_forward(x, wr, wgu, wd, k, residual=res, return_routing=True) for _ in range(2)]
+    plan = MoEPlan(MoEWeights(wr, wgu, wd), T, k)
+    staged = torch.empty((T, H), dtype=torch.bfloat16, device=cuda_dev)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(plan.stages) + 1)]
+    plan.run(x, staged, residual=res, events=evs)
+    torch.cuda.synchronize()
+    assert _C.device_error() == 0
+    out, idx, tw = outs[0]
+    assert torch.equal(out, outs[1][0])
+    assert torch.equal(idx, plan.topk_idx) and torch.equal(tw, plan.topk_w)
+    assert max_rel_err(to_f32_np(out), to_f32_np(staged)) <= 1e-2
+    ref = oracle.moe_block(x.cpu(), wr.cpu(), wgu.cpu(), wd.cpu(), k) + to_f32_np(res)
+    assert max_rel_err(to_f32_np(out), ref) <= MAX_REL
