@@ -427,6 +427,57 @@ __global__ void __launch_bounds__(256)
   const int gw = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (gw >= B * nh) return;
   const size_t base_idx = size_t(gw) * nsplit;
+  if (nsplit <= 64) {
+    // lane s holds splits s and s + 32: their maxima and sums in one round
+    // trip, the scales kept in registers; then the partial outputs 16 splits
+    // at a time with every load in flight.  Same sums in the same order as
+    // the general loop below.
+    float m0 = -INFINITY, l0 = 0.f, m1 = -INFINITY, l1 = 0.f;
+    if (lane < nsplit) {
+      const float2 ml = *reinterpret_cast<const float2*>(part_ml + (base_idx + lane) * 2);
+      m0 = ml.x;
+      l0 = ml.y;
+    }
+    if (lane + 32 < nsplit) {
+      const float2 ml = *reinterpret_cast<const float2*>(part_ml + (base_idx + lane + 32) * 2);
+      m1 = ml.x;
+      l1 = ml.y;
+    }
+    float M = fmaxf(m0, m1);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, off));
+    const float mb = M == -INFINITY ? 0.f : M;
+    const float sc0 = lane < nsplit ? exp2f(m0 - mb) : 0.f;
+    const float sc1 = lane + 32 < nsplit ? exp2f(m1 - mb) : 0.f;
+    float L = 0.f;
+    if (lane < nsplit) L += l0 * sc0;
+    if (lane + 32 < nsplit) L += l1 * sc1;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) L += __shfl_xor_sync(0xFFFFFFFFu, L, off);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int s0 = 0; s0 < nsplit; s0 += 16) {
+      float4 v[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (s0 + j < nsplit) v[j] = *reinterpret_cast<const float4*>(part_o + (base_idx + s0 + j) * kAttnD + lane * 4);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int sj = s0 + j;
+        if (sj >= nsplit) break;
+        const float sc = __shfl_sync(0xFFFFFFFFu, sj < 32 ? sc0 : sc1, sj & 31);
+        acc[0] += v[j].x * sc;
+        acc[1] += v[j].y * sc;
+        acc[2] += v[j].z * sc;
+        acc[3] += v[j].w * sc;
+      }
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    uint2 o;
+    o.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
+    o.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
+    *reinterpret_cast<uint2*>(out + size_t(gw) * kAttnD + lane * 4) = o;
+    return;
+  }
   // the splits' maxima and sums: lane s takes splits s, s+32, ... (one round
   // trip), then warp reductions
   float M = -INFINITY;

@@ -30,10 +30,18 @@ __global__ void __launch_bounds__(kNormThreads)
     rmsnorm_kernel(const Tin* __restrict__ x, const __nv_bfloat16* __restrict__ residual,
                    const float* __restrict__ w, int rows, int H, float eps, Tout* __restrict__ y,
                    __nv_bfloat16* __restrict__ residual_out) {
-  griddep_wait();
-  griddep_launch_dependents();
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // the norm weight is a parameter, not written by the previous kernel: its
+  // loads go out before the programmatic-launch wait
+  float4 wq[kChunks];
+#pragma unroll
+  for (int i = 0; i < kChunks; ++i) {
+    const int c = i * 128 + lane * 4;
+    wq[i] = c < H ? *reinterpret_cast<const float4*>(w + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  griddep_wait();
+  griddep_launch_dependents();
   const int row = blockIdx.x * (kNormThreads / 32) + warp;
   if (row >= rows) return;
   const Tin* xr = x + size_t(row) * H;
@@ -87,7 +95,7 @@ __global__ void __launch_bounds__(kNormThreads)
   for (int i = 0; i < kChunks; ++i) {
     const int c = i * 128 + lane * 4;
     if (c >= H) continue;
-    const float4 wv = *reinterpret_cast<const float4*>(w + c);
+    const float4 wv = wq[i];
     const float o0 = __fmul_rn(__fmul_rn(v[i][0], r), wv.x), o1 = __fmul_rn(__fmul_rn(v[i][1], r), wv.y),
                 o2 = __fmul_rn(__fmul_rn(v[i][2], r), wv.z), o3 = __fmul_rn(__fmul_rn(v[i][3], r), wv.w);
     if constexpr (sizeof(Tout) == 4) {
