@@ -283,6 +283,13 @@ QMOE_API int qmoe_embedding_gather(const void* table, int64_t V, int64_t H, cons
  *   out (T, H) bf16 = residual + MoE(x) (residual may be NULL)
  *   topk_idx (T, k) int32 / topk_w (T, k) fp32 outputs may be NULL
  *   workspace of qmoe_moe_forward_workspace_size() bytes, 256-byte aligned
+ *
+ * Kernels by batch size: 1-2 tokens (H of 1024 or 2048, I a multiple of
+ * 256, T*k <= 64) run the expert GEMMs as matrix-vector products on the CUDA
+ * cores, the down kernel summing each token's contributions in expert order
+ * (run-to-run identical); 3+ tokens run one persistent tcgen05 kernel for
+ * both expert GEMMs, whose combine adds in arrival order (results may differ
+ * from run to run in the last bit of the fp32 sums).
  * ---------------------------------------------------------------------- */
 QMOE_API size_t qmoe_moe_forward_workspace_size(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I);
 QMOE_API int qmoe_moe_forward(const void* x, const void* w_router, const float* router_bias,
@@ -325,7 +332,9 @@ QMOE_API int qmoe_moe_block_forward(const void* x, const void* residual, const f
  * "expert", dense row tiles).  Replaces the QKV and o_proj projections of
  * NeuronAttentionBase (qwen.py:313-341) and the LM head (the reference's
  * NKI LM-head kernel, qwen_with_nki.py:1766-1805).  Requires K % 64 == 0,
- * N % 128 == 0.  Decode rows (T <= 16) run a deep-ring configuration; with
+ * N % 128 == 0.  1-4 rows with K of 1024, 2048 or 4096 and at most 32 Mi
+ * weight elements run as matrix-vector products on the CUDA cores (split_ws
+ * unused).  Other decode rows (T <= 16) run a deep-ring configuration; with
  * split_ws (qmoe_grouped_gemm_gateup_split_workspace_size() bytes, zero-filled
  * before first use, left zero-filled, calls sharing it must not overlap on
  * the GPU) K is also split over up to 8 CTAs per 128 features when that puts
