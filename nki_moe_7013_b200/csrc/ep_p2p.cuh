@@ -33,7 +33,9 @@
 // graphs (one per parity) replay the steps alternately.
 //
 // Every cross-GPU wait is bounded (kWaitLimitNs); on time-out the kernel
-// records a device error and returns.  No cluster-multicast load anywhere.
+// records a device error and returns.  Peer memory is touched only by plain
+// loads and stores and by release/acquire flags; no load is broadcast
+// across a cluster.
 #pragma once
 
 #include "common.cuh"
