@@ -511,7 +511,7 @@ QMOE_API int qmoe_grouped_gemm_down_return(const void* act, const void* w_down, 
  * Same arguments and result as qmoe_moe_forward without the workspace.  Its
  * scratch is one built-in device array of QMOE_NOALLOC_SCRATCH_BYTES (8 MiB,
  * held on every GPU that loads the library until the process exits): enough
- * for up to 150 tokens per call at Qwen3-30B-A3B shapes.  Larger calls return
+ * for up to 156 tokens per call at Qwen3-30B-A3B shapes.  Larger calls return
  * QMOE_ERR_WORKSPACE_TOO_SMALL without launching anything.  The first call on
  * each device looks the array up (cudaGetSymbolAddress) -- make it before any
  * stream capture.  All calls share the array: calls that overlap on the GPU

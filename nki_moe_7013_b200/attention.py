@@ -53,6 +53,11 @@ class KVCache:
         self.lengths = [length] * self.n_slots
         return self
 
+    def reset(self) -> "KVCache":
+        """Empty every slot (the contents are overwritten by the next appends)."""
+        self.lengths = [0] * self.n_slots
+        return self
+
 
 @dataclass
 class AttnWeights:
@@ -84,6 +89,48 @@ class AttnWeights:
                            attn.k_norm.weight.detach().float().to(device).contiguous())
 
 
+class StageTimer:
+    """Optional per-stage CUDA events: ``with timer("name"):`` records an
+    event pair around the kernels issued inside on the current stream and
+    appends (name, start, end) to ``timer.marks``.  A ``None`` timer costs
+    nothing (``stage(None, name)``)."""
+
+    def __init__(self):
+        self.marks = []
+
+    def __call__(self, name: str):
+        return _Stage(self, name)
+
+    def totals_ms(self) -> dict:
+        """Summed elapsed time per stage name (synchronise first)."""
+        out: dict = {}
+        for name, a, b in self.marks:
+            out[name] = out.get(name, 0.0) + a.elapsed_time(b)
+        return out
+
+
+class _Stage:
+    def __init__(self, timer, name):
+        self.timer, self.name = timer, name
+
+    def __enter__(self):
+        if self.timer is not None:
+            self.a = torch.cuda.Event(enable_timing=True)
+            self.b = torch.cuda.Event(enable_timing=True)
+            self.a.record()
+        return self
+
+    def __exit__(self, *exc):
+        if self.timer is not None:
+            self.b.record()
+            self.timer.marks.append((self.name, self.a, self.b))
+        return False
+
+
+def stage(timer: Optional[StageTimer], name: str) -> _Stage:
+    return _Stage(timer, name)
+
+
 class Qwen3MoeAttention(nn.Module):
     def __init__(self, cfg: Qwen3MoeConfig, weights: Optional[AttnWeights] = None, device="cuda",
                  seed: int = 0):
@@ -99,7 +146,7 @@ class Qwen3MoeAttention(nn.Module):
         return KVCache(n_slots, self.cfg.num_key_value_heads, max_seq, self.cfg.head_dim, self.w.wqkv.device)
 
     def forward(self, hidden_states: torch.Tensor, position_ids: Optional[torch.Tensor] = None,
-                past_key_value: Optional[KVCache] = None):
+                past_key_value: Optional[KVCache] = None, timer: Optional[StageTimer] = None):
         cfg = self.cfg
         B, S, H = hidden_states.shape
         dev = hidden_states.device
@@ -119,18 +166,23 @@ class Qwen3MoeAttention(nn.Module):
                 raise ValueError("position_ids must continue each sequence's cache contiguously")
         positions = pos.reshape(-1).to(dev, non_blocking=True)
         slots = torch.arange(B, dtype=torch.int32).repeat_interleave(S).to(dev, non_blocking=True)
-        qkv = ops.linear(x2d, self.w.wqkv)
-        q = ops.qk_norm_rope(qkv, positions, self.w.q_norm, self.w.k_norm, self.inv_freq,
-                             cfg.num_attention_heads, cfg.num_key_value_heads, cfg.rms_norm_eps,
-                             cache.k, cache.v, cache_slot=slots)
+        with stage(timer, "qkv_proj"):
+            qkv = ops.linear(x2d, self.w.wqkv)
+        with stage(timer, "qk_norm_rope"):
+            q = ops.qk_norm_rope(qkv, positions, self.w.q_norm, self.w.k_norm, self.inv_freq,
+                                 cfg.num_attention_heads, cfg.num_key_value_heads, cfg.rms_norm_eps,
+                                 cache.k, cache.v, cache_slot=slots)
         if S == 1:
             kv_len = torch.tensor([l + 1 for l in L0], dtype=torch.int32).to(dev, non_blocking=True)
-            attn = ops.attention_decode(q, cache.k, cache.v, kv_len, max(L0) + 1,
-                                        workspace=self._decode_ws)
+            with stage(timer, "attention"):
+                attn = ops.attention_decode(q, cache.k, cache.v, kv_len, max(L0) + 1,
+                                            workspace=self._decode_ws)
         else:
             q_start = torch.tensor(L0, dtype=torch.int32).to(dev, non_blocking=True)
-            attn = ops.attention_prefill(q, cache.k, cache.v, q_start, B, S)
+            with stage(timer, "attention"):
+                attn = ops.attention_prefill(q, cache.k, cache.v, q_start, B, S)
         for b in range(B):
             cache.lengths[b] += S
-        out = ops.linear(attn, self.w.wo)
+        with stage(timer, "o_proj"):
+            out = ops.linear(attn, self.w.wo)
         return out.reshape(B, S, H), cache

@@ -1616,14 +1616,15 @@ QMOE_API int qmoe_trace_read(void* host, size_t bytes) {
 //
 //  - Size limit: kNoAllocScratchBytes (QMOE_NOALLOC_SCRATCH_BYTES, 8 MiB).
 //    At Qwen3-30B-A3B shapes (H 2048, 128 experts, top-8, I 768) that holds
-//    the scratch of up to 150 tokens per call -- decode-sized batches.
+//    the scratch of up to 156 tokens per call -- decode-sized batches.
 //    Larger calls are rejected with QMOE_ERR_WORKSPACE_TOO_SMALL before
 //    anything is launched.
 //  - The array lives in every GPU's memory as soon as the library's device
 //    code is loaded on that GPU, and stays there until the process exits.
 //  - Set-up: the first call on each device looks up the array's device
 //    address with cudaGetSymbolAddress (which also loads the module on that
-//    device); make that first call before any stream capture.
+//    device); make that first call before any stream capture.  A failed
+//    lookup is not remembered: the next call on that device retries it.
 //  - All calls share the one array and it keeps the last call's contents.
 //    Nothing in it needs to start at zero: the routing kernels rewrite every
 //    index buffer and the permutation kernel zero-fills the fp32 combine
@@ -1635,25 +1636,30 @@ namespace {
 constexpr size_t kNoAllocScratchBytes = QMOE_NOALLOC_SCRATCH_BYTES;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-std::once_flag g_noalloc_once[kMaxDevices];
+std::mutex g_noalloc_mutex;
 void* g_noalloc_ptr[kMaxDevices];
-cudaError_t g_noalloc_status[kMaxDevices];
 
-// Device address of g_noalloc_scratch on the current device (looked up once
-// per device, with that device current).
+// Device address of g_noalloc_scratch on the current device, looked up with
+// that device current.  Only a successful lookup is kept: if the first one
+// fails (e.g. it was made during a stream capture), the call returns the
+// error, clears it from the runtime's per-thread error state, and the next
+// call on that device tries again.
 int noalloc_scratch(void** out) {
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return set_error(QMOE_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(err));
   if (dev < 0 || dev >= kMaxDevices) return set_error(QMOE_ERR_DEVICE, "device ordinal %d out of range", dev);
-  std::call_once(g_noalloc_once[dev], [dev]() {
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_ptr[dev] == nullptr) {
     void* p = nullptr;
-    g_noalloc_status[dev] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (err != cudaSuccess || p == nullptr) {
+      (void)cudaGetLastError();  // do not leave the failure for the caller's next CUDA check
+      return set_error(QMOE_ERR_CUDA, "cudaGetSymbolAddress(scratch) on device %d: %s", dev,
+                       cudaGetErrorString(err));
+    }
     g_noalloc_ptr[dev] = p;
-  });
-  if (g_noalloc_status[dev] != cudaSuccess || g_noalloc_ptr[dev] == nullptr)
-    return set_error(QMOE_ERR_CUDA, "cudaGetSymbolAddress(scratch) on device %d: %s", dev,
-                     cudaGetErrorString(g_noalloc_status[dev]));
+  }
   *out = g_noalloc_ptr[dev];
   return QMOE_OK;
 }

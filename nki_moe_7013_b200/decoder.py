@@ -18,7 +18,15 @@ the final residual add are one library call (``qmoe_moe_block_forward``).  With 
 that path runs the add & norm and the MoE block as two calls.  RoPE is applied
 inside the attention kernels, so cos/sin caches are returned as None.
 ``attention_mask`` is accepted for signature compatibility; attention is
-causal over each sequence's cache.  ``capture_intermediates=True`` keeps the
+causal over each sequence's cache.
+
+``mlp``: the MoE module to use instead of a single-GPU
+``Qwen3MoeSparseMoeBlock`` -- e.g. an expert-parallel
+``ep.PeerExpertParallelMoE`` (attention then stays data-parallel: each rank
+runs its own sequences).  Such a block (``expert_parallel = True``) is called
+as ``mlp(h, residual=s)`` after a separate add & norm kernel.
+``timer`` (an ``attention.StageTimer`` keyword argument) records CUDA events
+around the layer's stages.  ``capture_intermediates=True`` keeps the
 post-attention residual stream and the MoE input of the last call in
 ``self.last`` (for layer-by-layer parity checks).
 """
@@ -30,7 +38,7 @@ import torch
 from torch import nn
 
 from . import ops
-from .attention import AttnWeights, KVCache, Qwen3MoeAttention
+from .attention import AttnWeights, KVCache, Qwen3MoeAttention, stage
 from .config import Qwen3MoeConfig
 from .moe import MoEWeights, Qwen3MoeSparseMoeBlock
 
@@ -38,12 +46,13 @@ from .moe import MoEWeights, Qwen3MoeSparseMoeBlock
 class Qwen3MoeDecoderLayer(nn.Module):
     def __init__(self, cfg: Qwen3MoeConfig, layer_idx: int = 0, attn_weights: Optional[AttnWeights] = None,
                  moe_weights: Optional[MoEWeights] = None, input_norm: Optional[torch.Tensor] = None,
-                 post_norm: Optional[torch.Tensor] = None, device="cuda", seed: int = 0):
+                 post_norm: Optional[torch.Tensor] = None, device="cuda", seed: int = 0,
+                 mlp: Optional[nn.Module] = None):
         super().__init__()
         self.cfg = cfg
         self.layer_idx = layer_idx
         self.self_attn = Qwen3MoeAttention(cfg, attn_weights, device=device, seed=seed)
-        self.mlp = Qwen3MoeSparseMoeBlock(cfg, moe_weights, device=device, seed=seed)
+        self.mlp = mlp if mlp is not None else Qwen3MoeSparseMoeBlock(cfg, moe_weights, device=device, seed=seed)
         g = torch.Generator(device=device)
         g.manual_seed(seed * 10 + 8)
         H = cfg.hidden_size
@@ -57,11 +66,25 @@ class Qwen3MoeDecoderLayer(nn.Module):
                 padding_mask: Optional[torch.Tensor] = None, **kwargs):
         B, S, H = hidden_states.shape
         eps = self.cfg.rms_norm_eps
+        timer = kwargs.get("timer")
         x2d = hidden_states.reshape(B * S, H).to(torch.bfloat16).contiguous()
-        h = ops.rmsnorm(x2d, self.input_layernorm, eps)
-        a, present = self.self_attn(h.reshape(B, S, H), position_ids, past_key_value)
+        with stage(timer, "input_norm"):
+            h = ops.rmsnorm(x2d, self.input_layernorm, eps)
+        a, present = self.self_attn(h.reshape(B, S, H), position_ids, past_key_value, timer=timer)
         a2d = a.reshape(B * S, H)
-        if padding_mask is None:
+        if getattr(self.mlp, "expert_parallel", False):
+            with stage(timer, "post_norm"):
+                h2, residual = ops.rmsnorm(a2d, self.post_attention_layernorm, eps, residual=x2d)
+            with stage(timer, "moe"):
+                if padding_mask is None:
+                    out = self.mlp(h2, residual=residual)
+                else:
+                    moe = self.mlp(h2)
+                    out = (residual.float() + moe.float() * padding_mask.reshape(-1, 1).float()).to(torch.bfloat16)
+        elif padding_mask is None and timer is not None and not kwargs.get("capture_intermediates"):
+            with stage(timer, "moe"):
+                out = self.mlp._block(a2d, x2d, self.post_attention_layernorm, eps)
+        elif padding_mask is None:
             capture = bool(kwargs.get("capture_intermediates"))
             h2 = torch.empty_like(x2d) if capture else None
             residual = torch.empty_like(x2d) if capture else None

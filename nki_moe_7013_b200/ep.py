@@ -124,31 +124,21 @@ class ExpertParallelMoE(nn.Module):
         return out.reshape(shape)
 
 
-class PeerExpertParallelMoE(nn.Module):
-    """Expert-parallel block whose exchange runs through peer memory inside
-    one node (CUDA IPC mappings over NVLink / NVSwitch) with no host sync, so
-    a step is a fixed sequence of stream-ordered kernels.
-
-    Kernels per step: router, permutation (counts / offsets / slot rows),
-    count exchange, dispatch (rows of x straight into the owners' receive
-    buffers, already grouped by expert), signal/wait, gate/up + down in one
-    persistent kernel on the receive buffer whose down epilogue stores the
-    weighted rows into the source ranks' return buffers, signal/wait, unpack.
+class PeerEPExchange:
+    """Device buffers and peer mappings of the peer-memory expert-parallel
+    exchange, shared by every EP block of a model (the blocks of a decoder
+    stack run one after another on one stream, so one set of buffers serves
+    all of them).
 
     Buffers (identical shapes on every rank, two parity halves each):
     receive rows (P*max_tokens*k, H), their meta, return rows
     (max_tokens*k, H), and the control block (counts + flags + the rank's
-    step counter).  The kernels take the step's epoch from the device-side
-    step counter, so each parity's step has fixed arguments: ``capture``
-    records one CUDA graph per parity and ``replay`` runs the next step with
-    no host work beyond the graph launch.  Every rank must run the same steps
-    in the same order (each step's exchange waits for every peer's step of
-    the same number); a rank that runs an extra step waits out the bounded
-    wait limit and records device error 5."""
+    step counter); plus the routing buffers of the local tokens.  The
+    receive, meta, return and control buffers are exported with CUDA IPC and
+    every peer's copy is mapped here (``peer``: name -> int64 tensor of the P
+    device pointers).  Creating one is collective over ``group``."""
 
-    def __init__(self, cfg: Qwen3MoeConfig, router_weight: torch.Tensor, local: MoEWeights,
-                 max_tokens: int, group=None):
-        super().__init__()
+    def __init__(self, cfg: Qwen3MoeConfig, max_tokens: int, group=None, device=None):
         from . import _C
 
         self._lib = _C.lib()
@@ -161,13 +151,8 @@ class PeerExpertParallelMoE(nn.Module):
             raise ValueError("num_experts must divide evenly over the ranks")
         self.E, self.H, self.I, self.k = E, H, I, k
         self.e_local = E // self.world
-        if local.gate_up.shape[0] != self.e_local:
-            raise ValueError("local expert weights do not match E / world")
-        self.router_weight = router_weight
-        self.local = local
-        self.router_bias: Optional[torch.Tensor] = None
         self.max_tokens = max_tokens
-        dev = router_weight.device
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         self.device = dev
         self.cap = self.world * max_tokens * k          # receive rows per parity
         self.ret_rows = max_tokens * k                  # return rows per parity
@@ -197,7 +182,7 @@ class PeerExpertParallelMoE(nn.Module):
         self.slot_row = torch.empty((max_tokens, k), **i32)
         self.perm_tiles = torch.empty(1 + 3 * ops.max_tiles(R, E), **i32)
         self.route_barrier = torch.zeros(2, **i32)  # left zero by every completed route
-        self._sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        self.sms = torch.cuda.get_device_properties(dev).multi_processor_count
         torch.cuda.synchronize(dev)
         self._imported = []
         names = ("recv_x", "recv_meta", "ret", "ctrl")
@@ -227,28 +212,102 @@ class PeerExpertParallelMoE(nn.Module):
         torch.cuda.synchronize(dev)
         dist.barrier(group=group)
         self.steps = 0        # steps issued (the device counter follows in stream order)
-        self._graphs = None   # (graph of parity 0, graph of parity 1)
-        self._static = None
 
     def close(self):
         """Unmap the peers' buffers (all ranks should be done with the exchange)."""
         from . import _C
 
         torch.cuda.synchronize(self.device)
-        self._graphs = None
         for base in self._imported:
             _C.check(self._lib.qmoe_ipc_close(base), "qmoe_ipc_close")
         self._imported = []
-
-    STAGES = ("route", "exchange", "dispatch", "experts", "return_wait", "unpack")
 
     def launches_per_step(self, T: int) -> int:
         """Kernels one step launches: route (router + permutation: one launch
         up to one router chunk per SM and T > 64, else router + scan +
         scatter), count exchange, dispatch, signal, experts, signal, unpack."""
         nchunks = (T + ops.ROUTER_CHUNK - 1) // ops.ROUTER_CHUNK
-        one = T > ops.ROUTER_SMALL_MAX_T and nchunks <= self._sms
+        one = T > ops.ROUTER_SMALL_MAX_T and nchunks <= self.sms
         return (1 if one else 3) + 6
+
+
+class PeerExpertParallelMoE(nn.Module):
+    """Expert-parallel block whose exchange runs through peer memory inside
+    one node (CUDA IPC mappings over NVLink / NVSwitch) with no host sync, so
+    a step is a fixed sequence of stream-ordered kernels.
+
+    Kernels per step: router, permutation (counts / offsets / slot rows),
+    count exchange, dispatch (rows of x straight into the owners' receive
+    buffers, already grouped by expert), signal/wait, gate/up + down in one
+    persistent kernel on the receive buffer whose down epilogue stores the
+    weighted rows into the source ranks' return buffers, signal/wait, unpack.
+
+    The buffers live in a ``PeerEPExchange`` (``exchange``): pass one shared
+    exchange to every block of a decoder stack, or let the block create its
+    own (``max_tokens`` sizes it).  The kernels take the step's epoch from the
+    device-side step counter, so each parity's step has fixed arguments:
+    ``capture`` records one CUDA graph per parity and ``replay`` runs the next
+    step with no host work beyond the graph launch.  Every rank must run the
+    same steps in the same order (each step's exchange waits for every peer's
+    step of the same number); a rank that runs an extra step waits out the
+    bounded wait limit and records device error 5."""
+
+    expert_parallel = True
+
+    def __init__(self, cfg: Qwen3MoeConfig, router_weight: torch.Tensor, local: MoEWeights,
+                 max_tokens: Optional[int] = None, group=None, exchange: Optional[PeerEPExchange] = None):
+        super().__init__()
+        from . import _C
+
+        self._lib = _C.lib()
+        if exchange is None:
+            if max_tokens is None:
+                raise ValueError("give max_tokens or a shared exchange")
+            exchange = PeerEPExchange(cfg, max_tokens, group=group, device=router_weight.device)
+            self._owns_exchange = True
+        else:
+            self._owns_exchange = False
+        self.x = exchange
+        self.cfg = cfg
+        self.group = exchange.group
+        self.world, self.rank = exchange.world, exchange.rank
+        self.E, self.H, self.I, self.k = exchange.E, exchange.H, exchange.I, exchange.k
+        self.e_local = exchange.e_local
+        if local.gate_up.shape[0] != self.e_local:
+            raise ValueError("local expert weights do not match E / world")
+        self.router_weight = router_weight
+        self.local = local
+        self.router_bias: Optional[torch.Tensor] = None
+        self.max_tokens = exchange.max_tokens
+        self.device = exchange.device
+        self._graphs = None   # (graph of parity 0, graph of parity 1)
+        self._static = None   # per parity: (x, residual, out)
+
+    # views of the shared exchange (read by callers and tests)
+    @property
+    def recv_rows(self) -> torch.Tensor:
+        return self.x.recv_rows
+
+    @property
+    def topk_idx(self) -> torch.Tensor:
+        return self.x.topk_idx
+
+    @property
+    def steps(self) -> int:
+        return self.x.steps
+
+    def close(self):
+        """Drop the graphs; unmap the peers' buffers if this block owns its
+        exchange (all ranks should be done with the exchange)."""
+        torch.cuda.synchronize(self.device)
+        self._graphs = None
+        if self._owns_exchange:
+            self.x.close()
+
+    STAGES = ("route", "exchange", "dispatch", "experts", "return_wait", "unpack")
+
+    def launches_per_step(self, T: int) -> int:
+        return self.x.launches_per_step(T)
 
     def _issue(self, x: torch.Tensor, residual: Optional[torch.Tensor], out: torch.Tensor, par: int,
                events=None) -> None:
@@ -262,47 +321,49 @@ class PeerExpertParallelMoE(nn.Module):
                 events[i].record()
 
         mark(0)
+        X = self.x
         T = x.shape[0]
         H, E, k, I = self.H, self.E, self.k, self.I
         lib, pt = self._lib, ops._ptr
         s = torch.cuda.current_stream(self.device).cuda_stream
         # router + permutation of the local tokens (one launch at prefill sizes)
         _C.check(lib.qmoe_route_permute(pt(x), pt(self.router_weight), pt(self.router_bias), T, H, E, k, 1,
-                                        pt(self.topk_idx), pt(self.topk_w), pt(self.hist), pt(self.counts),
-                                        pt(self.offsets), pt(self.row_token), pt(self.row_w), pt(self.slot_row),
-                                        pt(self.perm_tiles), None, None, None, 0, pt(self.route_barrier), s),
+                                        pt(X.topk_idx), pt(X.topk_w), pt(X.hist), pt(X.counts),
+                                        pt(X.offsets), pt(X.row_token), pt(X.row_w), pt(X.slot_row),
+                                        pt(X.perm_tiles), None, None, None, 0, pt(X.route_barrier), s),
                  "qmoe_route_permute")
         mark(1)
         _C.check(lib.qmoe_ep_exchange_counts(
-            pt(self.counts), pt(self.peer["ctrl"]), pt(self.ctrl), self.rank, self.world, E, self.e_local,
-            par, 0, pt(self.dest_base), pt(self.tiles), self.max_tiles, pt(self.recv_rows), self.cap,
-            pt(self.done), self.max_tiles + 2, s), "qmoe_ep_exchange_counts")
+            pt(X.counts), pt(X.peer["ctrl"]), pt(X.ctrl), self.rank, self.world, E, self.e_local,
+            par, 0, pt(X.dest_base), pt(X.tiles), X.max_tiles, pt(X.recv_rows), X.cap,
+            pt(X.done), X.max_tiles + 2, s), "qmoe_ep_exchange_counts")
         mark(2)
         _C.check(lib.qmoe_ep_dispatch(
-            pt(x), pt(self.topk_idx), pt(self.topk_w), pt(self.slot_row), pt(self.offsets), pt(self.dest_base),
-            pt(self.peer["recv_x"]), pt(self.peer["recv_meta"]), T, k, H, self.e_local, self.rank, par,
-            self.cap, s), "qmoe_ep_dispatch")
-        _C.check(lib.qmoe_ep_signal_wait(pt(self.peer["ctrl"]), pt(self.ctrl), self.world, E, self.rank, par, 1,
+            pt(x), pt(X.topk_idx), pt(X.topk_w), pt(X.slot_row), pt(X.offsets), pt(X.dest_base),
+            pt(X.peer["recv_x"]), pt(X.peer["recv_meta"]), T, k, H, self.e_local, self.rank, par,
+            X.cap, s), "qmoe_ep_dispatch")
+        _C.check(lib.qmoe_ep_signal_wait(pt(X.peer["ctrl"]), pt(X.ctrl), self.world, E, self.rank, par, 1,
                                          0, s), "qmoe_ep_signal_wait")
         mark(3)
-        recv_x = self.recv_x[par * self.cap:(par + 1) * self.cap]
+        recv_x = X.recv_x[par * X.cap:(par + 1) * X.cap]
         # gate/up + down in one persistent kernel; its down epilogue stores
         # each weighted row into the source rank's return buffer
         _C.check(lib.qmoe_moe_experts_return(
-            pt(recv_x), pt(self.local.gate_up), pt(self.local.down), pt(self.tiles), self.max_tiles,
-            pt(self.recv_meta[par * self.cap:]), pt(self.peer["ret"]), par * self.ret_rows, self.ret_rows,
-            self.world, self.cap, H, I, self.e_local, pt(self.act), pt(self.done), s), "qmoe_moe_experts_return")
+            pt(recv_x), pt(self.local.gate_up), pt(self.local.down), pt(X.tiles), X.max_tiles,
+            pt(X.recv_meta[par * X.cap:]), pt(X.peer["ret"]), par * X.ret_rows, X.ret_rows,
+            self.world, X.cap, H, I, self.e_local, pt(X.act), pt(X.done), s), "qmoe_moe_experts_return")
         mark(4)
-        _C.check(lib.qmoe_ep_signal_wait(pt(self.peer["ctrl"]), pt(self.ctrl), self.world, E, self.rank, par, 2,
+        _C.check(lib.qmoe_ep_signal_wait(pt(X.peer["ctrl"]), pt(X.ctrl), self.world, E, self.rank, par, 2,
                                          0, s), "qmoe_ep_signal_wait")
         mark(5)
-        y_back = self.ret[par * self.ret_rows:par * self.ret_rows + T * k]
+        y_back = X.ret[par * X.ret_rows:par * X.ret_rows + T * k]
         _C.check(lib.qmoe_ep_unpack(pt(y_back), None, pt(residual), T, H, k, T * k, pt(out), s),
                  "qmoe_ep_unpack")
         mark(6)
 
     def forward(self, hidden_states: torch.Tensor, residual: Optional[torch.Tensor] = None,
                 events=None) -> torch.Tensor:
+        """out = MoE(hidden_states) [+ residual], in the input's shape (bf16)."""
         shape = hidden_states.shape
         x = hidden_states.reshape(-1, self.H).to(torch.bfloat16).contiguous()
         T = x.shape[0]
@@ -310,36 +371,47 @@ class PeerExpertParallelMoE(nn.Module):
             raise ValueError(f"{T} tokens exceed max_tokens={self.max_tokens} of the EP buffers")
         res = None if residual is None else residual.reshape(-1, self.H).to(torch.bfloat16).contiguous()
         out = torch.empty((T, self.H), dtype=torch.bfloat16, device=self.device)
-        self.steps += 1
-        self._issue(x, res, out, self.steps & 1, events)
+        self.x.steps += 1
+        self._issue(x, res, out, self.x.steps & 1, events)
         return out.reshape(shape)
 
     def capture(self, hidden_states: torch.Tensor, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """Record one CUDA graph per parity over static copies of the inputs;
-        returns the static output that every ``replay`` overwrites.  Every
-        rank captures with the same shapes (no kernel runs during capture)."""
-        x = hidden_states.reshape(-1, self.H).to(torch.bfloat16).contiguous().clone()
+        """Record one CUDA graph per parity, each over its own static copies
+        of the inputs and its own output, so a caller can upload the next
+        step's input (``static_input()``) and download the last step's output
+        while a step runs.  Returns the output of the next replay.  Every rank
+        captures with the same shapes (no kernel runs during capture)."""
+        x = hidden_states.reshape(-1, self.H).to(torch.bfloat16).contiguous()
         T = x.shape[0]
-        res = None if residual is None else residual.reshape(-1, self.H).to(torch.bfloat16).contiguous().clone()
-        out = torch.empty((T, self.H), dtype=torch.bfloat16, device=self.device)
-        graphs = []
+        res = None if residual is None else residual.reshape(-1, self.H).to(torch.bfloat16).contiguous()
+        graphs, static = [], []
         for par in (0, 1):
+            xs = x.clone()
+            rs = None if res is None else res.clone()
+            out = torch.empty((T, self.H), dtype=torch.bfloat16, device=self.device)
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
-                self._issue(x, res, out, par)
+                self._issue(xs, rs, out, par)
             graphs.append(g)
+            static.append((xs, rs, out))
         self._graphs = tuple(graphs)
-        self._static = (x, res, out)
-        return out
+        self._static = tuple(static)
+        return self._static[(self.x.steps + 1) & 1][2]
 
     def replay(self) -> torch.Tensor:
-        """Run the next step from the captured graphs (inputs: the static
-        buffers ``capture`` returned alongside, ``static_input()``)."""
+        """Run the next step from the captured graphs; returns that step's
+        output buffer (overwritten again two steps later)."""
         if self._graphs is None:
             raise RuntimeError("capture() first")
-        self.steps += 1
-        self._graphs[self.steps & 1].replay()
-        return self._static[2]
+        self.x.steps += 1
+        par = self.x.steps & 1
+        self._graphs[par].replay()
+        return self._static[par][2]
 
-    def static_input(self) -> torch.Tensor:
-        return self._static[0]
+    def static_input(self, ahead: int = 1) -> torch.Tensor:
+        """The static input buffer the ``ahead``-th next ``replay`` reads
+        (1: the next one)."""
+        return self._static[(self.x.steps + ahead) & 1][0]
+
+    def static_output(self, ahead: int = 1) -> torch.Tensor:
+        return self._static[(self.x.steps + ahead) & 1][2]

@@ -5,7 +5,13 @@ token embedding -> ``num_hidden_layers`` decoder layers -> final RMSNorm ->
 LM head, with the embedding lookup and the LM head on this library's kernels
 (they replace the reference's NKI embedding and LM-head kernels,
 qwen_with_nki.py:1541-1578 and 1766-1805).  ``forward`` is the eager module
-path (host-side cache lengths, any number of new tokens).
+path (host-side cache lengths, any number of new tokens); a prefill can ask
+for the last position's logits only (``last_only``), as a serving prefill
+does.  ``Qwen3MoeModel.expert_parallel`` builds the same random-init model
+with every layer's MoE block expert-parallel over a process group (config 3:
+attention data-parallel, each rank holding its own sequences and E/P
+experts of every layer; the reference's EP option is qwen_with_nki.py:
+9870-9876 with the EP-aware MoE at 8148-8271).
 
 ``DecodeSession`` runs B sequences one token per step with static shapes:
 positions, cache lengths and the next tokens live on the device and advance
@@ -24,7 +30,7 @@ from . import ops
 from .attention import KVCache
 from .config import Qwen3MoeConfig
 from .decoder import Qwen3MoeDecoderLayer
-from .moe import MoEPlan
+from .moe import MoEPlan, MoEWeights, WorkspacePool
 
 
 class Qwen3MoeModel:
@@ -45,6 +51,65 @@ class Qwen3MoeModel:
         g.manual_seed(seed * 1000 + 3)
         self.norm = (1.0 + 0.1 * torch.randn(H, generator=g, device=self.device)).float().contiguous()
         self.lm_head = normal_bf16_device(seed * 1000 + 2, (V, H), std, self.device)
+        self.exchange = None
+        self._share_workspace()
+
+    def _share_workspace(self) -> None:
+        # the layers run one after another on one stream: one MoE workspace
+        pool = WorkspacePool()
+        for layer in self.layers:
+            if hasattr(layer.mlp, "workspace_pool"):
+                layer.mlp.workspace_pool = pool
+
+    @classmethod
+    def expert_parallel(cls, cfg: Qwen3MoeConfig, max_tokens: int, group=None, num_layers: Optional[int] = None,
+                        vocab_size: Optional[int] = None, device="cuda", seed: int = 0,
+                        std: float = 0.02) -> "Qwen3MoeModel":
+        """The model ``Qwen3MoeModel(cfg, num_layers, vocab_size, device,
+        seed, std)`` would build (identical weights), with each layer's MoE
+        block expert-parallel over ``group``: this rank keeps every layer's
+        router and its E/P experts [r*E/P, (r+1)*E/P); attention, norms,
+        embedding and LM head are replicated.  All blocks share one
+        ``PeerEPExchange`` sized for ``max_tokens`` local tokens per call.
+        Collective over ``group``; every rank must then run the same layers
+        in the same order.  ``close()`` unmaps the peers' buffers."""
+        import torch.distributed as dist
+
+        from .ep import PeerEPExchange, PeerExpertParallelMoE
+        from .synth import normal_bf16_device
+
+        m = cls.__new__(cls)
+        m.cfg = cfg
+        m.device = torch.device(device)
+        L = cfg.num_hidden_layers if num_layers is None else num_layers
+        V = cfg.vocab_size if vocab_size is None else vocab_size
+        H, E = cfg.hidden_size, cfg.num_experts
+        m.vocab_size = V
+        m.embed = normal_bf16_device(seed * 1000 + 1, (V, H), std, m.device)
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        el = E // world
+        with torch.cuda.device(m.device):
+            m.exchange = PeerEPExchange(cfg, max_tokens, group=group, device=m.device)
+        m.layers = []
+        for l in range(L):
+            s = seed * 1000 + 10 + l
+            full = MoEWeights.random(cfg, s, m.device)
+            local = MoEWeights(full.router, full.gate_up[rank * el:(rank + 1) * el].clone(),
+                               full.down[rank * el:(rank + 1) * el].clone())
+            del full
+            blk = PeerExpertParallelMoE(cfg, local.router, local, exchange=m.exchange)
+            m.layers.append(Qwen3MoeDecoderLayer(cfg, layer_idx=l, device=m.device, seed=s, mlp=blk))
+        g = torch.Generator(device=m.device)
+        g.manual_seed(seed * 1000 + 3)
+        m.norm = (1.0 + 0.1 * torch.randn(H, generator=g, device=m.device)).float().contiguous()
+        m.lm_head = normal_bf16_device(seed * 1000 + 2, (V, H), std, m.device)
+        return m
+
+    def close(self) -> None:
+        """Unmap the expert-parallel exchange's peer buffers (EP models)."""
+        if self.exchange is not None:
+            self.exchange.close()
+            self.exchange = None
 
     @classmethod
     def from_parts(cls, cfg: Qwen3MoeConfig, embed: torch.Tensor, layers: List[Qwen3MoeDecoderLayer],
@@ -60,20 +125,38 @@ class Qwen3MoeModel:
         m.layers = list(layers)
         m.norm = norm
         m.lm_head = lm_head
+        m.exchange = None
+        m._share_workspace()
         return m
 
     def new_caches(self, n_slots: int, max_seq: int) -> List[KVCache]:
         return [layer.self_attn.new_cache(n_slots, max_seq) for layer in self.layers]
 
-    def forward(self, input_ids: torch.Tensor, past_key_values: Optional[List[KVCache]] = None):
-        """input_ids (B, S) -> (logits (B, S, V) bf16, caches); the eager path
-        through the decoder-layer modules."""
+    def hidden_states(self, input_ids: torch.Tensor, past_key_values: Optional[List[KVCache]] = None,
+                      num_layers: Optional[int] = None, timer=None):
+        """input_ids (B, S) -> (hidden states (B, S, H) bf16 after the first
+        ``num_layers`` layers (all by default), caches).  ``timer``: an
+        ``attention.StageTimer`` given to every layer."""
         B, S = input_ids.shape
         H = self.cfg.hidden_size
         caches = past_key_values if past_key_values is not None else self.new_caches(B, S)
         x = ops.embedding(input_ids.reshape(-1).to(torch.int32).contiguous(), self.embed).reshape(B, S, H)
-        for layer, cache in zip(self.layers, caches):
-            x = layer(x, past_key_value=cache)[0]
+        n = len(self.layers) if num_layers is None else num_layers
+        for layer, cache in zip(self.layers[:n], caches):
+            x = layer(x, past_key_value=cache, timer=timer)[0]
+        return x, caches
+
+    def forward(self, input_ids: torch.Tensor, past_key_values: Optional[List[KVCache]] = None,
+                last_only: bool = False):
+        """input_ids (B, S) -> (logits (B, S, V) bf16, caches); the eager path
+        through the decoder-layer modules.  ``last_only``: logits of each
+        sequence's last position only, (B, 1, V)."""
+        B, S = input_ids.shape
+        H = self.cfg.hidden_size
+        x, caches = self.hidden_states(input_ids, past_key_values)
+        if last_only:
+            x = x[:, -1:].contiguous()
+            S = 1
         h = ops.rmsnorm(x.reshape(B * S, H), self.norm, self.cfg.rms_norm_eps)
         logits = ops.linear(h, self.lm_head)
         return logits.reshape(B, S, self.vocab_size), caches

@@ -76,8 +76,28 @@ class MoEWeights:
                           block.experts.down_proj.detach().to(**bf).contiguous())
 
 
+class WorkspacePool:
+    """One growing device byte buffer shared by MoE blocks that run one after
+    another on one stream (the layers of a decoder stack): a 16,384-token
+    prefill needs ~0.9 GB of workspace per call, which 48 blocks need not
+    hold each.  Blocks that may run concurrently on different streams must
+    not share a pool."""
+
+    def __init__(self):
+        self.buf: Optional[torch.Tensor] = None
+
+    def get(self, nbytes: int, device) -> torch.Tensor:
+        if self.buf is None or self.buf.numel() < nbytes or self.buf.device != torch.device(device):
+            self.buf = None
+            self.buf = torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+        return self.buf
+
+
 class Qwen3MoeSparseMoeBlock(nn.Module):
-    """Routed-expert MoE of Qwen3 (no shared experts, qwen.py:253-255)."""
+    """Routed-expert MoE of Qwen3 (no shared experts, qwen.py:253-255).
+
+    ``workspace_pool`` (a ``WorkspacePool``, optional) supplies the forward's
+    device workspace; without one the block keeps its own."""
 
     def __init__(self, cfg: Qwen3MoeConfig, weights: Optional[MoEWeights] = None, device="cuda",
                  seed: int = 0, return_router_logits: bool = False, return_expert_index: bool = False):
@@ -93,20 +113,26 @@ class Qwen3MoeSparseMoeBlock(nn.Module):
         self.down = nn.Parameter(w.down, requires_grad=False)
         self.router_bias: Optional[torch.Tensor] = None
         self._workspace: Optional[torch.Tensor] = None
+        self.workspace_pool: Optional[WorkspacePool] = None
 
     @property
     def weights(self) -> MoEWeights:
         return MoEWeights(self.router_weight.data, self.gate_up.data, self.down.data)
 
+    def _ws(self, nbytes: int, device) -> torch.Tensor:
+        if self.workspace_pool is not None:
+            return self.workspace_pool.get(nbytes, device)
+        if self._workspace is None or self._workspace.numel() < nbytes or self._workspace.device != device:
+            self._workspace = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device)
+        return self._workspace
+
     def _moe(self, x2d: torch.Tensor, residual: Optional[torch.Tensor] = None):
         T, H = x2d.shape
         ws = ops.moe_forward_workspace_size(T, H, self.cfg.num_experts, self.top_k,
                                             self.cfg.moe_intermediate_size)
-        if self._workspace is None or self._workspace.numel() < ws or self._workspace.device != x2d.device:
-            self._workspace = torch.empty(max(ws, 1), dtype=torch.uint8, device=x2d.device)
         return ops.moe_forward(x2d, self.router_weight, self.gate_up, self.down, self.top_k,
                                normalize=self.normalize, residual=residual, bias=self.router_bias,
-                               workspace=self._workspace, return_routing=True)
+                               workspace=self._ws(ws, x2d.device), return_routing=True)
 
     def _block(self, x2d: torch.Tensor, residual: torch.Tensor, norm_weight: torch.Tensor, eps: float,
                moe_in_out: Optional[torch.Tensor] = None, residual_out: Optional[torch.Tensor] = None):
@@ -114,11 +140,10 @@ class Qwen3MoeSparseMoeBlock(nn.Module):
         T, H = x2d.shape
         ws = ops.moe_block_forward_workspace_size(T, H, self.cfg.num_experts, self.top_k,
                                                   self.cfg.moe_intermediate_size)
-        if self._workspace is None or self._workspace.numel() < ws or self._workspace.device != x2d.device:
-            self._workspace = torch.empty(max(ws, 1), dtype=torch.uint8, device=x2d.device)
         return ops.moe_block_forward(x2d, residual, norm_weight, eps, self.router_weight, self.gate_up, self.down,
                                      self.top_k, normalize=self.normalize, bias=self.router_bias,
-                                     workspace=self._workspace, moe_in_out=moe_in_out, residual_out=residual_out)
+                                     workspace=self._ws(ws, x2d.device), moe_in_out=moe_in_out,
+                                     residual_out=residual_out)
 
     def forward(self, hidden_states: torch.Tensor, padding_mask: Optional[torch.Tensor] = None):
         shape = hidden_states.shape

@@ -119,3 +119,56 @@ def test_ep_nccl_matches_single_gpu_oracle(tmp_path):
     for r in range(world):
         errs = np.load(tmp_path / f"ep{r}.npy")
         assert np.all(errs <= MAX_REL), f"rank {r}: {errs}"
+
+
+def _ep_model_worker(rank, world, port, out_dir):
+    sys.path[:0] = [REPO, HERE]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    from nki_moe_7013_b200 import _C
+    from nki_moe_7013_b200.config import Qwen3MoeConfig
+    from nki_moe_7013_b200.model import Qwen3MoeModel
+
+    cfg = Qwen3MoeConfig()
+    B, S, V = 2, 96, 4096  # per rank: 2 sequences of 96 tokens (192 tokens through each EP block)
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    ids = torch.randint(0, V, (world * B, S), generator=g, device=dev, dtype=torch.int32)
+    mine = ids[rank * B:(rank + 1) * B].contiguous()
+    ep = Qwen3MoeModel.expert_parallel(cfg, B * S, num_layers=2, vocab_size=V, device=dev, seed=7)
+    h_ep, _ = ep.hidden_states(mine)
+    logits_ep, _ = ep.forward(mine, last_only=True)
+    torch.cuda.synchronize()
+    code = _C.device_error()
+    dist.barrier()
+    ep.close()
+    ref = Qwen3MoeModel(cfg, num_layers=2, vocab_size=V, device=dev, seed=7)
+    h_ref, _ = ref.hidden_states(mine)
+    logits_ref, _ = ref.forward(mine, last_only=True)
+    errs = [max_rel_err(to_f32_np(h_ep), to_f32_np(h_ref)), max_rel_err(to_f32_np(logits_ep), to_f32_np(logits_ref)),
+            float(code)]
+    np.save(os.path.join(out_dir, f"epm{rank}.npy"), np.array(errs))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_ep_model_matches_single_gpu_model(tmp_path):
+    """Config-3 path: a 2-layer model whose MoE blocks are expert-parallel over
+    2 (or 4) GPUs, attention data-parallel, against the same seeded model on
+    one GPU (hidden states and last-position logits of each rank's sequences)."""
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("expert parallelism needs 2+ GPUs on the box")
+    world = 2 if n < 4 else 4
+    mp.start_processes(_ep_model_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       start_method="spawn", join=True)
+    for r in range(world):
+        errs = np.load(tmp_path / f"epm{r}.npy")
+        assert errs[2] == 0, f"rank {r}: device error {errs[2]}"
+        assert np.all(errs[:2] <= MAX_REL), f"rank {r}: {errs}"
