@@ -379,29 +379,36 @@ QMOE_API int qmoe_qk_norm_rope(const void* qkv, const int32_t* positions, const 
  * K5  causal GQA flash-prefill over the KV cache (NxDI attention with the
  * flash kernel of qwen.py:25-28, 49).  B sequences of S queries each:
  *   q (B*S, nh, 128) bf16; query i of sequence b sits at position
- *   q_start[b] + i and attends to cache rows 0 .. q_start[b] + i of slot
- *   cache_slot[b] (NULL: slot b) of the (n_slots, nkv, max_seq, 128) caches.
- *   out (B*S, nh*128) bf16.  scale is usually 1/sqrt(128).  A q_start or
- *   slot outside the cache makes the CTA record QMOE device error 4 and
- *   write nothing.
+ *   q_start[b] + i and attends to cache rows kv_start[b] .. q_start[b] + i
+ *   of slot cache_slot[b] (NULL: slot b) of the (n_slots, nkv, max_seq, 128)
+ *   caches.  kv_start (NULL: all 0) marks left padding: cache rows before it
+ *   are never attended to, and a query before it (a padding position) gets
+ *   a zero output row.  out (B*S, nh*128) bf16.  scale is usually
+ *   1/sqrt(128).  A q_start or slot outside the cache makes the CTA record
+ *   QMOE device error 4 and write nothing.
+ *   Kernel: tcgen05 flash attention, 128 queries of one head per CTA, S and
+ *   P.V accumulated in TMEM, K/V tiles by TMA (192 KB of shared memory: one
+ *   CTA per SM).
  * ---------------------------------------------------------------------- */
 QMOE_API int qmoe_attention_prefill(const void* q, const void* k_cache, const void* v_cache,
-                                    const int32_t* q_start, const int32_t* cache_slot, int64_t B,
-                                    int64_t S, int64_t nh, int64_t nkv, int64_t head_dim,
-                                    int64_t n_slots, int64_t max_seq, float scale, void* out,
-                                    void* stream);
+                                    const int32_t* q_start, const int32_t* cache_slot,
+                                    const int32_t* kv_start, int64_t B, int64_t S, int64_t nh,
+                                    int64_t nkv, int64_t head_dim, int64_t n_slots,
+                                    int64_t max_seq, float scale, void* out, void* stream);
 
 /* ------------------------------------------------------------------------
  * K5  split-KV flash-decode: one query per sequence (q (B, nh, 128) bf16)
- * against kv_len[b] cache rows; 8 query heads per KV head.  max_len bounds
- * kv_len; nsplit from qmoe_attention_decode_splits; workspace of
+ * against cache rows kv_start[b] .. kv_len[b]-1 (kv_start NULL: from 0;
+ * rows before it are left padding); 8 query heads per KV head.  max_len
+ * bounds kv_len; nsplit from qmoe_attention_decode_splits; workspace of
  * qmoe_attention_decode_workspace_size bytes (256-byte aligned).
  * out (B, nh*128) bf16.
  * ---------------------------------------------------------------------- */
 QMOE_API int64_t qmoe_attention_decode_splits(int64_t B, int64_t nkv, int64_t max_len);
 QMOE_API size_t qmoe_attention_decode_workspace_size(int64_t B, int64_t nh, int64_t nsplit);
 QMOE_API int qmoe_attention_decode(const void* q, const void* k_cache, const void* v_cache,
-                                   const int32_t* kv_len, const int32_t* cache_slot, int64_t B,
+                                   const int32_t* kv_len, const int32_t* cache_slot,
+                                   const int32_t* kv_start, int64_t B,
                                    int64_t nh, int64_t nkv, int64_t head_dim, int64_t n_slots,
                                    int64_t max_seq, int64_t max_len, int64_t nsplit, float scale,
                                    void* out, void* workspace, size_t workspace_bytes, void* stream);

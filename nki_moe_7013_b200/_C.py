@@ -49,11 +49,11 @@ _SIGNATURES = {
     "qmoe_rmsnorm": (I32, [P, I32, P, P, I64, I64, ctypes.c_float, P, I32, P, P]),
     "qmoe_qk_norm_rope": (I32, [P, P, P, P, P, P, I64, I64, I64, I64, ctypes.c_float, P, P, P, I64,
                                 I64, P]),
-    "qmoe_attention_prefill": (I32, [P, P, P, P, P, I64, I64, I64, I64, I64, I64, I64,
+    "qmoe_attention_prefill": (I32, [P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, I64,
                                      ctypes.c_float, P, P]),
     "qmoe_attention_decode_splits": (I64, [I64, I64, I64]),
     "qmoe_attention_decode_workspace_size": (SZ, [I64, I64, I64]),
-    "qmoe_attention_decode": (I32, [P, P, P, P, P, I64, I64, I64, I64, I64, I64, I64, I64,
+    "qmoe_attention_decode": (I32, [P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, I64, I64,
                                     ctypes.c_float, P, P, SZ, P]),
     "qmoe_routing_histogram": (I32, [P, I64, I64, I64, P, P]),
     "qmoe_ep_pack": (I32, [P, P, P, I64, I64, I64, I64, I64, P, P, P, P, P, P, P]),

@@ -1,11 +1,21 @@
 """Attention sub-layer of the Qwen3-MoE decoder layer (secondary target).
 
 ``Qwen3MoeAttention.forward(hidden_states, position_ids=None,
-past_key_value=None) -> (out, present_kv)`` mirrors NxDI's
-NeuronQwen3MoEAttention (qwen.py:313-341): fused QKV projection, per-head
-q/k RMSNorm (qwen.py:333-335), RoPE theta 1e6 (qwen.py:315-319), causal GQA
-over a KV cache, o_proj.  Positions follow the HF convention (the position of
-a new token = the number of tokens already cached).
+past_key_value=None, attention_mask=None) -> (out, present_kv)`` mirrors
+NxDI's NeuronQwen3MoEAttention (qwen.py:313-341): fused QKV projection,
+per-head q/k RMSNorm (qwen.py:333-335), RoPE theta 1e6 (qwen.py:315-319),
+causal GQA over a KV cache, o_proj.  Positions follow the HF convention (the
+position of a new token = the number of tokens already cached).
+
+``attention_mask``: causal masking is built in; a 2D key-padding mask
+(batch, cached + new tokens; 1 = token, 0 = padding) with LEFT padding only
+(each row zeros then ones) is honoured -- the form NxDI / HF batch prefill
+uses.  The cache remembers each slot's padding, so later decode steps keep
+masking it.  RoPE is applied at the cache row; HF applies it at the
+pad-shifted position (cumsum(mask) - 1), and since the rotary score depends
+only on the difference of two positions the attention output is the same up
+to fp32 rounding.  Padding query rows get a zero attention output.  Any
+other mask (holes, right padding, 4D) is refused with a ValueError.
 
 All kernels come from the CUDA library: tcgen05 projections (``ops.linear``),
 the fused QK-norm + RoPE + cache append, flash-prefill / split-KV
@@ -38,6 +48,7 @@ class KVCache:
         self.k = torch.zeros((n_slots, nkv, max_seq, head_dim), dtype=torch.bfloat16, device=device)
         self.v = torch.zeros_like(self.k)
         self.lengths: List[int] = [0] * n_slots
+        self.pad: List[int] = [0] * n_slots      # leading padding rows per slot
         self.max_seq = max_seq
 
     @property
@@ -51,12 +62,34 @@ class KVCache:
         self.k[:, :, :length].normal_(generator=g)
         self.v[:, :, :length].normal_(generator=g)
         self.lengths = [length] * self.n_slots
+        self.pad = [0] * self.n_slots
         return self
 
     def reset(self) -> "KVCache":
         """Empty every slot (the contents are overwritten by the next appends)."""
         self.lengths = [0] * self.n_slots
+        self.pad = [0] * self.n_slots
         return self
+
+
+def left_padding(attention_mask: Optional[torch.Tensor], B: int, S: int, L0: List[int]) -> Optional[List[int]]:
+    """Leading padding count per sequence of a 2D key-padding mask (B, L0+S),
+    1 = token, 0 = padding; None for no mask.  Refuses every other mask."""
+    if attention_mask is None:
+        return None
+    if attention_mask.dim() != 2:
+        raise ValueError("attention_mask: only a 2D (batch, cached + new tokens) key-padding mask is "
+                         "supported; causal masking is built in")
+    m = (attention_mask != 0).to(torch.int32).cpu()
+    if m.shape[0] != B:
+        raise ValueError(f"attention_mask has {m.shape[0]} rows for a batch of {B}")
+    L = m.shape[1]
+    if any(l0 + S != L for l0 in L0):
+        raise ValueError(f"attention_mask must cover each sequence's cached and new tokens ({L0[0] + S}), "
+                         f"got {L}")
+    if L > 1 and not bool(torch.all(m[:, 1:] >= m[:, :-1])):
+        raise ValueError("attention_mask: only left padding (zeros before ones in every row) is supported")
+    return [int(v) for v in (L - m.sum(1)).tolist()]
 
 
 @dataclass
@@ -146,7 +179,8 @@ class Qwen3MoeAttention(nn.Module):
         return KVCache(n_slots, self.cfg.num_key_value_heads, max_seq, self.cfg.head_dim, self.w.wqkv.device)
 
     def forward(self, hidden_states: torch.Tensor, position_ids: Optional[torch.Tensor] = None,
-                past_key_value: Optional[KVCache] = None, timer: Optional[StageTimer] = None):
+                past_key_value: Optional[KVCache] = None, timer: Optional[StageTimer] = None,
+                attention_mask: Optional[torch.Tensor] = None):
         cfg = self.cfg
         B, S, H = hidden_states.shape
         dev = hidden_states.device
@@ -157,14 +191,22 @@ class Qwen3MoeAttention(nn.Module):
         if max(L0) + S > cache.max_seq:
             raise ValueError("KV cache is full")
         x2d = hidden_states.reshape(B * S, H).to(torch.bfloat16).contiguous()
-        if position_ids is None:
-            pos = (torch.tensor(L0, dtype=torch.int32).unsqueeze(1) + torch.arange(S, dtype=torch.int32))
-        else:
-            pos = position_ids.reshape(B, S).to(torch.int32).cpu()
-            if not torch.equal(pos[:, 0], torch.tensor(L0, dtype=torch.int32)) or (
-                    S > 1 and not torch.all(pos[:, 1:] - pos[:, :-1] == 1)):
-                raise ValueError("position_ids must continue each sequence's cache contiguously")
+        pads = left_padding(attention_mask, B, S, L0)
+        if pads is not None:
+            for b in range(B):
+                cache.pad[b] = pads[b]
+        pad_now = cache.pad[:B]
+        pos = (torch.tensor(L0, dtype=torch.int32).unsqueeze(1) + torch.arange(S, dtype=torch.int32))
+        if position_ids is not None:
+            given = position_ids.reshape(B, S).to(torch.int32).cpu()
+            shifted = pos - torch.tensor(pad_now, dtype=torch.int32).unsqueeze(1)
+            real = shifted >= 0  # padding tokens may carry any position
+            if not (torch.equal(given, pos) or bool(torch.all((given == shifted) | ~real))):
+                raise ValueError("position_ids must continue each sequence's cache contiguously (or, with left "
+                                 "padding, count from the first real token)")
         positions = pos.reshape(-1).to(dev, non_blocking=True)
+        kv_start = (torch.tensor(pad_now, dtype=torch.int32).to(dev, non_blocking=True)
+                    if any(pad_now) else None)
         slots = torch.arange(B, dtype=torch.int32).repeat_interleave(S).to(dev, non_blocking=True)
         with stage(timer, "qkv_proj"):
             qkv = ops.linear(x2d, self.w.wqkv)
@@ -176,11 +218,11 @@ class Qwen3MoeAttention(nn.Module):
             kv_len = torch.tensor([l + 1 for l in L0], dtype=torch.int32).to(dev, non_blocking=True)
             with stage(timer, "attention"):
                 attn = ops.attention_decode(q, cache.k, cache.v, kv_len, max(L0) + 1,
-                                            workspace=self._decode_ws)
+                                            workspace=self._decode_ws, kv_start=kv_start)
         else:
             q_start = torch.tensor(L0, dtype=torch.int32).to(dev, non_blocking=True)
             with stage(timer, "attention"):
-                attn = ops.attention_prefill(q, cache.k, cache.v, q_start, B, S)
+                attn = ops.attention_prefill(q, cache.k, cache.v, q_start, B, S, kv_start=kv_start)
         for b in range(B):
             cache.lengths[b] += S
         with stage(timer, "o_proj"):

@@ -1,15 +1,16 @@
-// K5: GQA attention over a KV cache -- flash-prefill (causal) and split-KV
-// flash-decode, head_dim 128, bf16 in / fp32 softmax and accumulation.
+// K5 decode: split-KV flash-decode GQA attention over a KV cache, head_dim
+// 128, bf16 in / fp32 softmax and accumulation.  (The prefill kernel is the
+// tcgen05 one in flash_prefill.cuh.)
 //
-// Reference semantics: NxDI NeuronAttentionBase with GQA (qwen.py:313-341;
-// flash kernel imported at qwen.py:25-28, 49), i.e.
-//   out_h = softmax(q_h K_g^T / sqrt(D) + causal) V_g,  g = h / (nh / nkv).
-// Query i of a sequence sits at absolute position q_start + i and attends to
-// cache positions 0 .. q_start + i.
+// Reference semantics: NxDI NeuronAttentionBase with GQA (qwen.py:313-341),
+// i.e. out_h = softmax(q_h K_g^T / sqrt(D)) V_g, g = h / (nh / nkv), over
+// cache positions kv_start[b] .. kv_len[b]-1 of sequence b (kv_start: left
+// padding, 0 without it).
 //
-// Both kernels use the warp-level bf16 MMA (m16n8k16, fp32 accumulate) on
-// tiles staged in shared memory with cp.async and read with ldmatrix;
-// rows are padded to 136 elements so ldmatrix is bank-conflict free.
+// Decode reads each cache byte once and is bound by HBM: the warp-level bf16
+// MMA (m16n8k16, fp32 accumulate) on tiles staged in shared memory with
+// cp.async and read with ldmatrix is enough for its 8 query rows per KV
+// head; rows are padded to 136 elements so ldmatrix is bank-conflict free.
 //
 // KV cache layout: (slots, nkv, max_seq, 128) bf16 for K and for V.
 #pragma once
@@ -21,7 +22,6 @@ namespace qmoe {
 constexpr int kAttnD = 128;
 constexpr int kAttnPad = kAttnD + 8;   // smem row stride in elements (272 B)
 constexpr int kAttnThreads = 128;      // 4 warps
-constexpr int kAttnBQ = 64;            // prefill: queries per CTA (16 per warp)
 constexpr int kAttnBK = 64;            // keys per smem tile
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -76,48 +76,6 @@ __device__ __forceinline__ void load_kv_tile(__nv_bfloat16* dst, const __nv_bflo
   }
 }
 
-// S (16 x 64) = Q_frag (16 x 128) . K_tile^T for one warp.
-__device__ __forceinline__ void qk_tile(float (&s)[8][4], const uint32_t (&qa)[8][4],
-                                        const __nv_bfloat16* ks, int lane) {
-#pragma unroll
-  for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) s[nt][i] = 0.f;
-  const int mi = lane >> 3, r = lane & 7;
-#pragma unroll
-  for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-    for (int kk = 0; kk < 8; kk += 2) {
-      uint32_t b[4];
-      ldsm_x4(b, ks + (nt * 8 + r) * kAttnPad + kk * 16 + mi * 8);
-      mma_bf16_16816(s[nt], qa[kk], b[0], b[1]);
-      mma_bf16_16816(s[nt], qa[kk + 1], b[2], b[3]);
-    }
-  }
-}
-
-// O (16 x 128) += P (16 x 64, as C fragments) . V_tile for one warp.
-__device__ __forceinline__ void pv_tile(float (&o)[16][4], const float (&p)[8][4],
-                                        const __nv_bfloat16* vs, int lane) {
-  const int mi = lane >> 3, r = lane & 7;
-#pragma unroll
-  for (int kk = 0; kk < 4; ++kk) {  // 16 keys per k-step
-    uint32_t a[4];
-    a[0] = pack_bf16x2(p[2 * kk][0], p[2 * kk][1]);
-    a[1] = pack_bf16x2(p[2 * kk][2], p[2 * kk][3]);
-    a[2] = pack_bf16x2(p[2 * kk + 1][0], p[2 * kk + 1][1]);
-    a[3] = pack_bf16x2(p[2 * kk + 1][2], p[2 * kk + 1][3]);
-#pragma unroll
-    for (int dn = 0; dn < 16; dn += 2) {
-      uint32_t b[4];
-      // matrices: keys +0..7 / +8..15 of this k-step, dims dn*8 / (dn+1)*8
-      ldsm_x4_trans(b, vs + (kk * 16 + (mi & 1) * 8 + r) * kAttnPad + (dn + (mi >> 1)) * 8);
-      mma_bf16_16816(o[dn], a, b[0], b[1]);
-      mma_bf16_16816(o[dn + 1], a, b[2], b[3]);
-    }
-  }
-}
-
 // Online-softmax update of one warp's 16 rows with a new S tile (already
 // scaled to log2 units and masked with -inf).  Rows g and g+8 of the lane.
 __device__ __forceinline__ void softmax_update(float (&s)[8][4], float (&m)[2], float (&l)[2],
@@ -147,106 +105,6 @@ __device__ __forceinline__ void softmax_update(float (&s)[8][4], float (&m)[2], 
     }
     l[h] += sum;
     m[h] = m_new;
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Prefill: grid (ceil(S/64), nh, B).  q (B*S, nh, 128); out (B*S, nh*128).
-// ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(kAttnThreads)
-    attn_prefill_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k_cache,
-                        const __nv_bfloat16* __restrict__ v_cache, const int32_t* __restrict__ q_start,
-                        const int32_t* __restrict__ cache_slot, int S, int nh, int nkv, int max_seq,
-                        int n_slots, float scale_log2, __nv_bfloat16* __restrict__ out) {
-  extern __shared__ __align__(16) uint8_t attn_smem[];
-  __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(attn_smem);    // [64][136]
-  __nv_bfloat16* ks = qs + kAttnBQ * kAttnPad;                          // [2][64][136]
-  __nv_bfloat16* vs = ks + 2 * kAttnBK * kAttnPad;                      // [2][64][136]
-  const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * kAttnBQ;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, tq = lane & 3;
-  const int kvh = h / (nh / nkv);
-  const int L0 = q_start[b];
-  const int slot = cache_slot ? cache_slot[b] : b;
-  if (L0 < 0 || L0 + S > max_seq || slot < 0 || slot >= n_slots) {  // block-uniform
-    if (threadIdx.x == 0) record_device_error(kDevErrBadIndex);
-    return;
-  }
-  const int nq = min(kAttnBQ, S - q0);
-  const int n_keys = L0 + q0 + nq;  // keys visible to the last query of the tile
-  const __nv_bfloat16* kh = k_cache + (size_t(slot) * nkv + kvh) * max_seq * kAttnD;
-  const __nv_bfloat16* vh = v_cache + (size_t(slot) * nkv + kvh) * max_seq * kAttnD;
-
-  // Q tile
-  for (int i = threadIdx.x; i < kAttnBQ * 16; i += kAttnThreads) {
-    const int r = i >> 4, c = (i & 15) * 8;
-    const bool ok = r < nq;
-    cp_async16(qs + r * kAttnPad + c, q + ((size_t(b) * S + q0 + (ok ? r : 0)) * nh + h) * kAttnD + c, ok);
-  }
-  load_kv_tile(ks, kh, 0, n_keys);
-  load_kv_tile(vs, vh, 0, n_keys);
-  cp_async_commit();
-  const int n_tiles = (n_keys + kAttnBK - 1) / kAttnBK;
-
-  float o[16][4];
-#pragma unroll
-  for (int dn = 0; dn < 16; ++dn)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) o[dn][i] = 0.f;
-  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-  uint32_t qa[8][4];
-  const int pos_g = L0 + q0 + warp * 16 + g;  // absolute position of row g (row g+8: +8)
-
-  for (int j = 0; j < n_tiles; ++j) {
-    const int buf = j & 1;
-    if (j + 1 < n_tiles) {
-      load_kv_tile(ks + (buf ^ 1) * kAttnBK * kAttnPad, kh, (j + 1) * kAttnBK, n_keys);
-      load_kv_tile(vs + (buf ^ 1) * kAttnBK * kAttnPad, vh, (j + 1) * kAttnBK, n_keys);
-      cp_async_commit();
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
-    if (j == 0) {
-      const int mi = lane >> 3, r = lane & 7;
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        ldsm_x4(qa[kk], qs + (warp * 16 + (mi & 1) * 8 + r) * kAttnPad + kk * 16 + (mi >> 1) * 8);
-    }
-    const int key0 = j * kAttnBK;
-    // skip tiles entirely above this warp's last row
-    if (key0 <= L0 + q0 + warp * 16 + 15) {
-      float s[8][4];
-      qk_tile(s, qa, ks + buf * kAttnBK * kAttnPad, lane);
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int key = key0 + nt * 8 + 2 * tq + (i & 1);
-          const int pos = pos_g + (i >> 1) * 8;
-          s[nt][i] = key <= pos ? s[nt][i] * scale_log2 : -INFINITY;
-        }
-      softmax_update(s, m, l, o);
-      pv_tile(o, s, vs + buf * kAttnBK * kAttnPad, lane);
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int h2 = 0; h2 < 2; ++h2) {
-    l[h2] += __shfl_xor_sync(0xFFFFFFFFu, l[h2], 1);
-    l[h2] += __shfl_xor_sync(0xFFFFFFFFu, l[h2], 2);
-  }
-#pragma unroll
-  for (int h2 = 0; h2 < 2; ++h2) {
-    const int r = warp * 16 + g + h2 * 8;
-    if (r >= nq) continue;
-    const float inv = l[h2] > 0.f ? 1.f / l[h2] : 0.f;
-    __nv_bfloat16* orow = out + ((size_t(b) * S + q0 + r) * nh + h) * kAttnD;
-#pragma unroll
-    for (int dn = 0; dn < 16; ++dn)
-      *reinterpret_cast<uint32_t*>(orow + dn * 8 + 2 * tq) =
-          pack_bf16x2(o[dn][2 * h2] * inv, o[dn][2 * h2 + 1] * inv);
   }
 }
 
@@ -281,9 +139,9 @@ __device__ __forceinline__ void qk_slice16(float (&s)[2][4], const uint32_t (&qa
 __global__ void __launch_bounds__(kAttnThreads)
     attn_decode_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k_cache,
                        const __nv_bfloat16* __restrict__ v_cache, const int32_t* __restrict__ kv_len,
-                       const int32_t* __restrict__ cache_slot, int nh, int nkv, int max_seq, int n_slots,
-                       int chunk, float scale_log2, float* __restrict__ part_o,
-                       float* __restrict__ part_ml) {
+                       const int32_t* __restrict__ cache_slot, const int32_t* __restrict__ kv_start, int nh,
+                       int nkv, int max_seq, int n_slots, int chunk, float scale_log2,
+                       float* __restrict__ part_o, float* __restrict__ part_ml) {
   extern __shared__ __align__(16) uint8_t attn_smem[];
   __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(attn_smem);  // [2][64][136]
   __nv_bfloat16* vs = ks + 2 * kAttnBK * kAttnPad;                   // [2][64][136]
@@ -302,6 +160,7 @@ __global__ void __launch_bounds__(kAttnThreads)
     L = 0;  // still write an empty partial so the combine stays defined
   }
   const int slot = bad ? 0 : slot_raw;
+  const int kv0 = kv_start ? kv_start[b] : 0;  // keys before it are padding
   const int k_begin = split * chunk;
   const int k_end = min(L, k_begin + chunk);
   const __nv_bfloat16* kh = k_cache + (size_t(slot) * nkv + kvh) * max_seq * kAttnD;
@@ -354,7 +213,7 @@ __global__ void __launch_bounds__(kAttnThreads)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int key = key0 + nt * 8 + 2 * tq + (i & 1);
-          s[nt][i] = (nt < 2 && key < k_end) ? s2[nt][i] * scale_log2 : -INFINITY;
+          s[nt][i] = (nt < 2 && key < k_end && key >= kv0) ? s2[nt][i] * scale_log2 : -INFINITY;
         }
       softmax_update(s, m, l, o);
       // P . V over this slice's 16 keys (one k-step)

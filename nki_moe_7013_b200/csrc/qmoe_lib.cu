@@ -14,6 +14,7 @@
 #include <utility>
 
 #include "attention.cuh"
+#include "flash_prefill.cuh"
 #include "blockwise.cuh"
 #include "common.cuh"
 #include "ep.cuh"
@@ -127,6 +128,26 @@ static int make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t inner, ui
     return set_error(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for %llux%llu box %ux%u",
                      int(r), (unsigned long long)outer, (unsigned long long)inner, box_outer,
                      box_inner);
+  return QMOE_OK;
+}
+
+// 3D bf16 tensor map: dims (d0 inner, d1, d2), byte strides of d1 and d2,
+// 128-byte swizzle, box (b0, b1, b2).  Out-of-range coordinates read as zero.
+static int make_tmap_bf16_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                             uint64_t stride1, uint64_t stride2, uint32_t b0, uint32_t b1, uint32_t b2) {
+  EncodeTiledFn enc = nullptr;
+  int st = get_encode(&enc);
+  if (st != QMOE_OK) return st;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {stride1, stride2};
+  cuuint32_t box[3] = {b0, b1, b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(QMOE_ERR_CUDA, "cuTensorMapEncodeTiled (3D) failed (%d) for %llux%llux%llu", int(r),
+                     (unsigned long long)d2, (unsigned long long)d1, (unsigned long long)d0);
   return QMOE_OK;
 }
 
@@ -1199,31 +1220,50 @@ int qmoe_qk_norm_rope(const void* qkv, const int32_t* positions, const int32_t* 
 }
 
 int qmoe_attention_prefill(const void* q, const void* k_cache, const void* v_cache,
-                           const int32_t* q_start, const int32_t* cache_slot, int64_t B, int64_t S,
-                           int64_t nh, int64_t nkv, int64_t head_dim, int64_t n_slots,
+                           const int32_t* q_start, const int32_t* cache_slot, const int32_t* kv_start, int64_t B,
+                           int64_t S, int64_t nh, int64_t nkv, int64_t head_dim, int64_t n_slots,
                            int64_t max_seq, float scale, void* out, void* stream) {
   QMOE_REQUIRE(q && k_cache && v_cache && q_start && out, QMOE_ERR_INVALID_ARGUMENT,
                "attention_prefill: null pointer");
-  QMOE_REQUIRE(head_dim == qmoe::kAttnD, QMOE_ERR_UNSUPPORTED_SHAPE, "attention_prefill: head_dim must be 128");
+  QMOE_REQUIRE(head_dim == qmoe::kFaD, QMOE_ERR_UNSUPPORTED_SHAPE, "attention_prefill: head_dim must be 128");
   QMOE_REQUIRE(nh > 0 && nkv > 0 && nh % nkv == 0 && nh <= 65535, QMOE_ERR_INVALID_ARGUMENT,
                "attention_prefill: bad heads");
-  QMOE_REQUIRE(B >= 0 && B <= 65535 && S >= 0 && S <= max_seq && max_seq > 0 && n_slots > 0 &&
-                   (cache_slot || B <= n_slots),
+  QMOE_REQUIRE(B >= 0 && B <= 65535 && S >= 0 && S <= max_seq && max_seq > 0 && max_seq < (int64_t(1) << 30) &&
+                   n_slots > 0 && n_slots * nkv < (int64_t(1) << 31) && (cache_slot || B <= n_slots),
                QMOE_ERR_INVALID_ARGUMENT, "attention_prefill: bad sizes");
+  const int64_t n_qtiles = (S + qmoe::kFaRows - 1) / qmoe::kFaRows;
+  QMOE_REQUIRE(B * S < (int64_t(1) << 31) && n_qtiles * nh * B < (int64_t(1) << 31), QMOE_ERR_INVALID_ARGUMENT,
+               "attention_prefill: too many queries");
   QMOE_REQUIRE(aligned16(q) && aligned16(k_cache) && aligned16(v_cache) && aligned16(out),
                QMOE_ERR_MISALIGNED, "attention_prefill: pointers must be 16-byte aligned");
   DeviceInfo* d = nullptr;
   QMOE_CHECK(device_info(&d));
   if (B == 0 || S == 0) return QMOE_OK;
-  const int smem = (qmoe::kAttnBQ + 4 * qmoe::kAttnBK) * qmoe::kAttnPad * 2;
-  QMOE_CHECK(set_smem(qmoe::attn_prefill_kernel, smem));
-  const dim3 grid(static_cast<unsigned>((S + qmoe::kAttnBQ - 1) / qmoe::kAttnBQ), static_cast<unsigned>(nh),
-                  static_cast<unsigned>(B));
-  qmoe::attn_prefill_kernel<<<grid, qmoe::kAttnThreads, smem, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k_cache),
-      static_cast<const __nv_bfloat16*>(v_cache), q_start, cache_slot, int(S), int(nh), int(nkv),
-      int(max_seq), int(n_slots), scale * 1.4426950408889634f, static_cast<__nv_bfloat16*>(out));
-  return check_launch("attn_prefill_kernel");
+  // q (B*S, nh, 128): tokens outermost; caches (slots*nkv, max_seq, 128)
+  CUtensorMap tq, tk, tv;
+  QMOE_CHECK(make_tmap_bf16_3d(&tq, q, 128, uint64_t(nh), uint64_t(B * S), 256, uint64_t(nh) * 256, 64, 1,
+                               qmoe::kFaRows));
+  QMOE_CHECK(make_tmap_bf16_3d(&tk, k_cache, 128, uint64_t(max_seq), uint64_t(n_slots * nkv), 256,
+                               uint64_t(max_seq) * 256, 64, qmoe::kFaRows, 1));
+  QMOE_CHECK(make_tmap_bf16_3d(&tv, v_cache, 128, uint64_t(max_seq), uint64_t(n_slots * nkv), 256,
+                               uint64_t(max_seq) * 256, 64, qmoe::kFaRows, 1));
+  qmoe::FlashPrefillArgs args{};
+  args.q_start = q_start;
+  args.cache_slot = cache_slot;
+  args.kv_start = kv_start;
+  args.out = static_cast<__nv_bfloat16*>(out);
+  args.S = int(S);
+  args.nh = int(nh);
+  args.nkv = int(nkv);
+  args.max_seq = int(max_seq);
+  args.n_slots = int(n_slots);
+  args.B = int(B);
+  args.n_qtiles = int(n_qtiles);
+  args.scale_log2 = scale * 1.4426950408889634f;
+  QMOE_CHECK(set_smem(qmoe::flash_prefill_kernel, qmoe::kFaSmemBytes));
+  return launch_kernel(qmoe::flash_prefill_kernel, dim3(unsigned(n_qtiles * nh * B)), dim3(qmoe::kFaThreads),
+                       size_t(qmoe::kFaSmemBytes), static_cast<cudaStream_t>(stream), true, "flash_prefill_kernel",
+                       tq, tk, tv, args);
 }
 
 int64_t qmoe_attention_decode_splits(int64_t B, int64_t nkv, int64_t max_len) {
@@ -1241,7 +1281,8 @@ size_t qmoe_attention_decode_workspace_size(int64_t B, int64_t nh, int64_t nspli
 }
 
 int qmoe_attention_decode(const void* q, const void* k_cache, const void* v_cache,
-                          const int32_t* kv_len, const int32_t* cache_slot, int64_t B, int64_t nh,
+                          const int32_t* kv_len, const int32_t* cache_slot, const int32_t* kv_start, int64_t B,
+                          int64_t nh,
                           int64_t nkv, int64_t head_dim, int64_t n_slots, int64_t max_seq, int64_t max_len,
                           int64_t nsplit, float scale, void* out, void* workspace,
                           size_t workspace_bytes, void* stream) {
@@ -1271,7 +1312,7 @@ int qmoe_attention_decode(const void* q, const void* k_cache, const void* v_cach
   QMOE_CHECK(launch_kernel(qmoe::attn_decode_kernel, grid, dim3(qmoe::kAttnThreads), size_t(smem), s, true,
                            "attn_decode_kernel", static_cast<const __nv_bfloat16*>(q),
                            static_cast<const __nv_bfloat16*>(k_cache), static_cast<const __nv_bfloat16*>(v_cache),
-                           kv_len, cache_slot, int(nh), int(nkv), int(max_seq), int(n_slots), int(chunk),
+                           kv_len, cache_slot, kv_start, int(nh), int(nkv), int(max_seq), int(n_slots), int(chunk),
                            scale * 1.4426950408889634f, part_o, part_ml));
   return launch_kernel(qmoe::attn_decode_combine_kernel, dim3(unsigned((B * nh + 7) / 8)), dim3(256), 0, s, true,
                        "attn_decode_combine_kernel", static_cast<const float*>(part_o),

@@ -17,8 +17,9 @@ the final residual add are one library call (``qmoe_moe_block_forward``).  With 
 ``padding_mask`` the masked MoE output needs the norm's outputs first, so
 that path runs the add & norm and the MoE block as two calls.  RoPE is applied
 inside the attention kernels, so cos/sin caches are returned as None.
-``attention_mask`` is accepted for signature compatibility; attention is
-causal over each sequence's cache.
+``attention_mask``: attention is causal over each sequence's cache; a 2D
+left-padding key mask (batch, cached + new tokens) is honoured and every
+other mask is refused (``attention.Qwen3MoeAttention``).
 
 ``mlp``: the MoE module to use instead of a single-GPU
 ``Qwen3MoeSparseMoeBlock`` -- e.g. an expert-parallel
@@ -70,7 +71,8 @@ class Qwen3MoeDecoderLayer(nn.Module):
         x2d = hidden_states.reshape(B * S, H).to(torch.bfloat16).contiguous()
         with stage(timer, "input_norm"):
             h = ops.rmsnorm(x2d, self.input_layernorm, eps)
-        a, present = self.self_attn(h.reshape(B, S, H), position_ids, past_key_value, timer=timer)
+        a, present = self.self_attn(h.reshape(B, S, H), position_ids, past_key_value, timer=timer,
+                                    attention_mask=attention_mask)
         a2d = a.reshape(B * S, H)
         if getattr(self.mlp, "expert_parallel", False):
             with stage(timer, "post_norm"):

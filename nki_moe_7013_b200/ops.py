@@ -502,10 +502,14 @@ def qk_norm_rope(qkv: torch.Tensor, positions: torch.Tensor, q_norm_w: torch.Ten
 
 def attention_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                       q_start: torch.Tensor, B: int, S: int, scale: Optional[float] = None,
-                      cache_slot: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Causal GQA over the cache; q (B*S, nh, 128) -> (B*S, nh*128) bf16."""
+                      cache_slot: Optional[torch.Tensor] = None,
+                      kv_start: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Causal GQA over the cache; q (B*S, nh, 128) -> (B*S, nh*128) bf16.
+    ``kv_start`` (B,) int32: left padding, cache rows before it are masked."""
     _need(q, "q", torch.bfloat16, 3)
     _need(q_start, "q_start", torch.int32, 1)
+    if kv_start is not None:
+        _need(kv_start, "kv_start", torch.int32, 1)
     nh, hd = q.shape[1], q.shape[2]
     nkv, max_seq = k_cache.shape[1], k_cache.shape[2]
     scale = hd ** -0.5 if scale is None else scale
@@ -513,7 +517,8 @@ def attention_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Ten
     out = torch.empty((B * S, nh * hd), dtype=torch.bfloat16, device=dev)
     with torch.cuda.device(dev):
         _C.check(_C.lib().qmoe_attention_prefill(
-            _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(q_start), _ptr(cache_slot), B, S, nh, nkv, hd,
+            _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(q_start), _ptr(cache_slot), _ptr(kv_start), B, S, nh,
+            nkv, hd,
             k_cache.shape[0], max_seq, float(scale), _ptr(out), _stream(dev)), "qmoe_attention_prefill")
     return out
 
@@ -521,10 +526,14 @@ def attention_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Ten
 def attention_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                      kv_len: torch.Tensor, max_len: int, scale: Optional[float] = None,
                      cache_slot: Optional[torch.Tensor] = None,
-                     workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Split-KV flash-decode; q (B, nh, 128) -> (B, nh*128) bf16."""
+                     workspace: Optional[torch.Tensor] = None,
+                     kv_start: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Split-KV flash-decode; q (B, nh, 128) -> (B, nh*128) bf16.
+    ``kv_start`` (B,) int32: left padding, cache rows before it are masked."""
     _need(q, "q", torch.bfloat16, 3)
     _need(kv_len, "kv_len", torch.int32, 1)
+    if kv_start is not None:
+        _need(kv_start, "kv_start", torch.int32, 1)
     B, nh, hd = q.shape
     nkv, max_seq = k_cache.shape[1], k_cache.shape[2]
     scale = hd ** -0.5 if scale is None else scale
@@ -537,7 +546,7 @@ def attention_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     out = torch.empty((B, nh * hd), dtype=torch.bfloat16, device=dev)
     with torch.cuda.device(dev):
         _C.check(lib.qmoe_attention_decode(
-            _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(kv_len), _ptr(cache_slot), B, nh, nkv, hd,
+            _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(kv_len), _ptr(cache_slot), _ptr(kv_start), B, nh, nkv, hd,
             k_cache.shape[0], max_seq, max_len, nsplit, float(scale), _ptr(out), _ptr(workspace),
             workspace.numel(), _stream(dev)),
             "qmoe_attention_decode")

@@ -293,18 +293,23 @@ def rope_apply(x: np.ndarray, pos: np.ndarray, inv_freq: np.ndarray) -> np.ndarr
 
 
 def attention_layer(x_bf16, wqkv_bf16, wo_bf16, q_norm_w, k_norm_w, nh: int, nkv: int, eps: float,
-                    theta: float, B: int, S: int, k_cache=None, v_cache=None, L0=None):
+                    theta: float, B: int, S: int, k_cache=None, v_cache=None, L0=None, pad=None):
     """Attention sub-layer on B sequences of S new tokens each.
 
     ``k_cache``/``v_cache`` (B, nkv, Lmax, hd) fp32 hold bf16 values of earlier
     tokens (rows [0, L0[b])).  Intermediates are rounded to bf16 where the GPU
     path stores bf16 (qkv, normalised+rotated q/k, attention output).
+    ``pad`` (per sequence, HF left padding as given by a 2D attention mask):
+    cache rows [0, pad[b]) are padding -- never attended to -- and, as in HF
+    transformers (position_ids = cumsum(mask) - 1), RoPE rotates the token in
+    cache row c by position c - pad[b]; padding query rows get a zero output.
     Returns (out fp32 (B*S, H) before its bf16 cast, new_k, new_v)."""
     x = bf16_bits_to_f32(as_bf16_bits(x_bf16)).astype(np.float64)
     wqkv = bf16_bits_to_f32(as_bf16_bits(wqkv_bf16)).astype(np.float64)
     wo = bf16_bits_to_f32(as_bf16_bits(wo_bf16)).astype(np.float64)
     hd = 128
     L0 = np.zeros(B, np.int64) if L0 is None else np.asarray(L0, np.int64)
+    pad = np.zeros(B, np.int64) if pad is None else np.asarray(pad, np.int64)
     qkv = round_to_bf16((x @ wqkv.T).astype(np.float32)).astype(np.float64)
     qkv = qkv.reshape(B, S, nh + 2 * nkv, hd)
     inv_freq = rope_inv_freq(hd, theta)
@@ -313,7 +318,8 @@ def attention_layer(x_bf16, wqkv_bf16, wo_bf16, q_norm_w, k_norm_w, nh: int, nkv
     new_k = np.zeros((B, nkv, Lmax, hd))
     new_v = np.zeros((B, nkv, Lmax, hd))
     for b in range(B):
-        pos = L0[b] + np.arange(S)
+        pos = L0[b] + np.arange(S)           # cache rows of the new tokens
+        rpos = np.maximum(pos - pad[b], 0)   # their RoPE positions
         q = qkv[b, :, :nh]
         k = qkv[b, :, nh:nh + nkv]
         v = qkv[b, :, nh + nkv:]
@@ -322,8 +328,8 @@ def attention_layer(x_bf16, wqkv_bf16, wo_bf16, q_norm_w, k_norm_w, nh: int, nkv
             var = np.mean(t * t, axis=-1, keepdims=True)
             return t / np.sqrt(var + eps) * np.asarray(w, np.float64)
 
-        q = rope_apply(head_norm(q, q_norm_w).transpose(1, 0, 2), pos, inv_freq)  # (nh, S, hd)
-        k = rope_apply(head_norm(k, k_norm_w).transpose(1, 0, 2), pos, inv_freq)  # (nkv, S, hd)
+        q = rope_apply(head_norm(q, q_norm_w).transpose(1, 0, 2), rpos, inv_freq)  # (nh, S, hd)
+        k = rope_apply(head_norm(k, k_norm_w).transpose(1, 0, 2), rpos, inv_freq)  # (nkv, S, hd)
         q = round_to_bf16(q.astype(np.float32)).astype(np.float64)
         k = round_to_bf16(k.astype(np.float32)).astype(np.float64)
         v = v.transpose(1, 0, 2)
@@ -336,11 +342,13 @@ def attention_layer(x_bf16, wqkv_bf16, wo_bf16, q_norm_w, k_norm_w, nh: int, nkv
         for h in range(nh):
             g = h // (nh // nkv)
             sc = q[h] @ new_k[b, g, :L].T / np.sqrt(hd)  # (S, L)
-            mask = np.arange(L)[None, :] > pos[:, None]
+            keys = np.arange(L)[None, :]
+            mask = (keys > pos[:, None]) | (keys < pad[b])
             sc = np.where(mask, -np.inf, sc)
-            sc = sc - sc.max(axis=1, keepdims=True)
+            live = ~np.all(mask, axis=1)          # padding queries see no key
+            sc = np.where(live[:, None], sc - np.where(live, sc.max(axis=1), 0.0)[:, None], -np.inf)
             p = np.exp(sc)
-            p /= p.sum(axis=1, keepdims=True)
+            p /= np.where(live, p.sum(axis=1), 1.0)[:, None]
             out_heads[b, :, h] = p @ new_v[b, g, :L]
     attn = round_to_bf16(out_heads.reshape(B * S, nh * hd).astype(np.float32)).astype(np.float64)
     return (attn @ wo.T).astype(np.float32), new_k, new_v

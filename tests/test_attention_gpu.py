@@ -222,3 +222,143 @@ def test_decoder_layer_cfg1_vs_oracle(cuda_dev, oracle):
     same = np.all(np.sort(idx_ref, 1) == np.sort(inter["topk_idx"], 1), axis=1)
     assert same.mean() > 0.97
     assert max_rel_err(to_f32_np(out).reshape(B * S, H)[same], full[same]) <= MAX_REL
+
+
+def _attention_ref_fp32(q, k_cache, v_cache, q_start, slots, pads, B, S, nh, nkv, scale):
+    """Plain torch fp32 causal GQA over the cache (the reference of the flash
+    kernels): rows [pad, q_start + i] of each sequence's slot; padding
+    queries (no visible key) give zeros."""
+    out = torch.zeros(B * S, nh, 128, dtype=torch.float32, device=q.device)
+    for b in range(B):
+        L = q_start[b] + S
+        kb = k_cache[slots[b], :, :L].float().repeat_interleave(nh // nkv, dim=0)  # (nh, L, 128)
+        vb = v_cache[slots[b], :, :L].float().repeat_interleave(nh // nkv, dim=0)
+        qb = q[b * S:(b + 1) * S].float().transpose(0, 1)                           # (nh, S, 128)
+        sc = torch.matmul(qb, kb.transpose(1, 2)) * scale                          # (nh, S, L)
+        keys = torch.arange(L, device=q.device)[None, :]
+        pos = (q_start[b] + torch.arange(S, device=q.device))[:, None]
+        masked = (keys > pos) | (keys < pads[b])
+        sc = sc.masked_fill(masked[None], float("-inf"))
+        live = ~masked.all(dim=1)
+        p = torch.softmax(sc.masked_fill(~live[None, :, None], 0.0), dim=-1) * live[None, :, None]
+        out[b * S:(b + 1) * S] = torch.matmul(p, vb).transpose(0, 1)
+    return out.reshape(B * S, nh * 128)
+
+
+# (B, S, L0, pads, slots): config-1 shape, partial query / key tiles, a
+# continuing cache, left padding (inside a tile, exactly one tile, a whole
+# sequence of padding), speculative-verify shape, slot remapping, config-3
+# sequence length
+@pytest.mark.parametrize("B,S,L0,pads,slots", [
+    (1, 1024, 0, None, None),
+    (2, 300, 37, [0, 50], None),
+    (3, 129, 0, [0, 0, 128], None),
+    (1, 5, 4096, None, None),
+    (2, 64, 0, [0, 64], None),
+    (4, 200, 100, [10, 0, 150, 299], [3, 1, 0, 2]),
+    (1, 2048, 0, None, None),
+])
+def test_flash_prefill_kernel(cuda_dev, B, S, L0, pads, slots):
+    """tcgen05 flash prefill against a plain torch fp32 reference.  Cache rows
+    past each sequence's end hold NaN: no key past the last query may reach
+    the output, not even through a zero probability."""
+    from nki_moe_7013_b200 import _C, ops
+
+    nh, nkv, hd = 32, 4, 128
+    n_slots = B if slots is None else max(slots) + 1
+    max_seq = L0 + S + 40
+    g = torch.Generator(device=cuda_dev)
+    g.manual_seed(B * 1000 + S)
+    k = torch.randn(n_slots, nkv, max_seq, hd, generator=g, device=cuda_dev).to(torch.bfloat16)
+    v = torch.randn(n_slots, nkv, max_seq, hd, generator=g, device=cuda_dev).to(torch.bfloat16)
+    k[:, :, L0 + S:] = float("nan")
+    v[:, :, L0 + S:] = float("nan")
+    q = torch.randn(B * S, nh, hd, generator=g, device=cuda_dev).to(torch.bfloat16)
+    q_start = torch.full((B,), L0, dtype=torch.int32, device=cuda_dev)
+    slot_t = None if slots is None else torch.tensor(slots, dtype=torch.int32, device=cuda_dev)
+    kv_start = None if pads is None else torch.tensor(pads, dtype=torch.int32, device=cuda_dev)
+    out = ops.attention_prefill(q, k, v, q_start, B, S, cache_slot=slot_t, kv_start=kv_start)
+    torch.cuda.synchronize()
+    assert _C.device_error() == 0
+    ref = _attention_ref_fp32(q, k, v, [L0] * B, slots or list(range(B)), pads or [0] * B, B, S, nh, nkv,
+                              hd ** -0.5)
+    o = out.float()
+    assert torch.isfinite(o).all()
+    err = float((o - ref).abs().max() / ref.abs().max())
+    assert err <= MAX_REL, f"flash prefill max rel err {err:.3e}"
+    if pads is not None:  # padding queries: exact zeros
+        for b in range(B):
+            n_pad_q = max(0, min(S, pads[b] - L0))
+            if n_pad_q:
+                assert torch.count_nonzero(out[b * S:b * S + n_pad_q]).item() == 0
+
+
+def test_flash_prefill_run_to_run_identical(cuda_dev):
+    from nki_moe_7013_b200 import ops
+
+    nh, nkv, hd, B, S = 32, 4, 128, 2, 333
+    k = torch.randn(B, nkv, S, hd, device=cuda_dev).to(torch.bfloat16)
+    v = torch.randn(B, nkv, S, hd, device=cuda_dev).to(torch.bfloat16)
+    q = torch.randn(B * S, nh, hd, device=cuda_dev).to(torch.bfloat16)
+    qs = torch.zeros(B, dtype=torch.int32, device=cuda_dev)
+    a = ops.attention_prefill(q, k, v, qs, B, S)
+    b = ops.attention_prefill(q, k, v, qs, B, S)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("B,L,pads", [(2, 300, [0, 120]), (3, 4096, [4000, 0, 1])])
+def test_flash_decode_left_padding(cuda_dev, B, L, pads):
+    from nki_moe_7013_b200 import _C, ops
+
+    nh, nkv, hd = 32, 4, 128
+    k = torch.randn(B, nkv, L + 8, hd, device=cuda_dev).to(torch.bfloat16)
+    v = torch.randn(B, nkv, L + 8, hd, device=cuda_dev).to(torch.bfloat16)
+    q = torch.randn(B, nh, hd, device=cuda_dev).to(torch.bfloat16)
+    lens = torch.full((B,), L, dtype=torch.int32, device=cuda_dev)
+    out = ops.attention_decode(q, k, v, lens, L, kv_start=torch.tensor(pads, dtype=torch.int32, device=cuda_dev))
+    torch.cuda.synchronize()
+    assert _C.device_error() == 0
+    ref = _attention_ref_fp32(q, k, v, [L - 1] * B, list(range(B)), pads, B, 1, nh, nkv, hd ** -0.5)
+    assert max_rel_err(to_f32_np(out), ref.cpu().numpy()) <= MAX_REL
+
+
+def test_attention_left_padding_vs_oracle(cuda_dev, oracle):
+    """A left-padded batch through the module (2D attention mask, HF
+    convention), then one decode step on the same cache without a mask:
+    real rows match the oracle's HF semantics (pad keys masked, RoPE at the
+    pad-shifted positions), padding rows are zero."""
+    from nki_moe_7013_b200 import _C
+    from nki_moe_7013_b200.attention import AttnWeights, KVCache, Qwen3MoeAttention
+    from nki_moe_7013_b200.config import Qwen3MoeConfig
+
+    cfg = Qwen3MoeConfig()
+    H, nh, nkv = cfg.hidden_size, cfg.num_attention_heads, cfg.num_key_value_heads
+    B, S, pads = 2, 70, [0, 23]
+    wqkv, wo, qn, kn = _attn_weights(cuda_dev, H, nh, nkv, 77)
+    attn = Qwen3MoeAttention(cfg, AttnWeights(wqkv, wo, qn, kn))
+    cache = KVCache(B, nkv, S + 4, 128, cuda_dev)
+    mask = torch.ones(B, S, dtype=torch.int64)
+    for b, p in enumerate(pads):
+        mask[b, :p] = 0
+    pos = (mask.cumsum(1) - 1).clamp_min(0)
+    x = activations(91, B * S, H, cuda_dev).reshape(B, S, H)
+    out, cache = attn(x, position_ids=pos, past_key_value=cache, attention_mask=mask)
+    torch.cuda.synchronize()
+    assert _C.device_error() == 0 and cache.pad == pads
+    args = dict(nh=nh, nkv=nkv, eps=cfg.rms_norm_eps, theta=cfg.rope_theta)
+    ref, rk, rv = oracle.attention_layer(x.reshape(B * S, H).cpu(), wqkv.cpu(), wo.cpu(), qn.cpu().numpy(),
+                                         kn.cpu().numpy(), B=B, S=S, pad=pads, **args)
+    o = to_f32_np(out).reshape(B, S, H)
+    r = ref.reshape(B, S, H)
+    for b, p in enumerate(pads):
+        assert max_rel_err(o[b, p:], r[b, p:]) <= MAX_REL
+        assert np.count_nonzero(o[b, :p]) == 0
+    # one decode step: the cache keeps masking the padding
+    x1 = activations(92, B, H, cuda_dev).reshape(B, 1, H)
+    out1, cache = attn(x1, past_key_value=cache)
+    torch.cuda.synchronize()
+    ref1, _, _ = oracle.attention_layer(x1.reshape(B, H).cpu(), wqkv.cpu(), wo.cpu(), qn.cpu().numpy(),
+                                        kn.cpu().numpy(), B=B, S=1, k_cache=rk, v_cache=rv, L0=[S] * B,
+                                        pad=pads, **args)
+    assert max_rel_err(to_f32_np(out1).reshape(B, H), ref1) <= MAX_REL
