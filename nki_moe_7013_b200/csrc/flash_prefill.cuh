@@ -7,34 +7,37 @@
 // cache positions kv_start[b] .. q_start[b] + i (kv_start: left padding,
 // 0 without it).  head_dim 128, bf16 in, fp32 scores / softmax / sums.
 //
-// One CTA = 128 queries (the TMEM lanes) of one (sequence, head); 192
-// threads in three roles:
-//   warp 4  TMA producer: Q once, then K and V tiles of 128 keys into two
-//           stages each (3D tensor maps; the cache's (slot, kv head) is the
-//           outer coordinate, so no load crosses into another head);
-//   warp 5  MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM score
-//           buffers (M=128 queries, N=128 keys, K=128 dims, both operands
-//           K-major), and O_j = P_j V_j into one of two TMEM output buffers
-//           (A = P from shared memory, K-major; B = V straight from its TMA
-//           tile, MN-major: dims are V's contiguous axis);
-//   warps 0-3  softmax: thread r owns query row r (TMEM lane r): row max of
-//           S_j, the running max / sum, P_j = exp2(S_j*scale - max) written
-//           as bf16 into the 128B-swizzled P tile, and the output kept in
-//           fp32 registers: o = (o + O_{j-1}) * exp2(m_{j-1} - m_j).
-// The MMA warp issues S_{j+1} before P_j V_j, so the tensor core computes the
-// next scores while the softmax warps work on the current ones.
+// One CTA = two tiles of 128 queries (A: rows q0..q0+127, B: the next 128)
+// of one (sequence, head), sharing every K / V tile of 128 keys; 320 threads:
+//   warps 0-3  softmax of tile A, warps 4-7 softmax of tile B: thread r of a
+//              group owns query row r (TMEM lane r);
+//   warp 8     TMA producer: Q_A and Q_B once, then K_0, V_0, K_1, V_1, ...
+//              through a pool of three 32 KB slots (3D tensor maps, the
+//              cache's (slot, kv head) as the outer coordinate);
+//   warp 9     MMA issuer (one thread), in the order
+//              S_A(0) S_B(0) | PV_A(0) S_A(1) PV_B(0) S_B(1) | PV_A(1) ...
+//              so the tensor core computes one tile's scores while the other
+//              tile's softmax runs.
+// S_X = Q_X K^T (M=128 queries, N=128 keys, K=128 dims, both K-major) lands
+// in TMEM; O_X += P_X V (A = P_X from shared memory, K-major; B = V straight
+// from its TMA tile, MN-major) accumulates in TMEM across the key tiles.
+// The softmax keeps a per-row running max m and sum l; P = exp2(S*scale - m)
+// in bf16.  When a row's max grows by more than 2^8 the group rescales its O
+// rows in TMEM (load, multiply, store) before releasing P; otherwise m stays
+// (P <= 2^8, exact enough in bf16) and O is never touched by the softmax.
+// A tile's whole score row is read with four TMEM loads and one wait.
 //
-// Shared memory (1024-aligned tiles of 32 KB: two 64-column halves of 128
-// rows x 128 B, 128-byte swizzle): Q | K[2] | V[2] | P = 192 KB, one CTA per
-// SM.  TMEM: 512 columns = S[2] + O[2].
+// Shared memory (1024-aligned 32 KB tiles = two 64-column halves of 128
+// rows x 128 B, 128-byte swizzle): Q_A | Q_B | pool[3] | P_A | P_B = 224 KB,
+// one CTA per SM.  TMEM: S_A | S_B | O_A | O_B = 512 columns.
 //
-// Keys past the end of the tile's last query (the last tile's tail) hold
-// whatever the cache holds there; their scores are masked, and the producer
-// zeroes those V rows in shared memory before the last P V product, so a
-// non-finite value in unused cache rows cannot reach the output (0 * inf).
+// Keys past the last query of the CTA (the last tile's tail) hold whatever
+// the cache holds there; their scores are masked, and the producer zeroes
+// those V rows in shared memory before the last P V products, so a
+// non-finite value in unused cache rows cannot reach a valid output row.
 //
 // Every wait is bounded (kWaitLimitNs): on time-out the role records a
-// device error, raises the CTA's abort flag, the MMA thread drains its
+// device error and raises the CTA's abort flag, the MMA thread drains its
 // outstanding MMAs, the producer waits for its loads in flight, TMEM is
 // freed and the CTA returns without writing its rows.
 #pragma once
@@ -43,21 +46,23 @@
 
 namespace qmoe {
 
-constexpr int kFaRows = 128;                    // queries per CTA = keys per tile
+constexpr int kFaRows = 128;                    // queries per tile = keys per tile
 constexpr int kFaD = 128;                       // head dim
-constexpr int kFaThreads = 192;
+constexpr int kFaThreads = 320;                 // 2 softmax groups, producer, MMA
 constexpr int kFaHalfBytes = kFaRows * 128;     // 128 rows x 64 bf16
 constexpr int kFaTileBytes = 2 * kFaHalfBytes;  // 32 KB
-constexpr int kFaTiles = 6;                     // Q, K[2], V[2], P
-constexpr int kFaBarriers = 20;
+constexpr int kFaPool = 3;                      // K / V slots
+constexpr int kFaTiles = 4 + kFaPool;           // Q_A, Q_B, pool, P_A, P_B
+constexpr int kFaBarriers = 16;
 constexpr int kFaSmemBytes = kFaTiles * kFaTileBytes + 1024 + kFaBarriers * 8 + 16;
+constexpr float kFaRescaleLog2 = 8.f;           // rescale O when a row max grows by more than 2^8
 
 struct FlashPrefillArgs {
   const int32_t* q_start;
   const int32_t* cache_slot;
   const int32_t* kv_start;
   __nv_bfloat16* out;
-  int S, nh, nkv, max_seq, n_slots, B, n_qtiles;
+  int S, nh, nkv, max_seq, n_slots, B, n_pairs;
   float scale_log2;
 };
 
@@ -81,6 +86,43 @@ __device__ __forceinline__ uint64_t make_sw128_desc_mn(uint32_t smem_addr, uint3
   d |= uint64_t(1) << 46;   // sm_100 descriptor version
   d |= uint64_t(2) << 61;   // 128B swizzle
   return d;
+}
+
+// 32 lanes x 32 bit, 32 consecutive columns per thread.
+__device__ __forceinline__ void tmem_ld_x32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st_x32(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // Bounded wait on an mbarrier phase for one thread; on time-out records
@@ -114,35 +156,30 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                          const __grid_constant__ CUtensorMap tm_v, const FlashPrefillArgs a) {
   extern __shared__ uint8_t fa_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fa_smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = smem + kFaTileBytes;       // [2]
-  uint8_t* sV = sK + 2 * kFaTileBytes;     // [2]
-  uint8_t* sP = sV + 2 * kFaTileBytes;
+  uint8_t* sQ = smem;                              // [2]: tiles A, B
+  uint8_t* sPool = smem + 2 * kFaTileBytes;        // [kFaPool]: K_0, V_0, K_1, V_1, ... in rotation
+  uint8_t* sP = sPool + kFaPool * kFaTileBytes;    // [2]: tiles A, B
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kFaTiles * kFaTileBytes);
   uint64_t* q_full = bar + 0;
-  uint64_t* k_full = bar + 1;    // [2]
-  uint64_t* v_full = bar + 3;    // [2]
-  uint64_t* k_empty = bar + 5;   // [2]
-  uint64_t* v_empty = bar + 7;   // [2]
-  uint64_t* s_full = bar + 9;    // [2]
-  uint64_t* s_empty = bar + 11;  // [2]
-  uint64_t* p_full = bar + 13;
-  uint64_t* o_full = bar + 14;   // [2]
-  uint64_t* o_empty = bar + 16;  // [2]
-  uint64_t* v_tail = bar + 18;
-  uint64_t* drain = bar + 19;
+  uint64_t* full = bar + 1;     // [kFaPool]
+  uint64_t* empty = bar + 4;    // [kFaPool]
+  uint64_t* s_full = bar + 7;   // [2] per query tile
+  uint64_t* p_full = bar + 9;   // [2]
+  uint64_t* o_full = bar + 11;  // [2]
+  uint64_t* v_tail = bar + 13;
+  uint64_t* drain = bar + 14;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + kFaBarriers);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  // heaviest query tiles (the latest ones: most keys) first over all heads
-  const int per_tile = a.nh * a.B;
-  const int qt = a.n_qtiles - 1 - int(blockIdx.x) / per_tile;
-  const int rest = int(blockIdx.x) % per_tile;
+  // heaviest tile pairs (the latest queries: most keys) first over all heads
+  const int per_pair = a.nh * a.B;
+  const int pc = a.n_pairs - 1 - int(blockIdx.x) / per_pair;
+  const int rest = int(blockIdx.x) % per_pair;
   const int h = rest % a.nh;
   const int b = rest / a.nh;
-  const int q0 = qt * kFaRows;
+  const int q0 = pc * 2 * kFaRows;
   const int kvh = h / (a.nh / a.nkv);
 
   griddep_wait();
@@ -152,8 +189,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     if (threadIdx.x == 0) record_device_error(kDevErrBadIndex);
     return;
   }
-  const int nq = min(kFaRows, a.S - q0);
-  const int n_keys = L0 + q0 + nq;  // keys visible to the tile's last query
+  const int nq_a = min(kFaRows, a.S - q0);
+  const int nq_b = max(0, min(kFaRows, a.S - q0 - kFaRows));
+  const int n_keys = L0 + q0 + (nq_b > 0 ? kFaRows + nq_b : nq_a);  // keys visible to the last query
   int kv0 = a.kv_start ? a.kv_start[b] : 0;
   kv0 = max(0, min(kv0, L0 + a.S));
   const int j0 = kv0 / kFaRows;
@@ -161,8 +199,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   const size_t out_ld = size_t(a.nh) * kFaD;
   __nv_bfloat16* out_tile = a.out + (size_t(b) * a.S + q0) * out_ld + size_t(h) * kFaD;
   if (n_tiles == 0) {
-    // every query of the tile is a padding position: no visible key, zeros
-    for (int i = threadIdx.x; i < nq * (kFaD / 8); i += blockDim.x)
+    // every query of the pair is a padding position: no visible key, zeros
+    for (int i = threadIdx.x; i < (nq_a + nq_b) * (kFaD / 8); i += blockDim.x)
       reinterpret_cast<uint4*>(out_tile + size_t(i / (kFaD / 8)) * out_ld)[i % (kFaD / 8)] = make_uint4(0, 0, 0, 0);
     return;
   }
@@ -170,17 +208,15 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&k_full[i], 1);
-      mbar_init(&v_full[i], 1);
-      mbar_init(&k_empty[i], 1);
-      mbar_init(&v_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 4);
-      mbar_init(&o_full[i], 1);
-      mbar_init(&o_empty[i], 4);
+    for (int i = 0; i < kFaPool; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
     }
-    mbar_init(p_full, 4);
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(&s_full[g], 1);
+      mbar_init(&p_full[g], 4);
+      mbar_init(&o_full[g], 1);
+    }
     mbar_init(v_tail, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -189,7 +225,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     prefetch_tmap(&tm_k);
     prefetch_tmap(&tm_v);
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -198,44 +234,41 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ---------------- TMA producer ----------------
     const int kv_z = slot * a.nkv + kvh;
-    int issued_k[2] = {0, 0}, issued_v[2] = {0, 0};
+    int issued[kFaPool] = {0, 0, 0};
     bool ok = true;
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, kFaTileBytes);
-      tma_load_3d(sQ, &tm_q, 0, h, b * a.S + q0, q_full);
-      tma_load_3d(sQ + kFaHalfBytes, &tm_q, 64, h, b * a.S + q0, q_full);
-      for (int i = 0; i < n_tiles; ++i) {
-        const int st = i & 1, use = i >> 1;
-        const int key0 = (j0 + i) * kFaRows;
-        if (i >= 2 && !fa_wait(&k_empty[st], (use - 1) & 1, abort_flag, kDevErrWaitTimeoutProducer)) {
+      mbar_arrive_expect_tx(q_full, 2 * kFaTileBytes);
+      for (int g = 0; g < 2; ++g) {
+        const int z = b * a.S + q0 + g * kFaRows;
+        tma_load_3d(sQ + g * kFaTileBytes, &tm_q, 0, h, z, q_full);
+        tma_load_3d(sQ + g * kFaTileBytes + kFaHalfBytes, &tm_q, 64, h, z, q_full);
+      }
+      for (int n = 0; n < 2 * n_tiles; ++n) {  // K_i = item 2i, V_i = item 2i + 1
+        const int sl = n % kFaPool, u = n / kFaPool;
+        if (n >= kFaPool && !fa_wait(&empty[sl], (u - 1) & 1, abort_flag, kDevErrWaitTimeoutProducer)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&k_full[st], kFaTileBytes);
-        tma_load_3d(sK + st * kFaTileBytes, &tm_k, 0, key0, kv_z, &k_full[st]);
-        tma_load_3d(sK + st * kFaTileBytes + kFaHalfBytes, &tm_k, 64, key0, kv_z, &k_full[st]);
-        ++issued_k[st];
-        if (i >= 2 && !fa_wait(&v_empty[st], (use - 1) & 1, abort_flag, kDevErrWaitTimeoutProducer)) {
-          ok = false;
-          break;
-        }
-        mbar_arrive_expect_tx(&v_full[st], kFaTileBytes);
-        tma_load_3d(sV + st * kFaTileBytes, &tm_v, 0, key0, kv_z, &v_full[st]);
-        tma_load_3d(sV + st * kFaTileBytes + kFaHalfBytes, &tm_v, 64, key0, kv_z, &v_full[st]);
-        ++issued_v[st];
+        const int key0 = (j0 + (n >> 1)) * kFaRows;
+        const CUtensorMap* tm = (n & 1) ? &tm_v : &tm_k;
+        uint8_t* dst = sPool + sl * kFaTileBytes;
+        mbar_arrive_expect_tx(&full[sl], kFaTileBytes);
+        tma_load_3d(dst, tm, 0, key0, kv_z, &full[sl]);
+        tma_load_3d(dst + kFaHalfBytes, tm, 64, key0, kv_z, &full[sl]);
+        ++issued[sl];
       }
     }
     ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;
     if (ok && tail) {
-      // zero the V rows of the last tile past the last visible key
-      const int last = n_tiles - 1;
-      const int st = last & 1;
-      if (fa_wait_warp(&v_full[st], (last >> 1) & 1, abort_flag, kDevErrWaitTimeoutProducer)) {
-        const int first = n_keys - (j0 + last) * kFaRows;  // rows [first, 128) are past n_keys
-        uint8_t* vt = sV + st * kFaTileBytes;
+      // zero the last V tile's rows past the last visible key
+      const int n = 2 * n_tiles - 1;
+      const int sl = n % kFaPool;
+      if (fa_wait_warp(&full[sl], (n / kFaPool) & 1, abort_flag, kDevErrWaitTimeoutProducer)) {
+        const int first = n_keys - (j0 + n_tiles - 1) * kFaRows;  // rows [first, 128) lie past n_keys
+        uint8_t* vt = sPool + sl * kFaTileBytes;
         for (int i = first * 8 + lane; i < kFaRows * 8; i += 32) {  // 16-byte chunks of whole rows
           const int r = i >> 3, c = i & 7;
           *reinterpret_cast<uint4*>(vt + r * 128 + c * 16) = make_uint4(0, 0, 0, 0);
@@ -249,58 +282,79 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     if (lane == 0) {
       // loads still in flight land before the CTA can exit
       fa_wait_landed(q_full, 0);
-      for (int st = 0; st < 2; ++st) {
-        if (issued_k[st]) fa_wait_landed(&k_full[st], (issued_k[st] - 1) & 1);
-        if (issued_v[st]) fa_wait_landed(&v_full[st], (issued_v[st] - 1) & 1);
-      }
+      for (int sl = 0; sl < kFaPool; ++sl)
+        if (issued[sl]) fa_wait_landed(&full[sl], (issued[sl] - 1) & 1);
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       const uint32_t idesc_s = make_idesc_bf16(kFaRows, kFaRows);
       const uint32_t idesc_o = make_idesc_bf16(kFaRows, kFaD) | (1u << 16);  // B (V) MN-major
-      const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
-      bool ok = fa_wait(q_full, 0, abort_flag, kDevErrWaitTimeoutMma);
-      for (int i = 0; ok && i <= n_tiles; ++i) {
-        if (i < n_tiles) {
-          const int st = i & 1, use = i >> 1;
-          if (!fa_wait(&k_full[st], use & 1, abort_flag, kDevErrWaitTimeoutMma) ||
-              (i >= 2 && !fa_wait(&s_empty[st], (use - 1) & 1, abort_flag, kDevErrWaitTimeoutMma))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t k_addr = smem_u32(sK + st * kFaTileBytes);
-          const uint32_t d = tmem_base + st * kFaRows;
+      const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP), pool = smem_u32(sPool);
+      auto item_full = [&](int n) {
+        return fa_wait(&full[n % kFaPool], (n / kFaPool) & 1, abort_flag, kDevErrWaitTimeoutMma);
+      };
+      auto issue_s = [&](int g, int i) {  // S_g = Q_g K_i^T
+        const uint32_t k_addr = pool + ((2 * i) % kFaPool) * kFaTileBytes;
+        const uint32_t qa = q_addr + g * kFaTileBytes;
+        const uint32_t d = tmem_base + g * kFaRows;
 #pragma unroll
-          for (int kk = 0; kk < kFaD / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kFaHalfBytes + (kk & 3) * 32;
-            umma_bf16(d, make_sw128_desc(q_addr + off), make_sw128_desc(k_addr + off), idesc_s, kk > 0 ? 1u : 0u);
-          }
-          umma_commit(&s_full[st]);
-          umma_commit(&k_empty[st]);
+        for (int kk = 0; kk < kFaD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kFaHalfBytes + (kk & 3) * 32;
+          umma_bf16(d, make_sw128_desc(qa + off), make_sw128_desc(k_addr + off), idesc_s, kk > 0 ? 1u : 0u);
         }
-        if (i >= 1) {
-          const int pi = i - 1;
-          const int st = pi & 1, use = pi >> 1;
-          if (!fa_wait(p_full, pi & 1, abort_flag, kDevErrWaitTimeoutMma) ||
-              !fa_wait(&v_full[st], use & 1, abort_flag, kDevErrWaitTimeoutMma) ||
-              (tail && pi == n_tiles - 1 && !fa_wait(v_tail, 0, abort_flag, kDevErrWaitTimeoutMma)) ||
-              (pi >= 2 && !fa_wait(&o_empty[st], (use - 1) & 1, abort_flag, kDevErrWaitTimeoutMma))) {
+        umma_commit(&s_full[g]);
+      };
+      auto issue_pv = [&](int g, int i) {  // O_g (+)= P_g V_i
+        const uint32_t v_addr = pool + ((2 * i + 1) % kFaPool) * kFaTileBytes;
+        const uint32_t pa = p_addr + g * kFaTileBytes;
+        const uint32_t d = tmem_base + 2 * kFaRows + g * kFaD;
+#pragma unroll
+        for (int kk = 0; kk < kFaRows / 16; ++kk) {  // 16 keys per MMA
+          const uint64_t adesc = make_sw128_desc(pa + (kk >> 2) * kFaHalfBytes + (kk & 3) * 32);
+          const uint64_t bdesc = make_sw128_desc_mn(v_addr + kk * 16 * 128, kFaHalfBytes, 1024);
+          umma_bf16(d, adesc, bdesc, idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = fa_wait(q_full, 0, abort_flag, kDevErrWaitTimeoutMma) && item_full(0);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+        umma_commit(&empty[0]);  // K_0 read by both
+      }
+      for (int i = 0; ok && i < n_tiles; ++i) {
+        const int nv = 2 * i + 1, nk = 2 * i + 2;
+        const bool last = i == n_tiles - 1;
+        // PV_A(i), then S_A(i+1)
+        if (!fa_wait(&p_full[0], i & 1, abort_flag, kDevErrWaitTimeoutMma) || !item_full(nv) ||
+            (tail && last && !fa_wait(v_tail, 0, abort_flag, kDevErrWaitTimeoutMma))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_pv(0, i);
+        if (last) umma_commit(&o_full[0]);
+        if (!last) {
+          if (!item_full(nk)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t v_addr = smem_u32(sV + st * kFaTileBytes);
-          const uint32_t d = tmem_base + 2 * kFaRows + st * kFaD;
-#pragma unroll
-          for (int kk = 0; kk < kFaRows / 16; ++kk) {  // 16 keys per MMA
-            const uint64_t adesc = make_sw128_desc(p_addr + (kk >> 2) * kFaHalfBytes + (kk & 3) * 32);
-            const uint64_t bdesc = make_sw128_desc_mn(v_addr + kk * 16 * 128, kFaHalfBytes, 1024);
-            umma_bf16(d, adesc, bdesc, idesc_o, kk > 0 ? 1u : 0u);
-          }
-          umma_commit(&o_full[st]);
-          umma_commit(&v_empty[st]);
+          issue_s(0, i + 1);
+        }
+        // PV_B(i), then S_B(i+1)
+        if (!fa_wait(&p_full[1], i & 1, abort_flag, kDevErrWaitTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_pv(1, i);
+        umma_commit(&empty[nv % kFaPool]);  // V_i read by both
+        if (last) umma_commit(&o_full[1]);
+        if (!last) {
+          issue_s(1, i + 1);
+          umma_commit(&empty[nk % kFaPool]);  // K_{i+1} read by both
         }
       }
       if (!ok) *abort_flag = 1;
@@ -314,77 +368,56 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       }
     }
   } else {
-    // ---------------- softmax (warps 0-3, one query row per thread) ----------------
-    const int row = warp * 32 + lane;
-    const int qpos = L0 + q0 + row;
-    const uint32_t t_lane = uint32_t(warp * 32) << 16;
-    const uint32_t p_row = smem_u32(sP) + row * 128;
-    const int sw = row & 7;
-    float o[kFaD];
-#pragma unroll
-    for (int d = 0; d < kFaD; ++d) o[d] = 0.f;
-    float m = -INFINITY, l = 0.f;
+    // ---------------- softmax: warps 0-3 tile A, warps 4-7 tile B ----------------
+    const int g = warp >> 2;
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int qbase = L0 + q0 + g * kFaRows + quad * 32;  // the warp's first query position
+    const int qpos = qbase + lane;
+    const uint32_t t_lane = uint32_t(quad * 32) << 16;
+    const uint32_t s_col = tmem_base + t_lane + g * kFaRows;
+    const uint32_t o_col = tmem_base + t_lane + 2 * kFaRows + g * kFaD;
+    const uint32_t p_row = smem_u32(sP + g * kFaTileBytes) + r * 128;
+    const int sw = r & 7;
+    float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int i = 0; i < n_tiles; ++i) {
-      const int st = i & 1, use = i >> 1;
-      if (!fa_wait_warp(&s_full[st], use & 1, abort_flag, kDevErrWaitTimeoutEpilogue)) {
+      if (!fa_wait_warp(&s_full[g], i & 1, abort_flag, kDevErrWaitTimeoutEpilogue)) {
         ok = false;
         break;
       }
       tc_fence_after();
       const int key0 = (j0 + i) * kFaRows;
-      const uint32_t sa = tmem_base + t_lane + st * kFaRows;
-      // pass 1: row max of the visible scores
+      float sv[kFaRows];
+#pragma unroll
+      for (int c = 0; c < kFaRows / 32; ++c) tmem_ld_x32(s_col + c * 32, sv + c * 32);
+      tmem_ld_wait();
+      if (!(key0 >= kv0 && key0 + kFaRows - 1 <= qbase)) {  // a tile this warp does not see whole
+#pragma unroll
+        for (int e = 0; e < kFaRows; ++e) {
+          const int key = key0 + e;
+          if (key < kv0 || key > qpos) sv[e] = -INFINITY;
+        }
+      }
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < kFaRows / 16; ++c) {
-        uint32_t v[16];
-        tmem_ld_32x32b_x16(sa + c * 16, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int key = key0 + c * 16 + e;
-          if (key >= kv0 && key <= qpos) mx = fmaxf(mx, __uint_as_float(v[e]));
-        }
+      for (int e = 0; e < kFaRows; ++e) mx = fmaxf(mx, sv[e]);
+      const float m_new = fmaxf(m_used, mx * a.scale_log2);
+      float alpha = 1.f;
+      if (m_new > m_used + kFaRescaleLog2) {
+        alpha = m_used == -INFINITY ? 0.f : exp2f(m_used - m_new);
+        m_used = m_new;
       }
-      const float m_new = fmaxf(m, mx * a.scale_log2);
-      const float alpha = m == -INFINITY ? 0.f : exp2f(m - m_new);
-      // fold the previous tile's P V into the registers (its P buffer is then free)
-      if (i >= 1) {
-        const int pst = (i - 1) & 1, puse = (i - 1) >> 1;
-        if (!fa_wait_warp(&o_full[pst], puse & 1, abort_flag, kDevErrWaitTimeoutEpilogue)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t oa = tmem_base + t_lane + 2 * kFaRows + pst * kFaD;
-#pragma unroll
-        for (int c = 0; c < kFaD / 16; ++c) {
-          uint32_t v[16];
-          tmem_ld_32x32b_x16(oa + c * 16, v);
-          tmem_ld_wait();
-#pragma unroll
-          for (int e = 0; e < 16; ++e) o[c * 16 + e] = (o[c * 16 + e] + __uint_as_float(v[e])) * alpha;
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&o_empty[pst]);
-      }
-      // pass 2: P = exp2(S*scale - m_new) as bf16 into the swizzled P tile
-      const float mb = m_new == -INFINITY ? 0.f : m_new;
+      const float mb = m_used == -INFINITY ? 0.f : m_used;
+      // P = exp2(S*scale - m) as bf16 into the swizzled P tile
       float lsum = 0.f;
 #pragma unroll
       for (int c = 0; c < kFaRows / 16; ++c) {
-        uint32_t v[16];
-        tmem_ld_32x32b_x16(sa + c * 16, v);
-        tmem_ld_wait();
         uint32_t pk[8];
 #pragma unroll
         for (int e = 0; e < 16; e += 2) {
-          const int key = key0 + c * 16 + e;
-          const float p0 = (key >= kv0 && key <= qpos) ? exp2f(__uint_as_float(v[e]) * a.scale_log2 - mb) : 0.f;
-          const float p1 =
-              (key + 1 >= kv0 && key + 1 <= qpos) ? exp2f(__uint_as_float(v[e + 1]) * a.scale_log2 - mb) : 0.f;
+          const float p0 = exp2f(sv[c * 16 + e] * a.scale_log2 - mb);
+          const float p1 = exp2f(sv[c * 16 + e + 1] * a.scale_log2 - mb);
           lsum += p0 + p1;
           const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
           pk[e >> 1] = *reinterpret_cast<const uint32_t*>(&pp);
@@ -399,51 +432,55 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                      "r"(pk[5]), "r"(pk[6]), "r"(pk[7])
                      : "memory");
       }
+      l = l * alpha + lsum;
+      // a grown row max: rescale this group's O rows (PV of the earlier tiles
+      // is complete -- it was issued before S of this tile)
+      if (i > 0 && __any_sync(0xFFFFFFFFu, alpha != 1.f)) {
+#pragma unroll
+        for (int c = 0; c < kFaD / 32; ++c) {
+          float ov[32];
+          tmem_ld_x32(o_col + c * 32, ov);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] *= alpha;
+          tmem_st_x32(o_col + c * 32, ov);
+        }
+        tmem_st_wait();
+      }
       tc_fence_before();
       fence_proxy_async_shared();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&s_empty[st]);
-        mbar_arrive(p_full);
-      }
-      l = l * alpha + lsum;
-      m = m_new;
+      if (lane == 0) mbar_arrive(&p_full[g]);
     }
-    if (ok) {
-      const int last = n_tiles - 1;
-      const int pst = last & 1;
-      if (fa_wait_warp(&o_full[pst], (last >> 1) & 1, abort_flag, kDevErrWaitTimeoutEpilogue)) {
-        tc_fence_after();
-        const uint32_t oa = tmem_base + t_lane + 2 * kFaRows + pst * kFaD;
+    if (ok && fa_wait_warp(&o_full[g], 0, abort_flag, kDevErrWaitTimeoutEpilogue)) {
+      tc_fence_after();
+      const int nq = g ? nq_b : nq_a;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      uint4* dst = reinterpret_cast<uint4*>(out_tile + size_t(g * kFaRows + r) * out_ld);
 #pragma unroll
-        for (int c = 0; c < kFaD / 16; ++c) {
-          uint32_t v[16];
-          tmem_ld_32x32b_x16(oa + c * 16, v);
-          tmem_ld_wait();
+      for (int c = 0; c < kFaD / 32; ++c) {
+        float ov[32];
+        tmem_ld_x32(o_col + c * 32, ov);
+        tmem_ld_wait();
+        if (r < nq) {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) o[c * 16 + e] += __uint_as_float(v[e]);
-        }
-        tc_fence_before();
-        if (row < nq) {
-          const float inv = l > 0.f ? 1.f / l : 0.f;
-          uint4* dst = reinterpret_cast<uint4*>(out_tile + size_t(row) * out_ld);
-#pragma unroll
-          for (int c = 0; c < kFaD / 8; ++c) {
+          for (int q = 0; q < 4; ++q) {
             uint32_t w[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const __nv_bfloat162 pp = __floats2bfloat162_rn(o[c * 8 + 2 * e] * inv, o[c * 8 + 2 * e + 1] * inv);
+              const __nv_bfloat162 pp = __floats2bfloat162_rn(ov[q * 8 + 2 * e] * inv, ov[q * 8 + 2 * e + 1] * inv);
               w[e] = *reinterpret_cast<const uint32_t*>(&pp);
             }
-            dst[c] = make_uint4(w[0], w[1], w[2], w[3]);
+            dst[c * 4 + q] = make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
       }
+      tc_fence_before();
     }
   }
 
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);

@@ -1231,8 +1231,8 @@ int qmoe_attention_prefill(const void* q, const void* k_cache, const void* v_cac
   QMOE_REQUIRE(B >= 0 && B <= 65535 && S >= 0 && S <= max_seq && max_seq > 0 && max_seq < (int64_t(1) << 30) &&
                    n_slots > 0 && n_slots * nkv < (int64_t(1) << 31) && (cache_slot || B <= n_slots),
                QMOE_ERR_INVALID_ARGUMENT, "attention_prefill: bad sizes");
-  const int64_t n_qtiles = (S + qmoe::kFaRows - 1) / qmoe::kFaRows;
-  QMOE_REQUIRE(B * S < (int64_t(1) << 31) && n_qtiles * nh * B < (int64_t(1) << 31), QMOE_ERR_INVALID_ARGUMENT,
+  const int64_t n_pairs = (S + 2 * qmoe::kFaRows - 1) / (2 * qmoe::kFaRows);  // CTAs per (sequence, head)
+  QMOE_REQUIRE(B * S < (int64_t(1) << 31) && n_pairs * nh * B < (int64_t(1) << 31), QMOE_ERR_INVALID_ARGUMENT,
                "attention_prefill: too many queries");
   QMOE_REQUIRE(aligned16(q) && aligned16(k_cache) && aligned16(v_cache) && aligned16(out),
                QMOE_ERR_MISALIGNED, "attention_prefill: pointers must be 16-byte aligned");
@@ -1258,10 +1258,10 @@ int qmoe_attention_prefill(const void* q, const void* k_cache, const void* v_cac
   args.max_seq = int(max_seq);
   args.n_slots = int(n_slots);
   args.B = int(B);
-  args.n_qtiles = int(n_qtiles);
+  args.n_pairs = int(n_pairs);
   args.scale_log2 = scale * 1.4426950408889634f;
   QMOE_CHECK(set_smem(qmoe::flash_prefill_kernel, qmoe::kFaSmemBytes));
-  return launch_kernel(qmoe::flash_prefill_kernel, dim3(unsigned(n_qtiles * nh * B)), dim3(qmoe::kFaThreads),
+  return launch_kernel(qmoe::flash_prefill_kernel, dim3(unsigned(n_pairs * nh * B)), dim3(qmoe::kFaThreads),
                        size_t(qmoe::kFaSmemBytes), static_cast<cudaStream_t>(stream), true, "flash_prefill_kernel",
                        tq, tk, tv, args);
 }
