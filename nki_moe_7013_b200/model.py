@@ -133,18 +133,32 @@ class Qwen3MoeModel:
         return [layer.self_attn.new_cache(n_slots, max_seq) for layer in self.layers]
 
     def hidden_states(self, input_ids: torch.Tensor, past_key_values: Optional[List[KVCache]] = None,
-                      num_layers: Optional[int] = None, timer=None):
+                      num_layers: Optional[int] = None, timer=None, moe_inputs: Optional[list] = None):
         """input_ids (B, S) -> (hidden states (B, S, H) bf16 after the first
         ``num_layers`` layers (all by default), caches).  ``timer``: an
-        ``attention.StageTimer`` given to every layer."""
+        ``attention.StageTimer`` given to every layer.  ``moe_inputs``: a
+        list that receives each layer's MoE-block input (T, H) (layer-by-layer
+        parity checks: the routing each layer saw)."""
         B, S = input_ids.shape
         H = self.cfg.hidden_size
         caches = past_key_values if past_key_values is not None else self.new_caches(B, S)
         x = ops.embedding(input_ids.reshape(-1).to(torch.int32).contiguous(), self.embed).reshape(B, S, H)
         n = len(self.layers) if num_layers is None else num_layers
         for layer, cache in zip(self.layers[:n], caches):
-            x = layer(x, past_key_value=cache, timer=timer)[0]
+            x = layer(x, past_key_value=cache, timer=timer, capture_intermediates=moe_inputs is not None)[0]
+            if moe_inputs is not None:
+                moe_inputs.append(layer.last["moe_in"])
         return x, caches
+
+    def routing_of(self, moe_inputs: list) -> list:
+        """Top-k expert ids (T, k) int32, each row sorted, of each captured
+        layer's MoE input (``hidden_states(..., moe_inputs=...)``)."""
+        k = self.cfg.num_experts_per_tok
+        out = []
+        for layer, h in zip(self.layers, moe_inputs):
+            idx, _ = ops.router_topk(h.contiguous(), layer.mlp.router_weight, k)
+            out.append(torch.sort(idx, dim=1).values)
+        return out
 
     def forward(self, input_ids: torch.Tensor, past_key_values: Optional[List[KVCache]] = None,
                 last_only: bool = False):
