@@ -73,6 +73,9 @@ def parse_args():
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
     ap.add_argument("--clock-settle-s", type=float, default=1.0,
                     help="untimed load before warm-up so clocks settle and get sampled")
+    ap.add_argument("--prefill-attention", default=None, metavar="BxS",
+                    help="profiling aid: only run the flash-prefill attention kernel on B sequences of S "
+                         "tokens (32 query / 4 KV heads of 128) for --steps launches and print its time")
     ap.add_argument("--decode-model", type=int, default=0, metavar="LAYERS",
                     help="profiling aid: only run the config-2 decode step of a LAYERS-layer model "
                          "(--tokens = batch) for --steps graph replays and print its time")
@@ -1143,8 +1146,46 @@ def run_decode_model_only(args):
     return 0
 
 
+def run_prefill_attention_only(args):
+    """The flash-prefill kernel alone on seeded q / K / V (~N(0,1) bf16), causal
+    over each sequence from an empty cache: device time per launch and the
+    causal FLOP rate against the measured bf16 peak."""
+    import torch
+
+    from nki_moe_7013_b200 import _C, ops
+
+    B, S = (int(v) for v in args.prefill_attention.lower().split("x"))
+    nh, nkv, hd = 32, 4, 128
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    k = torch.randn(B, nkv, S, hd, generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn(B, nkv, S, hd, generator=g, device=dev).to(torch.bfloat16)
+    q = torch.randn(B * S, nh, hd, generator=g, device=dev).to(torch.bfloat16)
+    qs = torch.zeros(B, dtype=torch.int32, device=dev)
+    for _ in range(max(args.warmup, 1)):
+        ops.attention_prefill(q, k, v, qs, B, S)
+    torch.cuda.synchronize()
+    e0, e1 = _events(2)
+    e0.record()
+    for _ in range(args.steps):
+        ops.attention_prefill(q, k, v, qs, B, S)
+    e1.record()
+    torch.cuda.synchronize()
+    if _C.device_error():
+        raise RuntimeError("device error word set")
+    us = e0.elapsed_time(e1) / max(args.steps, 1) * 1e3
+    flops = B * 4 * hd * nh * S * (S + 1) // 2
+    _, tf_burst, _, _ = load_peaks()
+    print(json.dumps({"prefill_attention": f"{B}x{S}", "us_per_launch": us, "causal_flops": flops,
+                      "tflops": flops / (us * 1e-6) / 1e12, "tensor_frac": flops / (us * 1e-6) / 1e12 / tf_burst}))
+    return 0
+
+
 def main():
     args = parse_args()
+    if args.prefill_attention:
+        return run_prefill_attention_only(args)
     if args.decode_model:
         return run_decode_model_only(args)
     if args.impl == "reference":
