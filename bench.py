@@ -56,6 +56,11 @@ DOWN_BYTES_PER_EXPERT = H * I_MOE * 2          # 3,145,728
 METRIC = "MoE-layer tokens/s/GPU (prefill & decode) at 1-8 B200; % of HBM/tensor roofline"
 UNIT = "tokens/s (whole job, all GPUs)"
 MAX_REL_ERR = 2e-2   # activations: max |ours - ref| / max |ref| (bf16 outputs, fp32 accumulation)
+# A token routed differently after last-bit differences upstream of the
+# router must be a near tie: its k-th and (k+1)-th fp32 logits within this
+# (a bf16 ulp of the router input moves the logits by ~2e-3; the median
+# k-th/(k+1)-th gap at these shapes is ~0.04)
+FLIP_GAP_MAX = 2e-2
 
 
 def parse_args():
@@ -949,6 +954,28 @@ def run_ours_ep(args):
     e2e_value = T * world * args.steps / (e2e_ms / 1e3)
     y_e2e = y_host[last_par].to(dev)
 
+    # what the host's copy paths give when every rank copies at once: the
+    # same pinned 4 MB input up and output down, back to back, no compute
+    def copy_rate(up: bool) -> float:
+        buf = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+        c0, c1 = _events(2)
+        barrier()
+        c0.record()
+        for _ in range(args.steps):
+            if up:
+                buf.copy_(x_host, non_blocking=True)
+            else:
+                y_host[0].copy_(buf, non_blocking=True)
+        c1.record()
+        barrier()
+        return _max_over_ranks(c0.elapsed_time(c1) / args.steps, dev, world)
+
+    h2d_ms, d2h_ms = copy_rate(True), copy_rate(False)
+    host_copy = {"h2d_gbs_per_gpu": T * H * 2 / (h2d_ms * 1e-3) / 1e9,
+                 "d2h_gbs_per_gpu": T * H * 2 / (d2h_ms * 1e-3) / 1e9, "concurrent_ranks": world,
+                 "copy_bound_tokens_per_s": T * world / (max(h2d_ms, d2h_ms) * 1e-3),
+                 "note": "all ranks copying 4 MB pinned host buffers at once, no compute (max over ranks)"}
+
     # ---------------- parity: one eager step vs the single-GPU forward ----------------
     y_ep = moe(x)
     idx_ep = moe.topk_idx[:T].clone()
@@ -973,7 +1000,8 @@ def run_ours_ep(args):
         "value_per_gpu": value / world,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2,
                 "api": "PeerExpertParallelMoE step (CUDA graph replay of its forward, one graph and input/output "
-                       "per parity), pinned host in/out, uploads and downloads on their own streams"},
+                       "per parity), pinned host in/out, uploads and downloads on their own streams",
+                "host_copy": host_copy},
         "gpu_launches": moe.launches_per_step(T) * args.steps,
         "stage_us_rank0": stage_us,
         "parity": parity,
@@ -1080,7 +1108,7 @@ def ep_prefill_model_line(cfg, dev, world, rank):
     import torch.distributed as dist
 
     from nki_moe_7013_b200 import _C
-    from nki_moe_7013_b200.model import Qwen3MoeModel
+    from nki_moe_7013_b200.model import Qwen3MoeModel, routing_agreement
 
     line, model, ids_local = prefill_model_line(cfg, dev, world, rank)
     # parity: hidden states after 2 layers, EP model vs the 2-layer model on
@@ -1100,9 +1128,10 @@ def ep_prefill_model_line(cfg, dev, world, rank):
     ref = Qwen3MoeModel(cfg, num_layers=2, device=dev, seed=3)
     mi_ref = []
     h_ref, _ = ref.hidden_states(ids_local, moe_inputs=mi_ref)
-    r_ref = ref.routing_of(mi_ref)
-    same1 = bool(torch.equal(r_ep[0], r_ref[0]))
-    agree = (r_ep[0] == r_ref[0]).all(1) & (r_ep[1] == r_ref[1]).all(1)
+    r_ref = ref.routing_of(mi_ref, with_logits=True)
+    same1 = bool(torch.equal(r_ep[0], r_ref[0][0]))
+    ag = routing_agreement(r_ep[1], r_ref[1][0], r_ref[1][1], K_TOP)
+    agree = ag["agree"] & (r_ep[0] == r_ref[0][0]).all(1)
     hv_ep = h_ep.reshape(-1, H).float()
     hv_ref = h_ref.reshape(-1, H).float()
     err = float((hv_ep[agree] - hv_ref[agree]).abs().max() / hv_ref.abs().max())
@@ -1111,11 +1140,16 @@ def ep_prefill_model_line(cfg, dev, world, rank):
     err = _max_over_ranks(err, dev, world)
     code = int(_max_over_ranks(code, dev, world))
     frac = -_max_over_ranks(-frac, dev, world)
+    gap = _max_over_ranks(ag["max_flip_gap"], dev, world)
     same1 = _max_over_ranks(0.0 if same1 else 1.0, dev, world) == 0.0
     line["parity"] = {"cut_layers": 2, "layer1_routing_equal": same1, "layer2_routing_agree_frac": frac,
+                      "layer2_max_flip_logit_gap": gap, "layer2_median_logit_gap": ag["median_gap"],
                       "max_rel_err_on_tokens_routed_alike": err, "device_error": code, "tolerance": MAX_REL_ERR,
-                      "ok": bool(same1 and frac >= 0.95 and err <= MAX_REL_ERR and code == 0),
-                      "reference": "the same seeded model, 2 layers, on one GPU, same sequences"}
+                      "ok": bool(same1 and frac >= 0.9 and gap <= FLIP_GAP_MAX and err <= MAX_REL_ERR and code == 0),
+                      "reference": "the same seeded model, 2 layers, on one GPU, same sequences",
+                      "rule": "layer-1 routing bit-exact; every layer-2 routing difference a near tie (k-th vs "
+                              "(k+1)-th fp32 logit within layer2_max_flip_logit_gap <= %g) and >= 90 %% of tokens "
+                              "routed alike; hidden states of those tokens within the tolerance" % FLIP_GAP_MAX}
     del ref
     torch.cuda.empty_cache()
     return line

@@ -150,15 +150,32 @@ class Qwen3MoeModel:
                 moe_inputs.append(layer.last["moe_in"])
         return x, caches
 
-    def routing_of(self, moe_inputs: list) -> list:
+    def routing_of(self, moe_inputs: list, with_logits: bool = False) -> list:
         """Top-k expert ids (T, k) int32, each row sorted, of each captured
-        layer's MoE input (``hidden_states(..., moe_inputs=...)``)."""
+        layer's MoE input (``hidden_states(..., moe_inputs=...)``); with
+        ``with_logits`` a list of (ids, fp32 router logits (T, E))."""
         k = self.cfg.num_experts_per_tok
         out = []
         for layer, h in zip(self.layers, moe_inputs):
-            idx, _ = ops.router_topk(h.contiguous(), layer.mlp.router_weight, k)
-            out.append(torch.sort(idx, dim=1).values)
+            idx, _, logits = ops.router_topk(h.contiguous(), layer.mlp.router_weight, k, return_logits=True)
+            ids = torch.sort(idx, dim=1).values
+            out.append((ids, logits) if with_logits else ids)
         return out
+
+
+def routing_agreement(ids_a: torch.Tensor, ids_b: torch.Tensor, logits_b: torch.Tensor, k: int) -> dict:
+    """Compare two routings of the same tokens (sorted (T, k) expert ids) made
+    from inputs that differ by rounding: ``agree`` (T,) bool marks tokens
+    routed alike; for the others ``max_flip_gap`` is the largest gap, in
+    routing ``b``'s fp32 logits, between its k-th and (k+1)-th expert -- small
+    when every difference is a near tie at the selection boundary."""
+    agree = (ids_a == ids_b).all(dim=1)
+    top = torch.topk(logits_b.float(), k + 1, dim=1).values
+    gap = top[:, k - 1] - top[:, k]
+    flips = ~agree
+    max_gap = float(gap[flips].max()) if bool(flips.any()) else 0.0
+    return {"agree": agree, "frac": float(agree.float().mean()), "max_flip_gap": max_gap,
+            "median_gap": float(gap.median())}
 
     def forward(self, input_ids: torch.Tensor, past_key_values: Optional[List[KVCache]] = None,
                 last_only: bool = False):

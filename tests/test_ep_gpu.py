@@ -133,7 +133,7 @@ def _ep_model_worker(rank, world, port, out_dir):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
     from nki_moe_7013_b200 import _C
     from nki_moe_7013_b200.config import Qwen3MoeConfig
-    from nki_moe_7013_b200.model import Qwen3MoeModel
+    from nki_moe_7013_b200.model import Qwen3MoeModel, routing_agreement
 
     cfg = Qwen3MoeConfig()
     B, S, V = 2, 96, 4096  # per rank: 2 sequences of 96 tokens (192 tokens through each EP block)
@@ -153,20 +153,23 @@ def _ep_model_worker(rank, world, port, out_dir):
     ref = Qwen3MoeModel(cfg, num_layers=2, vocab_size=V, device=dev, seed=7)
     mi_ref = []
     h_ref, _ = ref.hidden_states(mine, moe_inputs=mi_ref)
-    r_ref = ref.routing_of(mi_ref)
+    r_ref = ref.routing_of(mi_ref, with_logits=True)
     logits_ref, _ = ref.forward(mine, last_only=True)
+    ag = routing_agreement(r_ep[1], r_ref[1][0], r_ref[1][1], cfg.num_experts_per_tok)
+    r_ref = [r[0] for r in r_ref]
     # layer 1 sees identical inputs: routing bit-exact.  The EP combine rounds
     # each weighted expert row to bf16 before the sum, so layer 2's input can
     # differ in the last bit and a near-tie token may pick another 8th
-    # expert: compare the tokens routed alike in both layers (measured: 3-4 %
-    # of the tokens flip an 8th expert in layer 2 at these shapes).
+    # expert: compare the tokens routed alike in both layers, and check that
+    # every difference is such a near tie (measured: 3-4 % of the tokens flip
+    # an 8th expert in layer 2 at these shapes).
     same1 = float(torch.equal(r_ep[0], r_ref[0]))
     agree = (r_ep[0] == r_ref[0]).all(1) & (r_ep[1] == r_ref[1]).all(1)
     hv_ep, hv_ref = h_ep.reshape(-1, h_ep.shape[-1]), h_ref.reshape(-1, h_ref.shape[-1])
     err_h = max_rel_err(to_f32_np(hv_ep[agree]), to_f32_np(hv_ref[agree])) * (
         float(hv_ref[agree].float().abs().max()) / float(hv_ref.float().abs().max()))
     errs = [err_h, max_rel_err(to_f32_np(logits_ep), to_f32_np(logits_ref)), float(code), same1,
-            float(agree.float().mean())]
+            float(agree.float().mean()), ag["max_flip_gap"]]
     np.save(os.path.join(out_dir, f"epm{rank}.npy"), np.array(errs))
     dist.barrier()
     dist.destroy_process_group()
@@ -186,5 +189,7 @@ def test_ep_model_matches_single_gpu_model(tmp_path):
         errs = np.load(tmp_path / f"epm{r}.npy")
         assert errs[2] == 0, f"rank {r}: device error {errs[2]}"
         assert errs[3] == 1.0, f"rank {r}: layer-1 routing differs"
-        assert errs[4] >= 0.95, f"rank {r}: only {errs[4]:.3f} of the tokens routed alike in layer 2"
+        assert errs[4] >= 0.9, f"rank {r}: only {errs[4]:.3f} of the tokens routed alike in layer 2"
+        # every token routed differently is a near tie (k-th vs (k+1)-th logit)
+        assert errs[5] <= 2e-2, f"rank {r}: a layer-2 routing difference with logit gap {errs[5]:.3e}"
         assert np.all(errs[:2] <= MAX_REL), f"rank {r}: {errs}"
