@@ -82,16 +82,20 @@ __global__ void __launch_bounds__(kRouteSmallMaxE / kRouteSmallCtas * 32, 1)
   const int e_per = E / kRouteSmallCtas;
   const int Tpad = (T + 3) & ~3;
   if (threadIdx.x == 0) QMOE_TRACE_AT(0, 0);
-  griddep_wait();
-  griddep_launch_dependents();
-  if (threadIdx.x == 0) QMOE_TRACE_AT(0, 1);
-
-  // this warp's expert: its canonical weight slice, one load per group
+  // this warp's expert: its canonical weight slice, one load per group.  The
+  // router weights (and bias) are not produced by the kernels in front of
+  // this one, so their loads are in flight before the dependency wait and
+  // overlap the preceding kernel's tail; everything this kernel writes, and
+  // every read of x, comes after the wait.
   const int e = cta * e_per + warp;
   uint4 wv[G];
 #pragma unroll
   for (int g = 0; g < G; ++g)
     wv[g] = __ldg(reinterpret_cast<const uint4*>(w + size_t(e) * H + 256 * g + 8 * lane));
+  const float be = bias ? __ldg(bias + e) : 0.f;
+  griddep_wait();
+  griddep_launch_dependents();
+  if (threadIdx.x == 0) QMOE_TRACE_AT(0, 1);
   {
     const uint4* src = reinterpret_cast<const uint4*>(x);
     uint4* dst = reinterpret_cast<uint4*>(xs);
@@ -111,7 +115,6 @@ __global__ void __launch_bounds__(kRouteSmallMaxE / kRouteSmallCtas * 32, 1)
   __syncthreads();
 
   // logits: 4 tokens' chains interleaved
-  const float be = bias ? bias[e] : 0.f;
   for (int t0 = 0; t0 < T; t0 += 4) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
