@@ -556,37 +556,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int h = 0; h <= args.dn_two; ++h) {  // the unit's 128-feature halves
             if (h) tmem_ld_32x32b_x16(taddr + tsecond + c * 16, v);
             tmem_ld_wait();
-            if constexpr (kReturn) {
-              // the four epilogue warps stage their 4 x 32 features of these 16
-              // rows as weighted bf16 in one [16][128] tile, then every row
-              // leaves as one 256-byte run of 16-byte stores into the source
-              // rank's return buffer (over NVLink: 4x longer runs than the
-              // 64 bytes one warp's features give)
-              __nv_bfloat16* sb = reinterpret_cast<__nv_bfloat16*>(staging);
-              named_barrier_sync(1, 128);  // the previous chunk's rows have been read
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                const int n = c * 16 + i;
-                const float wv = n < nrows ? meta_w[n] : 0.f;
-                sb[i * kBM + quad * 32 + lane] = __float2bfloat16_rn(wv * __uint_as_float(v[i]));
-              }
-              named_barrier_sync(1, 128);
-              const int fcol = (mt * (1 + args.dn_two) + h) * kBM + (lane & 15) * 8;
-#pragma unroll
-              for (int j = 0; j < 2; ++j) {
-                const int i = (warp - 2) * 4 + 2 * j + (lane >> 4);
-                const int n = c * 16 + i;
-                if (n < nrows) {
-                  const int dst = meta_dst[n];
-                  if (dst >= 0) {
-                    __nv_bfloat16* ret =
-                        args.peer_ret[meta_src[n]] + (size_t(args.ret_row0) + dst) * args.acc_ld + fcol;
-                    *reinterpret_cast<uint4*>(ret) = *reinterpret_cast<const uint4*>(sb + i * kBM + (lane & 15) * 8);
-                  }
-                }
-              }
-              continue;
-            }
             // transpose through shared memory: a lane then holds 4 consecutive
             // features of one row, added with one 16-byte vector reduction
             float* wsb = staging + (warp - 2) * (16 * 33);
@@ -603,8 +572,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const int dst = meta_dst[n];
                 if (dst >= 0) {
                   const float wv = meta_w[n];
-                  red_add_v4_f32(args.acc + size_t(dst) * args.acc_ld + fcol, wv * wsb[i * 33 + fq],
-                                 wv * wsb[i * 33 + fq + 1], wv * wsb[i * 33 + fq + 2], wv * wsb[i * 33 + fq + 3]);
+                  if constexpr (kReturn) {
+                    // weighted row segment straight into the source rank's return buffer
+                    __nv_bfloat16* ret =
+                        args.peer_ret[meta_src[n]] + (size_t(args.ret_row0) + dst) * args.acc_ld + fcol;
+                    const __nv_bfloat162 lo =
+                        __floats2bfloat162_rn(wv * wsb[i * 33 + fq], wv * wsb[i * 33 + fq + 1]);
+                    const __nv_bfloat162 hi =
+                        __floats2bfloat162_rn(wv * wsb[i * 33 + fq + 2], wv * wsb[i * 33 + fq + 3]);
+                    uint2 pk;
+                    pk.x = *reinterpret_cast<const uint32_t*>(&lo);
+                    pk.y = *reinterpret_cast<const uint32_t*>(&hi);
+                    *reinterpret_cast<uint2*>(ret) = pk;
+                  } else {
+                    red_add_v4_f32(args.acc + size_t(dst) * args.acc_ld + fcol,
+                                   wv * wsb[i * 33 + fq], wv * wsb[i * 33 + fq + 1], wv * wsb[i * 33 + fq + 2],
+                                   wv * wsb[i * 33 + fq + 3]);
+                  }
                 }
               }
             }
