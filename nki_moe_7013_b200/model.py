@@ -163,20 +163,6 @@ class Qwen3MoeModel:
         return out
 
 
-def routing_agreement(ids_a: torch.Tensor, ids_b: torch.Tensor, logits_b: torch.Tensor, k: int) -> dict:
-    """Compare two routings of the same tokens (sorted (T, k) expert ids) made
-    from inputs that differ by rounding: ``agree`` (T,) bool marks tokens
-    routed alike; for the others ``max_flip_gap`` is the largest gap, in
-    routing ``b``'s fp32 logits, between its k-th and (k+1)-th expert -- small
-    when every difference is a near tie at the selection boundary."""
-    agree = (ids_a == ids_b).all(dim=1)
-    top = torch.topk(logits_b.float(), k + 1, dim=1).values
-    gap = top[:, k - 1] - top[:, k]
-    flips = ~agree
-    max_gap = float(gap[flips].max()) if bool(flips.any()) else 0.0
-    return {"agree": agree, "frac": float(agree.float().mean()), "max_flip_gap": max_gap,
-            "median_gap": float(gap.median())}
-
     def forward(self, input_ids: torch.Tensor, past_key_values: Optional[List[KVCache]] = None,
                 last_only: bool = False):
         """input_ids (B, S) -> (logits (B, S, V) bf16, caches); the eager path
@@ -191,6 +177,21 @@ def routing_agreement(ids_a: torch.Tensor, ids_b: torch.Tensor, logits_b: torch.
         h = ops.rmsnorm(x.reshape(B * S, H), self.norm, self.cfg.rms_norm_eps)
         logits = ops.linear(h, self.lm_head)
         return logits.reshape(B, S, self.vocab_size), caches
+
+
+def routing_agreement(ids_a: torch.Tensor, ids_b: torch.Tensor, logits_b: torch.Tensor, k: int) -> dict:
+    """Compare two routings of the same tokens (sorted (T, k) expert ids) made
+    from inputs that differ by rounding: ``agree`` (T,) bool marks tokens
+    routed alike; for the others ``max_flip_gap`` is the largest gap, in
+    routing ``b``'s fp32 logits, between its k-th and (k+1)-th expert -- small
+    when every difference is a near tie at the selection boundary."""
+    agree = (ids_a == ids_b).all(dim=1)
+    top = torch.topk(logits_b.float(), k + 1, dim=1).values
+    gap = top[:, k - 1] - top[:, k]
+    flips = ~agree
+    max_gap = float(gap[flips].max()) if bool(flips.any()) else 0.0
+    return {"agree": agree, "frac": float(agree.float().mean()), "max_flip_gap": max_gap,
+            "median_gap": float(gap.median())}
 
 
 class DecodeSession:
