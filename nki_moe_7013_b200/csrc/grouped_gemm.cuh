@@ -68,6 +68,8 @@ enum GemmMode : int {
   kModeGateUp = 1,  // two accumulators (gate, up) -> bf16 SiLU(gate)*up
   kModePlain = 2,   // one accumulator -> bf16 store (dense projections)
   kModeDownReturn = 3,  // weighted bf16 rows stored into the source rank's return buffer (EP)
+  kModePlainPair = 4,   // two accumulators (features f0.. and f0+128.. of a 256-feature unit) sharing
+                        // the row operand -> bf16 stores (dense projections of prefill size)
 };
 
 // kSmall: every tile has at most 16 rows (decode batches).  A stage's
@@ -78,16 +80,18 @@ enum GemmMode : int {
 template <int kMode, bool kSmall = false>
 struct GemmCfg {
   static constexpr bool kGateUp = kMode == kModeGateUp;
-  static constexpr int kATiles = kGateUp ? 2 : 1;
+  // two weight tiles per stage, two accumulators sharing the row tile
+  static constexpr bool kTwoA = kGateUp || kMode == kModePlainPair;
+  static constexpr int kATiles = kTwoA ? 2 : 1;
   static constexpr int kABytes = kBM * kBK * 2;           // 16 KB
   static constexpr int kBRows = kSmall ? kBoxRows : kBNMax;
   static constexpr int kBBytes = kBRows * kBK * 2;        // 16 KB (2 KB small)
   static constexpr int kStageBytes = kATiles * kABytes + kBBytes;
   // small plain GEMMs (decode projections) run alone: the deepest ring
   static constexpr int kStages =
-      kGateUp ? (kSmall ? 3 : 4) : kMode == kModePlain ? (kSmall ? 10 : 6) : (kSmall ? 5 : 6);
+      kTwoA ? (kSmall ? 3 : 4) : kMode == kModePlain ? (kSmall ? 10 : 6) : (kSmall ? 5 : 6);
   static constexpr int kUpCol = kSmall ? kBoxRows : kBM;  // TMEM column of the up accumulator
-  static constexpr int kAccCols = kGateUp ? 2 * kUpCol : kBRows;  // TMEM columns per accumulator buffer
+  static constexpr int kAccCols = kTwoA ? 2 * kUpCol : kBRows;  // TMEM columns per accumulator buffer
   static constexpr int kTmemCols = 2 * kAccCols < 32 ? 32 : 2 * kAccCols;
   static constexpr int kBarrierBytes = 256;
   // down epilogue: per epilogue warp a [16 rows][33] fp32 transpose buffer
@@ -413,7 +417,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int ksplit = max(1, min(min(args.k_splits, args.num_kb), int(gridDim.x) / units));
     plan = WorkPlan{0, ksplit, ntiles * args.n_mtiles * ksplit};
   }
-  if constexpr (kGateUp || kMode == kModePlain) plan = gateup_work_plan(args, ntiles, max_rows);
+  if constexpr (kGateUp || kMode == kModePlain || kMode == kModePlainPair)
+    plan = gateup_work_plan(args, ntiles, max_rows);
   const int total_units = plan.total;
 
   if (warp == 0) {
@@ -440,7 +445,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int row0 = tv.first_row(tile);
       const int nrows = tv.nrows(tile);
       const int nb = (nrows + kBoxRows - 1) / kBoxRows;
-      const int a_row = e * args.a_rows_per_expert + mt * kBM;
+      // a paired plain unit covers features [256 mt, 256 mt + 256): its second
+      // weight tile sits up_row_offset (128) rows below the first
+      const int a_row = e * args.a_rows_per_expert + mt * kBM * (kMode == kModePlainPair ? 2 : 1);
       const int n_g4 = (nrows + 3) / 4;
       int src[4] = {0, 0, 0, 0};
       if (gather && lane < n_g4) {
@@ -474,7 +481,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               }
               mbar_arrive_expect_tx(&full[stage], bytes);
               tma_load_2d_hint(sb, &tmA, kb * kBK, a_row, &full[stage], pol_w);
-              if (kGateUp)
+              if (C::kTwoA)
                 tma_load_2d_hint(sb + C::kABytes, &tmA, kb * kBK, a_row + args.up_row_offset,
                                  &full[stage], pol_w);
             }  // else: weights and the byte count were issued before the wait
@@ -559,7 +566,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint32_t accum = (kb | k) != 0 ? 1u : 0u;
             const uint64_t bdesc = make_sw128_desc(bsb + k * kUmmaK * 2);
             umma_bf16(d_gate, make_sw128_desc(sb + k * kUmmaK * 2), bdesc, idesc, accum);
-            if (kGateUp)
+            if (C::kTwoA)
               umma_bf16(d_up, make_sw128_desc(sb + C::kABytes + k * kUmmaK * 2), bdesc, idesc,
                         accum);
           }
@@ -654,6 +661,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int i = 0; i < 16; ++i) {
             const int n = c * 16 + i;
             if (n < nrows) args.act[size_t(row0 + n) * args.act_ld + feat] = __float2bfloat16_rn(g[i]);
+          }
+        } else if constexpr (kMode == kModePlainPair) {
+          uint32_t hi[16];
+          tmem_ld_32x32b_x16(taddr + C::kUpCol + c * 16, hi);
+          tmem_ld_wait();
+          const int f_lo = mt * 2 * kBM + m;  // this thread's features in the unit's two halves
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int n = c * 16 + i;
+            if (n < nrows) {
+              __nv_bfloat16* orow = args.act + size_t(row0 + n) * args.act_ld;
+              orow[f_lo] = __float2bfloat16_rn(__uint_as_float(v[i]));
+              orow[f_lo + kBM] = __float2bfloat16_rn(__uint_as_float(hi[i]));
+            }
           }
         } else if constexpr (kGateUp) {
           uint32_t up[16];

@@ -42,7 +42,8 @@ def test_rmsnorm_bf16_and_fused_residual(cuda_dev, oracle, rows, H):
     assert max_rel_err(to_f32_np(y2), oracle.rmsnorm(s_ref, w.cpu().numpy(), 1e-6)) < 1e-2
 
 
-@pytest.mark.parametrize("T,K,N", [(1, 2048, 5120), (1024, 2048, 5120), (77, 4096, 2048), (300, 256, 384)])
+@pytest.mark.parametrize("T,K,N", [(1, 2048, 5120), (1024, 2048, 5120), (77, 4096, 2048), (300, 256, 384),
+                                   (700, 4096, 2048), (2048, 2048, 5120), (513, 2048, 384)])
 def test_linear_tcgen05(cuda_dev, T, K, N):
     from nki_moe_7013_b200 import ops
 
