@@ -660,8 +660,9 @@ int launch_expert_rows(const void* x, const int32_t* row_token, const float* row
   return set_error(QMOE_ERR_UNSUPPORTED_SHAPE, "expert rows: I=%lld", (long long)I);
 }
 
-// Rows from which dense projections run 256-feature units (below, the
-// 128-feature units leave fewer SMs idle).
+// Rows from which dense projections may run 256-feature units (they do when
+// that still gives every SM a unit; otherwise the 128-feature units leave
+// fewer SMs idle).
 constexpr int64_t kPlainPairMinRows = 512;
 
 int launch_linear(const void* x, const void* w, int64_t T, int64_t K, int64_t N, void* out,
@@ -689,12 +690,13 @@ int launch_linear(const void* x, const void* w, int64_t T, int64_t K, int64_t N,
   if (grid <= 0) return QMOE_OK;
   if (small)
     return launch_gemm_cfg<qmoe::kModePlain, true>(tmA, tmB, a, grid, stream, "grouped_gemm_kernel<plain,small>");
-  if (N % (2 * qmoe::kBM) == 0 && T >= kPlainPairMinRows) {
-    // prefill-sized projections: 256-feature units, two accumulators sharing
-    // each 128-row tile (a quarter fewer operand bytes from L2 per FLOP)
+  const int64_t units2 = ((T + qmoe::kBNMax - 1) / qmoe::kBNMax) * (N / (2 * qmoe::kBM));
+  if (N % (2 * qmoe::kBM) == 0 && T >= kPlainPairMinRows && units2 >= num_sms(0)) {
+    // prefill-sized projections with at least a unit per SM: 256-feature
+    // units, two accumulators sharing each 128-row tile (a quarter fewer
+    // operand bytes from L2 per FLOP)
     a.n_mtiles = int(N / (2 * qmoe::kBM));
     a.up_row_offset = qmoe::kBM;
-    const int64_t units2 = ((T + qmoe::kBNMax - 1) / qmoe::kBNMax) * a.n_mtiles;
     const int grid2 = int(std::min<int64_t>(units2, num_sms(0)));
     return launch_gemm_cfg<qmoe::kModePlainPair, false>(tmA, tmB, a, grid2, stream,
                                                         "grouped_gemm_kernel<plain pair>");
