@@ -43,7 +43,7 @@ def test_rmsnorm_bf16_and_fused_residual(cuda_dev, oracle, rows, H):
 
 
 @pytest.mark.parametrize("T,K,N", [(1, 2048, 5120), (1024, 2048, 5120), (77, 4096, 2048), (300, 256, 384),
-                                   (700, 4096, 2048), (2048, 2048, 5120), (513, 2048, 384)])
+                                   (700, 4096, 2048), (2048, 2048, 5120), (513, 2048, 384), (1100, 2048, 5120)])
 def test_linear_tcgen05(cuda_dev, T, K, N):
     from nki_moe_7013_b200 import ops
 
