@@ -125,6 +125,14 @@ __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// 2^x with the SFU's approximate exp2, denormal results flushed to zero (the
+// probabilities are stored as bf16 and lie in [0, 2^8]; exp2(-inf) = 0).
+__device__ __forceinline__ float fa_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Bounded wait on an mbarrier phase for one thread; on time-out records
 // `code` and raises the abort flag.  Gives up at once if the flag is up.
 __device__ __forceinline__ bool fa_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
@@ -399,9 +407,15 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           if (key < kv0 || key > qpos) sv[e] = -INFINITY;
         }
       }
-      float mx = -INFINITY;
+      // row max as 8 independent chains (a single 128-long chain is ~4 cycles
+      // a step with only two softmax warps per scheduler to hide it)
+      float mx8[8];
 #pragma unroll
-      for (int e = 0; e < kFaRows; ++e) mx = fmaxf(mx, sv[e]);
+      for (int j = 0; j < 8; ++j) mx8[j] = sv[j];
+#pragma unroll
+      for (int e = 8; e < kFaRows; ++e) mx8[e & 7] = fmaxf(mx8[e & 7], sv[e]);
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float m_new = fmaxf(m_used, mx * a.scale_log2);
       float alpha = 1.f;
       if (m_new > m_used + kFaRescaleLog2) {
@@ -410,15 +424,15 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       }
       const float mb = m_used == -INFINITY ? 0.f : m_used;
       // P = exp2(S*scale - m) as bf16 into the swizzled P tile
-      float lsum = 0.f;
+      float ls8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // 8 independent partial sums
 #pragma unroll
       for (int c = 0; c < kFaRows / 16; ++c) {
         uint32_t pk[8];
 #pragma unroll
         for (int e = 0; e < 16; e += 2) {
-          const float p0 = exp2f(sv[c * 16 + e] * a.scale_log2 - mb);
-          const float p1 = exp2f(sv[c * 16 + e + 1] * a.scale_log2 - mb);
-          lsum += p0 + p1;
+          const float p0 = fa_exp2(sv[c * 16 + e] * a.scale_log2 - mb);
+          const float p1 = fa_exp2(sv[c * 16 + e + 1] * a.scale_log2 - mb);
+          ls8[e >> 1] += p0 + p1;
           const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
           pk[e >> 1] = *reinterpret_cast<const uint32_t*>(&pp);
         }
@@ -432,6 +446,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                      "r"(pk[5]), "r"(pk[6]), "r"(pk[7])
                      : "memory");
       }
+      const float lsum = ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
       l = l * alpha + lsum;
       // a grown row max: rescale this group's O rows (PV of the earlier tiles
       // is complete -- it was issued before S of this tile)
