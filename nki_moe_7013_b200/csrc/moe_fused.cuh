@@ -78,6 +78,7 @@ struct FusedArgs {
   int n_rows;            // R: rows of the permuted operands (a tile outside [0, R) is refused)
   int n_mt_gu, n_mt_dn;      // units per tile: I / 128 and H / (128 * (1 + dn_two))
   int dn_two;                // 1: a down unit covers 256 features (two accumulators)
+  int full_boxes;            // 1: tmB_*_full map whole 128-row tiles (one TMA load per stage)
   int num_kb_gu, num_kb_dn;  // k blocks: H / 64 and I / 64
   int a_rows_gu;             // 2I
   int up_off;                // I
@@ -138,6 +139,7 @@ template <bool kReturn = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     moe_fused_kernel(const __grid_constant__ CUtensorMap tmA_gu, const __grid_constant__ CUtensorMap tmB_gu,
                      const __grid_constant__ CUtensorMap tmA_dn, const __grid_constant__ CUtensorMap tmB_dn,
+                     const __grid_constant__ CUtensorMap tmB_gu_full, const __grid_constant__ CUtensorMap tmB_dn_full,
                      const FusedArgs args) {
   using C = FusedCfg;
   extern __shared__ uint8_t fused_smem_raw[];
@@ -181,6 +183,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     prefetch_tmap(&tmB_gu);
     prefetch_tmap(&tmA_dn);
     prefetch_tmap(&tmB_dn);
+    prefetch_tmap(&tmB_gu_full);
+    prefetch_tmap(&tmB_dn_full);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -277,9 +281,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           mbar_arrive_expect_tx(&full[stage], bytes);
           tma_load_2d_hint(sb, ta, kb * kBK, a_row, &full[stage], pol_w);
           if (two_a) tma_load_2d_hint(sb + C::kABytes, ta, kb * kBK, a2_row, &full[stage], pol_w);
-          for (int b = 0; b < nb; ++b)
-            tma_load_2d_hint(bs + b * (kBoxRows * kBK * 2), tb, kb * kBK, row0 + b * kBoxRows, &full[stage],
-                             pol_x);
+          if (args.full_boxes && nb == C::kMaxRows / kBoxRows)
+            tma_load_2d_hint(bs, gu ? &tmB_gu_full : &tmB_dn_full, kb * kBK, row0, &full[stage], pol_x);
+          else
+            for (int b = 0; b < nb; ++b)
+              tma_load_2d_hint(bs + b * (kBoxRows * kBK * 2), tb, kb * kBK, row0 + b * kBoxRows, &full[stage],
+                               pol_x);
           if (first) {
             QMOE_TRACE_AT(1, 2);
             first = false;
@@ -383,7 +390,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_arrive_expect_tx(&full[stage], bytes);
             tma_load_2d_hint(sb, ta, kb * kBK, a_row, &full[stage], pol_w);
             if (two_a) tma_load_2d_hint(sb + C::kABytes, ta, kb * kBK, a2_row, &full[stage], pol_w);
-            if (!g4)
+            if (!g4 && args.full_boxes && nb == C::kMaxRows / kBoxRows)
+              tma_load_2d_hint(bs, gu ? &tmB_gu_full : &tmB_dn_full, kb * kBK, row0, &full[stage], pol_x);
+            else if (!g4)
               for (int b = 0; b < nb; ++b)
                 tma_load_2d_hint(bs + b * (kBoxRows * kBK * 2), tb, kb * kBK, row0 + b * kBoxRows,
                                  &full[stage], pol_x);

@@ -529,7 +529,17 @@ int launch_moe_fused(const void* x, int64_t x_rows, const int32_t* gather_rows, 
     QMOE_CHECK(make_tmap_bf16(&tb_gu, x, uint64_t(H), uint64_t(R), qmoe::kBK, qmoe::kBoxRows));
   QMOE_CHECK(make_tmap_bf16(&ta_dn, w_down, uint64_t(I), uint64_t(E * H), qmoe::kBK, qmoe::kBM));
   QMOE_CHECK(make_tmap_bf16(&tb_dn, act, uint64_t(I), uint64_t(R), qmoe::kBK, qmoe::kBoxRows));
+  // whole 128-row tiles load as one box (eight times fewer TMA requests than
+  // 16-row boxes; same shared-memory layout); with a gather the gate/up rows
+  // come by gather4 and this map is not used
+  CUtensorMap tb_gu_full = tb_gu, tb_dn_full = tb_dn;
+  const bool full_boxes = R >= qmoe::kBNMax && !gather_rows;
+  if (full_boxes) {
+    QMOE_CHECK(make_tmap_bf16(&tb_gu_full, x, uint64_t(H), uint64_t(R), qmoe::kBK, qmoe::kBNMax));
+    QMOE_CHECK(make_tmap_bf16(&tb_dn_full, act, uint64_t(I), uint64_t(R), qmoe::kBK, qmoe::kBNMax));
+  }
   qmoe::FusedArgs a{};
+  a.full_boxes = full_boxes ? 1 : 0;
   a.tiles = tiles;
   a.max_tiles = int(max_tiles);
   a.n_rows = int(R);
@@ -562,11 +572,11 @@ int launch_moe_fused(const void* x, int64_t x_rows, const int32_t* gather_rows, 
   if (a.peer_ret != nullptr) {
     QMOE_CHECK(set_smem(qmoe::moe_fused_kernel<true>, C::kSmemBytes));
     return launch_kernel(qmoe::moe_fused_kernel<true>, dim3(grid), dim3(qmoe::kGemmThreads), C::kSmemBytes, stream,
-                         true, "moe_fused_kernel<return>", ta_gu, tb_gu, ta_dn, tb_dn, a);
+                         true, "moe_fused_kernel<return>", ta_gu, tb_gu, ta_dn, tb_dn, tb_gu_full, tb_dn_full, a);
   }
   QMOE_CHECK(set_smem(qmoe::moe_fused_kernel<false>, C::kSmemBytes));
   return launch_kernel(qmoe::moe_fused_kernel<false>, dim3(grid), dim3(qmoe::kGemmThreads), C::kSmemBytes, stream,
-                       true, "moe_fused_kernel", ta_gu, tb_gu, ta_dn, tb_dn, a);
+                       true, "moe_fused_kernel", ta_gu, tb_gu, ta_dn, tb_dn, tb_gu_full, tb_dn_full, a);
 }
 
 // RMSNorm launch with the row held in registers: kChunks 128-element chunks
