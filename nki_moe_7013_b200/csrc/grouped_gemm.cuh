@@ -117,6 +117,7 @@ struct GemmArgs {
   float* split_ws;
   int max_k_splits;
   int flags;             // kGemmTilesReady
+  int full_boxes;        // 1: tmB_full maps whole 128-row tiles (one TMA load per stage for them)
   // gate/up: when non-null, each finished unit (after its activation rows are
   // written; the last split of a split unit) adds 1 to tile_done[tile].
   // down: when non-null, a tile's activation rows are loaded once
@@ -311,8 +312,8 @@ __device__ __forceinline__ int down_pre_issue(const GemmArgs& a, const CUtensorM
 
 template <int kMode, bool kSmall = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmB_full, const GemmArgs args) {
   using C = GemmCfg<kMode, kSmall>;
   constexpr bool kGateUp = C::kGateUp;
   extern __shared__ uint8_t gemm_smem_raw[];
@@ -485,9 +486,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 tma_load_2d_hint(sb + C::kABytes, &tmA, kb * kBK, a_row + args.up_row_offset,
                                  &full[stage], pol_w);
             }  // else: weights and the byte count were issued before the wait
-            for (int b = 0; b < nb; ++b)
-              tma_load_2d_hint(bs + b * (kBoxRows * kBK * 2), &tmB, kb * kBK, row0 + b * kBoxRows,
-                               &full[stage], pol_x);
+            if (!kSmall && args.full_boxes && nb == kBNMax / kBoxRows)
+              tma_load_2d_hint(bs, &tmB_full, kb * kBK, row0, &full[stage], pol_x);
+            else
+              for (int b = 0; b < nb; ++b)
+                tma_load_2d_hint(bs + b * (kBoxRows * kBK * 2), &tmB, kb * kBK, row0 + b * kBoxRows,
+                                 &full[stage], pol_x);
           }
         } else {
           int w_ok = 1;

@@ -423,13 +423,14 @@ int launch_route_permute(const void* x, const void* w, const float* bias, int64_
 }
 
 // One grouped-GEMM launch in the normal or the small-tile configuration.
+// tmB_full (with a.full_boxes) maps whole 128-row tiles of the B operand.
 template <int kMode, bool kSmall>
 int launch_gemm_cfg(const CUtensorMap& tmA, const CUtensorMap& tmB, const qmoe::GemmArgs& a, int grid,
-                    cudaStream_t stream, const char* name) {
+                    cudaStream_t stream, const char* name, const CUtensorMap* tmB_full = nullptr) {
   using C = qmoe::GemmCfg<kMode, kSmall>;
   QMOE_CHECK(set_smem(qmoe::grouped_gemm_kernel<kMode, kSmall>, C::kSmemBytes));
   return launch_kernel(qmoe::grouped_gemm_kernel<kMode, kSmall>, dim3(grid), dim3(qmoe::kGemmThreads),
-                       C::kSmemBytes, stream, true, name, tmA, tmB, a);
+                       C::kSmemBytes, stream, true, name, tmA, tmB, tmB_full ? *tmB_full : tmB, a);
 }
 
 // Tiles of at most this many rows take the small configuration.
@@ -700,6 +701,12 @@ int launch_linear(const void* x, const void* w, int64_t T, int64_t K, int64_t N,
   if (grid <= 0) return QMOE_OK;
   if (small)
     return launch_gemm_cfg<qmoe::kModePlain, true>(tmA, tmB, a, grid, stream, "grouped_gemm_kernel<plain,small>");
+  // whole 128-row tiles of x load as one TMA box
+  CUtensorMap tmB_full = tmB;
+  if (T >= qmoe::kBNMax) {
+    QMOE_CHECK(make_tmap_bf16(&tmB_full, x, uint64_t(K), uint64_t(T), qmoe::kBK, qmoe::kBNMax));
+    a.full_boxes = 1;
+  }
   const int64_t units2 = ((T + qmoe::kBNMax - 1) / qmoe::kBNMax) * (N / (2 * qmoe::kBM));
   if (N % (2 * qmoe::kBM) == 0 && T >= kPlainPairMinRows && units2 >= num_sms(0)) {
     // prefill-sized projections with at least a unit per SM: 256-feature
@@ -709,9 +716,10 @@ int launch_linear(const void* x, const void* w, int64_t T, int64_t K, int64_t N,
     a.up_row_offset = qmoe::kBM;
     const int grid2 = int(std::min<int64_t>(units2, num_sms(0)));
     return launch_gemm_cfg<qmoe::kModePlainPair, false>(tmA, tmB, a, grid2, stream,
-                                                        "grouped_gemm_kernel<plain pair>");
+                                                        "grouped_gemm_kernel<plain pair>", &tmB_full);
   }
-  return launch_gemm_cfg<qmoe::kModePlain, false>(tmA, tmB, a, grid, stream, "grouped_gemm_kernel<plain>");
+  return launch_gemm_cfg<qmoe::kModePlain, false>(tmA, tmB, a, grid, stream, "grouped_gemm_kernel<plain>",
+                                                  &tmB_full);
 }
 
 int launch_finalize(const float* acc, const void* residual, int64_t T, int64_t H, void* out,
@@ -1577,7 +1585,7 @@ int qmoe_grouped_gemm_down_return(const void* act, const void* w_down, const int
   QMOE_CHECK(set_smem(qmoe::grouped_gemm_kernel<qmoe::kModeDownReturn>, C::kSmemBytes));
   return launch_kernel(qmoe::grouped_gemm_kernel<qmoe::kModeDownReturn>, dim3(grid), dim3(qmoe::kGemmThreads),
                        C::kSmemBytes, static_cast<cudaStream_t>(stream), true, "grouped_gemm_kernel<down_return>",
-                       tmA, tmB, a);
+                       tmA, tmB, tmB, a);
 }
 
 size_t qmoe_moe_forward_workspace_size(int64_t T, int64_t H, int64_t E, int64_t k, int64_t I) {
