@@ -281,8 +281,8 @@ namespace qmoe {
 //
 // At one token the two expert kernels above run back to back: the down
 // weights (a third of the 75 MB) only start streaming once the whole gate/up
-// grid has drained.  Here two CTAs per SM (grid-wide barrier, so every CTA
-// is resident) do, once the routing is known:
+// grid has drained.  Here one CTA per SM (grid-wide barrier, so every CTA is
+// resident) does, once the routing is known:
 //   1. TMA bulk copies of this CTA's share of the down weights -- output
 //      features [h0, h1) of every routed expert, (h1 - h0) x I contiguous
 //      bf16 per expert -- into shared memory (~170 KB at Qwen3-30B-A3B
@@ -301,7 +301,7 @@ namespace qmoe {
 constexpr int kRows1MaxTiles = 8;  // one token: at most k <= 8 tiles of one row
 
 template <int KC, int IC>  // H = 256 * KC, I = 256 * IC
-__global__ void __launch_bounds__(kGemvWarps * 32, 2)
+__global__ void __launch_bounds__(kGemvWarps * 32, 1)
     expert_rows1_kernel(const __nv_bfloat16* __restrict__ x, const int32_t* __restrict__ row_token,
                         const float* __restrict__ row_w, const __nv_bfloat16* __restrict__ w_gate_up,
                         const __nv_bfloat16* __restrict__ w_down, const int32_t* __restrict__ tiles, int max_tiles,
@@ -340,22 +340,35 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2)
         bulk_load(sdw + size_t(t) * h_per_cta * (I / 8), w_down + (size_t(meta[t].x) * H + h0) * I,
                   uint32_t(h1 - h0) * I * 2, &wbar);
   }
-  // 2. gate/up items (tile, intermediate feature), each warp's weight rows
-  //    all in flight at once (two CTAs per SM: 16 warps streaming)
+  // 2. gate/up items (tile, intermediate feature), the next item's rows in flight
   const int items = nt * I;
   const int stride = gridDim.x * kGemvWarps;
-  for (int u = blockIdx.x * kGemvWarps + warp; u < items; u += stride) {
-    const int t = u / I, i = u - t * I;
+  int u = blockIdx.x * kGemvWarps + warp;
+  uint4 gv[KC], uv[KC];
+  auto load_item = [&](int uu) {
+    const int t = uu / I, i = uu - t * I;
     const int4 m = meta[t];
-    if (m.z == 0) continue;
+    if (m.z == 0) return;
     const uint4* gr = reinterpret_cast<const uint4*>(w_gate_up + (size_t(m.x) * 2 * I + i) * H);
     const uint4* ur = reinterpret_cast<const uint4*>(w_gate_up + (size_t(m.x) * 2 * I + I + i) * H);
+#pragma unroll
+    for (int k = 0; k < KC; ++k) {
+      gv[k] = __ldg(gr + lane + 32 * k);
+      uv[k] = __ldg(ur + lane + 32 * k);
+    }
+  };
+  if (u < items) load_item(u);
+  for (; u < items; u += stride) {
+    const int t = u / I, i = u - t * I;
+    const int4 m = meta[t];
     uint4 gc[KC], uc[KC];
 #pragma unroll
     for (int k = 0; k < KC; ++k) {
-      gc[k] = __ldg(gr + lane + 32 * k);
-      uc[k] = __ldg(ur + lane + 32 * k);
+      gc[k] = gv[k];
+      uc[k] = uv[k];
     }
+    if (u + stride < items) load_item(u + stride);
+    if (m.z == 0) continue;
     const uint4* x0 = xs + lane;
     float g0 = 0.f, u0 = 0.f;
 #pragma unroll

@@ -648,7 +648,7 @@ int launch_expert_rows1(const void* x, const int32_t* row_token, const float* ro
                         int64_t I, int64_t E, void* act, const void* residual, void* out, int* grid_bar,
                         cudaStream_t s) {
   using bf16 = __nv_bfloat16;
-  const int grid = 2 * num_sms(0);  // two resident CTAs per SM
+  const int grid = num_sms(0);
   const int64_t h_per_cta = (H + grid - 1) / grid;
   const int smem = int(expert_rows1_smem(H, I, h_per_cta));
 #define QMOE_ROWS1_CASE(KC, IC)                                                                                 if (H == 256 * (KC) && I == 256 * (IC)) {                                                                        QMOE_CHECK(set_smem(qmoe::expert_rows1_kernel<KC, IC>, smem));                                                 return launch_kernel(qmoe::expert_rows1_kernel<KC, IC>, dim3(grid), dim3(qmoe::kGemvWarps * 32), size_t(smem),                          s, true, "expert_rows1_kernel", static_cast<const bf16*>(x), row_token, row_w,                                   static_cast<const bf16*>(w_gate_up), static_cast<const bf16*>(w_down), tiles,                                    int(max_tiles), int(R), int(E), int(h_per_cta), static_cast<bf16*>(act),                                        static_cast<const bf16*>(residual), static_cast<bf16*>(out), grid_bar);                 }
@@ -662,8 +662,8 @@ int launch_expert_rows1(const void* x, const int32_t* row_token, const float* ro
 
 bool expert_rows1_applies(int64_t T, int64_t H, int64_t k, int64_t I) {
   if (T != 1 || k > qmoe::kRows1MaxTiles || !(H == 1024 || H == 2048) || !(I == 512 || I == 768)) return false;
-  const int64_t grid = 2 * num_sms(0);  // two CTAs per SM must fit
-  return expert_rows1_smem(H, I, (H + grid - 1) / grid) <= 100 * 1024;
+  const int64_t grid = num_sms(0);
+  return expert_rows1_smem(H, I, (H + grid - 1) / grid) <= 200 * 1024;
 }
 
 int launch_expert_rows(const void* x, const int32_t* row_token, const float* row_w, const void* w_gate_up,
