@@ -258,9 +258,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2)
 #pragma unroll
           for (int k = 0; k < IC; ++k) d = dot8_bf16(wv[j][k], as[row * (I / 8) + lane + 32 * k], d);
           d = warp_sum(d);
-          // explicit fused multiply-add: the one-token kernel forms the same sums
-          if (tok[row] == 0) s0 = __fmaf_rn(rw[row], d, s0);
-          else if (tok[row] == 1) s1 = __fmaf_rn(rw[row], d, s1);
+          const float c = rw[row] * d;
+          if (tok[row] == 0) s0 += c;
+          else if (tok[row] == 1) s1 += c;
         }
       }
     }
@@ -268,153 +268,6 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2)
       float v = lane == 0 ? s0 : s1;
       if (residual) v += __bfloat162float(residual[size_t(lane) * H + h]);
       out[size_t(lane) * H + h] = __float2bfloat16_rn(v);
-    }
-  }
-}
-
-}  // namespace qmoe
-
-namespace qmoe {
-
-// ---------------------------------------------------------------------------
-// One-token decode: both expert GEMMs in ONE persistent kernel.
-//
-// At one token the two expert kernels above run back to back: the down
-// weights (a third of the 75 MB) only start streaming once the whole gate/up
-// grid has drained.  Here one CTA per SM (grid-wide barrier, so every CTA is
-// resident) does, once the routing is known:
-//   1. TMA bulk copies of this CTA's share of the down weights -- output
-//      features [h0, h1) of every routed expert, (h1 - h0) x I contiguous
-//      bf16 per expert -- into shared memory (~170 KB at Qwen3-30B-A3B
-//      shapes), in flight while
-//   2. its warps stream gate/up items exactly as expert_gateup_rows_kernel
-//      does (same lane mapping, same sums), with the next item's weight rows
-//      in flight while the current one is reduced;
-//   3. one grid-wide barrier: every activation row is written;
-//   4. the activation rows staged in shared memory, each warp forms output
-//      features h of [h0, h1) exactly as expert_down_rows_kernel does (tiles
-//      in tile order, the same per-lane dot products and warp sums), adds
-//      the residual and writes bf16.
-// So the result is bit-identical to the two-kernel path.  The grid-barrier
-// counter must be zero before the launch (the route kernel zeroes it).
-// ---------------------------------------------------------------------------
-constexpr int kRows1MaxTiles = 8;  // one token: at most k <= 8 tiles of one row
-
-template <int KC, int IC>  // H = 256 * KC, I = 256 * IC
-__global__ void __launch_bounds__(kGemvWarps * 32, 1)
-    expert_rows1_kernel(const __nv_bfloat16* __restrict__ x, const int32_t* __restrict__ row_token,
-                        const float* __restrict__ row_w, const __nv_bfloat16* __restrict__ w_gate_up,
-                        const __nv_bfloat16* __restrict__ w_down, const int32_t* __restrict__ tiles, int max_tiles,
-                        int R, int E, int h_per_cta, __nv_bfloat16* __restrict__ act,
-                        const __nv_bfloat16* __restrict__ residual, __nv_bfloat16* __restrict__ out,
-                        int* __restrict__ grid_bar) {
-  constexpr int H = KC * 256, I = IC * 256;
-  extern __shared__ __align__(128) uint8_t rows1_smem[];
-  uint4* sdw = reinterpret_cast<uint4*>(rows1_smem);                 // [tile][h - h0][I / 8]
-  uint4* sact = sdw + size_t(kRows1MaxTiles) * h_per_cta * (I / 8);  // [tile row][I / 8]
-  __shared__ uint4 xs[H / 8];
-  __shared__ int4 meta[kExpertRowsMaxTiles];
-  __shared__ int tok[kExpertRowsMaxR];
-  __shared__ float rw[kExpertRowsMaxR];
-  __shared__ __align__(8) uint64_t wbar;
-  __shared__ int abort_s;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h0 = blockIdx.x * h_per_cta, h1 = min(H, h0 + h_per_cta);
-  if (threadIdx.x == 0) {
-    mbar_init(&wbar, 1);
-    abort_s = 0;
-    fence_mbarrier_init();
-  }
-  griddep_wait();
-  griddep_launch_dependents();
-  for (int v = threadIdx.x; v < H / 8; v += blockDim.x) xs[v] = reinterpret_cast<const uint4*>(x)[v];
-  const int nt = min(stage_expert_tiles(tiles, max_tiles, row_token, row_w, R, E, 1, meta, tok, rw), kRows1MaxTiles);
-  // 1. this CTA's down weight rows of every routed expert into shared memory
-  if (threadIdx.x == 0 && h1 > h0) {
-    uint32_t bytes = 0;
-    for (int t = 0; t < nt; ++t)
-      if (meta[t].z) bytes += uint32_t(h1 - h0) * I * 2;
-    mbar_arrive_expect_tx(&wbar, bytes);
-    for (int t = 0; t < nt; ++t)
-      if (meta[t].z)
-        bulk_load(sdw + size_t(t) * h_per_cta * (I / 8), w_down + (size_t(meta[t].x) * H + h0) * I,
-                  uint32_t(h1 - h0) * I * 2, &wbar);
-  }
-  // 2. gate/up items (tile, intermediate feature), the next item's rows in flight
-  const int items = nt * I;
-  const int stride = gridDim.x * kGemvWarps;
-  int u = blockIdx.x * kGemvWarps + warp;
-  uint4 gv[KC], uv[KC];
-  auto load_item = [&](int uu) {
-    const int t = uu / I, i = uu - t * I;
-    const int4 m = meta[t];
-    if (m.z == 0) return;
-    const uint4* gr = reinterpret_cast<const uint4*>(w_gate_up + (size_t(m.x) * 2 * I + i) * H);
-    const uint4* ur = reinterpret_cast<const uint4*>(w_gate_up + (size_t(m.x) * 2 * I + I + i) * H);
-#pragma unroll
-    for (int k = 0; k < KC; ++k) {
-      gv[k] = __ldg(gr + lane + 32 * k);
-      uv[k] = __ldg(ur + lane + 32 * k);
-    }
-  };
-  if (u < items) load_item(u);
-  for (; u < items; u += stride) {
-    const int t = u / I, i = u - t * I;
-    const int4 m = meta[t];
-    uint4 gc[KC], uc[KC];
-#pragma unroll
-    for (int k = 0; k < KC; ++k) {
-      gc[k] = gv[k];
-      uc[k] = uv[k];
-    }
-    if (u + stride < items) load_item(u + stride);
-    if (m.z == 0) continue;
-    const uint4* x0 = xs + lane;
-    float g0 = 0.f, u0 = 0.f;
-#pragma unroll
-    for (int k = 0; k < KC; ++k) {
-      const uint4 xa = x0[32 * k];
-      g0 = dot8_bf16(gc[k], xa, g0);
-      u0 = dot8_bf16(uc[k], xa, u0);
-    }
-    g0 = warp_sum(g0);
-    u0 = warp_sum(u0);
-    if (lane == 0 && tok[m.y] >= 0) act[size_t(m.y) * I + i] = __float2bfloat16_rn(g0 / (1.0f + __expf(-g0)) * u0);
-  }
-  // 3. every activation row written, grid-wide
-  if (!grid_barrier_once(grid_bar, kDevErrWaitTimeoutEpilogue)) abort_s = 1;
-  // 4. down: activation rows into shared memory, then this CTA's features
-  for (int v = threadIdx.x; v < R * (I / 8); v += blockDim.x) sact[v] = __ldcg(reinterpret_cast<const uint4*>(act) + v);
-  __syncthreads();
-  bool ok = abort_s == 0 && h1 > h0;
-  if (h1 > h0) {
-    // every thread waits for the bulk copies (bounded): none may leave with them in flight
-    const unsigned long long t0 = globaltimer_ns();
-    while (!mbar_try_wait(&wbar, 0)) {
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
-        record_device_error(kDevErrWaitTimeoutProducer);
-        ok = false;
-        break;
-      }
-    }
-  }
-  if (!ok) return;
-  for (int h = h0 + warp; h < h1; h += kGemvWarps) {
-    float s0 = 0.f;
-    for (int t = 0; t < nt; ++t) {
-      const int4 m = meta[t];
-      if (m.z == 0) continue;
-      const uint4* wr = sdw + (size_t(t) * h_per_cta + (h - h0)) * (I / 8);
-      float d = 0.f;
-#pragma unroll
-      for (int k = 0; k < IC; ++k) d = dot8_bf16(wr[lane + 32 * k], sact[m.y * (I / 8) + lane + 32 * k], d);
-      d = warp_sum(d);
-      if (tok[m.y] == 0) s0 = __fmaf_rn(rw[m.y], d, s0);
-    }
-    if (lane == 0) {
-      float v = s0;
-      if (residual) v += __bfloat162float(residual[h]);
-      out[h] = __float2bfloat16_rn(v);
     }
   }
 }

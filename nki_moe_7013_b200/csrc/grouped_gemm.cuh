@@ -52,8 +52,7 @@ constexpr int kGemmThreads = 192;
 constexpr int kGemmTilesReady = 1;
 // split-K scratch: kSplitSlots partial slots of [2][16 rows][128 features]
 // fp32, then kSplitSlots arrival counters and 4 spare words (word kSplitSlots:
-// the grid-barrier counter of the fused decode finalisation; word
-// kSplitSlots + 1: that of the one-token expert kernel)
+// the grid-barrier counter of the fused decode finalisation)
 constexpr int kSplitSlots = 256;
 constexpr int kSplitSlotFloats = 2 * kBoxRows * kBM;
 // Per-tile unit counters of the decode forward (the down GEMM starts a tile

@@ -636,36 +636,6 @@ bool expert_rows_applies(int64_t T, int64_t H, int64_t k, int64_t I) {
          I / 256 <= 4 && T * k <= qmoe::kExpertRowsMaxR && T * k * I * 2 <= 96 * 1024;
 }
 
-// One token, both expert GEMMs in one persistent kernel (expert_rows1_kernel):
-// shared memory for this CTA's share of the down weights of every routed
-// expert, plus the activation rows.
-size_t expert_rows1_smem(int64_t H, int64_t I, int64_t h_per_cta) {
-  return size_t(qmoe::kRows1MaxTiles) * h_per_cta * I * 2 + size_t(qmoe::kRows1MaxTiles) * I * 2;
-}
-
-int launch_expert_rows1(const void* x, const int32_t* row_token, const float* row_w, const void* w_gate_up,
-                        const void* w_down, const int32_t* tiles, int64_t max_tiles, int64_t R, int64_t H,
-                        int64_t I, int64_t E, void* act, const void* residual, void* out, int* grid_bar,
-                        cudaStream_t s) {
-  using bf16 = __nv_bfloat16;
-  const int grid = num_sms(0);
-  const int64_t h_per_cta = (H + grid - 1) / grid;
-  const int smem = int(expert_rows1_smem(H, I, h_per_cta));
-#define QMOE_ROWS1_CASE(KC, IC)                                                                                 if (H == 256 * (KC) && I == 256 * (IC)) {                                                                        QMOE_CHECK(set_smem(qmoe::expert_rows1_kernel<KC, IC>, smem));                                                 return launch_kernel(qmoe::expert_rows1_kernel<KC, IC>, dim3(grid), dim3(qmoe::kGemvWarps * 32), size_t(smem),                          s, true, "expert_rows1_kernel", static_cast<const bf16*>(x), row_token, row_w,                                   static_cast<const bf16*>(w_gate_up), static_cast<const bf16*>(w_down), tiles,                                    int(max_tiles), int(R), int(E), int(h_per_cta), static_cast<bf16*>(act),                                        static_cast<const bf16*>(residual), static_cast<bf16*>(out), grid_bar);                 }
-  QMOE_ROWS1_CASE(8, 3)
-  QMOE_ROWS1_CASE(4, 3)
-  QMOE_ROWS1_CASE(8, 2)
-  QMOE_ROWS1_CASE(4, 2)
-#undef QMOE_ROWS1_CASE
-  return set_error(QMOE_ERR_UNSUPPORTED_SHAPE, "expert rows1: H=%lld I=%lld", (long long)H, (long long)I);
-}
-
-bool expert_rows1_applies(int64_t T, int64_t H, int64_t k, int64_t I) {
-  if (T != 1 || k > qmoe::kRows1MaxTiles || !(H == 1024 || H == 2048) || !(I == 512 || I == 768)) return false;
-  const int64_t grid = num_sms(0);
-  return expert_rows1_smem(H, I, (H + grid - 1) / grid) <= 200 * 1024;
-}
-
 int launch_expert_rows(const void* x, const int32_t* row_token, const float* row_w, const void* w_gate_up,
                        const void* w_down, const int32_t* tiles, int64_t max_tiles, int64_t R, int64_t H,
                        int64_t I, int64_t E, int64_t T, void* act, const void* residual, void* out,
@@ -900,11 +870,6 @@ int moe_forward_on(const void* x, const void* w_router, const float* router_bias
   }
   // 1-2 tokens: the expert GEMMs are matrix-vector products, run on the CUDA
   // cores; the down kernel also adds the residual and writes the output
-  if (split_counters && expert_rows1_applies(T, H, k, I))
-    // one token: both expert GEMMs in one kernel; its grid barrier uses a
-    // spare word of the split-K counters, which the route kernel zeroed
-    return launch_expert_rows1(x, row_token, row_w, w_gate_up, w_down, tiles, max_tiles, R, H, I, E, act,
-                               residual, out, split_counters + qmoe::kSplitSlots + 1, s);
   if (expert_rows_applies(T, H, k, I))
     return launch_expert_rows(x, row_token, row_w, w_gate_up, w_down, tiles, max_tiles, R, H, I, E, T, act,
                               residual, out, s);
