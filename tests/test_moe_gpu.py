@@ -382,3 +382,27 @@ def test_decode_expert_rows_match_tensor_core_path(cuda_dev, oracle, T, H, E, k,
     assert max_rel_err(to_f32_np(out), to_f32_np(staged)) <= 1e-2
     ref = oracle.moe_block(x.cpu(), wr.cpu(), wgu.cpu(), wd.cpu(), k) + to_f32_np(res)
     assert max_rel_err(to_f32_np(out), ref) <= MAX_REL
+
+
+@pytest.mark.parametrize("H,E,k,I", [(2048, 128, 8, 768), (1024, 64, 8, 512), (2048, 32, 4, 768)])
+def test_one_token_forward_matches_row_of_two_token_forward(cuda_dev, H, E, k, I):
+    """The decode expert kernels sum each token's expert outputs in ascending
+    expert order with no atomics, so a token's result does not depend on the
+    batch around it: a one-token forward equals row 0 of a two-token forward
+    bit for bit -- with and without a residual, call after call."""
+    from nki_moe_7013_b200 import _C, ops
+
+    wr, wgu, wd = moe_weights(130 + E, E, H, I, cuda_dev)
+    x2 = activations(131, 2, H, cuda_dev)
+    res2 = activations(132, 2, H, cuda_dev)
+    two, idx2, _ = ops.moe_forward(x2, wr, wgu, wd, k, residual=res2, return_routing=True)
+    two_nr = ops.moe_forward(x2, wr, wgu, wd, k)
+    for _ in range(2):
+        one, idx1, _ = ops.moe_forward(x2[:1].contiguous(), wr, wgu, wd, k, residual=res2[:1].contiguous(),
+                                       return_routing=True)
+        one_nr = ops.moe_forward(x2[:1].contiguous(), wr, wgu, wd, k)
+        torch.cuda.synchronize()
+        assert _C.device_error() == 0
+        assert torch.equal(idx1[0], idx2[0])
+        assert torch.equal(one[0], two[0])
+        assert torch.equal(one_nr[0], two_nr[0])
