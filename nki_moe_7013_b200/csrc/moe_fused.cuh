@@ -68,8 +68,11 @@ struct FusedCfg {
   static constexpr int kTmemCols = 512;
   static constexpr int kBarrierBytes = 256;
   static constexpr int kUnitQueue = 4;
-  static constexpr int kStagingBytes = 4 * 16 * 33 * 4 + kMaxRows * 12;
+  // per-warp transpose tiles, then per row: destination, weight, source
+  // rank and (return epilogue) the row's address in its return buffer
+  static constexpr int kStagingBytes = 4 * 16 * 33 * 4 + kMaxRows * 20;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes + kStagingBytes;
+  static_assert(1024 + kStages * kStageBytes + kBarrierBytes + kStagingBytes <= 232448, "227 KB per CTA");
 };
 
 struct FusedArgs {
@@ -504,6 +507,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int32_t* meta_dst = reinterpret_cast<int32_t*>(staging + 4 * 16 * 33);
     float* meta_w = reinterpret_cast<float*>(meta_dst + C::kMaxRows);
     int32_t* meta_src = meta_dst + 2 * C::kMaxRows;
+    __nv_bfloat16** meta_ptr = reinterpret_cast<__nv_bfloat16**>(meta_dst + 3 * C::kMaxRows);
     AccSeq acc;
     for (int local = 0;; ++local) {
       const int q = local % C::kUnitQueue;
@@ -521,12 +525,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int buf = acc.next;
       int my_dst = -1, my_src = 0;
       float my_w = 0.f;
+      __nv_bfloat16* my_ptr = nullptr;
       if (!gu && et < nrows) {
         if constexpr (kReturn) {
           const int4 m4 = args.row_meta[row0 + et];
           my_w = __int_as_float(m4.x);
           my_src = (m4.y >= 0 && m4.y < args.n_ranks) ? m4.y : -1;
           my_dst = my_src >= 0 ? m4.z : -1;
+          if (my_dst >= 0 && my_dst < args.n_acc)
+            my_ptr = args.peer_ret[my_src] + (size_t(args.ret_row0) + my_dst) * args.acc_ld;
         } else {
           my_dst = args.row_dst[row0 + et];
           my_w = args.row_w[row0 + et];
@@ -539,6 +546,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         meta_dst[et] = (my_dst >= 0 && my_dst < args.n_acc) ? my_dst : -1;
         meta_w[et] = my_w;
         meta_src[et] = my_src;
+        if constexpr (kReturn) meta_ptr[et] = my_ptr;
         named_barrier_sync(1, 128);
       }
       tc_fence_after();
@@ -571,32 +579,45 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
             for (int i = 0; i < 16; ++i) wsb[i * 33 + lane] = __uint_as_float(v[i]);
             __syncwarp();
-            const int fq = (lane & 7) * 4;
-            const int fcol = (mt * (1 + args.dn_two) + h) * kBM + quad * 32 + fq;
+            if constexpr (kReturn) {
+              // weighted row segments straight into the source ranks' return
+              // buffers: a lane stores 8 consecutive features (16 bytes) of
+              // one row, 8 rows per pass (row stride 33 words: conflict-free)
+              const int f8 = (lane & 3) * 8;
+              const int fcol = (mt * (1 + args.dn_two) + h) * kBM + quad * 32 + f8;
 #pragma unroll
-            for (int it = 0; it < 4; ++it) {
-              const int i = it * 4 + (lane >> 3);
-              const int n = c * 16 + i;
-              if (n < nrows) {
-                const int dst = meta_dst[n];
-                if (dst >= 0) {
-                  const float wv = meta_w[n];
-                  if constexpr (kReturn) {
-                    // weighted row segment straight into the source rank's return buffer
-                    __nv_bfloat16* ret =
-                        args.peer_ret[meta_src[n]] + (size_t(args.ret_row0) + dst) * args.acc_ld + fcol;
-                    const __nv_bfloat162 lo =
-                        __floats2bfloat162_rn(wv * wsb[i * 33 + fq], wv * wsb[i * 33 + fq + 1]);
-                    const __nv_bfloat162 hi =
-                        __floats2bfloat162_rn(wv * wsb[i * 33 + fq + 2], wv * wsb[i * 33 + fq + 3]);
-                    uint2 pk;
-                    pk.x = *reinterpret_cast<const uint32_t*>(&lo);
-                    pk.y = *reinterpret_cast<const uint32_t*>(&hi);
-                    *reinterpret_cast<uint2*>(ret) = pk;
-                  } else {
-                    red_add_v4_f32(args.acc + size_t(dst) * args.acc_ld + fcol,
-                                   wv * wsb[i * 33 + fq], wv * wsb[i * 33 + fq + 1], wv * wsb[i * 33 + fq + 2],
-                                   wv * wsb[i * 33 + fq + 3]);
+              for (int it = 0; it < 2; ++it) {
+                const int i = it * 8 + (lane >> 2);
+                const int n = c * 16 + i;
+                if (n < nrows) {
+                  __nv_bfloat16* ret = meta_ptr[n];
+                  if (ret != nullptr) {
+                    const float wv = meta_w[n];
+                    const float* sv = wsb + i * 33 + f8;
+                    uint4 pk;
+                    uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                      const __nv_bfloat162 b2 = __floats2bfloat162_rn(wv * sv[2 * j], wv * sv[2 * j + 1]);
+                      pw[j] = *reinterpret_cast<const uint32_t*>(&b2);
+                    }
+                    *reinterpret_cast<uint4*>(ret + fcol) = pk;
+                  }
+                }
+              }
+            } else {
+              const int fq = (lane & 7) * 4;
+              const int fcol = (mt * (1 + args.dn_two) + h) * kBM + quad * 32 + fq;
+#pragma unroll
+              for (int it = 0; it < 4; ++it) {
+                const int i = it * 4 + (lane >> 3);
+                const int n = c * 16 + i;
+                if (n < nrows) {
+                  const int dst = meta_dst[n];
+                  if (dst >= 0) {
+                    const float wv = meta_w[n];
+                    red_add_v4_f32(args.acc + size_t(dst) * args.acc_ld + fcol, wv * wsb[i * 33 + fq],
+                                   wv * wsb[i * 33 + fq + 1], wv * wsb[i * 33 + fq + 2], wv * wsb[i * 33 + fq + 3]);
                   }
                 }
               }

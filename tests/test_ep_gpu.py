@@ -50,6 +50,40 @@ def test_ep_pack_unpack_bit_exact(cuda_dev, oracle, T, E, k, P):
     assert np.array_equal(to_f32_np(out), oracle.round_to_bf16(exp.astype(np.float32)))
 
 
+@pytest.mark.parametrize("T", [37, 300, 1024])
+def test_experts_return_loopback_matches_forward(cuda_dev, T):
+    """The EP experts kernel with its return epilogue, run with this GPU as
+    the only rank (the return buffer is local): every weighted row lands in
+    its return row, and each token's k rows summed in fp32 (ep_unpack) match
+    the single-GPU forward within the activation bar."""
+    from nki_moe_7013_b200 import _C, ops
+
+    E, H, I, k = 128, 2048, 768, 8
+    wr, wgu, wd = moe_weights(50 + T, E, H, I, cuda_dev)
+    x = activations(50 + T, T, H, cuda_dev)
+    ref = ops.moe_forward(x, wr, wgu, wd, k)
+    p = ops.route_permute(x, wr, k)
+    R, mt = T * k, p["max_tiles"]
+    # return row of permuted row r = r; unpack reads token t's rows through slot_row
+    meta = torch.zeros((R, 4), dtype=torch.int32, device=cuda_dev)
+    meta[:, 0] = p["row_w"].view(torch.int32)
+    meta[:, 2] = torch.arange(R, dtype=torch.int32, device=cuda_dev)
+    y_rows = torch.full((R, H), float("nan"), dtype=torch.bfloat16, device=cuda_dev)
+    peer = torch.tensor([y_rows.data_ptr()], dtype=torch.int64, device=cuda_dev)
+    act = torch.empty((R, I), dtype=torch.bfloat16, device=cuda_dev)
+    done = torch.zeros(mt + 2, dtype=torch.int32, device=cuda_dev)
+    s = torch.cuda.current_stream(cuda_dev).cuda_stream
+    _C.check(_C.lib().qmoe_moe_experts_return(
+        p["x_perm"].data_ptr(), wgu.data_ptr(), wd.data_ptr(), p["tiles"].data_ptr(), mt, meta.data_ptr(),
+        peer.data_ptr(), 0, R, 1, R, H, I, E, act.data_ptr(), done.data_ptr(), s), "qmoe_moe_experts_return")
+    out = ops.ep_unpack(y_rows, p["slot_row"], None)
+    torch.cuda.synchronize()
+    assert _C.device_error() == 0
+    assert not torch.isnan(y_rows.float()).any(), "a return row was not written"
+    err = max_rel_err(out.float().cpu().numpy(), ref.float().cpu().numpy())
+    assert err <= MAX_REL, err
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
