@@ -885,14 +885,23 @@ def run_ours_ep(args):
     hbm_gbs, tf_burst, tf_sust, peak_kind = load_peaks()
     recv_rows = int(moe.recv_rows.item())
     idx = moe.topk_idx[:T]
-    remote_sent = int((idx // el != rank).sum().item())     # my rows that leave this GPU
+    remote_sent = int((idx // el != rank).sum().item())     # my (token, slot) rows served elsewhere
     local_rows = T * K_TOP - remote_sent
-    remote_recv = recv_rows - local_rows                    # rows other ranks sent me
+    remote_recv = recv_rows - local_rows                    # (token, slot) rows other ranks sent me
+    # dispatch sends each token row once per destination rank
+    present = torch.zeros((T, world), dtype=torch.int32, device=dev).scatter_(1, idx.long() // el, 1)
+    tok_to = present.sum(0)
+    tok_in = tok_to.clone()
+    if world > 1:
+        torch.distributed.all_reduce(tok_in)
+    tok_sent_remote = int(tok_to.sum().item() - tok_to[rank].item())
+    tok_recv_remote = int(tok_in[rank].item() - tok_to[rank].item())
     # expert GEMM FLOPs of this rank's experts, and the bytes that must
-    # cross NVLink per direction: rows out (dispatch) + rows I return out
+    # cross NVLink per direction: token rows out (dispatch) + weighted rows I
+    # return out, and token rows in + my weighted rows coming back
     flops_rank = recv_rows * 6 * H * I_MOE
-    nvl_out = (remote_sent + remote_recv) * H * 2
-    nvl_in = (remote_recv + remote_sent) * H * 2
+    nvl_out = (tok_sent_remote + remote_recv) * H * 2
+    nvl_in = (tok_recv_remote + remote_sent) * H * 2
     nvl_gbs_ref = 770.0
     t_tensor_us = flops_rank / (tf_burst * 1e12) * 1e6
     t_nvlink_us = max(nvl_out, nvl_in) / (nvl_gbs_ref * 1e9) * 1e6
@@ -1013,7 +1022,9 @@ def run_ours_ep(args):
                      "step_tensor_frac_of_sustained": step_tflops / tf_sust if tf_sust else None,
                      "nvlink": {"bytes_out_per_step": nvl_out, "bytes_in_per_step": nvl_in,
                                 "link_gbs_reference": nvl_gbs_ref,
-                                "dispatch_gbs": (remote_sent * H * 2) / (stage_us["dispatch"] * 1e-6) / 1e9},
+                                "dispatch_token_rows_out": tok_sent_remote,
+                                "dispatch_rows_undeduplicated": remote_sent,
+                                "dispatch_gbs": (tok_sent_remote * H * 2) / (stage_us["dispatch"] * 1e-6) / 1e9},
                      "step_target_us": target_us,
                      "step_target": {"tensor_us": t_tensor_us, "nvlink_us": t_nvlink_us, "weights_us": t_weights_us},
                      "step_frac_of_target": target_us / (ms_per_step * 1e3)},

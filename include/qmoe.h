@@ -467,9 +467,16 @@ QMOE_API int qmoe_ep_unpack(const void* y_back, const int32_t* pair_pos, const v
  *   buffer; the tile list of the local experts over this rank's receive
  *   buffer (expert ids local, 0..e_local-1); and recv_rows[0]; and zero-fills
  *   zero_words (n_zero_words int32, or NULL / 0).
- * qmoe_ep_dispatch: copies every (token, slot) row of x straight into the
- *   owner's receive buffer (peer_recv_x[d] + (parity*cap_rows + row)*H) with
- *   meta {weight bits, source rank, token*k + slot, 0} (int4 per row).
+ * qmoe_ep_dispatch: copies each token row of x ONCE to every rank d that
+ *   owns one of its experts, into d's token buffer at row
+ *   xrow = (parity*n_ranks + me)*max_tokens + token (peer_tok[d] + xrow*H),
+ *   and writes each (token, slot)'s entry of d's expert-grouped receive
+ *   list: peer_recv_meta[d][parity*cap_rows + row] = {weight bits, source
+ *   rank, token*k + slot, xrow} (int4).  T <= max_tokens.
+ * qmoe_ep_wait_expand: flags this rank's dispatch in every peer, waits
+ *   (bounded) for every rank's flag, then copies, for r < recv_rows[0], token
+ *   buffer row recv_meta[r].w of `tok` (tok_rows rows) into recv_x row r;
+ *   recv_meta and recv_x point at this parity's half.
  * qmoe_ep_signal_wait: one warp; flag `kind` (1 dispatch, 2 combine) of this
  *   rank in every peer, then wait (bounded) for every rank's flag; kind 2
  *   with epoch 0 then advances the step counter.
@@ -494,9 +501,13 @@ QMOE_API int qmoe_ep_exchange_counts(const int32_t* counts, int* const* peer_ctr
                                      int64_t n_zero_words, void* stream);
 QMOE_API int qmoe_ep_dispatch(const void* x, const int32_t* topk_idx, const float* topk_w,
                               const int32_t* slot_row, const int32_t* offsets, const int32_t* dest_base,
-                              void* const* peer_recv_x, void* const* peer_recv_meta, int64_t T, int64_t k,
-                              int64_t H, int64_t e_local, int64_t me, int64_t parity, int64_t cap_rows,
-                              void* stream);
+                              void* const* peer_tok, void* const* peer_recv_meta, int64_t T, int64_t k,
+                              int64_t H, int64_t e_local, int64_t me, int64_t n_ranks, int64_t parity,
+                              int64_t cap_rows, int64_t max_tokens, void* stream);
+QMOE_API int qmoe_ep_wait_expand(int* const* peer_ctrl, int* my_ctrl, int64_t n_ranks, int64_t E, int64_t me,
+                                 int64_t parity, int64_t epoch, const void* tok, int64_t tok_rows,
+                                 const void* recv_meta, void* recv_x, const int32_t* recv_rows,
+                                 int64_t cap_rows, int64_t H, void* stream);
 QMOE_API int qmoe_ep_signal_wait(int* const* peer_ctrl, int* my_ctrl, int64_t n_ranks, int64_t E,
                                  int64_t me, int64_t parity, int64_t kind, int64_t epoch, void* stream);
 QMOE_API int qmoe_moe_experts_return(const void* x, const void* w_gate_up, const void* w_down, const int32_t* tiles,

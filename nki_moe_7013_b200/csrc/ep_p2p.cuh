@@ -9,11 +9,17 @@
 //                      source rank, then by token),
 //        the tile list of my local experts over my receive buffer, and the
 //        number of rows I receive;
-//   2. ep_dispatch: each (token, slot) row of x goes straight from x into the
-//      destination rank's receive buffer (peer stores), with its routing
-//      weight and its return address (source rank, token*k + slot);
-//   3. ep_signal_wait: flag every peer "my rows are in your buffer", wait for
-//      everyone's flag;
+//   2. ep_dispatch: each token row crosses to every rank that owns one of
+//      its experts ONCE (peer stores into that rank's token buffer, at a
+//      fixed row per (parity, source rank, token)), and each (token, slot)
+//      leaves its meta in the destination's expert-grouped receive list:
+//      routing weight, return address (source rank, token*k + slot) and the
+//      token buffer row (a token whose 8 experts sit on 5 ranks sends 5
+//      rows instead of 8);
+//   3. ep_wait_expand: flag every peer "my rows are in your buffer", wait for
+//      everyone's flag, then copy each receive-list entry's token row into
+//      the expert-grouped receive rows (local memory, so the expert kernel
+//      reads whole 128-row tiles with one TMA box per stage);
 //   4. grouped gate/up + down GEMMs on the receive buffer; the down epilogue
 //      writes each weighted bf16 row back into the SOURCE rank's return
 //      buffer through peer stores (the combine, fused into the GEMM);
@@ -193,15 +199,18 @@ __global__ void __launch_bounds__(256)
 }
 
 // ---------------------------------------------------------------------------
-// 2. dispatch: one warp per (token, slot) row, grid-stride
-//   recv row meta = {weight bits, source rank, token*k + slot, 0}
+// 2. dispatch: one warp per (token, slot), grid-stride
+//   token buffer row of (parity p, source me, token t): (p*N + me)*max_tokens + t
+//   receive-list meta = {weight bits, source rank, token*k + slot, token buffer row}
+//   The row itself is stored by the warp of the token's first slot on each
+//   destination rank (experts of one token are distinct; slots are few).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256)
     ep_dispatch_kernel(const __nv_bfloat16* __restrict__ x, const int32_t* __restrict__ topk_idx,
                        const float* __restrict__ topk_w, const int32_t* __restrict__ slot_row,
                        const int32_t* __restrict__ offsets, const int32_t* __restrict__ dest_base,
-                       __nv_bfloat16* const* __restrict__ peer_recv_x, int4* const* __restrict__ peer_recv_meta,
-                       int T, int k, int H, int e_local, int me, int p, int cap_rows) {
+                       __nv_bfloat16* const* __restrict__ peer_tok, int4* const* __restrict__ peer_recv_meta,
+                       int T, int k, int H, int e_local, int me, int N, int p, int cap_rows, int max_tokens) {
   griddep_wait();
   griddep_launch_dependents();
   const int lane = threadIdx.x & 31;
@@ -209,24 +218,78 @@ __global__ void __launch_bounds__(256)
   const int vec = H / 8;  // 16-byte vectors per row
   for (int i = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); i < T * k; i += warps) {
     const int t = i / k;
+    const int j = i - t * k;
     const int e = topk_idx[i];
     const int d = e / e_local;
     const int row = dest_base[e] + (slot_row[i] - offsets[e]);
-    if (row < 0 || row >= cap_rows) {
+    if (row < 0 || row >= cap_rows || d < 0 || d >= N || t >= max_tokens) {
       if (lane == 0) record_device_error(kDevErrBadIndex);
       continue;
     }
-    const uint4* src = reinterpret_cast<const uint4*>(x + size_t(t) * H);
-    uint4* dst = reinterpret_cast<uint4*>(peer_recv_x[d] + (size_t(p) * cap_rows + row) * H);
-    for (int v = lane; v < vec; v += 32) dst[v] = src[v];
+    const int xrow = (p * N + me) * max_tokens + t;
+    bool first = true;
+    for (int jj = 0; jj < j; ++jj) first &= topk_idx[t * k + jj] / e_local != d;
+    if (first) {
+      const uint4* src = reinterpret_cast<const uint4*>(x + size_t(t) * H);
+      uint4* dst = reinterpret_cast<uint4*>(peer_tok[d] + size_t(xrow) * H);
+      for (int v = lane; v < vec; v += 32) dst[v] = src[v];
+    }
     if (lane == 0)
-      peer_recv_meta[d][size_t(p) * cap_rows + row] = make_int4(__float_as_int(topk_w[i]), me, i, 0);
+      peer_recv_meta[d][size_t(p) * cap_rows + row] = make_int4(__float_as_int(topk_w[i]), me, i, xrow);
   }
   __threadfence_system();
 }
 
 // ---------------------------------------------------------------------------
-// 3. signal + wait (one warp)
+// 3. signal, wait, expand: CTA 0 flags every peer "my rows are in your
+// buffer"; every CTA waits (bounded) for every peer's flag, then the CTAs copy
+// receive-list entry r's token row into receive row r (one warp per row,
+// grid-stride; rows past recv_rows are left alone).  On a time-out the rows
+// are not copied (the device error is set; the step's results are void).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+    ep_wait_expand_kernel(int* const* __restrict__ peer_ctrl, int* __restrict__ my_ctrl, int N, int E, int me,
+                          int p, int epoch, const __nv_bfloat16* __restrict__ tok, int tok_rows,
+                          const int4* __restrict__ recv_meta, __nv_bfloat16* __restrict__ recv_x,
+                          const int32_t* __restrict__ recv_rows, int cap_rows, int H) {
+  __shared__ int ok_s;
+  griddep_wait();
+  griddep_launch_dependents();
+  if (!ep_resolve_epoch(my_ctrl, N, E, p, epoch)) return;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x < 32) {
+    if (blockIdx.x == 0) {
+      __threadfence_system();
+      __syncwarp();
+      for (int d = lane; d < N; d += 32)
+        st_release_sys(peer_ctrl[d] + ep_flag_word(N, E, p, kEpFlagDispatch, me), epoch);
+    }
+    bool ok = true;
+    for (int s = lane; s < N; s += 32)
+      ok &= ep_wait_flag(my_ctrl + ep_flag_word(N, E, p, kEpFlagDispatch, s), epoch, kDevErrPeerTimeout);
+    ok = __all_sync(0xFFFFFFFFu, ok);
+    __threadfence_system();
+    if (lane == 0) ok_s = ok;
+  }
+  __syncthreads();
+  if (!ok_s) return;
+  const int n = min(recv_rows[0], cap_rows);
+  const int warps = gridDim.x * (blockDim.x / 32);
+  const int vec = H / 8;
+  for (int r = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); r < n; r += warps) {
+    const int xrow = __ldcg(&recv_meta[r].w);
+    if (xrow < 0 || xrow >= tok_rows) {
+      if (lane == 0) record_device_error(kDevErrBadIndex);
+      continue;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(tok + size_t(xrow) * H);
+    uint4* dst = reinterpret_cast<uint4*>(recv_x + size_t(r) * H);
+    for (int v = lane; v < vec; v += 32) dst[v] = __ldcg(src + v);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 4. signal + wait (one warp)
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(32)
     ep_signal_wait_kernel(int* const* __restrict__ peer_ctrl, int* __restrict__ my_ctrl, int N, int E, int me,

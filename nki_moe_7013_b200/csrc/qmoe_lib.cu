@@ -1494,13 +1494,15 @@ int qmoe_ep_exchange_counts(const int32_t* counts, int* const* peer_ctrl, int* m
 }
 
 int qmoe_ep_dispatch(const void* x, const int32_t* topk_idx, const float* topk_w, const int32_t* slot_row,
-                     const int32_t* offsets, const int32_t* dest_base, void* const* peer_recv_x,
+                     const int32_t* offsets, const int32_t* dest_base, void* const* peer_tok,
                      void* const* peer_recv_meta, int64_t T, int64_t k, int64_t H, int64_t e_local, int64_t me,
-                     int64_t parity, int64_t cap_rows, void* stream) {
-  QMOE_REQUIRE(x && topk_idx && topk_w && slot_row && offsets && dest_base && peer_recv_x && peer_recv_meta,
+                     int64_t n_ranks, int64_t parity, int64_t cap_rows, int64_t max_tokens, void* stream) {
+  QMOE_REQUIRE(x && topk_idx && topk_w && slot_row && offsets && dest_base && peer_tok && peer_recv_meta,
                QMOE_ERR_INVALID_ARGUMENT, "ep_dispatch: null pointer");
   QMOE_REQUIRE(T >= 0 && k >= 1 && k <= 32 && T * k < (int64_t(1) << 31) && H > 0 && H % 8 == 0 &&
-                   e_local >= 1 && (parity == 0 || parity == 1) && cap_rows > 0,
+                   e_local >= 1 && n_ranks >= 1 && n_ranks <= 32 && me >= 0 && me < n_ranks &&
+                   (parity == 0 || parity == 1) && cap_rows > 0 && T <= max_tokens &&
+                   2 * n_ranks * max_tokens < (int64_t(1) << 31),
                QMOE_ERR_INVALID_ARGUMENT, "ep_dispatch: bad sizes");
   QMOE_REQUIRE(aligned16(x), QMOE_ERR_MISALIGNED, "ep_dispatch: x not 16-byte aligned");
   DeviceInfo* d = nullptr;
@@ -1509,9 +1511,30 @@ int qmoe_ep_dispatch(const void* x, const int32_t* topk_idx, const float* topk_w
   const int grid = int(std::min<int64_t>((T * k + 7) / 8, 4 * int64_t(d->sms)));
   return launch_kernel(qmoe::ep_dispatch_kernel, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream), true,
                        "ep_dispatch_kernel", static_cast<const __nv_bfloat16*>(x), topk_idx, topk_w, slot_row,
-                       offsets, dest_base, reinterpret_cast<__nv_bfloat16* const*>(peer_recv_x),
+                       offsets, dest_base, reinterpret_cast<__nv_bfloat16* const*>(peer_tok),
                        reinterpret_cast<int4* const*>(peer_recv_meta), int(T), int(k), int(H), int(e_local),
-                       int(me), int(parity), int(cap_rows));
+                       int(me), int(n_ranks), int(parity), int(cap_rows), int(max_tokens));
+}
+
+int qmoe_ep_wait_expand(int* const* peer_ctrl, int* my_ctrl, int64_t n_ranks, int64_t E, int64_t me,
+                        int64_t parity, int64_t epoch, const void* tok, int64_t tok_rows, const void* recv_meta,
+                        void* recv_x, const int32_t* recv_rows, int64_t cap_rows, int64_t H, void* stream) {
+  QMOE_REQUIRE(peer_ctrl && my_ctrl && tok && recv_meta && recv_x && recv_rows, QMOE_ERR_INVALID_ARGUMENT,
+               "ep_wait_expand: null pointer");
+  QMOE_REQUIRE(n_ranks >= 1 && n_ranks <= 32 && me >= 0 && me < n_ranks && (parity == 0 || parity == 1) &&
+                   epoch >= 0 && epoch < (int64_t(1) << 31) && E >= 1 && tok_rows > 0 &&
+                   tok_rows < (int64_t(1) << 31) && cap_rows > 0 && cap_rows < (int64_t(1) << 31) && H > 0 &&
+                   H % 8 == 0,
+               QMOE_ERR_INVALID_ARGUMENT, "ep_wait_expand: bad arguments");
+  QMOE_REQUIRE(aligned16(tok) && aligned16(recv_x) && aligned16(recv_meta), QMOE_ERR_MISALIGNED,
+               "ep_wait_expand: buffers not 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  return launch_kernel(qmoe::ep_wait_expand_kernel, dim3(d->sms), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                       true, "ep_wait_expand_kernel", peer_ctrl, my_ctrl, int(n_ranks), int(E), int(me),
+                       int(parity), int(epoch), static_cast<const __nv_bfloat16*>(tok), int(tok_rows),
+                       static_cast<const int4*>(recv_meta), static_cast<__nv_bfloat16*>(recv_x), recv_rows,
+                       int(cap_rows), int(H));
 }
 
 int qmoe_ep_signal_wait(int* const* peer_ctrl, int* my_ctrl, int64_t n_ranks, int64_t E, int64_t me,

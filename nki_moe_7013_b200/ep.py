@@ -131,12 +131,14 @@ class PeerEPExchange:
     all of them).
 
     Buffers (identical shapes on every rank, two parity halves each):
-    receive rows (P*max_tokens*k, H), their meta, return rows
-    (max_tokens*k, H), and the control block (counts + flags + the rank's
-    step counter); plus the routing buffers of the local tokens.  The
-    receive, meta, return and control buffers are exported with CUDA IPC and
-    every peer's copy is mapped here (``peer``: name -> int64 tensor of the P
-    device pointers).  Creating one is collective over ``group``."""
+    token rows (P*max_tokens, H: one region per source rank, each token row
+    sent once per destination), the expert-grouped receive list (meta) and
+    receive rows (P*max_tokens*k, H), return rows (max_tokens*k, H), and the
+    control block (counts + flags + the rank's step counter); plus the
+    routing buffers of the local tokens.  The token, meta, return and control
+    buffers are exported with CUDA IPC and every peer's copy is mapped here
+    (``peer``: name -> int64 tensor of the P device pointers).  Creating one
+    is collective over ``group``."""
 
     def __init__(self, cfg: Qwen3MoeConfig, max_tokens: int, group=None, device=None):
         from . import _C
@@ -158,6 +160,8 @@ class PeerEPExchange:
         self.ret_rows = max_tokens * k                  # return rows per parity
         i32 = dict(dtype=torch.int32, device=dev)
         f32 = dict(dtype=torch.float32, device=dev)
+        self.tok_rows = 2 * self.world * max_tokens     # token rows, both parities
+        self.tok = torch.empty((self.tok_rows, H), dtype=torch.bfloat16, device=dev)
         self.recv_x = torch.empty((2 * self.cap, H), dtype=torch.bfloat16, device=dev)
         self.recv_meta = torch.zeros((2 * self.cap, 4), **i32)
         self.ret = torch.empty((2 * self.ret_rows, H), dtype=torch.bfloat16, device=dev)
@@ -185,7 +189,7 @@ class PeerEPExchange:
         self.sms = torch.cuda.get_device_properties(dev).multi_processor_count
         torch.cuda.synchronize(dev)
         self._imported = []
-        names = ("recv_x", "recv_meta", "ret", "ctrl")
+        names = ("tok", "recv_meta", "ret", "ctrl")
         mine = {}
         for n in names:
             h = ctypes.create_string_buffer(64)
@@ -225,7 +229,8 @@ class PeerEPExchange:
     def launches_per_step(self, T: int) -> int:
         """Kernels one step launches: route (router + permutation: one launch
         up to one router chunk per SM and T > 64, else router + scan +
-        scatter), count exchange, dispatch, signal, experts, signal, unpack."""
+        scatter), count exchange, dispatch, signal + wait + expand, experts,
+        signal, unpack."""
         nchunks = (T + ops.ROUTER_CHUNK - 1) // ops.ROUTER_CHUNK
         one = T > ops.ROUTER_SMALL_MAX_T and nchunks <= self.sms
         return (1 if one else 3) + 6
@@ -237,10 +242,12 @@ class PeerExpertParallelMoE(nn.Module):
     a step is a fixed sequence of stream-ordered kernels.
 
     Kernels per step: router, permutation (counts / offsets / slot rows),
-    count exchange, dispatch (rows of x straight into the owners' receive
-    buffers, already grouped by expert), signal/wait, gate/up + down in one
-    persistent kernel on the receive buffer whose down epilogue stores the
-    weighted rows into the source ranks' return buffers, signal/wait, unpack.
+    count exchange, dispatch (each token row once to every rank owning one
+    of its experts, plus a receive-list entry per (token, slot), grouped by
+    expert), signal/wait and the local expansion of the receive list into
+    expert-grouped rows, gate/up + down in one persistent kernel on those
+    rows whose down epilogue stores the weighted rows into the source ranks'
+    return buffers, signal/wait, unpack.
 
     The buffers live in a ``PeerEPExchange`` (``exchange``): pass one shared
     exchange to every block of a decoder stack, or let the block create its
@@ -340,12 +347,13 @@ class PeerExpertParallelMoE(nn.Module):
         mark(2)
         _C.check(lib.qmoe_ep_dispatch(
             pt(x), pt(X.topk_idx), pt(X.topk_w), pt(X.slot_row), pt(X.offsets), pt(X.dest_base),
-            pt(X.peer["recv_x"]), pt(X.peer["recv_meta"]), T, k, H, self.e_local, self.rank, par,
-            X.cap, s), "qmoe_ep_dispatch")
-        _C.check(lib.qmoe_ep_signal_wait(pt(X.peer["ctrl"]), pt(X.ctrl), self.world, E, self.rank, par, 1,
-                                         0, s), "qmoe_ep_signal_wait")
-        mark(3)
+            pt(X.peer["tok"]), pt(X.peer["recv_meta"]), T, k, H, self.e_local, self.rank, self.world, par,
+            X.cap, X.max_tokens, s), "qmoe_ep_dispatch")
         recv_x = X.recv_x[par * X.cap:(par + 1) * X.cap]
+        _C.check(lib.qmoe_ep_wait_expand(
+            pt(X.peer["ctrl"]), pt(X.ctrl), self.world, E, self.rank, par, 0, pt(X.tok), X.tok_rows,
+            pt(X.recv_meta[par * X.cap:]), pt(recv_x), pt(X.recv_rows), X.cap, H, s), "qmoe_ep_wait_expand")
+        mark(3)
         # gate/up + down in one persistent kernel; its down epilogue stores
         # each weighted row into the source rank's return buffer
         _C.check(lib.qmoe_moe_experts_return(

@@ -155,6 +155,17 @@ def test_ep_nccl_matches_single_gpu_oracle(tmp_path):
         assert np.all(errs <= MAX_REL), f"rank {r}: {errs}"
 
 
+def test_peer_ep_single_rank_matches_oracle(tmp_path):
+    """Both EP blocks with one rank, on any box: the peer-memory step then
+    sends every token row once into this GPU's own token buffer, expands it
+    into its 8 expert rows, and returns the weighted rows locally (eager
+    steps of both parities, a residual, a smaller batch, graph replays)."""
+    mp.start_processes(_nccl_worker, args=(1, _free_port(), str(tmp_path)), nprocs=1, start_method="spawn",
+                       join=True)
+    errs = np.load(tmp_path / "ep0.npy")
+    assert np.all(errs <= MAX_REL), errs
+
+
 def _ep_model_worker(rank, world, port, out_dir):
     sys.path[:0] = [REPO, HERE]
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
