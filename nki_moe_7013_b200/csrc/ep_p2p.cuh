@@ -243,10 +243,42 @@ __global__ void __launch_bounds__(256)
 // ---------------------------------------------------------------------------
 // 3. signal, wait, expand: CTA 0 flags every peer "my rows are in your
 // buffer"; every CTA waits (bounded) for every peer's flag, then the CTAs copy
-// receive-list entry r's token row into receive row r (one warp per row,
-// grid-stride; rows past recv_rows are left alone).  On a time-out the rows
-// are not copied (the device error is set; the step's results are void).
+// receive-list entry r's token row into receive row r (one warp per two rows,
+// grid-stride; every 16-byte load of both rows is issued before the first
+// store, so a warp keeps 8 KB in flight; rows past recv_rows are left alone).
+// On a time-out the rows are not copied (the device error is set; the step's
+// results are void).  kV: 16-byte vectors per lane per row (H = 256 * kV).
 // ---------------------------------------------------------------------------
+template <int kV>
+__device__ __forceinline__ void ep_expand_rows(const __nv_bfloat16* __restrict__ tok, int tok_rows,
+                                               const int4* __restrict__ recv_meta, __nv_bfloat16* __restrict__ recv_x,
+                                               int n, int H, int lane, int gw, int nw) {
+  for (int r0 = 2 * gw; r0 < n; r0 += 2 * nw) {
+    int xr[2];
+    bool ok[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      xr[u] = r0 + u < n ? __ldcg(&recv_meta[r0 + u].w) : -1;
+      ok[u] = xr[u] >= 0 && xr[u] < tok_rows;
+      if (r0 + u < n && !ok[u] && lane == 0) record_device_error(kDevErrBadIndex);
+    }
+    uint4 v[2][kV];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const uint4* src = reinterpret_cast<const uint4*>(tok + size_t(ok[u] ? xr[u] : 0) * H);
+#pragma unroll
+      for (int i = 0; i < kV; ++i) v[u][i] = ok[u] ? __ldcg(src + lane + 32 * i) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      if (!ok[u]) continue;
+      uint4* dst = reinterpret_cast<uint4*>(recv_x + size_t(r0 + u) * H);
+#pragma unroll
+      for (int i = 0; i < kV; ++i) dst[lane + 32 * i] = v[u][i];
+    }
+  }
+}
+
 __global__ void __launch_bounds__(256)
     ep_wait_expand_kernel(int* const* __restrict__ peer_ctrl, int* __restrict__ my_ctrl, int N, int E, int me,
                           int p, int epoch, const __nv_bfloat16* __restrict__ tok, int tok_rows,
@@ -274,17 +306,24 @@ __global__ void __launch_bounds__(256)
   __syncthreads();
   if (!ok_s) return;
   const int n = min(recv_rows[0], cap_rows);
-  const int warps = gridDim.x * (blockDim.x / 32);
-  const int vec = H / 8;
-  for (int r = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); r < n; r += warps) {
-    const int xrow = __ldcg(&recv_meta[r].w);
-    if (xrow < 0 || xrow >= tok_rows) {
-      if (lane == 0) record_device_error(kDevErrBadIndex);
-      continue;
+  const int nw = gridDim.x * (blockDim.x / 32);
+  const int gw = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (H == 2048) {
+    ep_expand_rows<8>(tok, tok_rows, recv_meta, recv_x, n, H, lane, gw, nw);
+  } else if (H == 4096) {
+    ep_expand_rows<16>(tok, tok_rows, recv_meta, recv_x, n, H, lane, gw, nw);
+  } else {
+    const int vec = H / 8;
+    for (int r = gw; r < n; r += nw) {
+      const int xrow = __ldcg(&recv_meta[r].w);
+      if (xrow < 0 || xrow >= tok_rows) {
+        if (lane == 0) record_device_error(kDevErrBadIndex);
+        continue;
+      }
+      const uint4* src = reinterpret_cast<const uint4*>(tok + size_t(xrow) * H);
+      uint4* dst = reinterpret_cast<uint4*>(recv_x + size_t(r) * H);
+      for (int v = lane; v < vec; v += 32) dst[v] = __ldcg(src + v);
     }
-    const uint4* src = reinterpret_cast<const uint4*>(tok + size_t(xrow) * H);
-    uint4* dst = reinterpret_cast<uint4*>(recv_x + size_t(r) * H);
-    for (int v = lane; v < vec; v += 32) dst[v] = __ldcg(src + v);
   }
 }
 

@@ -92,6 +92,20 @@ def _free_port():
     return p
 
 
+def _spawn(fn, world, out_dir, tries=3):
+    """Run fn(rank, world, port, out_dir) on `world` spawned processes; a
+    rendezvous port taken between the probe and the bind is retried on a new
+    port."""
+    for attempt in range(tries):
+        try:
+            mp.start_processes(fn, args=(world, _free_port(), out_dir), nprocs=world, start_method="spawn",
+                               join=True)
+            return
+        except mp.ProcessRaisedException as e:
+            if "EADDRINUSE" not in str(e) or attempt == tries - 1:
+                raise
+
+
 def _nccl_worker(rank, world, port, out_dir):
     sys.path[:0] = [REPO, HERE]
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -148,8 +162,7 @@ def test_ep_nccl_matches_single_gpu_oracle(tmp_path):
     if n < 2:
         pytest.skip("expert parallelism needs 2+ GPUs on the box")
     world = 2 if n < 4 else 4
-    mp.start_processes(_nccl_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
-                       start_method="spawn", join=True)
+    _spawn(_nccl_worker, world, str(tmp_path))
     for r in range(world):
         errs = np.load(tmp_path / f"ep{r}.npy")
         assert np.all(errs <= MAX_REL), f"rank {r}: {errs}"
@@ -160,8 +173,7 @@ def test_peer_ep_single_rank_matches_oracle(tmp_path):
     sends every token row once into this GPU's own token buffer, expands it
     into its 8 expert rows, and returns the weighted rows locally (eager
     steps of both parities, a residual, a smaller batch, graph replays)."""
-    mp.start_processes(_nccl_worker, args=(1, _free_port(), str(tmp_path)), nprocs=1, start_method="spawn",
-                       join=True)
+    _spawn(_nccl_worker, 1, str(tmp_path))
     errs = np.load(tmp_path / "ep0.npy")
     assert np.all(errs <= MAX_REL), errs
 
@@ -228,8 +240,7 @@ def test_ep_model_matches_single_gpu_model(tmp_path):
     if n < 2:
         pytest.skip("expert parallelism needs 2+ GPUs on the box")
     world = 2 if n < 4 else 4
-    mp.start_processes(_ep_model_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
-                       start_method="spawn", join=True)
+    _spawn(_ep_model_worker, world, str(tmp_path))
     for r in range(world):
         errs = np.load(tmp_path / f"epm{r}.npy")
         assert errs[2] == 0, f"rank {r}: device error {errs[2]}"
