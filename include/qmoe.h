@@ -480,6 +480,11 @@ QMOE_API int qmoe_ep_unpack(const void* y_back, const int32_t* pair_pos, const v
  * qmoe_ep_signal_wait: one warp; flag `kind` (1 dispatch, 2 combine) of this
  *   rank in every peer, then wait (bounded) for every rank's flag; kind 2
  *   with epoch 0 then advances the step counter.
+ * qmoe_ep_wait_unpack: flags this rank's combine in every peer, waits
+ *   (bounded) for every rank's flag, then out[t] = bf16(residual[t] +
+ *   sum_j y_back[t*k + j]) in fp32 (residual may be NULL); y_back points at
+ *   this parity's return rows.  With epoch 0 it advances the step counter
+ *   (the kind-2 signal of qmoe_ep_signal_wait folded in).
  * qmoe_moe_experts_return: gate/up + down in one persistent kernel (as
  *   qmoe_moe_experts, x = the receive rows) whose down epilogue stores into
  *   the source ranks' return buffers as qmoe_grouped_gemm_down_return does;
@@ -510,6 +515,9 @@ QMOE_API int qmoe_ep_wait_expand(int* const* peer_ctrl, int* my_ctrl, int64_t n_
                                  int64_t cap_rows, int64_t H, void* stream);
 QMOE_API int qmoe_ep_signal_wait(int* const* peer_ctrl, int* my_ctrl, int64_t n_ranks, int64_t E,
                                  int64_t me, int64_t parity, int64_t kind, int64_t epoch, void* stream);
+QMOE_API int qmoe_ep_wait_unpack(int* const* peer_ctrl, int* my_ctrl, int64_t n_ranks, int64_t E, int64_t me,
+                                 int64_t parity, int64_t epoch, const void* y_back, const void* residual,
+                                 int64_t T, int64_t H, int64_t k, void* out, void* stream);
 QMOE_API int qmoe_moe_experts_return(const void* x, const void* w_gate_up, const void* w_down, const int32_t* tiles,
                                      int64_t max_tiles, const void* row_meta, void* const* peer_ret,
                                      int64_t ret_row0, int64_t n_ret_rows, int64_t n_ranks, int64_t R, int64_t H,

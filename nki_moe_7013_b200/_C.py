@@ -66,6 +66,7 @@ _SIGNATURES = {
     "qmoe_moe_experts_return": (I32, [P, P, P, P, I64, P, P, I64, I64, I64, I64, I64, I64, I64, P, P, P]),
     "qmoe_ep_dispatch": (I32, [P, P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, I64, I64, I64, P]),
     "qmoe_ep_wait_expand": (I32, [P, P, I64, I64, I64, I64, I64, P, I64, P, P, P, I64, I64, P]),
+    "qmoe_ep_wait_unpack": (I32, [P, P, I64, I64, I64, I64, I64, P, P, I64, I64, I64, P, P]),
     "qmoe_ep_signal_wait": (I32, [P, P, I64, I64, I64, I64, I64, I64, P]),
     "qmoe_grouped_gemm_down_return": (I32, [P, P, P, I64, P, P, I64, I64, I64, I64, I64, I64, I64, P]),
     "qmoe_moe_forward_noalloc": (I32, [P, P, P, P, P, P, I64, I64, I64, I64, I64, I32, P, P, P, P]),

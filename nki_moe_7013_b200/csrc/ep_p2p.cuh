@@ -23,8 +23,9 @@
 //   4. grouped gate/up + down GEMMs on the receive buffer; the down epilogue
 //      writes each weighted bf16 row back into the SOURCE rank's return
 //      buffer through peer stores (the combine, fused into the GEMM);
-//   5. ep_signal_wait again ("your rows are back"), then ep_unpack sums the k
-//      returned rows of every token in fp32.
+//   5. ep_wait_unpack: flag "your rows are back" to every peer, wait for
+//      every peer's flag, then sum the k returned rows of every token in fp32
+//      (+ residual), all CTAs; the step's device counter advances here.
 //
 // Receive / return buffers and the control block have two halves used on
 // alternate steps (parity), so a fast rank can never overwrite data a peer
@@ -55,7 +56,8 @@ __host__ __device__ __forceinline__ size_t ep_ctrl_words_per_parity(int N, int E
 }
 enum EpFlagKind : int { kEpFlagCounts = 0, kEpFlagDispatch = 1, kEpFlagCombine = 2 };
 
-// Index of the device-side step counter (after both parity halves).
+// Index of the device-side step counter (after both parity halves); the
+// word after it counts the CTAs of ep_wait_unpack that have read the epoch.
 __host__ __device__ __forceinline__ size_t ep_step_word(int N, int E) { return 2 * ep_ctrl_words_per_parity(N, E); }
 
 // The step's epoch: the caller's, or (epoch == 0) the device counter + 1.
@@ -324,6 +326,92 @@ __global__ void __launch_bounds__(256)
       uint4* dst = reinterpret_cast<uint4*>(recv_x + size_t(r) * H);
       for (int v = lane; v < vec; v += 32) dst[v] = __ldcg(src + v);
     }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 5. signal, wait, unpack: CTA 0 flags every peer "your rows are back"; every
+// CTA waits (bounded) for every peer's flag, then one warp per (token,
+// 256-column slab), grid-stride, sums the token's k returned rows in fp32,
+// adds the residual and stores bf16.  With the device epoch (epoch == 0) the
+// step counter advances once every CTA has read it: the last CTA to arrive
+// (counted in the word after the counter, which it resets) writes it.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+    ep_wait_unpack_kernel(int* const* __restrict__ peer_ctrl, int* __restrict__ my_ctrl, int N, int E, int me,
+                          int p, int epoch, const __nv_bfloat16* __restrict__ y_back,
+                          const __nv_bfloat16* __restrict__ residual, int T, int H, int k,
+                          __nv_bfloat16* __restrict__ out) {
+  __shared__ int ok_s, epoch_s;
+  griddep_wait();
+  griddep_launch_dependents();
+  if (threadIdx.x == 0) {
+    // thread 0 alone reads the counter; the CTA's last reader advances it
+    const bool device_epoch = epoch == 0;
+    int ep = epoch;
+    const bool epoch_ok = ep_resolve_epoch(my_ctrl, N, E, p, ep);
+    epoch_s = epoch_ok ? ep : -1;
+    if (device_epoch) {
+      int* arrive = my_ctrl + ep_step_word(N, E) + 1;
+      __threadfence();
+      if (atomicAdd(arrive, 1) == int(gridDim.x) - 1) {
+        *arrive = 0;
+        if (epoch_ok) my_ctrl[ep_step_word(N, E)] = ep;
+      }
+    }
+  }
+  __syncthreads();
+  if (epoch_s < 0) return;
+  epoch = epoch_s;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x < 32) {
+    if (blockIdx.x == 0) {
+      __threadfence_system();
+      __syncwarp();
+      for (int d = lane; d < N; d += 32)
+        st_release_sys(peer_ctrl[d] + ep_flag_word(N, E, p, kEpFlagCombine, me), epoch);
+    }
+    bool ok = true;
+    for (int s = lane; s < N; s += 32)
+      ok &= ep_wait_flag(my_ctrl + ep_flag_word(N, E, p, kEpFlagCombine, s), epoch, kDevErrPeerTimeout);
+    ok = __all_sync(0xFFFFFFFFu, ok);
+    __threadfence_system();
+    if (lane == 0) ok_s = ok;
+  }
+  __syncthreads();
+  if (!ok_s) return;
+  const int slabs = H / 256;
+  const int nw = gridDim.x * (blockDim.x / 32);
+  for (int w = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); w < T * slabs; w += nw) {
+    const int t = w / slabs;
+    const int col = (w - t * slabs) * 256 + lane * 8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < k; ++j) {
+      const uint4 v = __ldcg(reinterpret_cast<const uint4*>(y_back + (size_t(t) * k + j) * H + col));
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        acc[2 * q] += bf16lo_to_f32(u[q]);
+        acc[2 * q + 1] += bf16hi_to_f32(u[q]);
+      }
+    }
+    if (residual) {
+      const uint4 v = *reinterpret_cast<const uint4*>(residual + size_t(t) * H + col);
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        acc[2 * q] += bf16lo_to_f32(u[q]);
+        acc[2 * q + 1] += bf16hi_to_f32(u[q]);
+      }
+    }
+    uint4 o;
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const __nv_bfloat162 b2 = __floats2bfloat162_rn(acc[2 * q], acc[2 * q + 1]);
+      ow[q] = *reinterpret_cast<const uint32_t*>(&b2);
+    }
+    *reinterpret_cast<uint4*>(out + size_t(t) * H + col) = o;
   }
 }
 

@@ -1470,7 +1470,8 @@ int qmoe_ipc_close(void* base) {
 
 int64_t qmoe_ep_ctrl_words(int64_t n_ranks, int64_t E) {
   if (n_ranks <= 0 || E <= 0) return 0;
-  return int64_t(qmoe::ep_step_word(int(n_ranks), int(E))) + 4;  // both halves + the step counter
+  // both halves, the step counter and ep_wait_unpack's arrival count (+2 spare)
+  return int64_t(qmoe::ep_step_word(int(n_ranks), int(E))) + 4;
 }
 
 int qmoe_ep_exchange_counts(const int32_t* counts, int* const* peer_ctrl, int* my_ctrl, int64_t me,
@@ -1548,6 +1549,27 @@ int qmoe_ep_signal_wait(int* const* peer_ctrl, int* my_ctrl, int64_t n_ranks, in
   return launch_kernel(qmoe::ep_signal_wait_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), true,
                        "ep_signal_wait_kernel", peer_ctrl, my_ctrl, int(n_ranks), int(E), int(me), int(parity),
                        int(kind), int(epoch));
+}
+
+int qmoe_ep_wait_unpack(int* const* peer_ctrl, int* my_ctrl, int64_t n_ranks, int64_t E, int64_t me,
+                        int64_t parity, int64_t epoch, const void* y_back, const void* residual, int64_t T,
+                        int64_t H, int64_t k, void* out, void* stream) {
+  QMOE_REQUIRE(peer_ctrl && my_ctrl && y_back && out, QMOE_ERR_INVALID_ARGUMENT, "ep_wait_unpack: null pointer");
+  QMOE_REQUIRE(n_ranks >= 1 && n_ranks <= 32 && me >= 0 && me < n_ranks && (parity == 0 || parity == 1) &&
+                   epoch >= 0 && epoch < (int64_t(1) << 31) && E >= 1 && T >= 0 && k >= 1 && k <= 32 &&
+                   T * k < (int64_t(1) << 31),
+               QMOE_ERR_INVALID_ARGUMENT, "ep_wait_unpack: bad arguments");
+  QMOE_REQUIRE(H > 0 && H % 256 == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "ep_wait_unpack: H %% 256 != 0");
+  QMOE_REQUIRE(aligned16(y_back) && aligned16(out) && (!residual || aligned16(residual)), QMOE_ERR_MISALIGNED,
+               "ep_wait_unpack: pointers must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  // the flags are waited for (and the step counter advanced) even when T == 0
+  return launch_kernel(qmoe::ep_wait_unpack_kernel, dim3(d->sms), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                       true, "ep_wait_unpack_kernel", peer_ctrl, my_ctrl, int(n_ranks), int(E), int(me),
+                       int(parity), int(epoch), static_cast<const __nv_bfloat16*>(y_back),
+                       static_cast<const __nv_bfloat16*>(residual), int(T), int(H), int(k),
+                       static_cast<__nv_bfloat16*>(out));
 }
 
 int qmoe_moe_experts_return(const void* x, const void* w_gate_up, const void* w_down, const int32_t* tiles,

@@ -230,10 +230,10 @@ class PeerEPExchange:
         """Kernels one step launches: route (router + permutation: one launch
         up to one router chunk per SM and T > 64, else router + scan +
         scatter), count exchange, dispatch, signal + wait + expand, experts,
-        signal, unpack."""
+        signal + wait + unpack."""
         nchunks = (T + ops.ROUTER_CHUNK - 1) // ops.ROUTER_CHUNK
         one = T > ops.ROUTER_SMALL_MAX_T and nchunks <= self.sms
-        return (1 if one else 3) + 6
+        return (1 if one else 3) + 5
 
 
 class PeerExpertParallelMoE(nn.Module):
@@ -247,7 +247,7 @@ class PeerExpertParallelMoE(nn.Module):
     expert), signal/wait and the local expansion of the receive list into
     expert-grouped rows, gate/up + down in one persistent kernel on those
     rows whose down epilogue stores the weighted rows into the source ranks'
-    return buffers, signal/wait, unpack.
+    return buffers, signal/wait and the unpack of the returned rows.
 
     The buffers live in a ``PeerEPExchange`` (``exchange``): pass one shared
     exchange to every block of a decoder stack, or let the block create its
@@ -311,7 +311,7 @@ class PeerExpertParallelMoE(nn.Module):
         if self._owns_exchange:
             self.x.close()
 
-    STAGES = ("route", "exchange", "dispatch", "experts", "return_wait", "unpack")
+    STAGES = ("route", "exchange", "dispatch", "experts", "return")
 
     def launches_per_step(self, T: int) -> int:
         return self.x.launches_per_step(T)
@@ -361,13 +361,12 @@ class PeerExpertParallelMoE(nn.Module):
             pt(X.recv_meta[par * X.cap:]), pt(X.peer["ret"]), par * X.ret_rows, X.ret_rows,
             self.world, X.cap, H, I, self.e_local, pt(X.act), pt(X.done), s), "qmoe_moe_experts_return")
         mark(4)
-        _C.check(lib.qmoe_ep_signal_wait(pt(X.peer["ctrl"]), pt(X.ctrl), self.world, E, self.rank, par, 2,
-                                         0, s), "qmoe_ep_signal_wait")
+        # "your rows are back" flags, the wait for every peer's, and the
+        # fp32 sum of each token's k returned rows (+ residual), one launch
+        y_back = X.ret[par * X.ret_rows:]
+        _C.check(lib.qmoe_ep_wait_unpack(pt(X.peer["ctrl"]), pt(X.ctrl), self.world, E, self.rank, par, 0,
+                                         pt(y_back), pt(residual), T, H, k, pt(out), s), "qmoe_ep_wait_unpack")
         mark(5)
-        y_back = X.ret[par * X.ret_rows:par * X.ret_rows + T * k]
-        _C.check(lib.qmoe_ep_unpack(pt(y_back), None, pt(residual), T, H, k, T * k, pt(out), s),
-                 "qmoe_ep_unpack")
-        mark(6)
 
     def forward(self, hidden_states: torch.Tensor, residual: Optional[torch.Tensor] = None,
                 events=None) -> torch.Tensor:
