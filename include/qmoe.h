@@ -267,6 +267,21 @@ QMOE_API int qmoe_blockwise_prepare(const void* x, const float* affinities, int6
 QMOE_API int qmoe_combine_finalize(const float* acc, const void* residual, int64_t T, int64_t H,
                           void* out, void* stream);
 
+/* out (T, H) bf16 = bf16(residual + mask[t] * y) in fp32, one rounding: the
+ * decoder layer's residual add of the MoE output under the block's
+ * padding_mask (qwen.py:429-430).  mask (T) fp32 or NULL (= 1), residual
+ * (T, H) bf16 or NULL (= 0).  H % 8 == 0. */
+QMOE_API int qmoe_masked_residual_add(const void* y, const float* mask, const void* residual, int64_t T,
+                                      int64_t H, void* out, void* stream);
+
+/* w (T, k) fp32 = affinities[t, idx[t, j]] (affinities (T, E) fp32), divided
+ * by max(sum_j |w[t, j]|, 1e-12) when normalize: the chosen-affinity gather and
+ * F.normalize(p=1) of ExpertMLPsV2.forward_selective_loading
+ * (qwen_with_nki.py:2398-2405).  An index outside [0, E) gives 0 and device
+ * error 4. */
+QMOE_API int qmoe_select_affinities(const float* affinities, const int32_t* idx, int64_t T, int64_t E, int64_t k,
+                                    int64_t normalize, float* w, void* stream);
+
 /* ------------------------------------------------------------------------
  * Token embedding lookup: out[i, :] = table[ids[i], :], table (V, H) bf16.
  * Replaces the reference's embedding kernel (qwen_with_nki.py:1541-1578).

@@ -19,6 +19,72 @@ __global__ void __launch_bounds__(256)
   if (threadIdx.x == 0) QMOE_TRACE_AT(3, 2);
 }
 
+// Masked residual add of the decoder layer's MoE output (qwen.py:429-430 with
+// the block's padding_mask): out[t] = bf16(residual[t] + mask[t] * y[t]),
+// computed in fp32 and rounded once; mask NULL = 1, residual NULL = 0.
+__global__ void __launch_bounds__(256)
+    masked_residual_kernel(const uint4* __restrict__ y, const float* __restrict__ mask,
+                           const uint4* __restrict__ residual, uint4* __restrict__ out, int T, int vec_per_row) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const long long total = (long long)T * vec_per_row;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int t = int(i / vec_per_row);
+    const float m = mask ? mask[t] : 1.f;
+    const uint4 v = y[i];
+    const uint32_t yv[4] = {v.x, v.y, v.z, v.w};
+    uint32_t rv[4] = {0u, 0u, 0u, 0u};
+    if (residual) {
+      const uint4 r = residual[i];
+      rv[0] = r.x;
+      rv[1] = r.y;
+      rv[2] = r.z;
+      rv[3] = r.w;
+    }
+    uint4 o;
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      // multiply, then add, each rounded (no fused multiply-add): the same
+      // fp32 value as residual.float() + y.float() * mask
+      const float lo = __fadd_rn(bf16lo_to_f32(rv[q]), __fmul_rn(m, bf16lo_to_f32(yv[q])));
+      const float hi = __fadd_rn(bf16hi_to_f32(rv[q]), __fmul_rn(m, bf16hi_to_f32(yv[q])));
+      const __nv_bfloat162 b2 = __floats2bfloat162_rn(lo, hi);
+      ow[q] = *reinterpret_cast<const uint32_t*>(&b2);
+    }
+    out[i] = o;
+  }
+}
+
+// Chosen expert affinities of the ExpertMLPs seam (qwen_with_nki.py:2398-2405):
+// w[t, j] = affinities[t, idx[t, j]], then (normalize) divided by
+// max(sum_j |w[t, j]|, 1e-12) -- F.normalize(p=1) -- summed in slot order.
+// One thread per token; an index outside [0, E) gives weight 0 and device
+// error 4.
+__global__ void __launch_bounds__(256)
+    select_affinities_kernel(const float* __restrict__ aff, const int32_t* __restrict__ idx, int T, int E, int k,
+                             int normalize, float* __restrict__ w) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  float v[32];
+  float s = 0.f;
+  for (int j = 0; j < k; ++j) {
+    const int e = idx[size_t(t) * k + j];
+    float a = 0.f;
+    if (e < 0 || e >= E)
+      record_device_error(kDevErrBadIndex);
+    else
+      a = aff[size_t(t) * E + e];
+    v[j] = a;
+    s += fabsf(a);
+  }
+  const float d = normalize ? fmaxf(s, 1e-12f) : 1.f;
+  for (int j = 0; j < k; ++j) w[size_t(t) * k + j] = normalize ? v[j] / d : v[j];
+}
+
 }  // namespace qmoe
 
 namespace qmoe {

@@ -1109,6 +1109,36 @@ int qmoe_moe_experts(const void* x, int64_t x_rows, const int32_t* gather_rows, 
                           act, acc, n_acc, done, static_cast<cudaStream_t>(stream));
 }
 
+int qmoe_masked_residual_add(const void* y, const float* mask, const void* residual, int64_t T, int64_t H,
+                             void* out, void* stream) {
+  QMOE_REQUIRE(y && out, QMOE_ERR_INVALID_ARGUMENT, "masked_residual_add: null pointer");
+  QMOE_REQUIRE(T >= 0 && T < (int64_t(1) << 31), QMOE_ERR_INVALID_ARGUMENT, "masked_residual_add: bad T");
+  QMOE_REQUIRE(H > 0 && H % 8 == 0, QMOE_ERR_UNSUPPORTED_SHAPE, "masked_residual_add: H %% 8 != 0");
+  QMOE_REQUIRE(aligned16(y) && aligned16(out) && (!residual || aligned16(residual)), QMOE_ERR_MISALIGNED,
+               "masked_residual_add: pointers must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  if (T == 0) return QMOE_OK;
+  const long long total = (long long)T * (H / 8);
+  const int grid = int(std::min<long long>((total + 255) / 256, (long long)d->sms * 8));
+  return launch_kernel(qmoe::masked_residual_kernel, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                       true, "masked_residual_kernel", static_cast<const uint4*>(y), mask,
+                       static_cast<const uint4*>(residual), static_cast<uint4*>(out), int(T), int(H / 8));
+}
+
+int qmoe_select_affinities(const float* affinities, const int32_t* idx, int64_t T, int64_t E, int64_t k,
+                           int64_t normalize, float* w, void* stream) {
+  QMOE_REQUIRE(affinities && idx && w, QMOE_ERR_INVALID_ARGUMENT, "select_affinities: null pointer");
+  QMOE_REQUIRE(T >= 0 && T < (int64_t(1) << 31) && E >= 1 && T * E < (int64_t(1) << 40) && k >= 1 && k <= 32,
+               QMOE_ERR_INVALID_ARGUMENT, "select_affinities: bad sizes");
+  DeviceInfo* d = nullptr;
+  QMOE_CHECK(device_info(&d));
+  if (T == 0) return QMOE_OK;
+  return launch_kernel(qmoe::select_affinities_kernel, dim3(int((T + 255) / 256)), dim3(256), 0,
+                       static_cast<cudaStream_t>(stream), true, "select_affinities_kernel", affinities, idx, int(T),
+                       int(E), int(k), normalize ? 1 : 0, w);
+}
+
 int qmoe_embedding_gather(const void* table, int64_t V, int64_t H, const int32_t* ids, int64_t n, void* out,
                           void* stream) {
   QMOE_REQUIRE(table && ids && out, QMOE_ERR_INVALID_ARGUMENT, "embedding: null pointer");

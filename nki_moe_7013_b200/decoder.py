@@ -15,7 +15,8 @@ like NeuronQwen3MoeDecoderLayer.forward (qwen.py:378-436):
 Here the residual add before the second norm, the norm, the MoE block and
 the final residual add are one library call (``qmoe_moe_block_forward``).  With a
 ``padding_mask`` the masked MoE output needs the norm's outputs first, so
-that path runs the add & norm and the MoE block as two calls.  RoPE is applied
+that path runs the add & norm, the MoE block and the masked residual add
+(``ops.masked_residual_add``, one kernel) as three calls.  RoPE is applied
 inside the attention kernels, so cos/sin caches are returned as None.
 ``attention_mask``: attention is causal over each sequence's cache; a 2D
 left-padding key mask (batch, cached + new tokens) is honoured and every
@@ -81,8 +82,7 @@ class Qwen3MoeDecoderLayer(nn.Module):
                 if padding_mask is None:
                     out = self.mlp(h2, residual=residual)
                 else:
-                    moe = self.mlp(h2)
-                    out = (residual.float() + moe.float() * padding_mask.reshape(-1, 1).float()).to(torch.bfloat16)
+                    out = ops.masked_residual_add(self.mlp(h2), padding_mask, residual)
         elif padding_mask is None and timer is not None and not kwargs.get("capture_intermediates"):
             with stage(timer, "moe"):
                 out = self.mlp._block(a2d, x2d, self.post_attention_layernorm, eps)
@@ -95,7 +95,7 @@ class Qwen3MoeDecoderLayer(nn.Module):
         else:
             h2, residual = ops.rmsnorm(a2d, self.post_attention_layernorm, eps, residual=x2d)
             moe, _, _ = self.mlp._moe(h2)
-            out = (residual.float() + moe.float() * padding_mask.reshape(-1, 1).float()).to(torch.bfloat16)
+            out = ops.masked_residual_add(moe, padding_mask, residual)
         if kwargs.get("capture_intermediates"):
             self.last = dict(attn=a2d, residual=residual, moe_in=h2)
         return (out.reshape(B, S, H), present, None, None, None)

@@ -151,7 +151,7 @@ class Qwen3MoeSparseMoeBlock(nn.Module):
         out, idx, tw = self._moe(x2d)
         if padding_mask is not None:
             # padded positions (mask == 0) produce no MoE output
-            out = out * padding_mask.reshape(-1, 1).to(out.dtype)
+            out = ops.masked_residual_add(out, padding_mask)
         out = out.reshape(shape)
         result = (out,)
         if self.return_router_logits:
@@ -188,10 +188,8 @@ class ExpertMLPs(nn.Module):
         E = self.w.num_experts
         idx = expert_index.reshape(T, -1).to(torch.int32).contiguous()
         k = idx.shape[1]
-        chosen = torch.gather(expert_affinities.reshape(T, E).float(), 1, idx.long())
-        if self.normalize_top_k_affinities:
-            chosen = torch.nn.functional.normalize(chosen, p=1.0, dim=1)
-        return _run_routed(x, self.w, idx, chosen.contiguous(), k)
+        chosen = ops.select_affinities(expert_affinities.reshape(T, E), idx, self.normalize_top_k_affinities)
+        return _run_routed(x, self.w, idx, chosen, k)
 
     def torch_blockwise_matmul_inference(self, block_size, num_blocks, hidden_states,
                                          expert_affinities_masked, token_position_to_id,

@@ -343,6 +343,47 @@ def embedding(ids: torch.Tensor, table: torch.Tensor, out: Optional[torch.Tensor
     return out
 
 
+def masked_residual_add(y: torch.Tensor, mask: Optional[torch.Tensor] = None,
+                        residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out = bf16(residual + mask[:, None] * y), fp32 arithmetic and one
+    rounding (mask None = 1, residual None = 0): the MoE output under the
+    block's padding_mask plus the decoder layer's residual, in one launch."""
+    _need(y, "y", torch.bfloat16, 2)
+    T, H = y.shape
+    dev = y.device
+    m = None
+    if mask is not None:
+        m = mask.reshape(-1).to(device=dev, dtype=torch.float32).contiguous()
+        if m.numel() != T:
+            raise ValueError(f"mask has {m.numel()} entries for {T} rows")
+    if residual is not None:
+        _need(residual, "residual", torch.bfloat16, 2)
+        if tuple(residual.shape) != (T, H):
+            raise ValueError("residual must have the shape of y")
+        residual = residual.contiguous()
+    y = y.contiguous()
+    out = torch.empty_like(y)
+    with torch.cuda.device(dev):
+        _C.check(_C.lib().qmoe_masked_residual_add(_ptr(y), _ptr(m), _ptr(residual), T, H, _ptr(out),
+                                                   _stream(dev)), "qmoe_masked_residual_add")
+    return out
+
+
+def select_affinities(affinities: torch.Tensor, idx: torch.Tensor, normalize: bool = True) -> torch.Tensor:
+    """w (T, k) fp32 = affinities[t, idx[t, j]], L1-normalised per token when
+    ``normalize`` (F.normalize(p=1): divided by max(sum |w|, 1e-12))."""
+    _need(idx, "idx", torch.int32, 2)
+    T, k = idx.shape
+    dev = idx.device
+    a = affinities.reshape(T, -1).to(device=dev, dtype=torch.float32).contiguous()
+    w = torch.empty((T, k), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _C.check(_C.lib().qmoe_select_affinities(_ptr(a), _ptr(idx.contiguous()), T, a.shape[1], k,
+                                                 1 if normalize else 0, _ptr(w), _stream(dev)),
+                 "qmoe_select_affinities")
+    return w
+
+
 def moe_forward_workspace_size(T: int, H: int, E: int, k: int, I: int) -> int:
     return int(_C.lib().qmoe_moe_forward_workspace_size(T, H, E, k, I))
 

@@ -95,3 +95,86 @@ def test_module_dropins(cuda_dev, oracle):
     w2 = MoEWeights.from_neuron_layout(w.router, w.gate_up.transpose(1, 2), w.down.transpose(1, 2),
                                        device=cuda_dev)
     assert torch.equal(w2.gate_up, w.gate_up) and torch.equal(w2.down, w.down)
+
+
+def test_masked_residual_add_bit_exact(cuda_dev):
+    """ops.masked_residual_add equals the eager fp32 formula bit for bit, with
+    0/1 and fractional masks, with and without a residual."""
+    from nki_moe_7013_b200 import ops
+
+    T, H = 300, 2048
+    y = activations(60, T, H, cuda_dev)
+    res = activations(61, T, H, cuda_dev)
+    g = torch.Generator(device=cuda_dev)
+    g.manual_seed(62)
+    for mask in ((torch.rand(T, generator=g, device=cuda_dev) > 0.3).to(torch.int64),
+                 torch.rand(T, generator=g, device=cuda_dev)):
+        m = mask.reshape(-1, 1).float()
+        assert torch.equal(ops.masked_residual_add(y, mask), (y.float() * m).to(torch.bfloat16))
+        assert torch.equal(ops.masked_residual_add(y, mask, res), (res.float() + y.float() * m).to(torch.bfloat16))
+    assert torch.equal(ops.masked_residual_add(y, None, res), (res.float() + y.float()).to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("normalize", [True, False])
+def test_select_affinities_matches_torch(cuda_dev, normalize):
+    """The chosen-affinity gather + F.normalize(p=1) kernel against torch."""
+    from nki_moe_7013_b200 import ops
+
+    T, E, k = 257, 128, 8
+    g = torch.Generator(device=cuda_dev)
+    g.manual_seed(63)
+    aff = torch.softmax(torch.randn(T, E, generator=g, device=cuda_dev), -1)
+    idx = torch.topk(aff, k, dim=-1).indices.to(torch.int32)
+    w = ops.select_affinities(aff, idx, normalize)
+    ref = torch.gather(aff, 1, idx.long())
+    if normalize:
+        ref = torch.nn.functional.normalize(ref, p=1.0, dim=1)
+    # the kernel sums |w| in slot order, torch's reduction in its own order:
+    # the L1 norms, and so the quotients, differ by a few fp32 ulps
+    torch.testing.assert_close(w, ref, rtol=1e-6, atol=0)
+
+
+def test_moe_block_padding_mask(cuda_dev):
+    """Qwen3MoeSparseMoeBlock(x, padding_mask): masked tokens give zero rows,
+    the others the unmasked output bit for bit."""
+    from nki_moe_7013_b200.config import Qwen3MoeConfig
+    from nki_moe_7013_b200.moe import MoEWeights, Qwen3MoeSparseMoeBlock
+
+    cfg = Qwen3MoeConfig()
+    blk = Qwen3MoeSparseMoeBlock(cfg, MoEWeights.random(cfg, seed=12, device=cuda_dev), device=cuda_dev)
+    B, S = 2, 40
+    x = activations(64, B * S, cfg.hidden_size, cuda_dev).reshape(B, S, cfg.hidden_size)
+    mask = torch.ones(B, S, dtype=torch.int64, device=cuda_dev)
+    mask[0, :7] = 0  # left padding of the first sequence
+    full = blk(x)[0]
+    masked = blk(x, mask)[0]
+    torch.cuda.synchronize()
+    keep = mask.bool()
+    assert torch.equal(masked[keep], full[keep])
+    assert not masked[~keep].any()
+
+
+def test_decoder_layer_padding_mask(cuda_dev):
+    """Decoder layer with a padding_mask: a masked token's output is its
+    post-attention residual exactly; the others match the unmasked layer to
+    the rounding of the MoE output (the unmasked layer rounds residual + MoE
+    once, the masked path rounds the MoE output to bf16 first: at most half
+    an ulp of |MoE| <= |out| + |residual|, plus one ulp of the sum)."""
+    from nki_moe_7013_b200.config import Qwen3MoeConfig
+    from nki_moe_7013_b200.decoder import Qwen3MoeDecoderLayer
+
+    cfg = Qwen3MoeConfig()
+    layer = Qwen3MoeDecoderLayer(cfg, device=cuda_dev, seed=13)
+    B, S, H = 2, 48, cfg.hidden_size
+    x = activations(65, B * S, H, cuda_dev).reshape(B, S, H)
+    pm = torch.ones(B * S, dtype=torch.float32, device=cuda_dev)
+    pm[S:S + 5] = 0.0
+    full = layer(x, capture_intermediates=True)[0].reshape(B * S, H)
+    masked = layer(x, padding_mask=pm, capture_intermediates=True)[0].reshape(B * S, H)
+    residual = layer.last["residual"]
+    torch.cuda.synchronize()
+    keep = pm.bool()
+    assert torch.equal(masked[~keep], residual[~keep])
+    m, f, r = masked[keep].float(), full[keep].float(), residual[keep].float()
+    tol = 2.0 ** -7 * (f.abs() + r.abs()) + 1e-6
+    assert bool(((m - f).abs() <= tol).all()), float(((m - f).abs() - tol).max())
