@@ -282,6 +282,14 @@ QMOE_API int qmoe_masked_residual_add(const void* y, const float* mask, const vo
 QMOE_API int qmoe_select_affinities(const float* affinities, const int32_t* idx, int64_t T, int64_t E, int64_t k,
                                     int64_t normalize, float* w, void* stream);
 
+/* Greedy pick of a decode step: tokens[b] = argmax_v logits[b, v] (logits
+ * (B, V) bf16; the first index of the largest value, NaN largest, as
+ * torch.argmax; the reference's generation loop compares these argmaxes,
+ * main.py:576, 611), then positions[b] += 1 and lengths[b] += 1 when not
+ * NULL.  One launch. */
+QMOE_API int qmoe_greedy_pick(const void* logits, int64_t B, int64_t V, int32_t* tokens, int32_t* positions,
+                              int32_t* lengths, void* stream);
+
 /* ------------------------------------------------------------------------
  * Token embedding lookup: out[i, :] = table[ids[i], :], table (V, H) bf16.
  * Replaces the reference's embedding kernel (qwen_with_nki.py:1541-1578).

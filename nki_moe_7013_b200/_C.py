@@ -41,6 +41,7 @@ _SIGNATURES = {
     "qmoe_combine_finalize": (I32, [P, P, I64, I64, P, P]),
     "qmoe_embedding_gather": (I32, [P, I64, I64, P, I64, P, P]),
     "qmoe_masked_residual_add": (I32, [P, P, P, I64, I64, P, P]),
+    "qmoe_greedy_pick": (I32, [P, I64, I64, P, P, P, P]),
     "qmoe_select_affinities": (I32, [P, P, I64, I64, I64, I64, P, P]),
     "qmoe_moe_forward_workspace_size": (SZ, [I64, I64, I64, I64, I64]),
     "qmoe_moe_forward": (I32, [P, P, P, P, P, P, I64, I64, I64, I64, I64, I32, P, P, P, P, SZ, P]),

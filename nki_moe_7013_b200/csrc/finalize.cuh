@@ -85,6 +85,65 @@ __global__ void __launch_bounds__(256)
   for (int j = 0; j < k; ++j) w[size_t(t) * k + j] = normalize ? v[j] / d : v[j];
 }
 
+// Greedy pick of a decode step (the argmax of the logits the reference's
+// generation loop compares, main.py:576, 611): tokens[b] = the first index of
+// the largest of logits[b, :] (NaN counts as larger than every number, as
+// torch.argmax propagates it), then positions[b] += 1 and lengths[b] += 1
+// when given -- the step's bookkeeping in the same launch.  One CTA per row.
+__device__ __forceinline__ unsigned long long greedy_key(float f, int v) {
+  unsigned int u = __float_as_uint(f);
+  unsigned int key;
+  if (f != f)
+    key = 0xFFFFFFFFu;
+  else {
+    if (u == 0x80000000u) u = 0u;  // -0 ranks as +0
+    key = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  }
+  // larger value first, then lower index
+  return (static_cast<unsigned long long>(key) << 32) | (0xFFFFFFFFu - static_cast<unsigned int>(v));
+}
+
+__global__ void __launch_bounds__(1024)
+    greedy_pick_kernel(const __nv_bfloat16* __restrict__ logits, int V, int32_t* __restrict__ tokens,
+                       int32_t* __restrict__ positions, int32_t* __restrict__ lengths) {
+  __shared__ unsigned long long warp_best[32];
+  griddep_wait();
+  griddep_launch_dependents();
+  const int b = blockIdx.x;
+  const __nv_bfloat16* row = logits + size_t(b) * V;
+  unsigned long long best = 0ull;
+  const bool vec = (V % 8) == 0;
+  if (vec) {
+    const uint4* r4 = reinterpret_cast<const uint4*>(row);
+    for (int i = threadIdx.x; i < V / 8; i += blockDim.x) {
+      const uint4 q = r4[i];
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        best = max(best, greedy_key(bf16lo_to_f32(w[j]), 8 * i + 2 * j));
+        best = max(best, greedy_key(bf16hi_to_f32(w[j]), 8 * i + 2 * j + 1));
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < V; i += blockDim.x) best = max(best, greedy_key(__bfloat162float(row[i]), i));
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) best = max(best, __shfl_xor_sync(0xFFFFFFFFu, best, off));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) warp_best[warp] = best;
+  __syncthreads();
+  if (warp == 0) {
+    best = lane < int(blockDim.x >> 5) ? warp_best[lane] : 0ull;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) best = max(best, __shfl_xor_sync(0xFFFFFFFFu, best, off));
+    if (lane == 0) {
+      tokens[b] = int32_t(0xFFFFFFFFu - static_cast<unsigned int>(best & 0xFFFFFFFFull));
+      if (positions) positions[b] += 1;
+      if (lengths) lengths[b] += 1;
+    }
+  }
+}
+
 }  // namespace qmoe
 
 namespace qmoe {

@@ -1139,6 +1139,18 @@ int qmoe_select_affinities(const float* affinities, const int32_t* idx, int64_t 
                        int(E), int(k), normalize ? 1 : 0, w);
 }
 
+int qmoe_greedy_pick(const void* logits, int64_t B, int64_t V, int32_t* tokens, int32_t* positions,
+                     int32_t* lengths, void* stream) {
+  QMOE_REQUIRE(logits && tokens, QMOE_ERR_INVALID_ARGUMENT, "greedy_pick: null pointer");
+  QMOE_REQUIRE(B >= 0 && B < (int64_t(1) << 31) && V > 0 && V < (int64_t(1) << 31), QMOE_ERR_INVALID_ARGUMENT,
+               "greedy_pick: bad sizes");
+  QMOE_REQUIRE(V % 8 != 0 || aligned16(logits), QMOE_ERR_MISALIGNED, "greedy_pick: logits not 16-byte aligned");
+  if (B == 0) return QMOE_OK;
+  return launch_kernel(qmoe::greedy_pick_kernel, dim3(unsigned(B)), dim3(1024), 0, static_cast<cudaStream_t>(stream),
+                       true, "greedy_pick_kernel", static_cast<const __nv_bfloat16*>(logits), int(V), tokens,
+                       positions, lengths);
+}
+
 int qmoe_embedding_gather(const void* table, int64_t V, int64_t H, const int32_t* ids, int64_t n, void* out,
                           void* stream) {
   QMOE_REQUIRE(table && ids && out, QMOE_ERR_INVALID_ARGUMENT, "embedding: null pointer");

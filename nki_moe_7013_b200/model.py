@@ -266,9 +266,8 @@ class DecodeSession:
             x = out
         hf = ops.rmsnorm(x, m.norm, m.cfg.rms_norm_eps)
         ops.linear(hf, m.lm_head, out=self.logits, split_ws=self.split_ws)
-        self.tokens.copy_(torch.argmax(self.logits, dim=-1).to(torch.int32))
-        self.positions.add_(1)
-        self.kv_len.add_(1)
+        # greedy pick + the next step's position and cache length, one launch
+        ops.greedy_pick(self.logits, self.tokens, self.positions, self.kv_len)
 
     def capture(self) -> None:
         """Capture one step into a CUDA graph (run one eager step first so

@@ -369,6 +369,27 @@ def masked_residual_add(y: torch.Tensor, mask: Optional[torch.Tensor] = None,
     return out
 
 
+def greedy_pick(logits: torch.Tensor, tokens: Optional[torch.Tensor] = None,
+                positions: Optional[torch.Tensor] = None, lengths: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """tokens[b] = argmax of logits[b] (int32; first maximal index, NaN
+    largest), and positions / lengths (int32, B) advanced by one, in one
+    launch."""
+    _need(logits, "logits", torch.bfloat16, 2)
+    B, V = logits.shape
+    dev = logits.device
+    logits = logits.contiguous()
+    tokens = torch.empty(B, dtype=torch.int32, device=dev) if tokens is None else tokens
+    for name, t in (("tokens", tokens), ("positions", positions), ("lengths", lengths)):
+        if t is not None:
+            _need(t, name, torch.int32, 1)
+            if t.shape[0] != B or not t.is_contiguous():
+                raise ValueError(f"{name} must be a contiguous ({B},) int32 tensor")
+    with torch.cuda.device(dev):
+        _C.check(_C.lib().qmoe_greedy_pick(_ptr(logits), B, V, _ptr(tokens), _ptr(positions), _ptr(lengths),
+                                           _stream(dev)), "qmoe_greedy_pick")
+    return tokens
+
+
 def select_affinities(affinities: torch.Tensor, idx: torch.Tensor, normalize: bool = True) -> torch.Tensor:
     """w (T, k) fp32 = affinities[t, idx[t, j]], L1-normalised per token when
     ``normalize`` (F.normalize(p=1): divided by max(sum |w|, 1e-12))."""

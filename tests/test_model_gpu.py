@@ -92,3 +92,26 @@ def test_decode_graph_replay_matches_eager_steps(cuda_dev):
     assert torch.equal(eager.positions, graphed.positions)
     assert max_rel_err(to_f32_np(graphed.logits), to_f32_np(eager.logits)) <= 1e-2
     graphed.release()
+
+
+@pytest.mark.parametrize("B,V", [(1, 151936), (4, 4096), (3, 1001)])
+def test_greedy_pick_matches_argmax(cuda_dev, B, V):
+    """ops.greedy_pick equals torch.argmax (first maximal index, NaN largest)
+    and advances positions and lengths by one; rows with ties and NaNs."""
+    from nki_moe_7013_b200 import ops
+
+    g = torch.Generator(device=cuda_dev)
+    g.manual_seed(B * 7 + V)
+    logits = torch.randn(B, V, generator=g, device=cuda_dev).to(torch.bfloat16)
+    logits[0, V // 3] = 50.0
+    logits[0, V // 2] = 50.0  # a tie: the lower index wins
+    if B > 1:
+        logits[1, V - 1] = float("nan")
+        logits[1, 5] = float("inf")
+    pos = torch.arange(B, dtype=torch.int32, device=cuda_dev)
+    lens = pos + 10
+    tok = ops.greedy_pick(logits, None, pos, lens)
+    torch.cuda.synchronize()
+    assert torch.equal(tok.long(), torch.argmax(logits, dim=-1))
+    assert torch.equal(pos, torch.arange(B, dtype=torch.int32, device=cuda_dev) + 1)
+    assert torch.equal(lens, pos + 10)
