@@ -57,7 +57,9 @@ __host__ __device__ __forceinline__ size_t ep_ctrl_words_per_parity(int N, int E
 enum EpFlagKind : int { kEpFlagCounts = 0, kEpFlagDispatch = 1, kEpFlagCombine = 2 };
 
 // Index of the device-side step counter (after both parity halves); the
-// word after it counts the CTAs of ep_wait_unpack that have read the epoch.
+// word after it counts the CTAs of ep_wait_unpack that have read the epoch,
+// the next two carry the epochs whose returned rows (ep_wait_unpack) and
+// dispatched rows (ep_wait_expand) have all landed.
 __host__ __device__ __forceinline__ size_t ep_step_word(int N, int E) { return 2 * ep_ctrl_words_per_parity(N, E); }
 
 // The step's epoch: the caller's, or (epoch == 0) the device counter + 1.
@@ -82,6 +84,23 @@ __device__ __forceinline__ int ld_acquire_sys(const int* ptr) {
   int v;
   asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
   return v;
+}
+
+__device__ __forceinline__ void st_release_gpu(int* ptr, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+// Spin (bounded) until *flag >= epoch on a word of this GPU written by this
+// GPU.  Returns false and records `code` on time-out.
+__device__ __forceinline__ bool ep_wait_flag_gpu(const int* flag, int epoch, unsigned int code) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (ld_acquire_gpu(flag) < epoch) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      record_device_error(code);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
 }
 
 // Spin (bounded) until *flag >= epoch.  Returns false and records `code` on
@@ -291,18 +310,24 @@ __global__ void __launch_bounds__(256)
   griddep_launch_dependents();
   if (!ep_resolve_epoch(my_ctrl, N, E, p, epoch)) return;
   const int lane = threadIdx.x & 31;
+  // CTA 0 signals and waits for the peers (system scope), then publishes the
+  // epoch in a local word the other CTAs wait on at GPU scope
+  int* local_go = my_ctrl + ep_step_word(N, E) + 3;
   if (threadIdx.x < 32) {
+    bool ok = true;
     if (blockIdx.x == 0) {
       __threadfence_system();
       __syncwarp();
       for (int d = lane; d < N; d += 32)
         st_release_sys(peer_ctrl[d] + ep_flag_word(N, E, p, kEpFlagDispatch, me), epoch);
+      for (int s = lane; s < N; s += 32)
+        ok &= ep_wait_flag(my_ctrl + ep_flag_word(N, E, p, kEpFlagDispatch, s), epoch, kDevErrPeerTimeout);
+      ok = __all_sync(0xFFFFFFFFu, ok);
+      __threadfence_system();
+      if (ok && lane == 0) st_release_gpu(local_go, epoch);
+    } else if (lane == 0) {
+      ok = ep_wait_flag_gpu(local_go, epoch, kDevErrPeerTimeout);
     }
-    bool ok = true;
-    for (int s = lane; s < N; s += 32)
-      ok &= ep_wait_flag(my_ctrl + ep_flag_word(N, E, p, kEpFlagDispatch, s), epoch, kDevErrPeerTimeout);
-    ok = __all_sync(0xFFFFFFFFu, ok);
-    __threadfence_system();
     if (lane == 0) ok_s = ok;
   }
   __syncthreads();
@@ -364,18 +389,26 @@ __global__ void __launch_bounds__(256)
   if (epoch_s < 0) return;
   epoch = epoch_s;
   const int lane = threadIdx.x & 31;
+  // CTA 0 signals the peers and waits for theirs (system scope), then
+  // publishes the epoch in a local word; the other CTAs wait on that word at
+  // GPU scope (the peers' stores happen before CTA 0's acquire, which comes
+  // before its release of the word)
+  int* local_go = my_ctrl + ep_step_word(N, E) + 2;
   if (threadIdx.x < 32) {
+    bool ok = true;
     if (blockIdx.x == 0) {
       __threadfence_system();
       __syncwarp();
       for (int d = lane; d < N; d += 32)
         st_release_sys(peer_ctrl[d] + ep_flag_word(N, E, p, kEpFlagCombine, me), epoch);
+      for (int s = lane; s < N; s += 32)
+        ok &= ep_wait_flag(my_ctrl + ep_flag_word(N, E, p, kEpFlagCombine, s), epoch, kDevErrPeerTimeout);
+      ok = __all_sync(0xFFFFFFFFu, ok);
+      __threadfence_system();
+      if (ok && lane == 0) st_release_gpu(local_go, epoch);
+    } else if (lane == 0) {
+      ok = ep_wait_flag_gpu(local_go, epoch, kDevErrPeerTimeout);
     }
-    bool ok = true;
-    for (int s = lane; s < N; s += 32)
-      ok &= ep_wait_flag(my_ctrl + ep_flag_word(N, E, p, kEpFlagCombine, s), epoch, kDevErrPeerTimeout);
-    ok = __all_sync(0xFFFFFFFFu, ok);
-    __threadfence_system();
     if (lane == 0) ok_s = ok;
   }
   __syncthreads();
@@ -386,7 +419,22 @@ __global__ void __launch_bounds__(256)
     const int t = w / slabs;
     const int col = (w - t * slabs) * 256 + lane * 8;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int j = 0; j < k; ++j) {
+    // the first 8 rows' loads all in flight before the sums (slot order kept)
+    uint4 rv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j < k) rv[j] = __ldcg(reinterpret_cast<const uint4*>(y_back + (size_t(t) * k + j) * H + col));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j >= k) break;
+      const uint32_t u[4] = {rv[j].x, rv[j].y, rv[j].z, rv[j].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        acc[2 * q] += bf16lo_to_f32(u[q]);
+        acc[2 * q + 1] += bf16hi_to_f32(u[q]);
+      }
+    }
+    for (int j = 8; j < k; ++j) {
       const uint4 v = __ldcg(reinterpret_cast<const uint4*>(y_back + (size_t(t) * k + j) * H + col));
       const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll

@@ -1512,7 +1512,8 @@ int qmoe_ipc_close(void* base) {
 
 int64_t qmoe_ep_ctrl_words(int64_t n_ranks, int64_t E) {
   if (n_ranks <= 0 || E <= 0) return 0;
-  // both halves, the step counter and ep_wait_unpack's arrival count (+2 spare)
+  // both halves, the step counter, ep_wait_unpack's arrival count and the
+  // local go words of ep_wait_unpack and ep_wait_expand
   return int64_t(qmoe::ep_step_word(int(n_ranks), int(E))) + 4;
 }
 
@@ -1606,8 +1607,12 @@ int qmoe_ep_wait_unpack(int* const* peer_ctrl, int* my_ctrl, int64_t n_ranks, in
                "ep_wait_unpack: pointers must be 16-byte aligned");
   DeviceInfo* d = nullptr;
   QMOE_CHECK(device_info(&d));
-  // the flags are waited for (and the step counter advanced) even when T == 0
-  return launch_kernel(qmoe::ep_wait_unpack_kernel, dim3(d->sms), dim3(256), 0, static_cast<cudaStream_t>(stream),
+  // a warp per (token, 256-column slab), up to 8 CTAs per SM; at least one
+  // CTA: the flags are waited for (and the step counter advanced) even when
+  // T == 0
+  const int64_t warps = T * (H / 256);
+  const int grid = int(std::max<int64_t>(1, std::min<int64_t>((warps + 7) / 8, 8 * int64_t(d->sms))));
+  return launch_kernel(qmoe::ep_wait_unpack_kernel, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream),
                        true, "ep_wait_unpack_kernel", peer_ctrl, my_ctrl, int(n_ranks), int(E), int(me),
                        int(parity), int(epoch), static_cast<const __nv_bfloat16*>(y_back),
                        static_cast<const __nv_bfloat16*>(residual), int(T), int(H), int(k),
