@@ -979,11 +979,38 @@ def run_ours_ep(args):
         barrier()
         return _max_over_ranks(c0.elapsed_time(c1) / args.steps, dev, world)
 
+    def copy_rate_both() -> float:
+        # upload and download at once on their own streams, as the e2e loop does
+        buf_in = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+        buf_out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+        c0, c1 = _events(2)
+        s_in.wait_stream(torch.cuda.current_stream(dev))
+        s_out.wait_stream(torch.cuda.current_stream(dev))
+        barrier()
+        c0.record()
+        s_in.wait_event(c0)
+        s_out.wait_event(c0)
+        for _ in range(args.steps):
+            with torch.cuda.stream(s_in):
+                buf_in.copy_(x_host, non_blocking=True)
+            with torch.cuda.stream(s_out):
+                y_host[1].copy_(buf_out, non_blocking=True)
+        torch.cuda.current_stream(dev).wait_stream(s_in)
+        torch.cuda.current_stream(dev).wait_stream(s_out)
+        c1.record()
+        barrier()
+        return _max_over_ranks(c0.elapsed_time(c1) / args.steps, dev, world)
+
     h2d_ms, d2h_ms = copy_rate(True), copy_rate(False)
+    both_ms = copy_rate_both()
     host_copy = {"h2d_gbs_per_gpu": T * H * 2 / (h2d_ms * 1e-3) / 1e9,
                  "d2h_gbs_per_gpu": T * H * 2 / (d2h_ms * 1e-3) / 1e9, "concurrent_ranks": world,
                  "copy_bound_tokens_per_s": T * world / (max(h2d_ms, d2h_ms) * 1e-3),
-                 "note": "all ranks copying 4 MB pinned host buffers at once, no compute (max over ranks)"}
+                 "both_directions_ms_per_step": both_ms,
+                 "copy_bound_both_directions_tokens_per_s": T * world / (both_ms * 1e-3),
+                 "note": "all ranks copying 4 MB pinned host buffers at once, no compute (max over ranks); "
+                         "both_directions: each rank uploads and downloads 4 MB at once per step, as the e2e "
+                         "loop does"}
 
     # ---------------- parity: one eager step vs the single-GPU forward ----------------
     y_ep = moe(x)
