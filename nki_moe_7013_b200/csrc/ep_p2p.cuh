@@ -134,6 +134,34 @@ __device__ __forceinline__ bool ep_signal_and_wait(int* const* peer_ctrl, int* m
   return ok;
 }
 
+// Exclusive scan of one int per thread over the CTA (blockDim.x a multiple
+// of 32, at most 1024); *total = the sum.  warp_sums: 32 ints of shared
+// memory.  Every thread of the CTA must call it.
+__device__ __forceinline__ int ep_block_exclusive_scan(int v, int* total, int* warp_sums) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int n = __shfl_up_sync(0xFFFFFFFFu, incl, off);
+    if (lane >= off) incl += n;
+  }
+  __syncthreads();  // warp_sums free from any earlier use
+  if (lane == 31) warp_sums[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int ws = lane < nw ? warp_sums[lane] : 0;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int n = __shfl_up_sync(0xFFFFFFFFu, ws, off);
+      if (lane >= off) ws += n;
+    }
+    if (lane < nw) warp_sums[lane] = ws;
+  }
+  __syncthreads();
+  *total = warp_sums[nw - 1];
+  return (warp > 0 ? warp_sums[warp - 1] : 0) + incl - v;
+}
+
 // ---------------------------------------------------------------------------
 // 1. count exchange (one CTA of 256 threads; E <= 256, N <= 32)
 // ---------------------------------------------------------------------------
@@ -145,6 +173,7 @@ __global__ void __launch_bounds__(256)
                               int n_zero_words) {
   __shared__ int tot[256];
   __shared__ int expert_off[257];
+  __shared__ int scan_s[32];
   __shared__ int ok_s;
   const int tid = threadIdx.x;
   griddep_wait();
@@ -178,36 +207,44 @@ __global__ void __launch_bounds__(256)
     return;
   }
   const volatile int* M = my_ctrl + size_t(p) * ep_ctrl_words_per_parity(N, E);
-  for (int e = tid; e < E; e += blockDim.x) {
+  // thread e (E <= 256 = blockDim.x): expert e's rows over all sources
+  const int tot_e = tid < E ? [&] {
     int t = 0;
-    for (int s = 0; s < N; ++s) t += M[s * E + e];
-    tot[e] = t;
-  }
+    for (int s = 0; s < N; ++s) t += M[s * E + tid];
+    return t;
+  }()
+                            : 0;
+  if (tid < E) tot[tid] = tot_e;
+  // row offset of each expert inside its owner's receive buffer: an exclusive
+  // scan of the totals, less the scan at the owner's first expert
+  int all = 0;
+  const int excl = ep_block_exclusive_scan(tot_e, &all, scan_s);
+  if (tid < E) expert_off[tid] = excl;
   __syncthreads();
+  const int off_e = tid < E ? excl - expert_off[(tid / e_local) * e_local] : 0;
+  __syncthreads();
+  if (tid < E) expert_off[tid] = off_e;
+  // tiles of my local experts: thread le writes expert me*e_local + le's
+  // 128-row tiles after those of the local experts before it
+  const int e_mine = me * e_local + tid;
+  const int tot_mine = tid < e_local ? tot[e_mine] : 0;
+  const int nt_e = (tot_mine + 127) / 128;
+  int nt = 0;
+  const int first_tile = ep_block_exclusive_scan(nt_e, &nt, scan_s);
+  if (tid < e_local) {
+    for (int j = 0; j < nt_e; ++j) {
+      const int i = first_tile + j;
+      if (i < max_tiles) {
+        tiles[1 + i] = tid;
+        tiles[1 + max_tiles + i] = expert_off[e_mine] + j * 128;
+        tiles[1 + 2 * max_tiles + i] = min(128, tot_mine - j * 128);
+      }
+    }
+  }
   if (tid == 0) {
-    // row offset of each expert inside its owner's receive buffer
-    for (int d = 0; d < N; ++d) {
-      int o = 0;
-      for (int e = d * e_local; e < (d + 1) * e_local; ++e) {
-        expert_off[e] = o;
-        o += tot[e];
-      }
-      if (d == me) recv_rows[0] = o;
-    }
-    // tiles of my local experts
-    int nt = 0;
-    for (int le = 0; le < e_local; ++le) {
-      const int e = me * e_local + le;
-      for (int r = 0; r < tot[e]; r += 128) {
-        if (nt < max_tiles) {
-          tiles[1 + nt] = le;
-          tiles[1 + max_tiles + nt] = expert_off[e] + r;
-          tiles[1 + 2 * max_tiles + nt] = min(128, tot[e] - r);
-        }
-        ++nt;
-      }
-    }
     tiles[0] = min(nt, max_tiles);
+    const int last = me * e_local + e_local - 1;  // my rows end where my last expert's do
+    recv_rows[0] = expert_off[last] + tot[last];
   }
   __syncthreads();
   for (int e = tid; e < E; e += blockDim.x) {
