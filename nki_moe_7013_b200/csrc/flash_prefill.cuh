@@ -140,7 +140,7 @@ __device__ __forceinline__ bool fa_wait(uint64_t* bar, uint32_t parity, volatile
   return mbar_wait_bounded(bar, parity, abort_flag, code);
 }
 
-// The same wait taken by every lane of a warp, with one verdict for all of
+// The same wait taken by every lane of a warp, with one outcome for all of
 // them (a lane that timed out never leaves the others at a warp barrier).
 __device__ __forceinline__ bool fa_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                              unsigned int code) {
