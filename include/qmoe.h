@@ -146,6 +146,8 @@ QMOE_API int qmoe_moe_permute(const int32_t* topk_idx, const float* topk_w, int3
  * otherwise); barrier: two int32 of device scratch, zero-filled before the
  * first call; every completed call leaves them zero again (a call that
  * records a wait time-out may not: zero them again before the next).
+ * T == 0 (also in qmoe_route_small): counts and offsets are zeroed, the tile
+ * list is empty and zero_words are zeroed -- no launch.
  * ---------------------------------------------------------------------- */
 QMOE_API int qmoe_route_permute(const void* x, const void* w_router, const float* bias, int64_t T, int64_t H,
                                 int64_t E, int64_t k, int normalize, int32_t* topk_idx, float* topk_w,

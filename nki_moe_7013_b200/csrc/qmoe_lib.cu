@@ -344,7 +344,8 @@ int launch_route_small(const void* x, const void* w, const float* bias, int64_t 
 
 int check_router_args(const void* x, const void* w, int64_t T, int64_t H, int64_t E, int64_t k,
                       const int32_t* topk_idx, const float* topk_w) {
-  QMOE_REQUIRE(x && w && topk_idx && topk_w, QMOE_ERR_INVALID_ARGUMENT, "router: null pointer");
+  // an empty batch (T == 0) may come with a null x (an empty tensor's data)
+  QMOE_REQUIRE((T == 0 || x) && w && topk_idx && topk_w, QMOE_ERR_INVALID_ARGUMENT, "router: null pointer");
   QMOE_REQUIRE(T >= 0 && T < (int64_t(1) << 31) / 32, QMOE_ERR_INVALID_ARGUMENT, "router: bad T=%lld",
                (long long)T);
   QMOE_REQUIRE(H > 0 && H % 256 == 0 && H <= 4096, QMOE_ERR_UNSUPPORTED_SHAPE,
@@ -990,6 +991,20 @@ int qmoe_moe_permute(const int32_t* topk_idx, const float* topk_w, int32_t* chun
                         int(n_zero_words));
 }
 
+// An empty batch still leaves consistent routing outputs: zero counts and
+// offsets, an empty tile list and the scratch words zeroed (a consumer that
+// reads the counts -- the expert-parallel count exchange -- then sees no rows
+// instead of a previous batch's).
+static int route_empty(int32_t* counts, int32_t* offsets, int32_t* tiles, int64_t E, int32_t* zero_words,
+                int64_t n_zero_words, cudaStream_t s) {
+  cudaError_t e = cudaMemsetAsync(counts, 0, size_t(E) * 4, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(offsets, 0, size_t(E + 1) * 4, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(tiles, 0, 4, s);
+  if (e == cudaSuccess && zero_words && n_zero_words > 0) e = cudaMemsetAsync(zero_words, 0, size_t(n_zero_words) * 4, s);
+  QMOE_REQUIRE(e == cudaSuccess, QMOE_ERR_CUDA, "route (empty batch): %s", cudaGetErrorString(e));
+  return QMOE_OK;
+}
+
 int qmoe_route_permute(const void* x, const void* w_router, const float* bias, int64_t T, int64_t H, int64_t E,
                        int64_t k, int normalize, int32_t* topk_idx, float* topk_w, int32_t* chunk_hist,
                        int32_t* counts, int32_t* offsets, int32_t* row_token, float* row_w, int32_t* slot_row,
@@ -1002,8 +1017,8 @@ int qmoe_route_permute(const void* x, const void* w_router, const float* bias, i
                "route_permute: null barrier or chunk_hist not 16-byte aligned");
   DeviceInfo* d = nullptr;
   QMOE_CHECK(device_info(&d));
-  if (T == 0) return QMOE_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (T == 0) return route_empty(counts, offsets, tiles, E, zero_words, n_zero_words, s);
   const int64_t nchunks = (T + qmoe::kRouterChunk - 1) / qmoe::kRouterChunk;
   if (T > kRouterSmallMaxT && nchunks <= num_sms(0))
     return launch_route_permute(x, w_router, bias, T, H, E, k, normalize, topk_idx, topk_w, chunk_hist, counts,
@@ -1028,7 +1043,7 @@ int qmoe_route_small(const void* x, const void* w_router, const float* bias, int
   QMOE_REQUIRE(!acc_zero || aligned16(acc_zero), QMOE_ERR_MISALIGNED, "route_small: acc not 16-byte aligned");
   DeviceInfo* d = nullptr;
   QMOE_CHECK(device_info(&d));
-  if (T == 0) return QMOE_OK;
+  if (T == 0) return route_empty(counts, offsets, tiles, E, nullptr, 0, static_cast<cudaStream_t>(stream));
   return launch_route_small(x, w_router, bias, T, H, E, k, normalize, logits, topk_idx, topk_w, counts, offsets,
                             row_token, row_w, slot_row, tiles, qmoe_max_tiles(T * k, E), acc_zero,
                             static_cast<cudaStream_t>(stream));
@@ -1541,7 +1556,8 @@ int qmoe_ep_dispatch(const void* x, const int32_t* topk_idx, const float* topk_w
                      const int32_t* offsets, const int32_t* dest_base, void* const* peer_tok,
                      void* const* peer_recv_meta, int64_t T, int64_t k, int64_t H, int64_t e_local, int64_t me,
                      int64_t n_ranks, int64_t parity, int64_t cap_rows, int64_t max_tokens, void* stream) {
-  QMOE_REQUIRE(x && topk_idx && topk_w && slot_row && offsets && dest_base && peer_tok && peer_recv_meta,
+  QMOE_REQUIRE((T == 0 || x) && topk_idx && topk_w && slot_row && offsets && dest_base && peer_tok &&
+                   peer_recv_meta,
                QMOE_ERR_INVALID_ARGUMENT, "ep_dispatch: null pointer");
   QMOE_REQUIRE(T >= 0 && k >= 1 && k <= 32 && T * k < (int64_t(1) << 31) && H > 0 && H % 8 == 0 &&
                    e_local >= 1 && n_ranks >= 1 && n_ranks <= 32 && me >= 0 && me < n_ranks &&
@@ -1597,7 +1613,8 @@ int qmoe_ep_signal_wait(int* const* peer_ctrl, int* my_ctrl, int64_t n_ranks, in
 int qmoe_ep_wait_unpack(int* const* peer_ctrl, int* my_ctrl, int64_t n_ranks, int64_t E, int64_t me,
                         int64_t parity, int64_t epoch, const void* y_back, const void* residual, int64_t T,
                         int64_t H, int64_t k, void* out, void* stream) {
-  QMOE_REQUIRE(peer_ctrl && my_ctrl && y_back && out, QMOE_ERR_INVALID_ARGUMENT, "ep_wait_unpack: null pointer");
+  QMOE_REQUIRE(peer_ctrl && my_ctrl && (T == 0 || (y_back && out)), QMOE_ERR_INVALID_ARGUMENT,
+               "ep_wait_unpack: null pointer");
   QMOE_REQUIRE(n_ranks >= 1 && n_ranks <= 32 && me >= 0 && me < n_ranks && (parity == 0 || parity == 1) &&
                    epoch >= 0 && epoch < (int64_t(1) << 31) && E >= 1 && T >= 0 && k >= 1 && k <= 32 &&
                    T * k < (int64_t(1) << 31),

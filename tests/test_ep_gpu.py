@@ -84,6 +84,46 @@ def test_experts_return_loopback_matches_forward(cuda_dev, T):
     assert err <= MAX_REL, err
 
 
+def test_route_empty_batch_zeroes_outputs(cuda_dev):
+    """qmoe_route_permute / qmoe_route_small with T == 0: counts, offsets and
+    the tile count become zero (no stale routing from an earlier batch)."""
+    from nki_moe_7013_b200 import _C
+
+    E, H, k = 128, 2048, 8
+    wr = moe_weights(70, E, H, 128, cuda_dev)[0]
+    x = activations(70, 4, H, cuda_dev)
+    i32 = dict(dtype=torch.int32, device=cuda_dev)
+    lib, s = _C.lib(), torch.cuda.current_stream(cuda_dev).cuda_stream
+    for small in (False, True):
+        counts = torch.full((E,), 7, **i32)
+        offsets = torch.full((E + 1,), 7, **i32)
+        tiles = torch.full((1 + 3 * 64,), 7, **i32)
+        zero_words = torch.full((10,), 7, **i32)
+        idx = torch.empty((4, k), **i32)
+        tw = torch.empty((4, k), dtype=torch.float32, device=cuda_dev)
+        rt = torch.empty(32, **i32)
+        rw = torch.empty(32, dtype=torch.float32, device=cuda_dev)
+        sr = torch.empty((4, k), **i32)
+        if small:
+            logits = torch.empty((4, E), dtype=torch.float32, device=cuda_dev)
+            _C.check(lib.qmoe_route_small(x.data_ptr(), wr.data_ptr(), None, 0, H, E, k, 1, logits.data_ptr(),
+                                          idx.data_ptr(), tw.data_ptr(), counts.data_ptr(), offsets.data_ptr(),
+                                          rt.data_ptr(), rw.data_ptr(), sr.data_ptr(), tiles.data_ptr(), None, s),
+                     "qmoe_route_small")
+        else:
+            hist = torch.empty((1, E), **i32)
+            barrier = torch.zeros(2, **i32)
+            _C.check(lib.qmoe_route_permute(x.data_ptr(), wr.data_ptr(), None, 0, H, E, k, 1, idx.data_ptr(),
+                                            tw.data_ptr(), hist.data_ptr(), counts.data_ptr(), offsets.data_ptr(),
+                                            rt.data_ptr(), rw.data_ptr(), sr.data_ptr(), tiles.data_ptr(), None,
+                                            None, zero_words.data_ptr(), 10, barrier.data_ptr(), s),
+                     "qmoe_route_permute")
+        torch.cuda.synchronize()
+        assert not counts.any() and not offsets.any() and int(tiles[0]) == 0
+        if not small:
+            assert not zero_words.any()
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -140,7 +180,10 @@ def _nccl_worker(rank, world, port, out_dir):
     # smaller batch on the last one, and a residual
     peer = PeerExpertParallelMoE(cfg, wr, local, max_tokens=T)
     res = normal_bf16_device(200 + rank, (T, H), 1.0, dev)
-    outs += [peer(x), peer(x, residual=res), peer(x[: T // 2])]
+    outs += [peer(x), peer(x, residual=res)]
+    # an empty step: every rank still takes it (counts published as zero)
+    assert peer(x[:0]).shape == (0, H)
+    outs += [peer(x[: T // 2])]
     # graph replays (one graph per parity), after the eager steps
     peer.capture(x)
     outs += [peer.replay().clone(), peer.replay().clone()]
