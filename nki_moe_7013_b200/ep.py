@@ -311,7 +311,7 @@ class PeerExpertParallelMoE(nn.Module):
         if self._owns_exchange:
             self.x.close()
 
-    STAGES = ("route", "exchange", "dispatch", "experts", "return")
+    STAGES = ("route", "exchange", "dispatch", "wait_expand", "experts", "return")
 
     def launches_per_step(self, T: int) -> int:
         return self.x.launches_per_step(T)
@@ -349,24 +349,25 @@ class PeerExpertParallelMoE(nn.Module):
             pt(x), pt(X.topk_idx), pt(X.topk_w), pt(X.slot_row), pt(X.offsets), pt(X.dest_base),
             pt(X.peer["tok"]), pt(X.peer["recv_meta"]), T, k, H, self.e_local, self.rank, self.world, par,
             X.cap, X.max_tokens, s), "qmoe_ep_dispatch")
+        mark(3)
         recv_x = X.recv_x[par * X.cap:(par + 1) * X.cap]
         _C.check(lib.qmoe_ep_wait_expand(
             pt(X.peer["ctrl"]), pt(X.ctrl), self.world, E, self.rank, par, 0, pt(X.tok), X.tok_rows,
             pt(X.recv_meta[par * X.cap:]), pt(recv_x), pt(X.recv_rows), X.cap, H, s), "qmoe_ep_wait_expand")
-        mark(3)
+        mark(4)
         # gate/up + down in one persistent kernel; its down epilogue stores
         # each weighted row into the source rank's return buffer
         _C.check(lib.qmoe_moe_experts_return(
             pt(recv_x), pt(self.local.gate_up), pt(self.local.down), pt(X.tiles), X.max_tiles,
             pt(X.recv_meta[par * X.cap:]), pt(X.peer["ret"]), par * X.ret_rows, X.ret_rows,
             self.world, X.cap, H, I, self.e_local, pt(X.act), pt(X.done), s), "qmoe_moe_experts_return")
-        mark(4)
+        mark(5)
         # "your rows are back" flags, the wait for every peer's, and the
         # fp32 sum of each token's k returned rows (+ residual), one launch
         y_back = X.ret[par * X.ret_rows:]
         _C.check(lib.qmoe_ep_wait_unpack(pt(X.peer["ctrl"]), pt(X.ctrl), self.world, E, self.rank, par, 0,
                                          pt(y_back), pt(residual), T, H, k, pt(out), s), "qmoe_ep_wait_unpack")
-        mark(5)
+        mark(6)
 
     def forward(self, hidden_states: torch.Tensor, residual: Optional[torch.Tensor] = None,
                 events=None) -> torch.Tensor:
