@@ -6,7 +6,7 @@ import numpy as np
 import pytest
 import torch
 
-from helpers import MAX_REL, activations, max_rel_err, moe_weights, to_f32_np
+from helpers import MAX_REL, activations, assert_within_one_ulp, max_rel_err, moe_weights, to_f32_np
 
 pytestmark = pytest.mark.gpu
 
@@ -136,7 +136,9 @@ def test_select_affinities_matches_torch(cuda_dev, normalize):
 
 def test_moe_block_padding_mask(cuda_dev):
     """Qwen3MoeSparseMoeBlock(x, padding_mask): masked tokens give zero rows,
-    the others the unmasked output bit for bit."""
+    the others the unmasked output (two separate forwards: the combine adds a
+    token's expert rows with fp32 atomics in a run-dependent order, so within
+    one bf16 ulp)."""
     from nki_moe_7013_b200.config import Qwen3MoeConfig
     from nki_moe_7013_b200.moe import MoEWeights, Qwen3MoeSparseMoeBlock
 
@@ -150,7 +152,7 @@ def test_moe_block_padding_mask(cuda_dev):
     masked = blk(x, mask)[0]
     torch.cuda.synchronize()
     keep = mask.bool()
-    assert torch.equal(masked[keep], full[keep])
+    assert_within_one_ulp(masked[keep], full[keep], "unmasked tokens")
     assert not masked[~keep].any()
 
 
