@@ -583,9 +583,27 @@ int launch_moe_fused(const void* x, int64_t x_rows, const int32_t* gather_rows, 
 
 // RMSNorm launch with the row held in registers: kChunks 128-element chunks
 // per warp (H <= 4096).
+// Above this many rows, bf16 rows take the low-register prefill kernel.
+constexpr int kNormPrefetchMaxRows = 1024;
+
 template <typename Tin, typename Tout>
 int launch_rmsnorm(int chunks, int grid, cudaStream_t s, const Tin* x, const __nv_bfloat16* res, const float* w,
                    int rows, int H, float eps, Tout* y, __nv_bfloat16* res_out) {
+  if constexpr (sizeof(Tin) == 2) {
+    if (rows > kNormPrefetchMaxRows) {
+#define QMOE_RMSNORM_ROWS_CASE(CH)                                                                              \
+  if (chunks <= CH)                                                                                             \
+    return launch_kernel(qmoe::rmsnorm_rows_kernel<Tout, CH>, dim3(grid), dim3(qmoe::kNormThreads), 0, s, true, \
+                         "rmsnorm_rows_kernel", x, res, w, rows, H, eps, y, res_out);
+      QMOE_RMSNORM_ROWS_CASE(1)
+      QMOE_RMSNORM_ROWS_CASE(2)
+      QMOE_RMSNORM_ROWS_CASE(4)
+      QMOE_RMSNORM_ROWS_CASE(8)
+      QMOE_RMSNORM_ROWS_CASE(16)
+      QMOE_RMSNORM_ROWS_CASE(32)
+#undef QMOE_RMSNORM_ROWS_CASE
+    }
+  }
 #define QMOE_RMSNORM_CASE(CH)                                                                               \
   if (chunks <= CH)                                                                                         \
     return launch_kernel(qmoe::rmsnorm_kernel<Tin, Tout, CH>, dim3(grid), dim3(qmoe::kNormThreads), 0, s, true, \
@@ -1292,6 +1310,8 @@ int qmoe_qk_norm_rope(const void* qkv, const int32_t* positions, const int32_t* 
   QMOE_REQUIRE(head_dim == qmoe::kQkHeadDim, QMOE_ERR_UNSUPPORTED_SHAPE,
                "qk_norm_rope: head_dim must be 128");
   QMOE_REQUIRE(nh > 0 && nkv > 0 && nh % nkv == 0, QMOE_ERR_INVALID_ARGUMENT, "qk_norm_rope: bad heads");
+  QMOE_REQUIRE(nh + 2 * nkv <= qmoe::kQkWarps * qmoe::kQkMaxHeadsPerWarp, QMOE_ERR_UNSUPPORTED_SHAPE,
+               "qk_norm_rope: more than %d heads", qmoe::kQkWarps * qmoe::kQkMaxHeadsPerWarp);
   QMOE_REQUIRE(T >= 0 && T * (nh + 2 * nkv) < (int64_t(1) << 31), QMOE_ERR_INVALID_ARGUMENT,
                "qk_norm_rope: bad T");
   QMOE_REQUIRE(n_slots > 0 && max_seq > 0, QMOE_ERR_INVALID_ARGUMENT, "qk_norm_rope: bad cache shape");
@@ -1301,8 +1321,8 @@ int qmoe_qk_norm_rope(const void* qkv, const int32_t* positions, const int32_t* 
   DeviceInfo* d = nullptr;
   QMOE_CHECK(device_info(&d));
   if (T == 0) return QMOE_OK;
-  const int64_t warps = T * (nh + 2 * nkv);
-  return launch_kernel(qmoe::qk_norm_rope_kernel, dim3(unsigned((warps + 7) / 8)), dim3(256), 0,
+  // a CTA per token, each warp several heads
+  return launch_kernel(qmoe::qk_norm_rope_kernel, dim3(unsigned(T)), dim3(32 * qmoe::kQkWarps), 0,
                        static_cast<cudaStream_t>(stream), true, "qk_norm_rope_kernel",
                        static_cast<const __nv_bfloat16*>(qkv), positions, cache_slot, q_norm_w, k_norm_w, inv_freq,
                        int(T), int(nh), int(nkv), eps, static_cast<__nv_bfloat16*>(q_out),

@@ -25,7 +25,7 @@ def test_rmsnorm_known_answer_on_gpu(cuda_dev, oracle):
     assert np.max(np.abs(got.cpu().numpy() - expected)) < 1e-3
 
 
-@pytest.mark.parametrize("rows,H", [(1, 2048), (1000, 2048), (33, 512)])
+@pytest.mark.parametrize("rows,H", [(1, 2048), (1000, 2048), (33, 512), (4096, 2048), (2500, 4096)])
 def test_rmsnorm_bf16_and_fused_residual(cuda_dev, oracle, rows, H):
     from nki_moe_7013_b200 import ops
 
@@ -40,6 +40,29 @@ def test_rmsnorm_bf16_and_fused_residual(cuda_dev, oracle, rows, H):
     s_ref = oracle.round_to_bf16(to_f32_np(x) + to_f32_np(r))
     assert np.array_equal(to_f32_np(s), s_ref)  # the residual stream is bit-exact
     assert max_rel_err(to_f32_np(y2), oracle.rmsnorm(s_ref, w.cpu().numpy(), 1e-6)) < 1e-2
+
+
+@pytest.mark.parametrize("H", [2048, 4096])
+def test_rmsnorm_prefill_rows_match_decode_rows(cuda_dev, H):
+    """bf16 RMSNorm over many rows (the low-register prefill kernel) equals,
+    bit for bit, the same rows normalised 1024 at a time (the kernel that
+    holds the norm weight in registers), with and without the residual add,
+    for bf16 and fp32 outputs."""
+    from nki_moe_7013_b200 import ops
+
+    rows = 4096
+    x = activations(80 + H, rows, H, cuda_dev)
+    r = activations(81 + H, rows, H, cuda_dev)
+    w = (1.0 + 0.1 * torch.randn(H, device=cuda_dev)).float()
+    for dt in (torch.bfloat16, torch.float32):
+        whole = ops.rmsnorm(x, w, 1e-6, out_dtype=dt)
+        parts = torch.cat([ops.rmsnorm(x[i:i + 1024], w, 1e-6, out_dtype=dt) for i in range(0, rows, 1024)])
+        assert torch.equal(whole, parts)
+        y, s = ops.rmsnorm(x, w, 1e-6, residual=r, out_dtype=dt)
+        pieces = [ops.rmsnorm(x[i:i + 1024], w, 1e-6, residual=r[i:i + 1024], out_dtype=dt)
+                  for i in range(0, rows, 1024)]
+        assert torch.equal(y, torch.cat([p[0] for p in pieces]))
+        assert torch.equal(s, torch.cat([p[1] for p in pieces]))
 
 
 @pytest.mark.parametrize("T,K,N", [(1, 2048, 5120), (1024, 2048, 5120), (77, 4096, 2048), (300, 256, 384),
