@@ -34,3 +34,26 @@ def test_routing_agreement_marks_near_ties():
     ids_a[2] = torch.tensor([0, 2], dtype=torch.int32)   # a difference at a clear gap
     r = model.routing_agreement(ids_a, ids_b, logits, k)
     assert abs(r["max_flip_gap"] - 1.0) < 1e-6
+
+
+def test_ops_refuse_cpu_tensors():
+    """The torch wrappers check their tensors before any library call: a CPU
+    tensor is refused (there is no CPU path to fall back to)."""
+    import pytest
+
+    from nki_moe_7013_b200 import ops
+
+    y = torch.zeros(4, 256, dtype=torch.bfloat16)
+    ids = torch.zeros(4, 8, dtype=torch.int32)
+    calls = [
+        lambda: ops.masked_residual_add(y, torch.ones(4)),
+        lambda: ops.greedy_pick(y),
+        lambda: ops.select_affinities(torch.zeros(4, 128), ids),
+        lambda: ops.rmsnorm(y, torch.ones(256), 1e-6),
+        lambda: ops.moe_forward(y, torch.zeros(128, 256, dtype=torch.bfloat16),
+                                torch.zeros(128, 256, 256, dtype=torch.bfloat16),
+                                torch.zeros(128, 256, 128, dtype=torch.bfloat16), 8),
+    ]
+    for call in calls:
+        with pytest.raises(ValueError, match="no CPU path"):
+            call()
